@@ -1,0 +1,22 @@
+"""af2cuda: host-side mirror of alphafold2-webgpu's pair-stack operator API over
+libaf2cuda.so (sm_100a CUDA kernels behind a C ABI).
+
+The class and option names follow the reference's TypeScript exports
+(src/index.ts) so parity tests read like the reference's own tests.
+"""
+from ._lib import Af2Error, RangeError, lib
+from .bundle import TriangleReferenceBundle, load_triangle_reference_bundle_from_files
+from .device import Device
+from .triangle import (TriangleGpuOptions, TriangleGpuResult, TriangleMultiplicationIncomingGpu,
+                       TriangleMultiplicationOutgoingGpu, encode_triangle_multiplication,
+                       encode_triangle_multiplication_tensors, triangle_weight_count, triangle_workspace_bytes)
+from .types import (ORDER, TriangleMultiplicationInput, TriangleMultiplicationWeights, TriangleShape,
+                    error_metrics, expected_weight_element_count, pack_weights, validate_triangle_input)
+
+__all__ = [
+    "Af2Error", "RangeError", "lib", "Device", "TriangleReferenceBundle", "load_triangle_reference_bundle_from_files",
+    "TriangleGpuOptions", "TriangleGpuResult", "TriangleMultiplicationIncomingGpu", "TriangleMultiplicationOutgoingGpu",
+    "encode_triangle_multiplication", "encode_triangle_multiplication_tensors", "triangle_weight_count",
+    "triangle_workspace_bytes", "ORDER", "TriangleMultiplicationInput", "TriangleMultiplicationWeights",
+    "TriangleShape", "error_metrics", "expected_weight_element_count", "pack_weights", "validate_triangle_input",
+]

@@ -1,0 +1,103 @@
+"""Loads libaf2cuda.so and declares its C ABI (include/af2cuda.h) for ctypes.
+
+There is no fallback: if the library is missing or cannot be loaded the
+import of an operator fails with the loader's message.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+PKG_DIR = Path(__file__).resolve().parent.parent
+LIB_PATH = Path(os.environ.get("AF2CUDA_LIBRARY", PKG_DIR / "libaf2cuda.so"))
+
+AF2_OK = 0
+AF2_ERR_INVALID_ARGUMENT = 1
+AF2_ERR_UNSUPPORTED = 2
+AF2_ERR_OUT_OF_MEMORY = 3
+AF2_ERR_CUDA = 4
+AF2_ERR_DEVICE_TIMEOUT = 5
+AF2_ERR_NCCL = 6
+AF2_ERR_NO_DEVICE = 7
+
+AF2_F32, AF2_F16, AF2_BF16 = 0, 1, 2
+AF2_OUTGOING, AF2_INCOMING = 0, 1
+
+# Every symbol include/af2cuda.h declares, with (restype, argtypes).
+_vp = ctypes.c_void_p
+_i64 = ctypes.c_int64
+_i32 = ctypes.c_int
+_f64 = ctypes.c_double
+
+
+class TriangleShape(ctypes.Structure):
+    _fields_ = [("length", _i64), ("c_z", _i64), ("c_hidden", _i64)]
+
+
+class TriangleOptions(ctypes.Structure):
+    _fields_ = [("block_rows", ctypes.c_int32), ("residual", ctypes.c_int32)]
+
+
+class OpStats(ctypes.Structure):
+    _fields_ = [("device_milliseconds", _f64), ("host_milliseconds", _f64), ("flops", _f64),
+                ("workspace_bytes", ctypes.c_uint64), ("peak_bytes", ctypes.c_uint64)]
+
+
+SIGNATURES = {
+    "af2_version": (_i32, []),
+    "af2_status_string": (ctypes.c_char_p, [_i32]),
+    "af2_create": (_i32, [_i32, ctypes.POINTER(_vp)]),
+    "af2_destroy": (None, [_vp]),
+    "af2_last_error": (ctypes.c_char_p, [_vp]),
+    "af2_sync": (_i32, [_vp, _vp]),
+    "af2_launch_count": (ctypes.c_uint64, [_vp]),
+    "af2_triangle_weight_count": (_i64, [_i64, _i64]),
+    "af2_triangle_check": (_i32, [_i32, ctypes.POINTER(TriangleShape), _i64, _f64, ctypes.c_char_p, ctypes.c_size_t]),
+    "af2_triangle_workspace_bytes": (_i32, [ctypes.POINTER(TriangleShape), ctypes.POINTER(TriangleOptions),
+                                            ctypes.POINTER(ctypes.c_uint64)]),
+    "af2_triangle_multiplication_host": (_i32, [_vp, _i32, ctypes.POINTER(TriangleShape), _vp, _vp, _vp, _i64, _f64,
+                                                ctypes.POINTER(TriangleOptions), _i32, _vp,
+                                                ctypes.POINTER(OpStats)]),
+    "af2_triangle_multiplication": (_i32, [_vp, _i32, ctypes.POINTER(TriangleShape), _vp, _i32, _vp, _vp, _i64, _f64,
+                                           ctypes.POINTER(TriangleOptions), _vp, _i32, _vp, _vp]),
+}
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded library; raises OSError when it is absent (no fallback)."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise OSError(f"libaf2cuda.so not found at {LIB_PATH}; build it with "
+                          "`python alphafold2-webgpu_b200/build.py`")
+        handle = ctypes.CDLL(str(LIB_PATH))
+        for name, (restype, argtypes) in SIGNATURES.items():
+            fn = getattr(handle, name)
+            fn.restype = restype
+            fn.argtypes = argtypes
+        _lib = handle
+    return _lib
+
+
+class Af2Error(RuntimeError):
+    """A non-OK af2_status, with the library's message."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(f"{message} ({lib().af2_status_string(status).decode()})")
+        self.status = status
+
+
+class RangeError(ValueError):
+    """The reference's RangeError: a shape, length or epsilon it rejects."""
+
+
+def check(status: int, ctx=None) -> None:
+    if status == AF2_OK:
+        return
+    msg = lib().af2_last_error(ctx).decode() if ctx else lib().af2_status_string(status).decode()
+    if status == AF2_ERR_INVALID_ARGUMENT:
+        raise RangeError(msg)
+    raise Af2Error(status, msg)

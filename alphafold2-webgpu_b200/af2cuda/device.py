@@ -1,0 +1,48 @@
+"""A CUDA device context: the af2_ctx handle behind every operator.
+
+Plays the role the reference gives a GPUDevice from requestAlphaFoldDevice
+(src/runtime/device.ts:375): operators are constructed with one.
+"""
+from __future__ import annotations
+
+import ctypes
+
+from . import _lib
+
+
+class Device:
+    def __init__(self, ordinal: int = 0):
+        handle = ctypes.c_void_p()
+        status = _lib.lib().af2_create(ordinal, ctypes.byref(handle))
+        if status != _lib.AF2_OK:
+            raise _lib.Af2Error(status, f"cannot open CUDA device {ordinal}")
+        self.ordinal = ordinal
+        self.handle = handle
+
+    def sync(self, stream: int | None = None) -> None:
+        """Waits for `stream` (default: the context's) and raises on kernel-side failures."""
+        _lib.check(_lib.lib().af2_sync(self.handle, stream), self.handle)
+
+    @property
+    def launch_count(self) -> int:
+        return int(_lib.lib().af2_launch_count(self.handle))
+
+    def close(self) -> None:
+        if self.handle:
+            _lib.lib().af2_destroy(self.handle)
+            self.handle = None
+
+    def destroy(self) -> None:  # GPUDevice.destroy()
+        self.close()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -1,0 +1,70 @@
+// af2_internal.h -- host-side pieces shared by the C-ABI layer (api.cu) and
+// the per-operator launchers (triangle.cu, ...).  Nothing here crosses the ABI.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "../../include/af2cuda.h"
+
+namespace af2 {
+
+// Device-side scratch owned by a context: grown on demand, never shrunk.
+struct DeviceBuffer {
+  void *ptr = nullptr;
+  size_t bytes = 0;
+};
+
+}  // namespace af2
+
+struct af2_ctx {
+  int device = 0;
+  int sm_count = 0;
+  cudaStream_t stream = nullptr;
+  unsigned int *err_word = nullptr;  // device word the kernels flag failures in
+  af2::DeviceBuffer workspace;       // device-form scratch
+  af2::DeviceBuffer staging[4];      // host-form device copies (z, mask, weights, out)
+  cudaEvent_t ev_start = nullptr, ev_stop = nullptr;
+  uint64_t launches = 0;
+  uint64_t allocated = 0, peak = 0;
+  std::string last_error;
+};
+
+namespace af2 {
+
+// Sets ctx->last_error and returns `status`.
+af2_status fail(af2_ctx *ctx, af2_status status, const std::string &message);
+// Maps a CUDA error to AF2_ERR_CUDA (or AF2_ERR_OUT_OF_MEMORY) with context.
+af2_status cuda_fail(af2_ctx *ctx, cudaError_t e, const char *what);
+// Ensures `buf` holds at least `bytes` (256-byte aligned device memory).
+af2_status ensure(af2_ctx *ctx, DeviceBuffer &buf, size_t bytes, const char *what);
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point.
+bool encode_map_3d(CUtensorMap *map, CUtensorMapDataType dtype, const void *base, uint64_t d0, uint64_t d1,
+                   uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t b0, uint32_t b1,
+                   uint32_t b2, CUtensorMapSwizzle swizzle);
+
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// ---- triangle multiplication (triangle.cu) ----
+
+struct TriangleLayout {
+  int64_t n = 0, cz = 0, ch = 0;
+  int64_t block_rows = 0;   // output rows per block
+  int64_t kp = 0;           // row pitch (elements) of the projected operands
+  int64_t jp = 0;           // row pitch (elements) of the contracted block
+  bool pad_z = false;       // z is re-laid as f16 [P][128] before the kernels
+  size_t off_w16 = 0, off_vec = 0, off_z16 = 0, off_a = 0, off_b = 0, off_x = 0, total = 0;
+};
+
+TriangleLayout triangle_layout(int64_t n, int64_t cz, int64_t ch, int64_t block_rows, int z_dtype);
+
+// Launches the whole op on `stream`; the workspace holds TriangleLayout::total bytes.
+af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L, const void *z, int z_dtype,
+                           const float *mask, const float *packed, double eps, int residual, void *out,
+                           int out_dtype, void *workspace, cudaStream_t stream);
+
+}  // namespace af2

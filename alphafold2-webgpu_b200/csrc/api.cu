@@ -1,0 +1,324 @@
+// api.cu -- the extern "C" surface of libaf2cuda.so: contexts, validation
+// that mirrors the reference's RangeError checks, the host form (upload, run,
+// read back) and the device form of each operator.
+#include <cudaTypedefs.h>
+
+#include <chrono>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "af2_internal.h"
+
+namespace af2 {
+
+af2_status fail(af2_ctx *ctx, af2_status status, const std::string &message) {
+  if (ctx) ctx->last_error = message;
+  return status;
+}
+
+af2_status cuda_fail(af2_ctx *ctx, cudaError_t e, const char *what) {
+  const af2_status s = (e == cudaErrorMemoryAllocation) ? AF2_ERR_OUT_OF_MEMORY : AF2_ERR_CUDA;
+  return fail(ctx, s, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+af2_status ensure(af2_ctx *ctx, DeviceBuffer &buf, size_t bytes, const char *what) {
+  if (buf.bytes >= bytes) return AF2_OK;
+  if (buf.ptr) {
+    cudaError_t e = cudaStreamSynchronize(ctx->stream);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "synchronize before regrowing scratch");
+    cudaFree(buf.ptr);
+    ctx->allocated -= buf.bytes;
+    buf.ptr = nullptr;
+    buf.bytes = 0;
+  }
+  const size_t want = align_up(bytes, 1 << 20);
+  cudaError_t e = cudaMalloc(&buf.ptr, want);
+  if (e != cudaSuccess) {
+    buf.ptr = nullptr;
+    cudaGetLastError();
+    return fail(ctx, AF2_ERR_OUT_OF_MEMORY,
+                std::string("device allocation of ") + std::to_string(want) + " bytes for " + what + " failed: " +
+                    cudaGetErrorString(e));
+  }
+  buf.bytes = want;
+  ctx->allocated += want;
+  if (ctx->allocated > ctx->peak) ctx->peak = ctx->allocated;
+  return AF2_OK;
+}
+
+namespace {
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+void load_encode() {
+  void *fn = nullptr;
+  cudaDriverEntryPointQueryResult q{};
+  if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q) ==
+          cudaSuccess &&
+      q == cudaDriverEntryPointSuccess)
+    g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+}
+}  // namespace
+
+bool encode_map_3d(CUtensorMap *map, CUtensorMapDataType dtype, const void *base, uint64_t d0, uint64_t d1,
+                   uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t b0, uint32_t b1,
+                   uint32_t b2, CUtensorMapSwizzle swizzle) {
+  std::call_once(g_encode_once, load_encode);
+  if (!g_encode) return false;
+  const cuuint64_t dims[3] = {d0, d1, d2};
+  const cuuint64_t strides[2] = {stride1_bytes, stride2_bytes};
+  const cuuint32_t box[3] = {b0, b1, b2};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return g_encode(map, dtype, 3, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+namespace {
+
+constexpr int64_t kMaxSafeInteger = 9007199254740991LL;  // Number.MAX_SAFE_INTEGER
+
+bool positive_safe(int64_t v) { return v > 0 && v <= kMaxSafeInteger; }
+
+size_t dtype_bytes(int dtype) { return dtype == AF2_F32 ? 4 : 2; }
+
+bool valid_dtype(int dtype) { return dtype == AF2_F32 || dtype == AF2_F16 || dtype == AF2_BF16; }
+
+// validateTriangleInput (src/triangle/types.ts:54-89), for what a C caller hands over.
+af2_status validate_triangle(af2_ctx *ctx, int direction, const af2_triangle_shape *shape, int64_t weight_count,
+                             double epsilon) {
+  if (!shape) return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "shape is NULL");
+  if (direction != AF2_OUTGOING && direction != AF2_INCOMING)
+    return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "direction must be 0 (outgoing) or 1 (incoming)");
+  const char *names[3] = {"length", "cZ", "cHidden"};
+  const int64_t vals[3] = {shape->length, shape->c_z, shape->c_hidden};
+  for (int i = 0; i < 3; ++i)
+    if (!positive_safe(vals[i]))
+      return fail(ctx, AF2_ERR_INVALID_ARGUMENT, std::string(names[i]) + " must be a positive safe integer; received " +
+                                                     std::to_string(vals[i]));
+  const double pair_count = (double)shape->length * (double)shape->length;
+  if (pair_count * (double)std::max(shape->c_z, shape->c_hidden) > (double)kMaxSafeInteger)
+    return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "tensor dimensions exceed JavaScript's safe integer range");
+  const int64_t expected = af2_triangle_weight_count(shape->c_z, shape->c_hidden);
+  if (weight_count != expected)
+    return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "packed weights have " + std::to_string(weight_count) +
+                                                   " values; expected " + std::to_string(expected));
+  if (!(epsilon > 0) || !std::isfinite(epsilon))
+    return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "epsilon must be finite and positive; received " +
+                                                   std::to_string(epsilon));
+  if (shape->c_z > 128 || shape->c_hidden > 128)
+    return fail(ctx, AF2_ERR_UNSUPPORTED, "c_z and c_hidden above 128 are not supported by the sm_100a kernels");
+  if (shape->length > (1 << 20))
+    return fail(ctx, AF2_ERR_UNSUPPORTED, "length above 1048576 is not supported");
+  return AF2_OK;
+}
+
+af2_status check_device_errors(af2_ctx *ctx) {
+  unsigned int word = 0;
+  cudaError_t e = cudaMemcpy(&word, ctx->err_word, sizeof(word), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "read the device error word");
+  if (word != 0) {
+    cudaMemset(ctx->err_word, 0, sizeof(unsigned int));
+    char buf[160];
+    std::snprintf(buf, sizeof buf,
+                  "a kernel's bounded wait ran out (error bits 0x%x); the kernel returned without finishing", word);
+    return fail(ctx, AF2_ERR_DEVICE_TIMEOUT, buf);
+  }
+  return AF2_OK;
+}
+
+}  // namespace
+}  // namespace af2
+
+using namespace af2;
+
+extern "C" {
+
+int af2_version(void) { return AF2CUDA_VERSION; }
+
+const char *af2_status_string(af2_status status) {
+  switch (status) {
+    case AF2_OK: return "ok";
+    case AF2_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case AF2_ERR_UNSUPPORTED: return "unsupported";
+    case AF2_ERR_OUT_OF_MEMORY: return "out of device memory";
+    case AF2_ERR_CUDA: return "CUDA error";
+    case AF2_ERR_DEVICE_TIMEOUT: return "device-side wait timed out";
+    case AF2_ERR_NCCL: return "NCCL error";
+    case AF2_ERR_NO_DEVICE: return "no usable device";
+  }
+  return "unknown status";
+}
+
+af2_status af2_create(int device_ordinal, af2_ctx **out) {
+  if (!out) return AF2_ERR_INVALID_ARGUMENT;
+  *out = nullptr;
+  int count = 0;
+  if (cudaGetDeviceCount(&count) != cudaSuccess || count == 0) {
+    cudaGetLastError();
+    return AF2_ERR_NO_DEVICE;
+  }
+  if (device_ordinal < 0 || device_ordinal >= count) return AF2_ERR_INVALID_ARGUMENT;
+  cudaDeviceProp prop{};
+  if (cudaGetDeviceProperties(&prop, device_ordinal) != cudaSuccess) return AF2_ERR_NO_DEVICE;
+  if (prop.major != 10) return AF2_ERR_NO_DEVICE;  // built for sm_100a only
+  if (cudaSetDevice(device_ordinal) != cudaSuccess) return AF2_ERR_NO_DEVICE;
+  af2_ctx *ctx = new af2_ctx();
+  ctx->device = device_ordinal;
+  ctx->sm_count = prop.multiProcessorCount;
+  if (cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaMalloc(&ctx->err_word, sizeof(unsigned int)) != cudaSuccess ||
+      cudaMemset(ctx->err_word, 0, sizeof(unsigned int)) != cudaSuccess ||
+      cudaEventCreate(&ctx->ev_start) != cudaSuccess || cudaEventCreate(&ctx->ev_stop) != cudaSuccess) {
+    af2_destroy(ctx);
+    return AF2_ERR_CUDA;
+  }
+  *out = ctx;
+  return AF2_OK;
+}
+
+void af2_destroy(af2_ctx *ctx) {
+  if (!ctx) return;
+  cudaSetDevice(ctx->device);
+  if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+  if (ctx->workspace.ptr) cudaFree(ctx->workspace.ptr);
+  for (auto &s : ctx->staging)
+    if (s.ptr) cudaFree(s.ptr);
+  if (ctx->err_word) cudaFree(ctx->err_word);
+  if (ctx->ev_start) cudaEventDestroy(ctx->ev_start);
+  if (ctx->ev_stop) cudaEventDestroy(ctx->ev_stop);
+  if (ctx->stream) cudaStreamDestroy(ctx->stream);
+  delete ctx;
+}
+
+const char *af2_last_error(const af2_ctx *ctx) { return ctx ? ctx->last_error.c_str() : "no context"; }
+
+uint64_t af2_launch_count(const af2_ctx *ctx) { return ctx ? ctx->launches : 0; }
+
+af2_status af2_sync(af2_ctx *ctx, void *stream) {
+  if (!ctx) return AF2_ERR_INVALID_ARGUMENT;
+  cudaSetDevice(ctx->device);
+  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+  cudaError_t e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "stream synchronize");
+  return check_device_errors(ctx);
+}
+
+int64_t af2_triangle_weight_count(int64_t c_z, int64_t c_hidden) {
+  return 2 * c_z + 4 * (c_hidden * c_z + c_hidden) + 2 * c_hidden + (c_z * c_hidden + c_z) + (c_z * c_z + c_z);
+}
+
+af2_status af2_triangle_check(int direction, const af2_triangle_shape *shape, int64_t weight_count, double epsilon,
+                              char *message, size_t capacity) {
+  af2_ctx scratch;  // carries the message only; no device is touched
+  const af2_status st = validate_triangle(&scratch, direction, shape, weight_count, epsilon);
+  if (message && capacity > 0) {
+    std::strncpy(message, scratch.last_error.c_str(), capacity - 1);
+    message[capacity - 1] = '\0';
+  }
+  return st;
+}
+
+af2_status af2_triangle_workspace_bytes(const af2_triangle_shape *shape, const af2_triangle_options *options,
+                                        uint64_t *bytes) {
+  if (!shape || !bytes || !positive_safe(shape->length) || !positive_safe(shape->c_z) ||
+      !positive_safe(shape->c_hidden))
+    return AF2_ERR_INVALID_ARGUMENT;
+  // The z re-layout is sized in, whatever z's dtype turns out to be.
+  const TriangleLayout L = triangle_layout(shape->length, shape->c_z, shape->c_hidden,
+                                           options ? options->block_rows : 0, AF2_F32);
+  *bytes = L.total;
+  return AF2_OK;
+}
+
+af2_status af2_triangle_multiplication(af2_ctx *ctx, int direction, const af2_triangle_shape *shape, const void *z,
+                                       int z_dtype, const float *mask, const float *packed_weights,
+                                       int64_t weight_count, double epsilon, const af2_triangle_options *options,
+                                       void *out, int out_dtype, void *workspace, void *stream) {
+  if (!ctx) return AF2_ERR_INVALID_ARGUMENT;
+  af2_status st = validate_triangle(ctx, direction, shape, weight_count, epsilon);
+  if (st != AF2_OK) return st;
+  if (!z || !mask || !packed_weights || !out) return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "a tensor pointer is NULL");
+  if (!valid_dtype(z_dtype) || !valid_dtype(out_dtype))
+    return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "dtype must be AF2_F32, AF2_F16 or AF2_BF16");
+  if (options && options->block_rows < 0)
+    return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "blockRows must be a positive safe integer");
+  cudaSetDevice(ctx->device);
+  const TriangleLayout L = triangle_layout(shape->length, shape->c_z, shape->c_hidden,
+                                           options ? options->block_rows : 0, z_dtype);
+  void *ws = workspace;
+  if (!ws) {
+    st = ensure(ctx, ctx->workspace, L.total, "triangle scratch");
+    if (st != AF2_OK) return st;
+    ws = ctx->workspace.ptr;
+  } else if (reinterpret_cast<uintptr_t>(ws) % 256 != 0) {
+    return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "workspace must be 256-byte aligned");
+  }
+  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+  return triangle_launch(ctx, direction, L, z, z_dtype, mask, packed_weights, epsilon,
+                         options ? options->residual : 0, out, out_dtype, ws, s);
+}
+
+af2_status af2_triangle_multiplication_host(af2_ctx *ctx, int direction, const af2_triangle_shape *shape,
+                                            const void *z, const float *mask, const float *packed_weights,
+                                            int64_t weight_count, double epsilon,
+                                            const af2_triangle_options *options, int io_dtype, void *out,
+                                            af2_op_stats *stats) {
+  if (!ctx) return AF2_ERR_INVALID_ARGUMENT;
+  af2_status st = validate_triangle(ctx, direction, shape, weight_count, epsilon);
+  if (st != AF2_OK) return st;
+  if (!z || !mask || !packed_weights || !out) return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "a tensor pointer is NULL");
+  if (!valid_dtype(io_dtype)) return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "dtype must be AF2_F32, AF2_F16 or AF2_BF16");
+  cudaSetDevice(ctx->device);
+  const auto t0 = std::chrono::steady_clock::now();
+  const size_t pairs = (size_t)shape->length * shape->length;
+  const size_t z_bytes = pairs * shape->c_z * dtype_bytes(io_dtype);
+  const size_t mask_bytes = pairs * sizeof(float);
+  const size_t w_bytes = (size_t)weight_count * sizeof(float);
+  if ((st = ensure(ctx, ctx->staging[0], z_bytes, "z upload")) != AF2_OK ||
+      (st = ensure(ctx, ctx->staging[1], mask_bytes, "mask upload")) != AF2_OK ||
+      (st = ensure(ctx, ctx->staging[2], w_bytes, "weight upload")) != AF2_OK ||
+      (st = ensure(ctx, ctx->staging[3], z_bytes, "output")) != AF2_OK)
+    return st;
+  const TriangleLayout L = triangle_layout(shape->length, shape->c_z, shape->c_hidden,
+                                           options ? options->block_rows : 0, io_dtype);
+  if ((st = ensure(ctx, ctx->workspace, L.total, "triangle scratch")) != AF2_OK) return st;
+  cudaStream_t s = ctx->stream;
+  const int residual = options ? options->residual : 0;
+  cudaError_t e;
+  if ((e = cudaMemcpyAsync(ctx->staging[0].ptr, z, z_bytes, cudaMemcpyHostToDevice, s)) != cudaSuccess ||
+      (e = cudaMemcpyAsync(ctx->staging[1].ptr, mask, mask_bytes, cudaMemcpyHostToDevice, s)) != cudaSuccess ||
+      (e = cudaMemcpyAsync(ctx->staging[2].ptr, packed_weights, w_bytes, cudaMemcpyHostToDevice, s)) != cudaSuccess)
+    return cuda_fail(ctx, e, "upload inputs");
+  if (residual &&
+      (e = cudaMemcpyAsync(ctx->staging[3].ptr, ctx->staging[0].ptr, z_bytes, cudaMemcpyDeviceToDevice, s)) !=
+          cudaSuccess)
+    return cuda_fail(ctx, e, "seed residual output");
+  cudaEventRecord(ctx->ev_start, s);
+  st = triangle_launch(ctx, direction, L, ctx->staging[0].ptr, io_dtype, static_cast<const float *>(ctx->staging[1].ptr),
+                       static_cast<const float *>(ctx->staging[2].ptr), epsilon, residual, ctx->staging[3].ptr,
+                       io_dtype, ctx->workspace.ptr, s);
+  if (st != AF2_OK) return st;
+  cudaEventRecord(ctx->ev_stop, s);
+  if ((e = cudaMemcpyAsync(out, ctx->staging[3].ptr, z_bytes, cudaMemcpyDeviceToHost, s)) != cudaSuccess)
+    return cuda_fail(ctx, e, "read back output");
+  if ((e = cudaStreamSynchronize(s)) != cudaSuccess) return cuda_fail(ctx, e, "triangle multiplication");
+  if ((st = check_device_errors(ctx)) != AF2_OK) return st;
+  if (stats) {
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, ctx->ev_start, ctx->ev_stop);
+    const double n = (double)shape->length, cz = (double)shape->c_z, ch = (double)shape->c_hidden;
+    stats->device_milliseconds = ms;
+    stats->host_milliseconds =
+        std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+    // kernel-cost.ts:158-162: gate, block + whole projections, contraction, output.
+    stats->flops = 2 * n * n * (cz * cz + 2 * cz * 2 * ch + n * ch + ch * cz);
+    stats->workspace_bytes = L.total;
+    stats->peak_bytes = ctx->peak;
+  }
+  return AF2_OK;
+}
+
+}  // extern "C"

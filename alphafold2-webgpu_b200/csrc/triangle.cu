@@ -1,0 +1,1054 @@
+// triangle.cu -- triangle multiplication (outgoing and incoming) on sm_100a.
+//
+// Reference: src/triangle/cpu-reference.ts:56-100 (the maths),
+// src/triangle/shaders.ts:151-589 (the seven WGSL kernels this replaces) and
+// src/evoformer/block.ts:1497-1671 (the in-model encoder).
+//
+// Three persistent, warp-specialised kernels per call:
+//
+//  1. project  -- LayerNorm(z) on load, then the four c_z -> c_h projections
+//     (a_p, a_g, b_p, b_g) as one tcgen05 GEMM per 64-pair tile, computed
+//     transposed (D[h][pair] = W[h][:] . zn[pair][:]) so that a TMEM lane is a
+//     hidden channel and the gated result a = mask (p + b_p) sigmoid(g + b_g)
+//     is stored channel-major [h][row][k] with 16-byte vector stores.  The
+//     incoming direction reads z in transposed pair order, so its operands
+//     come out as a'[h][j][k] = a[k][j] and the contraction below is the same
+//     NT GEMM for both directions.
+//  2. contract -- per hidden channel h, X[h] = (1/N) A[h] B[h]^T with TMA-fed
+//     128x256x64 tiles, a 4-deep mbarrier pipeline and two TMEM accumulators
+//     so the epilogue of one tile overlaps the MMAs of the next.  X is stored
+//     f16, pre-scaled by 1/N so any N stays inside the f16 range.
+//  3. output   -- per 128-pair tile: the [h][pair] block of X is transposed
+//     and layer-normalised in shared memory (eps scaled by 1/N^2 to undo the
+//     pre-scale), z is layer-normalised again, and two tcgen05 GEMMs give
+//     LN_out(X) W_z^T and LN(z) W_g^T; the epilogue applies the biases, the
+//     sigmoid gate and the optional residual add and writes the pair rows.
+//
+// All channel dimensions are padded to 128 (weights zero-padded), with the
+// LayerNorm statistics taken over the real channel counts.
+#include "af2_device.cuh"
+#include "af2_internal.h"
+
+#include <algorithm>
+
+namespace af2 {
+namespace tri {
+
+constexpr int C = 128;  // padded channel count of every triangle tile
+
+// Prepared weights: six [128][128] f16 matrices, [out][in] row-major.
+enum { kWAP = 0, kWAG = 1, kWBP = 2, kWBG = 3, kWZ = 4, kWG = 5, kMatCount = 6 };
+// Prepared vectors: 128 f32 each.
+enum {
+  kVLnInW = 0, kVLnInB, kVBAP, kVBAG, kVBBP, kVBBG, kVLnOutW, kVLnOutB, kVBZ, kVBG, kVecCount
+};
+
+constexpr unsigned kFull = 0xffffffffu;
+
+__device__ __forceinline__ uint8_t *align1024(uint8_t *p) {
+  return reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
+}
+
+__device__ __forceinline__ float reduce16(float v) {
+  v += __shfl_xor_sync(kFull, v, 8);
+  v += __shfl_xor_sync(kFull, v, 4);
+  v += __shfl_xor_sync(kFull, v, 2);
+  v += __shfl_xor_sync(kFull, v, 1);
+  return v;
+}
+
+// Warp-uniform bounded wait: every lane waits, and the warp proceeds only if
+// every lane saw the phase complete.
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatile int *abort_flag,
+                                          unsigned int *err, unsigned int code) {
+  const bool ok = mbar_wait(bar, parity, abort_flag, err, code);
+  return __all_sync(kFull, ok);
+}
+
+// ---------------------------------------------------------------------------
+// Weight preparation: the packed f32 array in the reference's ORDER
+// (src/triangle/weights.ts:4-10) -> zero-padded f16 matrices + f32 vectors.
+// ---------------------------------------------------------------------------
+__global__ void prep_weights_kernel(const float *__restrict__ packed, int cz, int ch, __half *__restrict__ w16,
+                                    float *__restrict__ vec) {
+  const int64_t o_lniw = 0, o_lnib = cz, o_apw = 2 * cz;
+  const int64_t o_apb = o_apw + (int64_t)ch * cz, o_agw = o_apb + ch, o_agb = o_agw + (int64_t)ch * cz;
+  const int64_t o_bpw = o_agb + ch, o_bpb = o_bpw + (int64_t)ch * cz, o_bgw = o_bpb + ch;
+  const int64_t o_bgb = o_bgw + (int64_t)ch * cz, o_lnow = o_bgb + ch, o_lnob = o_lnow + ch;
+  const int64_t o_zw = o_lnob + ch, o_zb = o_zw + (int64_t)cz * ch, o_gw = o_zb + cz, o_gb = o_gw + (int64_t)cz * cz;
+  const int stride = gridDim.x * blockDim.x;
+  for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < kMatCount * C * C; idx += stride) {
+    const int m = idx / (C * C), r = (idx / C) % C, c = idx % C;
+    float v = 0.f;
+    switch (m) {
+      case kWAP: if (r < ch && c < cz) v = packed[o_apw + (int64_t)r * cz + c]; break;
+      case kWAG: if (r < ch && c < cz) v = packed[o_agw + (int64_t)r * cz + c]; break;
+      case kWBP: if (r < ch && c < cz) v = packed[o_bpw + (int64_t)r * cz + c]; break;
+      case kWBG: if (r < ch && c < cz) v = packed[o_bgw + (int64_t)r * cz + c]; break;
+      case kWZ: if (r < cz && c < ch) v = packed[o_zw + (int64_t)r * ch + c]; break;
+      default: if (r < cz && c < cz) v = packed[o_gw + (int64_t)r * cz + c]; break;
+    }
+    w16[idx] = __float2half_rn(v);
+  }
+  for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < kVecCount * C; idx += stride) {
+    const int q = idx / C, e = idx % C;
+    float v = 0.f;
+    switch (q) {
+      case kVLnInW: if (e < cz) v = packed[o_lniw + e]; break;
+      case kVLnInB: if (e < cz) v = packed[o_lnib + e]; break;
+      case kVBAP: if (e < ch) v = packed[o_apb + e]; break;
+      case kVBAG: if (e < ch) v = packed[o_agb + e]; break;
+      case kVBBP: if (e < ch) v = packed[o_bpb + e]; break;
+      case kVBBG: if (e < ch) v = packed[o_bgb + e]; break;
+      case kVLnOutW: if (e < ch) v = packed[o_lnow + e]; break;
+      case kVLnOutB: if (e < ch) v = packed[o_lnob + e]; break;
+      case kVBZ: if (e < cz) v = packed[o_zb + e]; break;
+      default: if (e < cz) v = packed[o_gb + e]; break;
+    }
+    vec[idx] = v;
+  }
+}
+
+// z [pairs][cz] (any dtype) -> f16 [pairs][128], zero-padded channels.
+template <typename T>
+__global__ void pad_z_kernel(const T *__restrict__ z, int64_t pairs, int cz, __half *__restrict__ z16) {
+  const int64_t total = pairs * C;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t p = idx / C;
+    const int c = static_cast<int>(idx % C);
+    z16[idx] = c < cz ? __float2half_rn(to_f32<T>(z[p * cz + c])) : __float2half_rn(0.f);
+  }
+}
+
+// Loads a [128][128] f16 row-major matrix into two 128B-swizzled K chunks.
+__device__ __forceinline__ void load_weight_matrix(uint8_t *dst, const __half *src, int tid, int nthreads) {
+  for (int q = tid; q < C * 16; q += nthreads) {
+    const int row = q >> 4, c16 = q & 15;
+    const uint4 v = *reinterpret_cast<const uint4 *>(src + row * C + c16 * 8);
+    *reinterpret_cast<uint4 *>(dst + (c16 >> 3) * 16384 + sw128_offset(row, c16 & 7)) = v;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Kernel 1: fused LayerNorm + gated projections.
+// ---------------------------------------------------------------------------
+constexpr int PJ_TILE = 64;      // pairs per tile
+constexpr int PJ_STAGES = 3;
+constexpr int PJ_THREADS = 320;  // warp 0 TMA, 1 MMA, 2-5 LayerNorm, 6-9 epilogue
+constexpr uint32_t PJ_CHUNK = PJ_TILE * 128;            // one 64-channel K chunk: 8 KB
+constexpr uint32_t PJ_STAGE_BYTES = 2 * PJ_CHUNK;       // 16 KB
+constexpr uint32_t PJ_W_BYTES = 4 * 2 * 16384;          // 128 KB
+constexpr uint32_t PJ_OFF_STAGE = PJ_W_BYTES;
+constexpr uint32_t PJ_OFF_BAR = PJ_OFF_STAGE + PJ_STAGES * PJ_STAGE_BYTES;
+constexpr uint32_t PJ_SMEM = PJ_OFF_BAR + 256 + 1024;
+
+struct ProjectArgs {
+  const float *mask;
+  int64_t mask_rs, mask_ks;  // mask of tile row r, pair k: mask[r * mask_rs + k * mask_ks]
+  __half *a_out, *b_out;     // [128][rows][kp]
+  int64_t out_hs, out_rs;
+  const __half *w16;
+  const float *vec;
+  int n, cz, tiles_k, total_tiles;
+  int transposed;  // incoming: the z map is [k][j][c] and the box walks k in its outer dimension
+  float eps;
+  unsigned int *err;
+};
+
+// LayerNorm of one 128-channel row held by 16 lanes (8 channels each) inside a
+// 128B-swizzled K-major tile, in place, as f16.  Channels >= cz are padding
+// (zero input, zero gamma/beta) and are left out of the statistics.
+template <typename ZT>
+__device__ __forceinline__ void ln_row_inplace(uint8_t *stage, uint32_t chunk_bytes, int row, int c16,
+                                               const float (&g)[8], const float (&bt)[8], int cz, float inv_cz,
+                                               float eps) {
+  uint8_t *ptr = stage + (c16 >> 3) * chunk_bytes + sw128_offset(row, c16 & 7);
+  const uint4 v = *reinterpret_cast<const uint4 *>(ptr);
+  float x[8];
+  unpack8<ZT>(v, x);
+  float sum = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) sum += x[i];
+  const float mean = reduce16(sum) * inv_cz;
+  float sq = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float d = x[i] - mean;
+    sq += (c16 * 8 + i < cz) ? d * d : 0.f;
+  }
+  const float rstd = rsqrtf(reduce16(sq) * inv_cz + eps);
+  uint4 o;
+  o.x = pack_half2((x[0] - mean) * rstd * g[0] + bt[0], (x[1] - mean) * rstd * g[1] + bt[1]);
+  o.y = pack_half2((x[2] - mean) * rstd * g[2] + bt[2], (x[3] - mean) * rstd * g[3] + bt[3]);
+  o.z = pack_half2((x[4] - mean) * rstd * g[4] + bt[4], (x[5] - mean) * rstd * g[5] + bt[5]);
+  o.w = pack_half2((x[6] - mean) * rstd * g[6] + bt[6], (x[7] - mean) * rstd * g[7] + bt[7]);
+  *reinterpret_cast<uint4 *>(ptr) = o;
+}
+
+// 32 gated values of one channel row -> f16 at dst (count valid of them).
+__device__ __forceinline__ void store_gated(__half *dst, const uint32_t (&vp)[32], const uint32_t (&vg)[32],
+                                            const float (&mk)[32], float bp, float bg, int valid) {
+  uint32_t packed[16];
+#pragma unroll
+  for (int c = 0; c < 32; c += 2) {
+    const float y0 = mk[c] * (__uint_as_float(vp[c]) + bp) * sigmoidf(__uint_as_float(vg[c]) + bg);
+    const float y1 = mk[c + 1] * (__uint_as_float(vp[c + 1]) + bp) * sigmoidf(__uint_as_float(vg[c + 1]) + bg);
+    packed[c >> 1] = pack_half2(y0, y1);
+  }
+  if (valid >= 32) {
+    uint4 *d = reinterpret_cast<uint4 *>(dst);
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      d[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+  } else {
+    const __half *h = reinterpret_cast<const __half *>(packed);
+    for (int c = 0; c < valid; ++c) dst[c] = h[c];
+  }
+}
+
+template <typename ZT>
+__global__ void __launch_bounds__(PJ_THREADS, 1)
+    project_kernel(const __grid_constant__ CUtensorMap zmap, const ProjectArgs p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = align1024(smem_raw);
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bar0 = sbase + PJ_OFF_BAR;
+  // barriers: z_full[3] z_ready[3] z_empty[3] acc_full[2] acc_empty[2] drain
+  auto z_full = [&](int s) { return bar0 + 8u * s; };
+  auto z_ready = [&](int s) { return bar0 + 8u * (3 + s); };
+  auto z_empty = [&](int s) { return bar0 + 8u * (6 + s); };
+  auto acc_full = [&](int b) { return bar0 + 8u * (9 + b); };
+  auto acc_empty = [&](int b) { return bar0 + 8u * (11 + b); };
+  const uint32_t drain = bar0 + 8u * 13;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + PJ_OFF_BAR + 128);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + PJ_OFF_BAR + 136);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  for (int m = 0; m < 4; ++m)
+    load_weight_matrix(smem + m * 32768, p.w16 + (size_t)m * C * C, threadIdx.x, PJ_THREADS);
+  fence_async_smem();
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < PJ_STAGES; ++s) {
+      mbar_init(z_full(s), 1);
+      mbar_init(z_ready(s), 4);
+      mbar_init(z_empty(s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(acc_full(b), 1);
+      mbar_init(acc_empty(b), 4);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---- TMA producer ----
+    if (lane == 0) {
+      tma_prefetch_map(&zmap);
+      int it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x, ++it) {
+        const int s = it % PJ_STAGES;
+        const uint32_t ph = (it / PJ_STAGES) & 1;
+        if (!mbar_wait(z_empty(s), ph ^ 1, abort_flag, p.err, kErrWaitProducer)) {
+          ok = false;
+          break;
+        }
+        const int r = t / p.tiles_k, kb = t % p.tiles_k;
+        const uint32_t dst = sbase + PJ_OFF_STAGE + s * PJ_STAGE_BYTES;
+        mbar_arrive_expect_tx(z_full(s), PJ_STAGE_BYTES);
+        const int c1 = p.transposed ? r : kb * PJ_TILE, c2 = p.transposed ? kb * PJ_TILE : r;
+        tma_load_3d(dst, &zmap, z_full(s), 0, c1, c2);
+        tma_load_3d(dst + PJ_CHUNK, &zmap, z_full(s), 64, c1, c2);
+      }
+      if (!ok) {  // wait for the loads still landing before the CTA exits
+        for (int j = std::max(0, it - PJ_STAGES); j < it; ++j)
+          mbar_wait_drain(z_full(j % PJ_STAGES), (j / PJ_STAGES) & 1, p.err);
+      }
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer ----
+    if (lane == 0) {
+      constexpr uint32_t kIdesc = idesc_f16_f32(128, PJ_TILE);
+      int it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x, ++it) {
+        const int s = it % PJ_STAGES;
+        const uint32_t ph = (it / PJ_STAGES) & 1;
+        const int buf = it & 1;
+        const uint32_t bph = (it >> 1) & 1;
+        if (!mbar_wait(acc_empty(buf), bph ^ 1, abort_flag, p.err, kErrWaitMma) ||
+            !mbar_wait(z_ready(s), ph, abort_flag, p.err, kErrWaitMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t zs = sbase + PJ_OFF_STAGE + s * PJ_STAGE_BYTES;
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+          const uint32_t d = tmem + buf * 256 + m * PJ_TILE;
+#pragma unroll
+          for (int kc = 0; kc < 2; ++kc) {
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks) {
+              const uint64_t ad = sdesc_k_sw128(sbase + (m * 2 + kc) * 16384 + ks * 32);
+              const uint64_t bd = sdesc_k_sw128(zs + kc * PJ_CHUNK + ks * 32);
+              mma_f16(d, ad, bd, kIdesc, (kc | ks) != 0);
+            }
+          }
+        }
+        mma_commit(z_empty(s));
+        mma_commit(acc_full(buf));
+      }
+      if (!ok) {
+        mma_commit(drain);
+        mbar_wait_drain(drain, 0, p.err);
+      }
+    }
+    __syncwarp();
+  } else if (warp < 6) {
+    // ---- LayerNorm of the z tile, in place, bf16/f16 -> f16 ----
+    const int nw = warp - 2, sub = lane >> 4, c16 = lane & 15;
+    float g[8], bt[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      g[i] = p.vec[kVLnInW * C + c16 * 8 + i];
+      bt[i] = p.vec[kVLnInB * C + c16 * 8 + i];
+    }
+    const float inv_cz = 1.f / static_cast<float>(p.cz);
+    int it = 0;
+    for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x, ++it) {
+      const int s = it % PJ_STAGES;
+      const uint32_t ph = (it / PJ_STAGES) & 1;
+      if (!warp_wait(z_full(s), ph, abort_flag, p.err, kErrWaitNormalizer)) break;
+      uint8_t *stage = smem + PJ_OFF_STAGE + s * PJ_STAGE_BYTES;
+#pragma unroll 1
+      for (int pass = 0; pass < PJ_TILE / 8; ++pass)
+        ln_row_inplace<ZT>(stage, PJ_CHUNK, pass * 8 + nw * 2 + sub, c16, g, bt, p.cz, inv_cz, p.eps);
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(z_ready(s));
+    }
+  } else {
+    // ---- epilogue: TMEM -> gated f16 operands, channel-major ----
+    const int q = warp & 3;
+    const int h = q * 32 + lane;
+    const float bap = p.vec[kVBAP * C + h], bag = p.vec[kVBAG * C + h];
+    const float bbp = p.vec[kVBBP * C + h], bbg = p.vec[kVBBG * C + h];
+    int it = 0;
+    for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x, ++it) {
+      const int r = t / p.tiles_k, k0 = (t % p.tiles_k) * PJ_TILE;
+      const int buf = it & 1;
+      const uint32_t bph = (it >> 1) & 1;
+      const float m0 = (k0 + lane < p.n) ? p.mask[r * p.mask_rs + (int64_t)(k0 + lane) * p.mask_ks] : 0.f;
+      const float m1 =
+          (k0 + 32 + lane < p.n) ? p.mask[r * p.mask_rs + (int64_t)(k0 + 32 + lane) * p.mask_ks] : 0.f;
+      if (!warp_wait(acc_full(buf), bph, abort_flag, p.err, kErrWaitEpilogue)) break;
+      tc_fence_after();
+      const uint32_t trow = tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * 256;
+      __half *a_row = p.a_out + h * p.out_hs + r * p.out_rs + k0;
+      __half *b_row = p.b_out + h * p.out_hs + r * p.out_rs + k0;
+#pragma unroll 1
+      for (int half = 0; half < 2; ++half) {
+        float mk[32];
+        const float msrc = half ? m1 : m0;
+#pragma unroll
+        for (int c = 0; c < 32; ++c) mk[c] = __shfl_sync(kFull, msrc, c);
+        const int valid = p.n - (k0 + half * 32);
+        uint32_t vp[32], vg[32];
+        tmem_ld32(trow + 0 * PJ_TILE + half * 32, vp);
+        tmem_ld32(trow + 1 * PJ_TILE + half * 32, vg);
+        tmem_ld_wait();
+        store_gated(a_row + half * 32, vp, vg, mk, bap, bag, valid);
+        tmem_ld32(trow + 2 * PJ_TILE + half * 32, vp);
+        tmem_ld32(trow + 3 * PJ_TILE + half * 32, vg);
+        tmem_ld_wait();
+        store_gated(b_row + half * 32, vp, vg, mk, bbp, bbg, valid);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acc_empty(buf));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Kernel 2: per-channel contraction X[h] = s * A[h] B[h]^T.
+// ---------------------------------------------------------------------------
+constexpr int CT_BM = 128, CT_BN = 256, CT_BK = 64, CT_STAGES = 4, CT_THREADS = 192;
+constexpr uint32_t CT_A_BYTES = CT_BM * 128, CT_B_BYTES = CT_BN * 128;
+constexpr uint32_t CT_STAGE_BYTES = CT_A_BYTES + CT_B_BYTES;
+constexpr uint32_t CT_OFF_BAR = CT_STAGES * CT_STAGE_BYTES;
+constexpr uint32_t CT_SMEM = CT_OFF_BAR + 256 + 1024;
+
+struct ContractArgs {
+  __half *x_out;  // [128][row_count][jp]
+  int64_t x_hs, x_rs;
+  int n, row_begin, row_count;
+  int tiles_m, tiles_n, k_blocks, total_tiles;
+  float scale;
+  unsigned int *err;
+};
+
+__global__ void __launch_bounds__(CT_THREADS, 1)
+    contract_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap bmap,
+                    const ContractArgs p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = align1024(smem_raw);
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bar0 = sbase + CT_OFF_BAR;
+  auto full = [&](int s) { return bar0 + 8u * s; };
+  auto empty = [&](int s) { return bar0 + 8u * (CT_STAGES + s); };
+  auto acc_full = [&](int b) { return bar0 + 8u * (2 * CT_STAGES + b); };
+  auto acc_empty = [&](int b) { return bar0 + 8u * (2 * CT_STAGES + 2 + b); };
+  const uint32_t drain = bar0 + 8u * (2 * CT_STAGES + 4);
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + CT_OFF_BAR + 128);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + CT_OFF_BAR + 136);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tiles_per_h = p.tiles_m * p.tiles_n;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < CT_STAGES; ++s) {
+      mbar_init(full(s), 1);
+      mbar_init(empty(s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(acc_full(b), 1);
+      mbar_init(acc_empty(b), 4);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_map(&amap);
+      tma_prefetch_map(&bmap);
+      int it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
+        const int h = t / tiles_per_h, rem = t % tiles_per_h;
+        const int mi = rem / p.tiles_n, ni = rem % p.tiles_n;
+        for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
+          const int s = it % CT_STAGES;
+          const uint32_t ph = (it / CT_STAGES) & 1;
+          if (!mbar_wait(empty(s), ph ^ 1, abort_flag, p.err, kErrWaitProducer)) {
+            ok = false;
+            break;
+          }
+          const uint32_t dst = sbase + s * CT_STAGE_BYTES;
+          mbar_arrive_expect_tx(full(s), CT_STAGE_BYTES);
+          tma_load_3d(dst, &amap, full(s), kb * CT_BK, p.row_begin + mi * CT_BM, h);
+          tma_load_3d(dst + CT_A_BYTES, &bmap, full(s), kb * CT_BK, ni * CT_BN, h);
+        }
+      }
+      if (!ok) {
+        for (int j = std::max(0, it - CT_STAGES); j < it; ++j)
+          mbar_wait_drain(full(j % CT_STAGES), (j / CT_STAGES) & 1, p.err);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t kIdesc = idesc_f16_f32(CT_BM, CT_BN);
+      int it = 0, tile_it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x, ++tile_it) {
+        const int buf = tile_it & 1;
+        const uint32_t bph = (tile_it >> 1) & 1;
+        if (!mbar_wait(acc_empty(buf), bph ^ 1, abort_flag, p.err, kErrWaitMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem + buf * CT_BN;
+        for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
+          const int s = it % CT_STAGES;
+          const uint32_t ph = (it / CT_STAGES) & 1;
+          if (!mbar_wait(full(s), ph, abort_flag, p.err, kErrWaitMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t as = sbase + s * CT_STAGE_BYTES, bs = as + CT_A_BYTES;
+#pragma unroll
+          for (int ks = 0; ks < CT_BK / 16; ++ks)
+            mma_f16(d, sdesc_k_sw128(as + ks * 32), sdesc_k_sw128(bs + ks * 32), kIdesc, (kb | ks) != 0);
+          mma_commit(empty(s));
+        }
+        if (ok) mma_commit(acc_full(buf));
+      }
+      if (!ok) {
+        mma_commit(drain);
+        mbar_wait_drain(drain, 0, p.err);
+      }
+    }
+    __syncwarp();
+  } else {
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    int tile_it = 0;
+    for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x, ++tile_it) {
+      const int h = t / tiles_per_h, rem = t % tiles_per_h;
+      const int mi = rem / p.tiles_n, ni = rem % p.tiles_n;
+      const int buf = tile_it & 1;
+      const uint32_t bph = (tile_it >> 1) & 1;
+      if (!warp_wait(acc_full(buf), bph, abort_flag, p.err, kErrWaitEpilogue)) break;
+      tc_fence_after();
+      const int gi = mi * CT_BM + row;  // row inside this block
+      const bool row_ok = gi < p.row_count;
+      const int j0 = ni * CT_BN;
+      const bool full_cols = j0 + CT_BN <= p.n;
+      __half *xr = p.x_out + h * p.x_hs + (int64_t)gi * p.x_rs + j0;
+      const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * CT_BN;
+#pragma unroll 1
+      for (int chunk = 0; chunk < CT_BN / 32; ++chunk) {
+        uint32_t v[32];
+        tmem_ld32(taddr + chunk * 32, v);
+        tmem_ld_wait();
+        uint32_t pk[16];
+#pragma unroll
+        for (int c = 0; c < 32; c += 2)
+          pk[c >> 1] = pack_half2(__uint_as_float(v[c]) * p.scale, __uint_as_float(v[c + 1]) * p.scale);
+        if (row_ok) {
+          if (full_cols) {
+            uint4 *d = reinterpret_cast<uint4 *>(xr + chunk * 32);
+#pragma unroll
+            for (int w = 0; w < 4; ++w) d[w] = make_uint4(pk[4 * w], pk[4 * w + 1], pk[4 * w + 2], pk[4 * w + 3]);
+          } else {
+            const __half *hv = reinterpret_cast<const __half *>(pk);
+            for (int c = 0; c < 32; ++c)
+              if (j0 + chunk * 32 + c < p.n) xr[chunk * 32 + c] = hv[c];
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acc_empty(buf));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Kernel 3: LN_out + output projection + gate + residual.
+// ---------------------------------------------------------------------------
+constexpr int OP_STAGES = 2, OP_THREADS = 320;
+constexpr uint32_t OP_W_BYTES = 2 * 2 * 16384;                 // W_z, W_g
+constexpr uint32_t OP_X_BYTES = 128 * 256, OP_Z_BYTES = 128 * 256;
+constexpr uint32_t OP_STAGE_BYTES = OP_X_BYTES + OP_Z_BYTES;
+constexpr uint32_t OP_OFF_STAGE = OP_W_BYTES;
+constexpr uint32_t OP_OFF_VEC = OP_OFF_STAGE + OP_STAGES * OP_STAGE_BYTES;  // ln_out w/b, b_z, b_g
+constexpr uint32_t OP_OFF_BAR = OP_OFF_VEC + 4 * 512;
+constexpr uint32_t OP_SMEM = OP_OFF_BAR + 256 + 1024;
+
+struct OutputArgs {
+  void *out;
+  int64_t out_rs;  // elements per pair row (c_z)
+  const __half *w16;
+  const float *vec;
+  int n, cz, ch, row_begin, row_count, tiles_j, total_tiles, residual;
+  float eps_in, eps_out;
+  unsigned int *err;
+};
+
+template <typename OT>
+__device__ __forceinline__ void store_out_row(OT *row, const float (&v)[32], int zc0, int cz, int residual) {
+  if (cz == C) {
+    if constexpr (sizeof(OT) == 4) {
+      float4 *d = reinterpret_cast<float4 *>(row + zc0);
+#pragma unroll
+      for (int w = 0; w < 8; ++w) {
+        float4 o = make_float4(v[4 * w], v[4 * w + 1], v[4 * w + 2], v[4 * w + 3]);
+        if (residual) {
+          const float4 old = d[w];
+          o.x += old.x; o.y += old.y; o.z += old.z; o.w += old.w;
+        }
+        d[w] = o;
+      }
+    } else {
+      uint4 *d = reinterpret_cast<uint4 *>(row + zc0);
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        float x[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) x[i] = v[8 * w + i];
+        if (residual) {
+          float old[8];
+          unpack8<OT>(d[w], old);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) x[i] += old[i];
+        }
+        uint4 o;
+        OT *e = reinterpret_cast<OT *>(&o);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) e[i] = from_f32<OT>(x[i]);
+        d[w] = o;
+      }
+    }
+  } else {
+    for (int c = 0; c < 32; ++c) {
+      const int zc = zc0 + c;
+      if (zc < cz) {
+        float x = v[c];
+        if (residual) x += to_f32<OT>(row[zc]);
+        row[zc] = from_f32<OT>(x);
+      }
+    }
+  }
+}
+
+template <typename ZT, typename OT>
+__global__ void __launch_bounds__(OP_THREADS, 1)
+    output_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap zmap,
+                  const OutputArgs p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = align1024(smem_raw);
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bar0 = sbase + OP_OFF_BAR;
+  auto full = [&](int s) { return bar0 + 8u * s; };
+  auto ready = [&](int s) { return bar0 + 8u * (2 + s); };
+  auto empty = [&](int s) { return bar0 + 8u * (4 + s); };
+  auto acc_full = [&](int b) { return bar0 + 8u * (6 + b); };
+  auto acc_empty = [&](int b) { return bar0 + 8u * (8 + b); };
+  const uint32_t drain = bar0 + 8u * 10;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + OP_OFF_BAR + 128);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + OP_OFF_BAR + 136);
+  float *sv = reinterpret_cast<float *>(smem + OP_OFF_VEC);  // [0] ln_out w, [128] ln_out b, [256] b_z, [384] b_g
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  load_weight_matrix(smem, p.w16 + (size_t)kWZ * C * C, threadIdx.x, OP_THREADS);
+  load_weight_matrix(smem + 32768, p.w16 + (size_t)kWG * C * C, threadIdx.x, OP_THREADS);
+  for (int i = threadIdx.x; i < 4 * C; i += OP_THREADS) {
+    const int q = i / C, e = i % C;
+    const int src = q == 0 ? kVLnOutW : q == 1 ? kVLnOutB : q == 2 ? kVBZ : kVBG;
+    sv[i] = p.vec[src * C + e];
+  }
+  fence_async_smem();
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < OP_STAGES; ++s) {
+      mbar_init(full(s), 1);
+      mbar_init(ready(s), 4);
+      mbar_init(empty(s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(acc_full(b), 1);
+      mbar_init(acc_empty(b), 4);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_map(&xmap);
+      tma_prefetch_map(&zmap);
+      int it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x, ++it) {
+        const int s = it % OP_STAGES;
+        const uint32_t ph = (it / OP_STAGES) & 1;
+        if (!mbar_wait(empty(s), ph ^ 1, abort_flag, p.err, kErrWaitProducer)) {
+          ok = false;
+          break;
+        }
+        const int il = t / p.tiles_j, j0 = (t % p.tiles_j) * 128;
+        const uint32_t xs = sbase + OP_OFF_STAGE + s * OP_STAGE_BYTES, zs = xs + OP_X_BYTES;
+        mbar_arrive_expect_tx(full(s), OP_STAGE_BYTES);
+        tma_load_3d(xs, &xmap, full(s), j0, il, 0);
+        tma_load_3d(zs, &zmap, full(s), 0, j0, p.row_begin + il);
+        tma_load_3d(zs + 16384, &zmap, full(s), 64, j0, p.row_begin + il);
+      }
+      if (!ok) {
+        for (int j = std::max(0, it - OP_STAGES); j < it; ++j)
+          mbar_wait_drain(full(j % OP_STAGES), (j / OP_STAGES) & 1, p.err);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t kIdesc = idesc_f16_f32(128, 128);
+      int it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x, ++it) {
+        const int s = it % OP_STAGES;
+        const uint32_t ph = (it / OP_STAGES) & 1;
+        const int buf = it & 1;
+        const uint32_t bph = (it >> 1) & 1;
+        if (!mbar_wait(acc_empty(buf), bph ^ 1, abort_flag, p.err, kErrWaitMma) ||
+            !mbar_wait(ready(s), ph, abort_flag, p.err, kErrWaitMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t xs = sbase + OP_OFF_STAGE + s * OP_STAGE_BYTES, zs = xs + OP_X_BYTES;
+        const uint32_t d = tmem + buf * 256;
+#pragma unroll
+        for (int kc = 0; kc < 2; ++kc) {
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks) {
+            const uint32_t koff = kc * 16384 + ks * 32;
+            mma_f16(d, sdesc_k_sw128(xs + koff), sdesc_k_sw128(sbase + koff), kIdesc, (kc | ks) != 0);
+            mma_f16(d + 128, sdesc_k_sw128(zs + koff), sdesc_k_sw128(sbase + 32768 + koff), kIdesc,
+                    (kc | ks) != 0);
+          }
+        }
+        mma_commit(empty(s));
+        mma_commit(acc_full(buf));
+      }
+      if (!ok) {
+        mma_commit(drain);
+        mbar_wait_drain(drain, 0, p.err);
+      }
+    }
+    __syncwarp();
+  } else if (warp < 6) {
+    // ---- transpose + LN_out of X, LN_in of z ----
+    const int nw = warp - 2, pr = nw * 32 + lane;  // pair row of the tile this thread transposes
+    const int sub = lane >> 4, c16 = lane & 15;
+    float g[8], bt[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      g[i] = p.vec[kVLnInW * C + c16 * 8 + i];
+      bt[i] = p.vec[kVLnInB * C + c16 * 8 + i];
+    }
+    const float inv_cz = 1.f / static_cast<float>(p.cz), inv_ch = 1.f / static_cast<float>(p.ch);
+    int it = 0;
+    for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x, ++it) {
+      const int s = it % OP_STAGES;
+      const uint32_t ph = (it / OP_STAGES) & 1;
+      if (!warp_wait(full(s), ph, abort_flag, p.err, kErrWaitNormalizer)) break;
+      uint8_t *xs = smem + OP_OFF_STAGE + s * OP_STAGE_BYTES;
+      uint8_t *zs = xs + OP_X_BYTES;
+      // X arrives [h][pair] (256-byte rows); this thread owns column `pr`.
+      __half2 xv[64];
+      float sum = 0.f;
+#pragma unroll
+      for (int h2 = 0; h2 < 64; ++h2) {
+        const __half lo = *reinterpret_cast<const __half *>(xs + (2 * h2) * 256 + pr * 2);
+        const __half hi = *reinterpret_cast<const __half *>(xs + (2 * h2 + 1) * 256 + pr * 2);
+        xv[h2] = __halves2half2(lo, hi);
+        sum += __half2float(lo) + __half2float(hi);
+      }
+      const float mean = sum * inv_ch;
+      float sq = 0.f;
+#pragma unroll
+      for (int h2 = 0; h2 < 64; ++h2) {
+        const float2 f = __half22float2(xv[h2]);
+        const float d0 = f.x - mean, d1 = f.y - mean;
+        sq += (2 * h2 < p.ch ? d0 * d0 : 0.f) + (2 * h2 + 1 < p.ch ? d1 * d1 : 0.f);
+      }
+      const float rstd = rsqrtf(sq * inv_ch + p.eps_out);
+      named_barrier(1, 128);  // every column read before the tile is overwritten
+#pragma unroll
+      for (int cc = 0; cc < 16; ++cc) {
+        uint32_t w[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int hh = cc * 8 + 2 * i;
+          const float2 f = __half22float2(xv[cc * 4 + i]);
+          w[i] = pack_half2((f.x - mean) * rstd * sv[hh] + sv[C + hh],
+                            (f.y - mean) * rstd * sv[hh + 1] + sv[C + hh + 1]);
+        }
+        *reinterpret_cast<uint4 *>(xs + (cc >> 3) * 16384 + sw128_offset(pr, cc & 7)) =
+            make_uint4(w[0], w[1], w[2], w[3]);
+      }
+#pragma unroll 1
+      for (int pass = 0; pass < 16; ++pass)
+        ln_row_inplace<ZT>(zs, 16384, pass * 8 + nw * 2 + sub, c16, g, bt, p.cz, inv_cz, p.eps_in);
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(ready(s));
+    }
+  } else {
+    // ---- epilogue ----
+    const int q = warp & 3;
+    const int pr = q * 32 + lane;
+    int it = 0;
+    for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x, ++it) {
+      const int il = t / p.tiles_j, j = (t % p.tiles_j) * 128 + pr;
+      const int buf = it & 1;
+      const uint32_t bph = (it >> 1) & 1;
+      if (!warp_wait(acc_full(buf), bph, abort_flag, p.err, kErrWaitEpilogue)) break;
+      tc_fence_after();
+      const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * 256;
+      OT *orow = reinterpret_cast<OT *>(p.out) + ((int64_t)(p.row_begin + il) * p.n + j) * p.out_rs;
+#pragma unroll 1
+      for (int chunk = 0; chunk < 4; ++chunk) {
+        uint32_t vo[32], vg[32];
+        tmem_ld32(taddr + chunk * 32, vo);
+        tmem_ld32(taddr + 128 + chunk * 32, vg);
+        tmem_ld_wait();
+        float v[32];
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          const int zc = chunk * 32 + c;
+          v[c] = (__uint_as_float(vo[c]) + sv[2 * C + zc]) * sigmoidf(__uint_as_float(vg[c]) + sv[3 * C + zc]);
+        }
+        if (j < p.n) store_out_row<OT>(orow, v, chunk * 32, p.cz, p.residual);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acc_empty(buf));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace tri
+
+// ---------------------------------------------------------------------------
+// Host side.
+// ---------------------------------------------------------------------------
+
+TriangleLayout triangle_layout(int64_t n, int64_t cz, int64_t ch, int64_t block_rows, int z_dtype) {
+  TriangleLayout L;
+  L.n = n;
+  L.cz = cz;
+  L.ch = ch;
+  L.block_rows = (block_rows <= 0 || block_rows > n) ? n : block_rows;
+  L.kp = static_cast<int64_t>(align_up(static_cast<size_t>(n), 8));
+  L.jp = L.kp;
+  L.pad_z = (z_dtype == AF2_F32) || cz != tri::C;
+  size_t off = 0;
+  L.off_w16 = off;
+  off = align_up(off + sizeof(__half) * tri::kMatCount * tri::C * tri::C, 256);
+  L.off_vec = off;
+  off = align_up(off + sizeof(float) * tri::kVecCount * tri::C, 256);
+  L.off_z16 = off;
+  if (L.pad_z) off = align_up(off + sizeof(__half) * (size_t)n * n * tri::C, 256);
+  L.off_a = off;
+  off = align_up(off + sizeof(__half) * (size_t)tri::C * n * L.kp, 256);
+  L.off_b = off;
+  off = align_up(off + sizeof(__half) * (size_t)tri::C * n * L.kp, 256);
+  L.off_x = off;
+  off = align_up(off + sizeof(__half) * (size_t)tri::C * L.block_rows * L.jp, 256);
+  L.total = off;
+  return L;
+}
+
+namespace {
+
+CUtensorMapDataType map_type(int dtype) {
+  return dtype == AF2_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+}
+
+template <typename ZT>
+af2_status launch_project(af2_ctx *ctx, const CUtensorMap &zmap, const tri::ProjectArgs &a, cudaStream_t stream) {
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(tri::project_kernel<ZT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         tri::PJ_SMEM);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "configure project kernel");
+    configured = true;
+  }
+  const int grid = std::max(1, std::min(a.total_tiles, ctx->sm_count));
+  tri::project_kernel<ZT><<<grid, tri::PJ_THREADS, tri::PJ_SMEM, stream>>>(zmap, a);
+  ctx->launches++;
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? AF2_OK : cuda_fail(ctx, e, "launch project kernel");
+}
+
+template <typename ZT, typename OT>
+af2_status launch_output(af2_ctx *ctx, const CUtensorMap &xmap, const CUtensorMap &zmap, const tri::OutputArgs &a,
+                         cudaStream_t stream) {
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(tri::output_kernel<ZT, OT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         tri::OP_SMEM);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "configure output kernel");
+    configured = true;
+  }
+  const int grid = std::max(1, std::min(a.total_tiles, ctx->sm_count));
+  tri::output_kernel<ZT, OT><<<grid, tri::OP_THREADS, tri::OP_SMEM, stream>>>(xmap, zmap, a);
+  ctx->launches++;
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? AF2_OK : cuda_fail(ctx, e, "launch output kernel");
+}
+
+template <typename ZT>
+af2_status launch_output_any(af2_ctx *ctx, int out_dtype, const CUtensorMap &xmap, const CUtensorMap &zmap,
+                             const tri::OutputArgs &a, cudaStream_t stream) {
+  switch (out_dtype) {
+    case AF2_F32: return launch_output<ZT, float>(ctx, xmap, zmap, a, stream);
+    case AF2_F16: return launch_output<ZT, __half>(ctx, xmap, zmap, a, stream);
+    default: return launch_output<ZT, __nv_bfloat16>(ctx, xmap, zmap, a, stream);
+  }
+}
+
+}  // namespace
+
+af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L, const void *z, int z_dtype,
+                           const float *mask, const float *packed, double eps, int residual, void *out,
+                           int out_dtype, void *workspace, cudaStream_t stream) {
+  using namespace tri;
+  uint8_t *ws = static_cast<uint8_t *>(workspace);
+  __half *w16 = reinterpret_cast<__half *>(ws + L.off_w16);
+  float *vec = reinterpret_cast<float *>(ws + L.off_vec);
+  __half *a = reinterpret_cast<__half *>(ws + L.off_a);
+  __half *b = reinterpret_cast<__half *>(ws + L.off_b);
+  __half *x = reinterpret_cast<__half *>(ws + L.off_x);
+  const int n = static_cast<int>(L.n);
+  const int64_t pairs = L.n * L.n;
+
+  prep_weights_kernel<<<96, 256, 0, stream>>>(packed, (int)L.cz, (int)L.ch, w16, vec);
+  ctx->launches++;
+  if (cudaError_t e = cudaGetLastError(); e != cudaSuccess) return cuda_fail(ctx, e, "launch weight preparation");
+
+  const void *zsrc = z;
+  int zt = z_dtype;
+  if (L.pad_z) {
+    __half *z16 = reinterpret_cast<__half *>(ws + L.off_z16);
+    const int grid = static_cast<int>(std::min<int64_t>((pairs * C + 255) / 256, 8 * 1024));
+    switch (z_dtype) {
+      case AF2_F32: pad_z_kernel<float><<<grid, 256, 0, stream>>>(static_cast<const float *>(z), pairs, (int)L.cz, z16); break;
+      case AF2_F16: pad_z_kernel<__half><<<grid, 256, 0, stream>>>(static_cast<const __half *>(z), pairs, (int)L.cz, z16); break;
+      default: pad_z_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(static_cast<const __nv_bfloat16 *>(z), pairs, (int)L.cz, z16); break;
+    }
+    ctx->launches++;
+    if (cudaError_t e = cudaGetLastError(); e != cudaSuccess) return cuda_fail(ctx, e, "launch z re-layout");
+    zsrc = z16;
+    zt = AF2_F16;
+  }
+
+  // ---- projections ----
+  const uint64_t row_bytes = C * 2;  // one pair row of the 128-channel z
+  CUtensorMap zmap_proj;
+  const bool out_dir = direction == AF2_OUTGOING;
+  // Tile rows are pairs (r, k0..k0+63) outgoing and (k0..k0+63, r) incoming.  Both maps
+  // describe z in its natural [row][col][c] order; the incoming box is one column wide
+  // and 64 rows tall, which lands the same [64 rows][128 B] tile in shared memory.
+  if (!encode_map_3d(&zmap_proj, map_type(zt), zsrc, C, L.n, L.n, row_bytes, row_bytes * L.n, 64,
+                     out_dir ? PJ_TILE : 1, out_dir ? 1 : PJ_TILE, CU_TENSOR_MAP_SWIZZLE_128B))
+    return fail(ctx, AF2_ERR_CUDA, "cuTensorMapEncodeTiled failed for the projection's z map");
+  ProjectArgs pa;
+  pa.mask = mask;
+  pa.mask_rs = out_dir ? L.n : 1;
+  pa.mask_ks = out_dir ? 1 : L.n;
+  pa.a_out = a;
+  pa.b_out = b;
+  pa.out_hs = L.n * L.kp;
+  pa.out_rs = L.kp;
+  pa.w16 = w16;
+  pa.vec = vec;
+  pa.n = n;
+  pa.cz = (int)L.cz;
+  pa.tiles_k = (n + PJ_TILE - 1) / PJ_TILE;
+  pa.total_tiles = n * pa.tiles_k;
+  pa.transposed = out_dir ? 0 : 1;
+  pa.eps = static_cast<float>(eps);
+  pa.err = ctx->err_word;
+  af2_status st = zt == AF2_BF16 ? launch_project<__nv_bfloat16>(ctx, zmap_proj, pa, stream)
+                                 : launch_project<__half>(ctx, zmap_proj, pa, stream);
+  if (st != AF2_OK) return st;
+
+  // ---- per block of output rows: contraction, then output ----
+  const __half *m_op = out_dir ? a : b;  // rows i of the product
+  const __half *n_op = out_dir ? b : a;  // rows j of the product
+  CUtensorMap amap, bmap, zmap_out;
+  if (!encode_map_3d(&amap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, m_op, L.n, L.n, C, L.kp * 2, L.n * L.kp * 2, CT_BK,
+                     CT_BM, 1, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_map_3d(&bmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, n_op, L.n, L.n, C, L.kp * 2, L.n * L.kp * 2, CT_BK,
+                     CT_BN, 1, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_map_3d(&zmap_out, map_type(zt), zsrc, C, L.n, L.n, row_bytes, row_bytes * L.n, 64, 128, 1,
+                     CU_TENSOR_MAP_SWIZZLE_128B))
+    return fail(ctx, AF2_ERR_CUDA, "cuTensorMapEncodeTiled failed for the contraction maps");
+  static bool contract_configured = false;
+  if (!contract_configured) {
+    cudaError_t e = cudaFuncSetAttribute(contract_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, CT_SMEM);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "configure contraction kernel");
+    contract_configured = true;
+  }
+  for (int64_t rb = 0; rb < L.n; rb += L.block_rows) {
+    const int rc = static_cast<int>(std::min<int64_t>(L.block_rows, L.n - rb));
+    ContractArgs ca;
+    ca.x_out = x;
+    ca.x_hs = (int64_t)rc * L.jp;
+    ca.x_rs = L.jp;
+    ca.n = n;
+    ca.row_begin = static_cast<int>(rb);
+    ca.row_count = rc;
+    ca.tiles_m = (rc + CT_BM - 1) / CT_BM;
+    ca.tiles_n = (n + CT_BN - 1) / CT_BN;
+    ca.k_blocks = (n + CT_BK - 1) / CT_BK;
+    ca.total_tiles = C * ca.tiles_m * ca.tiles_n;
+    ca.scale = 1.0f / static_cast<float>(n);
+    ca.err = ctx->err_word;
+    const int grid = std::max(1, std::min(ca.total_tiles, ctx->sm_count));
+    contract_kernel<<<grid, CT_THREADS, CT_SMEM, stream>>>(amap, bmap, ca);
+    ctx->launches++;
+    if (cudaError_t e = cudaGetLastError(); e != cudaSuccess) return cuda_fail(ctx, e, "launch contraction");
+
+    CUtensorMap xmap;
+    if (!encode_map_3d(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x, L.n, rc, C, L.jp * 2, (uint64_t)rc * L.jp * 2,
+                       128, 1, C, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return fail(ctx, AF2_ERR_CUDA, "cuTensorMapEncodeTiled failed for the contracted block");
+    OutputArgs oa;
+    oa.out = out;
+    oa.out_rs = L.cz;
+    oa.w16 = w16;
+    oa.vec = vec;
+    oa.n = n;
+    oa.cz = (int)L.cz;
+    oa.ch = (int)L.ch;
+    oa.row_begin = static_cast<int>(rb);
+    oa.row_count = rc;
+    oa.tiles_j = (n + 127) / 128;
+    oa.total_tiles = rc * oa.tiles_j;
+    oa.residual = residual;
+    oa.eps_in = static_cast<float>(eps);
+    oa.eps_out = static_cast<float>(eps / ((double)n * (double)n));
+    oa.err = ctx->err_word;
+    st = zt == AF2_BF16 ? launch_output_any<__nv_bfloat16>(ctx, out_dtype, xmap, zmap_out, oa, stream)
+                        : launch_output_any<__half>(ctx, out_dtype, xmap, zmap_out, oa, stream);
+    if (st != AF2_OK) return st;
+  }
+  return AF2_OK;
+}
+
+}  // namespace af2

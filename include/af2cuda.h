@@ -1,0 +1,167 @@
+/*
+ * af2cuda.h -- C ABI of libaf2cuda.so, the B200 (sm_100a) implementation of
+ * the Evoformer pair-stack contractions of alphafold2-webgpu.
+ *
+ * Every entry point is plain C: opaque handles, plain pointers, sizes and
+ * enums, no exceptions.  Each returns an af2_status; af2_last_error() gives
+ * the message of the last failure on a context.
+ *
+ * Two call forms mirror the reference's two layers (all paths relative to the
+ * reference repository):
+ *
+ *   host form   -- mirrors the standalone operator classes, whose run() takes
+ *                  host Float32Arrays, uploads them, runs, reads back and
+ *                  returns a fresh Float32Array plus timing
+ *                  (src/triangle/webgpu.ts:56-201,
+ *                   src/evoformer/outer-product-mean.ts:549-646,
+ *                   src/evoformer/transition.ts:264-361);
+ *   device form -- mirrors the in-model encoders on device-resident tensors,
+ *                  with an optional residual add into the output
+ *                  (src/evoformer/block.ts:1497-1671, :1115-1246, :625-740).
+ *
+ * Tensor layouts are the reference's: row-major, pair tensors [N, N, C],
+ * triangle weights [out, in] (src/triangle/types.ts:9-26), OPM and transition
+ * weights [in, out] (outer-product-mean.ts:10-19, transition.ts:9-16), packed
+ * in the reference's orders (src/triangle/weights.ts:4-10,
+ * outer-product-mean.ts:68-72, transition.ts:140-177).
+ *
+ * Arithmetic: operands are rounded to f16 (bf16-range activations are
+ * normalised first) and multiplied on the tcgen05 tensor cores with f32
+ * accumulation; LayerNorm statistics, gating and bias terms are f32.
+ *
+ * Threading: one context per device; calls on one context are serialised by
+ * the caller.  Device-form calls are asynchronous on the given stream
+ * (NULL = the context's stream); af2_sync() waits and reports any
+ * device-side failure flagged by the kernels.
+ */
+#ifndef AF2CUDA_H
+#define AF2CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define AF2CUDA_VERSION 1
+
+#if defined(__GNUC__)
+#define AF2_API __attribute__((visibility("default")))
+#else
+#define AF2_API
+#endif
+
+typedef struct af2_ctx af2_ctx;
+
+typedef enum af2_status {
+    AF2_OK = 0,
+    /* A shape, length or epsilon the reference rejects with RangeError
+     * (src/triangle/types.ts:42-89, outer-product-mean.ts:45-65). */
+    AF2_ERR_INVALID_ARGUMENT = 1,
+    /* A valid shape outside what the kernels cover (for example c_z > 128). */
+    AF2_ERR_UNSUPPORTED = 2,
+    /* Device allocation failed (GpuMemoryBudgetError, runtime/allocator.ts:76-90). */
+    AF2_ERR_OUT_OF_MEMORY = 3,
+    /* A CUDA runtime error ("WebGPU validation failed", triangle/webgpu.ts:191-192). */
+    AF2_ERR_CUDA = 4,
+    /* A kernel's bounded wait ran out; the kernel returned without finishing. */
+    AF2_ERR_DEVICE_TIMEOUT = 5,
+    /* An NCCL call failed or a rank did not answer. */
+    AF2_ERR_NCCL = 6,
+    /* No CUDA device, or the device is not sm_100. */
+    AF2_ERR_NO_DEVICE = 7
+} af2_status;
+
+typedef enum af2_dtype { AF2_F32 = 0, AF2_F16 = 1, AF2_BF16 = 2 } af2_dtype;
+
+typedef enum af2_direction { AF2_OUTGOING = 0, AF2_INCOMING = 1 } af2_direction;
+
+/* TriangleShape, src/triangle/types.ts:3-7. */
+typedef struct af2_triangle_shape {
+    int64_t length;
+    int64_t c_z;
+    int64_t c_hidden;
+} af2_triangle_shape;
+
+/* TriangleGpuOptions, src/triangle/webgpu.ts:9-15, plus the encoder's residual. */
+typedef struct af2_triangle_options {
+    /* Output rows per block; 0 = the whole length.  Bounds the contracted
+     * scratch only: results are bit-identical for every value. */
+    int32_t block_rows;
+    /* 1: out += update (encodeTriangleMultiplication with residualTarget). */
+    int32_t residual;
+} af2_triangle_options;
+
+/* What a call cost: the counterpart of {elapsedMilliseconds, memory}. */
+typedef struct af2_op_stats {
+    double device_milliseconds; /* CUDA-event time of the kernels */
+    double host_milliseconds;   /* host form: copies in, kernels, copy out */
+    double flops;               /* algorithmic FLOPs (src/runtime/kernel-cost.ts:71-162) */
+    uint64_t workspace_bytes;   /* scratch the call used */
+    uint64_t peak_bytes;        /* context's device allocation high-water mark */
+} af2_op_stats;
+
+/* ---- context --------------------------------------------------------- */
+
+/* Opens device `device_ordinal` (replaces requestAlphaFoldDevice, runtime/device.ts:375). */
+AF2_API af2_status af2_create(int device_ordinal, af2_ctx **out);
+AF2_API void af2_destroy(af2_ctx *ctx);
+AF2_API const char *af2_last_error(const af2_ctx *ctx);
+AF2_API const char *af2_status_string(af2_status status);
+AF2_API int af2_version(void);
+/* Waits for `stream` (NULL = context stream) and reports kernel-side failures. */
+AF2_API af2_status af2_sync(af2_ctx *ctx, void *stream);
+/* Number of kernels this context has launched (monotonic). */
+AF2_API uint64_t af2_launch_count(const af2_ctx *ctx);
+
+/* ---- triangle multiplication ------------------------------------------ */
+
+/* expectedWeightElementCount, src/triangle/weights.ts:36-40. */
+AF2_API int64_t af2_triangle_weight_count(int64_t c_z, int64_t c_hidden);
+
+/*
+ * validateTriangleInput (src/triangle/types.ts:54-89) for what a C caller
+ * passes: positive safe-integer dimensions, the packed weight count, a finite
+ * positive epsilon; then the kernels' own limits.  Needs no device.  The
+ * message (NUL-terminated, truncated to `capacity`) may be NULL.
+ */
+AF2_API af2_status af2_triangle_check(int direction, const af2_triangle_shape *shape, int64_t weight_count, double epsilon,
+                              char *message, size_t capacity);
+
+/* Scratch bytes the device form needs for this shape and options. */
+AF2_API af2_status af2_triangle_workspace_bytes(const af2_triangle_shape *shape,
+                                        const af2_triangle_options *options, uint64_t *bytes);
+
+/*
+ * Host form of TriangleMultiplication{Outgoing,Incoming}Gpu.run
+ * (src/triangle/webgpu.ts:56-201, classes :204-214).
+ * z [N,N,c_z] and out [N,N,c_z] are host arrays of `io_dtype` (AF2_F32 is the
+ * reference's Float32Array); mask [N,N] f32; packed_weights f32 in ORDER with
+ * weight_count = af2_triangle_weight_count(c_z, c_hidden).  Host buffers may
+ * be pageable or pinned.  options may be NULL; stats may be NULL.
+ */
+AF2_API af2_status af2_triangle_multiplication_host(af2_ctx *ctx, int direction, const af2_triangle_shape *shape,
+                                            const void *z, const float *mask, const float *packed_weights,
+                                            int64_t weight_count, double epsilon,
+                                            const af2_triangle_options *options, int io_dtype, void *out,
+                                            af2_op_stats *stats);
+
+/*
+ * Device form: encodeTriangleMultiplication (src/evoformer/block.ts:1497-1671).
+ * All pointers are device pointers.  z has z_dtype, out has out_dtype; with
+ * options->residual = 1 the update is added into out (pass out == z to update
+ * the pair in place).  workspace: NULL = context-owned scratch, else at least
+ * af2_triangle_workspace_bytes() bytes, 256-byte aligned.
+ */
+AF2_API af2_status af2_triangle_multiplication(af2_ctx *ctx, int direction, const af2_triangle_shape *shape,
+                                       const void *z, int z_dtype, const float *mask,
+                                       const float *packed_weights, int64_t weight_count, double epsilon,
+                                       const af2_triangle_options *options, void *out, int out_dtype,
+                                       void *workspace, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* AF2CUDA_H */

@@ -1,0 +1,127 @@
+"""CPU tests of the C ABI: the library loads, exports every symbol the header
+declares, and its host-side logic (validation, sizing) behaves like the
+reference's.  No kernel runs here."""
+import ctypes
+import re
+import subprocess
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+import af2cuda
+from af2cuda import _lib
+from conftest import ROOT, bundle_path
+
+HEADER = ROOT / "include" / "af2cuda.h"
+
+
+def declared_symbols() -> list[str]:
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    return sorted(set(re.findall(r"\b(af2_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.lib()
+    names = declared_symbols()
+    assert len(names) >= 10
+    for name in names:
+        assert hasattr(lib, name), name
+    # ...and the ctypes table covers exactly the header.
+    assert sorted(_lib.SIGNATURES) == names
+    exported = subprocess.run(["nm", "-D", "--defined-only", str(_lib.LIB_PATH)], capture_output=True, text=True).stdout
+    public = sorted(set(re.findall(r"\bT (af2_[a-z0-9_]+)$", exported, flags=re.M)))
+    assert public == names
+
+
+def test_build_targets_sm100a_only():
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("af2_build", ROOT / "alphafold2-webgpu_b200" / "build.py")
+    build = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(build)
+    assert build.ARCH == ["-gencode", "arch=compute_100a,code=sm_100a"]
+
+
+def test_version_and_status_strings():
+    lib = _lib.lib()
+    assert lib.af2_version() == 1
+    assert lib.af2_status_string(_lib.AF2_ERR_INVALID_ARGUMENT) == b"invalid argument"
+    assert lib.af2_status_string(99) == b"unknown status"
+
+
+def test_weight_count_matches_reference_formula():
+    for cz, ch in [(7, 6), (128, 128), (64, 64), (1, 1)]:
+        expected = af2cuda.expected_weight_element_count(af2cuda.TriangleShape(1, cz, ch))
+        assert af2cuda.triangle_weight_count(cz, ch) == expected
+    assert af2cuda.triangle_weight_count(128, 128) == 99_584  # packWeights at c = 128
+
+
+def _check(direction, n, cz, ch, count=None, eps=1e-5):
+    shape = _lib.TriangleShape(n, cz, ch)
+    msg = ctypes.create_string_buffer(256)
+    if count is None:
+        count = af2cuda.triangle_weight_count(max(cz, 1), max(ch, 1))
+    st = _lib.lib().af2_triangle_check(direction, ctypes.byref(shape), count, eps, msg, 256)
+    return st, msg.value.decode()
+
+
+def test_c_validation_mirrors_validate_triangle_input():
+    assert _check(0, 5, 7, 6) == (0, "")
+    assert _check(1, 1024, 128, 128)[0] == 0
+    st, msg = _check(0, 0, 7, 6)
+    assert st == _lib.AF2_ERR_INVALID_ARGUMENT and msg == "length must be a positive safe integer; received 0"
+    st, msg = _check(0, 5, -1, 6)
+    assert st == _lib.AF2_ERR_INVALID_ARGUMENT and "cZ must be a positive safe integer" in msg
+    st, msg = _check(0, 5, 7, 6, count=10)
+    assert st == _lib.AF2_ERR_INVALID_ARGUMENT and msg == "packed weights have 10 values; expected 323"
+    for eps in (0.0, -1.0, float("inf"), float("nan")):
+        assert _check(0, 5, 7, 6, eps=eps)[0] == _lib.AF2_ERR_INVALID_ARGUMENT
+    assert _check(2, 5, 7, 6)[0] == _lib.AF2_ERR_INVALID_ARGUMENT
+    assert _check(0, 2**27, 128, 128)[1] == "tensor dimensions exceed JavaScript's safe integer range"
+    # valid for the reference, beyond the kernels
+    assert _check(0, 5, 256, 128)[0] == _lib.AF2_ERR_UNSUPPORTED
+
+
+def test_python_validation_mirrors_reference():
+    bundle = af2cuda.load_triangle_reference_bundle_from_files(bundle_path("openfold-triangle-small"))
+    inp = bundle.input
+    af2cuda.validate_triangle_input(inp)
+    bad = af2cuda.TriangleMultiplicationInput(inp.shape, inp.z[1:], inp.mask, inp.weights)
+    with pytest.raises(af2cuda.RangeError, match="z has"):
+        af2cuda.validate_triangle_input(bad)
+    with pytest.raises(af2cuda.RangeError, match="epsilon must be finite and positive"):
+        af2cuda.validate_triangle_input(af2cuda.TriangleMultiplicationInput(inp.shape, inp.z, inp.mask,
+                                                                            inp.weights, epsilon=0.0))
+    with pytest.raises(af2cuda.RangeError, match="length must be a positive safe integer"):
+        af2cuda.validate_triangle_input(af2cuda.TriangleMultiplicationInput(
+            af2cuda.TriangleShape(0, 7, 6), inp.z, inp.mask, inp.weights))
+
+
+def test_workspace_bytes_scale_with_block_rows():
+    whole = af2cuda.triangle_workspace_bytes(1024, 128, 128)
+    blocked = af2cuda.triangle_workspace_bytes(1024, 128, 128, block_rows=128)
+    # a, b and the z re-layout stay; the contracted block shrinks 8x.
+    assert whole - blocked == 128 * (1024 - 128) * 1024 * 2
+    assert whole < 1.2e9
+
+
+def test_no_device_is_reported_not_faked():
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    handle = ctypes.c_void_p()
+    assert _lib.lib().af2_create(0, ctypes.byref(handle)) == _lib.AF2_ERR_NO_DEVICE
+    with pytest.raises(af2cuda.Af2Error):
+        af2cuda.Device(0)
+
+
+def test_loader_fails_loudly_without_the_library(tmp_path, monkeypatch):
+    import importlib
+    monkeypatch.setenv("AF2CUDA_LIBRARY", str(tmp_path / "missing.so"))
+    mod = importlib.reload(_lib)
+    try:
+        with pytest.raises(OSError, match="libaf2cuda.so not found"):
+            mod.lib()
+    finally:
+        monkeypatch.delenv("AF2CUDA_LIBRARY")
+        importlib.reload(_lib)
