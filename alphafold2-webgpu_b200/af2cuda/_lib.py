@@ -52,6 +52,10 @@ SIGNATURES = {
     "af2_last_error": (ctypes.c_char_p, [_vp]),
     "af2_sync": (_i32, [_vp, _vp]),
     "af2_launch_count": (ctypes.c_uint64, [_vp]),
+    "af2_profile_enable": (_i32, [_vp, _i32]),
+    "af2_profile_reset": (_i32, [_vp]),
+    "af2_profile_kernel_name": (ctypes.c_char_p, [_i32]),
+    "af2_profile_read": (_i32, [_vp, ctypes.c_char_p, ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(_f64)]),
     "af2_triangle_weight_count": (_i64, [_i64, _i64]),
     "af2_triangle_check": (_i32, [_i32, ctypes.POINTER(TriangleShape), _i64, _f64, ctypes.c_char_p, ctypes.c_size_t]),
     "af2_triangle_workspace_bytes": (_i32, [ctypes.POINTER(TriangleShape), ctypes.POINTER(TriangleOptions),

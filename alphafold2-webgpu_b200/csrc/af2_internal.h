@@ -7,6 +7,7 @@
 #include <stdint.h>
 
 #include <string>
+#include <vector>
 
 #include "../../include/af2cuda.h"
 
@@ -20,6 +21,24 @@ struct DeviceBuffer {
 
 }  // namespace af2
 
+namespace af2 {
+// Kernels the per-launch profiler distinguishes (labels follow the reference's
+// dispatch labels, src/runtime/kernel-cost.ts:158-162).
+enum ProfileKernel {
+  kProfTrianglePrepare = 0,
+  kProfTriangleRelayout,
+  kProfTriangleProject,
+  kProfTriangleContract,
+  kProfTriangleOutput,
+  kProfCount
+};
+const char *profile_name(int id);
+struct ProfilePending {
+  int id;
+  cudaEvent_t start, stop;
+};
+}  // namespace af2
+
 struct af2_ctx {
   int device = 0;
   int sm_count = 0;
@@ -29,6 +48,11 @@ struct af2_ctx {
   af2::DeviceBuffer staging[4];      // host-form device copies (z, mask, weights, out)
   cudaEvent_t ev_start = nullptr, ev_stop = nullptr;
   uint64_t launches = 0;
+  bool profiling = false;
+  std::vector<cudaEvent_t> free_events;
+  std::vector<af2::ProfilePending> pending;
+  uint64_t prof_launches[af2::kProfCount] = {};
+  double prof_ms[af2::kProfCount] = {};
   uint64_t allocated = 0, peak = 0;
   std::string last_error;
 };
@@ -48,6 +72,22 @@ bool encode_map_3d(CUtensorMap *map, CUtensorMapDataType dtype, const void *base
                    uint32_t b2, CUtensorMapSwizzle swizzle);
 
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Brackets one kernel launch with CUDA events on its stream while the
+// context's profiler is on; counts the launch either way.
+class LaunchScope {
+ public:
+  LaunchScope(af2_ctx *ctx, cudaStream_t stream, int id);
+  ~LaunchScope();
+  LaunchScope(const LaunchScope &) = delete;
+  LaunchScope &operator=(const LaunchScope &) = delete;
+
+ private:
+  af2_ctx *ctx_;
+  cudaStream_t stream_;
+  int id_;
+  cudaEvent_t start_ = nullptr;
+};
 
 // ---- triangle multiplication (triangle.cu) ----
 

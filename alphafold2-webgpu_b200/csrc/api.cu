@@ -49,6 +49,42 @@ af2_status ensure(af2_ctx *ctx, DeviceBuffer &buf, size_t bytes, const char *wha
   return AF2_OK;
 }
 
+const char *profile_name(int id) {
+  static const char *names[kProfCount] = {"triangle.prepare", "triangle.relayout", "triangle.project",
+                                          "triangle.contract", "triangle.output"};
+  return (id >= 0 && id < kProfCount) ? names[id] : nullptr;
+}
+
+static cudaEvent_t take_event(af2_ctx *ctx) {
+  if (!ctx->free_events.empty()) {
+    cudaEvent_t e = ctx->free_events.back();
+    ctx->free_events.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
+  return e;
+}
+
+LaunchScope::LaunchScope(af2_ctx *ctx, cudaStream_t stream, int id) : ctx_(ctx), stream_(stream), id_(id) {
+  ctx_->launches++;
+  if (ctx_->profiling) {
+    start_ = take_event(ctx_);
+    if (start_) cudaEventRecord(start_, stream_);
+  }
+}
+
+LaunchScope::~LaunchScope() {
+  if (!start_) return;
+  cudaEvent_t stop = take_event(ctx_);
+  if (!stop) {
+    ctx_->free_events.push_back(start_);
+    return;
+  }
+  cudaEventRecord(stop, stream_);
+  ctx_->pending.push_back({id_, start_, stop});
+}
+
 namespace {
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 std::once_flag g_encode_once;
@@ -187,6 +223,11 @@ void af2_destroy(af2_ctx *ctx) {
   for (auto &s : ctx->staging)
     if (s.ptr) cudaFree(s.ptr);
   if (ctx->err_word) cudaFree(ctx->err_word);
+  for (const ProfilePending &p : ctx->pending) {
+    cudaEventDestroy(p.start);
+    cudaEventDestroy(p.stop);
+  }
+  for (cudaEvent_t e : ctx->free_events) cudaEventDestroy(e);
   if (ctx->ev_start) cudaEventDestroy(ctx->ev_start);
   if (ctx->ev_stop) cudaEventDestroy(ctx->ev_stop);
   if (ctx->stream) cudaStreamDestroy(ctx->stream);
@@ -204,6 +245,54 @@ af2_status af2_sync(af2_ctx *ctx, void *stream) {
   cudaError_t e = cudaStreamSynchronize(s);
   if (e != cudaSuccess) return cuda_fail(ctx, e, "stream synchronize");
   return check_device_errors(ctx);
+}
+
+af2_status af2_profile_enable(af2_ctx *ctx, int enable) {
+  if (!ctx) return AF2_ERR_INVALID_ARGUMENT;
+  ctx->profiling = enable != 0;
+  return AF2_OK;
+}
+
+static af2_status profile_fold(af2_ctx *ctx) {
+  cudaSetDevice(ctx->device);
+  for (const ProfilePending &p : ctx->pending) {
+    cudaError_t e = cudaEventSynchronize(p.stop);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "profile event");
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, p.start, p.stop);
+    ctx->prof_launches[p.id]++;
+    ctx->prof_ms[p.id] += ms;
+    ctx->free_events.push_back(p.start);
+    ctx->free_events.push_back(p.stop);
+  }
+  ctx->pending.clear();
+  return AF2_OK;
+}
+
+af2_status af2_profile_reset(af2_ctx *ctx) {
+  if (!ctx) return AF2_ERR_INVALID_ARGUMENT;
+  af2_status st = profile_fold(ctx);
+  for (int i = 0; i < kProfCount; ++i) {
+    ctx->prof_launches[i] = 0;
+    ctx->prof_ms[i] = 0;
+  }
+  return st;
+}
+
+const char *af2_profile_kernel_name(int index) { return profile_name(index); }
+
+af2_status af2_profile_read(af2_ctx *ctx, const char *kernel, uint64_t *launches, double *milliseconds) {
+  if (!ctx || !kernel || !launches || !milliseconds) return AF2_ERR_INVALID_ARGUMENT;
+  af2_status st = profile_fold(ctx);
+  if (st != AF2_OK) return st;
+  for (int i = 0; i < kProfCount; ++i) {
+    if (std::strcmp(kernel, profile_name(i)) == 0) {
+      *launches = ctx->prof_launches[i];
+      *milliseconds = ctx->prof_ms[i];
+      return AF2_OK;
+    }
+  }
+  return fail(ctx, AF2_ERR_INVALID_ARGUMENT, std::string("unknown kernel label ") + kernel);
 }
 
 int64_t af2_triangle_weight_count(int64_t c_z, int64_t c_hidden) {

@@ -888,8 +888,10 @@ af2_status launch_project(af2_ctx *ctx, const CUtensorMap &zmap, const tri::Proj
     configured = true;
   }
   const int grid = std::max(1, std::min(a.total_tiles, ctx->sm_count));
-  tri::project_kernel<ZT><<<grid, tri::PJ_THREADS, tri::PJ_SMEM, stream>>>(zmap, a);
-  ctx->launches++;
+  {
+    LaunchScope scope(ctx, stream, kProfTriangleProject);
+    tri::project_kernel<ZT><<<grid, tri::PJ_THREADS, tri::PJ_SMEM, stream>>>(zmap, a);
+  }
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? AF2_OK : cuda_fail(ctx, e, "launch project kernel");
 }
@@ -905,8 +907,10 @@ af2_status launch_output(af2_ctx *ctx, const CUtensorMap &xmap, const CUtensorMa
     configured = true;
   }
   const int grid = std::max(1, std::min(a.total_tiles, ctx->sm_count));
-  tri::output_kernel<ZT, OT><<<grid, tri::OP_THREADS, tri::OP_SMEM, stream>>>(xmap, zmap, a);
-  ctx->launches++;
+  {
+    LaunchScope scope(ctx, stream, kProfTriangleOutput);
+    tri::output_kernel<ZT, OT><<<grid, tri::OP_THREADS, tri::OP_SMEM, stream>>>(xmap, zmap, a);
+  }
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? AF2_OK : cuda_fail(ctx, e, "launch output kernel");
 }
@@ -936,8 +940,10 @@ af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L,
   const int n = static_cast<int>(L.n);
   const int64_t pairs = L.n * L.n;
 
-  prep_weights_kernel<<<96, 256, 0, stream>>>(packed, (int)L.cz, (int)L.ch, w16, vec);
-  ctx->launches++;
+  {
+    LaunchScope scope(ctx, stream, kProfTrianglePrepare);
+    prep_weights_kernel<<<96, 256, 0, stream>>>(packed, (int)L.cz, (int)L.ch, w16, vec);
+  }
   if (cudaError_t e = cudaGetLastError(); e != cudaSuccess) return cuda_fail(ctx, e, "launch weight preparation");
 
   const void *zsrc = z;
@@ -945,12 +951,12 @@ af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L,
   if (L.pad_z) {
     __half *z16 = reinterpret_cast<__half *>(ws + L.off_z16);
     const int grid = static_cast<int>(std::min<int64_t>((pairs * C + 255) / 256, 8 * 1024));
+    LaunchScope scope(ctx, stream, kProfTriangleRelayout);
     switch (z_dtype) {
       case AF2_F32: pad_z_kernel<float><<<grid, 256, 0, stream>>>(static_cast<const float *>(z), pairs, (int)L.cz, z16); break;
       case AF2_F16: pad_z_kernel<__half><<<grid, 256, 0, stream>>>(static_cast<const __half *>(z), pairs, (int)L.cz, z16); break;
       default: pad_z_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(static_cast<const __nv_bfloat16 *>(z), pairs, (int)L.cz, z16); break;
     }
-    ctx->launches++;
     if (cudaError_t e = cudaGetLastError(); e != cudaSuccess) return cuda_fail(ctx, e, "launch z re-layout");
     zsrc = z16;
     zt = AF2_F16;
@@ -1020,8 +1026,10 @@ af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L,
     ca.scale = 1.0f / static_cast<float>(n);
     ca.err = ctx->err_word;
     const int grid = std::max(1, std::min(ca.total_tiles, ctx->sm_count));
-    contract_kernel<<<grid, CT_THREADS, CT_SMEM, stream>>>(amap, bmap, ca);
-    ctx->launches++;
+    {
+      LaunchScope scope(ctx, stream, kProfTriangleContract);
+      contract_kernel<<<grid, CT_THREADS, CT_SMEM, stream>>>(amap, bmap, ca);
+    }
     if (cudaError_t e = cudaGetLastError(); e != cudaSuccess) return cuda_fail(ctx, e, "launch contraction");
 
     CUtensorMap xmap;

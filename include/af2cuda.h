@@ -115,6 +115,18 @@ AF2_API af2_status af2_sync(af2_ctx *ctx, void *stream);
 /* Number of kernels this context has launched (monotonic). */
 AF2_API uint64_t af2_launch_count(const af2_ctx *ctx);
 
+/*
+ * Per-kernel device timing (the counterpart of the reference's timestamp-query
+ * profile, src/runtime/execution.ts:482-533).  While enabled every kernel
+ * launch is bracketed by CUDA events on its own stream.  af2_profile_read
+ * synchronises, folds the recorded launches into per-kernel totals and
+ * returns the totals of `kernel` (names as af2_profile_kernel_name gives them).
+ */
+AF2_API af2_status af2_profile_enable(af2_ctx *ctx, int enable);
+AF2_API af2_status af2_profile_reset(af2_ctx *ctx);
+AF2_API const char *af2_profile_kernel_name(int index);
+AF2_API af2_status af2_profile_read(af2_ctx *ctx, const char *kernel, uint64_t *launches, double *milliseconds);
+
 /* ---- triangle multiplication ------------------------------------------ */
 
 /* expectedWeightElementCount, src/triangle/weights.ts:36-40. */
