@@ -96,6 +96,8 @@ struct TriangleLayout {
   int64_t block_rows = 0;   // output rows per block
   int64_t kp = 0;           // row pitch (elements) of the projected operands
   int64_t jp = 0;           // row pitch (elements) of the contracted block
+  int64_t ab_hs = 0;        // channel pitch (elements) of the projected operands
+  int64_t x_hs = 0;         // channel pitch (elements) of the contracted block (full block)
   bool pad_z = false;       // z is re-laid as f16 [P][128] before the kernels
   size_t off_w16 = 0, off_vec = 0, off_z16 = 0, off_a = 0, off_b = 0, off_x = 0, total = 0;
 };

@@ -35,6 +35,7 @@ namespace af2 {
 namespace tri {
 
 constexpr int C = 128;  // padded channel count of every triangle tile
+constexpr int64_t kChannelPad = 64;  // elements added to every channel pitch
 
 // Prepared weights: six [128][128] f16 matrices, [out][in] row-major.
 enum { kWAP = 0, kWAG = 1, kWBP = 2, kWBG = 3, kWZ = 4, kWG = 5, kMatCount = 6 };
@@ -847,6 +848,7 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
 // ---------------------------------------------------------------------------
 
 TriangleLayout triangle_layout(int64_t n, int64_t cz, int64_t ch, int64_t block_rows, int z_dtype) {
+  using tri::kChannelPad;
   TriangleLayout L;
   L.n = n;
   L.cz = cz;
@@ -854,6 +856,10 @@ TriangleLayout triangle_layout(int64_t n, int64_t cz, int64_t ch, int64_t block_
   L.block_rows = (block_rows <= 0 || block_rows > n) ? n : block_rows;
   L.kp = static_cast<int64_t>(align_up(static_cast<size_t>(n), 8));
   L.jp = L.kp;
+  // Channel pitches are padded by 128 bytes so that the per-channel planes do
+  // not sit an exact power of two apart (rows of 2^k bytes times 2^k rows).
+  L.ab_hs = L.n * L.kp + kChannelPad;
+  L.x_hs = L.block_rows * L.jp + kChannelPad;
   L.pad_z = (z_dtype == AF2_F32) || cz != tri::C;
   size_t off = 0;
   L.off_w16 = off;
@@ -863,11 +869,11 @@ TriangleLayout triangle_layout(int64_t n, int64_t cz, int64_t ch, int64_t block_
   L.off_z16 = off;
   if (L.pad_z) off = align_up(off + sizeof(__half) * (size_t)n * n * tri::C, 256);
   L.off_a = off;
-  off = align_up(off + sizeof(__half) * (size_t)tri::C * n * L.kp, 256);
+  off = align_up(off + sizeof(__half) * (size_t)tri::C * L.ab_hs, 256);
   L.off_b = off;
-  off = align_up(off + sizeof(__half) * (size_t)tri::C * n * L.kp, 256);
+  off = align_up(off + sizeof(__half) * (size_t)tri::C * L.ab_hs, 256);
   L.off_x = off;
-  off = align_up(off + sizeof(__half) * (size_t)tri::C * L.block_rows * L.jp, 256);
+  off = align_up(off + sizeof(__half) * (size_t)tri::C * L.x_hs, 256);
   L.total = off;
   return L;
 }
@@ -978,7 +984,7 @@ af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L,
   pa.mask_ks = out_dir ? 1 : L.n;
   pa.a_out = a;
   pa.b_out = b;
-  pa.out_hs = L.n * L.kp;
+  pa.out_hs = L.ab_hs;
   pa.out_rs = L.kp;
   pa.w16 = w16;
   pa.vec = vec;
@@ -997,9 +1003,9 @@ af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L,
   const __half *m_op = out_dir ? a : b;  // rows i of the product
   const __half *n_op = out_dir ? b : a;  // rows j of the product
   CUtensorMap amap, bmap, zmap_out;
-  if (!encode_map_3d(&amap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, m_op, L.n, L.n, C, L.kp * 2, L.n * L.kp * 2, CT_BK,
+  if (!encode_map_3d(&amap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, m_op, L.n, L.n, C, L.kp * 2, L.ab_hs * 2, CT_BK,
                      CT_BM, 1, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !encode_map_3d(&bmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, n_op, L.n, L.n, C, L.kp * 2, L.n * L.kp * 2, CT_BK,
+      !encode_map_3d(&bmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, n_op, L.n, L.n, C, L.kp * 2, L.ab_hs * 2, CT_BK,
                      CT_BN, 1, CU_TENSOR_MAP_SWIZZLE_128B) ||
       !encode_map_3d(&zmap_out, map_type(zt), zsrc, C, L.n, L.n, row_bytes, row_bytes * L.n, 64, 128, 1,
                      CU_TENSOR_MAP_SWIZZLE_128B))
@@ -1014,7 +1020,7 @@ af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L,
     const int rc = static_cast<int>(std::min<int64_t>(L.block_rows, L.n - rb));
     ContractArgs ca;
     ca.x_out = x;
-    ca.x_hs = (int64_t)rc * L.jp;
+    ca.x_hs = (int64_t)rc * L.jp + kChannelPad;
     ca.x_rs = L.jp;
     ca.n = n;
     ca.row_begin = static_cast<int>(rb);
@@ -1033,7 +1039,7 @@ af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L,
     if (cudaError_t e = cudaGetLastError(); e != cudaSuccess) return cuda_fail(ctx, e, "launch contraction");
 
     CUtensorMap xmap;
-    if (!encode_map_3d(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x, L.n, rc, C, L.jp * 2, (uint64_t)rc * L.jp * 2,
+    if (!encode_map_3d(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x, L.n, rc, C, L.jp * 2, (uint64_t)ca.x_hs * 2,
                        128, 1, C, CU_TENSOR_MAP_SWIZZLE_NONE))
       return fail(ctx, AF2_ERR_CUDA, "cuTensorMapEncodeTiled failed for the contracted block");
     OutputArgs oa;
