@@ -67,19 +67,33 @@ __device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
   return done != 0;
 }
 
+// try_wait with a suspend-time hint: the thread sleeps until the phase
+// completes or `hint_ns` passes, instead of spinning on issue slots.
+__device__ __forceinline__ bool mbar_test_sleep(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(bar), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return done != 0;
+}
+
+constexpr uint32_t kSleepHintNs = 200000;  // 0.2 ms per try; the overall bound is kWaitLimitNs
+
 // Waits until the phase of parity `parity` of `bar` has completed.  Returns
 // false (and sets the abort flag and the error word) when the wait runs out
 // or another role has aborted.
-__device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort_flag,
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort_flag,
                                        unsigned int *err, unsigned int code) {
   if (mbar_test(bar, parity)) return true;
   const unsigned long long start = globaltimer();
-  for (uint32_t spin = 1; spin < 0x7fffffffu; ++spin) {
-    if (mbar_test(bar, parity)) return true;
-    if ((spin & 31u) == 0) {
-      if (*abort_flag) return false;
-      if (globaltimer() - start > kWaitLimitNs) break;
-    }
+  for (uint32_t tries = 0; tries < 0x7fffffffu; ++tries) {
+    if (mbar_test_sleep(bar, parity, kSleepHintNs)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer() - start > kWaitLimitNs) break;
   }
   *abort_flag = 1;
   atomicOr(err, code);
@@ -87,11 +101,11 @@ __device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile i
 }
 
 // Drain-time wait: bounded, never raises the abort flag (it is already up).
-__device__ __noinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity, unsigned int *err) {
+__device__ __forceinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity, unsigned int *err) {
   const unsigned long long start = globaltimer();
-  for (uint32_t spin = 0; spin < 0x7fffffffu; ++spin) {
-    if (mbar_test(bar, parity)) return true;
-    if ((spin & 31u) == 0 && globaltimer() - start > kWaitLimitNs) break;
+  for (uint32_t tries = 0; tries < 0x7fffffffu; ++tries) {
+    if (mbar_test_sleep(bar, parity, kSleepHintNs)) return true;
+    if (globaltimer() - start > kWaitLimitNs) break;
   }
   atomicOr(err, kErrWaitDrain);
   return false;
@@ -179,6 +193,16 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "r"(taddr));
 }
 
+// 32 lanes x 16 consecutive 32-bit columns.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32"
+      " {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // Shared-memory matrix descriptor for a K-major operand tile in the 128-byte
@@ -195,6 +219,21 @@ __device__ __forceinline__ uint64_t sdesc_k_sw128(uint32_t saddr) {
   return d;
 }
 
+// Shared-memory matrix descriptor for an MN-major operand tile in the 128-byte
+// swizzled layout: K-rows of 64 16-bit MN-elements (128 B), 8 K-rows per
+// 1024-byte atom.  `lbo` is the byte distance between consecutive 64-element
+// MN blocks, `sbo` between consecutive groups of 8 K-rows.  Stepping K by 16
+// adds 2 * sbo to the start address.
+__device__ __forceinline__ uint64_t sdesc_mn_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+  d |= static_cast<uint64_t>(1) << 46;
+  d |= static_cast<uint64_t>(2) << 61;
+  return d;
+}
+
 // Instruction descriptor, kind::f16: f16 A and B, f32 D, both K-major.
 __host__ __device__ constexpr uint32_t idesc_f16_f32(int m, int n) {
   return (1u << 4)                                   // D format f32
@@ -202,6 +241,9 @@ __host__ __device__ constexpr uint32_t idesc_f16_f32(int m, int n) {
          | (static_cast<uint32_t>(n >> 3) << 17)     // N / 8
          | (static_cast<uint32_t>(m >> 4) << 24);    // M / 16
 }
+
+// The same with A MN-major (transpose-A bit).
+__host__ __device__ constexpr uint32_t idesc_f16_f32_amn(int m, int n) { return idesc_f16_f32(m, n) | (1u << 15); }
 
 // Byte offset of 16-byte chunk `chunk` (0..7) of row `row` in a 128B-swizzled tile.
 __device__ __forceinline__ uint32_t sw128_offset(uint32_t row, uint32_t chunk) {
@@ -253,6 +295,26 @@ __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
   return *reinterpret_cast<uint32_t *>(&h);
 }
 
-__device__ __forceinline__ float sigmoidf(float v) { return 1.0f / (1.0f + __expf(-v)); }
+// Logistic function from the hardware base-2 exponential and reciprocal
+// (ex2.approx and rcp.approx, both within 2 ulp of f32): 1 / (1 + 2^(-v log2 e)).
+// Saturates cleanly: a large negative v gives 1/inf = 0, a large positive one 1/1.
+__device__ __forceinline__ float sigmoidf(float v) {
+  float e, r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(v * -1.4426950408889634f));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(1.0f + e));
+  return r;
+}
+
+// Two 16-bit values of a 32-bit word -> f32 (low half first).
+template <typename T>
+__device__ __forceinline__ float2 unpack2(uint32_t w);
+template <>
+__device__ __forceinline__ float2 unpack2<__half>(uint32_t w) {
+  return __half22float2(*reinterpret_cast<const __half2 *>(&w));
+}
+template <>
+__device__ __forceinline__ float2 unpack2<__nv_bfloat16>(uint32_t w) {
+  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
 
 }  // namespace af2

@@ -136,12 +136,16 @@ __device__ __forceinline__ void load_weight_matrix(uint8_t *dst, const __half *s
 // ---------------------------------------------------------------------------
 constexpr int PJ_TILE = 64;      // pairs per tile
 constexpr int PJ_STAGES = 3;
-constexpr int PJ_THREADS = 320;  // warp 0 TMA, 1 MMA, 2-5 LayerNorm, 6-9 epilogue
+// warp 0 TMA, 1 MMA, 2-5 LayerNorm (two groups of two warps taking alternate
+// tiles, one thread per pair row), 6-9 epilogue of a, 10-13 epilogue of b.
+constexpr int PJ_THREADS = 448;
 constexpr uint32_t PJ_CHUNK = PJ_TILE * 128;            // one 64-channel K chunk: 8 KB
 constexpr uint32_t PJ_STAGE_BYTES = 2 * PJ_CHUNK;       // 16 KB
 constexpr uint32_t PJ_W_BYTES = 4 * 2 * 16384;          // 128 KB
 constexpr uint32_t PJ_OFF_STAGE = PJ_W_BYTES;
-constexpr uint32_t PJ_OFF_BAR = PJ_OFF_STAGE + PJ_STAGES * PJ_STAGE_BYTES;
+constexpr uint32_t PJ_OFF_VEC = PJ_OFF_STAGE + PJ_STAGES * PJ_STAGE_BYTES;  // LN-in gamma, beta
+constexpr uint32_t PJ_OFF_MASK = PJ_OFF_VEC + 2 * 512;                       // 8 warps x 64 f32
+constexpr uint32_t PJ_OFF_BAR = PJ_OFF_MASK + 8 * 256;
 constexpr uint32_t PJ_SMEM = PJ_OFF_BAR + 256 + 1024;
 
 struct ProjectArgs {
@@ -157,54 +161,57 @@ struct ProjectArgs {
   unsigned int *err;
 };
 
-// LayerNorm of one 128-channel row held by 16 lanes (8 channels each) inside a
-// 128B-swizzled K-major tile, in place, as f16.  Channels >= cz are padding
-// (zero input, zero gamma/beta) and are left out of the statistics.
+// LayerNorm of pair row `row` of a 128B-swizzled K-major tile (two 64-channel
+// chunks `chunk_bytes` apart), in place, 16-bit input -> f16, one thread per
+// row.  gamma/beta live in shared memory (every lane reads the same channel,
+// a broadcast).  Channels >= cz are padding: zero input, zero gamma and beta,
+// and outside the statistics.  The statistics are one pass over values
+// shifted by the row's first element, which keeps the f32 sums well
+// conditioned.
 template <typename ZT>
-__device__ __forceinline__ void ln_row_inplace(uint8_t *stage, uint32_t chunk_bytes, int row, int c16,
-                                               const float (&g)[8], const float (&bt)[8], int cz, float inv_cz,
-                                               float eps) {
-  uint8_t *ptr = stage + (c16 >> 3) * chunk_bytes + sw128_offset(row, c16 & 7);
-  const uint4 v = *reinterpret_cast<const uint4 *>(ptr);
-  float x[8];
-  unpack8<ZT>(v, x);
-  float sum = 0.f;
+__device__ __forceinline__ void ln_row_thread(uint8_t *tile, uint32_t chunk_bytes, int row, const float *gamma,
+                                              const float *beta, int cz, float inv_cz, float eps) {
+  auto chunk_ptr = [&](int c) { return tile + (c >> 3) * chunk_bytes + sw128_offset(row, c & 7); };
+  const float x0 = unpack2<ZT>(reinterpret_cast<const uint32_t *>(chunk_ptr(0))[0]).x;
+  float s1 = 0.f, s2 = 0.f;
+#pragma unroll 4
+  for (int c = 0; c < 16; ++c) {
+    const uint4 v = *reinterpret_cast<const uint4 *>(chunk_ptr(c));
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-  for (int i = 0; i < 8; ++i) sum += x[i];
-  const float mean = reduce16(sum) * inv_cz;
-  float sq = 0.f;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const float d = x[i] - mean;
-    sq += (c16 * 8 + i < cz) ? d * d : 0.f;
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = unpack2<ZT>(w[i]);
+      const int ch = c * 8 + 2 * i;
+      const float d0 = (cz == 128 || ch < cz) ? f.x - x0 : 0.f;
+      const float d1 = (cz == 128 || ch + 1 < cz) ? f.y - x0 : 0.f;
+      s1 += d0 + d1;
+      s2 = fmaf(d0, d0, fmaf(d1, d1, s2));
+    }
   }
-  const float rstd = rsqrtf(reduce16(sq) * inv_cz + eps);
-  uint4 o;
-  o.x = pack_half2((x[0] - mean) * rstd * g[0] + bt[0], (x[1] - mean) * rstd * g[1] + bt[1]);
-  o.y = pack_half2((x[2] - mean) * rstd * g[2] + bt[2], (x[3] - mean) * rstd * g[3] + bt[3]);
-  o.z = pack_half2((x[4] - mean) * rstd * g[4] + bt[4], (x[5] - mean) * rstd * g[5] + bt[5]);
-  o.w = pack_half2((x[6] - mean) * rstd * g[6] + bt[6], (x[7] - mean) * rstd * g[7] + bt[7]);
-  *reinterpret_cast<uint4 *>(ptr) = o;
-}
-
-// 32 gated values of one channel row -> f16 at dst (count valid of them).
-__device__ __forceinline__ void store_gated(__half *dst, const uint32_t (&vp)[32], const uint32_t (&vg)[32],
-                                            const float (&mk)[32], float bp, float bg, int valid) {
-  uint32_t packed[16];
+  const float m1 = s1 * inv_cz;
+  const float mean = x0 + m1;
+  const float var = fmaxf(s2 * inv_cz - m1 * m1, 0.f);
+  const float rstd = rsqrtf(var + eps);
+  const float shift = -mean * rstd;
+#pragma unroll 4
+  for (int c = 0; c < 16; ++c) {
+    uint8_t *ptr = chunk_ptr(c);
+    const uint4 v = *reinterpret_cast<const uint4 *>(ptr);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    const float4 g0 = *reinterpret_cast<const float4 *>(gamma + c * 8);
+    const float4 g1 = *reinterpret_cast<const float4 *>(gamma + c * 8 + 4);
+    const float4 b0 = *reinterpret_cast<const float4 *>(beta + c * 8);
+    const float4 b1 = *reinterpret_cast<const float4 *>(beta + c * 8 + 4);
+    const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+    const float b[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+    uint32_t o[4];
 #pragma unroll
-  for (int c = 0; c < 32; c += 2) {
-    const float y0 = mk[c] * (__uint_as_float(vp[c]) + bp) * sigmoidf(__uint_as_float(vg[c]) + bg);
-    const float y1 = mk[c + 1] * (__uint_as_float(vp[c + 1]) + bp) * sigmoidf(__uint_as_float(vg[c + 1]) + bg);
-    packed[c >> 1] = pack_half2(y0, y1);
-  }
-  if (valid >= 32) {
-    uint4 *d = reinterpret_cast<uint4 *>(dst);
-#pragma unroll
-    for (int q = 0; q < 4; ++q)
-      d[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
-  } else {
-    const __half *h = reinterpret_cast<const __half *>(packed);
-    for (int c = 0; c < valid; ++c) dst[c] = h[c];
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = unpack2<ZT>(w[i]);
+      o[i] = pack_half2(fmaf(fmaf(f.x, rstd, shift), g[2 * i], b[2 * i]),
+                        fmaf(fmaf(f.y, rstd, shift), g[2 * i + 1], b[2 * i + 1]));
+    }
+    *reinterpret_cast<uint4 *>(ptr) = make_uint4(o[0], o[1], o[2], o[3]);
   }
 }
 
@@ -224,20 +231,22 @@ __global__ void __launch_bounds__(PJ_THREADS, 1)
   const uint32_t drain = bar0 + 8u * 13;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + PJ_OFF_BAR + 128);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + PJ_OFF_BAR + 136);
+  float *sv = reinterpret_cast<float *>(smem + PJ_OFF_VEC);  // [0,128) gamma, [128,256) beta
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   for (int m = 0; m < 4; ++m)
     load_weight_matrix(smem + m * 32768, p.w16 + (size_t)m * C * C, threadIdx.x, PJ_THREADS);
+  for (int i = threadIdx.x; i < 2 * C; i += PJ_THREADS) sv[i] = p.vec[(i < C ? kVLnInW : kVLnInB) * C + (i % C)];
   fence_async_smem();
   if (threadIdx.x == 0) {
     for (int s = 0; s < PJ_STAGES; ++s) {
       mbar_init(z_full(s), 1);
-      mbar_init(z_ready(s), 4);
+      mbar_init(z_ready(s), 2);
       mbar_init(z_empty(s), 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(acc_full(b), 1);
-      mbar_init(acc_empty(b), 4);
+      mbar_init(acc_empty(b), 8);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -273,7 +282,7 @@ __global__ void __launch_bounds__(PJ_THREADS, 1)
         tma_load_3d(dst + PJ_CHUNK, &zmap, z_full(s), 64, c1, c2);
       }
       if (!ok) {  // wait for the loads still landing before the CTA exits
-        for (int j = std::max(0, it - PJ_STAGES); j < it; ++j)
+        for (int j = it > PJ_STAGES ? it - PJ_STAGES : 0; j < it; ++j)
           mbar_wait_drain(z_full(j % PJ_STAGES), (j / PJ_STAGES) & 1, p.err);
       }
     }
@@ -318,63 +327,87 @@ __global__ void __launch_bounds__(PJ_THREADS, 1)
     }
     __syncwarp();
   } else if (warp < 6) {
-    // ---- LayerNorm of the z tile, in place, bf16/f16 -> f16 ----
-    const int nw = warp - 2, sub = lane >> 4, c16 = lane & 15;
-    float g[8], bt[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      g[i] = p.vec[kVLnInW * C + c16 * 8 + i];
-      bt[i] = p.vec[kVLnInB * C + c16 * 8 + i];
-    }
+    // ---- LayerNorm of the z tile, in place, 16-bit -> f16 ----
+    const int grp = (warp - 2) >> 1;
+    const int row = ((warp - 2) & 1) * 32 + lane;
     const float inv_cz = 1.f / static_cast<float>(p.cz);
-    int it = 0;
-    for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x, ++it) {
+    int it = grp;
+    for (int t = blockIdx.x + grp * gridDim.x; t < p.total_tiles; t += 2 * gridDim.x, it += 2) {
       const int s = it % PJ_STAGES;
       const uint32_t ph = (it / PJ_STAGES) & 1;
       if (!warp_wait(z_full(s), ph, abort_flag, p.err, kErrWaitNormalizer)) break;
-      uint8_t *stage = smem + PJ_OFF_STAGE + s * PJ_STAGE_BYTES;
-#pragma unroll 1
-      for (int pass = 0; pass < PJ_TILE / 8; ++pass)
-        ln_row_inplace<ZT>(stage, PJ_CHUNK, pass * 8 + nw * 2 + sub, c16, g, bt, p.cz, inv_cz, p.eps);
+      ln_row_thread<ZT>(smem + PJ_OFF_STAGE + s * PJ_STAGE_BYTES, PJ_CHUNK, row, sv, sv + C, p.cz, inv_cz, p.eps);
       fence_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(z_ready(s));
     }
   } else {
-    // ---- epilogue: TMEM -> gated f16 operands, channel-major ----
-    const int q = warp & 3;
+    // ---- epilogue: TMEM -> gated f16 operand rows, channel-major ----
+    const int e = warp - 6;        // 0..7
+    const int op = e >> 2;         // 0: a (a_p, a_g), 1: b (b_p, b_g)
+    const int q = warp & 3;        // TMEM lane quarter this warp may read
     const int h = q * 32 + lane;
-    const float bap = p.vec[kVBAP * C + h], bag = p.vec[kVBAG * C + h];
-    const float bbp = p.vec[kVBBP * C + h], bbg = p.vec[kVBBG * C + h];
+    const float bias_p = p.vec[(op ? kVBBP : kVBAP) * C + h];
+    const float bias_g = p.vec[(op ? kVBBG : kVBAG) * C + h];
+    __half *out = op ? p.b_out : p.a_out;
+    float *msk = reinterpret_cast<float *>(smem + PJ_OFF_MASK) + e * 64;
+    auto mask_at = [&](int t, int k) -> float {
+      if (t >= p.total_tiles || k >= p.n) return 0.f;
+      return p.mask[(int64_t)(t / p.tiles_k) * p.mask_rs + (int64_t)k * p.mask_ks];
+    };
+    int t = blockIdx.x;
+    float m0 = mask_at(t, (t % p.tiles_k) * PJ_TILE + lane);
+    float m1 = mask_at(t, (t % p.tiles_k) * PJ_TILE + 32 + lane);
     int it = 0;
-    for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x, ++it) {
+    for (; t < p.total_tiles; t += gridDim.x, ++it) {
       const int r = t / p.tiles_k, k0 = (t % p.tiles_k) * PJ_TILE;
       const int buf = it & 1;
       const uint32_t bph = (it >> 1) & 1;
-      const float m0 = (k0 + lane < p.n) ? p.mask[r * p.mask_rs + (int64_t)(k0 + lane) * p.mask_ks] : 0.f;
-      const float m1 =
-          (k0 + 32 + lane < p.n) ? p.mask[r * p.mask_rs + (int64_t)(k0 + 32 + lane) * p.mask_ks] : 0.f;
+      // this tile's mask goes to shared memory; the next tile's is fetched now
+      msk[lane] = m0;
+      msk[32 + lane] = m1;
+      const int tn = t + gridDim.x;
+      m0 = mask_at(tn, (tn % p.tiles_k) * PJ_TILE + lane);
+      m1 = mask_at(tn, (tn % p.tiles_k) * PJ_TILE + 32 + lane);
+      __syncwarp();
       if (!warp_wait(acc_full(buf), bph, abort_flag, p.err, kErrWaitEpilogue)) break;
       tc_fence_after();
-      const uint32_t trow = tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * 256;
-      __half *a_row = p.a_out + h * p.out_hs + r * p.out_rs + k0;
-      __half *b_row = p.b_out + h * p.out_hs + r * p.out_rs + k0;
+      const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * 256 + op * 2 * PJ_TILE;
+      __half *row_out = out + h * p.out_hs + r * p.out_rs + k0;
 #pragma unroll 1
-      for (int half = 0; half < 2; ++half) {
-        float mk[32];
-        const float msrc = half ? m1 : m0;
+      for (int part = 0; part < PJ_TILE / 16; ++part) {
+        uint32_t vp[16], vg[16];
+        tmem_ld16(taddr + part * 16, vp);
+        tmem_ld16(taddr + PJ_TILE + part * 16, vg);
+        tmem_ld_wait();
+        uint32_t pk[8];
 #pragma unroll
-        for (int c = 0; c < 32; ++c) mk[c] = __shfl_sync(kFull, msrc, c);
-        const int valid = p.n - (k0 + half * 32);
-        uint32_t vp[32], vg[32];
-        tmem_ld32(trow + 0 * PJ_TILE + half * 32, vp);
-        tmem_ld32(trow + 1 * PJ_TILE + half * 32, vg);
-        tmem_ld_wait();
-        store_gated(a_row + half * 32, vp, vg, mk, bap, bag, valid);
-        tmem_ld32(trow + 2 * PJ_TILE + half * 32, vp);
-        tmem_ld32(trow + 3 * PJ_TILE + half * 32, vg);
-        tmem_ld_wait();
-        store_gated(b_row + half * 32, vp, vg, mk, bbp, bbg, valid);
+        for (int c4 = 0; c4 < 4; ++c4) {
+          const float4 mk = *reinterpret_cast<const float4 *>(msk + part * 16 + c4 * 4);
+          const float mm[4] = {mk.x, mk.y, mk.z, mk.w};
+          float y[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int c = c4 * 4 + i;
+            y[i] = mm[i] * (__uint_as_float(vp[c]) + bias_p) * sigmoidf(__uint_as_float(vg[c]) + bias_g);
+          }
+          pk[c4 * 2] = pack_half2(y[0], y[1]);
+          pk[c4 * 2 + 1] = pack_half2(y[2], y[3]);
+        }
+        const int valid = p.n - (k0 + part * 16);
+        __half *dst = row_out + part * 16;
+        if (valid >= 16) {
+          uint4 *d4 = reinterpret_cast<uint4 *>(dst);
+          d4[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          d4[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+        } else {
+#pragma unroll
+          for (int c = 0; c < 16; c += 2) {
+            const __half2 hv = *reinterpret_cast<const __half2 *>(&pk[c >> 1]);
+            if (c < valid) dst[c] = __low2half(hv);
+            if (c + 1 < valid) dst[c + 1] = __high2half(hv);
+          }
+        }
       }
       tc_fence_before();
       __syncwarp();
@@ -389,7 +422,6 @@ __global__ void __launch_bounds__(PJ_THREADS, 1)
     tmem_dealloc(tmem, 512);
   }
 }
-
 // ---------------------------------------------------------------------------
 // Kernel 2: per-channel contraction X[h] = s * A[h] B[h]^T.
 // ---------------------------------------------------------------------------
@@ -470,7 +502,7 @@ __global__ void __launch_bounds__(CT_THREADS, 1)
         }
       }
       if (!ok) {
-        for (int j = std::max(0, it - CT_STAGES); j < it; ++j)
+        for (int j = it > CT_STAGES ? it - CT_STAGES : 0; j < it; ++j)
           mbar_wait_drain(full(j % CT_STAGES), (j / CT_STAGES) & 1, p.err);
       }
     }
@@ -565,13 +597,17 @@ __global__ void __launch_bounds__(CT_THREADS, 1)
 // ---------------------------------------------------------------------------
 // Kernel 3: LN_out + output projection + gate + residual.
 // ---------------------------------------------------------------------------
-constexpr int OP_STAGES = 2, OP_THREADS = 320;
+constexpr int OP_STAGES = 2;
+// warp 0 TMA, 1 MMA, 2-5 transpose/LayerNorm (one thread per pair row),
+// 6-9 epilogue of output channels [0, 64), 10-13 of [64, 128).
+constexpr int OP_THREADS = 448;
 constexpr uint32_t OP_W_BYTES = 2 * 2 * 16384;                 // W_z, W_g
 constexpr uint32_t OP_X_BYTES = 128 * 256, OP_Z_BYTES = 128 * 256;
 constexpr uint32_t OP_STAGE_BYTES = OP_X_BYTES + OP_Z_BYTES;
 constexpr uint32_t OP_OFF_STAGE = OP_W_BYTES;
-constexpr uint32_t OP_OFF_VEC = OP_OFF_STAGE + OP_STAGES * OP_STAGE_BYTES;  // ln_out w/b, b_z, b_g
-constexpr uint32_t OP_OFF_BAR = OP_OFF_VEC + 4 * 512;
+// ln_out gamma/beta, b_z, b_g, ln_in gamma/beta
+constexpr uint32_t OP_OFF_VEC = OP_OFF_STAGE + OP_STAGES * OP_STAGE_BYTES;
+constexpr uint32_t OP_OFF_BAR = OP_OFF_VEC + 6 * 512;
 constexpr uint32_t OP_SMEM = OP_OFF_BAR + 256 + 1024;
 
 struct OutputArgs {
@@ -584,48 +620,39 @@ struct OutputArgs {
   unsigned int *err;
 };
 
+// 16 consecutive channels of one output row: residual add (from `res`, the
+// row's old values as loaded earlier) and store.
 template <typename OT>
-__device__ __forceinline__ void store_out_row(OT *row, const float (&v)[32], int zc0, int cz, int residual) {
-  if (cz == C) {
-    if constexpr (sizeof(OT) == 4) {
-      float4 *d = reinterpret_cast<float4 *>(row + zc0);
+__device__ __forceinline__ void store_out16(OT *dst, const float (&v)[16], const uint4 *res, int residual) {
+  if constexpr (sizeof(OT) == 4) {
+    float4 *d = reinterpret_cast<float4 *>(dst);
 #pragma unroll
-      for (int w = 0; w < 8; ++w) {
-        float4 o = make_float4(v[4 * w], v[4 * w + 1], v[4 * w + 2], v[4 * w + 3]);
-        if (residual) {
-          const float4 old = d[w];
-          o.x += old.x; o.y += old.y; o.z += old.z; o.w += old.w;
-        }
-        d[w] = o;
+    for (int w = 0; w < 4; ++w) {
+      float4 o = make_float4(v[4 * w], v[4 * w + 1], v[4 * w + 2], v[4 * w + 3]);
+      if (residual) {
+        const float4 old = *reinterpret_cast<const float4 *>(&res[w]);
+        o.x += old.x; o.y += old.y; o.z += old.z; o.w += old.w;
       }
-    } else {
-      uint4 *d = reinterpret_cast<uint4 *>(row + zc0);
-#pragma unroll
-      for (int w = 0; w < 4; ++w) {
-        float x[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) x[i] = v[8 * w + i];
-        if (residual) {
-          float old[8];
-          unpack8<OT>(d[w], old);
-#pragma unroll
-          for (int i = 0; i < 8; ++i) x[i] += old[i];
-        }
-        uint4 o;
-        OT *e = reinterpret_cast<OT *>(&o);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) e[i] = from_f32<OT>(x[i]);
-        d[w] = o;
-      }
+      d[w] = o;
     }
   } else {
-    for (int c = 0; c < 32; ++c) {
-      const int zc = zc0 + c;
-      if (zc < cz) {
-        float x = v[c];
-        if (residual) x += to_f32<OT>(row[zc]);
-        row[zc] = from_f32<OT>(x);
+    uint4 *d = reinterpret_cast<uint4 *>(dst);
+#pragma unroll
+    for (int w = 0; w < 2; ++w) {
+      float x[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) x[i] = v[8 * w + i];
+      if (residual) {
+        float old[8];
+        unpack8<OT>(res[w], old);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) x[i] += old[i];
       }
+      uint4 o;
+      OT *e = reinterpret_cast<OT *>(&o);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) e[i] = from_f32<OT>(x[i]);
+      d[w] = o;
     }
   }
 }
@@ -646,14 +673,15 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
   const uint32_t drain = bar0 + 8u * 10;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + OP_OFF_BAR + 128);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + OP_OFF_BAR + 136);
-  float *sv = reinterpret_cast<float *>(smem + OP_OFF_VEC);  // [0] ln_out w, [128] ln_out b, [256] b_z, [384] b_g
+  // [0] ln_out gamma, [128] ln_out beta, [256] b_z, [384] b_g, [512] ln_in gamma, [640] ln_in beta
+  float *sv = reinterpret_cast<float *>(smem + OP_OFF_VEC);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   load_weight_matrix(smem, p.w16 + (size_t)kWZ * C * C, threadIdx.x, OP_THREADS);
   load_weight_matrix(smem + 32768, p.w16 + (size_t)kWG * C * C, threadIdx.x, OP_THREADS);
-  for (int i = threadIdx.x; i < 4 * C; i += OP_THREADS) {
+  for (int i = threadIdx.x; i < 6 * C; i += OP_THREADS) {
     const int q = i / C, e = i % C;
-    const int src = q == 0 ? kVLnOutW : q == 1 ? kVLnOutB : q == 2 ? kVBZ : kVBG;
+    const int src = q == 0 ? kVLnOutW : q == 1 ? kVLnOutB : q == 2 ? kVBZ : q == 3 ? kVBG : q == 4 ? kVLnInW : kVLnInB;
     sv[i] = p.vec[src * C + e];
   }
   fence_async_smem();
@@ -665,7 +693,7 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(acc_full(b), 1);
-      mbar_init(acc_empty(b), 4);
+      mbar_init(acc_empty(b), 8);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -697,17 +725,19 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
         const uint32_t xs = sbase + OP_OFF_STAGE + s * OP_STAGE_BYTES, zs = xs + OP_X_BYTES;
         mbar_arrive_expect_tx(full(s), OP_STAGE_BYTES);
         tma_load_3d(xs, &xmap, full(s), j0, il, 0);
+        tma_load_3d(xs + 16384, &xmap, full(s), j0 + 64, il, 0);
         tma_load_3d(zs, &zmap, full(s), 0, j0, p.row_begin + il);
         tma_load_3d(zs + 16384, &zmap, full(s), 64, j0, p.row_begin + il);
       }
       if (!ok) {
-        for (int j = std::max(0, it - OP_STAGES); j < it; ++j)
+        for (int j = it > OP_STAGES ? it - OP_STAGES : 0; j < it; ++j)
           mbar_wait_drain(full(j % OP_STAGES), (j / OP_STAGES) & 1, p.err);
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t kIdesc = idesc_f16_f32(128, 128);
+      constexpr uint32_t kIdescMn = idesc_f16_f32_amn(128, 128);
       int it = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x, ++it) {
@@ -728,7 +758,9 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
 #pragma unroll
           for (int ks = 0; ks < 4; ++ks) {
             const uint32_t koff = kc * 16384 + ks * 32;
-            mma_f16(d, sdesc_k_sw128(xs + koff), sdesc_k_sw128(sbase + koff), kIdesc, (kc | ks) != 0);
+            // X is MN-major: K step (kc * 4 + ks) * 16 rows = that many 1024-byte atoms / 8 * 2.
+            mma_f16(d, sdesc_mn_sw128(xs + (kc * 4 + ks) * 2048, 16384, 1024), sdesc_k_sw128(sbase + koff),
+                    kIdescMn, (kc | ks) != 0);
             mma_f16(d + 128, sdesc_k_sw128(zs + koff), sdesc_k_sw128(sbase + 32768 + koff), kIdesc,
                     (kc | ks) != 0);
           }
@@ -743,16 +775,14 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
     }
     __syncwarp();
   } else if (warp < 6) {
-    // ---- transpose + LN_out of X, LN_in of z ----
-    const int nw = warp - 2, pr = nw * 32 + lane;  // pair row of the tile this thread transposes
-    const int sub = lane >> 4, c16 = lane & 15;
-    float g[8], bt[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      g[i] = p.vec[kVLnInW * C + c16 * 8 + i];
-      bt[i] = p.vec[kVLnInB * C + c16 * 8 + i];
-    }
+    // ---- LN_out of X in place (warps 2-3), LN_in of z (warps 4-5) ----
+    // X arrives MN-major: two 64-pair blocks 16 KB apart, each 128 h-rows of
+    // 128 B, 128B-swizzled.  A thread owns the adjacent pairs (2c, 2c + 1), so
+    // it reads and writes whole 32-bit words and never touches another
+    // thread's columns.
     const float inv_cz = 1.f / static_cast<float>(p.cz), inv_ch = 1.f / static_cast<float>(p.ch);
+    const bool x_role = warp < 4;
+    const int c = (warp & 1) * 32 + lane;  // 0..63
     int it = 0;
     for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x, ++it) {
       const int s = it % OP_STAGES;
@@ -760,72 +790,110 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
       if (!warp_wait(full(s), ph, abort_flag, p.err, kErrWaitNormalizer)) break;
       uint8_t *xs = smem + OP_OFF_STAGE + s * OP_STAGE_BYTES;
       uint8_t *zs = xs + OP_X_BYTES;
-      // X arrives [h][pair] (256-byte rows); this thread owns column `pr`.
-      __half2 xv[64];
-      float sum = 0.f;
-#pragma unroll
-      for (int h2 = 0; h2 < 64; ++h2) {
-        const __half lo = *reinterpret_cast<const __half *>(xs + (2 * h2) * 256 + pr * 2);
-        const __half hi = *reinterpret_cast<const __half *>(xs + (2 * h2 + 1) * 256 + pr * 2);
-        xv[h2] = __halves2half2(lo, hi);
-        sum += __half2float(lo) + __half2float(hi);
-      }
-      const float mean = sum * inv_ch;
-      float sq = 0.f;
-#pragma unroll
-      for (int h2 = 0; h2 < 64; ++h2) {
-        const float2 f = __half22float2(xv[h2]);
-        const float d0 = f.x - mean, d1 = f.y - mean;
-        sq += (2 * h2 < p.ch ? d0 * d0 : 0.f) + (2 * h2 + 1 < p.ch ? d1 * d1 : 0.f);
-      }
-      const float rstd = rsqrtf(sq * inv_ch + p.eps_out);
-      named_barrier(1, 128);  // every column read before the tile is overwritten
-#pragma unroll
-      for (int cc = 0; cc < 16; ++cc) {
-        uint32_t w[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int hh = cc * 8 + 2 * i;
-          const float2 f = __half22float2(xv[cc * 4 + i]);
-          w[i] = pack_half2((f.x - mean) * rstd * sv[hh] + sv[C + hh],
-                            (f.y - mean) * rstd * sv[hh + 1] + sv[C + hh + 1]);
+      if (x_role) {
+        const int pair = 2 * c, mh = pair >> 6, pl = pair & 63;
+        uint8_t *col = xs + mh * 16384 + (pl & 7) * 2;
+        auto word = [&](int h) {
+          return reinterpret_cast<uint32_t *>(col + h * 128 + ((((pl >> 3) ^ (h & 7))) << 4));
+        };
+        const float2 x0 = __half22float2(*reinterpret_cast<const __half2 *>(word(0)));
+        float s1a = 0.f, s2a = 0.f, s1b = 0.f, s2b = 0.f;
+#pragma unroll 8
+        for (int h = 0; h < C; ++h) {
+          const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(word(h)));
+          const bool in = p.ch == C || h < p.ch;
+          const float da = in ? f.x - x0.x : 0.f, db = in ? f.y - x0.y : 0.f;
+          s1a += da;
+          s2a = fmaf(da, da, s2a);
+          s1b += db;
+          s2b = fmaf(db, db, s2b);
         }
-        *reinterpret_cast<uint4 *>(xs + (cc >> 3) * 16384 + sw128_offset(pr, cc & 7)) =
-            make_uint4(w[0], w[1], w[2], w[3]);
+        const float ma = s1a * inv_ch, mb = s1b * inv_ch;
+        const float ra = rsqrtf(fmaxf(s2a * inv_ch - ma * ma, 0.f) + p.eps_out);
+        const float rb = rsqrtf(fmaxf(s2b * inv_ch - mb * mb, 0.f) + p.eps_out);
+        const float sha = -(x0.x + ma) * ra, shb = -(x0.y + mb) * rb;
+#pragma unroll 8
+        for (int h = 0; h < C; ++h) {
+          uint32_t *w = word(h);
+          const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(w));
+          const float g = sv[h], b = sv[C + h];
+          *w = pack_half2(fmaf(fmaf(f.x, ra, sha), g, b), fmaf(fmaf(f.y, rb, shb), g, b));
+        }
+      } else {
+        ln_row_thread<ZT>(zs, 16384, c, sv + 4 * C, sv + 5 * C, p.cz, inv_cz, p.eps_in);
+        ln_row_thread<ZT>(zs, 16384, c + 64, sv + 4 * C, sv + 5 * C, p.cz, inv_cz, p.eps_in);
       }
-#pragma unroll 1
-      for (int pass = 0; pass < 16; ++pass)
-        ln_row_inplace<ZT>(zs, 16384, pass * 8 + nw * 2 + sub, c16, g, bt, p.cz, inv_cz, p.eps_in);
       fence_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(ready(s));
     }
   } else {
-    // ---- epilogue ----
+    // ---- epilogue: (LN_out(X) W_z^T + b_z) * sigmoid(LN(z) W_g^T + b_g) (+ residual) ----
+    const int e = warp - 6;
+    const int half = e >> 2;       // output channels [64 half, 64 half + 64)
     const int q = warp & 3;
     const int pr = q * 32 + lane;
+    const bool vec_path = p.cz == C;
     int it = 0;
     for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x, ++it) {
       const int il = t / p.tiles_j, j = (t % p.tiles_j) * 128 + pr;
       const int buf = it & 1;
       const uint32_t bph = (it >> 1) & 1;
+      OT *orow = reinterpret_cast<OT *>(p.out) + ((int64_t)(p.row_begin + il) * p.n + j) * p.out_rs;
+      const bool live = j < p.n;
       if (!warp_wait(acc_full(buf), bph, abort_flag, p.err, kErrWaitEpilogue)) break;
       tc_fence_after();
       const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * 256;
-      OT *orow = reinterpret_cast<OT *>(p.out) + ((int64_t)(p.row_begin + il) * p.n + j) * p.out_rs;
-#pragma unroll 1
-      for (int chunk = 0; chunk < 4; ++chunk) {
-        uint32_t vo[32], vg[32];
-        tmem_ld32(taddr + chunk * 32, vo);
-        tmem_ld32(taddr + 128 + chunk * 32, vg);
-        tmem_ld_wait();
-        float v[32];
+      constexpr int kResWords = sizeof(OT) * 16 / 16;  // uint4 words per 16 channels
+      const bool load_res = p.residual && live && vec_path;
+      uint4 res[kResWords];
+      if (load_res) {
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const int zc = chunk * 32 + c;
-          v[c] = (__uint_as_float(vo[c]) + sv[2 * C + zc]) * sigmoidf(__uint_as_float(vg[c]) + sv[3 * C + zc]);
+        for (int w = 0; w < kResWords; ++w) res[w] = reinterpret_cast<const uint4 *>(orow + half * 64)[w];
+      }
+#pragma unroll 1
+      for (int part = 0; part < 4; ++part) {
+        const int c0 = half * 64 + part * 16;
+        uint32_t vo[16], vg[16];
+        tmem_ld16(taddr + c0, vo);
+        tmem_ld16(taddr + 128 + c0, vg);
+        // the next part's residual is fetched while this part computes
+        uint4 res_next[kResWords];
+        if (load_res && part < 3) {
+#pragma unroll
+          for (int w = 0; w < kResWords; ++w) res_next[w] = reinterpret_cast<const uint4 *>(orow + c0 + 16)[w];
         }
-        if (j < p.n) store_out_row<OT>(orow, v, chunk * 32, p.cz, p.residual);
+        tmem_ld_wait();
+        float v[16];
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4) {
+          const float4 bz = *reinterpret_cast<const float4 *>(sv + 2 * C + c0 + c4 * 4);
+          const float4 bg = *reinterpret_cast<const float4 *>(sv + 3 * C + c0 + c4 * 4);
+          const float bzz[4] = {bz.x, bz.y, bz.z, bz.w}, bgg[4] = {bg.x, bg.y, bg.z, bg.w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int c = c4 * 4 + i;
+            v[c] = (__uint_as_float(vo[c]) + bzz[i]) * sigmoidf(__uint_as_float(vg[c]) + bgg[i]);
+          }
+        }
+        if (live) {
+          if (vec_path) {
+            store_out16<OT>(orow + c0, v, res, p.residual);
+          } else {
+#pragma unroll
+            for (int c = 0; c < 16; ++c) {
+              if (c0 + c < p.cz) {
+                float x = v[c];
+                if (p.residual) x += to_f32<OT>(orow[c0 + c]);
+                orow[c0 + c] = from_f32<OT>(x);
+              }
+            }
+          }
+        }
+        if (load_res) {
+#pragma unroll
+          for (int w = 0; w < kResWords; ++w) res[w] = res_next[w];
+        }
       }
       tc_fence_before();
       __syncwarp();
@@ -840,7 +908,6 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
     tmem_dealloc(tmem, 512);
   }
 }
-
 }  // namespace tri
 
 // ---------------------------------------------------------------------------
@@ -1040,7 +1107,7 @@ af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L,
 
     CUtensorMap xmap;
     if (!encode_map_3d(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x, L.n, rc, C, L.jp * 2, (uint64_t)ca.x_hs * 2,
-                       128, 1, C, CU_TENSOR_MAP_SWIZZLE_NONE))
+                       64, 1, C, CU_TENSOR_MAP_SWIZZLE_128B))
       return fail(ctx, AF2_ERR_CUDA, "cuTensorMapEncodeTiled failed for the contracted block");
     OutputArgs oa;
     oa.out = out;
