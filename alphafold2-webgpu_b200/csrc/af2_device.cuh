@@ -305,6 +305,22 @@ __device__ __forceinline__ float sigmoidf(float v) {
   return r;
 }
 
+// Logistic function from one hardware tanh: sigmoid(v) = 0.5 + 0.5 tanh(v / 2).
+// tanh.approx has a relative error below 2^-10.98, so the result is within
+// about 2.5e-4 absolute -- used where the multi-function unit, not memory,
+// would otherwise bound the kernel (the gated projections).
+__device__ __forceinline__ float tanhf_approx(float v) {
+  float t;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(v));
+  return t;
+}
+
+// Packed f32x2 arithmetic (two lanes of f32 per instruction on sm_100).
+__device__ __forceinline__ float2 f2fma(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+__device__ __forceinline__ float2 f2add(float2 a, float2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ float2 f2mul(float2 a, float2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ float2 f2(float a) { return make_float2(a, a); }
+
 // Two 16-bit values of a 32-bit word -> f32 (low half first).
 template <typename T>
 __device__ __forceinline__ float2 unpack2(uint32_t w);

@@ -172,27 +172,30 @@ template <typename ZT>
 __device__ __forceinline__ void ln_row_thread(uint8_t *tile, uint32_t chunk_bytes, int row, const float *gamma,
                                               const float *beta, int cz, float inv_cz, float eps) {
   auto chunk_ptr = [&](int c) { return tile + (c >> 3) * chunk_bytes + sw128_offset(row, c & 7); };
-  const float x0 = unpack2<ZT>(reinterpret_cast<const uint32_t *>(chunk_ptr(0))[0]).x;
-  float s1 = 0.f, s2 = 0.f;
+  const float2 x0 = f2(unpack2<ZT>(reinterpret_cast<const uint32_t *>(chunk_ptr(0))[0]).x);
+  const float2 neg_x0 = f2(-x0.x);
+  float2 s1 = f2(0.f), s2 = f2(0.f);  // even and odd channels, summed separately
 #pragma unroll 4
   for (int c = 0; c < 16; ++c) {
     const uint4 v = *reinterpret_cast<const uint4 *>(chunk_ptr(c));
     const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const float2 f = unpack2<ZT>(w[i]);
-      const int ch = c * 8 + 2 * i;
-      const float d0 = (cz == 128 || ch < cz) ? f.x - x0 : 0.f;
-      const float d1 = (cz == 128 || ch + 1 < cz) ? f.y - x0 : 0.f;
-      s1 += d0 + d1;
-      s2 = fmaf(d0, d0, fmaf(d1, d1, s2));
+      float2 d = f2add(unpack2<ZT>(w[i]), neg_x0);
+      if (cz != 128) {
+        const int ch = c * 8 + 2 * i;
+        d.x = ch < cz ? d.x : 0.f;
+        d.y = ch + 1 < cz ? d.y : 0.f;
+      }
+      s1 = f2add(s1, d);
+      s2 = f2fma(d, d, s2);
     }
   }
-  const float m1 = s1 * inv_cz;
-  const float mean = x0 + m1;
-  const float var = fmaxf(s2 * inv_cz - m1 * m1, 0.f);
+  const float m1 = (s1.x + s1.y) * inv_cz;
+  const float mean = x0.x + m1;
+  const float var = fmaxf((s2.x + s2.y) * inv_cz - m1 * m1, 0.f);
   const float rstd = rsqrtf(var + eps);
-  const float shift = -mean * rstd;
+  const float2 r2 = f2(rstd), sh2 = f2(-mean * rstd);
 #pragma unroll 4
   for (int c = 0; c < 16; ++c) {
     uint8_t *ptr = chunk_ptr(c);
@@ -202,14 +205,15 @@ __device__ __forceinline__ void ln_row_thread(uint8_t *tile, uint32_t chunk_byte
     const float4 g1 = *reinterpret_cast<const float4 *>(gamma + c * 8 + 4);
     const float4 b0 = *reinterpret_cast<const float4 *>(beta + c * 8);
     const float4 b1 = *reinterpret_cast<const float4 *>(beta + c * 8 + 4);
-    const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
-    const float b[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+    const float2 g[4] = {make_float2(g0.x, g0.y), make_float2(g0.z, g0.w), make_float2(g1.x, g1.y),
+                         make_float2(g1.z, g1.w)};
+    const float2 b[4] = {make_float2(b0.x, b0.y), make_float2(b0.z, b0.w), make_float2(b1.x, b1.y),
+                         make_float2(b1.z, b1.w)};
     uint32_t o[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const float2 f = unpack2<ZT>(w[i]);
-      o[i] = pack_half2(fmaf(fmaf(f.x, rstd, shift), g[2 * i], b[2 * i]),
-                        fmaf(fmaf(f.y, rstd, shift), g[2 * i + 1], b[2 * i + 1]));
+      const float2 y = f2fma(f2fma(unpack2<ZT>(w[i]), r2, sh2), g[i], b[i]);
+      o[i] = pack_half2(y.x, y.y);
     }
     *reinterpret_cast<uint4 *>(ptr) = make_uint4(o[0], o[1], o[2], o[3]);
   }
@@ -349,6 +353,7 @@ __global__ void __launch_bounds__(PJ_THREADS, 1)
     const int h = q * 32 + lane;
     const float bias_p = p.vec[(op ? kVBBP : kVBAP) * C + h];
     const float bias_g = p.vec[(op ? kVBBG : kVBAG) * C + h];
+    const float2 half2f = f2(0.5f), gate_shift = f2(0.5f * bias_g), bias_p2 = f2(bias_p);
     __half *out = op ? p.b_out : p.a_out;
     float *msk = reinterpret_cast<float *>(smem + PJ_OFF_MASK) + e * 64;
     auto mask_at = [&](int t, int k) -> float {
@@ -384,15 +389,18 @@ __global__ void __launch_bounds__(PJ_THREADS, 1)
 #pragma unroll
         for (int c4 = 0; c4 < 4; ++c4) {
           const float4 mk = *reinterpret_cast<const float4 *>(msk + part * 16 + c4 * 4);
-          const float mm[4] = {mk.x, mk.y, mk.z, mk.w};
-          float y[4];
+          const float2 mm[2] = {make_float2(mk.x, mk.y), make_float2(mk.z, mk.w)};
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int c = c4 * 4 + i;
-            y[i] = mm[i] * (__uint_as_float(vp[c]) + bias_p) * sigmoidf(__uint_as_float(vg[c]) + bias_g);
+          for (int i = 0; i < 2; ++i) {
+            const int c = c4 * 4 + 2 * i;
+            // a = mask (p + b_p) sigmoid(g + b_g), sigmoid(x) = 0.5 + 0.5 tanh(x / 2)
+            const float2 arg = f2fma(make_float2(__uint_as_float(vg[c]), __uint_as_float(vg[c + 1])), half2f,
+                                     gate_shift);
+            const float2 sg = f2fma(make_float2(tanhf_approx(arg.x), tanhf_approx(arg.y)), half2f, half2f);
+            const float2 pb = f2add(make_float2(__uint_as_float(vp[c]), __uint_as_float(vp[c + 1])), bias_p2);
+            const float2 y = f2mul(f2mul(pb, sg), mm[i]);
+            pk[c4 * 2 + i] = pack_half2(y.x, y.y);
           }
-          pk[c4 * 2] = pack_half2(y[0], y[1]);
-          pk[c4 * 2 + 1] = pack_half2(y[2], y[3]);
         }
         const int valid = p.n - (k0 + part * 16);
         __half *dst = row_out + part * 16;
@@ -598,8 +606,9 @@ __global__ void __launch_bounds__(CT_THREADS, 1)
 // Kernel 3: LN_out + output projection + gate + residual.
 // ---------------------------------------------------------------------------
 constexpr int OP_STAGES = 2;
-// warp 0 TMA, 1 MMA, 2-5 transpose/LayerNorm (one thread per pair row),
-// 6-9 epilogue of output channels [0, 64), 10-13 of [64, 128).
+// warp 0 TMA, 1 MMA, 2-5 LN_out of X (two threads per pair of pairs, each
+// over half the channels), 6-9 LN_in of z (one thread per pair row), 10-13
+// epilogue (one thread per pair row, all 128 output channels).
 constexpr int OP_THREADS = 448;
 constexpr uint32_t OP_W_BYTES = 2 * 2 * 16384;                 // W_z, W_g
 constexpr uint32_t OP_X_BYTES = 128 * 256, OP_Z_BYTES = 128 * 256;
@@ -607,7 +616,8 @@ constexpr uint32_t OP_STAGE_BYTES = OP_X_BYTES + OP_Z_BYTES;
 constexpr uint32_t OP_OFF_STAGE = OP_W_BYTES;
 // ln_out gamma/beta, b_z, b_g, ln_in gamma/beta
 constexpr uint32_t OP_OFF_VEC = OP_OFF_STAGE + OP_STAGES * OP_STAGE_BYTES;
-constexpr uint32_t OP_OFF_BAR = OP_OFF_VEC + 6 * 512;
+constexpr uint32_t OP_OFF_XSTAT = OP_OFF_VEC + 6 * 512;  // [2 tiles][2 halves][64] float4 partial sums
+constexpr uint32_t OP_OFF_BAR = OP_OFF_XSTAT + 2 * 2 * 64 * 16;
 constexpr uint32_t OP_SMEM = OP_OFF_BAR + 256 + 1024;
 
 struct OutputArgs {
@@ -673,7 +683,7 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
   const uint32_t drain = bar0 + 8u * 10;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + OP_OFF_BAR + 128);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + OP_OFF_BAR + 136);
-  // [0] ln_out gamma, [128] ln_out beta, [256] b_z, [384] b_g, [512] ln_in gamma, [640] ln_in beta
+  // [0] ln_out gamma, [128] ln_out beta, [256] b_z, [384] -log2(e) b_g, [512] ln_in gamma, [640] ln_in beta
   float *sv = reinterpret_cast<float *>(smem + OP_OFF_VEC);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -682,18 +692,19 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
   for (int i = threadIdx.x; i < 6 * C; i += OP_THREADS) {
     const int q = i / C, e = i % C;
     const int src = q == 0 ? kVLnOutW : q == 1 ? kVLnOutB : q == 2 ? kVBZ : q == 3 ? kVBG : q == 4 ? kVLnInW : kVLnInB;
-    sv[i] = p.vec[src * C + e];
+    // b_g is kept pre-multiplied by -log2(e): the gate is 1 / (1 + 2^(-(x + b_g) log2 e)).
+    sv[i] = q == 3 ? p.vec[src * C + e] * -1.4426950408889634f : p.vec[src * C + e];
   }
   fence_async_smem();
   if (threadIdx.x == 0) {
     for (int s = 0; s < OP_STAGES; ++s) {
       mbar_init(full(s), 1);
-      mbar_init(ready(s), 4);
+      mbar_init(ready(s), 8);
       mbar_init(empty(s), 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(acc_full(b), 1);
-      mbar_init(acc_empty(b), 8);
+      mbar_init(acc_empty(b), 4);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -774,15 +785,19 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
       }
     }
     __syncwarp();
-  } else if (warp < 6) {
-    // ---- LN_out of X in place (warps 2-3), LN_in of z (warps 4-5) ----
+  } else if (warp < 10) {
+    // ---- LN_out of X in place (warps 2-5) and LN_in of z (warps 6-9) ----
     // X arrives MN-major: two 64-pair blocks 16 KB apart, each 128 h-rows of
-    // 128 B, 128B-swizzled.  A thread owns the adjacent pairs (2c, 2c + 1), so
-    // it reads and writes whole 32-bit words and never touches another
-    // thread's columns.
+    // 128 B, 128B-swizzled.  An X thread owns the adjacent pairs (2c, 2c + 1)
+    // over half of the channels; the two halves' shifted sums meet in shared
+    // memory.  Nobody touches another thread's columns, so the normalisation
+    // is in place.
     const float inv_cz = 1.f / static_cast<float>(p.cz), inv_ch = 1.f / static_cast<float>(p.ch);
-    const bool x_role = warp < 4;
-    const int c = (warp & 1) * 32 + lane;  // 0..63
+    const bool x_role = warp < 6;
+    const int tx = (warp - 2) * 32 + lane;  // 0..127 among the X warps
+    const int c = tx & 63, hh = tx >> 6;
+    const int zrow = (warp - 6) * 32 + lane;
+    float4 *xstat = reinterpret_cast<float4 *>(smem + OP_OFF_XSTAT);
     int it = 0;
     for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x, ++it) {
       const int s = it % OP_STAGES;
@@ -797,31 +812,36 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
           return reinterpret_cast<uint32_t *>(col + h * 128 + ((((pl >> 3) ^ (h & 7))) << 4));
         };
         const float2 x0 = __half22float2(*reinterpret_cast<const __half2 *>(word(0)));
-        float s1a = 0.f, s2a = 0.f, s1b = 0.f, s2b = 0.f;
+        const float2 neg_x0 = make_float2(-x0.x, -x0.y);
+        float2 s1 = f2(0.f), s2 = f2(0.f);
+        const int h0 = hh * 64;
 #pragma unroll 8
-        for (int h = 0; h < C; ++h) {
-          const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(word(h)));
-          const bool in = p.ch == C || h < p.ch;
-          const float da = in ? f.x - x0.x : 0.f, db = in ? f.y - x0.y : 0.f;
-          s1a += da;
-          s2a = fmaf(da, da, s2a);
-          s1b += db;
-          s2b = fmaf(db, db, s2b);
+        for (int h = h0; h < h0 + 64; ++h) {
+          float2 d = f2add(__half22float2(*reinterpret_cast<const __half2 *>(word(h))), neg_x0);
+          if (p.ch != C && h >= p.ch) d = f2(0.f);
+          s1 = f2add(s1, d);
+          s2 = f2fma(d, d, s2);
         }
-        const float ma = s1a * inv_ch, mb = s1b * inv_ch;
-        const float ra = rsqrtf(fmaxf(s2a * inv_ch - ma * ma, 0.f) + p.eps_out);
-        const float rb = rsqrtf(fmaxf(s2b * inv_ch - mb * mb, 0.f) + p.eps_out);
-        const float sha = -(x0.x + ma) * ra, shb = -(x0.y + mb) * rb;
+        float4 *slot = xstat + (it & 1) * 128;
+        slot[hh * 64 + c] = make_float4(s1.x, s1.y, s2.x, s2.y);
+        named_barrier(1, 128);
+        const float4 o = slot[(hh ^ 1) * 64 + c];
+        s1 = f2add(s1, make_float2(o.x, o.y));
+        s2 = f2add(s2, make_float2(o.z, o.w));
+        const float2 m1 = f2mul(s1, f2(inv_ch));
+        const float ra = rsqrtf(fmaxf(s2.x * inv_ch - m1.x * m1.x, 0.f) + p.eps_out);
+        const float rb = rsqrtf(fmaxf(s2.y * inv_ch - m1.y * m1.y, 0.f) + p.eps_out);
+        const float2 r2 = make_float2(ra, rb);
+        const float2 sh2 = make_float2(-(x0.x + m1.x) * ra, -(x0.y + m1.y) * rb);
 #pragma unroll 8
-        for (int h = 0; h < C; ++h) {
+        for (int h = h0; h < h0 + 64; ++h) {
           uint32_t *w = word(h);
-          const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(w));
-          const float g = sv[h], b = sv[C + h];
-          *w = pack_half2(fmaf(fmaf(f.x, ra, sha), g, b), fmaf(fmaf(f.y, rb, shb), g, b));
+          const float2 y = f2fma(f2fma(__half22float2(*reinterpret_cast<const __half2 *>(w)), r2, sh2), f2(sv[h]),
+                                 f2(sv[C + h]));
+          *w = pack_half2(y.x, y.y);
         }
       } else {
-        ln_row_thread<ZT>(zs, 16384, c, sv + 4 * C, sv + 5 * C, p.cz, inv_cz, p.eps_in);
-        ln_row_thread<ZT>(zs, 16384, c + 64, sv + 4 * C, sv + 5 * C, p.cz, inv_cz, p.eps_in);
+        ln_row_thread<ZT>(zs, 16384, zrow, sv + 4 * C, sv + 5 * C, p.cz, inv_cz, p.eps_in);
       }
       fence_async_smem();
       __syncwarp();
@@ -829,11 +849,11 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
     }
   } else {
     // ---- epilogue: (LN_out(X) W_z^T + b_z) * sigmoid(LN(z) W_g^T + b_g) (+ residual) ----
-    const int e = warp - 6;
-    const int half = e >> 2;       // output channels [64 half, 64 half + 64)
     const int q = warp & 3;
     const int pr = q * 32 + lane;
     const bool vec_path = p.cz == C;
+    const float2 one = f2(1.f), nlog2e = f2(-1.4426950408889634f);
+    constexpr int kResWords = sizeof(OT) * 16 / 16;  // uint4 words per 16 channels
     int it = 0;
     for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x, ++it) {
       const int il = t / p.tiles_j, j = (t % p.tiles_j) * 128 + pr;
@@ -841,25 +861,23 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
       const uint32_t bph = (it >> 1) & 1;
       OT *orow = reinterpret_cast<OT *>(p.out) + ((int64_t)(p.row_begin + il) * p.n + j) * p.out_rs;
       const bool live = j < p.n;
+      const bool load_res = p.residual && live && vec_path;
+      uint4 res[kResWords];
+      if (load_res) {  // the row's old values, fetched before the wait
+#pragma unroll
+        for (int w = 0; w < kResWords; ++w) res[w] = reinterpret_cast<const uint4 *>(orow)[w];
+      }
       if (!warp_wait(acc_full(buf), bph, abort_flag, p.err, kErrWaitEpilogue)) break;
       tc_fence_after();
       const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * 256;
-      constexpr int kResWords = sizeof(OT) * 16 / 16;  // uint4 words per 16 channels
-      const bool load_res = p.residual && live && vec_path;
-      uint4 res[kResWords];
-      if (load_res) {
-#pragma unroll
-        for (int w = 0; w < kResWords; ++w) res[w] = reinterpret_cast<const uint4 *>(orow + half * 64)[w];
-      }
 #pragma unroll 1
-      for (int part = 0; part < 4; ++part) {
-        const int c0 = half * 64 + part * 16;
+      for (int part = 0; part < 8; ++part) {
+        const int c0 = part * 16;
         uint32_t vo[16], vg[16];
         tmem_ld16(taddr + c0, vo);
         tmem_ld16(taddr + 128 + c0, vg);
-        // the next part's residual is fetched while this part computes
         uint4 res_next[kResWords];
-        if (load_res && part < 3) {
+        if (load_res && part < 7) {
 #pragma unroll
           for (int w = 0; w < kResWords; ++w) res_next[w] = reinterpret_cast<const uint4 *>(orow + c0 + 16)[w];
         }
@@ -869,11 +887,24 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
         for (int c4 = 0; c4 < 4; ++c4) {
           const float4 bz = *reinterpret_cast<const float4 *>(sv + 2 * C + c0 + c4 * 4);
           const float4 bg = *reinterpret_cast<const float4 *>(sv + 3 * C + c0 + c4 * 4);
-          const float bzz[4] = {bz.x, bz.y, bz.z, bz.w}, bgg[4] = {bg.x, bg.y, bg.z, bg.w};
+          const float2 bz2[2] = {make_float2(bz.x, bz.y), make_float2(bz.z, bz.w)};
+          const float2 bg2[2] = {make_float2(bg.x, bg.y), make_float2(bg.z, bg.w)};
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int c = c4 * 4 + i;
-            v[c] = (__uint_as_float(vo[c]) + bzz[i]) * sigmoidf(__uint_as_float(vg[c]) + bgg[i]);
+          for (int i = 0; i < 2; ++i) {
+            const int cc = c4 * 4 + 2 * i;
+            const float2 arg =
+                f2fma(make_float2(__uint_as_float(vg[cc]), __uint_as_float(vg[cc + 1])), nlog2e, bg2[i]);
+            float2 e;
+            asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e.x) : "f"(arg.x));
+            asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e.y) : "f"(arg.y));
+            const float2 den = f2add(e, one);
+            float2 gate;
+            asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(gate.x) : "f"(den.x));
+            asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(gate.y) : "f"(den.y));
+            const float2 y =
+                f2mul(f2add(make_float2(__uint_as_float(vo[cc]), __uint_as_float(vo[cc + 1])), bz2[i]), gate);
+            v[cc] = y.x;
+            v[cc + 1] = y.y;
           }
         }
         if (live) {
@@ -881,11 +912,11 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
             store_out16<OT>(orow + c0, v, res, p.residual);
           } else {
 #pragma unroll
-            for (int c = 0; c < 16; ++c) {
-              if (c0 + c < p.cz) {
-                float x = v[c];
-                if (p.residual) x += to_f32<OT>(orow[c0 + c]);
-                orow[c0 + c] = from_f32<OT>(x);
+            for (int cc = 0; cc < 16; ++cc) {
+              if (c0 + cc < p.cz) {
+                float x = v[cc];
+                if (p.residual) x += to_f32<OT>(orow[c0 + cc]);
+                orow[c0 + cc] = from_f32<OT>(x);
               }
             }
           }
