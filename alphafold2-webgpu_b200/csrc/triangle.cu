@@ -46,8 +46,13 @@ enum {
 
 constexpr unsigned kFull = 0xffffffffu;
 
+// Rounds the dynamic shared-memory base up to 1024 bytes (the 128-byte
+// swizzle atom).  The offset is added to the __shared__ pointer itself so the
+// compiler still knows every access through it is a shared-memory access
+// (LDS/STS); rounding through an integer would turn them into generic loads.
 __device__ __forceinline__ uint8_t *align1024(uint8_t *p) {
-  return reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
+  const uint32_t a = smem_u32(p);
+  return p + (((a + 1023u) & ~1023u) - a);
 }
 
 __device__ __forceinline__ float reduce16(float v) {
