@@ -39,6 +39,9 @@ sys.path.insert(0, str(ROOT / "alphafold2-webgpu_b200"))
 N = 1024
 CZ = CH = 128
 METRIC = "Evoformer pair-GEMM TFLOP/s & ms/block at N=1024; % of B200 bf16 TC peak"
+# dram__bytes_read.sum + dram__bytes_write.sum of one contract_kernel launch, from one ncu
+# capture of this script (profiles/triangle_contract_n1024_dram.md).
+CONTRACT_DRAM_BYTES = {1024: 771_527_680}
 
 
 def triangle_flops(n: int, cz: int = CZ, ch: int = CH) -> float:
@@ -265,10 +268,7 @@ def run_ours(args) -> None:
     # ---- roofline of the dominant kernel (the per-channel contraction) ----
     con = kernel["triangle.contract"]
     achieved = contraction_flops(N) / (con["avg_us"] * 1e-6) / 1e12
-    traffic_path = ROOT / "profiles" / "traffic.json"
-    traffic = None
-    if traffic_path.exists():
-        traffic = json.loads(traffic_path.read_text()).get("triangle.contract@N=1024")
+    traffic = CONTRACT_DRAM_BYTES.get(N)
     roofline = {"kernel": "triangle.contract", "bound": "tensor", "achieved": achieved,
                 "peak": peaks["bf16_tflops"], "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
                 "traffic": traffic, "peak_source": f"{peaks['source']} burst bf16",
