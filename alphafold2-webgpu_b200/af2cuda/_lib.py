@@ -65,6 +65,8 @@ SIGNATURES = {
                                                 ctypes.POINTER(OpStats)]),
     "af2_triangle_multiplication": (_i32, [_vp, _i32, ctypes.POINTER(TriangleShape), _vp, _i32, _vp, _vp, _i64, _f64,
                                            ctypes.POINTER(TriangleOptions), _vp, _i32, _vp, _vp]),
+    "af2_triangle_multiplication_static": (_i32, [_vp, _i32, ctypes.POINTER(TriangleShape), _vp, _i32, _vp, _vp, _i64,
+                                                  _f64, ctypes.POINTER(TriangleOptions), _vp, _i32, _vp]),
 }
 
 _lib = None

@@ -172,6 +172,25 @@ AF2_API af2_status af2_triangle_multiplication(af2_ctx *ctx, int direction, cons
                                        const af2_triangle_options *options, void *out, int out_dtype,
                                        void *workspace, void *stream);
 
+/*
+ * The device form above, taking its scratch from a fixed array in device
+ * memory instead of allocating.  No counterpart in the reference.  For hosts
+ * that cannot let a library call cudaMalloc: a memory manager that owns the
+ * device under a fixed budget, or a latency-sensitive path where cudaMalloc
+ * and cudaFree would synchronise the device.  The call allocates nothing; the
+ * array (16.5 MiB, enough for length <= 128 at c_z = c_hidden = 128) is held
+ * on each device where the library is loaded until the process exits, and
+ * larger shapes return AF2_ERR_UNSUPPORTED.  The first call on each device
+ * looks up the array's device address (once); make that first call before any
+ * stream capture.  All calls share the array: calls that overlap on the GPU
+ * race.  Arguments as af2_triangle_multiplication, without `workspace`.
+ */
+AF2_API af2_status af2_triangle_multiplication_static(af2_ctx *ctx, int direction, const af2_triangle_shape *shape,
+                                                      const void *z, int z_dtype, const float *mask,
+                                                      const float *packed_weights, int64_t weight_count,
+                                                      double epsilon, const af2_triangle_options *options,
+                                                      void *out, int out_dtype, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
