@@ -150,7 +150,11 @@ constexpr uint32_t PJ_W_BYTES = 4 * 2 * 16384;          // 128 KB
 constexpr uint32_t PJ_OFF_STAGE = PJ_W_BYTES;
 constexpr uint32_t PJ_OFF_VEC = PJ_OFF_STAGE + PJ_STAGES * PJ_STAGE_BYTES;  // LN-in gamma, beta
 constexpr uint32_t PJ_OFF_MASK = PJ_OFF_VEC + 2 * 512;                       // 8 warps x 64 f32
-constexpr uint32_t PJ_OFF_BAR = PJ_OFF_MASK + 8 * 256;
+// Output staging: the tile's gated a and b, each [128 h][64 pairs] f16 in
+// 128B-swizzled rows, written to HBM by two TMA stores.
+constexpr uint32_t PJ_OFF_OUT = PJ_OFF_MASK + 8 * 256;
+constexpr uint32_t PJ_OUT_BYTES = 128 * 128;
+constexpr uint32_t PJ_OFF_BAR = PJ_OFF_OUT + 2 * PJ_OUT_BYTES;
 constexpr uint32_t PJ_SMEM = PJ_OFF_BAR + 256 + 1024;
 
 struct ProjectArgs {
@@ -226,7 +230,8 @@ __device__ __forceinline__ void ln_row_thread(uint8_t *tile, uint32_t chunk_byte
 
 template <typename ZT>
 __global__ void __launch_bounds__(PJ_THREADS, 1)
-    project_kernel(const __grid_constant__ CUtensorMap zmap, const ProjectArgs p) {
+    project_kernel(const __grid_constant__ CUtensorMap zmap, const __grid_constant__ CUtensorMap amap,
+                   const __grid_constant__ CUtensorMap bmap, const ProjectArgs p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = align1024(smem_raw);
   const uint32_t sbase = smem_u32(smem);
@@ -238,8 +243,10 @@ __global__ void __launch_bounds__(PJ_THREADS, 1)
   auto acc_full = [&](int b) { return bar0 + 8u * (9 + b); };
   auto acc_empty = [&](int b) { return bar0 + 8u * (11 + b); };
   const uint32_t drain = bar0 + 8u * 13;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + PJ_OFF_BAR + 128);
-  volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + PJ_OFF_BAR + 136);
+  const uint32_t out_full = bar0 + 8u * 14;  // all 8 epilogue warps have staged the tile
+  const uint32_t out_free = bar0 + 8u * 15;  // the staged tile has been read by the TMA stores
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + PJ_OFF_BAR + 192);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + PJ_OFF_BAR + 200);
   float *sv = reinterpret_cast<float *>(smem + PJ_OFF_VEC);  // [0,128) gamma, [128,256) beta
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -258,6 +265,8 @@ __global__ void __launch_bounds__(PJ_THREADS, 1)
       mbar_init(acc_empty(b), 8);
     }
     mbar_init(drain, 1);
+    mbar_init(out_full, 8);
+    mbar_init(out_free, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -274,6 +283,8 @@ __global__ void __launch_bounds__(PJ_THREADS, 1)
     // ---- TMA producer ----
     if (lane == 0) {
       tma_prefetch_map(&zmap);
+      tma_prefetch_map(&amap);
+      tma_prefetch_map(&bmap);
       int it = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x, ++it) {
@@ -351,15 +362,16 @@ __global__ void __launch_bounds__(PJ_THREADS, 1)
       if (lane == 0) mbar_arrive(z_ready(s));
     }
   } else {
-    // ---- epilogue: TMEM -> gated f16 operand rows, channel-major ----
+    // ---- epilogue: TMEM -> gated f16 operand rows, staged, stored by TMA ----
     const int e = warp - 6;        // 0..7
     const int op = e >> 2;         // 0: a (a_p, a_g), 1: b (b_p, b_g)
     const int q = warp & 3;        // TMEM lane quarter this warp may read
     const int h = q * 32 + lane;
+    const bool storer = e == 0 && lane == 0;
     const float bias_p = p.vec[(op ? kVBBP : kVBAP) * C + h];
     const float bias_g = p.vec[(op ? kVBBG : kVBAG) * C + h];
     const float2 half2f = f2(0.5f), gate_shift = f2(0.5f * bias_g), bias_p2 = f2(bias_p);
-    __half *out = op ? p.b_out : p.a_out;
+    uint8_t *stage_row = smem + PJ_OFF_OUT + op * PJ_OUT_BYTES + h * 128;
     float *msk = reinterpret_cast<float *>(smem + PJ_OFF_MASK) + e * 64;
     auto mask_at = [&](int t, int k) -> float {
       if (t >= p.total_tiles || k >= p.n) return 0.f;
@@ -380,10 +392,11 @@ __global__ void __launch_bounds__(PJ_THREADS, 1)
       m0 = mask_at(tn, (tn % p.tiles_k) * PJ_TILE + lane);
       m1 = mask_at(tn, (tn % p.tiles_k) * PJ_TILE + 32 + lane);
       __syncwarp();
-      if (!warp_wait(acc_full(buf), bph, abort_flag, p.err, kErrWaitEpilogue)) break;
+      if (!warp_wait(acc_full(buf), bph, abort_flag, p.err, kErrWaitEpilogue) ||
+          !warp_wait(out_free, (it & 1) ^ 1, abort_flag, p.err, kErrWaitEpilogue))
+        break;
       tc_fence_after();
       const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * 256 + op * 2 * PJ_TILE;
-      __half *row_out = out + h * p.out_hs + r * p.out_rs + k0;
 #pragma unroll 1
       for (int part = 0; part < PJ_TILE / 16; ++part) {
         uint32_t vp[16], vg[16];
@@ -407,25 +420,34 @@ __global__ void __launch_bounds__(PJ_THREADS, 1)
             pk[c4 * 2 + i] = pack_half2(y.x, y.y);
           }
         }
-        const int valid = p.n - (k0 + part * 16);
-        __half *dst = row_out + part * 16;
-        if (valid >= 16) {
-          uint4 *d4 = reinterpret_cast<uint4 *>(dst);
-          d4[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-          d4[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
-        } else {
-#pragma unroll
-          for (int c = 0; c < 16; c += 2) {
-            const __half2 hv = *reinterpret_cast<const __half2 *>(&pk[c >> 1]);
-            if (c < valid) dst[c] = __low2half(hv);
-            if (c + 1 < valid) dst[c + 1] = __high2half(hv);
-          }
-        }
+        // 16 pairs = 16-byte chunks 2 part and 2 part + 1 of this channel's staged row
+        *reinterpret_cast<uint4 *>(stage_row + ((((2 * part) ^ (h & 7))) << 4)) =
+            make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        *reinterpret_cast<uint4 *>(stage_row + ((((2 * part + 1) ^ (h & 7))) << 4)) =
+            make_uint4(pk[4], pk[5], pk[6], pk[7]);
       }
+      fence_async_smem();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(acc_empty(buf));
+      if (lane == 0) {
+        mbar_arrive(acc_empty(buf));
+        mbar_arrive(out_full);
+      }
+      if (storer) {
+        // both operand tiles staged: one TMA store each ([128 h] x 64 pairs of row r)
+        if (!mbar_wait(out_full, it & 1, abort_flag, p.err, kErrWaitEpilogue)) {
+          it = -1;
+        } else {
+          tma_store_3d(&amap, sbase + PJ_OFF_OUT, k0, r, 0);
+          tma_store_3d(&bmap, sbase + PJ_OFF_OUT + PJ_OUT_BYTES, k0, r, 0);
+          bulk_commit();
+          bulk_wait_read_all();
+          mbar_arrive(out_free);
+        }
+      }
+      if (__shfl_sync(kFull, it, 0) < 0) break;
     }
+    if (storer) bulk_wait_all();
   }
 
   tc_fence_before();
@@ -988,7 +1010,8 @@ CUtensorMapDataType map_type(int dtype) {
 }
 
 template <typename ZT>
-af2_status launch_project(af2_ctx *ctx, const CUtensorMap &zmap, const tri::ProjectArgs &a, cudaStream_t stream) {
+af2_status launch_project(af2_ctx *ctx, const CUtensorMap &zmap, const CUtensorMap &amap, const CUtensorMap &bmap,
+                          const tri::ProjectArgs &a, cudaStream_t stream) {
   static bool configured = false;
   if (!configured) {
     cudaError_t e = cudaFuncSetAttribute(tri::project_kernel<ZT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -999,7 +1022,7 @@ af2_status launch_project(af2_ctx *ctx, const CUtensorMap &zmap, const tri::Proj
   const int grid = std::max(1, std::min(a.total_tiles, ctx->sm_count));
   {
     LaunchScope scope(ctx, stream, kProfTriangleProject);
-    tri::project_kernel<ZT><<<grid, tri::PJ_THREADS, tri::PJ_SMEM, stream>>>(zmap, a);
+    tri::project_kernel<ZT><<<grid, tri::PJ_THREADS, tri::PJ_SMEM, stream>>>(zmap, amap, bmap, a);
   }
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? AF2_OK : cuda_fail(ctx, e, "launch project kernel");
@@ -1098,8 +1121,15 @@ af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L,
   pa.transposed = out_dir ? 0 : 1;
   pa.eps = static_cast<float>(eps);
   pa.err = ctx->err_word;
-  af2_status st = zt == AF2_BF16 ? launch_project<__nv_bfloat16>(ctx, zmap_proj, pa, stream)
-                                 : launch_project<__half>(ctx, zmap_proj, pa, stream);
+  // The gated operands leave through TMA stores: [128 h][N rows][kp], one box = 64 pairs x 128 channels.
+  CUtensorMap amap_st, bmap_st;
+  if (!encode_map_3d(&amap_st, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a, L.n, L.n, C, L.kp * 2, L.ab_hs * 2, PJ_TILE, 1, C,
+                     CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_map_3d(&bmap_st, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, b, L.n, L.n, C, L.kp * 2, L.ab_hs * 2, PJ_TILE, 1, C,
+                     CU_TENSOR_MAP_SWIZZLE_128B))
+    return fail(ctx, AF2_ERR_CUDA, "cuTensorMapEncodeTiled failed for the projection's store maps");
+  af2_status st = zt == AF2_BF16 ? launch_project<__nv_bfloat16>(ctx, zmap_proj, amap_st, bmap_st, pa, stream)
+                                 : launch_project<__half>(ctx, zmap_proj, amap_st, bmap_st, pa, stream);
   if (st != AF2_OK) return st;
 
   // ---- per block of output rows: contraction, then output ----
