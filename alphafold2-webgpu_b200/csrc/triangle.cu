@@ -30,6 +30,7 @@
 #include "af2_internal.h"
 
 #include <algorithm>
+#include <cstring>
 
 namespace af2 {
 namespace tri {
@@ -633,18 +634,19 @@ __global__ void __launch_bounds__(CT_THREADS, 1)
 // Kernel 3: LN_out + output projection + gate + residual.
 // ---------------------------------------------------------------------------
 constexpr int OP_STAGES = 2;
-// warp 0 TMA, 1 MMA, 2-5 LN_out of X (two threads per pair of pairs, each
-// over half the channels), 6-9 LN_in of z (one thread per pair row), 10-13
+// warp 0 TMA, 1 MMA, 2-5 LN_out of X (two lanes per pair of pairs, each over
+// half the channels), 6-9 LN_in of z (one thread per pair row), 10-13
 // epilogue (one thread per pair row, all 128 output channels).
 constexpr int OP_THREADS = 448;
 constexpr uint32_t OP_W_BYTES = 2 * 2 * 16384;                 // W_z, W_g
 constexpr uint32_t OP_X_BYTES = 128 * 256, OP_Z_BYTES = 128 * 256;
 constexpr uint32_t OP_STAGE_BYTES = OP_X_BYTES + OP_Z_BYTES;
 constexpr uint32_t OP_OFF_STAGE = OP_W_BYTES;
-// ln_out gamma/beta, b_z, b_g, ln_in gamma/beta
-constexpr uint32_t OP_OFF_VEC = OP_OFF_STAGE + OP_STAGES * OP_STAGE_BYTES;
-constexpr uint32_t OP_OFF_XSTAT = OP_OFF_VEC + 6 * 512;  // [2 tiles][2 halves][64] float4 partial sums
-constexpr uint32_t OP_OFF_BAR = OP_OFF_XSTAT + 2 * 2 * 64 * 16;
+// Output staging for 16-bit outputs: [128 pairs][128 channels] as two
+// 128B-swizzled halves of 64 channels, written by TMA (store or add).
+constexpr uint32_t OP_OFF_OUT = OP_OFF_STAGE + OP_STAGES * OP_STAGE_BYTES;
+constexpr uint32_t OP_OUT_BYTES = 128 * 256;
+constexpr uint32_t OP_OFF_BAR = OP_OFF_OUT + OP_OUT_BYTES;
 constexpr uint32_t OP_SMEM = OP_OFF_BAR + 256 + 1024;
 
 struct OutputArgs {
@@ -657,47 +659,10 @@ struct OutputArgs {
   unsigned int *err;
 };
 
-// 16 consecutive channels of one output row: residual add (from `res`, the
-// row's old values as loaded earlier) and store.
-template <typename OT>
-__device__ __forceinline__ void store_out16(OT *dst, const float (&v)[16], const uint4 *res, int residual) {
-  if constexpr (sizeof(OT) == 4) {
-    float4 *d = reinterpret_cast<float4 *>(dst);
-#pragma unroll
-    for (int w = 0; w < 4; ++w) {
-      float4 o = make_float4(v[4 * w], v[4 * w + 1], v[4 * w + 2], v[4 * w + 3]);
-      if (residual) {
-        const float4 old = *reinterpret_cast<const float4 *>(&res[w]);
-        o.x += old.x; o.y += old.y; o.z += old.z; o.w += old.w;
-      }
-      d[w] = o;
-    }
-  } else {
-    uint4 *d = reinterpret_cast<uint4 *>(dst);
-#pragma unroll
-    for (int w = 0; w < 2; ++w) {
-      float x[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) x[i] = v[8 * w + i];
-      if (residual) {
-        float old[8];
-        unpack8<OT>(res[w], old);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) x[i] += old[i];
-      }
-      uint4 o;
-      OT *e = reinterpret_cast<OT *>(&o);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) e[i] = from_f32<OT>(x[i]);
-      d[w] = o;
-    }
-  }
-}
-
 template <typename ZT, typename OT>
 __global__ void __launch_bounds__(OP_THREADS, 1)
     output_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap zmap,
-                  const OutputArgs p) {
+                  const __grid_constant__ CUtensorMap omap, const OutputArgs p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = align1024(smem_raw);
   const uint32_t sbase = smem_u32(smem);
@@ -708,20 +673,19 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
   auto acc_full = [&](int b) { return bar0 + 8u * (6 + b); };
   auto acc_empty = [&](int b) { return bar0 + 8u * (8 + b); };
   const uint32_t drain = bar0 + 8u * 10;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + OP_OFF_BAR + 128);
-  volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + OP_OFF_BAR + 136);
-  // [0] ln_out gamma, [128] ln_out beta, [256] b_z, [384] -log2(e) b_g, [512] ln_in gamma, [640] ln_in beta
-  float *sv = reinterpret_cast<float *>(smem + OP_OFF_VEC);
+  const uint32_t out_full = bar0 + 8u * 11;  // all 4 epilogue warps have staged the tile
+  const uint32_t out_free = bar0 + 8u * 12;  // the staged tile has been read by TMA
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + OP_OFF_BAR + 192);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + OP_OFF_BAR + 200);
+  // Per-channel vectors are read straight from global memory: every lane of a
+  // warp reads the same element, one broadcast through L1.
+  const float *__restrict__ vln_out_w = p.vec + kVLnOutW * C, *__restrict__ vln_out_b = p.vec + kVLnOutB * C;
+  const float *__restrict__ vbz = p.vec + kVBZ * C, *__restrict__ vbg = p.vec + kVBG * C;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bool staged_out = sizeof(OT) == 2 && p.cz == C;
 
   load_weight_matrix(smem, p.w16 + (size_t)kWZ * C * C, threadIdx.x, OP_THREADS);
   load_weight_matrix(smem + 32768, p.w16 + (size_t)kWG * C * C, threadIdx.x, OP_THREADS);
-  for (int i = threadIdx.x; i < 6 * C; i += OP_THREADS) {
-    const int q = i / C, e = i % C;
-    const int src = q == 0 ? kVLnOutW : q == 1 ? kVLnOutB : q == 2 ? kVBZ : q == 3 ? kVBG : q == 4 ? kVLnInW : kVLnInB;
-    // b_g is kept pre-multiplied by -log2(e): the gate is 1 / (1 + 2^(-(x + b_g) log2 e)).
-    sv[i] = q == 3 ? p.vec[src * C + e] * -1.4426950408889634f : p.vec[src * C + e];
-  }
   fence_async_smem();
   if (threadIdx.x == 0) {
     for (int s = 0; s < OP_STAGES; ++s) {
@@ -734,6 +698,8 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
       mbar_init(acc_empty(b), 4);
     }
     mbar_init(drain, 1);
+    mbar_init(out_full, 4);
+    mbar_init(out_free, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -750,6 +716,7 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
     if (lane == 0) {
       tma_prefetch_map(&xmap);
       tma_prefetch_map(&zmap);
+      if (staged_out) tma_prefetch_map(&omap);
       int it = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x, ++it) {
@@ -815,16 +782,15 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
   } else if (warp < 10) {
     // ---- LN_out of X in place (warps 2-5) and LN_in of z (warps 6-9) ----
     // X arrives MN-major: two 64-pair blocks 16 KB apart, each 128 h-rows of
-    // 128 B, 128B-swizzled.  An X thread owns the adjacent pairs (2c, 2c + 1)
-    // over half of the channels; the two halves' shifted sums meet in shared
-    // memory.  Nobody touches another thread's columns, so the normalisation
-    // is in place.
+    // 128 B, 128B-swizzled.  Lanes 2c and 2c + 1 of an X warp own the adjacent
+    // pairs (2c', 2c' + 1) over the lower and upper half of the channels and
+    // combine their shifted sums with one shuffle.  Nobody touches another
+    // lane's columns, so the normalisation is in place.
     const float inv_cz = 1.f / static_cast<float>(p.cz), inv_ch = 1.f / static_cast<float>(p.ch);
     const bool x_role = warp < 6;
     const int tx = (warp - 2) * 32 + lane;  // 0..127 among the X warps
-    const int c = tx & 63, hh = tx >> 6;
+    const int c = tx >> 1, hh = tx & 1;
     const int zrow = (warp - 6) * 32 + lane;
-    float4 *xstat = reinterpret_cast<float4 *>(smem + OP_OFF_XSTAT);
     int it = 0;
     for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x, ++it) {
       const int s = it % OP_STAGES;
@@ -849,12 +815,10 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
           s1 = f2add(s1, d);
           s2 = f2fma(d, d, s2);
         }
-        float4 *slot = xstat + (it & 1) * 128;
-        slot[hh * 64 + c] = make_float4(s1.x, s1.y, s2.x, s2.y);
-        named_barrier(1, 128);
-        const float4 o = slot[(hh ^ 1) * 64 + c];
-        s1 = f2add(s1, make_float2(o.x, o.y));
-        s2 = f2add(s2, make_float2(o.z, o.w));
+        s1.x += __shfl_xor_sync(kFull, s1.x, 1);
+        s1.y += __shfl_xor_sync(kFull, s1.y, 1);
+        s2.x += __shfl_xor_sync(kFull, s2.x, 1);
+        s2.y += __shfl_xor_sync(kFull, s2.y, 1);
         const float2 m1 = f2mul(s1, f2(inv_ch));
         const float ra = rsqrtf(fmaxf(s2.x * inv_ch - m1.x * m1.x, 0.f) + p.eps_out);
         const float rb = rsqrtf(fmaxf(s2.y * inv_ch - m1.y * m1.y, 0.f) + p.eps_out);
@@ -863,12 +827,12 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
 #pragma unroll 8
         for (int h = h0; h < h0 + 64; ++h) {
           uint32_t *w = word(h);
-          const float2 y = f2fma(f2fma(__half22float2(*reinterpret_cast<const __half2 *>(w)), r2, sh2), f2(sv[h]),
-                                 f2(sv[C + h]));
+          const float2 y = f2fma(f2fma(__half22float2(*reinterpret_cast<const __half2 *>(w)), r2, sh2),
+                                 f2(vln_out_w[h]), f2(vln_out_b[h]));
           *w = pack_half2(y.x, y.y);
         }
       } else {
-        ln_row_thread<ZT>(zs, 16384, zrow, sv + 4 * C, sv + 5 * C, p.cz, inv_cz, p.eps_in);
+        ln_row_thread<ZT>(zs, 16384, zrow, p.vec + kVLnInW * C, p.vec + kVLnInB * C, p.cz, inv_cz, p.eps_in);
       }
       fence_async_smem();
       __syncwarp();
@@ -876,25 +840,25 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
     }
   } else {
     // ---- epilogue: (LN_out(X) W_z^T + b_z) * sigmoid(LN(z) W_g^T + b_g) (+ residual) ----
+    // 16-bit outputs with 128 channels are staged in shared memory and leave
+    // through TMA: a plain store, or an add into the pair for the residual
+    // form (the old values never pass through the SM).  Other outputs are
+    // written (and, for the residual, read) by the thread that owns the row.
     const int q = warp & 3;
     const int pr = q * 32 + lane;
-    const bool vec_path = p.cz == C;
+    const bool storer = warp == 10 && lane == 0;
     const float2 one = f2(1.f), nlog2e = f2(-1.4426950408889634f);
-    constexpr int kResWords = sizeof(OT) * 16 / 16;  // uint4 words per 16 channels
+    uint8_t *stage_row = smem + OP_OFF_OUT + pr * 128;
     int it = 0;
     for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x, ++it) {
-      const int il = t / p.tiles_j, j = (t % p.tiles_j) * 128 + pr;
+      const int il = t / p.tiles_j, j0 = (t % p.tiles_j) * 128, j = j0 + pr;
       const int buf = it & 1;
       const uint32_t bph = (it >> 1) & 1;
       OT *orow = reinterpret_cast<OT *>(p.out) + ((int64_t)(p.row_begin + il) * p.n + j) * p.out_rs;
       const bool live = j < p.n;
-      const bool load_res = p.residual && live && vec_path;
-      uint4 res[kResWords];
-      if (load_res) {  // the row's old values, fetched before the wait
-#pragma unroll
-        for (int w = 0; w < kResWords; ++w) res[w] = reinterpret_cast<const uint4 *>(orow)[w];
-      }
-      if (!warp_wait(acc_full(buf), bph, abort_flag, p.err, kErrWaitEpilogue)) break;
+      if (!warp_wait(acc_full(buf), bph, abort_flag, p.err, kErrWaitEpilogue) ||
+          (staged_out && !warp_wait(out_free, (it & 1) ^ 1, abort_flag, p.err, kErrWaitEpilogue)))
+        break;
       tc_fence_after();
       const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * 256;
 #pragma unroll 1
@@ -903,22 +867,18 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
         uint32_t vo[16], vg[16];
         tmem_ld16(taddr + c0, vo);
         tmem_ld16(taddr + 128 + c0, vg);
-        uint4 res_next[kResWords];
-        if (load_res && part < 7) {
-#pragma unroll
-          for (int w = 0; w < kResWords; ++w) res_next[w] = reinterpret_cast<const uint4 *>(orow + c0 + 16)[w];
-        }
         tmem_ld_wait();
         float v[16];
 #pragma unroll
         for (int c4 = 0; c4 < 4; ++c4) {
-          const float4 bz = *reinterpret_cast<const float4 *>(sv + 2 * C + c0 + c4 * 4);
-          const float4 bg = *reinterpret_cast<const float4 *>(sv + 3 * C + c0 + c4 * 4);
+          const float4 bz = *reinterpret_cast<const float4 *>(vbz + c0 + c4 * 4);
+          const float4 bg = *reinterpret_cast<const float4 *>(vbg + c0 + c4 * 4);
           const float2 bz2[2] = {make_float2(bz.x, bz.y), make_float2(bz.z, bz.w)};
-          const float2 bg2[2] = {make_float2(bg.x, bg.y), make_float2(bg.z, bg.w)};
+          const float2 bg2[2] = {f2mul(make_float2(bg.x, bg.y), nlog2e), f2mul(make_float2(bg.z, bg.w), nlog2e)};
 #pragma unroll
           for (int i = 0; i < 2; ++i) {
             const int cc = c4 * 4 + 2 * i;
+            // gate = 1 / (1 + 2^(-(g + b_g) log2 e))
             const float2 arg =
                 f2fma(make_float2(__uint_as_float(vg[cc]), __uint_as_float(vg[cc + 1])), nlog2e, bg2[i]);
             float2 e;
@@ -934,29 +894,54 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
             v[cc + 1] = y.y;
           }
         }
-        if (live) {
-          if (vec_path) {
-            store_out16<OT>(orow + c0, v, res, p.residual);
-          } else {
+        if (staged_out) {
+          // channels c0..c0+15 = 16-byte chunks (c0 % 64) / 8 and +1 of half c0 / 64 of row pr
+          uint4 o[2];
+          OT *e16 = reinterpret_cast<OT *>(o);
 #pragma unroll
-            for (int cc = 0; cc < 16; ++cc) {
-              if (c0 + cc < p.cz) {
-                float x = v[cc];
-                if (p.residual) x += to_f32<OT>(orow[c0 + cc]);
-                orow[c0 + cc] = from_f32<OT>(x);
-              }
+          for (int cc = 0; cc < 16; ++cc) e16[cc] = from_f32<OT>(v[cc]);
+          uint8_t *half_row = stage_row + (c0 >> 6) * 16384;
+          const int ch8 = (c0 & 63) >> 3;
+          *reinterpret_cast<uint4 *>(half_row + (((ch8) ^ (pr & 7)) << 4)) = o[0];
+          *reinterpret_cast<uint4 *>(half_row + (((ch8 + 1) ^ (pr & 7)) << 4)) = o[1];
+        } else if (live) {
+#pragma unroll
+          for (int cc = 0; cc < 16; ++cc) {
+            if (c0 + cc < p.cz) {
+              float x = v[cc];
+              if (p.residual) x += to_f32<OT>(orow[c0 + cc]);
+              orow[c0 + cc] = from_f32<OT>(x);
             }
           }
         }
-        if (load_res) {
-#pragma unroll
-          for (int w = 0; w < kResWords; ++w) res[w] = res_next[w];
-        }
       }
+      if (staged_out) fence_async_smem();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(acc_empty(buf));
+      if (lane == 0) {
+        mbar_arrive(acc_empty(buf));
+        if (staged_out) mbar_arrive(out_full);
+      }
+      if (staged_out && storer) {
+        if (!mbar_wait(out_full, it & 1, abort_flag, p.err, kErrWaitEpilogue)) {
+          it = -1;
+        } else {
+          const int i = p.row_begin + il;
+          if (p.residual) {
+            tma_reduce_add_3d(&omap, sbase + OP_OFF_OUT, 0, j0, i);
+            tma_reduce_add_3d(&omap, sbase + OP_OFF_OUT + 16384, 64, j0, i);
+          } else {
+            tma_store_3d(&omap, sbase + OP_OFF_OUT, 0, j0, i);
+            tma_store_3d(&omap, sbase + OP_OFF_OUT + 16384, 64, j0, i);
+          }
+          bulk_commit();
+          bulk_wait_read_all();
+          mbar_arrive(out_free);
+        }
+      }
+      if (__shfl_sync(kFull, it, 0) < 0) break;
     }
+    if (staged_out && storer) bulk_wait_all();
   }
 
   tc_fence_before();
@@ -1029,8 +1014,8 @@ af2_status launch_project(af2_ctx *ctx, const CUtensorMap &zmap, const CUtensorM
 }
 
 template <typename ZT, typename OT>
-af2_status launch_output(af2_ctx *ctx, const CUtensorMap &xmap, const CUtensorMap &zmap, const tri::OutputArgs &a,
-                         cudaStream_t stream) {
+af2_status launch_output(af2_ctx *ctx, const CUtensorMap &xmap, const CUtensorMap &zmap, const CUtensorMap &omap,
+                         const tri::OutputArgs &a, cudaStream_t stream) {
   static bool configured = false;
   if (!configured) {
     cudaError_t e = cudaFuncSetAttribute(tri::output_kernel<ZT, OT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1041,7 +1026,7 @@ af2_status launch_output(af2_ctx *ctx, const CUtensorMap &xmap, const CUtensorMa
   const int grid = std::max(1, std::min(a.total_tiles, ctx->sm_count));
   {
     LaunchScope scope(ctx, stream, kProfTriangleOutput);
-    tri::output_kernel<ZT, OT><<<grid, tri::OP_THREADS, tri::OP_SMEM, stream>>>(xmap, zmap, a);
+    tri::output_kernel<ZT, OT><<<grid, tri::OP_THREADS, tri::OP_SMEM, stream>>>(xmap, zmap, omap, a);
   }
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? AF2_OK : cuda_fail(ctx, e, "launch output kernel");
@@ -1049,11 +1034,11 @@ af2_status launch_output(af2_ctx *ctx, const CUtensorMap &xmap, const CUtensorMa
 
 template <typename ZT>
 af2_status launch_output_any(af2_ctx *ctx, int out_dtype, const CUtensorMap &xmap, const CUtensorMap &zmap,
-                             const tri::OutputArgs &a, cudaStream_t stream) {
+                             const CUtensorMap &omap, const tri::OutputArgs &a, cudaStream_t stream) {
   switch (out_dtype) {
-    case AF2_F32: return launch_output<ZT, float>(ctx, xmap, zmap, a, stream);
-    case AF2_F16: return launch_output<ZT, __half>(ctx, xmap, zmap, a, stream);
-    default: return launch_output<ZT, __nv_bfloat16>(ctx, xmap, zmap, a, stream);
+    case AF2_F32: return launch_output<ZT, float>(ctx, xmap, zmap, omap, a, stream);
+    case AF2_F16: return launch_output<ZT, __half>(ctx, xmap, zmap, omap, a, stream);
+    default: return launch_output<ZT, __nv_bfloat16>(ctx, xmap, zmap, omap, a, stream);
   }
 }
 
@@ -1143,6 +1128,13 @@ af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L,
       !encode_map_3d(&zmap_out, map_type(zt), zsrc, C, L.n, L.n, row_bytes, row_bytes * L.n, 64, 128, 1,
                      CU_TENSOR_MAP_SWIZZLE_128B))
     return fail(ctx, AF2_ERR_CUDA, "cuTensorMapEncodeTiled failed for the contraction maps");
+  // 16-bit outputs with 128 channels leave through TMA: [N][N][128], one box = 64 channels x 128 pairs.
+  CUtensorMap omap;
+  std::memset(&omap, 0, sizeof omap);
+  if (out_dtype != AF2_F32 && L.cz == C &&
+      !encode_map_3d(&omap, map_type(out_dtype), out, C, L.n, L.n, row_bytes, row_bytes * L.n, 64, 128, 1,
+                     CU_TENSOR_MAP_SWIZZLE_128B))
+    return fail(ctx, AF2_ERR_CUDA, "cuTensorMapEncodeTiled failed for the output store map");
   static bool contract_configured = false;
   if (!contract_configured) {
     cudaError_t e = cudaFuncSetAttribute(contract_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, CT_SMEM);
@@ -1191,8 +1183,8 @@ af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L,
     oa.eps_in = static_cast<float>(eps);
     oa.eps_out = static_cast<float>(eps / ((double)n * (double)n));
     oa.err = ctx->err_word;
-    st = zt == AF2_BF16 ? launch_output_any<__nv_bfloat16>(ctx, out_dtype, xmap, zmap_out, oa, stream)
-                        : launch_output_any<__half>(ctx, out_dtype, xmap, zmap_out, oa, stream);
+    st = zt == AF2_BF16 ? launch_output_any<__nv_bfloat16>(ctx, out_dtype, xmap, zmap_out, omap, oa, stream)
+                        : launch_output_any<__half>(ctx, out_dtype, xmap, zmap_out, omap, oa, stream);
     if (st != AF2_OK) return st;
   }
   return AF2_OK;
