@@ -78,6 +78,9 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatil
 // ---------------------------------------------------------------------------
 __global__ void prep_weights_kernel(const float *__restrict__ packed, int cz, int ch, __half *__restrict__ w16,
                                     float *__restrict__ vec) {
+  // The LayerNorm affine maps are folded into the projections that follow
+  // them: LN(x) W^T + b = ((x - mean) rstd) (W diag(gamma))^T + (b + W beta),
+  // so the kernels normalise without gamma/beta and the weights carry them.
   const int64_t o_lniw = 0, o_lnib = cz, o_apw = 2 * cz;
   const int64_t o_apb = o_apw + (int64_t)ch * cz, o_agw = o_apb + ch, o_agb = o_agw + (int64_t)ch * cz;
   const int64_t o_bpw = o_agb + ch, o_bpb = o_bpw + (int64_t)ch * cz, o_bgw = o_bpb + ch;
@@ -88,31 +91,35 @@ __global__ void prep_weights_kernel(const float *__restrict__ packed, int cz, in
     const int m = idx / (C * C), r = (idx / C) % C, c = idx % C;
     float v = 0.f;
     switch (m) {
-      case kWAP: if (r < ch && c < cz) v = packed[o_apw + (int64_t)r * cz + c]; break;
-      case kWAG: if (r < ch && c < cz) v = packed[o_agw + (int64_t)r * cz + c]; break;
-      case kWBP: if (r < ch && c < cz) v = packed[o_bpw + (int64_t)r * cz + c]; break;
-      case kWBG: if (r < ch && c < cz) v = packed[o_bgw + (int64_t)r * cz + c]; break;
-      case kWZ: if (r < cz && c < ch) v = packed[o_zw + (int64_t)r * ch + c]; break;
-      default: if (r < cz && c < cz) v = packed[o_gw + (int64_t)r * cz + c]; break;
+      case kWAP: if (r < ch && c < cz) v = packed[o_apw + (int64_t)r * cz + c] * packed[o_lniw + c]; break;
+      case kWAG: if (r < ch && c < cz) v = packed[o_agw + (int64_t)r * cz + c] * packed[o_lniw + c]; break;
+      case kWBP: if (r < ch && c < cz) v = packed[o_bpw + (int64_t)r * cz + c] * packed[o_lniw + c]; break;
+      case kWBG: if (r < ch && c < cz) v = packed[o_bgw + (int64_t)r * cz + c] * packed[o_lniw + c]; break;
+      case kWZ: if (r < cz && c < ch) v = packed[o_zw + (int64_t)r * ch + c] * packed[o_lnow + c]; break;
+      default: if (r < cz && c < cz) v = packed[o_gw + (int64_t)r * cz + c] * packed[o_lniw + c]; break;
     }
     w16[idx] = __float2half_rn(v);
   }
+  // Biases: b + W beta (f64 sums), padded with zeros.
   for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < kVecCount * C; idx += stride) {
     const int q = idx / C, e = idx % C;
-    float v = 0.f;
+    double v = 0.0;
+    auto fold = [&](int64_t o_w, int64_t o_b, int64_t o_beta, int rows, int cols) {
+      if (e >= rows) return 0.0;
+      double acc = packed[o_b + e];
+      for (int k = 0; k < cols; ++k) acc += (double)packed[o_w + (int64_t)e * cols + k] * (double)packed[o_beta + k];
+      return acc;
+    };
     switch (q) {
-      case kVLnInW: if (e < cz) v = packed[o_lniw + e]; break;
-      case kVLnInB: if (e < cz) v = packed[o_lnib + e]; break;
-      case kVBAP: if (e < ch) v = packed[o_apb + e]; break;
-      case kVBAG: if (e < ch) v = packed[o_agb + e]; break;
-      case kVBBP: if (e < ch) v = packed[o_bpb + e]; break;
-      case kVBBG: if (e < ch) v = packed[o_bgb + e]; break;
-      case kVLnOutW: if (e < ch) v = packed[o_lnow + e]; break;
-      case kVLnOutB: if (e < ch) v = packed[o_lnob + e]; break;
-      case kVBZ: if (e < cz) v = packed[o_zb + e]; break;
-      default: if (e < cz) v = packed[o_gb + e]; break;
+      case kVBAP: v = fold(o_apw, o_apb, o_lnib, ch, cz); break;
+      case kVBAG: v = fold(o_agw, o_agb, o_lnib, ch, cz); break;
+      case kVBBP: v = fold(o_bpw, o_bpb, o_lnib, ch, cz); break;
+      case kVBBG: v = fold(o_bgw, o_bgb, o_lnib, ch, cz); break;
+      case kVBZ: v = fold(o_zw, o_zb, o_lnob, cz, ch); break;
+      case kVBG: v = fold(o_gw, o_gb, o_lnib, cz, cz); break;
+      default: v = 0.0; break;  // the LayerNorm slots are not used by the kernels
     }
-    vec[idx] = v;
+    vec[idx] = static_cast<float>(v);
   }
 }
 
@@ -149,8 +156,7 @@ constexpr uint32_t PJ_CHUNK = PJ_TILE * 128;            // one 64-channel K chun
 constexpr uint32_t PJ_STAGE_BYTES = 2 * PJ_CHUNK;       // 16 KB
 constexpr uint32_t PJ_W_BYTES = 4 * 2 * 16384;          // 128 KB
 constexpr uint32_t PJ_OFF_STAGE = PJ_W_BYTES;
-constexpr uint32_t PJ_OFF_VEC = PJ_OFF_STAGE + PJ_STAGES * PJ_STAGE_BYTES;  // LN-in gamma, beta
-constexpr uint32_t PJ_OFF_MASK = PJ_OFF_VEC + 2 * 512;                       // 8 warps x 64 f32
+constexpr uint32_t PJ_OFF_MASK = PJ_OFF_STAGE + PJ_STAGES * PJ_STAGE_BYTES;  // 8 warps x 64 f32
 // Output staging: the tile's gated a and b, each [128 h][64 pairs] f16 in
 // 128B-swizzled rows, written to HBM by two TMA stores.
 constexpr uint32_t PJ_OFF_OUT = PJ_OFF_MASK + 8 * 256;
@@ -171,16 +177,16 @@ struct ProjectArgs {
   unsigned int *err;
 };
 
-// LayerNorm of pair row `row` of a 128B-swizzled K-major tile (two 64-channel
-// chunks `chunk_bytes` apart), in place, 16-bit input -> f16, one thread per
-// row.  gamma/beta live in shared memory (every lane reads the same channel,
-// a broadcast).  Channels >= cz are padding: zero input, zero gamma and beta,
-// and outside the statistics.  The statistics are one pass over values
-// shifted by the row's first element, which keeps the f32 sums well
-// conditioned.
+// Normalisation of pair row `row` of a 128B-swizzled K-major tile (two
+// 64-channel chunks `chunk_bytes` apart), in place, 16-bit input -> f16, one
+// thread per row: (x - mean) * rstd.  The LayerNorm's gamma and beta are
+// folded into the weights that consume the tile.  Channels >= cz are padding
+// (zero input) and stay out of the statistics; the weights ignore them.  The
+// statistics are one pass over values shifted by the row's first element,
+// which keeps the f32 sums well conditioned.
 template <typename ZT>
-__device__ __forceinline__ void ln_row_thread(uint8_t *tile, uint32_t chunk_bytes, int row, const float *gamma,
-                                              const float *beta, int cz, float inv_cz, float eps) {
+__device__ __forceinline__ void ln_row_thread(uint8_t *tile, uint32_t chunk_bytes, int row, int cz, float inv_cz,
+                                              float eps) {
   auto chunk_ptr = [&](int c) { return tile + (c >> 3) * chunk_bytes + sw128_offset(row, c & 7); };
   const float2 x0 = f2(unpack2<ZT>(reinterpret_cast<const uint32_t *>(chunk_ptr(0))[0]).x);
   const float2 neg_x0 = f2(-x0.x);
@@ -211,18 +217,10 @@ __device__ __forceinline__ void ln_row_thread(uint8_t *tile, uint32_t chunk_byte
     uint8_t *ptr = chunk_ptr(c);
     const uint4 v = *reinterpret_cast<const uint4 *>(ptr);
     const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-    const float4 g0 = *reinterpret_cast<const float4 *>(gamma + c * 8);
-    const float4 g1 = *reinterpret_cast<const float4 *>(gamma + c * 8 + 4);
-    const float4 b0 = *reinterpret_cast<const float4 *>(beta + c * 8);
-    const float4 b1 = *reinterpret_cast<const float4 *>(beta + c * 8 + 4);
-    const float2 g[4] = {make_float2(g0.x, g0.y), make_float2(g0.z, g0.w), make_float2(g1.x, g1.y),
-                         make_float2(g1.z, g1.w)};
-    const float2 b[4] = {make_float2(b0.x, b0.y), make_float2(b0.z, b0.w), make_float2(b1.x, b1.y),
-                         make_float2(b1.z, b1.w)};
     uint32_t o[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const float2 y = f2fma(f2fma(unpack2<ZT>(w[i]), r2, sh2), g[i], b[i]);
+      const float2 y = f2fma(unpack2<ZT>(w[i]), r2, sh2);
       o[i] = pack_half2(y.x, y.y);
     }
     *reinterpret_cast<uint4 *>(ptr) = make_uint4(o[0], o[1], o[2], o[3]);
@@ -248,12 +246,10 @@ __global__ void __launch_bounds__(PJ_THREADS, 1)
   const uint32_t out_free = bar0 + 8u * 15;  // the staged tile has been read by the TMA stores
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + PJ_OFF_BAR + 192);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + PJ_OFF_BAR + 200);
-  float *sv = reinterpret_cast<float *>(smem + PJ_OFF_VEC);  // [0,128) gamma, [128,256) beta
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   for (int m = 0; m < 4; ++m)
     load_weight_matrix(smem + m * 32768, p.w16 + (size_t)m * C * C, threadIdx.x, PJ_THREADS);
-  for (int i = threadIdx.x; i < 2 * C; i += PJ_THREADS) sv[i] = p.vec[(i < C ? kVLnInW : kVLnInB) * C + (i % C)];
   fence_async_smem();
   if (threadIdx.x == 0) {
     for (int s = 0; s < PJ_STAGES; ++s) {
@@ -357,7 +353,7 @@ __global__ void __launch_bounds__(PJ_THREADS, 1)
       const int s = it % PJ_STAGES;
       const uint32_t ph = (it / PJ_STAGES) & 1;
       if (!warp_wait(z_full(s), ph, abort_flag, p.err, kErrWaitNormalizer)) break;
-      ln_row_thread<ZT>(smem + PJ_OFF_STAGE + s * PJ_STAGE_BYTES, PJ_CHUNK, row, sv, sv + C, p.cz, inv_cz, p.eps);
+      ln_row_thread<ZT>(smem + PJ_OFF_STAGE + s * PJ_STAGE_BYTES, PJ_CHUNK, row, p.cz, inv_cz, p.eps);
       fence_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(z_ready(s));
@@ -679,7 +675,6 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
   volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + OP_OFF_BAR + 200);
   // Per-channel vectors are read straight from global memory: every lane of a
   // warp reads the same element, one broadcast through L1.
-  const float *__restrict__ vln_out_w = p.vec + kVLnOutW * C, *__restrict__ vln_out_b = p.vec + kVLnOutB * C;
   const float *__restrict__ vbz = p.vec + kVBZ * C, *__restrict__ vbg = p.vec + kVBG * C;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool staged_out = sizeof(OT) == 2 && p.cz == C;
@@ -807,9 +802,12 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
         const float2 x0 = __half22float2(*reinterpret_cast<const __half2 *>(word(0)));
         const float2 neg_x0 = make_float2(-x0.x, -x0.y);
         float2 s1 = f2(0.f), s2 = f2(0.f);
-        const int h0 = hh * 64;
+        // The upper half visits its rows in XOR-4 order within each group of
+        // 8, so the two halves of a warp read disjoint banks.
+        const int h0 = hh * 64, hx = hh * 4;
 #pragma unroll 8
-        for (int h = h0; h < h0 + 64; ++h) {
+        for (int k = 0; k < 64; ++k) {
+          const int h = h0 + (k ^ hx);
           float2 d = f2add(__half22float2(*reinterpret_cast<const __half2 *>(word(h))), neg_x0);
           if (p.ch != C && h >= p.ch) d = f2(0.f);
           s1 = f2add(s1, d);
@@ -825,14 +823,13 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
         const float2 r2 = make_float2(ra, rb);
         const float2 sh2 = make_float2(-(x0.x + m1.x) * ra, -(x0.y + m1.y) * rb);
 #pragma unroll 8
-        for (int h = h0; h < h0 + 64; ++h) {
-          uint32_t *w = word(h);
-          const float2 y = f2fma(f2fma(__half22float2(*reinterpret_cast<const __half2 *>(w)), r2, sh2),
-                                 f2(vln_out_w[h]), f2(vln_out_b[h]));
+        for (int k = 0; k < 64; ++k) {
+          uint32_t *w = word(h0 + (k ^ hx));
+          const float2 y = f2fma(__half22float2(*reinterpret_cast<const __half2 *>(w)), r2, sh2);
           *w = pack_half2(y.x, y.y);
         }
       } else {
-        ln_row_thread<ZT>(zs, 16384, zrow, p.vec + kVLnInW * C, p.vec + kVLnInB * C, p.cz, inv_cz, p.eps_in);
+        ln_row_thread<ZT>(zs, 16384, zrow, p.cz, inv_cz, p.eps_in);
       }
       fence_async_smem();
       __syncwarp();
