@@ -298,7 +298,7 @@ __global__ void __launch_bounds__(PJ_THREADS, 1)
         tma_load_3d(dst, &zmap, z_full(s), 0, c1, c2);
         tma_load_3d(dst + PJ_CHUNK, &zmap, z_full(s), 64, c1, c2);
       }
-      if (!ok) {  // wait for the loads still landing before the CTA exits
+      {  // every load issued has landed before the CTA exits (immediate unless a consumer gave up)
         for (int j = it > PJ_STAGES ? it - PJ_STAGES : 0; j < it; ++j)
           mbar_wait_drain(z_full(j % PJ_STAGES), (j / PJ_STAGES) & 1, p.err);
       }
@@ -337,10 +337,10 @@ __global__ void __launch_bounds__(PJ_THREADS, 1)
         mma_commit(z_empty(s));
         mma_commit(acc_full(buf));
       }
-      if (!ok) {
-        mma_commit(drain);
-        mbar_wait_drain(drain, 0, p.err);
-      }
+      // Every MMA has completed before TMEM is freed, whether or not a consumer gave up.
+      (void)ok;
+      mma_commit(drain);
+      mbar_wait_drain(drain, 0, p.err);
     }
     __syncwarp();
   } else if (warp < 6) {
@@ -533,7 +533,7 @@ __global__ void __launch_bounds__(CT_THREADS, 1)
           tma_load_3d(dst + CT_A_BYTES, &bmap, full(s), kb * CT_BK, ni * CT_BN, h);
         }
       }
-      if (!ok) {
+      {  // every load issued has landed before the CTA exits (immediate unless a consumer gave up)
         for (int j = it > CT_STAGES ? it - CT_STAGES : 0; j < it; ++j)
           mbar_wait_drain(full(j % CT_STAGES), (j / CT_STAGES) & 1, p.err);
       }
@@ -568,10 +568,10 @@ __global__ void __launch_bounds__(CT_THREADS, 1)
         }
         if (ok) mma_commit(acc_full(buf));
       }
-      if (!ok) {
-        mma_commit(drain);
-        mbar_wait_drain(drain, 0, p.err);
-      }
+      // Every MMA has completed before TMEM is freed, whether or not a consumer gave up.
+      (void)ok;
+      mma_commit(drain);
+      mbar_wait_drain(drain, 0, p.err);
     }
     __syncwarp();
   } else {
@@ -729,7 +729,7 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
         tma_load_3d(zs, &zmap, full(s), 0, j0, p.row_begin + il);
         tma_load_3d(zs + 16384, &zmap, full(s), 64, j0, p.row_begin + il);
       }
-      if (!ok) {
+      {  // every load issued has landed before the CTA exits (immediate unless a consumer gave up)
         for (int j = it > OP_STAGES ? it - OP_STAGES : 0; j < it; ++j)
           mbar_wait_drain(full(j % OP_STAGES), (j / OP_STAGES) & 1, p.err);
       }
@@ -768,10 +768,10 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
         mma_commit(empty(s));
         mma_commit(acc_full(buf));
       }
-      if (!ok) {
-        mma_commit(drain);
-        mbar_wait_drain(drain, 0, p.err);
-      }
+      // Every MMA has completed before TMEM is freed, whether or not a consumer gave up.
+      (void)ok;
+      mma_commit(drain);
+      mbar_wait_drain(drain, 0, p.err);
     }
     __syncwarp();
   } else if (warp < 10) {
