@@ -365,6 +365,7 @@ __global__ void __launch_bounds__(PJ_THREADS, 1)
     const int q = warp & 3;        // TMEM lane quarter this warp may read
     const int h = q * 32 + lane;
     const bool storer = e == 0 && lane == 0;
+    bool store_pending = false;  // storer: a committed store may still be reading the staging buffer
     const float bias_p = p.vec[(op ? kVBBP : kVBAP) * C + h];
     const float bias_g = p.vec[(op ? kVBBG : kVBAG) * C + h];
     const float2 half2f = f2(0.5f), gate_shift = f2(0.5f * bias_g), bias_p2 = f2(bias_p);
@@ -389,18 +390,25 @@ __global__ void __launch_bounds__(PJ_THREADS, 1)
       m0 = mask_at(tn, (tn % p.tiles_k) * PJ_TILE + lane);
       m1 = mask_at(tn, (tn % p.tiles_k) * PJ_TILE + 32 + lane);
       __syncwarp();
-      if (!warp_wait(acc_full(buf), bph, abort_flag, p.err, kErrWaitEpilogue) ||
-          !warp_wait(out_free, (it & 1) ^ 1, abort_flag, p.err, kErrWaitEpilogue))
-        break;
+      if (!warp_wait(acc_full(buf), bph, abort_flag, p.err, kErrWaitEpilogue)) break;
       tc_fence_after();
       const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * 256 + op * 2 * PJ_TILE;
-#pragma unroll 1
+      // The whole tile leaves TMEM first (loads pipelined one part ahead of the
+      // math) and stays in registers as packed f16, so the accumulator is
+      // released early and the previous tile's TMA store keeps reading the
+      // staging buffer meanwhile.
+      uint32_t pk[PJ_TILE / 2];
+      uint32_t vp[2][16], vg[2][16];
+      tmem_ld16(taddr, vp[0]);
+      tmem_ld16(taddr + PJ_TILE, vg[0]);
+      tmem_ld_wait();
+#pragma unroll
       for (int part = 0; part < PJ_TILE / 16; ++part) {
-        uint32_t vp[16], vg[16];
-        tmem_ld16(taddr + part * 16, vp);
-        tmem_ld16(taddr + PJ_TILE + part * 16, vg);
-        tmem_ld_wait();
-        uint32_t pk[8];
+        const int cur = part & 1;
+        if (part + 1 < PJ_TILE / 16) {
+          tmem_ld16(taddr + (part + 1) * 16, vp[cur ^ 1]);
+          tmem_ld16(taddr + PJ_TILE + (part + 1) * 16, vg[cur ^ 1]);
+        }
 #pragma unroll
         for (int c4 = 0; c4 < 4; ++c4) {
           const float4 mk = *reinterpret_cast<const float4 *>(msk + part * 16 + c4 * 4);
@@ -409,27 +417,34 @@ __global__ void __launch_bounds__(PJ_THREADS, 1)
           for (int i = 0; i < 2; ++i) {
             const int c = c4 * 4 + 2 * i;
             // a = mask (p + b_p) sigmoid(g + b_g), sigmoid(x) = 0.5 + 0.5 tanh(x / 2)
-            const float2 arg = f2fma(make_float2(__uint_as_float(vg[c]), __uint_as_float(vg[c + 1])), half2f,
-                                     gate_shift);
+            const float2 arg = f2fma(make_float2(__uint_as_float(vg[cur][c]), __uint_as_float(vg[cur][c + 1])),
+                                     half2f, gate_shift);
             const float2 sg = f2fma(make_float2(tanhf_approx(arg.x), tanhf_approx(arg.y)), half2f, half2f);
-            const float2 pb = f2add(make_float2(__uint_as_float(vp[c]), __uint_as_float(vp[c + 1])), bias_p2);
+            const float2 pb =
+                f2add(make_float2(__uint_as_float(vp[cur][c]), __uint_as_float(vp[cur][c + 1])), bias_p2);
             const float2 y = f2mul(f2mul(pb, sg), mm[i]);
-            pk[c4 * 2 + i] = pack_half2(y.x, y.y);
+            pk[part * 8 + c4 * 2 + i] = pack_half2(y.x, y.y);
           }
         }
-        // 16 pairs = 16-byte chunks 2 part and 2 part + 1 of this channel's staged row
-        *reinterpret_cast<uint4 *>(stage_row + ((((2 * part) ^ (h & 7))) << 4)) =
-            make_uint4(pk[0], pk[1], pk[2], pk[3]);
-        *reinterpret_cast<uint4 *>(stage_row + ((((2 * part + 1) ^ (h & 7))) << 4)) =
-            make_uint4(pk[4], pk[5], pk[6], pk[7]);
+        if (part + 1 < PJ_TILE / 16) tmem_ld_wait();
       }
-      fence_async_smem();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(acc_empty(buf));
-        mbar_arrive(out_full);
+      if (lane == 0) mbar_arrive(acc_empty(buf));
+      if (storer && store_pending) {  // the previous tile's stores have read the staging buffer
+        bulk_wait_read_all();
+        mbar_arrive(out_free);
+        store_pending = false;
       }
+      if (!warp_wait(out_free, (it & 1) ^ 1, abort_flag, p.err, kErrWaitEpilogue)) break;
+      // 64 pairs = the eight 16-byte chunks of this channel's staged row
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch)
+        *reinterpret_cast<uint4 *>(stage_row + (((ch ^ (h & 7))) << 4)) =
+            make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]);
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(out_full);
       if (storer) {
         // both operand tiles staged: one TMA store each ([128 h] x 64 pairs of row r)
         if (!mbar_wait(out_full, it & 1, abort_flag, p.err, kErrWaitEpilogue)) {
@@ -438,8 +453,7 @@ __global__ void __launch_bounds__(PJ_THREADS, 1)
           tma_store_3d(&amap, sbase + PJ_OFF_OUT, k0, r, 0);
           tma_store_3d(&bmap, sbase + PJ_OFF_OUT + PJ_OUT_BYTES, k0, r, 0);
           bulk_commit();
-          bulk_wait_read_all();
-          mbar_arrive(out_free);
+          store_pending = true;
         }
       }
       if (__shfl_sync(kFull, it, 0) < 0) break;
