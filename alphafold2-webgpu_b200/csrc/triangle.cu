@@ -853,80 +853,124 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
     // ---- epilogue: (LN_out(X) W_z^T + b_z) * sigmoid(LN(z) W_g^T + b_g) (+ residual) ----
     // 16-bit outputs with 128 channels are staged in shared memory and leave
     // through TMA: a plain store, or an add into the pair for the residual
-    // form (the old values never pass through the SM).  Other outputs are
-    // written (and, for the residual, read) by the thread that owns the row.
+    // form (the old values never pass through the SM).  The first 48
+    // channels of a row are computed into registers before the staging buffer
+    // is claimed, so the previous tile's TMA keeps reading it meanwhile.
+    // Other outputs are written (and, for the residual, read) by the thread
+    // that owns the row.
     const int q = warp & 3;
     const int pr = q * 32 + lane;
     const bool storer = warp == 10 && lane == 0;
+    bool store_pending = false;
     const float2 one = f2(1.f), nlog2e = f2(-1.4426950408889634f);
     uint8_t *stage_row = smem + OP_OFF_OUT + pr * 128;
+    // Output values of 16 channels from their two accumulators.
+    auto gate16 = [&](const uint32_t (&vo)[16], const uint32_t (&vg)[16], int c0, float (&v)[16]) {
+#pragma unroll
+      for (int c4 = 0; c4 < 4; ++c4) {
+        const float4 bz = *reinterpret_cast<const float4 *>(vbz + c0 + c4 * 4);
+        const float4 bg = *reinterpret_cast<const float4 *>(vbg + c0 + c4 * 4);
+        const float2 bz2[2] = {make_float2(bz.x, bz.y), make_float2(bz.z, bz.w)};
+        const float2 bg2[2] = {f2mul(make_float2(bg.x, bg.y), nlog2e), f2mul(make_float2(bg.z, bg.w), nlog2e)};
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          const int cc = c4 * 4 + 2 * i;
+          // gate = 1 / (1 + 2^(-(g + b_g) log2 e))
+          const float2 arg = f2fma(make_float2(__uint_as_float(vg[cc]), __uint_as_float(vg[cc + 1])), nlog2e, bg2[i]);
+          float2 e;
+          asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e.x) : "f"(arg.x));
+          asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e.y) : "f"(arg.y));
+          const float2 den = f2add(e, one);
+          float2 gate;
+          asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(gate.x) : "f"(den.x));
+          asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(gate.y) : "f"(den.y));
+          const float2 y =
+              f2mul(f2add(make_float2(__uint_as_float(vo[cc]), __uint_as_float(vo[cc + 1])), bz2[i]), gate);
+          v[cc] = y.x;
+          v[cc + 1] = y.y;
+        }
+      }
+    };
+    // 16 channels c0.. as OT into the staged row: chunks (c0 % 64) / 8 and +1 of half c0 / 64.
+    auto stage16 = [&](const uint4 (&o)[2], int c0) {
+      uint8_t *half_row = stage_row + (c0 >> 6) * 16384;
+      const int ch8 = (c0 & 63) >> 3;
+      *reinterpret_cast<uint4 *>(half_row + (((ch8) ^ (pr & 7)) << 4)) = o[0];
+      *reinterpret_cast<uint4 *>(half_row + (((ch8 + 1) ^ (pr & 7)) << 4)) = o[1];
+    };
     int it = 0;
     for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x, ++it) {
       const int il = t / p.tiles_j, j0 = (t % p.tiles_j) * 128, j = j0 + pr;
       const int buf = it & 1;
       const uint32_t bph = (it >> 1) & 1;
-      OT *orow = reinterpret_cast<OT *>(p.out) + ((int64_t)(p.row_begin + il) * p.n + j) * p.out_rs;
-      const bool live = j < p.n;
-      if (!warp_wait(acc_full(buf), bph, abort_flag, p.err, kErrWaitEpilogue) ||
-          (staged_out && !warp_wait(out_free, (it & 1) ^ 1, abort_flag, p.err, kErrWaitEpilogue)))
-        break;
+      if (!warp_wait(acc_full(buf), bph, abort_flag, p.err, kErrWaitEpilogue)) break;
       tc_fence_after();
       const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * 256;
-#pragma unroll 1
-      for (int part = 0; part < 8; ++part) {
-        const int c0 = part * 16;
-        uint32_t vo[16], vg[16];
-        tmem_ld16(taddr + c0, vo);
-        tmem_ld16(taddr + 128 + c0, vg);
+      if (staged_out) {
+        uint32_t vo[2][16], vg[2][16];
+        uint4 held[3][2];  // channels 0..47 as OT, waiting for the staging buffer
+        tmem_ld16(taddr, vo[0]);
+        tmem_ld16(taddr + 128, vg[0]);
         tmem_ld_wait();
-        float v[16];
+        bool ok = true;
 #pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4) {
-          const float4 bz = *reinterpret_cast<const float4 *>(vbz + c0 + c4 * 4);
-          const float4 bg = *reinterpret_cast<const float4 *>(vbg + c0 + c4 * 4);
-          const float2 bz2[2] = {make_float2(bz.x, bz.y), make_float2(bz.z, bz.w)};
-          const float2 bg2[2] = {f2mul(make_float2(bg.x, bg.y), nlog2e), f2mul(make_float2(bg.z, bg.w), nlog2e)};
-#pragma unroll
-          for (int i = 0; i < 2; ++i) {
-            const int cc = c4 * 4 + 2 * i;
-            // gate = 1 / (1 + 2^(-(g + b_g) log2 e))
-            const float2 arg =
-                f2fma(make_float2(__uint_as_float(vg[cc]), __uint_as_float(vg[cc + 1])), nlog2e, bg2[i]);
-            float2 e;
-            asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e.x) : "f"(arg.x));
-            asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e.y) : "f"(arg.y));
-            const float2 den = f2add(e, one);
-            float2 gate;
-            asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(gate.x) : "f"(den.x));
-            asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(gate.y) : "f"(den.y));
-            const float2 y =
-                f2mul(f2add(make_float2(__uint_as_float(vo[cc]), __uint_as_float(vo[cc + 1])), bz2[i]), gate);
-            v[cc] = y.x;
-            v[cc + 1] = y.y;
+        for (int part = 0; part < 8; ++part) {
+          const int cur = part & 1;
+          if (part + 1 < 8) {
+            tmem_ld16(taddr + (part + 1) * 16, vo[cur ^ 1]);
+            tmem_ld16(taddr + 128 + (part + 1) * 16, vg[cur ^ 1]);
           }
-        }
-        if (staged_out) {
-          // channels c0..c0+15 = 16-byte chunks (c0 % 64) / 8 and +1 of half c0 / 64 of row pr
+          float v[16];
+          gate16(vo[cur], vg[cur], part * 16, v);
           uint4 o[2];
           OT *e16 = reinterpret_cast<OT *>(o);
 #pragma unroll
           for (int cc = 0; cc < 16; ++cc) e16[cc] = from_f32<OT>(v[cc]);
-          uint8_t *half_row = stage_row + (c0 >> 6) * 16384;
-          const int ch8 = (c0 & 63) >> 3;
-          *reinterpret_cast<uint4 *>(half_row + (((ch8) ^ (pr & 7)) << 4)) = o[0];
-          *reinterpret_cast<uint4 *>(half_row + (((ch8 + 1) ^ (pr & 7)) << 4)) = o[1];
-        } else if (live) {
+          if (part < 3) {
+            held[part][0] = o[0];
+            held[part][1] = o[1];
+          } else {
+            if (part == 3) {  // claim the staging buffer, then release the held channels into it
+              if (storer && store_pending) {
+                bulk_wait_read_all();
+                mbar_arrive(out_free);
+                store_pending = false;
+              }
+              ok = warp_wait(out_free, (it & 1) ^ 1, abort_flag, p.err, kErrWaitEpilogue);
+              if (!ok) break;
 #pragma unroll
-          for (int cc = 0; cc < 16; ++cc) {
-            if (c0 + cc < p.cz) {
-              float x = v[cc];
-              if (p.residual) x += to_f32<OT>(orow[c0 + cc]);
-              orow[c0 + cc] = from_f32<OT>(x);
+              for (int hp = 0; hp < 3; ++hp) stage16(held[hp], hp * 16);
+            }
+            stage16(o, part * 16);
+          }
+          if (part + 1 < 8) tmem_ld_wait();
+        }
+        if (!ok) break;
+        fence_async_smem();
+      } else {
+        OT *orow = reinterpret_cast<OT *>(p.out) + ((int64_t)(p.row_begin + il) * p.n + j) * p.out_rs;
+        const bool live = j < p.n;
+#pragma unroll 1
+        for (int part = 0; part < 8; ++part) {
+          const int c0 = part * 16;
+          uint32_t vo[16], vg[16];
+          tmem_ld16(taddr + c0, vo);
+          tmem_ld16(taddr + 128 + c0, vg);
+          tmem_ld_wait();
+          float v[16];
+          gate16(vo, vg, c0, v);
+          if (live) {
+#pragma unroll
+            for (int cc = 0; cc < 16; ++cc) {
+              if (c0 + cc < p.cz) {
+                float x = v[cc];
+                if (p.residual) x += to_f32<OT>(orow[c0 + cc]);
+                orow[c0 + cc] = from_f32<OT>(x);
+              }
             }
           }
         }
       }
-      if (staged_out) fence_async_smem();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
@@ -946,8 +990,7 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
             tma_store_3d(&omap, sbase + OP_OFF_OUT + 16384, 64, j0, i);
           }
           bulk_commit();
-          bulk_wait_read_all();
-          mbar_arrive(out_free);
+          store_pending = true;
         }
       }
       if (__shfl_sync(kFull, it, 0) < 0) break;
