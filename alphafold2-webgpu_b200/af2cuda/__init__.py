@@ -10,6 +10,9 @@ from .device import Device
 from .triangle import (TriangleGpuOptions, TriangleGpuResult, TriangleMultiplicationIncomingGpu,
                        TriangleMultiplicationOutgoingGpu, encode_triangle_multiplication,
                        encode_triangle_multiplication_tensors, triangle_weight_count, triangle_workspace_bytes)
+from .transition import (Q8Matrix, TransitionGpu, TransitionInput, TransitionResult, TransitionWeights,
+                         dequant_q8_tensors, encode_transition_tensors, pack_transition_weights,
+                         transition_weight_count, transition_workspace_bytes, validate_transition_input)
 from .types import (ORDER, TriangleMultiplicationInput, TriangleMultiplicationWeights, TriangleShape,
                     error_metrics, expected_weight_element_count, pack_weights, validate_triangle_input)
 
@@ -19,4 +22,7 @@ __all__ = [
     "encode_triangle_multiplication", "encode_triangle_multiplication_tensors", "triangle_weight_count",
     "triangle_workspace_bytes", "ORDER", "TriangleMultiplicationInput", "TriangleMultiplicationWeights",
     "TriangleShape", "error_metrics", "expected_weight_element_count", "pack_weights", "validate_triangle_input",
+    "Q8Matrix", "TransitionGpu", "TransitionInput", "TransitionResult", "TransitionWeights", "dequant_q8_tensors",
+    "encode_transition_tensors", "pack_transition_weights", "transition_weight_count", "transition_workspace_bytes",
+    "validate_transition_input",
 ]

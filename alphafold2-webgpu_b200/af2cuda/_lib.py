@@ -23,6 +23,7 @@ AF2_ERR_NO_DEVICE = 7
 
 AF2_F32, AF2_F16, AF2_BF16 = 0, 1, 2
 AF2_OUTGOING, AF2_INCOMING = 0, 1
+AF2_WEIGHTS_F32, AF2_WEIGHTS_Q8_BLOCK, AF2_WEIGHTS_Q8_CHANNEL = 0, 1, 2
 
 # Every symbol include/af2cuda.h declares, with (restype, argtypes).
 _vp = ctypes.c_void_p
@@ -42,6 +43,23 @@ class TriangleOptions(ctypes.Structure):
 class OpStats(ctypes.Structure):
     _fields_ = [("device_milliseconds", _f64), ("host_milliseconds", _f64), ("flops", _f64),
                 ("workspace_bytes", ctypes.c_uint64), ("peak_bytes", ctypes.c_uint64)]
+
+
+class Matrix(ctypes.Structure):
+    _fields_ = [("format", ctypes.c_int32), ("block", ctypes.c_int32), ("values", _vp), ("scales", _vp)]
+
+
+class TransitionShape(ctypes.Structure):
+    _fields_ = [("rows", _i64), ("channels", _i64), ("hidden_channels", _i64)]
+
+
+class TransitionWeights(ctypes.Structure):
+    _fields_ = [("layer_norm_scale", _vp), ("layer_norm_offset", _vp), ("first_weight", Matrix),
+                ("first_bias", _vp), ("second_weight", Matrix), ("second_bias", _vp)]
+
+
+class TransitionOptions(ctypes.Structure):
+    _fields_ = [("max_chunk_rows", ctypes.c_int32), ("residual", ctypes.c_int32)]
 
 
 SIGNATURES = {
@@ -67,6 +85,14 @@ SIGNATURES = {
                                            ctypes.POINTER(TriangleOptions), _vp, _i32, _vp, _vp]),
     "af2_triangle_multiplication_static": (_i32, [_vp, _i32, ctypes.POINTER(TriangleShape), _vp, _i32, _vp, _vp, _i64,
                                                   _f64, ctypes.POINTER(TriangleOptions), _vp, _i32, _vp]),
+    "af2_dequant_q8": (_i32, [_vp, ctypes.POINTER(Matrix), _i64, _i64, _vp, _vp]),
+    "af2_transition_weight_count": (_i64, [_i64, _i64]),
+    "af2_transition_check": (_i32, [ctypes.POINTER(TransitionShape), _i64, _f64, ctypes.c_char_p, ctypes.c_size_t]),
+    "af2_transition_workspace_bytes": (_i32, [ctypes.POINTER(TransitionShape), ctypes.POINTER(ctypes.c_uint64)]),
+    "af2_transition_host": (_i32, [_vp, ctypes.POINTER(TransitionShape), _vp, _vp, _i64, _f64,
+                                   ctypes.POINTER(TransitionOptions), _i32, _vp, ctypes.POINTER(OpStats)]),
+    "af2_transition": (_i32, [_vp, ctypes.POINTER(TransitionShape), _vp, _i32, ctypes.POINTER(TransitionWeights),
+                              _f64, ctypes.POINTER(TransitionOptions), _vp, _i32, _vp, _vp]),
 }
 
 _lib = None

@@ -30,6 +30,10 @@ enum ProfileKernel {
   kProfTriangleProject,
   kProfTriangleContract,
   kProfTriangleOutput,
+  kProfTransitionPrepare,
+  kProfTransitionNormalize,
+  kProfTransition,
+  kProfDequant,
   kProfCount
 };
 const char *profile_name(int id);
@@ -108,5 +112,25 @@ TriangleLayout triangle_layout(int64_t n, int64_t cz, int64_t ch, int64_t block_
 af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L, const void *z, int z_dtype,
                            const float *mask, const float *packed, double eps, int residual, void *out,
                            int out_dtype, void *workspace, cudaStream_t stream);
+
+// ---- transition (transition.cu) ----
+
+struct TransitionLayout {
+  int64_t rows = 0, c = 0, h = 0;
+  int64_t cp = 0;          // channels padded to 64 or 128 (the first GEMM's K, the second's N)
+  int64_t hp = 0;          // hidden channels padded to 64
+  bool fast_in = false;    // 16-bit x with 16-byte rows: TMA straight into the kernel, LayerNorm in place
+  int64_t chunk_rows = 0;  // rows per kernel launch (bounds the normalised copy otherwise)
+  size_t off_w1 = 0, off_w2 = 0, off_vec = 0, off_xn = 0, total = 0;
+};
+
+TransitionLayout transition_layout(int64_t rows, int64_t c, int64_t h, int x_dtype);
+
+af2_status transition_launch(af2_ctx *ctx, const TransitionLayout &L, const void *x, int x_dtype,
+                             const af2_transition_weights &w, double eps, int residual, void *out, int out_dtype,
+                             void *workspace, cudaStream_t stream);
+
+af2_status dequant_launch(af2_ctx *ctx, const af2_matrix &m, int64_t inner, int64_t cols, float *out,
+                          cudaStream_t stream);
 
 }  // namespace af2

@@ -3,6 +3,7 @@
 // read back) and the device form of each operator.
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <chrono>
 #include <cmath>
 #include <cstdio>
@@ -50,8 +51,9 @@ af2_status ensure(af2_ctx *ctx, DeviceBuffer &buf, size_t bytes, const char *wha
 }
 
 const char *profile_name(int id) {
-  static const char *names[kProfCount] = {"triangle.prepare", "triangle.relayout", "triangle.project",
-                                          "triangle.contract", "triangle.output"};
+  static const char *names[kProfCount] = {"triangle.prepare",     "triangle.relayout",     "triangle.project",
+                                          "triangle.contract",    "triangle.output",       "transition.prepare",
+                                          "transition.normalize", "transition.fused",      "q8.decode"};
   return (id >= 0 && id < kProfCount) ? names[id] : nullptr;
 }
 
@@ -162,6 +164,36 @@ af2_status check_device_errors(af2_ctx *ctx) {
                   "a kernel's bounded wait ran out (error bits 0x%x); the kernel returned without finishing", word);
     return fail(ctx, AF2_ERR_DEVICE_TIMEOUT, buf);
   }
+  return AF2_OK;
+}
+
+// validate (src/evoformer/transition.ts:140-156) for a C caller, then the kernels' limits.
+af2_status validate_transition(af2_ctx *ctx, const af2_transition_shape *shape, double epsilon) {
+  if (!shape) return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "shape is NULL");
+  if (!positive_safe(shape->rows) || !positive_safe(shape->channels) || !positive_safe(shape->hidden_channels))
+    return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "transition dimensions must be positive safe integers");
+  if ((double)shape->rows * (double)std::max(shape->channels, shape->hidden_channels) > (double)kMaxSafeInteger)
+    return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "tensor dimensions exceed JavaScript's safe integer range");
+  if (!(epsilon > 0) || !std::isfinite(epsilon))
+    return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "epsilon must be finite and positive; received " +
+                                                   std::to_string(epsilon));
+  if (shape->channels > 128)
+    return fail(ctx, AF2_ERR_UNSUPPORTED, "transition channels above 128 are not supported by the sm_100a kernel");
+  if (shape->hidden_channels > 1024)
+    return fail(ctx, AF2_ERR_UNSUPPORTED, "transition hidden channels above 1024 are not supported");
+  if (shape->rows > (int64_t(1) << 30))
+    return fail(ctx, AF2_ERR_UNSUPPORTED, "transition rows beyond 2^30 are not supported");
+  return AF2_OK;
+}
+
+af2_status validate_matrix(af2_ctx *ctx, const af2_matrix &m, const char *name) {
+  if (!m.values) return fail(ctx, AF2_ERR_INVALID_ARGUMENT, std::string(name) + " values are NULL");
+  if (m.format == AF2_WEIGHTS_F32) return AF2_OK;
+  if (m.format != AF2_WEIGHTS_Q8_BLOCK && m.format != AF2_WEIGHTS_Q8_CHANNEL)
+    return fail(ctx, AF2_ERR_INVALID_ARGUMENT, std::string(name) + " has an unknown weight format");
+  if (!m.scales) return fail(ctx, AF2_ERR_INVALID_ARGUMENT, std::string(name) + " scales are NULL");
+  if (m.format == AF2_WEIGHTS_Q8_BLOCK && m.block <= 0)
+    return fail(ctx, AF2_ERR_INVALID_ARGUMENT, std::string(name) + " block must be positive");
   return AF2_OK;
 }
 
@@ -408,6 +440,148 @@ af2_status af2_triangle_multiplication_host(af2_ctx *ctx, int direction, const a
     stats->peak_bytes = ctx->peak;
   }
   return AF2_OK;
+}
+
+int64_t af2_transition_weight_count(int64_t channels, int64_t hidden_channels) {
+  return 2 * channels + channels * hidden_channels + hidden_channels + hidden_channels * channels + channels;
+}
+
+af2_status af2_transition_check(const af2_transition_shape *shape, int64_t weight_count, double epsilon,
+                                char *message, size_t capacity) {
+  af2_ctx scratch;
+  af2_status st = validate_transition(&scratch, shape, epsilon);
+  if (st == AF2_OK) {
+    const int64_t expected = af2_transition_weight_count(shape->channels, shape->hidden_channels);
+    if (weight_count != expected)
+      st = fail(&scratch, AF2_ERR_INVALID_ARGUMENT, "packed weights have " + std::to_string(weight_count) +
+                                                        " values; expected " + std::to_string(expected));
+  }
+  if (message && capacity > 0) {
+    std::strncpy(message, scratch.last_error.c_str(), capacity - 1);
+    message[capacity - 1] = '\0';
+  }
+  return st;
+}
+
+af2_status af2_transition_workspace_bytes(const af2_transition_shape *shape, uint64_t *bytes) {
+  if (!shape || !bytes || !positive_safe(shape->rows) || !positive_safe(shape->channels) ||
+      !positive_safe(shape->hidden_channels))
+    return AF2_ERR_INVALID_ARGUMENT;
+  // Sized for the normalised copy too, whatever x's dtype turns out to be.
+  *bytes = transition_layout(shape->rows, shape->channels, shape->hidden_channels, AF2_F32).total;
+  return AF2_OK;
+}
+
+af2_status af2_transition(af2_ctx *ctx, const af2_transition_shape *shape, const void *x, int x_dtype,
+                          const af2_transition_weights *weights, double epsilon, const af2_transition_options *options,
+                          void *out, int out_dtype, void *workspace, void *stream) {
+  if (!ctx) return AF2_ERR_INVALID_ARGUMENT;
+  af2_status st = validate_transition(ctx, shape, epsilon);
+  if (st != AF2_OK) return st;
+  if (!x || !out || !weights) return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "a tensor pointer is NULL");
+  if (!weights->layer_norm_scale || !weights->layer_norm_offset || !weights->first_bias || !weights->second_bias)
+    return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "a weight vector is NULL");
+  if ((st = validate_matrix(ctx, weights->first_weight, "firstWeight")) != AF2_OK ||
+      (st = validate_matrix(ctx, weights->second_weight, "secondWeight")) != AF2_OK)
+    return st;
+  if (!valid_dtype(x_dtype) || !valid_dtype(out_dtype))
+    return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "dtype must be AF2_F32, AF2_F16 or AF2_BF16");
+  if (options && options->max_chunk_rows < 0)
+    return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "maxChunkRows must be a positive safe integer");
+  cudaSetDevice(ctx->device);
+  const TransitionLayout L = transition_layout(shape->rows, shape->channels, shape->hidden_channels, x_dtype);
+  void *ws = workspace;
+  if (!ws) {
+    if ((st = ensure(ctx, ctx->workspace, L.total, "transition scratch")) != AF2_OK) return st;
+    ws = ctx->workspace.ptr;
+  } else if (reinterpret_cast<uintptr_t>(ws) % 256 != 0) {
+    return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "workspace must be 256-byte aligned");
+  }
+  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+  return transition_launch(ctx, L, x, x_dtype, *weights, epsilon, options ? options->residual : 0, out, out_dtype,
+                           ws, s);
+}
+
+af2_status af2_transition_host(af2_ctx *ctx, const af2_transition_shape *shape, const void *x,
+                               const float *packed_weights, int64_t weight_count, double epsilon,
+                               const af2_transition_options *options, int io_dtype, void *out, af2_op_stats *stats) {
+  if (!ctx) return AF2_ERR_INVALID_ARGUMENT;
+  af2_status st = validate_transition(ctx, shape, epsilon);
+  if (st != AF2_OK) return st;
+  const int64_t expected = af2_transition_weight_count(shape->channels, shape->hidden_channels);
+  if (weight_count != expected)
+    return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "packed weights have " + std::to_string(weight_count) +
+                                                   " values; expected " + std::to_string(expected));
+  if (!x || !packed_weights || !out) return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "a tensor pointer is NULL");
+  if (!valid_dtype(io_dtype)) return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "dtype must be AF2_F32, AF2_F16 or AF2_BF16");
+  if (options && options->max_chunk_rows < 0)
+    return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "maxChunkRows must be a positive safe integer");
+  cudaSetDevice(ctx->device);
+  const auto t0 = std::chrono::steady_clock::now();
+  const int64_t c = shape->channels, h = shape->hidden_channels;
+  const size_t x_bytes = (size_t)shape->rows * c * dtype_bytes(io_dtype);
+  const size_t w_bytes = (size_t)weight_count * sizeof(float);
+  if ((st = ensure(ctx, ctx->staging[0], x_bytes, "x upload")) != AF2_OK ||
+      (st = ensure(ctx, ctx->staging[2], w_bytes, "weight upload")) != AF2_OK ||
+      (st = ensure(ctx, ctx->staging[3], x_bytes, "output")) != AF2_OK)
+    return st;
+  const TransitionLayout L = transition_layout(shape->rows, c, h, io_dtype);
+  if ((st = ensure(ctx, ctx->workspace, L.total, "transition scratch")) != AF2_OK) return st;
+  cudaStream_t s = ctx->stream;
+  const int residual = options ? options->residual : 0;
+  cudaError_t e;
+  if ((e = cudaMemcpyAsync(ctx->staging[0].ptr, x, x_bytes, cudaMemcpyHostToDevice, s)) != cudaSuccess ||
+      (e = cudaMemcpyAsync(ctx->staging[2].ptr, packed_weights, w_bytes, cudaMemcpyHostToDevice, s)) != cudaSuccess)
+    return cuda_fail(ctx, e, "upload inputs");
+  if (residual &&
+      (e = cudaMemcpyAsync(ctx->staging[3].ptr, ctx->staging[0].ptr, x_bytes, cudaMemcpyDeviceToDevice, s)) !=
+          cudaSuccess)
+    return cuda_fail(ctx, e, "seed residual output");
+  // packTransitionWeights order (transition.ts:140-177): LN scale, LN offset, W1, b1, W2, b2.
+  const float *pw = static_cast<const float *>(ctx->staging[2].ptr);
+  af2_transition_weights w{};
+  w.layer_norm_scale = pw;
+  w.layer_norm_offset = pw + c;
+  w.first_weight = af2_matrix{AF2_WEIGHTS_F32, 0, pw + 2 * c, nullptr};
+  w.first_bias = pw + 2 * c + c * h;
+  w.second_weight = af2_matrix{AF2_WEIGHTS_F32, 0, pw + 2 * c + c * h + h, nullptr};
+  w.second_bias = pw + 2 * c + 2 * c * h + h;
+  cudaEventRecord(ctx->ev_start, s);
+  st = transition_launch(ctx, L, ctx->staging[0].ptr, io_dtype, w, epsilon, residual, ctx->staging[3].ptr, io_dtype,
+                         ctx->workspace.ptr, s);
+  if (st != AF2_OK) return st;
+  cudaEventRecord(ctx->ev_stop, s);
+  if ((e = cudaMemcpyAsync(out, ctx->staging[3].ptr, x_bytes, cudaMemcpyDeviceToHost, s)) != cudaSuccess)
+    return cuda_fail(ctx, e, "read back output");
+  if ((e = cudaStreamSynchronize(s)) != cudaSuccess) return cuda_fail(ctx, e, "transition");
+  if ((st = check_device_errors(ctx)) != AF2_OK) return st;
+  if (stats) {
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, ctx->ev_start, ctx->ev_stop);
+    stats->device_milliseconds = ms;
+    stats->host_milliseconds =
+        std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+    // kernel-cost.ts: two GEMMs, rows x C x H each.
+    stats->flops = 4.0 * (double)shape->rows * (double)c * (double)h;
+    stats->workspace_bytes = L.total;
+    stats->peak_bytes = ctx->peak;
+  }
+  return AF2_OK;
+}
+
+af2_status af2_dequant_q8(af2_ctx *ctx, const af2_matrix *matrix, int64_t inner, int64_t cols, float *out,
+                          void *stream) {
+  if (!ctx) return AF2_ERR_INVALID_ARGUMENT;
+  if (!matrix || !out) return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "matrix or output is NULL");
+  if (!positive_safe(inner) || !positive_safe(cols))
+    return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "matrix dimensions must be positive safe integers");
+  if (matrix->format != AF2_WEIGHTS_Q8_BLOCK && matrix->format != AF2_WEIGHTS_Q8_CHANNEL)
+    return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "af2_dequant_q8 decodes q8 matrices only");
+  af2_status st = validate_matrix(ctx, *matrix, "matrix");
+  if (st != AF2_OK) return st;
+  cudaSetDevice(ctx->device);
+  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+  return dequant_launch(ctx, *matrix, inner, cols, out, s);
 }
 
 }  // extern "C"

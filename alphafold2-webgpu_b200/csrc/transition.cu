@@ -1,0 +1,792 @@
+// transition.cu -- the Evoformer transition (LayerNorm -> Linear C->H -> ReLU
+// -> Linear H->C, optional residual) as one persistent tcgen05 kernel, the
+// weight preparation that turns f32 or mixed-q8 weights into its f16 operand
+// tiles, and the bit-exact q8 decode.
+//
+// Reference: src/evoformer/transition.ts:91-138 (createLinearShader, the
+// A W + b (ReLU) projection), :179-245 (the LayerNorm kernel), :264-361
+// (TransitionGpu.run: normalise, first linear, second linear per row chunk)
+// and src/evoformer/block.ts:625-740 (encodeTransition with residualTarget);
+// q8 decode src/reference/dtype.ts:86-97.
+//
+// Kernel (one CTA per SM, 128-row tiles, persistent):
+//   warp 0      TMA: the x tile (16-bit, straight into the first GEMM's A
+//               operand) and the weight chunks through a 4-deep ring;
+//   warp 1      tcgen05 issue over one continuous stream of 64-wide hidden
+//               chunks j (all tiles of the CTA back to back): D1[j%4] =
+//               xn W1[:, chunk], and three chunks behind it, D2[tile] +=
+//               H[j-3] W2[chunk j-3, :] -- so the tensor pipe always has three
+//               first-GEMM chunks queued while the epilogue turns a finished
+//               one into the second GEMM's operand;
+//   warps 2-5   LayerNorm of the x tile in place, one thread per row;
+//   warps 6-9   first epilogue: D1 -> relu(scale1 * acc + b1) as f16 into
+//               the second GEMM's A operand (shared memory, never HBM);
+//   warps 10-13 second epilogue: D2 -> scale2 * acc + b2, staged and written
+//               by per-warp TMA stores (or TMA adds for the residual).
+// The hidden activations (4C per row) never leave the SM, so HBM traffic is
+// one read of x and one write of the output.
+//
+// Weights: the kernel multiplies f16 operands.  Every output column o of a
+// matrix carries an f32 scale applied in the epilogue: for per-channel q8 it
+// is the given scale and the operand holds the int8 codes themselves (exact
+// in f16); for f32 and block-q8 weights (decoded exactly to f32 first) it is
+// a power of two that brings the column's largest magnitude into [0.5, 1),
+// so the f16 rounding error is relative to the column's range.
+#include <algorithm>
+#include <string>
+
+#include "af2_device.cuh"
+#include "af2_internal.h"
+
+namespace af2 {
+namespace trn {
+
+constexpr int TILE = 128;     // rows per tile (one TMEM lane each)
+constexpr int HC = 64;        // hidden channels per chunk
+constexpr int STAGES = 4;     // weight-chunk ring
+constexpr int LAG = 3;        // second-GEMM chunks trail the first by this many
+constexpr int NBUF = 4;       // D1 accumulators and H operand buffers (> LAG)
+constexpr int THREADS = 448;  // 14 warps: 0 TMA, 1 MMA, 2-5 LayerNorm, 6-9 / 10-13 epilogues
+
+// Shared-memory map (bytes from the 1024-aligned base); kb = channel blocks of 64.
+//   A  2 x [kb][128 rows][128 B]      x tiles (normalised in place)
+//   W  STAGES x kb x 8 KB             weight chunks
+//   H  NBUF x [128 rows][128 B]       relu(hidden) chunks, f16
+//   O  [128 rows][128 B]              output staging (64 channels at a time)
+//   barriers, then gamma beta scale2 bias2 [cp] and scale1 bias1 [hp]
+__host__ __device__ constexpr uint32_t off_w(int kb) { return 2u * kb * 16384u; }
+__host__ __device__ constexpr uint32_t off_h(int kb) { return off_w(kb) + STAGES * kb * 8192u; }
+__host__ __device__ constexpr uint32_t off_o(int kb) { return off_h(kb) + NBUF * 16384u; }
+__host__ __device__ constexpr uint32_t off_bar(int kb) { return off_o(kb) + 16384u; }
+__host__ __device__ constexpr uint32_t off_vec(int kb) { return off_bar(kb) + 512u; }
+
+// Output modes.
+enum { kOutTmaStore = 0, kOutTmaAdd = 1, kOutDirect = 2, kOutDirectAdd = 3 };
+
+struct Args {
+  const float *vec;  // gamma[cp] beta[cp] s1[hp] b1[hp] s2[cp] b2[cp]
+  void *out;         // direct-store modes: [rows][c] of OT
+  int64_t rows;
+  int c, cp, kb, hp, nh, total_tiles;
+  int normalize;  // 1: x is raw 16-bit, normalised in place; 0: x is already LayerNorm(x) in f16
+  int out_mode;
+  float eps;
+  unsigned int *err;
+};
+
+// LayerNorm of row `row` of a 128B-swizzled K-major tile ([kb][128 rows][128 B])
+// in place, 16-bit in -> f16 out: (x - mean) * rstd * gamma + beta.  Channels
+// >= c are zero padding: outside the statistics, and gamma = beta = 0 there.
+// The sums run over values shifted by the row's first element, which keeps
+// the single-pass f32 variance well conditioned.
+template <typename XT>
+__device__ __forceinline__ void ln_row(uint8_t *tile, int kb, int row, int c, float inv_c, float eps,
+                                       const float *gamma, const float *beta) {
+  auto chunk_ptr = [&](int j) { return tile + (j >> 3) * 16384 + sw128_offset(row, j & 7); };
+  const int chunks = kb * 8;
+  const float x0 = unpack2<XT>(reinterpret_cast<const uint32_t *>(chunk_ptr(0))[0]).x;
+  const float2 neg_x0 = f2(-x0);
+  float2 s1 = f2(0.f), s2 = f2(0.f);
+#pragma unroll 4
+  for (int j = 0; j < chunks; ++j) {
+    const uint4 v = *reinterpret_cast<const uint4 *>(chunk_ptr(j));
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float2 d = f2add(unpack2<XT>(w[i]), neg_x0);
+      const int ch = j * 8 + 2 * i;
+      d.x = ch < c ? d.x : 0.f;
+      d.y = ch + 1 < c ? d.y : 0.f;
+      s1 = f2add(s1, d);
+      s2 = f2fma(d, d, s2);
+    }
+  }
+  const float m1 = (s1.x + s1.y) * inv_c;
+  const float mean = x0 + m1;
+  const float var = fmaxf((s2.x + s2.y) * inv_c - m1 * m1, 0.f);
+  const float rstd = rsqrtf(var + eps);
+  const float2 r2 = f2(rstd), nm2 = f2(-mean);
+#pragma unroll 2
+  for (int j = 0; j < chunks; ++j) {
+    uint8_t *ptr = chunk_ptr(j);
+    const uint4 v = *reinterpret_cast<const uint4 *>(ptr);
+    const float4 g0 = *reinterpret_cast<const float4 *>(gamma + j * 8);
+    const float4 g1 = *reinterpret_cast<const float4 *>(gamma + j * 8 + 4);
+    const float4 b0 = *reinterpret_cast<const float4 *>(beta + j * 8);
+    const float4 b1 = *reinterpret_cast<const float4 *>(beta + j * 8 + 4);
+    const float2 g[4] = {make_float2(g0.x, g0.y), make_float2(g0.z, g0.w), make_float2(g1.x, g1.y),
+                         make_float2(g1.z, g1.w)};
+    const float2 b[4] = {make_float2(b0.x, b0.y), make_float2(b0.z, b0.w), make_float2(b1.x, b1.y),
+                         make_float2(b1.z, b1.w)};
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 a = f2mul(g[i], r2);              // rstd * gamma
+      const float2 y = f2fma(f2add(unpack2<XT>(w[i]), nm2), a, b[i]);
+      o[i] = pack_half2(y.x, y.y);
+    }
+    *reinterpret_cast<uint4 *>(ptr) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+// Two f32 -> packed f16 with ReLU (cvt.rn.relu: max(0, round(v)) = round(max(0, v))).
+__device__ __forceinline__ uint32_t pack_half2_relu(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.relu.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+template <typename OT>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi);
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) {
+  return pack_half2(lo, hi);
+}
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float lo, float hi) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t *>(&h);
+}
+template <>
+__device__ __forceinline__ uint32_t pack2<float>(float, float) {
+  return 0;  // f32 output never goes through the 16-bit staging
+}
+
+template <typename XT, typename OT>
+__global__ void __launch_bounds__(THREADS, 1)
+    transition_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap w1map,
+                      const __grid_constant__ CUtensorMap w2map, const __grid_constant__ CUtensorMap omap,
+                      const Args p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = align1024(smem_raw);
+  const uint32_t sbase = smem_u32(smem);
+  const int kb = p.kb;
+  const uint32_t OFF_W = off_w(kb), OFF_H = off_h(kb), OFF_O = off_o(kb), OFF_BAR = off_bar(kb);
+  const uint32_t A_BYTES = kb * 16384u, W_BYTES = kb * 8192u;
+  const uint32_t bar0 = sbase + OFF_BAR;
+  auto a_raw = [&](int b) { return bar0 + 8u * b; };
+  auto a_full = [&](int b) { return bar0 + 8u * (2 + b); };
+  auto a_empty = [&](int b) { return bar0 + 8u * (4 + b); };
+  auto w_full = [&](int s) { return bar0 + 8u * (6 + s); };
+  auto w_empty = [&](int s) { return bar0 + 8u * (10 + s); };
+  auto d1_full = [&](int b) { return bar0 + 8u * (14 + b); };
+  auto d1_empty = [&](int b) { return bar0 + 8u * (18 + b); };
+  auto h_full = [&](int b) { return bar0 + 8u * (22 + b); };
+  auto h_empty = [&](int b) { return bar0 + 8u * (26 + b); };
+  auto d2_full = [&](int b) { return bar0 + 8u * (30 + b); };
+  auto d2_empty = [&](int b) { return bar0 + 8u * (32 + b); };
+  const uint32_t drain = bar0 + 8u * 34;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + OFF_BAR + 384);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + OFF_BAR + 392);
+  float *vec = reinterpret_cast<float *>(smem + off_vec(kb));
+  const float *gamma = vec, *beta = vec + p.cp, *s2v = vec + 2 * p.cp, *b2v = vec + 3 * p.cp;
+  const float *s1v = vec + 4 * p.cp, *b1v = vec + 4 * p.cp + p.hp;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nh = p.nh;
+  const int my_tiles = blockIdx.x < p.total_tiles ? (p.total_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  const int total = my_tiles * nh;  // hidden chunks this CTA works through
+
+  for (int i = threadIdx.x; i < 2 * p.cp; i += THREADS) vec[i] = p.vec[i];
+  for (int i = threadIdx.x; i < 2 * p.cp; i += THREADS) vec[2 * p.cp + i] = p.vec[2 * p.cp + 2 * p.hp + i];
+  for (int i = threadIdx.x; i < 2 * p.hp; i += THREADS) vec[4 * p.cp + i] = p.vec[2 * p.cp + i];
+  if (threadIdx.x == 0) {
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(a_raw(b), 1);
+      mbar_init(a_full(b), 4);
+      mbar_init(a_empty(b), 1);
+      mbar_init(d2_full(b), 1);
+      mbar_init(d2_empty(b), 4);
+    }
+    for (int b = 0; b < NBUF; ++b) {
+      mbar_init(d1_full(b), 1);
+      mbar_init(d1_empty(b), 4);
+      mbar_init(h_full(b), 4);
+      mbar_init(h_empty(b), 1);
+    }
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(w_full(s), 1);
+      mbar_init(w_empty(s), 1);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---- TMA producer: the same chunk stream as the MMA issuer ----
+    if (lane == 0) {
+      tma_prefetch_map(&xmap);
+      tma_prefetch_map(&w1map);
+      tma_prefetch_map(&w2map);
+      int x_issued = 0, ws = 0;
+      bool ok = true;
+      auto issue_x = [&](int it) -> bool {
+        const int b = it & 1;
+        if (!mbar_wait(a_empty(b), ((it >> 1) & 1) ^ 1, abort_flag, p.err, kErrWaitProducer)) return false;
+        const uint32_t dst = sbase + b * A_BYTES;
+        const int row0 = (blockIdx.x + it * gridDim.x) * TILE;
+        mbar_arrive_expect_tx(a_raw(b), A_BYTES);
+        for (int k = 0; k < kb; ++k) tma_load_3d(dst + k * 16384, &xmap, a_raw(b), k * 64, row0, 0);
+        ++x_issued;
+        return true;
+      };
+      auto issue_w = [&](bool first, int h) -> bool {
+        const int s = ws % STAGES;
+        if (!mbar_wait(w_empty(s), ((ws / STAGES) & 1) ^ 1, abort_flag, p.err, kErrWaitProducer)) return false;
+        const uint32_t dst = sbase + OFF_W + s * W_BYTES;
+        mbar_arrive_expect_tx(w_full(s), W_BYTES);
+        if (first)
+          tma_load_3d(dst, &w1map, w_full(s), 0, h * HC, 0);
+        else
+          tma_load_3d(dst, &w2map, w_full(s), h * HC, 0, 0);
+        ++ws;
+        return true;
+      };
+      if (my_tiles > 0) ok = issue_x(0);
+      const int early = nh > 1 ? 1 : 0;  // the next tile's x goes out after this chunk's W1
+      for (int j = 0; ok && j < total + LAG; ++j) {
+        if (j < total) {
+          ok = issue_w(true, j % nh);
+          const int it = j / nh;
+          if (ok && j % nh == early && it + 1 < my_tiles) ok = issue_x(it + 1);
+        }
+        if (ok && j >= LAG) ok = issue_w(false, (j - LAG) % nh);
+      }
+      // Every load issued lands before the CTA exits (immediate unless a consumer gave up).
+      for (int i = std::max(0, ws - STAGES); i < ws; ++i) mbar_wait_drain(w_full(i % STAGES), (i / STAGES) & 1, p.err);
+      for (int i = std::max(0, x_issued - 2); i < x_issued; ++i) mbar_wait_drain(a_raw(i & 1), (i >> 1) & 1, p.err);
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer ----
+    if (lane == 0) {
+      const uint32_t idesc1 = idesc_f16_f32(TILE, HC);
+      const uint32_t idesc2 = idesc_f16_f32(TILE, p.cp);
+      int ws = 0;
+      for (int j = 0; j < total + LAG; ++j) {
+        if (j < total) {  // first GEMM of chunk j -> D1[j % NBUF]
+          const int it = j / nh, h = j % nh, buf = it & 1, db = j % NBUF, s = ws % STAGES;
+          if ((h == 0 && !mbar_wait(a_full(buf), (it >> 1) & 1, abort_flag, p.err, kErrWaitMma)) ||
+              !mbar_wait(d1_empty(db), ((j / NBUF) & 1) ^ 1, abort_flag, p.err, kErrWaitMma) ||
+              !mbar_wait(w_full(s), (ws / STAGES) & 1, abort_flag, p.err, kErrWaitMma))
+            break;
+          tc_fence_after();
+          const uint32_t a_base = sbase + buf * A_BYTES, wb = sbase + OFF_W + s * W_BYTES;
+          for (int k = 0; k < kb; ++k)
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks)
+              mma_f16(tmem + db * HC, sdesc_k_sw128(a_base + k * 16384 + ks * 32),
+                      sdesc_k_sw128(wb + k * 8192 + ks * 32), idesc1, (k | ks) != 0);
+          mma_commit(w_empty(s));
+          mma_commit(d1_full(db));
+          if (h == nh - 1) mma_commit(a_empty(buf));
+          ++ws;
+        }
+        if (j >= LAG) {  // second GEMM of chunk i = j - LAG: D2[tile] += H[i % NBUF] W2[chunk]
+          const int i = j - LAG, it = i / nh, h = i % nh, buf = it & 1, hb = i % NBUF, s = ws % STAGES;
+          if (!mbar_wait(h_full(hb), (i / NBUF) & 1, abort_flag, p.err, kErrWaitMma) ||
+              !mbar_wait(w_full(s), (ws / STAGES) & 1, abort_flag, p.err, kErrWaitMma) ||
+              (h == 0 && !mbar_wait(d2_empty(buf), ((it >> 1) & 1) ^ 1, abort_flag, p.err, kErrWaitMma)))
+            break;
+          tc_fence_after();
+          const uint32_t hbase = sbase + OFF_H + hb * 16384, wb = sbase + OFF_W + s * W_BYTES;
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks)
+            mma_f16(tmem + 256 + buf * 128, sdesc_k_sw128(hbase + ks * 32), sdesc_k_sw128(wb + ks * 32), idesc2,
+                    (h > 0 || ks > 0) ? 1u : 0u);
+          mma_commit(w_empty(s));
+          mma_commit(h_empty(hb));
+          if (h == nh - 1) mma_commit(d2_full(buf));
+          ++ws;
+        }
+      }
+      // Every MMA has completed before TMEM is freed, whether or not a consumer gave up.
+      mma_commit(drain);
+      mbar_wait_drain(drain, 0, p.err);
+    }
+    __syncwarp();
+  } else if (warp < 6) {
+    // ---- LayerNorm of the x tile, in place ----
+    const int row = (warp - 2) * 32 + lane;
+    const float inv_c = 1.f / static_cast<float>(p.c);
+    for (int it = 0; it < my_tiles; ++it) {
+      const int buf = it & 1;
+      if (!warp_wait(a_raw(buf), (it >> 1) & 1, abort_flag, p.err, kErrWaitNormalizer)) break;
+      if (p.normalize) {
+        ln_row<XT>(smem + buf * A_BYTES, kb, row, p.c, inv_c, p.eps, gamma, beta);
+        fence_async_smem();
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(a_full(buf));
+    }
+  } else if (warp < 10) {
+    // ---- first epilogue: D1 chunk -> relu(scale1 * acc + b1) -> f16 H operand rows ----
+    const int q = warp & 3;  // TMEM lane quarter this warp may read
+    const int row = q * 32 + lane;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
+    for (int j = 0; j < total; ++j) {
+      const int db = j % NBUF, h = j % nh;
+      const uint32_t ph = (j / NBUF) & 1;
+      if (!warp_wait(d1_full(db), ph, abort_flag, p.err, kErrWaitEpilogue)) break;
+      tc_fence_after();
+      uint32_t v[2][32];
+      tmem_ld32(lane_base + db * HC, v[0]);
+      tmem_ld32(lane_base + db * HC + 32, v[1]);
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(d1_empty(db));
+      const float4 *sc = reinterpret_cast<const float4 *>(s1v + h * HC);
+      const float4 *bi = reinterpret_cast<const float4 *>(b1v + h * HC);
+      if (!warp_wait(h_empty(db), ph ^ 1, abort_flag, p.err, kErrWaitEpilogue)) break;
+      uint8_t *hrow = smem + OFF_H + db * 16384;
+#pragma unroll
+      for (int c16 = 0; c16 < 8; ++c16) {  // 8 hidden channels = one 16-byte chunk of the row
+        uint32_t pk[4];
+#pragma unroll
+        for (int i2 = 0; i2 < 2; ++i2) {
+          const float4 s = sc[c16 * 2 + i2], b = bi[c16 * 2 + i2];
+          const int c = c16 * 8 + i2 * 4;
+          const float2 y0 = f2fma(make_float2(__uint_as_float(v[c >> 5][c & 31]), __uint_as_float(v[c >> 5][(c + 1) & 31])),
+                                  make_float2(s.x, s.y), make_float2(b.x, b.y));
+          const float2 y1 =
+              f2fma(make_float2(__uint_as_float(v[c >> 5][(c + 2) & 31]), __uint_as_float(v[c >> 5][(c + 3) & 31])),
+                    make_float2(s.z, s.w), make_float2(b.z, b.w));
+          pk[i2 * 2] = pack_half2_relu(y0.x, y0.y);
+          pk[i2 * 2 + 1] = pack_half2_relu(y1.x, y1.y);
+        }
+        *reinterpret_cast<uint4 *>(hrow + sw128_offset(row, c16)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      }
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(h_full(db));
+    }
+  } else {
+    // ---- second epilogue: D2 -> scale2 * acc + b2, 64 channels at a time ----
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
+    bool store_pending = false;
+    for (int it = 0; it < my_tiles; ++it) {
+      const int buf = it & 1, t = blockIdx.x + it * gridDim.x;
+      if (!warp_wait(d2_full(buf), (it >> 1) & 1, abort_flag, p.err, kErrWaitEpilogue)) break;
+      tc_fence_after();
+      const int64_t grow = static_cast<int64_t>(t) * TILE + row;
+      for (int half = 0; half < kb; ++half) {
+        const int col0 = half * 64;
+        uint32_t v[2][32];
+        const uint32_t d2 = lane_base + 256 + buf * 128 + col0;
+        tmem_ld32(d2, v[0]);
+        tmem_ld32(d2 + 32, v[1]);
+        tmem_ld_wait();
+        if (half == kb - 1) {  // the whole accumulator is in registers: release it
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(d2_empty(buf));
+        }
+        const float *sc = s2v + col0, *bi = b2v + col0;
+        if (p.out_mode <= kOutTmaAdd) {
+          if (lane == 0 && store_pending) bulk_wait_read_all();  // this warp's last store has read the stage
+          __syncwarp();
+          uint8_t *stage = smem + OFF_O;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {  // 8 output channels = one 16-byte chunk of the staged row
+            uint32_t pk[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int c = j * 8 + 2 * i;
+              const float2 s = *reinterpret_cast<const float2 *>(sc + c);
+              const float2 b = *reinterpret_cast<const float2 *>(bi + c);
+              const float2 y = f2fma(
+                  make_float2(__uint_as_float(v[c >> 5][c & 31]), __uint_as_float(v[c >> 5][(c + 1) & 31])), s, b);
+              pk[i] = pack2<OT>(y.x, y.y);
+            }
+            *reinterpret_cast<uint4 *>(stage + sw128_offset(row, j)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          }
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            const uint32_t src = sbase + OFF_O + q * 4096;
+            if (p.out_mode == kOutTmaAdd)
+              tma_reduce_add_3d(&omap, src, col0, t * TILE + q * 32, 0);
+            else
+              tma_store_3d(&omap, src, col0, t * TILE + q * 32, 0);
+            bulk_commit();
+            store_pending = true;
+          }
+        } else if (grow < p.rows) {
+          OT *orow = static_cast<OT *>(p.out) + grow * p.c;
+          const bool add = p.out_mode == kOutDirectAdd;
+#pragma unroll
+          for (int i = 0; i < 64; ++i) {
+            const int ch = col0 + i;
+            if (ch < p.c) {
+              const float y = fmaf(__uint_as_float(v[i >> 5][i & 31]), sc[i], bi[i]);
+              orow[ch] = from_f32<OT>(add ? to_f32<OT>(orow[ch]) + y : y);
+            }
+          }
+        }
+      }
+    }
+    if (lane == 0 && store_pending) bulk_wait_all();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// LayerNorm of [rows][c] (any dtype, any c) into f16 [rows][cp], zero padded:
+// the input for the kernel when x cannot go straight into a TMA tile (f32, or
+// a row pitch that is not a multiple of 16 bytes).  One warp per row.
+template <typename XT>
+__global__ void normalize_kernel(const XT *__restrict__ x, int64_t rows, int c, int cp, const float *__restrict__ vec,
+                                 float eps, __half *__restrict__ xn) {
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const XT *xr = x + row * c;
+  float v[4];
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int ch = lane + 32 * i;
+    v[i] = ch < c ? to_f32<XT>(xr[ch]) : 0.f;
+    s += v[i];
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(kFull, s, o);
+  const float mean = s / static_cast<float>(c);
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int ch = lane + 32 * i;
+    const float d = ch < c ? v[i] - mean : 0.f;
+    q += d * d;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(kFull, q, o);
+  const float rstd = rsqrtf(q / static_cast<float>(c) + eps);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int ch = lane + 32 * i;
+    if (ch < cp) xn[row * cp + ch] = __float2half_rn(ch < c ? (v[i] - mean) * rstd * vec[ch] + vec[cp + ch] : 0.f);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Weight preparation.
+// ---------------------------------------------------------------------------
+
+struct MatrixDev {
+  int format, block;
+  const void *values, *scales;
+};
+
+// f32 value of element i of a matrix of format FMT (exact decode for q8
+// block; codes as-is for q8 channel, whose scale is applied in the epilogue).
+template <int FMT>
+__device__ __forceinline__ float matrix_element(const MatrixDev &m, int64_t i) {
+  if (FMT == AF2_WEIGHTS_F32) return static_cast<const float *>(m.values)[i];
+  const float code = static_cast<float>(static_cast<const int8_t *>(m.values)[i]);
+  if (FMT == AF2_WEIGHTS_Q8_CHANNEL) return code;
+  const uint16_t bits = static_cast<const uint16_t *>(m.scales)[i / m.block];
+  return code * __half2float(__ushort_as_half(bits));
+}
+
+// One block per 32 output columns of one matrix; warp w walks k = w, w + 32,
+// ... so each load instruction reads 32 consecutive columns of one row.
+// Pass 1 finds the column's scale (the largest magnitude's power of two, or
+// the given q8 channel scale), pass 2 writes the f16 operand column.
+// Matrix 1 ([c][h]) -> w1p [kb][hp][64]; matrix 2 ([h][c]) -> w2p [cp][hp].
+constexpr int PREP_THREADS = 1024;
+constexpr int kPrepBatch = 16;  // values per thread loaded before any is used
+
+template <int FMT>
+__device__ __forceinline__ void prep_columns(const MatrixDev &m, bool first, int o, int inner, int cols, int kpad,
+                                             int cp, int hp, int c, int h, const float *__restrict__ b1,
+                                             const float *__restrict__ b2, __half *__restrict__ w1p,
+                                             __half *__restrict__ w2p, float *__restrict__ vec) {
+  __shared__ float red[32][33];
+  __shared__ float col_scale[32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr bool codes = FMT == AF2_WEIGHTS_Q8_CHANNEL;
+  // Pass 1: the column's values for this warp (k = warp, warp + 32, ...) in
+  // batches, all loads of a batch in flight together.
+  // Zero first: a warp whose first k is already past `inner` never enters the
+  // loop, and pass 2 writes these registers out as the zero padding.
+  float vals[kPrepBatch];
+#pragma unroll
+  for (int b = 0; b < kPrepBatch; ++b) vals[b] = 0.f;
+  float mx = 0.f;
+  for (int k0 = warp; k0 < inner; k0 += 32 * kPrepBatch) {
+#pragma unroll
+    for (int b = 0; b < kPrepBatch; ++b) {
+      const int k = k0 + 32 * b;
+      vals[b] = (o < cols && k < inner) ? matrix_element<FMT>(m, static_cast<int64_t>(k) * cols + o) : 0.f;
+    }
+#pragma unroll
+    for (int b = 0; b < kPrepBatch; ++b) mx = fmaxf(mx, fabsf(vals[b]));
+  }
+  red[warp][lane] = mx;
+  __syncthreads();
+  if (warp == 0) {
+    float v = 0.f;
+    for (int w = 0; w < 32; ++w) v = fmaxf(v, red[w][lane]);
+    float scale = 1.f;
+    if (o < cols) {
+      if (codes) {
+        scale = static_cast<const float *>(m.scales)[o];
+      } else if (v > 0.f && isfinite(v)) {
+        int e;
+        frexpf(v, &e);  // v = f 2^e, f in [0.5, 1)
+        scale = ldexpf(1.f, e);
+      }
+    }
+    col_scale[lane] = scale;
+    if (first) {
+      vec[2 * cp + o] = scale;
+      vec[2 * cp + hp + o] = o < h ? b1[o] : 0.f;
+    } else {
+      vec[2 * cp + 2 * hp + o] = scale;
+      vec[3 * cp + 2 * hp + o] = o < c ? b2[o] : 0.f;
+    }
+  }
+  __syncthreads();
+  // Pass 2: the f16 operand column (value / scale, a power of two: exact).
+  const float inv = codes ? 1.f : 1.f / col_scale[lane];
+  auto put = [&](int k, float w) {
+    if (first)
+      w1p[(static_cast<int64_t>(k >> 6) * hp + o) * 64 + (k & 63)] = __float2half_rn(w);
+    else
+      w2p[static_cast<int64_t>(o) * hp + k] = __float2half_rn(w);
+  };
+  if (inner <= 32 * kPrepBatch) {  // the common case: every value is still in registers
+#pragma unroll
+    for (int b = 0; b < kPrepBatch; ++b) {
+      const int k = warp + 32 * b;
+      if (k < kpad) put(k, vals[b] * inv);
+    }
+    for (int k = warp + 32 * kPrepBatch; k < kpad; k += 32) put(k, 0.f);
+  } else {
+    for (int k = warp; k < kpad; k += 32) {
+      float w = 0.f;
+      if (o < cols && k < inner) w = matrix_element<FMT>(m, static_cast<int64_t>(k) * cols + o) * inv;
+      put(k, w);
+    }
+  }
+}
+
+// One block per 32 output columns of one matrix.  Matrix 1 ([c][h]) ->
+// w1p [kb][hp][64]; matrix 2 ([h][c]) -> w2p [cp][hp]; plus the vectors
+// gamma beta [cp], scale1 bias1 [hp], scale2 bias2 [cp] (zero padded).
+__global__ void __launch_bounds__(PREP_THREADS)
+    prep_kernel(MatrixDev m1, MatrixDev m2, const float *__restrict__ gamma, const float *__restrict__ beta,
+                const float *__restrict__ b1, const float *__restrict__ b2, int c, int h, int cp, int hp,
+                __half *__restrict__ w1p, __half *__restrict__ w2p, float *__restrict__ vec) {
+  const int groups1 = hp / 32;
+  const bool first = static_cast<int>(blockIdx.x) < groups1;
+  const int o = (first ? blockIdx.x : blockIdx.x - groups1) * 32 + (threadIdx.x & 31);
+  const MatrixDev &m = first ? m1 : m2;
+  const int inner = first ? c : h, cols = first ? h : c, kpad = first ? cp : hp;
+  if (blockIdx.x == 0)
+    for (int i = threadIdx.x; i < cp; i += PREP_THREADS) {
+      vec[i] = i < c ? gamma[i] : 0.f;
+      vec[cp + i] = i < c ? beta[i] : 0.f;
+    }
+  if (m.format == AF2_WEIGHTS_Q8_CHANNEL)
+    prep_columns<AF2_WEIGHTS_Q8_CHANNEL>(m, first, o, inner, cols, kpad, cp, hp, c, h, b1, b2, w1p, w2p, vec);
+  else if (m.format == AF2_WEIGHTS_Q8_BLOCK)
+    prep_columns<AF2_WEIGHTS_Q8_BLOCK>(m, first, o, inner, cols, kpad, cp, hp, c, h, b1, b2, w1p, w2p, vec);
+  else
+    prep_columns<AF2_WEIGHTS_F32>(m, first, o, inner, cols, kpad, cp, hp, c, h, b1, b2, w1p, w2p, vec);
+}
+
+// Bit-exact q8 decode (dtype.ts:86-97; per-channel: the f32 product).
+__global__ void dequant_kernel(MatrixDev m, int64_t count, int64_t cols, float *__restrict__ out) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < count;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const float code = static_cast<float>(static_cast<const int8_t *>(m.values)[i]);
+    if (m.format == AF2_WEIGHTS_Q8_CHANNEL)
+      out[i] = __fmul_rn(code, static_cast<const float *>(m.scales)[i % cols]);
+    else
+      out[i] = __fmul_rn(code, __half2float(__ushort_as_half(static_cast<const uint16_t *>(m.scales)[i / m.block])));
+  }
+}
+
+}  // namespace trn
+
+namespace {
+
+using namespace trn;
+
+MatrixDev to_dev(const af2_matrix &m) { return MatrixDev{m.format, m.block, m.values, m.scales}; }
+
+uint32_t smem_bytes(int kb, int hp) { return off_vec(kb) + (4u * kb * 64 + 2u * hp) * 4u + 1024u; }
+
+template <typename XT, typename OT>
+af2_status launch_kernel(af2_ctx *ctx, const CUtensorMap &xmap, const CUtensorMap &w1map, const CUtensorMap &w2map,
+                         const CUtensorMap &omap, const Args &a, cudaStream_t stream) {
+  auto kernel = transition_kernel<XT, OT>;
+  const uint32_t smem = smem_bytes(a.kb, a.hp);
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "transition kernel attributes");
+  const int grid = std::min(a.total_tiles, ctx->sm_count);
+  LaunchScope scope(ctx, stream, kProfTransition);
+  kernel<<<grid, THREADS, smem, stream>>>(xmap, w1map, w2map, omap, a);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? AF2_OK : cuda_fail(ctx, e, "transition kernel launch");
+}
+
+template <typename XT>
+af2_status launch_out(af2_ctx *ctx, int out_dtype, const CUtensorMap &xmap, const CUtensorMap &w1map,
+                      const CUtensorMap &w2map, const CUtensorMap &omap, const Args &a, cudaStream_t stream) {
+  if (out_dtype == AF2_F16) return launch_kernel<XT, __half>(ctx, xmap, w1map, w2map, omap, a, stream);
+  if (out_dtype == AF2_BF16) return launch_kernel<XT, __nv_bfloat16>(ctx, xmap, w1map, w2map, omap, a, stream);
+  return launch_kernel<XT, float>(ctx, xmap, w1map, w2map, omap, a, stream);
+}
+
+CUtensorMapDataType map_dtype(int dtype) {
+  return dtype == AF2_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                           : (dtype == AF2_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32);
+}
+
+}  // namespace
+
+TransitionLayout transition_layout(int64_t rows, int64_t c, int64_t h, int x_dtype) {
+  TransitionLayout L;
+  L.rows = rows;
+  L.c = c;
+  L.h = h;
+  L.cp = c <= 64 ? 64 : 128;
+  L.hp = (h + 63) / 64 * 64;
+  L.fast_in = x_dtype != AF2_F32 && c % 8 == 0;
+  L.chunk_rows = L.fast_in ? rows : std::min<int64_t>(rows, 65536);
+  size_t off = 0;
+  L.off_w1 = off;
+  off = align_up(off + (size_t)L.cp * L.hp * 2, 256);
+  L.off_w2 = off;
+  off = align_up(off + (size_t)L.cp * L.hp * 2, 256);
+  L.off_vec = off;
+  off = align_up(off + (size_t)(4 * L.cp + 2 * L.hp) * 4, 256);
+  L.off_xn = off;
+  if (!L.fast_in) off = align_up(off + (size_t)L.chunk_rows * L.cp * 2, 256);
+  L.total = off;
+  return L;
+}
+
+af2_status transition_prepare(af2_ctx *ctx, const TransitionLayout &L, const af2_transition_weights &w,
+                              void *workspace, cudaStream_t stream) {
+  uint8_t *ws = static_cast<uint8_t *>(workspace);
+  const unsigned blocks = static_cast<unsigned>(L.hp / 32 + L.cp / 32);
+  LaunchScope scope(ctx, stream, kProfTransitionPrepare);
+  prep_kernel<<<blocks, PREP_THREADS, 0, stream>>>(
+      to_dev(w.first_weight), to_dev(w.second_weight), w.layer_norm_scale, w.layer_norm_offset, w.first_bias,
+      w.second_bias, (int)L.c, (int)L.h, (int)L.cp, (int)L.hp, reinterpret_cast<__half *>(ws + L.off_w1),
+      reinterpret_cast<__half *>(ws + L.off_w2), reinterpret_cast<float *>(ws + L.off_vec));
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? AF2_OK : cuda_fail(ctx, e, "transition weight preparation");
+}
+
+af2_status transition_launch(af2_ctx *ctx, const TransitionLayout &L, const void *x, int x_dtype,
+                             const af2_transition_weights &w, double eps, int residual, void *out, int out_dtype,
+                             void *workspace, cudaStream_t stream) {
+  af2_status st = transition_prepare(ctx, L, w, workspace, stream);
+  if (st != AF2_OK) return st;
+  uint8_t *ws = static_cast<uint8_t *>(workspace);
+  const int kb = static_cast<int>(L.cp / 64);
+  CUtensorMap w1map, w2map;
+  if (!encode_map_3d(&w1map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, ws + L.off_w1, 64, L.hp, kb, 128,
+                     (uint64_t)L.hp * 128, 64, HC, kb, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_map_3d(&w2map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, ws + L.off_w2, L.hp, L.cp, 1, L.hp * 2,
+                     (uint64_t)L.hp * 2 * L.cp, 64, L.cp, 1, CU_TENSOR_MAP_SWIZZLE_128B))
+    return fail(ctx, AF2_ERR_CUDA, "cuTensorMapEncodeTiled failed for the transition weights");
+  const size_t xb = x_dtype == AF2_F32 ? 4 : 2, ob = out_dtype == AF2_F32 ? 4 : 2;
+  const bool tma_out = out_dtype != AF2_F32 && L.c % 8 == 0;
+  Args a{};
+  a.vec = reinterpret_cast<const float *>(ws + L.off_vec);
+  a.c = (int)L.c;
+  a.cp = (int)L.cp;
+  a.kb = kb;
+  a.hp = (int)L.hp;
+  a.nh = (int)(L.hp / HC);
+  a.eps = static_cast<float>(eps);
+  a.err = ctx->err_word;
+  a.out_mode = tma_out ? (residual ? kOutTmaAdd : kOutTmaStore) : (residual ? kOutDirectAdd : kOutDirect);
+  for (int64_t r0 = 0; r0 < L.rows; r0 += L.chunk_rows) {
+    const int64_t rows = std::min(L.chunk_rows, L.rows - r0);
+    const void *xsrc = static_cast<const uint8_t *>(x) + r0 * L.c * xb;
+    void *odst = static_cast<uint8_t *>(out) + r0 * L.c * ob;
+    CUtensorMap xmap, omap;
+    int xdt = x_dtype;
+    if (!L.fast_in) {
+      __half *xn = reinterpret_cast<__half *>(ws + L.off_xn);
+      const int warps = 8;
+      const unsigned blocks = (unsigned)((rows + warps - 1) / warps);
+      {
+        LaunchScope scope(ctx, stream, kProfTransitionNormalize);
+        const float *vec = reinterpret_cast<const float *>(ws + L.off_vec);
+        if (x_dtype == AF2_F32)
+          normalize_kernel<float><<<blocks, warps * 32, 0, stream>>>(static_cast<const float *>(xsrc), rows, a.c,
+                                                                     a.cp, vec, a.eps, xn);
+        else if (x_dtype == AF2_F16)
+          normalize_kernel<__half><<<blocks, warps * 32, 0, stream>>>(static_cast<const __half *>(xsrc), rows, a.c,
+                                                                      a.cp, vec, a.eps, xn);
+        else
+          normalize_kernel<__nv_bfloat16><<<blocks, warps * 32, 0, stream>>>(
+              static_cast<const __nv_bfloat16 *>(xsrc), rows, a.c, a.cp, vec, a.eps, xn);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return cuda_fail(ctx, e, "transition normalisation");
+      }
+      xsrc = xn;
+      xdt = AF2_F16;
+      if (!encode_map_3d(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, xsrc, L.cp, rows, 1, L.cp * 2,
+                         (uint64_t)rows * L.cp * 2, 64, TILE, 1, CU_TENSOR_MAP_SWIZZLE_128B))
+        return fail(ctx, AF2_ERR_CUDA, "cuTensorMapEncodeTiled failed for the normalised activations");
+    } else if (!encode_map_3d(&xmap, map_dtype(x_dtype), xsrc, L.c, rows, 1, L.c * xb, (uint64_t)rows * L.c * xb,
+                              64, TILE, 1, CU_TENSOR_MAP_SWIZZLE_128B)) {
+      return fail(ctx, AF2_ERR_CUDA, "cuTensorMapEncodeTiled failed for the activations");
+    }
+    if (tma_out) {
+      if (!encode_map_3d(&omap, map_dtype(out_dtype), odst, L.c, rows, 1, L.c * ob, (uint64_t)rows * L.c * ob, 64,
+                         32, 1, CU_TENSOR_MAP_SWIZZLE_128B))
+        return fail(ctx, AF2_ERR_CUDA, "cuTensorMapEncodeTiled failed for the output");
+    } else {
+      omap = xmap;  // unused by the direct-store modes
+    }
+    a.out = odst;
+    a.rows = rows;
+    a.total_tiles = (int)((rows + TILE - 1) / TILE);
+    a.normalize = L.fast_in ? 1 : 0;
+    if (xdt == AF2_BF16)
+      st = launch_out<__nv_bfloat16>(ctx, out_dtype, xmap, w1map, w2map, omap, a, stream);
+    else
+      st = launch_out<__half>(ctx, out_dtype, xmap, w1map, w2map, omap, a, stream);
+    if (st != AF2_OK) return st;
+  }
+  return AF2_OK;
+}
+
+af2_status dequant_launch(af2_ctx *ctx, const af2_matrix &m, int64_t inner, int64_t cols, float *out,
+                          cudaStream_t stream) {
+  const int64_t count = inner * cols;
+  const int threads = 256;
+  const unsigned blocks = (unsigned)std::min<int64_t>((count + threads - 1) / threads, 4LL * ctx->sm_count * 8);
+  LaunchScope scope(ctx, stream, kProfDequant);
+  dequant_kernel<<<std::max(1u, blocks), threads, 0, stream>>>(to_dev(m), count, cols, out);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? AF2_OK : cuda_fail(ctx, e, "q8 decode");
+}
+
+}  // namespace af2

@@ -45,33 +45,6 @@ enum {
   kVLnInW = 0, kVLnInB, kVBAP, kVBAG, kVBBP, kVBBG, kVLnOutW, kVLnOutB, kVBZ, kVBG, kVecCount
 };
 
-constexpr unsigned kFull = 0xffffffffu;
-
-// Rounds the dynamic shared-memory base up to 1024 bytes (the 128-byte
-// swizzle atom).  The offset is added to the __shared__ pointer itself so the
-// compiler still knows every access through it is a shared-memory access
-// (LDS/STS); rounding through an integer would turn them into generic loads.
-__device__ __forceinline__ uint8_t *align1024(uint8_t *p) {
-  const uint32_t a = smem_u32(p);
-  return p + (((a + 1023u) & ~1023u) - a);
-}
-
-__device__ __forceinline__ float reduce16(float v) {
-  v += __shfl_xor_sync(kFull, v, 8);
-  v += __shfl_xor_sync(kFull, v, 4);
-  v += __shfl_xor_sync(kFull, v, 2);
-  v += __shfl_xor_sync(kFull, v, 1);
-  return v;
-}
-
-// Warp-uniform bounded wait: every lane waits, and the warp proceeds only if
-// every lane saw the phase complete.
-__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatile int *abort_flag,
-                                          unsigned int *err, unsigned int code) {
-  const bool ok = mbar_wait(bar, parity, abort_flag, err, code);
-  return __all_sync(kFull, ok);
-}
-
 // ---------------------------------------------------------------------------
 // Weight preparation: the packed f32 array in the reference's ORDER
 // (src/triangle/weights.ts:4-10) -> zero-padded f16 matrices + f32 vectors.

@@ -191,6 +191,97 @@ AF2_API af2_status af2_triangle_multiplication_static(af2_ctx *ctx, int directio
                                                       double epsilon, const af2_triangle_options *options,
                                                       void *out, int out_dtype, void *stream);
 
+/* ---- weights: f32 or mixed-q8 ------------------------------------------ */
+
+typedef enum af2_weight_format {
+    /* f32 values. */
+    AF2_WEIGHTS_F32 = 0,
+    /* int8 codes with one f16 scale (stored as its 16 bits) per `block`
+     * consecutive elements of the flattened matrix: w[i] = code[i] *
+     * f16(scale[i / block]).  The reference's mixed-q8 files use block = 64
+     * (src/reference/dtype.ts:86-97, tools/quantize-web-model.ts:98-119). */
+    AF2_WEIGHTS_Q8_BLOCK = 1,
+    /* int8 codes with one f32 scale per output column of an [in, out]
+     * matrix: w[k][o] = code[k][o] * scale[o]. */
+    AF2_WEIGHTS_Q8_CHANNEL = 2
+} af2_weight_format;
+
+/* One weight matrix, [in, out] row-major (transition.ts:115). */
+typedef struct af2_matrix {
+    int32_t format;     /* af2_weight_format */
+    int32_t block;      /* AF2_WEIGHTS_Q8_BLOCK: elements per scale (64 in the reference's files) */
+    const void *values; /* float[in * out] or int8_t[in * out] */
+    const void *scales; /* uint16_t[ceil(in * out / block)] (Q8_BLOCK), float[out] (Q8_CHANNEL), NULL (F32) */
+} af2_matrix;
+
+/*
+ * Bit-exact decode of a q8 matrix to f32 (readTensorRange's int8 branch,
+ * src/reference/dtype.ts:86-97, for the whole tensor; for Q8_CHANNEL the f32
+ * product code * scale[o]).  Device pointers; out holds inner * cols floats.
+ */
+AF2_API af2_status af2_dequant_q8(af2_ctx *ctx, const af2_matrix *matrix, int64_t inner, int64_t cols, float *out,
+                                  void *stream);
+
+/* ---- transition ---------------------------------------------------------- */
+
+/* TransitionInput's dimensions, src/evoformer/transition.ts:18-25. */
+typedef struct af2_transition_shape {
+    int64_t rows;
+    int64_t channels;
+    int64_t hidden_channels;
+} af2_transition_shape;
+
+/* TransitionWeights (transition.ts:9-16), each matrix f32 or q8. */
+typedef struct af2_transition_weights {
+    const float *layer_norm_scale;  /* [channels] */
+    const float *layer_norm_offset; /* [channels] */
+    af2_matrix first_weight;        /* [channels, hidden_channels] */
+    const float *first_bias;        /* [hidden_channels] */
+    af2_matrix second_weight;       /* [hidden_channels, channels] */
+    const float *second_bias;       /* [channels] */
+} af2_transition_weights;
+
+typedef struct af2_transition_options {
+    /* TransitionGpuOptions.maxChunkRows (transition.ts:33-36): 0 = none.  It
+     * bounds the reference's scratch only; results are identical for every
+     * value, and the fused kernel keeps the hidden activations on chip. */
+    int32_t max_chunk_rows;
+    /* 1: out += transition(x) (encodeTransition with residualTarget). */
+    int32_t residual;
+} af2_transition_options;
+
+/* Length of packTransitionWeights(input).data (transition.ts:140-177). */
+AF2_API int64_t af2_transition_weight_count(int64_t channels, int64_t hidden_channels);
+
+/* validate (transition.ts:140-156) plus the kernels' limits; no device needed. */
+AF2_API af2_status af2_transition_check(const af2_transition_shape *shape, int64_t weight_count, double epsilon,
+                                        char *message, size_t capacity);
+
+AF2_API af2_status af2_transition_workspace_bytes(const af2_transition_shape *shape, uint64_t *bytes);
+
+/*
+ * Host form of TransitionGpu.run (transition.ts:264-361): x and out are host
+ * arrays [rows, channels] of io_dtype; packed_weights is f32 in the order of
+ * packTransitionWeights.  out = Linear2(ReLU(Linear1(LayerNorm(x)))), plus x
+ * when options->residual is 1.
+ */
+AF2_API af2_status af2_transition_host(af2_ctx *ctx, const af2_transition_shape *shape, const void *x,
+                                       const float *packed_weights, int64_t weight_count, double epsilon,
+                                       const af2_transition_options *options, int io_dtype, void *out,
+                                       af2_op_stats *stats);
+
+/*
+ * Device form: encodeTransition (src/evoformer/block.ts:625-740).  x [rows,
+ * channels] of x_dtype, out of out_dtype; weights hold device pointers, f32
+ * or q8.  With options->residual = 1 the result is added into out (out == x
+ * updates the activations in place).  workspace: NULL = context-owned, else
+ * af2_transition_workspace_bytes() bytes, 256-byte aligned.
+ */
+AF2_API af2_status af2_transition(af2_ctx *ctx, const af2_transition_shape *shape, const void *x, int x_dtype,
+                                  const af2_transition_weights *weights, double epsilon,
+                                  const af2_transition_options *options, void *out, int out_dtype, void *workspace,
+                                  void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -116,12 +116,54 @@ def test_no_device_is_reported_not_faked():
 
 
 def test_loader_fails_loudly_without_the_library(tmp_path, monkeypatch):
-    import importlib
-    monkeypatch.setenv("AF2CUDA_LIBRARY", str(tmp_path / "missing.so"))
-    mod = importlib.reload(_lib)
-    try:
-        with pytest.raises(OSError, match="libaf2cuda.so not found"):
-            mod.lib()
-    finally:
-        monkeypatch.delenv("AF2CUDA_LIBRARY")
-        importlib.reload(_lib)
+    monkeypatch.setattr(_lib, "LIB_PATH", tmp_path / "missing.so")
+    monkeypatch.setattr(_lib, "_lib", None)
+    with pytest.raises(OSError, match="libaf2cuda.so not found"):
+        _lib.lib()
+
+
+def _tcheck(rows, c, h, count=None, eps=1e-5):
+    shape = _lib.TransitionShape(rows, c, h)
+    msg = ctypes.create_string_buffer(256)
+    if count is None:
+        count = af2cuda.transition_weight_count(max(c, 1), max(h, 1))
+    st = _lib.lib().af2_transition_check(ctypes.byref(shape), count, eps, msg, 256)
+    return st, msg.value.decode()
+
+
+def test_transition_weight_count_and_validation():
+    # packTransitionWeights: LN scale + offset, W1, b1, W2, b2 (transition.ts:158-177)
+    assert af2cuda.transition_weight_count(128, 512) == 2 * 128 + 128 * 512 + 512 + 512 * 128 + 128
+    assert _tcheck(65536, 128, 512) == (0, "")
+    assert _tcheck(0, 128, 512) == (_lib.AF2_ERR_INVALID_ARGUMENT,
+                                    "transition dimensions must be positive safe integers")
+    assert _tcheck(5, 7, 6, count=3) == (_lib.AF2_ERR_INVALID_ARGUMENT, "packed weights have 3 values; expected 111")
+    for eps in (0.0, -1.0, float("inf"), float("nan")):
+        assert _tcheck(5, 7, 6, eps=eps)[0] == _lib.AF2_ERR_INVALID_ARGUMENT
+    st, msg = _tcheck(5, 256, 1024)
+    assert st == _lib.AF2_ERR_UNSUPPORTED and "above 128" in msg
+
+
+def test_transition_python_validation_and_packing():
+    rng = np.random.default_rng(0)
+    c, h = 4, 6
+    w = af2cuda.TransitionWeights(*(rng.standard_normal(n).astype(np.float32) for n in (c, c, c * h, h, h * c, c)))
+    inp = af2cuda.TransitionInput(rng.standard_normal(3 * c).astype(np.float32), 3, c, h, w)
+    af2cuda.validate_transition_input(inp)
+    data, offsets = af2cuda.pack_transition_weights(inp)
+    assert offsets == (0, c, 2 * c, 2 * c + c * h, 2 * c + c * h + h, 2 * c + 2 * c * h + h)
+    assert data.size == af2cuda.transition_weight_count(c, h)
+    assert np.array_equal(data[offsets[4]:offsets[5]], w.secondWeight)
+    bad = af2cuda.TransitionInput(inp.activations[:-1], 3, c, h, w)
+    with pytest.raises(af2cuda.RangeError, match="activations has 11 values; expected 12"):
+        af2cuda.validate_transition_input(bad)
+    with pytest.raises(af2cuda.RangeError):
+        af2cuda.TransitionGpu.__new__(af2cuda.TransitionGpu).__init__(None, {"maxChunkRows": 0})
+
+
+def test_transition_workspace_is_small():
+    # the hidden activations never reach HBM: scratch is prepared weights plus
+    # a bounded normalised copy, independent of rows beyond 65536
+    small = af2cuda.transition_workspace_bytes(65536, 128, 512)
+    big = af2cuda.transition_workspace_bytes(4 * 65536, 128, 512)
+    assert small == big and small < 32 << 20
