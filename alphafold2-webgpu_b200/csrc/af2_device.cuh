@@ -195,6 +195,26 @@ __device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_
       : "memory");
 }
 
+// The same with the accumulate predicate fixed: D = A B (first K step) and
+// D += A B.  A single thread issues every MMA of a CTA, so the issue path is
+// kept free of per-instruction predicate and descriptor arithmetic: callers
+// compute descriptors once and step them by constant offsets (desc_add).
+__device__ __forceinline__ void mma_f16_first(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc) {
+  asm volatile("tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, 0;" ::"r"(d_tmem), "l"(adesc), "l"(bdesc),
+               "r"(idesc)
+               : "memory");
+}
+__device__ __forceinline__ void mma_f16_acc(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc) {
+  asm volatile("tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, 1;" ::"r"(d_tmem), "l"(adesc), "l"(bdesc),
+               "r"(idesc)
+               : "memory");
+}
+
+// A shared-memory descriptor moved by `bytes` (a multiple of 16): the start
+// address field is address >> 4 in the low 14 bits, and every shared address
+// is below 2^18, so the add never carries out of the field.
+__host__ __device__ constexpr uint64_t desc_add(uint64_t desc, uint32_t bytes) { return desc + (bytes >> 4); }
+
 // Arrives once on `bar` when every tcgen05 op this thread issued so far has completed.
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)

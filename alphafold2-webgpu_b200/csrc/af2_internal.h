@@ -118,7 +118,7 @@ af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L,
 struct TransitionLayout {
   int64_t rows = 0, c = 0, h = 0;
   int64_t cp = 0;          // channels padded to 64 or 128 (the first GEMM's K, the second's N)
-  int64_t hp = 0;          // hidden channels padded to 64
+  int64_t hp = 0;          // hidden channels padded to 128 (the kernel works in 128-wide chunks)
   bool fast_in = false;    // 16-bit x with 16-byte rows: TMA straight into the kernel, LayerNorm in place
   int64_t chunk_rows = 0;  // rows per kernel launch (bounds the normalised copy otherwise)
   size_t off_w1 = 0, off_w2 = 0, off_vec = 0, off_xn = 0, total = 0;

@@ -18,11 +18,13 @@
 //               H[j-3] W2[chunk j-3, :] -- so the tensor pipe always has three
 //               first-GEMM chunks queued while the epilogue turns a finished
 //               one into the second GEMM's operand;
-//   warps 2-5   LayerNorm of the x tile in place, one thread per row;
-//   warps 6-9   first epilogue: D1 -> relu(scale1 * acc + b1) as f16 into
-//               the second GEMM's A operand (shared memory, never HBM);
-//   warps 10-13 second epilogue: D2 -> scale2 * acc + b2, staged and written
-//               by per-warp TMA stores (or TMA adds for the residual).
+//   warps 2-5   row warps: LayerNorm of the next x tile in place (one
+//               thread per row), then the second epilogue of this tile:
+//               D2 -> scale2 * acc + b2, staged and written by per-warp TMA
+//               stores (or TMA adds for the residual);
+//   warps 6-13  first epilogue, two groups of four taking alternate chunks:
+//               D1 -> relu(scale1 * acc + b1) as f16 into the second GEMM's
+//               A operand (shared memory, never HBM).
 // The hidden activations (4C per row) never leave the SM, so HBM traffic is
 // one read of x and one write of the output.
 //
@@ -42,21 +44,21 @@ namespace af2 {
 namespace trn {
 
 constexpr int TILE = 128;     // rows per tile (one TMEM lane each)
-constexpr int HC = 64;        // hidden channels per chunk
-constexpr int STAGES = 4;     // weight-chunk ring
-constexpr int LAG = 3;        // second-GEMM chunks trail the first by this many
-constexpr int NBUF = 4;       // D1 accumulators and H operand buffers (> LAG)
-constexpr int THREADS = 448;  // 14 warps: 0 TMA, 1 MMA, 2-5 LayerNorm, 6-9 / 10-13 epilogues
+constexpr int HC = 128;       // hidden channels per chunk (the first GEMM's N)
+constexpr int STAGES = 2;     // weight-chunk ring
+constexpr int LAG = 1;        // second-GEMM chunks trail the first by this many
+constexpr int NBUF = 2;       // D1 accumulators and H operand buffers (> LAG)
+constexpr int THREADS = 448;  // 14 warps: 0 TMA, 1 MMA, 2-5 LayerNorm + second epilogue, 6-13 first epilogue
 
 // Shared-memory map (bytes from the 1024-aligned base); kb = channel blocks of 64.
 //   A  2 x [kb][128 rows][128 B]      x tiles (normalised in place)
-//   W  STAGES x kb x 8 KB             weight chunks
-//   H  NBUF x [128 rows][128 B]       relu(hidden) chunks, f16
+//   W  STAGES x kb x 16 KB            weight chunks: W1 [kb][128 h][128 B], W2 [2][cp][128 B]
+//   H  NBUF x [2][128 rows][128 B]    relu(hidden) chunks, f16
 //   O  [128 rows][128 B]              output staging (64 channels at a time)
 //   barriers, then gamma beta scale2 bias2 [cp] and scale1 bias1 [hp]
 __host__ __device__ constexpr uint32_t off_w(int kb) { return 2u * kb * 16384u; }
-__host__ __device__ constexpr uint32_t off_h(int kb) { return off_w(kb) + STAGES * kb * 8192u; }
-__host__ __device__ constexpr uint32_t off_o(int kb) { return off_h(kb) + NBUF * 16384u; }
+__host__ __device__ constexpr uint32_t off_h(int kb) { return off_w(kb) + STAGES * kb * 16384u; }
+__host__ __device__ constexpr uint32_t off_o(int kb) { return off_h(kb) + NBUF * 32768u; }
 __host__ __device__ constexpr uint32_t off_bar(int kb) { return off_o(kb) + 16384u; }
 __host__ __device__ constexpr uint32_t off_vec(int kb) { return off_bar(kb) + 512u; }
 
@@ -72,6 +74,31 @@ struct Args {
   int out_mode;
   float eps;
   unsigned int *err;
+};
+
+// Position in a CTA's stream of hidden chunks without runtime divisions (the
+// issuing threads are single threads on the critical path, where an integer
+// division by nh costs more than the MMAs it schedules): tile `it` of the
+// CTA, step `h` within the tile, and the hidden chunk that step covers.  Each
+// tile starts its walk at chunk (tile index mod nh), so the CTAs do not all
+// fetch the same weight chunk at the same moment; the order depends on the
+// tile alone, so results do not depend on the grid.
+struct ChunkCursor {
+  int it = 0, h = 0, chunk = 0, nh = 1;
+  __device__ __forceinline__ void start(int nh_) {
+    nh = nh_;
+    it = h = 0;
+    chunk = static_cast<int>(blockIdx.x) % nh;
+  }
+  __device__ __forceinline__ void advance() {
+    if (++h == nh) {
+      h = 0;
+      ++it;
+      chunk = static_cast<int>((blockIdx.x + it * gridDim.x) % nh);
+    } else if (++chunk == nh) {
+      chunk = 0;
+    }
+  }
 };
 
 // LayerNorm of row `row` of a 128B-swizzled K-major tile ([kb][128 rows][128 B])
@@ -153,7 +180,7 @@ __device__ __forceinline__ uint32_t pack2<float>(float, float) {
   return 0;  // f32 output never goes through the 16-bit staging
 }
 
-template <typename XT, typename OT>
+template <typename XT, typename OT, int KB>
 __global__ void __launch_bounds__(THREADS, 1)
     transition_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap w1map,
                       const __grid_constant__ CUtensorMap w2map, const __grid_constant__ CUtensorMap omap,
@@ -161,9 +188,10 @@ __global__ void __launch_bounds__(THREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = align1024(smem_raw);
   const uint32_t sbase = smem_u32(smem);
-  const int kb = p.kb;
+  constexpr int kb = KB;
   const uint32_t OFF_W = off_w(kb), OFF_H = off_h(kb), OFF_O = off_o(kb), OFF_BAR = off_bar(kb);
-  const uint32_t A_BYTES = kb * 16384u, W_BYTES = kb * 8192u;
+  const uint32_t A_BYTES = kb * 16384u, W_BYTES = kb * 16384u;
+  const uint32_t W2_KSTRIDE = p.cp * 128u;  // bytes between the two 64-wide K blocks of a W2 chunk
   const uint32_t bar0 = sbase + OFF_BAR;
   auto a_raw = [&](int b) { return bar0 + 8u * b; };
   auto a_full = [&](int b) { return bar0 + 8u * (2 + b); };
@@ -186,7 +214,6 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int nh = p.nh;
   const int my_tiles = blockIdx.x < p.total_tiles ? (p.total_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
   const int total = my_tiles * nh;  // hidden chunks this CTA works through
-
   for (int i = threadIdx.x; i < 2 * p.cp; i += THREADS) vec[i] = p.vec[i];
   for (int i = threadIdx.x; i < 2 * p.cp; i += THREADS) vec[2 * p.cp + i] = p.vec[2 * p.cp + 2 * p.hp + i];
   for (int i = threadIdx.x; i < 2 * p.hp; i += THREADS) vec[4 * p.cp + i] = p.vec[2 * p.cp + i];
@@ -247,19 +274,25 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (first)
           tma_load_3d(dst, &w1map, w_full(s), 0, h * HC, 0);
         else
-          tma_load_3d(dst, &w2map, w_full(s), h * HC, 0, 0);
+          tma_load_3d(dst, &w2map, w_full(s), 0, 0, h * 2);
         ++ws;
         return true;
       };
       if (my_tiles > 0) ok = issue_x(0);
-      const int early = nh > 1 ? 1 : 0;  // the next tile's x goes out after this chunk's W1
+      const int early = nh > 1 ? 1 : 0;  // the next tile's x goes out after this step's W1
+      ChunkCursor c1, c2;
+      c1.start(nh);
+      c2.start(nh);
       for (int j = 0; ok && j < total + LAG; ++j) {
         if (j < total) {
-          ok = issue_w(true, j % nh);
-          const int it = j / nh;
-          if (ok && j % nh == early && it + 1 < my_tiles) ok = issue_x(it + 1);
+          ok = issue_w(true, c1.chunk);
+          if (ok && c1.h == early && c1.it + 1 < my_tiles) ok = issue_x(c1.it + 1);
+          c1.advance();
         }
-        if (ok && j >= LAG) ok = issue_w(false, (j - LAG) % nh);
+        if (ok && j >= LAG) {
+          ok = issue_w(false, c2.chunk);
+          c2.advance();
+        }
       }
       // Every load issued lands before the CTA exits (immediate unless a consumer gave up).
       for (int i = std::max(0, ws - STAGES); i < ws; ++i) mbar_wait_drain(w_full(i % STAGES), (i / STAGES) & 1, p.err);
@@ -270,42 +303,60 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (lane == 0) {
       const uint32_t idesc1 = idesc_f16_f32(TILE, HC);
       const uint32_t idesc2 = idesc_f16_f32(TILE, p.cp);
+      // Base descriptors; every operand below is one of these plus a constant.
+      const uint64_t a_desc = sdesc_k_sw128(sbase), w_desc = sdesc_k_sw128(sbase + OFF_W),
+                     h_desc = sdesc_k_sw128(sbase + OFF_H);
       int ws = 0;
+      int it1 = 0, h1 = 0, it2 = 0, h2 = 0;  // tile and step of the next first / second GEMM
       for (int j = 0; j < total + LAG; ++j) {
-        if (j < total) {  // first GEMM of chunk j -> D1[j % NBUF]
-          const int it = j / nh, h = j % nh, buf = it & 1, db = j % NBUF, s = ws % STAGES;
-          if ((h == 0 && !mbar_wait(a_full(buf), (it >> 1) & 1, abort_flag, p.err, kErrWaitMma)) ||
+        if (j < total) {  // first GEMM of step j -> D1[j % NBUF]
+          const int buf = it1 & 1, db = j % NBUF, s = ws % STAGES;
+          if ((h1 == 0 && !mbar_wait(a_full(buf), (it1 >> 1) & 1, abort_flag, p.err, kErrWaitMma)) ||
               !mbar_wait(d1_empty(db), ((j / NBUF) & 1) ^ 1, abort_flag, p.err, kErrWaitMma) ||
               !mbar_wait(w_full(s), (ws / STAGES) & 1, abort_flag, p.err, kErrWaitMma))
             break;
           tc_fence_after();
-          const uint32_t a_base = sbase + buf * A_BYTES, wb = sbase + OFF_W + s * W_BYTES;
-          for (int k = 0; k < kb; ++k)
+          const uint64_t ad = desc_add(a_desc, buf * A_BYTES), wd = desc_add(w_desc, s * W_BYTES);
+          const uint32_t d = tmem + db * HC;
+          mma_f16_first(d, ad, wd, idesc1);
 #pragma unroll
-            for (int ks = 0; ks < 4; ++ks)
-              mma_f16(tmem + db * HC, sdesc_k_sw128(a_base + k * 16384 + ks * 32),
-                      sdesc_k_sw128(wb + k * 8192 + ks * 32), idesc1, (k | ks) != 0);
+          for (int ks = 1; ks < 4 * KB; ++ks)
+            mma_f16_acc(d, desc_add(ad, (ks >> 2) * 16384 + (ks & 3) * 32), desc_add(wd, (ks >> 2) * 16384 + (ks & 3) * 32),
+                        idesc1);
           mma_commit(w_empty(s));
           mma_commit(d1_full(db));
-          if (h == nh - 1) mma_commit(a_empty(buf));
+          if (h1 == nh - 1) mma_commit(a_empty(buf));
           ++ws;
+          if (++h1 == nh) {
+            h1 = 0;
+            ++it1;
+          }
         }
-        if (j >= LAG) {  // second GEMM of chunk i = j - LAG: D2[tile] += H[i % NBUF] W2[chunk]
-          const int i = j - LAG, it = i / nh, h = i % nh, buf = it & 1, hb = i % NBUF, s = ws % STAGES;
+        if (j >= LAG) {  // second GEMM of step i = j - LAG: D2[tile] += H[i % NBUF] W2[chunk]
+          const int i = j - LAG, buf = it2 & 1, hb = i % NBUF, s = ws % STAGES;
           if (!mbar_wait(h_full(hb), (i / NBUF) & 1, abort_flag, p.err, kErrWaitMma) ||
               !mbar_wait(w_full(s), (ws / STAGES) & 1, abort_flag, p.err, kErrWaitMma) ||
-              (h == 0 && !mbar_wait(d2_empty(buf), ((it >> 1) & 1) ^ 1, abort_flag, p.err, kErrWaitMma)))
+              (h2 == 0 && !mbar_wait(d2_empty(buf), ((it2 >> 1) & 1) ^ 1, abort_flag, p.err, kErrWaitMma)))
             break;
           tc_fence_after();
-          const uint32_t hbase = sbase + OFF_H + hb * 16384, wb = sbase + OFF_W + s * W_BYTES;
+          const uint64_t hd = desc_add(h_desc, hb * 32768), wd = desc_add(w_desc, s * W_BYTES);
+          const uint32_t d = tmem + 256 + buf * 128;
+          if (h2 == 0)
+            mma_f16_first(d, hd, wd, idesc2);
+          else
+            mma_f16_acc(d, hd, wd, idesc2);
 #pragma unroll
-          for (int ks = 0; ks < 4; ++ks)
-            mma_f16(tmem + 256 + buf * 128, sdesc_k_sw128(hbase + ks * 32), sdesc_k_sw128(wb + ks * 32), idesc2,
-                    (h > 0 || ks > 0) ? 1u : 0u);
+          for (int ks = 1; ks < 8; ++ks)
+            mma_f16_acc(d, desc_add(hd, (ks >> 2) * 16384 + (ks & 3) * 32),
+                        desc_add(wd, (ks >> 2) * W2_KSTRIDE + (ks & 3) * 32), idesc2);
           mma_commit(w_empty(s));
           mma_commit(h_empty(hb));
-          if (h == nh - 1) mma_commit(d2_full(buf));
+          if (h2 == nh - 1) mma_commit(d2_full(buf));
           ++ws;
+          if (++h2 == nh) {
+            h2 = 0;
+            ++it2;
+          }
         }
       }
       // Every MMA has completed before TMEM is freed, whether or not a consumer gave up.
@@ -314,70 +365,26 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     __syncwarp();
   } else if (warp < 6) {
-    // ---- LayerNorm of the x tile, in place ----
-    const int row = (warp - 2) * 32 + lane;
+    // ---- row warps: LayerNorm of tile it+1, then the second epilogue of tile it ----
+    const int q = warp & 3;  // TMEM lane quarter this warp may read
+    const int row = q * 32 + lane;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
     const float inv_c = 1.f / static_cast<float>(p.c);
-    for (int it = 0; it < my_tiles; ++it) {
+    bool store_pending = false;
+    auto layer_norm = [&](int it) -> bool {  // x tile in place, one thread per row
       const int buf = it & 1;
-      if (!warp_wait(a_raw(buf), (it >> 1) & 1, abort_flag, p.err, kErrWaitNormalizer)) break;
+      if (!warp_wait(a_raw(buf), (it >> 1) & 1, abort_flag, p.err, kErrWaitNormalizer)) return false;
       if (p.normalize) {
         ln_row<XT>(smem + buf * A_BYTES, kb, row, p.c, inv_c, p.eps, gamma, beta);
         fence_async_smem();
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(a_full(buf));
-    }
-  } else if (warp < 10) {
-    // ---- first epilogue: D1 chunk -> relu(scale1 * acc + b1) -> f16 H operand rows ----
-    const int q = warp & 3;  // TMEM lane quarter this warp may read
-    const int row = q * 32 + lane;
-    const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
-    for (int j = 0; j < total; ++j) {
-      const int db = j % NBUF, h = j % nh;
-      const uint32_t ph = (j / NBUF) & 1;
-      if (!warp_wait(d1_full(db), ph, abort_flag, p.err, kErrWaitEpilogue)) break;
-      tc_fence_after();
-      uint32_t v[2][32];
-      tmem_ld32(lane_base + db * HC, v[0]);
-      tmem_ld32(lane_base + db * HC + 32, v[1]);
-      tmem_ld_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(d1_empty(db));
-      const float4 *sc = reinterpret_cast<const float4 *>(s1v + h * HC);
-      const float4 *bi = reinterpret_cast<const float4 *>(b1v + h * HC);
-      if (!warp_wait(h_empty(db), ph ^ 1, abort_flag, p.err, kErrWaitEpilogue)) break;
-      uint8_t *hrow = smem + OFF_H + db * 16384;
-#pragma unroll
-      for (int c16 = 0; c16 < 8; ++c16) {  // 8 hidden channels = one 16-byte chunk of the row
-        uint32_t pk[4];
-#pragma unroll
-        for (int i2 = 0; i2 < 2; ++i2) {
-          const float4 s = sc[c16 * 2 + i2], b = bi[c16 * 2 + i2];
-          const int c = c16 * 8 + i2 * 4;
-          const float2 y0 = f2fma(make_float2(__uint_as_float(v[c >> 5][c & 31]), __uint_as_float(v[c >> 5][(c + 1) & 31])),
-                                  make_float2(s.x, s.y), make_float2(b.x, b.y));
-          const float2 y1 =
-              f2fma(make_float2(__uint_as_float(v[c >> 5][(c + 2) & 31]), __uint_as_float(v[c >> 5][(c + 3) & 31])),
-                    make_float2(s.z, s.w), make_float2(b.z, b.w));
-          pk[i2 * 2] = pack_half2_relu(y0.x, y0.y);
-          pk[i2 * 2 + 1] = pack_half2_relu(y1.x, y1.y);
-        }
-        *reinterpret_cast<uint4 *>(hrow + sw128_offset(row, c16)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-      }
-      fence_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(h_full(db));
-    }
-  } else {
-    // ---- second epilogue: D2 -> scale2 * acc + b2, 64 channels at a time ----
-    const int q = warp & 3;
-    const int row = q * 32 + lane;
-    const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
-    bool store_pending = false;
-    for (int it = 0; it < my_tiles; ++it) {
+      return true;
+    };
+    auto second_epilogue = [&](int it) -> bool {  // D2 -> scale2 * acc + b2, 64 channels at a time
       const int buf = it & 1, t = blockIdx.x + it * gridDim.x;
-      if (!warp_wait(d2_full(buf), (it >> 1) & 1, abort_flag, p.err, kErrWaitEpilogue)) break;
+      if (!warp_wait(d2_full(buf), (it >> 1) & 1, abort_flag, p.err, kErrWaitEpilogue)) return false;
       tc_fence_after();
       const int64_t grow = static_cast<int64_t>(t) * TILE + row;
       for (int half = 0; half < kb; ++half) {
@@ -435,8 +442,70 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
         }
       }
+      return true;
+    };
+    // The next tile's LayerNorm comes first: the first GEMM of tile it+1 must
+    // not wait for the output of tile it.
+    bool ok = my_tiles == 0 || layer_norm(0);
+    for (int it = 0; ok && it < my_tiles; ++it) {
+      if (it + 1 < my_tiles) ok = layer_norm(it + 1);
+      ok = ok && second_epilogue(it);
     }
     if (lane == 0 && store_pending) bulk_wait_all();
+  } else {
+    // ---- first epilogue, two groups of four warps taking alternate chunks:
+    //      D1 chunk -> relu(scale1 * acc + b1) -> f16 H operand rows ----
+    const int q = warp & 3;  // TMEM lane quarter this warp may read
+    const int group = (warp - 6) >> 2;
+    const int row = q * 32 + lane;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
+    ChunkCursor cur;
+    cur.start(nh);
+    if (group == 1) cur.advance();
+    for (int j = group; j < total; j += 2, cur.advance(), cur.advance()) {
+      const int db = j % NBUF, h = cur.chunk;
+      const uint32_t ph = (j / NBUF) & 1;
+      if (!warp_wait(d1_full(db), ph, abort_flag, p.err, kErrWaitEpilogue)) break;
+      tc_fence_after();
+      if (!warp_wait(h_empty(db), ph ^ 1, abort_flag, p.err, kErrWaitEpilogue)) break;
+      uint8_t *hbuf = smem + OFF_H + db * 32768;
+#pragma unroll 1
+      for (int half = 0; half < 2; ++half) {  // 64 hidden channels = one 128-byte K block of the H row
+        uint32_t v[2][32];
+        tmem_ld32(lane_base + db * HC + half * 64, v[0]);
+        tmem_ld32(lane_base + db * HC + half * 64 + 32, v[1]);
+        tmem_ld_wait();
+        if (half == 1) {  // the whole accumulator has been read: release it
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(d1_empty(db));
+        }
+        const float4 *sc = reinterpret_cast<const float4 *>(s1v + h * HC + half * 64);
+        const float4 *bi = reinterpret_cast<const float4 *>(b1v + h * HC + half * 64);
+        uint8_t *hrow = hbuf + half * 16384;
+#pragma unroll
+        for (int c16 = 0; c16 < 8; ++c16) {  // 8 hidden channels = one 16-byte chunk of the row
+          uint32_t pk[4];
+#pragma unroll
+          for (int i2 = 0; i2 < 2; ++i2) {
+            const float4 sv = sc[c16 * 2 + i2], bv = bi[c16 * 2 + i2];
+            const int c = c16 * 8 + i2 * 4;
+            const float2 y0 =
+                f2fma(make_float2(__uint_as_float(v[c >> 5][c & 31]), __uint_as_float(v[c >> 5][(c + 1) & 31])),
+                      make_float2(sv.x, sv.y), make_float2(bv.x, bv.y));
+            const float2 y1 =
+                f2fma(make_float2(__uint_as_float(v[c >> 5][(c + 2) & 31]), __uint_as_float(v[c >> 5][(c + 3) & 31])),
+                      make_float2(sv.z, sv.w), make_float2(bv.z, bv.w));
+            pk[i2 * 2] = pack_half2_relu(y0.x, y0.y);
+            pk[i2 * 2 + 1] = pack_half2_relu(y1.x, y1.y);
+          }
+          *reinterpret_cast<uint4 *>(hrow + sw128_offset(row, c16)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        }
+      }
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(h_full(db));
+    }
   }
 
   tc_fence_before();
@@ -509,17 +578,27 @@ __device__ __forceinline__ float matrix_element(const MatrixDev &m, int64_t i) {
 // ... so each load instruction reads 32 consecutive columns of one row.
 // Pass 1 finds the column's scale (the largest magnitude's power of two, or
 // the given q8 channel scale), pass 2 writes the f16 operand column.
-// Matrix 1 ([c][h]) -> w1p [kb][hp][64]; matrix 2 ([h][c]) -> w2p [cp][hp].
+// Matrix 1 ([c][h]) -> w1p [kb][hp][64]; matrix 2 ([h][c]) -> w2p [hp/64][cp][64].
 constexpr int PREP_THREADS = 1024;
 constexpr int kPrepBatch = 16;  // values per thread loaded before any is used
 
+// Shared memory of one preparation block: the column maxima and, for pass 2,
+// a window of 256 K values of the block's 32 columns, which leaves as whole
+// 128-byte operand rows (coalesced) instead of scattered 2-byte stores.
+struct PrepShared {
+  float red[32][33];
+  float col_scale[32];
+  __align__(16) __half stage[32][264];
+};
+
 template <int FMT>
-__device__ __forceinline__ void prep_columns(const MatrixDev &m, bool first, int o, int inner, int cols, int kpad,
-                                             int cp, int hp, int c, int h, const float *__restrict__ b1,
-                                             const float *__restrict__ b2, __half *__restrict__ w1p,
-                                             __half *__restrict__ w2p, float *__restrict__ vec) {
-  __shared__ float red[32][33];
-  __shared__ float col_scale[32];
+__device__ __forceinline__ void prep_columns(PrepShared &sh, const MatrixDev &m, bool first, int o, int inner,
+                                             int cols, int kpad, int cp, int hp, int c, int h,
+                                             const float *__restrict__ b1, const float *__restrict__ b2,
+                                             __half *__restrict__ w1p, __half *__restrict__ w2p,
+                                             float *__restrict__ vec) {
+  float(&red)[32][33] = sh.red;
+  float(&col_scale)[32] = sh.col_scale;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr bool codes = FMT == AF2_WEIGHTS_Q8_CHANNEL;
   // Pass 1: the column's values for this warp (k = warp, warp + 32, ...) in
@@ -564,32 +643,43 @@ __device__ __forceinline__ void prep_columns(const MatrixDev &m, bool first, int
     }
   }
   __syncthreads();
-  // Pass 2: the f16 operand column (value / scale, a power of two: exact).
+  // Pass 2: the f16 operand columns (value / scale, a power of two: exact),
+  // staged 256 K values at a time and written as whole operand rows.
   const float inv = codes ? 1.f : 1.f / col_scale[lane];
-  auto put = [&](int k, float w) {
-    if (first)
-      w1p[(static_cast<int64_t>(k >> 6) * hp + o) * 64 + (k & 63)] = __float2half_rn(w);
-    else
-      w2p[static_cast<int64_t>(o) * hp + k] = __float2half_rn(w);
-  };
-  if (inner <= 32 * kPrepBatch) {  // the common case: every value is still in registers
+  const int o0 = o - lane;
+  __half *dst_base = first ? w1p : w2p;
+  const int rows_per_block = first ? hp : cp;  // operand rows in one 64-wide K block
+  for (int k0 = 0; k0 < kpad; k0 += 256) {
+    const int kend = min(k0 + 256, kpad);
+    if (inner <= 32 * kPrepBatch) {  // the common case: every value is still in registers
 #pragma unroll
-    for (int b = 0; b < kPrepBatch; ++b) {
-      const int k = warp + 32 * b;
-      if (k < kpad) put(k, vals[b] * inv);
+      for (int b = 0; b < kPrepBatch; ++b) {
+        const int k = warp + 32 * b;
+        if (k >= k0 && k < kend) sh.stage[lane][k - k0] = __float2half_rn(vals[b] * inv);
+      }
+      for (int k = k0 + warp; k < kend; k += 32)
+        if (k >= 32 * kPrepBatch) sh.stage[lane][k - k0] = __float2half_rn(0.f);
+    } else {
+      for (int k = k0 + warp; k < kend; k += 32) {
+        float w = 0.f;
+        if (o < cols && k < inner) w = matrix_element<FMT>(m, static_cast<int64_t>(k) * cols + o) * inv;
+        sh.stage[lane][k - k0] = __float2half_rn(w);
+      }
     }
-    for (int k = warp + 32 * kPrepBatch; k < kpad; k += 32) put(k, 0.f);
-  } else {
-    for (int k = warp; k < kpad; k += 32) {
-      float w = 0.f;
-      if (o < cols && k < inner) w = matrix_element<FMT>(m, static_cast<int64_t>(k) * cols + o) * inv;
-      put(k, w);
+    __syncthreads();
+    const int blocks = (kend - k0) >> 6;  // 64-wide K blocks in the window: 32 rows x 128 B each
+    for (int i = threadIdx.x; i < blocks * 256; i += PREP_THREADS) {
+      const int blk = i >> 8, r = (i >> 3) & 31, c16 = i & 7;
+      const uint4 v = *reinterpret_cast<const uint4 *>(&sh.stage[r][blk * 64 + c16 * 8]);
+      const int64_t kb_index = (k0 >> 6) + blk;
+      *reinterpret_cast<uint4 *>(dst_base + (kb_index * rows_per_block + o0 + r) * 64 + c16 * 8) = v;
     }
+    __syncthreads();
   }
 }
 
 // One block per 32 output columns of one matrix.  Matrix 1 ([c][h]) ->
-// w1p [kb][hp][64]; matrix 2 ([h][c]) -> w2p [cp][hp]; plus the vectors
+// w1p [kb][hp][64]; matrix 2 ([h][c]) -> w2p [hp/64][cp][64]; plus the vectors
 // gamma beta [cp], scale1 bias1 [hp], scale2 bias2 [cp] (zero padded).
 __global__ void __launch_bounds__(PREP_THREADS)
     prep_kernel(MatrixDev m1, MatrixDev m2, const float *__restrict__ gamma, const float *__restrict__ beta,
@@ -605,12 +695,13 @@ __global__ void __launch_bounds__(PREP_THREADS)
       vec[i] = i < c ? gamma[i] : 0.f;
       vec[cp + i] = i < c ? beta[i] : 0.f;
     }
+  __shared__ PrepShared sh;
   if (m.format == AF2_WEIGHTS_Q8_CHANNEL)
-    prep_columns<AF2_WEIGHTS_Q8_CHANNEL>(m, first, o, inner, cols, kpad, cp, hp, c, h, b1, b2, w1p, w2p, vec);
+    prep_columns<AF2_WEIGHTS_Q8_CHANNEL>(sh, m, first, o, inner, cols, kpad, cp, hp, c, h, b1, b2, w1p, w2p, vec);
   else if (m.format == AF2_WEIGHTS_Q8_BLOCK)
-    prep_columns<AF2_WEIGHTS_Q8_BLOCK>(m, first, o, inner, cols, kpad, cp, hp, c, h, b1, b2, w1p, w2p, vec);
+    prep_columns<AF2_WEIGHTS_Q8_BLOCK>(sh, m, first, o, inner, cols, kpad, cp, hp, c, h, b1, b2, w1p, w2p, vec);
   else
-    prep_columns<AF2_WEIGHTS_F32>(m, first, o, inner, cols, kpad, cp, hp, c, h, b1, b2, w1p, w2p, vec);
+    prep_columns<AF2_WEIGHTS_F32>(sh, m, first, o, inner, cols, kpad, cp, hp, c, h, b1, b2, w1p, w2p, vec);
 }
 
 // Bit-exact q8 decode (dtype.ts:86-97; per-channel: the f32 product).
@@ -638,7 +729,7 @@ uint32_t smem_bytes(int kb, int hp) { return off_vec(kb) + (4u * kb * 64 + 2u * 
 template <typename XT, typename OT>
 af2_status launch_kernel(af2_ctx *ctx, const CUtensorMap &xmap, const CUtensorMap &w1map, const CUtensorMap &w2map,
                          const CUtensorMap &omap, const Args &a, cudaStream_t stream) {
-  auto kernel = transition_kernel<XT, OT>;
+  auto kernel = a.kb == 2 ? transition_kernel<XT, OT, 2> : transition_kernel<XT, OT, 1>;
   const uint32_t smem = smem_bytes(a.kb, a.hp);
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return cuda_fail(ctx, e, "transition kernel attributes");
@@ -670,7 +761,7 @@ TransitionLayout transition_layout(int64_t rows, int64_t c, int64_t h, int x_dty
   L.c = c;
   L.h = h;
   L.cp = c <= 64 ? 64 : 128;
-  L.hp = (h + 63) / 64 * 64;
+  L.hp = (h + 127) / 128 * 128;
   L.fast_in = x_dtype != AF2_F32 && c % 8 == 0;
   L.chunk_rows = L.fast_in ? rows : std::min<int64_t>(rows, 65536);
   size_t off = 0;
@@ -709,8 +800,8 @@ af2_status transition_launch(af2_ctx *ctx, const TransitionLayout &L, const void
   CUtensorMap w1map, w2map;
   if (!encode_map_3d(&w1map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, ws + L.off_w1, 64, L.hp, kb, 128,
                      (uint64_t)L.hp * 128, 64, HC, kb, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !encode_map_3d(&w2map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, ws + L.off_w2, L.hp, L.cp, 1, L.hp * 2,
-                     (uint64_t)L.hp * 2 * L.cp, 64, L.cp, 1, CU_TENSOR_MAP_SWIZZLE_128B))
+      !encode_map_3d(&w2map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, ws + L.off_w2, 64, L.cp, L.hp / 64, 128,
+                     (uint64_t)L.cp * 128, 64, L.cp, 2, CU_TENSOR_MAP_SWIZZLE_128B))
     return fail(ctx, AF2_ERR_CUDA, "cuTensorMapEncodeTiled failed for the transition weights");
   const size_t xb = x_dtype == AF2_F32 ? 4 : 2, ob = out_dtype == AF2_F32 ? 4 : 2;
   const bool tma_out = out_dtype != AF2_F32 && L.c % 8 == 0;
