@@ -10,6 +10,9 @@ from .device import Device
 from .triangle import (TriangleGpuOptions, TriangleGpuResult, TriangleMultiplicationIncomingGpu,
                        TriangleMultiplicationOutgoingGpu, encode_triangle_multiplication,
                        encode_triangle_multiplication_tensors, triangle_weight_count, triangle_workspace_bytes)
+from .opm import (OuterProductMeanGpu, OuterProductMeanInput, OuterProductMeanResult, OuterProductMeanWeights,
+                  encode_outer_product_mean_tensors, linear_tensors, opm_weight_count, opm_workspace_bytes,
+                  pack_outer_product_mean_weights, validate_outer_product_mean_input)
 from .transition import (Q8Matrix, TransitionGpu, TransitionInput, TransitionResult, TransitionWeights,
                          dequant_q8_tensors, encode_transition_tensors, pack_transition_weights,
                          transition_weight_count, transition_workspace_bytes, validate_transition_input)
@@ -24,5 +27,7 @@ __all__ = [
     "TriangleShape", "error_metrics", "expected_weight_element_count", "pack_weights", "validate_triangle_input",
     "Q8Matrix", "TransitionGpu", "TransitionInput", "TransitionResult", "TransitionWeights", "dequant_q8_tensors",
     "encode_transition_tensors", "pack_transition_weights", "transition_weight_count", "transition_workspace_bytes",
-    "validate_transition_input",
+    "validate_transition_input", "OuterProductMeanGpu", "OuterProductMeanInput", "OuterProductMeanResult",
+    "OuterProductMeanWeights", "encode_outer_product_mean_tensors", "linear_tensors", "opm_weight_count",
+    "opm_workspace_bytes", "pack_outer_product_mean_weights", "validate_outer_product_mean_input",
 ]

@@ -62,6 +62,19 @@ class TransitionOptions(ctypes.Structure):
     _fields_ = [("max_chunk_rows", ctypes.c_int32), ("residual", ctypes.c_int32)]
 
 
+class OpmShape(ctypes.Structure):
+    _fields_ = [("sequences", _i64), ("length", _i64), ("c_m", _i64), ("c_outer", _i64), ("c_z", _i64)]
+
+
+class OpmOptions(ctypes.Structure):
+    _fields_ = [("layer_norm_epsilon", _f64), ("normalization_epsilon", _f64), ("row_block_residues", ctypes.c_int32),
+                ("residual", ctypes.c_int32)]
+
+
+class LinearShape(ctypes.Structure):
+    _fields_ = [("rows", _i64), ("inner", _i64), ("columns", _i64)]
+
+
 SIGNATURES = {
     "af2_version": (_i32, []),
     "af2_status_string": (ctypes.c_char_p, [_i32]),
@@ -93,6 +106,17 @@ SIGNATURES = {
                                    ctypes.POINTER(TransitionOptions), _i32, _vp, ctypes.POINTER(OpStats)]),
     "af2_transition": (_i32, [_vp, ctypes.POINTER(TransitionShape), _vp, _i32, ctypes.POINTER(TransitionWeights),
                               _f64, ctypes.POINTER(TransitionOptions), _vp, _i32, _vp, _vp]),
+    "af2_opm_weight_count": (_i64, [ctypes.POINTER(OpmShape)]),
+    "af2_opm_check": (_i32, [ctypes.POINTER(OpmShape), _i64, ctypes.c_char_p, ctypes.c_size_t]),
+    "af2_opm_workspace_bytes": (_i32, [ctypes.POINTER(OpmShape), ctypes.POINTER(OpmOptions),
+                                       ctypes.POINTER(ctypes.c_uint64)]),
+    "af2_outer_product_mean_host": (_i32, [_vp, ctypes.POINTER(OpmShape), _vp, _vp, _vp, _i64,
+                                           ctypes.POINTER(OpmOptions), _i32, _vp, ctypes.POINTER(OpStats)]),
+    "af2_outer_product_mean": (_i32, [_vp, ctypes.POINTER(OpmShape), _vp, _i32, _vp, _vp, _i64,
+                                      ctypes.POINTER(OpmOptions), _vp, _i32, _vp, _vp]),
+    "af2_linear_workspace_bytes": (_i32, [ctypes.POINTER(LinearShape), _i32, ctypes.POINTER(ctypes.c_uint64)]),
+    "af2_linear": (_i32, [_vp, ctypes.POINTER(LinearShape), _vp, _i32, ctypes.POINTER(Matrix), _vp, _i32, _i32, _vp,
+                          _i32, _vp, _vp]),
 }
 
 _lib = None

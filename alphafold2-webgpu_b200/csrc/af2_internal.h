@@ -34,6 +34,14 @@ enum ProfileKernel {
   kProfTransitionNormalize,
   kProfTransition,
   kProfDequant,
+  kProfPrepare,
+  kProfConvert,
+  kProfLinear,
+  kProfOpmNormalize,
+  kProfOpmProject,
+  kProfOpmCount,
+  kProfOpmOuter,
+  kProfOpmOutput,
   kProfCount
 };
 const char *profile_name(int id);
@@ -132,5 +140,68 @@ af2_status transition_launch(af2_ctx *ctx, const TransitionLayout &L, const void
 
 af2_status dequant_launch(af2_ctx *ctx, const af2_matrix &m, int64_t inner, int64_t cols, float *out,
                           cudaStream_t stream);
+
+// ---- shared dense projection (gemm.cu) ----
+
+// One tcgen05 GEMM D = A W over prepared weights, with its epilogue.
+struct LinearOperands {
+  const void *a = nullptr;        // f16 rows [rows][lda], the first `inner` columns used
+  int64_t lda = 0;
+  const void *w = nullptr;        // prepared weights [k_pad / 64][cols_pad][64] f16
+  const float *scale = nullptr;   // per column (cols_pad entries)
+  const float *bias = nullptr;    // per column (cols_pad entries)
+  const float *row_scale = nullptr;  // per row, or NULL
+  const float *row_mask = nullptr;   // OPM projection: per row
+  int64_t rows = 0, inner = 0, cols = 0;
+  void *out = nullptr;            // linear: [rows][ldo] of out_dtype
+  int64_t ldo = 0;
+  int out_dtype = AF2_F32;
+  int relu = 0, residual = 0;
+  bool opm_projection = false;    // columns [0, cols/2) -> left, the rest -> right (f16), times row_mask
+  void *left = nullptr, *right = nullptr;
+  int prof = kProfLinear;
+};
+
+// Tile width the GEMM uses for `cols` output columns, and the padded column count.
+inline int64_t linear_tile_n(int64_t cols) { return cols >= 256 ? 256 : align_up(cols, 64); }
+inline int64_t linear_cols_pad(int64_t cols) { return align_up(cols, linear_tile_n(cols)); }
+
+// Prepares an [inner][cols] matrix as operand rows [inner_pad / 64][rows_total][64] starting at row
+// row0 (rows_total 0 = cols_pad), and its per-column scales (times extra_scale) at scale_out[row0 ...].
+af2_status prepare_matrix(af2_ctx *ctx, const af2_matrix &w, int64_t inner, int64_t cols, int64_t inner_pad,
+                          int64_t cols_pad, float extra_scale, void *out, float *scale_out, cudaStream_t stream,
+                          int64_t row0 = 0, int64_t rows_total = 0);
+af2_status pad_vector(af2_ctx *ctx, const float *src, int64_t n, int64_t n_pad, float *dst, cudaStream_t stream);
+af2_status convert_rows_f16(af2_ctx *ctx, const void *src, int dtype, int64_t rows, int64_t inner, int64_t inner_pad,
+                            void *dst, cudaStream_t stream);
+af2_status linear_launch(af2_ctx *ctx, const LinearOperands &op, cudaStream_t stream);
+
+struct LinearLayout {
+  int64_t k_pad = 0, cols_pad = 0;
+  bool convert = false;  // A goes through an f16 copy first
+  size_t off_w = 0, off_scale = 0, off_bias = 0, off_a = 0, total = 0;
+};
+
+LinearLayout linear_layout(int64_t rows, int64_t inner, int64_t cols, int a_dtype);
+af2_status linear_run(af2_ctx *ctx, const LinearLayout &L, int64_t rows, int64_t inner, int64_t cols, const void *a,
+                      int a_dtype, const af2_matrix &weight, const float *bias, int activation, int residual,
+                      void *out, int out_dtype, void *workspace, cudaStream_t stream);
+
+// ---- outer-product mean (opm.cu) ----
+
+struct OpmLayout {
+  int64_t s = 0, n = 0, cm = 0, c = 0, cz = 0;
+  int64_t cmp = 0;          // c_m padded to 64
+  int64_t block_rows = 0;   // residues i per output block (a multiple of 4)
+  int out_shift = 0;        // outer is stored times 2^-out_shift (2^out_shift >= S)
+  size_t off_wlr = 0, off_wlr_scale = 0, off_wlr_bias = 0, off_wo = 0, off_wo_scale = 0, off_wo_bias = 0;
+  size_t off_ln = 0, off_xn = 0, off_left = 0, off_right = 0, off_rowscale = 0, off_outer = 0, total = 0;
+};
+
+OpmLayout opm_layout(int64_t s, int64_t n, int64_t cm, int64_t c, int64_t cz, int64_t row_block);
+
+af2_status opm_launch(af2_ctx *ctx, const OpmLayout &L, const void *m, int m_dtype, const float *mask,
+                      const float *packed, double ln_eps, double norm_eps, int residual, void *out, int out_dtype,
+                      void *workspace, cudaStream_t stream);
 
 }  // namespace af2

@@ -51,9 +51,12 @@ af2_status ensure(af2_ctx *ctx, DeviceBuffer &buf, size_t bytes, const char *wha
 }
 
 const char *profile_name(int id) {
-  static const char *names[kProfCount] = {"triangle.prepare",     "triangle.relayout",     "triangle.project",
-                                          "triangle.contract",    "triangle.output",       "transition.prepare",
-                                          "transition.normalize", "transition.fused",      "q8.decode"};
+  static const char *names[kProfCount] = {
+      "triangle.prepare",    "triangle.relayout",    "triangle.project",  "triangle.contract",
+      "triangle.output",     "transition.prepare",   "transition.normalize", "transition.fused",
+      "q8.decode",           "weights.prepare",      "activations.convert",  "linear",
+      "opm.normalize",       "opm.project",          "opm.count",         "opm.outer",
+      "opm.output"};
   return (id >= 0 && id < kProfCount) ? names[id] : nullptr;
 }
 
@@ -183,6 +186,29 @@ af2_status validate_transition(af2_ctx *ctx, const af2_transition_shape *shape, 
     return fail(ctx, AF2_ERR_UNSUPPORTED, "transition hidden channels above 1024 are not supported");
   if (shape->rows > (int64_t(1) << 30))
     return fail(ctx, AF2_ERR_UNSUPPORTED, "transition rows beyond 2^30 are not supported");
+  return AF2_OK;
+}
+
+// validate (src/evoformer/outer-product-mean.ts:45-65) for a C caller, then the kernels' limits.
+af2_status validate_opm(af2_ctx *ctx, const af2_opm_shape *shape, int64_t weight_count) {
+  if (!shape) return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "shape is NULL");
+  const int64_t dims[5] = {shape->sequences, shape->length, shape->c_m, shape->c_outer, shape->c_z};
+  for (int64_t d : dims)
+    if (!positive_safe(d))
+      return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "outer product mean dimensions must be positive safe integers");
+  if ((double)shape->sequences * (double)shape->length * (double)shape->c_m > (double)kMaxSafeInteger ||
+      (double)shape->length * (double)shape->length * (double)shape->c_z > (double)kMaxSafeInteger)
+    return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "tensor dimensions exceed JavaScript's safe integer range");
+  const int64_t expected = af2_opm_weight_count(shape);
+  if (weight_count != expected)
+    return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "packed weights have " + std::to_string(weight_count) +
+                                                   " values; expected " + std::to_string(expected));
+  if (shape->c_outer != 32)
+    return fail(ctx, AF2_ERR_UNSUPPORTED, "the sm_100a outer-product kernel is built for c_outer = 32");
+  if (shape->c_m > 256) return fail(ctx, AF2_ERR_UNSUPPORTED, "c_m above 256 is not supported");
+  if (shape->c_z > 4096) return fail(ctx, AF2_ERR_UNSUPPORTED, "c_z above 4096 is not supported");
+  if (shape->length > 65536 || shape->sequences > (1 << 24))
+    return fail(ctx, AF2_ERR_UNSUPPORTED, "length above 65536 or more than 2^24 sequences are not supported");
   return AF2_OK;
 }
 
@@ -582,6 +608,166 @@ af2_status af2_dequant_q8(af2_ctx *ctx, const af2_matrix *matrix, int64_t inner,
   cudaSetDevice(ctx->device);
   cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
   return dequant_launch(ctx, *matrix, inner, cols, out, s);
+}
+
+int64_t af2_opm_weight_count(const af2_opm_shape *shape) {
+  if (!shape) return 0;
+  const int64_t cm = shape->c_m, c = shape->c_outer, cz = shape->c_z;
+  return 2 * cm + 2 * (cm * c + c) + c * c * cz + cz;
+}
+
+af2_status af2_opm_check(const af2_opm_shape *shape, int64_t weight_count, char *message, size_t capacity) {
+  af2_ctx scratch;
+  const af2_status st = validate_opm(&scratch, shape, weight_count);
+  if (message && capacity > 0) {
+    std::strncpy(message, scratch.last_error.c_str(), capacity - 1);
+    message[capacity - 1] = '\0';
+  }
+  return st;
+}
+
+af2_status af2_opm_workspace_bytes(const af2_opm_shape *shape, const af2_opm_options *options, uint64_t *bytes) {
+  if (!shape || !bytes) return AF2_ERR_INVALID_ARGUMENT;
+  af2_ctx scratch;
+  if (validate_opm(&scratch, shape, af2_opm_weight_count(shape)) != AF2_OK) return AF2_ERR_INVALID_ARGUMENT;
+  *bytes = opm_layout(shape->sequences, shape->length, shape->c_m, shape->c_outer, shape->c_z,
+                      options ? options->row_block_residues : 0)
+               .total;
+  return AF2_OK;
+}
+
+static af2_status opm_options(af2_ctx *ctx, const af2_opm_options *o, double *ln_eps, double *norm_eps, int *rb,
+                              int *residual) {
+  *ln_eps = (o && o->layer_norm_epsilon != 0) ? o->layer_norm_epsilon : 1e-5;
+  *norm_eps = (o && o->normalization_epsilon != 0) ? o->normalization_epsilon : 1e-3;
+  *rb = o ? o->row_block_residues : 0;
+  *residual = o ? o->residual : 0;
+  if (!(*ln_eps > 0) || !std::isfinite(*ln_eps) || !(*norm_eps > 0) || !std::isfinite(*norm_eps))
+    return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "epsilons must be finite and positive");
+  if (*rb < 0) return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "rowBlockResidues must be a positive safe integer");
+  return AF2_OK;
+}
+
+af2_status af2_outer_product_mean(af2_ctx *ctx, const af2_opm_shape *shape, const void *m, int m_dtype,
+                                  const float *mask, const float *packed_weights, int64_t weight_count,
+                                  const af2_opm_options *options, void *out, int out_dtype, void *workspace,
+                                  void *stream) {
+  if (!ctx) return AF2_ERR_INVALID_ARGUMENT;
+  af2_status st = validate_opm(ctx, shape, weight_count);
+  if (st != AF2_OK) return st;
+  if (!m || !mask || !packed_weights || !out) return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "a tensor pointer is NULL");
+  if (!valid_dtype(m_dtype) || !valid_dtype(out_dtype))
+    return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "dtype must be AF2_F32, AF2_F16 or AF2_BF16");
+  double ln_eps, norm_eps;
+  int rb, residual;
+  if ((st = opm_options(ctx, options, &ln_eps, &norm_eps, &rb, &residual)) != AF2_OK) return st;
+  cudaSetDevice(ctx->device);
+  const OpmLayout L = opm_layout(shape->sequences, shape->length, shape->c_m, shape->c_outer, shape->c_z, rb);
+  void *ws = workspace;
+  if (!ws) {
+    if ((st = ensure(ctx, ctx->workspace, L.total, "outer product mean scratch")) != AF2_OK) return st;
+    ws = ctx->workspace.ptr;
+  } else if (reinterpret_cast<uintptr_t>(ws) % 256 != 0) {
+    return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "workspace must be 256-byte aligned");
+  }
+  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+  return opm_launch(ctx, L, m, m_dtype, mask, packed_weights, ln_eps, norm_eps, residual, out, out_dtype, ws, s);
+}
+
+af2_status af2_outer_product_mean_host(af2_ctx *ctx, const af2_opm_shape *shape, const void *m, const float *mask,
+                                       const float *packed_weights, int64_t weight_count,
+                                       const af2_opm_options *options, int io_dtype, void *out, af2_op_stats *stats) {
+  if (!ctx) return AF2_ERR_INVALID_ARGUMENT;
+  af2_status st = validate_opm(ctx, shape, weight_count);
+  if (st != AF2_OK) return st;
+  if (!m || !mask || !packed_weights || !out) return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "a tensor pointer is NULL");
+  if (!valid_dtype(io_dtype)) return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "dtype must be AF2_F32, AF2_F16 or AF2_BF16");
+  double ln_eps, norm_eps;
+  int rb, residual;
+  if ((st = opm_options(ctx, options, &ln_eps, &norm_eps, &rb, &residual)) != AF2_OK) return st;
+  cudaSetDevice(ctx->device);
+  const auto t0 = std::chrono::steady_clock::now();
+  const int64_t S = shape->sequences, N = shape->length;
+  const size_t m_bytes = (size_t)S * N * shape->c_m * dtype_bytes(io_dtype);
+  const size_t mask_bytes = (size_t)S * N * sizeof(float);
+  const size_t w_bytes = (size_t)weight_count * sizeof(float);
+  const size_t out_bytes = (size_t)N * N * shape->c_z * dtype_bytes(io_dtype);
+  if ((st = ensure(ctx, ctx->staging[0], m_bytes, "m upload")) != AF2_OK ||
+      (st = ensure(ctx, ctx->staging[1], mask_bytes, "mask upload")) != AF2_OK ||
+      (st = ensure(ctx, ctx->staging[2], w_bytes, "weight upload")) != AF2_OK ||
+      (st = ensure(ctx, ctx->staging[3], out_bytes, "output")) != AF2_OK)
+    return st;
+  const OpmLayout L = opm_layout(S, N, shape->c_m, shape->c_outer, shape->c_z, rb);
+  if ((st = ensure(ctx, ctx->workspace, L.total, "outer product mean scratch")) != AF2_OK) return st;
+  cudaStream_t s = ctx->stream;
+  cudaError_t e;
+  if ((e = cudaMemcpyAsync(ctx->staging[0].ptr, m, m_bytes, cudaMemcpyHostToDevice, s)) != cudaSuccess ||
+      (e = cudaMemcpyAsync(ctx->staging[1].ptr, mask, mask_bytes, cudaMemcpyHostToDevice, s)) != cudaSuccess ||
+      (e = cudaMemcpyAsync(ctx->staging[2].ptr, packed_weights, w_bytes, cudaMemcpyHostToDevice, s)) != cudaSuccess)
+    return cuda_fail(ctx, e, "upload inputs");
+  if (residual && (e = cudaMemsetAsync(ctx->staging[3].ptr, 0, out_bytes, s)) != cudaSuccess)
+    return cuda_fail(ctx, e, "clear residual output");
+  cudaEventRecord(ctx->ev_start, s);
+  st = opm_launch(ctx, L, ctx->staging[0].ptr, io_dtype, static_cast<const float *>(ctx->staging[1].ptr),
+                  static_cast<const float *>(ctx->staging[2].ptr), ln_eps, norm_eps, residual, ctx->staging[3].ptr,
+                  io_dtype, ctx->workspace.ptr, s);
+  if (st != AF2_OK) return st;
+  cudaEventRecord(ctx->ev_stop, s);
+  if ((e = cudaMemcpyAsync(out, ctx->staging[3].ptr, out_bytes, cudaMemcpyDeviceToHost, s)) != cudaSuccess)
+    return cuda_fail(ctx, e, "read back output");
+  if ((e = cudaStreamSynchronize(s)) != cudaSuccess) return cuda_fail(ctx, e, "outer product mean");
+  if ((st = check_device_errors(ctx)) != AF2_OK) return st;
+  if (stats) {
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, ctx->ev_start, ctx->ev_stop);
+    const double dS = (double)S, dN = (double)N, cm = (double)shape->c_m, c = (double)shape->c_outer,
+                 cz = (double)shape->c_z;
+    stats->device_milliseconds = ms;
+    stats->host_milliseconds =
+        std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+    // kernel-cost.ts: projection 2 S N c_m 2c, contraction 2 (N c)^2 S, output 2 N^2 c^2 c_z.
+    stats->flops = 2 * dS * dN * cm * 2 * c + 2 * dN * c * dN * c * dS + 2 * dN * dN * c * c * cz;
+    stats->workspace_bytes = L.total;
+    stats->peak_bytes = ctx->peak;
+  }
+  return AF2_OK;
+}
+
+af2_status af2_linear_workspace_bytes(const af2_linear_shape *shape, int a_dtype, uint64_t *bytes) {
+  if (!shape || !bytes || !positive_safe(shape->rows) || !positive_safe(shape->inner) ||
+      !positive_safe(shape->columns))
+    return AF2_ERR_INVALID_ARGUMENT;
+  *bytes = linear_layout(shape->rows, shape->inner, shape->columns, a_dtype).total;
+  return AF2_OK;
+}
+
+af2_status af2_linear(af2_ctx *ctx, const af2_linear_shape *shape, const void *a, int a_dtype,
+                      const af2_matrix *weight, const float *bias, int activation, int residual, void *out,
+                      int out_dtype, void *workspace, void *stream) {
+  if (!ctx) return AF2_ERR_INVALID_ARGUMENT;
+  if (!shape || !positive_safe(shape->rows) || !positive_safe(shape->inner) || !positive_safe(shape->columns))
+    return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "linear dimensions must be positive safe integers");
+  if (!a || !weight || !out) return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "a tensor pointer is NULL");
+  af2_status st = validate_matrix(ctx, *weight, "weight");
+  if (st != AF2_OK) return st;
+  if (!valid_dtype(a_dtype) || !valid_dtype(out_dtype))
+    return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "dtype must be AF2_F32, AF2_F16 or AF2_BF16");
+  if (activation != AF2_ACTIVATION_NONE && activation != AF2_ACTIVATION_RELU)
+    return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "activation must be AF2_ACTIVATION_NONE or AF2_ACTIVATION_RELU");
+  if (shape->rows > (int64_t(1) << 31) - 256 || shape->inner > 65536 || shape->columns > 65536)
+    return fail(ctx, AF2_ERR_UNSUPPORTED, "linear layer beyond 2^31 rows or 65536 channels");
+  cudaSetDevice(ctx->device);
+  const LinearLayout L = linear_layout(shape->rows, shape->inner, shape->columns, a_dtype);
+  void *ws = workspace;
+  if (!ws) {
+    if ((st = ensure(ctx, ctx->workspace, L.total, "linear scratch")) != AF2_OK) return st;
+    ws = ctx->workspace.ptr;
+  } else if (reinterpret_cast<uintptr_t>(ws) % 256 != 0) {
+    return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "workspace must be 256-byte aligned");
+  }
+  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+  return linear_run(ctx, L, shape->rows, shape->inner, shape->columns, a, a_dtype, *weight, bias, activation,
+                    residual, out, out_dtype, ws, s);
 }
 
 }  // extern "C"

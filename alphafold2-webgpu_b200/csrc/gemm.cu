@@ -1,0 +1,511 @@
+// gemm.cu -- the shared dense projection on sm_100a: weight preparation (f32
+// or mixed-q8 [in, out] matrices -> f16 operand rows with per-column scales)
+// and one persistent tcgen05 GEMM, D = A W, with the epilogues its callers
+// need: the linear layer out (=, +=) act(scale * D + bias) (optionally times a
+// per-row factor), and the outer-product-mean projection that splits the
+// masked result into its left and right operands.
+//
+// Reference: src/evoformer/transition.ts:91-138 (createLinearShader: A W + b,
+// optional ReLU, optional accumulate into the output) and
+// src/runtime/gemm.ts:836-1000 (the tiled GEMM it is written against);
+// src/evoformer/outer-product-mean.ts:189-231 (the masked left/right
+// projection) and :433-486 (the output projection, divided per pair by
+// norm_eps + count).
+//
+// Kernel: one CTA per SM, 128-row tiles of A times BN-column tiles of W (BN
+// <= 256), K in 64-wide blocks through a 4-deep TMA ring; warp 0 issues TMA,
+// warp 1 the tcgen05 MMAs into one of two TMEM accumulators, warps 2-5 drain
+// the other accumulator (one TMEM lane = one output row per thread).
+#include <algorithm>
+#include <string>
+
+#include "af2_device.cuh"
+#include "af2_internal.h"
+
+namespace af2 {
+namespace gemm {
+
+constexpr int BM = 128, BK = 64, STAGES = 4, THREADS = 192;
+constexpr uint32_t A_BYTES = BM * 128;
+
+struct LinearArgs {
+  const float *scale, *bias;  // per output column (padded to the tile)
+  const float *row_scale;     // per output row, or NULL
+  const float *row_mask;      // OPM projection: mask per row
+  void *out;                  // LINEAR: [rows][ldo] of OT
+  __half *left, *right;       // OPM projection: [rows][half_cols] each
+  int64_t rows, ldo;
+  int cols, half_cols, k_blocks, tiles_m, tiles_n, total_tiles, bn;
+  int relu, residual;
+  unsigned int *err;
+};
+
+enum { kModeLinear = 0, kModeOpmProjection = 1 };
+
+template <typename OT, int MODE>
+__global__ void __launch_bounds__(THREADS, 1)
+    linear_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap bmap,
+                  const LinearArgs p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = align1024(smem_raw);
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t B_BYTES = p.bn * 128u, STAGE_BYTES = A_BYTES + B_BYTES;
+  const uint32_t OFF_BAR = STAGES * STAGE_BYTES;
+  const uint32_t bar0 = sbase + OFF_BAR;
+  auto full = [&](int s) { return bar0 + 8u * s; };
+  auto empty = [&](int s) { return bar0 + 8u * (STAGES + s); };
+  auto acc_full = [&](int b) { return bar0 + 8u * (2 * STAGES + b); };
+  auto acc_empty = [&](int b) { return bar0 + 8u * (2 * STAGES + 2 + b); };
+  const uint32_t drain = bar0 + 8u * (2 * STAGES + 4);
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + OFF_BAR + 128);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + OFF_BAR + 136);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full(s), 1);
+      mbar_init(empty(s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(acc_full(b), 1);
+      mbar_init(acc_empty(b), 4);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---- TMA producer ----
+    if (lane == 0) {
+      tma_prefetch_map(&amap);
+      tma_prefetch_map(&bmap);
+      int it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < p.total_tiles; t += gridDim.x) {
+        const int mi = t / p.tiles_n, ni = t - mi * p.tiles_n;
+        for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
+          const int s = it % STAGES;
+          if (!mbar_wait(empty(s), ((it / STAGES) & 1) ^ 1, abort_flag, p.err, kErrWaitProducer)) {
+            ok = false;
+            break;
+          }
+          const uint32_t dst = sbase + s * STAGE_BYTES;
+          mbar_arrive_expect_tx(full(s), STAGE_BYTES);
+          tma_load_3d(dst, &amap, full(s), kb * BK, mi * BM, 0);
+          tma_load_3d(dst + A_BYTES, &bmap, full(s), 0, ni * p.bn, kb);
+        }
+      }
+      for (int j = std::max(0, it - STAGES); j < it; ++j) mbar_wait_drain(full(j % STAGES), (j / STAGES) & 1, p.err);
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer ----
+    if (lane == 0) {
+      const uint32_t idesc = idesc_f16_f32(BM, p.bn);
+      const uint64_t a_desc = sdesc_k_sw128(sbase);
+      int it = 0, tile_it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < p.total_tiles; t += gridDim.x, ++tile_it) {
+        const int buf = tile_it & 1;
+        if (!mbar_wait(acc_empty(buf), ((tile_it >> 1) & 1) ^ 1, abort_flag, p.err, kErrWaitMma)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + buf * 256;
+        for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
+          const int s = it % STAGES;
+          if (!mbar_wait(full(s), (it / STAGES) & 1, abort_flag, p.err, kErrWaitMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t ad = desc_add(a_desc, s * STAGE_BYTES), bd = desc_add(ad, A_BYTES);
+          if (kb == 0)
+            mma_f16_first(d, ad, bd, idesc);
+          else
+            mma_f16_acc(d, ad, bd, idesc);
+#pragma unroll
+          for (int ks = 1; ks < BK / 16; ++ks) mma_f16_acc(d, desc_add(ad, ks * 32), desc_add(bd, ks * 32), idesc);
+          mma_commit(empty(s));
+        }
+        if (ok) mma_commit(acc_full(buf));
+      }
+      mma_commit(drain);
+      mbar_wait_drain(drain, 0, p.err);
+    }
+    __syncwarp();
+  } else {
+    // ---- epilogue: one output row per thread ----
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    int tile_it = 0;
+    for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x, ++tile_it) {
+      const int mi = t / p.tiles_n, ni = t - mi * p.tiles_n;
+      const int buf = tile_it & 1;
+      if (!warp_wait(acc_full(buf), (tile_it >> 1) & 1, abort_flag, p.err, kErrWaitEpilogue)) break;
+      tc_fence_after();
+      const int64_t m = static_cast<int64_t>(mi) * BM + row;
+      const bool row_ok = m < p.rows;
+      const int n0 = ni * p.bn;
+      const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * 256;
+      float rs = 1.f;
+      if (MODE == kModeLinear && p.row_scale && row_ok) rs = p.row_scale[m];
+      if (MODE == kModeOpmProjection && row_ok) rs = p.row_mask[m];
+      for (int chunk = 0; chunk < p.bn / 32; ++chunk) {
+        uint32_t v[32];
+        tmem_ld32(taddr + chunk * 32, v);
+        tmem_ld_wait();
+        const int c0 = n0 + chunk * 32;
+        if (!row_ok || c0 >= p.cols) continue;
+        float y[32];
+        const float4 *sc = reinterpret_cast<const float4 *>(p.scale + c0);
+        const float4 *bi = reinterpret_cast<const float4 *>(p.bias + c0);
+#pragma unroll
+        for (int i4 = 0; i4 < 8; ++i4) {
+          const float4 s4 = __ldg(sc + i4), b4 = __ldg(bi + i4);
+          y[4 * i4 + 0] = fmaf(__uint_as_float(v[4 * i4 + 0]), s4.x, b4.x);
+          y[4 * i4 + 1] = fmaf(__uint_as_float(v[4 * i4 + 1]), s4.y, b4.y);
+          y[4 * i4 + 2] = fmaf(__uint_as_float(v[4 * i4 + 2]), s4.z, b4.z);
+          y[4 * i4 + 3] = fmaf(__uint_as_float(v[4 * i4 + 3]), s4.w, b4.w);
+        }
+        if (MODE == kModeOpmProjection) {
+          // columns [0, half) -> left, [half, 2 half) -> right, both scaled by the mask
+          const int half = p.half_cols;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int col = c0 + i;
+            if (col < p.cols) {
+              __half *dst = col < half ? p.left + m * half + col : p.right + m * half + (col - half);
+              *dst = __float2half_rn(y[i] * rs);
+            }
+          }
+        } else {
+          OT *orow = static_cast<OT *>(p.out) + m * p.ldo;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int col = c0 + i;
+            if (col < p.cols) {
+              float val = p.relu ? fmaxf(y[i], 0.f) : y[i];
+              val *= rs;
+              orow[col] = from_f32<OT>(p.residual ? to_f32<OT>(orow[col]) + val : val);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acc_empty(buf));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Weight preparation: an [inner][cols] matrix (f32, q8 block or q8 channel)
+// -> f16 operand rows [inner_pad / 64][cols_pad][64] (K-blocked, one row per
+// output column) and a per-column f32 scale.  For q8 channel weights the rows
+// hold the int8 codes (exact in f16) and the scale is the given one; for f32
+// and q8 block weights (decoded exactly to f32 first) the scale is the power
+// of two bringing the column's largest magnitude into [0.5, 1).
+// ---------------------------------------------------------------------------
+constexpr int PREP_THREADS = 1024;
+constexpr int kPrepBatch = 16;
+
+struct MatrixDev {
+  int format, block;
+  const void *values, *scales;
+};
+
+template <int FMT>
+__device__ __forceinline__ float element(const MatrixDev &m, int64_t i) {
+  if (FMT == AF2_WEIGHTS_F32) return static_cast<const float *>(m.values)[i];
+  const float code = static_cast<float>(static_cast<const int8_t *>(m.values)[i]);
+  if (FMT == AF2_WEIGHTS_Q8_CHANNEL) return code;
+  const uint16_t bits = static_cast<const uint16_t *>(m.scales)[i / m.block];
+  return code * __half2float(__ushort_as_half(bits));
+}
+
+struct PrepShared {
+  float red[32][33];
+  float col_scale[32];
+  __align__(16) __half stage[32][264];
+};
+
+template <int FMT>
+__device__ __forceinline__ void prep_block(PrepShared &sh, const MatrixDev &m, int inner, int cols, int inner_pad,
+                                           int cols_pad, int row0, int rows_total, float extra_scale,
+                                           __half *__restrict__ out, float *__restrict__ scale_out) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int o0 = blockIdx.x * 32, o = o0 + lane;
+  constexpr bool codes = FMT == AF2_WEIGHTS_Q8_CHANNEL;
+  float vals[kPrepBatch];
+#pragma unroll
+  for (int b = 0; b < kPrepBatch; ++b) vals[b] = 0.f;  // warps past `inner` keep zeros (the padding)
+  float mx = 0.f;
+  for (int k0 = warp; k0 < inner; k0 += 32 * kPrepBatch) {
+#pragma unroll
+    for (int b = 0; b < kPrepBatch; ++b) {
+      const int k = k0 + 32 * b;
+      vals[b] = (o < cols && k < inner) ? element<FMT>(m, static_cast<int64_t>(k) * cols + o) : 0.f;
+    }
+#pragma unroll
+    for (int b = 0; b < kPrepBatch; ++b) mx = fmaxf(mx, fabsf(vals[b]));
+  }
+  sh.red[warp][lane] = mx;
+  __syncthreads();
+  if (warp == 0) {
+    float v = 0.f;
+    for (int w = 0; w < 32; ++w) v = fmaxf(v, sh.red[w][lane]);
+    float scale = 1.f;
+    if (o < cols) {
+      if (codes) {
+        scale = static_cast<const float *>(m.scales)[o];
+      } else if (v > 0.f && isfinite(v)) {
+        int e;
+        frexpf(v, &e);
+        scale = ldexpf(1.f, e);
+      }
+    }
+    sh.col_scale[lane] = scale;
+    if (o < cols_pad) scale_out[row0 + o] = scale * extra_scale;
+  }
+  __syncthreads();
+  const float inv = codes ? 1.f : 1.f / sh.col_scale[lane];
+  for (int k0 = 0; k0 < inner_pad; k0 += 256) {
+    const int kend = min(k0 + 256, inner_pad);
+    if (inner <= 32 * kPrepBatch) {
+#pragma unroll
+      for (int b = 0; b < kPrepBatch; ++b) {
+        const int k = warp + 32 * b;
+        if (k >= k0 && k < kend) sh.stage[lane][k - k0] = __float2half_rn(vals[b] * inv);
+      }
+      for (int k = k0 + warp; k < kend; k += 32)
+        if (k >= 32 * kPrepBatch) sh.stage[lane][k - k0] = __float2half_rn(0.f);
+    } else {
+      for (int k = k0 + warp; k < kend; k += 32) {
+        float w = 0.f;
+        if (o < cols && k < inner) w = element<FMT>(m, static_cast<int64_t>(k) * cols + o) * inv;
+        sh.stage[lane][k - k0] = __float2half_rn(w);
+      }
+    }
+    __syncthreads();
+    const int blocks = (kend - k0) >> 6;
+    for (int i = threadIdx.x; i < blocks * 256; i += PREP_THREADS) {
+      const int blk = i >> 8, r = (i >> 3) & 31, c16 = i & 7;
+      if (o0 + r < cols_pad) {
+        const uint4 v = *reinterpret_cast<const uint4 *>(&sh.stage[r][blk * 64 + c16 * 8]);
+        *reinterpret_cast<uint4 *>(
+            out + ((static_cast<int64_t>((k0 >> 6) + blk) * rows_total + row0 + o0 + r) * 64 + c16 * 8)) = v;
+      }
+    }
+    __syncthreads();
+  }
+}
+
+__global__ void __launch_bounds__(PREP_THREADS)
+    prep_matrix_kernel(MatrixDev m, int inner, int cols, int inner_pad, int cols_pad, int row0, int rows_total,
+                       float extra_scale, __half *__restrict__ out, float *__restrict__ scale_out) {
+  __shared__ PrepShared sh;
+  if (m.format == AF2_WEIGHTS_Q8_CHANNEL)
+    prep_block<AF2_WEIGHTS_Q8_CHANNEL>(sh, m, inner, cols, inner_pad, cols_pad, row0, rows_total, extra_scale, out,
+                                       scale_out);
+  else if (m.format == AF2_WEIGHTS_Q8_BLOCK)
+    prep_block<AF2_WEIGHTS_Q8_BLOCK>(sh, m, inner, cols, inner_pad, cols_pad, row0, rows_total, extra_scale, out,
+                                     scale_out);
+  else
+    prep_block<AF2_WEIGHTS_F32>(sh, m, inner, cols, inner_pad, cols_pad, row0, rows_total, extra_scale, out,
+                                scale_out);
+}
+
+// dst[i] = i < n ? src[i] : 0 for i < n_pad (src may be NULL: zeros).
+__global__ void pad_vector_kernel(const float *__restrict__ src, int n, int n_pad, float *__restrict__ dst) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n_pad) dst[i] = (src && i < n) ? src[i] : 0.f;
+}
+
+// f32 / 16-bit rows [rows][inner] -> f16 rows [rows][inner_pad] (zero padded).
+template <typename T>
+__global__ void to_f16_kernel(const T *__restrict__ src, int64_t rows, int inner, int inner_pad,
+                              __half *__restrict__ dst) {
+  const int64_t total = rows * inner_pad;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / inner_pad;
+    const int k = static_cast<int>(i - r * inner_pad);
+    dst[i] = __float2half_rn(k < inner ? to_f32<T>(src[r * inner + k]) : 0.f);
+  }
+}
+
+}  // namespace gemm
+
+using namespace gemm;
+
+namespace {
+CUtensorMapDataType f16map() { return CU_TENSOR_MAP_DATA_TYPE_FLOAT16; }
+}  // namespace
+
+af2_status prepare_matrix(af2_ctx *ctx, const af2_matrix &w, int64_t inner, int64_t cols, int64_t inner_pad,
+                          int64_t cols_pad, float extra_scale, void *out, float *scale_out, cudaStream_t stream,
+                          int64_t row0, int64_t rows_total) {
+  MatrixDev m{w.format, w.block, w.values, w.scales};
+  if (rows_total == 0) rows_total = cols_pad;
+  LaunchScope scope(ctx, stream, kProfPrepare);
+  prep_matrix_kernel<<<(unsigned)((cols_pad + 31) / 32), PREP_THREADS, 0, stream>>>(
+      m, (int)inner, (int)cols, (int)inner_pad, (int)cols_pad, (int)row0, (int)rows_total, extra_scale,
+      static_cast<__half *>(out), scale_out);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? AF2_OK : cuda_fail(ctx, e, "weight preparation");
+}
+
+af2_status pad_vector(af2_ctx *ctx, const float *src, int64_t n, int64_t n_pad, float *dst, cudaStream_t stream) {
+  LaunchScope scope(ctx, stream, kProfPrepare);
+  pad_vector_kernel<<<(unsigned)((n_pad + 255) / 256), 256, 0, stream>>>(src, (int)n, (int)n_pad, dst);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? AF2_OK : cuda_fail(ctx, e, "vector preparation");
+}
+
+af2_status convert_rows_f16(af2_ctx *ctx, const void *src, int dtype, int64_t rows, int64_t inner, int64_t inner_pad,
+                            void *dst, cudaStream_t stream) {
+  const int threads = 256;
+  const unsigned blocks = (unsigned)std::min<int64_t>((rows * inner_pad + threads - 1) / threads, 8LL * ctx->sm_count * 8);
+  LaunchScope scope(ctx, stream, kProfConvert);
+  __half *d = static_cast<__half *>(dst);
+  if (dtype == AF2_F32)
+    to_f16_kernel<float><<<blocks, threads, 0, stream>>>(static_cast<const float *>(src), rows, (int)inner,
+                                                         (int)inner_pad, d);
+  else if (dtype == AF2_BF16)
+    to_f16_kernel<__nv_bfloat16><<<blocks, threads, 0, stream>>>(static_cast<const __nv_bfloat16 *>(src), rows,
+                                                                 (int)inner, (int)inner_pad, d);
+  else
+    to_f16_kernel<__half><<<blocks, threads, 0, stream>>>(static_cast<const __half *>(src), rows, (int)inner,
+                                                          (int)inner_pad, d);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? AF2_OK : cuda_fail(ctx, e, "activation conversion");
+}
+
+namespace {
+
+template <typename OT, int MODE>
+af2_status launch_linear_t(af2_ctx *ctx, const CUtensorMap &amap, const CUtensorMap &bmap, const LinearArgs &a,
+                           int prof, cudaStream_t stream) {
+  auto kernel = linear_kernel<OT, MODE>;
+  const uint32_t smem = STAGES * (A_BYTES + a.bn * 128u) + 256 + 1024;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "linear kernel attributes");
+  const int grid = std::min(a.total_tiles, ctx->sm_count);
+  LaunchScope scope(ctx, stream, prof);
+  kernel<<<grid, THREADS, smem, stream>>>(amap, bmap, a);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? AF2_OK : cuda_fail(ctx, e, "linear kernel launch");
+}
+
+}  // namespace
+
+af2_status linear_launch(af2_ctx *ctx, const LinearOperands &op, cudaStream_t stream) {
+  const int64_t k_pad = align_up(op.inner, 64);
+  const int bn = op.cols >= 256 ? 256 : (int)align_up(op.cols, 64);
+  const int64_t cols_pad = align_up(op.cols, bn);
+  CUtensorMap amap, bmap;
+  // A: f16 rows of pitch lda; K past `inner` reads as zero (TMA fill), matching the zero-padded W rows.
+  if (!encode_map_3d(&amap, f16map(), op.a, op.inner, op.rows, 1, op.lda * 2, (uint64_t)op.rows * op.lda * 2, 64, BM, 1,
+                     CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_map_3d(&bmap, f16map(), op.w, 64, cols_pad, k_pad / 64, 128, (uint64_t)cols_pad * 128, 64, bn, 1,
+                     CU_TENSOR_MAP_SWIZZLE_128B))
+    return fail(ctx, AF2_ERR_CUDA, "cuTensorMapEncodeTiled failed for a linear layer");
+  LinearArgs a{};
+  a.scale = op.scale;
+  a.bias = op.bias;
+  a.row_scale = op.row_scale;
+  a.row_mask = op.row_mask;
+  a.out = op.out;
+  a.left = static_cast<__half *>(op.left);
+  a.right = static_cast<__half *>(op.right);
+  a.rows = op.rows;
+  a.ldo = op.ldo;
+  a.cols = (int)op.cols;
+  a.half_cols = (int)(op.cols / 2);
+  a.k_blocks = (int)(k_pad / 64);
+  a.tiles_m = (int)((op.rows + BM - 1) / BM);
+  a.tiles_n = (int)(cols_pad / bn);
+  a.total_tiles = a.tiles_m * a.tiles_n;
+  a.bn = bn;
+  a.relu = op.relu;
+  a.residual = op.residual;
+  a.err = ctx->err_word;
+  if (op.opm_projection) return launch_linear_t<__half, kModeOpmProjection>(ctx, amap, bmap, a, op.prof, stream);
+  if (op.out_dtype == AF2_F16) return launch_linear_t<__half, kModeLinear>(ctx, amap, bmap, a, op.prof, stream);
+  if (op.out_dtype == AF2_BF16) return launch_linear_t<__nv_bfloat16, kModeLinear>(ctx, amap, bmap, a, op.prof, stream);
+  return launch_linear_t<float, kModeLinear>(ctx, amap, bmap, a, op.prof, stream);
+}
+
+}  // namespace af2
+
+namespace af2 {
+
+// Scratch of af2_linear: prepared weights, their column scales and biases,
+// and an f16 copy of A when A is not already f16 rows with a 16-byte pitch.
+LinearLayout linear_layout(int64_t rows, int64_t inner, int64_t cols, int a_dtype) {
+  LinearLayout L;
+  L.k_pad = align_up(inner, 64);
+  L.cols_pad = linear_cols_pad(cols);
+  L.convert = a_dtype != AF2_F16 || inner % 8 != 0;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = off;
+    off = align_up(off + bytes, 256);
+    return at;
+  };
+  L.off_w = take((size_t)L.k_pad * L.cols_pad * 2);
+  L.off_scale = take((size_t)L.cols_pad * 4);
+  L.off_bias = take((size_t)L.cols_pad * 4);
+  L.off_a = L.convert ? take((size_t)rows * L.k_pad * 2) : off;
+  L.total = off;
+  return L;
+}
+
+af2_status linear_run(af2_ctx *ctx, const LinearLayout &L, int64_t rows, int64_t inner, int64_t cols, const void *a,
+                      int a_dtype, const af2_matrix &weight, const float *bias, int activation, int residual,
+                      void *out, int out_dtype, void *workspace, cudaStream_t stream) {
+  uint8_t *ws = static_cast<uint8_t *>(workspace);
+  float *scale = reinterpret_cast<float *>(ws + L.off_scale), *bvec = reinterpret_cast<float *>(ws + L.off_bias);
+  af2_status st;
+  if ((st = prepare_matrix(ctx, weight, inner, cols, L.k_pad, L.cols_pad, 1.f, ws + L.off_w, scale, stream)) !=
+          AF2_OK ||
+      (st = pad_vector(ctx, bias, bias ? cols : 0, L.cols_pad, bvec, stream)) != AF2_OK)
+    return st;
+  LinearOperands op;
+  op.a = a;
+  op.lda = inner;
+  if (L.convert) {
+    if ((st = convert_rows_f16(ctx, a, a_dtype, rows, inner, L.k_pad, ws + L.off_a, stream)) != AF2_OK) return st;
+    op.a = ws + L.off_a;
+    op.lda = L.k_pad;
+  }
+  op.inner = inner;
+  op.w = ws + L.off_w;
+  op.scale = scale;
+  op.bias = bvec;
+  op.rows = rows;
+  op.cols = cols;
+  op.out = out;
+  op.ldo = cols;
+  op.out_dtype = out_dtype;
+  op.relu = activation == AF2_ACTIVATION_RELU;
+  op.residual = residual;
+  op.prof = kProfLinear;
+  return linear_launch(ctx, op, stream);
+}
+
+}  // namespace af2

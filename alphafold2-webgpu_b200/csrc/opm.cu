@@ -1,0 +1,404 @@
+// opm.cu -- the outer-product mean on sm_100a.
+//
+// Reference: src/evoformer/outer-product-mean.ts:114-153 (LayerNorm over c_m),
+// :189-231 (left/right = mask * (LN(m) W + b), one GEMM with 2c columns),
+// :317-332 (pair counts), :350-417 (outer[i,j,a,b] = sum_s left[s,i,a]
+// right[s,j,b]), :433-486 (out = (outer W_o + b_o) / (eps + count)) and
+// :506-536 (residue blocks bounding the outer scratch); the in-model encoder
+// is src/evoformer/block.ts:1115-1246.  The reference's own CPU formulation is
+// test/outer-product-mean-reference.gpu.test.ts:22-79.
+//
+// Launches per call (weights prepared first):
+//   normalize  LayerNorm of every MSA row -> f16 [S*N][c_m]
+//   project    the shared tcgen05 GEMM: LN(m) [W_left | W_right], bias, times
+//              the row's mask, split into left and right, f16 [S][N][c]
+//   count      1 / (norm_eps + sum_s mask[s,i] mask[s,j]) per pair
+//   per residue block of output rows i:
+//     outer    tcgen05 GEMM over s with both operands read MN-major straight
+//              from the [S][N*c] layouts: a 128 x 256 tile is 4 residues i x
+//              8 residues j (x 32 x 32 channels); its epilogue writes each pair
+//              row (i, j) as 1024 contiguous f16 (index a*c + b, the order of
+//              W_o's rows), scaled by 2^-k with 2^k >= S to stay in f16 range
+//     output   the shared GEMM: outer W_o (column scales carry the 2^k back),
+//              + b_o, times the pair's 1/(eps + count), written or added
+// Blocking over residues bounds the outer scratch only: every output element
+// is computed the same way whatever the block, so results are bit-identical.
+#include <algorithm>
+#include <cmath>
+#include <string>
+
+#include "af2_device.cuh"
+#include "af2_internal.h"
+
+namespace af2 {
+namespace opm {
+
+constexpr int C = 32;  // outer channels c: the outer tile maps 32 channels to 32 TMEM lanes / columns
+
+// ---- LayerNorm over c_m (<= 256), one warp per MSA row ----
+template <typename MT>
+__global__ void norm_kernel(const MT *__restrict__ m, int64_t rows, int cm, int cmp, const float *__restrict__ gamma,
+                            const float *__restrict__ beta, float eps, __half *__restrict__ xn) {
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const MT *xr = m + row * cm;
+  float v[8];
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int ch = lane + 32 * i;
+    v[i] = ch < cm ? to_f32<MT>(xr[ch]) : 0.f;
+    s += v[i];
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(kFull, s, o);
+  const float mean = s / static_cast<float>(cm);
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int ch = lane + 32 * i;
+    const float d = ch < cm ? v[i] - mean : 0.f;
+    q += d * d;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(kFull, q, o);
+  const float rstd = rsqrtf(q / static_cast<float>(cm) + eps);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int ch = lane + 32 * i;
+    if (ch < cmp) xn[row * cmp + ch] = __float2half_rn(ch < cm ? (v[i] - mean) * rstd * gamma[ch] + beta[ch] : 0.f);
+  }
+}
+
+// ---- pair counts: rowscale[i*N + j] = 1 / (norm_eps + sum_s mask[s,i] mask[s,j]) ----
+__global__ void count_kernel(const float *__restrict__ mask, int s_count, int n, float norm_eps,
+                             float *__restrict__ rowscale) {
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= static_cast<int64_t>(n) * n) return;
+  const int i = static_cast<int>(idx / n), j = static_cast<int>(idx - static_cast<int64_t>(i) * n);
+  float cnt = 0.f;
+  for (int s = 0; s < s_count; ++s) cnt = fmaf(mask[static_cast<int64_t>(s) * n + i], mask[static_cast<int64_t>(s) * n + j], cnt);
+  rowscale[idx] = 1.f / (norm_eps + cnt);
+}
+
+// ---- outer products: outer[(i, j)][a*32 + b] = 2^-shift sum_s left[s][i][a] right[s][j][b] ----
+constexpr int OBM = 128, OBN = 256, OBK = 64, OSTAGES = 4, OTHREADS = 192;
+constexpr uint32_t OA_BYTES = OBM * 128, OB_BYTES = OBN * 128, OSTAGE = OA_BYTES + OB_BYTES;
+constexpr uint32_t OOFF_BAR = OSTAGES * OSTAGE;
+constexpr uint32_t OSMEM = OOFF_BAR + 256 + 1024;
+
+struct OuterArgs {
+  __half *outer;  // [(i - i_begin) * n + j][1024]
+  int n, i_begin, i_count, tiles_j, k_blocks, total_tiles;
+  float scale;
+  unsigned int *err;
+};
+
+__global__ void __launch_bounds__(OTHREADS, 1)
+    outer_kernel(const __grid_constant__ CUtensorMap lmap, const __grid_constant__ CUtensorMap rmap,
+                 const OuterArgs p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = align1024(smem_raw);
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bar0 = sbase + OOFF_BAR;
+  auto full = [&](int s) { return bar0 + 8u * s; };
+  auto empty = [&](int s) { return bar0 + 8u * (OSTAGES + s); };
+  auto acc_full = [&](int b) { return bar0 + 8u * (2 * OSTAGES + b); };
+  auto acc_empty = [&](int b) { return bar0 + 8u * (2 * OSTAGES + 2 + b); };
+  const uint32_t drain = bar0 + 8u * (2 * OSTAGES + 4);
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + OOFF_BAR + 128);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + OOFF_BAR + 136);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < OSTAGES; ++s) {
+      mbar_init(full(s), 1);
+      mbar_init(empty(s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(acc_full(b), 1);
+      mbar_init(acc_empty(b), 4);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_map(&lmap);
+      tma_prefetch_map(&rmap);
+      int it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < p.total_tiles; t += gridDim.x) {
+        const int ti = t / p.tiles_j, tj = t - ti * p.tiles_j;
+        const int i0 = p.i_begin + ti * 4, j0 = tj * 8;
+        for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
+          const int s = it % OSTAGES;
+          if (!mbar_wait(empty(s), ((it / OSTAGES) & 1) ^ 1, abort_flag, p.err, kErrWaitProducer)) {
+            ok = false;
+            break;
+          }
+          const uint32_t dst = sbase + s * OSTAGE;
+          mbar_arrive_expect_tx(full(s), OSTAGE);
+          // [64 s rows][64 (i, a) elements] boxes: 2 for the 128-wide A tile, 4 for the 256-wide B tile
+          for (int b = 0; b < 2; ++b) tma_load_3d(dst + b * 8192, &lmap, full(s), i0 * C + b * 64, kb * OBK, 0);
+          for (int b = 0; b < 4; ++b)
+            tma_load_3d(dst + OA_BYTES + b * 8192, &rmap, full(s), j0 * C + b * 64, kb * OBK, 0);
+        }
+      }
+      for (int j = std::max(0, it - OSTAGES); j < it; ++j) mbar_wait_drain(full(j % OSTAGES), (j / OSTAGES) & 1, p.err);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // both operands MN-major: 64-element MN blocks 8 KB apart, 8-row K groups 1 KB apart
+      constexpr uint32_t kIdesc = idesc_f16_f32(OBM, OBN) | (1u << 15) | (1u << 16);
+      const uint64_t a_desc = sdesc_mn_sw128(sbase, 8192, 1024);
+      int it = 0, tile_it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < p.total_tiles; t += gridDim.x, ++tile_it) {
+        const int buf = tile_it & 1;
+        if (!mbar_wait(acc_empty(buf), ((tile_it >> 1) & 1) ^ 1, abort_flag, p.err, kErrWaitMma)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + buf * OBN;
+        for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
+          const int s = it % OSTAGES;
+          if (!mbar_wait(full(s), (it / OSTAGES) & 1, abort_flag, p.err, kErrWaitMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t ad = desc_add(a_desc, s * OSTAGE), bd = desc_add(ad, OA_BYTES);
+          if (kb == 0)
+            mma_f16_first(d, ad, bd, kIdesc);
+          else
+            mma_f16_acc(d, ad, bd, kIdesc);
+#pragma unroll
+          for (int ks = 1; ks < OBK / 16; ++ks) mma_f16_acc(d, desc_add(ad, ks * 2048), desc_add(bd, ks * 2048), kIdesc);
+          mma_commit(empty(s));
+        }
+        if (ok) mma_commit(acc_full(buf));
+      }
+      mma_commit(drain);
+      mbar_wait_drain(drain, 0, p.err);
+    }
+    __syncwarp();
+  } else {
+    // TMEM lane = (i_local, a) with i_local = this warp's quarter, a = lane;
+    // columns = (j_local, b).  Each (pair, a) is 32 contiguous f16 of the row.
+    const int q = warp & 3;
+    int tile_it = 0;
+    for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x, ++tile_it) {
+      const int ti = t / p.tiles_j, tj = t - ti * p.tiles_j;
+      const int i = p.i_begin + ti * 4 + q, j0 = tj * 8;
+      const int buf = tile_it & 1;
+      if (!warp_wait(acc_full(buf), (tile_it >> 1) & 1, abort_flag, p.err, kErrWaitEpilogue)) break;
+      tc_fence_after();
+      const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * OBN;
+      const bool i_ok = i < p.i_begin + p.i_count;
+#pragma unroll 1
+      for (int jl = 0; jl < 8; ++jl) {
+        uint32_t v[32];
+        tmem_ld32(taddr + jl * 32, v);
+        tmem_ld_wait();
+        const int j = j0 + jl;
+        if (!i_ok || j >= p.n) continue;
+        uint32_t pk[16];
+#pragma unroll
+        for (int c = 0; c < 32; c += 2)
+          pk[c >> 1] = pack_half2(__uint_as_float(v[c]) * p.scale, __uint_as_float(v[c + 1]) * p.scale);
+        uint4 *dst = reinterpret_cast<uint4 *>(p.outer + (static_cast<int64_t>(i - p.i_begin) * p.n + j) * (C * C) +
+                                              lane * C);
+#pragma unroll
+        for (int w = 0; w < 4; ++w) dst[w] = make_uint4(pk[4 * w], pk[4 * w + 1], pk[4 * w + 2], pk[4 * w + 3]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acc_empty(buf));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace opm
+
+using namespace opm;
+
+OpmLayout opm_layout(int64_t s, int64_t n, int64_t cm, int64_t c, int64_t cz, int64_t row_block) {
+  OpmLayout L;
+  L.s = s;
+  L.n = n;
+  L.cm = cm;
+  L.c = c;
+  L.cz = cz;
+  L.cmp = align_up(cm, 64);
+  // Residue block: the outer scratch stays within 256 MiB unless asked otherwise; a multiple of 4.
+  int64_t rb = row_block > 0 ? row_block : std::max<int64_t>(4, (int64_t(256) << 20) / (n * c * c * 2));
+  rb = std::min<int64_t>(align_up(std::max<int64_t>(rb, 1), 4), align_up(n, 4));
+  L.block_rows = rb;
+  int k = 0;
+  while ((int64_t(1) << k) < s) ++k;
+  L.out_shift = k;
+  const int64_t lr_cols = linear_cols_pad(2 * c), o_cols = linear_cols_pad(cz), o_inner = align_up(c * c, 64);
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = off;
+    off = align_up(off + bytes, 256);
+    return at;
+  };
+  L.off_wlr = take((size_t)L.cmp * lr_cols * 2);
+  L.off_wlr_scale = take((size_t)lr_cols * 4);
+  L.off_wlr_bias = take((size_t)lr_cols * 4);
+  L.off_wo = take((size_t)o_inner * o_cols * 2);
+  L.off_wo_scale = take((size_t)o_cols * 4);
+  L.off_wo_bias = take((size_t)o_cols * 4);
+  L.off_ln = take((size_t)L.cmp * 2 * 4);
+  L.off_xn = take((size_t)s * n * L.cmp * 2);
+  L.off_left = take((size_t)s * n * c * 2);
+  L.off_right = take((size_t)s * n * c * 2);
+  L.off_rowscale = take((size_t)n * n * 4);
+  L.off_outer = take((size_t)rb * n * c * c * 2);
+  L.total = off;
+  return L;
+}
+
+af2_status opm_launch(af2_ctx *ctx, const OpmLayout &L, const void *m, int m_dtype, const float *mask,
+                      const float *packed, double ln_eps, double norm_eps, int residual, void *out, int out_dtype,
+                      void *workspace, cudaStream_t stream) {
+  uint8_t *ws = static_cast<uint8_t *>(workspace);
+  const int64_t s = L.s, n = L.n, cm = L.cm, c = L.c, cz = L.cz;
+  // packOuterProductMeanWeights order (outer-product-mean.ts:68-72).
+  const float *ln_w = packed, *ln_b = ln_w + cm, *lw = ln_b + cm, *lb = lw + cm * c, *rw = lb + c, *rb = rw + cm * c;
+  const float *ow = rb + c, *ob = ow + c * c * cz;
+  const int64_t lr_cols = linear_cols_pad(2 * c), o_cols = linear_cols_pad(cz), o_inner = align_up(c * c, 64);
+  float *wlr_scale = reinterpret_cast<float *>(ws + L.off_wlr_scale), *wlr_bias = reinterpret_cast<float *>(ws + L.off_wlr_bias);
+  float *wo_scale = reinterpret_cast<float *>(ws + L.off_wo_scale), *wo_bias = reinterpret_cast<float *>(ws + L.off_wo_bias);
+  float *ln = reinterpret_cast<float *>(ws + L.off_ln);
+  af2_status st;
+  // ---- weights ----
+  const af2_matrix left_m{AF2_WEIGHTS_F32, 0, lw, nullptr}, right_m{AF2_WEIGHTS_F32, 0, rw, nullptr};
+  const af2_matrix out_m{AF2_WEIGHTS_F32, 0, ow, nullptr};
+  if ((st = prepare_matrix(ctx, left_m, cm, c, L.cmp, c, 1.f, ws + L.off_wlr, wlr_scale, stream, 0, lr_cols)) != AF2_OK ||
+      (st = prepare_matrix(ctx, right_m, cm, c, L.cmp, c, 1.f, ws + L.off_wlr, wlr_scale, stream, c, lr_cols)) !=
+          AF2_OK ||
+      (st = pad_vector(ctx, lb, c, c, wlr_bias, stream)) != AF2_OK ||
+      (st = pad_vector(ctx, rb, c, lr_cols - c, wlr_bias + c, stream)) != AF2_OK ||
+      (st = prepare_matrix(ctx, out_m, c * c, cz, o_inner, o_cols, std::ldexp(1.f, L.out_shift), ws + L.off_wo,
+                           wo_scale, stream)) != AF2_OK ||
+      (st = pad_vector(ctx, ob, cz, o_cols, wo_bias, stream)) != AF2_OK ||
+      (st = pad_vector(ctx, ln_w, cm, L.cmp, ln, stream)) != AF2_OK ||
+      (st = pad_vector(ctx, ln_b, cm, L.cmp, ln + L.cmp, stream)) != AF2_OK)
+    return st;
+  if (lr_cols > 2 * c && (st = pad_vector(ctx, nullptr, 0, lr_cols - 2 * c, wlr_scale + 2 * c, stream)) != AF2_OK)
+    return st;
+  // ---- LayerNorm ----
+  const int64_t rows = s * n;
+  __half *xn = reinterpret_cast<__half *>(ws + L.off_xn);
+  {
+    const int warps = 8;
+    const unsigned blocks = (unsigned)((rows + warps - 1) / warps);
+    LaunchScope scope(ctx, stream, kProfOpmNormalize);
+    if (m_dtype == AF2_F32)
+      norm_kernel<float><<<blocks, warps * 32, 0, stream>>>(static_cast<const float *>(m), rows, (int)cm, (int)L.cmp,
+                                                            ln, ln + L.cmp, (float)ln_eps, xn);
+    else if (m_dtype == AF2_F16)
+      norm_kernel<__half><<<blocks, warps * 32, 0, stream>>>(static_cast<const __half *>(m), rows, (int)cm,
+                                                             (int)L.cmp, ln, ln + L.cmp, (float)ln_eps, xn);
+    else
+      norm_kernel<__nv_bfloat16><<<blocks, warps * 32, 0, stream>>>(static_cast<const __nv_bfloat16 *>(m), rows,
+                                                                    (int)cm, (int)L.cmp, ln, ln + L.cmp, (float)ln_eps,
+                                                                    xn);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "OPM normalisation");
+  }
+  // ---- left / right projection ----
+  {
+    LinearOperands op;
+    op.a = xn;
+    op.lda = L.cmp;
+    op.inner = L.cmp;
+    op.w = ws + L.off_wlr;
+    op.scale = wlr_scale;
+    op.bias = wlr_bias;
+    op.row_mask = mask;
+    op.rows = rows;
+    op.cols = 2 * c;
+    op.opm_projection = true;
+    op.left = ws + L.off_left;
+    op.right = ws + L.off_right;
+    op.prof = kProfOpmProject;
+    if ((st = linear_launch(ctx, op, stream)) != AF2_OK) return st;
+  }
+  // ---- pair counts ----
+  float *rowscale = reinterpret_cast<float *>(ws + L.off_rowscale);
+  {
+    LaunchScope scope(ctx, stream, kProfOpmCount);
+    count_kernel<<<(unsigned)((n * n + 255) / 256), 256, 0, stream>>>(mask, (int)s, (int)n, (float)norm_eps, rowscale);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "OPM pair counts");
+  }
+  // ---- outer products and output projection, block by block ----
+  CUtensorMap lmap, rmap;
+  if (!encode_map_3d(&lmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, ws + L.off_left, n * c, s, 1, n * c * 2,
+                     (uint64_t)s * n * c * 2, 64, 64, 1, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_map_3d(&rmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, ws + L.off_right, n * c, s, 1, n * c * 2,
+                     (uint64_t)s * n * c * 2, 64, 64, 1, CU_TENSOR_MAP_SWIZZLE_128B))
+    return fail(ctx, AF2_ERR_CUDA, "cuTensorMapEncodeTiled failed for the OPM operands");
+  cudaError_t e = cudaFuncSetAttribute(outer_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, OSMEM);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "outer kernel attributes");
+  __half *outer = reinterpret_cast<__half *>(ws + L.off_outer);
+  const size_t ob_bytes = out_dtype == AF2_F32 ? 4 : 2;
+  for (int64_t i0 = 0; i0 < n; i0 += L.block_rows) {
+    const int64_t ic = std::min<int64_t>(L.block_rows, n - i0);
+    OuterArgs a{};
+    a.outer = outer;
+    a.n = (int)n;
+    a.i_begin = (int)i0;
+    a.i_count = (int)ic;
+    a.tiles_j = (int)((n + 7) / 8);
+    a.k_blocks = (int)((s + OBK - 1) / OBK);
+    a.total_tiles = (int)((ic + 3) / 4) * a.tiles_j;
+    a.scale = std::ldexp(1.f, -L.out_shift);
+    a.err = ctx->err_word;
+    {
+      LaunchScope scope(ctx, stream, kProfOpmOuter);
+      outer_kernel<<<std::min(a.total_tiles, ctx->sm_count), OTHREADS, OSMEM, stream>>>(lmap, rmap, a);
+      e = cudaGetLastError();
+      if (e != cudaSuccess) return cuda_fail(ctx, e, "outer kernel launch");
+    }
+    LinearOperands op;
+    op.a = outer;
+    op.lda = c * c;
+    op.inner = c * c;
+    op.w = ws + L.off_wo;
+    op.scale = wo_scale;
+    op.bias = wo_bias;
+    op.row_scale = rowscale + i0 * n;
+    op.rows = ic * n;
+    op.cols = cz;
+    op.out = static_cast<uint8_t *>(out) + (size_t)i0 * n * cz * ob_bytes;
+    op.ldo = cz;
+    op.out_dtype = out_dtype;
+    op.residual = residual;
+    op.prof = kProfOpmOutput;
+    if ((st = linear_launch(ctx, op, stream)) != AF2_OK) return st;
+  }
+  return AF2_OK;
+}
+
+}  // namespace af2

@@ -528,6 +528,7 @@ __global__ void __launch_bounds__(CT_THREADS, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t kIdesc = idesc_f16_f32(CT_BM, CT_BN);
+      const uint64_t a_desc = sdesc_k_sw128(sbase);  // stage s: + s * CT_STAGE_BYTES; B follows A
       int it = 0, tile_it = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x, ++tile_it) {
@@ -547,10 +548,13 @@ __global__ void __launch_bounds__(CT_THREADS, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t as = sbase + s * CT_STAGE_BYTES, bs = as + CT_A_BYTES;
+          const uint64_t ad = desc_add(a_desc, s * CT_STAGE_BYTES), bd = desc_add(ad, CT_A_BYTES);
+          if (kb == 0)
+            mma_f16_first(d, ad, bd, kIdesc);
+          else
+            mma_f16_acc(d, ad, bd, kIdesc);
 #pragma unroll
-          for (int ks = 0; ks < CT_BK / 16; ++ks)
-            mma_f16(d, sdesc_k_sw128(as + ks * 32), sdesc_k_sw128(bs + ks * 32), kIdesc, (kb | ks) != 0);
+          for (int ks = 1; ks < CT_BK / 16; ++ks) mma_f16_acc(d, desc_add(ad, ks * 32), desc_add(bd, ks * 32), kIdesc);
           mma_commit(empty(s));
         }
         if (ok) mma_commit(acc_full(buf));

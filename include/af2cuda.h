@@ -282,6 +282,77 @@ AF2_API af2_status af2_transition(af2_ctx *ctx, const af2_transition_shape *shap
                                   const af2_transition_options *options, void *out, int out_dtype, void *workspace,
                                   void *stream);
 
+/* ---- outer-product mean -------------------------------------------------- */
+
+/* OuterProductMeanInput's dimensions, src/evoformer/outer-product-mean.ts:21-34. */
+typedef struct af2_opm_shape {
+    int64_t sequences; /* S */
+    int64_t length;    /* N residues */
+    int64_t c_m;
+    int64_t c_outer;   /* c */
+    int64_t c_z;
+} af2_opm_shape;
+
+typedef struct af2_opm_options {
+    double layer_norm_epsilon;    /* layerNormEpsilon: 0 = 1e-5 */
+    double normalization_epsilon; /* normalizationEpsilon: 0 = 1e-3 */
+    /* rowBlockResidues: output residues per block (0 = automatic).  It bounds
+     * the outer-product scratch only; results are bit-identical for every value. */
+    int32_t row_block_residues;
+    /* 1: out += OPM(m) (encodeOuterProductMean with residualTarget). */
+    int32_t residual;
+} af2_opm_options;
+
+/* Length of packOuterProductMeanWeights(input).data (outer-product-mean.ts:68-80). */
+AF2_API int64_t af2_opm_weight_count(const af2_opm_shape *shape);
+
+/* validate (outer-product-mean.ts:45-65) plus the kernels' limits (c_outer = 32,
+ * c_m <= 256, c_z <= 4096); no device needed. */
+AF2_API af2_status af2_opm_check(const af2_opm_shape *shape, int64_t weight_count, char *message, size_t capacity);
+
+AF2_API af2_status af2_opm_workspace_bytes(const af2_opm_shape *shape, const af2_opm_options *options,
+                                           uint64_t *bytes);
+
+/*
+ * Host form of OuterProductMeanGpu.run (outer-product-mean.ts:538-647): m
+ * [S, N, c_m] of io_dtype, mask [S, N] f32, packed_weights f32 in the order of
+ * packOuterProductMeanWeights; out [N, N, c_z] of io_dtype.
+ */
+AF2_API af2_status af2_outer_product_mean_host(af2_ctx *ctx, const af2_opm_shape *shape, const void *m,
+                                               const float *mask, const float *packed_weights, int64_t weight_count,
+                                               const af2_opm_options *options, int io_dtype, void *out,
+                                               af2_op_stats *stats);
+
+/* Device form: encodeOuterProductMean (src/evoformer/block.ts:1115-1246).  All
+ * pointers on the device; workspace NULL = context-owned. */
+AF2_API af2_status af2_outer_product_mean(af2_ctx *ctx, const af2_opm_shape *shape, const void *m, int m_dtype,
+                                          const float *mask, const float *packed_weights, int64_t weight_count,
+                                          const af2_opm_options *options, void *out, int out_dtype, void *workspace,
+                                          void *stream);
+
+/* ---- the shared dense projection ----------------------------------------- */
+
+/* createLinearShader (transition.ts:91-138): out (=, +=) act(A W + b). */
+typedef struct af2_linear_shape {
+    int64_t rows;
+    int64_t inner;
+    int64_t columns;
+} af2_linear_shape;
+
+typedef enum af2_activation { AF2_ACTIVATION_NONE = 0, AF2_ACTIVATION_RELU = 1 } af2_activation;
+
+AF2_API af2_status af2_linear_workspace_bytes(const af2_linear_shape *shape, int a_dtype, uint64_t *bytes);
+
+/*
+ * Device form: A [rows, inner] of a_dtype, weight [inner, columns] ([in, out],
+ * f32 or q8), bias [columns] f32 or NULL, out [rows, columns] of out_dtype;
+ * residual = 1 adds into out.  Operands are multiplied as f16 with f32
+ * accumulation.  workspace NULL = context-owned.
+ */
+AF2_API af2_status af2_linear(af2_ctx *ctx, const af2_linear_shape *shape, const void *a, int a_dtype,
+                              const af2_matrix *weight, const float *bias, int activation, int residual, void *out,
+                              int out_dtype, void *workspace, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -167,3 +167,42 @@ def test_transition_workspace_is_small():
     small = af2cuda.transition_workspace_bytes(65536, 128, 512)
     big = af2cuda.transition_workspace_bytes(4 * 65536, 128, 512)
     assert small == big and small < 32 << 20
+
+
+def test_opm_weight_count_and_validation():
+    shape = _lib.OpmShape(512, 256, 256, 32, 128)
+    count = af2cuda.opm_weight_count(512, 256, 256, 32, 128)
+    assert count == 2 * 256 + 2 * (256 * 32 + 32) + 32 * 32 * 128 + 128
+    msg = ctypes.create_string_buffer(256)
+    assert _lib.lib().af2_opm_check(ctypes.byref(shape), count, msg, 256) == 0
+    assert _lib.lib().af2_opm_check(ctypes.byref(shape), count - 1, msg, 256) == _lib.AF2_ERR_INVALID_ARGUMENT
+    assert msg.value.decode() == f"packed weights have {count - 1} values; expected {count}"
+    bad = _lib.OpmShape(0, 256, 256, 32, 128)
+    assert _lib.lib().af2_opm_check(ctypes.byref(bad), count, msg, 256) == _lib.AF2_ERR_INVALID_ARGUMENT
+    c16 = _lib.OpmShape(512, 256, 256, 16, 128)
+    n16 = af2cuda.opm_weight_count(512, 256, 256, 16, 128)
+    assert _lib.lib().af2_opm_check(ctypes.byref(c16), n16, msg, 256) == _lib.AF2_ERR_UNSUPPORTED
+
+
+def test_opm_python_validation_and_packing():
+    rng = np.random.default_rng(0)
+    s, n, cm, c, cz = 2, 3, 4, 32, 5
+    w = af2cuda.OuterProductMeanWeights(*(rng.standard_normal(k).astype(np.float32)
+                                          for k in (cm, cm, cm * c, c, cm * c, c, c * c * cz, cz)))
+    inp = af2cuda.OuterProductMeanInput(rng.standard_normal(s * n * cm).astype(np.float32),
+                                        np.ones(s * n, np.float32), s, n, cm, c, cz, w)
+    af2cuda.validate_outer_product_mean_input(inp)
+    data, offsets = af2cuda.pack_outer_product_mean_weights(inp)
+    assert data.size == af2cuda.opm_weight_count(s, n, cm, c, cz)
+    assert offsets[6] == 2 * cm + 2 * (cm * c + c) and np.array_equal(data[offsets[6]:offsets[7]], w.outputWeight)
+    with pytest.raises(af2cuda.RangeError, match="mask has 5 values; expected 6"):
+        af2cuda.validate_outer_product_mean_input(
+            af2cuda.OuterProductMeanInput(inp.activations, np.ones(5, np.float32), s, n, cm, c, cz, w))
+
+
+def test_opm_workspace_blocks_bound_the_outer_scratch():
+    whole = af2cuda.opm_workspace_bytes(512, 768, 256, 32, 128)
+    b4 = af2cuda.opm_workspace_bytes(512, 768, 256, 32, 128, row_block=4)
+    b8 = af2cuda.opm_workspace_bytes(512, 768, 256, 32, 128, row_block=8)
+    assert b4 < b8 <= whole
+    assert b8 - b4 == 4 * 768 * 32 * 32 * 2  # four more residue rows of f16 outer products
