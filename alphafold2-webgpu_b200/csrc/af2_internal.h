@@ -171,6 +171,21 @@ inline int64_t linear_cols_pad(int64_t cols) { return align_up(cols, linear_tile
 af2_status prepare_matrix(af2_ctx *ctx, const af2_matrix &w, int64_t inner, int64_t cols, int64_t inner_pad,
                           int64_t cols_pad, float extra_scale, void *out, float *scale_out, cudaStream_t stream,
                           int64_t row0 = 0, int64_t rows_total = 0);
+// Up to 8 zero-padded vector copies done by one launch.
+struct VectorSegments {
+  const float *src[8];
+  float *dst[8];
+  int n[8], n_pad[8];
+  int count;
+  void add(const float *s, int64_t len, int64_t len_pad, float *d) {
+    src[count] = s;
+    dst[count] = d;
+    n[count] = static_cast<int>(len);
+    n_pad[count] = static_cast<int>(len_pad);
+    ++count;
+  }
+};
+af2_status pad_vectors(af2_ctx *ctx, const VectorSegments &v, cudaStream_t stream);
 af2_status pad_vector(af2_ctx *ctx, const float *src, int64_t n, int64_t n_pad, float *dst, cudaStream_t stream);
 af2_status convert_rows_f16(af2_ctx *ctx, const void *src, int dtype, int64_t rows, int64_t inner, int64_t inner_pad,
                             void *dst, cudaStream_t stream);

@@ -37,10 +37,27 @@ struct LinearArgs {
   int64_t rows, ldo;
   int cols, half_cols, k_blocks, tiles_m, tiles_n, total_tiles, bn;
   int relu, residual;
+  int vector_out;  // out rows are 16-byte aligned: whole 32-column chunks use vector access
   unsigned int *err;
 };
 
 enum { kModeLinear = 0, kModeOpmProjection = 1 };
+
+template <typename OT>
+__device__ __forceinline__ uint32_t pack2_t(float lo, float hi);
+template <>
+__device__ __forceinline__ uint32_t pack2_t<__half>(float lo, float hi) {
+  return pack_half2(lo, hi);
+}
+template <>
+__device__ __forceinline__ uint32_t pack2_t<__nv_bfloat16>(float lo, float hi) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t *>(&h);
+}
+template <>
+__device__ __forceinline__ uint32_t pack2_t<float>(float, float) {
+  return 0;
+}
 
 template <typename OT, int MODE>
 __global__ void __launch_bounds__(THREADS, 1)
@@ -175,25 +192,61 @@ __global__ void __launch_bounds__(THREADS, 1)
           y[4 * i4 + 3] = fmaf(__uint_as_float(v[4 * i4 + 3]), s4.w, b4.w);
         }
         if (MODE == kModeOpmProjection) {
-          // columns [0, half) -> left, [half, 2 half) -> right, both scaled by the mask
-          const int half = p.half_cols;
+          // columns [0, half) -> left, [half, 2 half) -> right, both scaled by the mask;
+          // half is 32, so a chunk is one whole left or right row: 4 x 16-byte stores.
+          __half *dst = (c0 < p.half_cols ? p.left : p.right) + m * p.half_cols;
+          uint32_t pk[16];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int col = c0 + i;
-            if (col < p.cols) {
-              __half *dst = col < half ? p.left + m * half + col : p.right + m * half + (col - half);
-              *dst = __float2half_rn(y[i] * rs);
-            }
-          }
+          for (int i = 0; i < 16; ++i) pk[i] = pack_half2(y[2 * i] * rs, y[2 * i + 1] * rs);
+          uint4 *d4 = reinterpret_cast<uint4 *>(dst);
+#pragma unroll
+          for (int w = 0; w < 4; ++w) d4[w] = make_uint4(pk[4 * w], pk[4 * w + 1], pk[4 * w + 2], pk[4 * w + 3]);
         } else {
           OT *orow = static_cast<OT *>(p.out) + m * p.ldo;
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int col = c0 + i;
-            if (col < p.cols) {
-              float val = p.relu ? fmaxf(y[i], 0.f) : y[i];
-              val *= rs;
-              orow[col] = from_f32<OT>(p.residual ? to_f32<OT>(orow[col]) + val : val);
+          for (int i = 0; i < 32; ++i) y[i] = (p.relu ? fmaxf(y[i], 0.f) : y[i]) * rs;
+          if (p.vector_out && c0 + 32 <= p.cols) {
+            // 32 contiguous outputs of this row: 16-byte loads (residual) and stores
+            if constexpr (sizeof(OT) == 4) {
+              float4 *o4 = reinterpret_cast<float4 *>(orow + c0);
+#pragma unroll
+              for (int w = 0; w < 8; ++w) {
+                float4 val = make_float4(y[4 * w], y[4 * w + 1], y[4 * w + 2], y[4 * w + 3]);
+                if (p.residual) {
+                  const float4 r = o4[w];
+                  val.x += r.x;
+                  val.y += r.y;
+                  val.z += r.z;
+                  val.w += r.w;
+                }
+                o4[w] = val;
+              }
+            } else {
+              uint4 *o4 = reinterpret_cast<uint4 *>(orow + c0);
+#pragma unroll
+              for (int w = 0; w < 4; ++w) {
+                float v8[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) v8[i] = y[8 * w + i];
+                if (p.residual) {
+                  const uint4 r = o4[w];
+                  const uint32_t rw[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+                  for (int i = 0; i < 4; ++i) {
+                    const float2 f = unpack2<OT>(rw[i]);
+                    v8[2 * i] += f.x;
+                    v8[2 * i + 1] += f.y;
+                  }
+                }
+                o4[w] = make_uint4(pack2_t<OT>(v8[0], v8[1]), pack2_t<OT>(v8[2], v8[3]), pack2_t<OT>(v8[4], v8[5]),
+                                   pack2_t<OT>(v8[6], v8[7]));
+              }
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const int col = c0 + i;
+              if (col < p.cols) orow[col] = from_f32<OT>(p.residual ? to_f32<OT>(orow[col]) + y[i] : y[i]);
             }
           }
         }
@@ -221,7 +274,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 // of two bringing the column's largest magnitude into [0.5, 1).
 // ---------------------------------------------------------------------------
 constexpr int PREP_THREADS = 1024;
-constexpr int kPrepBatch = 16;
+constexpr int kPrepBatch = 32;  // K values per thread held in registers: inner <= 1024 is read once
 
 struct MatrixDev {
   int format, block;
@@ -329,10 +382,11 @@ __global__ void __launch_bounds__(PREP_THREADS)
                                 scale_out);
 }
 
-// dst[i] = i < n ? src[i] : 0 for i < n_pad (src may be NULL: zeros).
-__global__ void pad_vector_kernel(const float *__restrict__ src, int n, int n_pad, float *__restrict__ dst) {
+// Segment k: dst[i] = i < n ? src[i] : 0 for i < n_pad (src may be NULL: zeros).
+__global__ void pad_vectors_kernel(VectorSegments v) {
+  const int k = blockIdx.y;
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < n_pad) dst[i] = (src && i < n) ? src[i] : 0.f;
+  if (k < v.count && i < v.n_pad[k]) v.dst[k][i] = (v.src[k] && i < v.n[k]) ? v.src[k][i] : 0.f;
 }
 
 // f32 / 16-bit rows [rows][inner] -> f16 rows [rows][inner_pad] (zero padded).
@@ -369,11 +423,19 @@ af2_status prepare_matrix(af2_ctx *ctx, const af2_matrix &w, int64_t inner, int6
   return e == cudaSuccess ? AF2_OK : cuda_fail(ctx, e, "weight preparation");
 }
 
-af2_status pad_vector(af2_ctx *ctx, const float *src, int64_t n, int64_t n_pad, float *dst, cudaStream_t stream) {
+af2_status pad_vectors(af2_ctx *ctx, const VectorSegments &v, cudaStream_t stream) {
+  int widest = 1;
+  for (int k = 0; k < v.count; ++k) widest = std::max(widest, v.n_pad[k]);
   LaunchScope scope(ctx, stream, kProfPrepare);
-  pad_vector_kernel<<<(unsigned)((n_pad + 255) / 256), 256, 0, stream>>>(src, (int)n, (int)n_pad, dst);
+  pad_vectors_kernel<<<dim3((unsigned)((widest + 255) / 256), (unsigned)v.count), 256, 0, stream>>>(v);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? AF2_OK : cuda_fail(ctx, e, "vector preparation");
+}
+
+af2_status pad_vector(af2_ctx *ctx, const float *src, int64_t n, int64_t n_pad, float *dst, cudaStream_t stream) {
+  VectorSegments v{};
+  v.add(src, n, n_pad, dst);
+  return pad_vectors(ctx, v, stream);
 }
 
 af2_status convert_rows_f16(af2_ctx *ctx, const void *src, int dtype, int64_t rows, int64_t inner, int64_t inner_pad,
@@ -443,6 +505,10 @@ af2_status linear_launch(af2_ctx *ctx, const LinearOperands &op, cudaStream_t st
   a.bn = bn;
   a.relu = op.relu;
   a.residual = op.residual;
+  {
+    const size_t ob = op.out_dtype == AF2_F32 ? 4 : 2;
+    a.vector_out = !op.opm_projection && reinterpret_cast<uintptr_t>(op.out) % 16 == 0 && (op.ldo * ob) % 16 == 0;
+  }
   a.err = ctx->err_word;
   if (op.opm_projection) return launch_linear_t<__half, kModeOpmProjection>(ctx, amap, bmap, a, op.prof, stream);
   if (op.out_dtype == AF2_F16) return launch_linear_t<__half, kModeLinear>(ctx, amap, bmap, a, op.prof, stream);

@@ -36,7 +36,10 @@ namespace opm {
 constexpr int C = 32;  // outer channels c: the outer tile maps 32 channels to 32 TMEM lanes / columns
 
 // ---- LayerNorm over c_m (<= 256), one warp per MSA row ----
-template <typename MT>
+// VEC: c_m = 256 with 16-byte rows: each lane holds 8 contiguous channels
+// (two float4 or one 16-byte load of 16-bit values) and writes them back as one
+// 16-byte store of f16.  Otherwise lanes stride the channels one by one.
+template <typename MT, bool VEC>
 __global__ void norm_kernel(const MT *__restrict__ m, int64_t rows, int cm, int cmp, const float *__restrict__ gamma,
                             const float *__restrict__ beta, float eps, __half *__restrict__ xn) {
   const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -44,42 +47,86 @@ __global__ void norm_kernel(const MT *__restrict__ m, int64_t rows, int cm, int 
   if (row >= rows) return;
   const MT *xr = m + row * cm;
   float v[8];
+  if (VEC) {
+    if constexpr (sizeof(MT) == 4) {
+      const float4 a = reinterpret_cast<const float4 *>(xr)[2 * lane], b = reinterpret_cast<const float4 *>(xr)[2 * lane + 1];
+      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    } else {
+      unpack8<MT>(reinterpret_cast<const uint4 *>(xr)[lane], v);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int ch = lane + 32 * i;
+      v[i] = ch < cm ? to_f32<MT>(xr[ch]) : 0.f;
+    }
+  }
   float s = 0.f;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int ch = lane + 32 * i;
-    v[i] = ch < cm ? to_f32<MT>(xr[ch]) : 0.f;
-    s += v[i];
-  }
+  for (int i = 0; i < 8; ++i) s += v[i];
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(kFull, s, o);
   const float mean = s / static_cast<float>(cm);
   float q = 0.f;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    const int ch = lane + 32 * i;
+    const int ch = VEC ? lane * 8 + i : lane + 32 * i;
     const float d = ch < cm ? v[i] - mean : 0.f;
     q += d * d;
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(kFull, q, o);
   const float rstd = rsqrtf(q / static_cast<float>(cm) + eps);
+  if (VEC) {
+    const float4 g0 = reinterpret_cast<const float4 *>(gamma)[2 * lane], g1 = reinterpret_cast<const float4 *>(gamma)[2 * lane + 1];
+    const float4 b0 = reinterpret_cast<const float4 *>(beta)[2 * lane], b1 = reinterpret_cast<const float4 *>(beta)[2 * lane + 1];
+    const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+    const float b[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+    uint32_t pk[4];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int ch = lane + 32 * i;
-    if (ch < cmp) xn[row * cmp + ch] = __float2half_rn(ch < cm ? (v[i] - mean) * rstd * gamma[ch] + beta[ch] : 0.f);
+    for (int i = 0; i < 4; ++i)
+      pk[i] = pack_half2((v[2 * i] - mean) * rstd * g[2 * i] + b[2 * i],
+                         (v[2 * i + 1] - mean) * rstd * g[2 * i + 1] + b[2 * i + 1]);
+    reinterpret_cast<uint4 *>(xn + row * cmp)[lane] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int ch = lane + 32 * i;
+      if (ch < cmp)
+        xn[row * cmp + ch] = __float2half_rn(ch < cm ? (v[i] - mean) * rstd * gamma[ch] + beta[ch] : 0.f);
+    }
   }
 }
 
 // ---- pair counts: rowscale[i*N + j] = 1 / (norm_eps + sum_s mask[s,i] mask[s,j]) ----
-__global__ void count_kernel(const float *__restrict__ mask, int s_count, int n, float norm_eps,
-                             float *__restrict__ rowscale) {
-  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (idx >= static_cast<int64_t>(n) * n) return;
-  const int i = static_cast<int>(idx / n), j = static_cast<int>(idx - static_cast<int64_t>(i) * n);
-  float cnt = 0.f;
-  for (int s = 0; s < s_count; ++s) cnt = fmaf(mask[static_cast<int64_t>(s) * n + i], mask[static_cast<int64_t>(s) * n + j], cnt);
-  rowscale[idx] = 1.f / (norm_eps + cnt);
+// A 32 x 32 block of pairs per CTA; 64 MSA rows of both residue columns at a
+// time through shared memory; every count sums s in order.
+__global__ void __launch_bounds__(256) count_kernel(const float *__restrict__ mask, int s_count, int n,
+                                                    float norm_eps, float *__restrict__ rowscale) {
+  __shared__ float mi[64][33], mj[64][33];
+  const int i0 = blockIdx.y * 32, j0 = blockIdx.x * 32;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int s0 = 0; s0 < s_count; s0 += 64) {
+    for (int r = ty; r < 64; r += 8) {
+      const int64_t s = s0 + r;
+      mi[r][tx] = (s < s_count && i0 + tx < n) ? mask[s * n + i0 + tx] : 0.f;
+      mj[r][tx] = (s < s_count && j0 + tx < n) ? mask[s * n + j0 + tx] : 0.f;
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int r = 0; r < 64; ++r) {
+      const float b = mj[r][tx];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) acc[k] = fmaf(mi[r][ty + 8 * k], b, acc[k]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int i = i0 + ty + 8 * k, j = j0 + tx;
+    if (i < n && j < n) rowscale[static_cast<int64_t>(i) * n + j] = 1.f / (norm_eps + acc[k]);
+  }
 }
 
 // ---- outer products: outer[(i, j)][a*32 + b] = 2^-shift sum_s left[s][i][a] right[s][j][b] ----
@@ -293,18 +340,19 @@ af2_status opm_launch(af2_ctx *ctx, const OpmLayout &L, const void *m, int m_dty
   // ---- weights ----
   const af2_matrix left_m{AF2_WEIGHTS_F32, 0, lw, nullptr}, right_m{AF2_WEIGHTS_F32, 0, rw, nullptr};
   const af2_matrix out_m{AF2_WEIGHTS_F32, 0, ow, nullptr};
+  VectorSegments vs{};
+  vs.add(lb, c, c, wlr_bias);
+  vs.add(rb, c, lr_cols - c, wlr_bias + c);
+  vs.add(ob, cz, o_cols, wo_bias);
+  vs.add(ln_w, cm, L.cmp, ln);
+  vs.add(ln_b, cm, L.cmp, ln + L.cmp);
+  if (lr_cols > 2 * c) vs.add(nullptr, 0, lr_cols - 2 * c, wlr_scale + 2 * c);
   if ((st = prepare_matrix(ctx, left_m, cm, c, L.cmp, c, 1.f, ws + L.off_wlr, wlr_scale, stream, 0, lr_cols)) != AF2_OK ||
       (st = prepare_matrix(ctx, right_m, cm, c, L.cmp, c, 1.f, ws + L.off_wlr, wlr_scale, stream, c, lr_cols)) !=
           AF2_OK ||
-      (st = pad_vector(ctx, lb, c, c, wlr_bias, stream)) != AF2_OK ||
-      (st = pad_vector(ctx, rb, c, lr_cols - c, wlr_bias + c, stream)) != AF2_OK ||
       (st = prepare_matrix(ctx, out_m, c * c, cz, o_inner, o_cols, std::ldexp(1.f, L.out_shift), ws + L.off_wo,
                            wo_scale, stream)) != AF2_OK ||
-      (st = pad_vector(ctx, ob, cz, o_cols, wo_bias, stream)) != AF2_OK ||
-      (st = pad_vector(ctx, ln_w, cm, L.cmp, ln, stream)) != AF2_OK ||
-      (st = pad_vector(ctx, ln_b, cm, L.cmp, ln + L.cmp, stream)) != AF2_OK)
-    return st;
-  if (lr_cols > 2 * c && (st = pad_vector(ctx, nullptr, 0, lr_cols - 2 * c, wlr_scale + 2 * c, stream)) != AF2_OK)
+      (st = pad_vectors(ctx, vs, stream)) != AF2_OK)
     return st;
   // ---- LayerNorm ----
   const int64_t rows = s * n;
@@ -313,16 +361,23 @@ af2_status opm_launch(af2_ctx *ctx, const OpmLayout &L, const void *m, int m_dty
     const int warps = 8;
     const unsigned blocks = (unsigned)((rows + warps - 1) / warps);
     LaunchScope scope(ctx, stream, kProfOpmNormalize);
+    const bool vec = cm == 256 && reinterpret_cast<uintptr_t>(m) % 16 == 0;
+    auto run = [&](auto tag) {
+      using MT = decltype(tag);
+      const MT *mp = static_cast<const MT *>(m);
+      if (vec)
+        norm_kernel<MT, true><<<blocks, warps * 32, 0, stream>>>(mp, rows, (int)cm, (int)L.cmp, ln, ln + L.cmp,
+                                                                 (float)ln_eps, xn);
+      else
+        norm_kernel<MT, false><<<blocks, warps * 32, 0, stream>>>(mp, rows, (int)cm, (int)L.cmp, ln, ln + L.cmp,
+                                                                  (float)ln_eps, xn);
+    };
     if (m_dtype == AF2_F32)
-      norm_kernel<float><<<blocks, warps * 32, 0, stream>>>(static_cast<const float *>(m), rows, (int)cm, (int)L.cmp,
-                                                            ln, ln + L.cmp, (float)ln_eps, xn);
+      run(float{});
     else if (m_dtype == AF2_F16)
-      norm_kernel<__half><<<blocks, warps * 32, 0, stream>>>(static_cast<const __half *>(m), rows, (int)cm,
-                                                             (int)L.cmp, ln, ln + L.cmp, (float)ln_eps, xn);
+      run(__half{});
     else
-      norm_kernel<__nv_bfloat16><<<blocks, warps * 32, 0, stream>>>(static_cast<const __nv_bfloat16 *>(m), rows,
-                                                                    (int)cm, (int)L.cmp, ln, ln + L.cmp, (float)ln_eps,
-                                                                    xn);
+      run(__nv_bfloat16{});
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(ctx, e, "OPM normalisation");
   }
@@ -348,7 +403,8 @@ af2_status opm_launch(af2_ctx *ctx, const OpmLayout &L, const void *m, int m_dty
   float *rowscale = reinterpret_cast<float *>(ws + L.off_rowscale);
   {
     LaunchScope scope(ctx, stream, kProfOpmCount);
-    count_kernel<<<(unsigned)((n * n + 255) / 256), 256, 0, stream>>>(mask, (int)s, (int)n, (float)norm_eps, rowscale);
+    const dim3 grid((unsigned)((n + 31) / 32), (unsigned)((n + 31) / 32));
+    count_kernel<<<grid, 256, 0, stream>>>(mask, (int)s, (int)n, (float)norm_eps, rowscale);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(ctx, e, "OPM pair counts");
   }
