@@ -105,21 +105,32 @@ class LaunchScope {
 
 struct TriangleLayout {
   int64_t n = 0, cz = 0, ch = 0;
+  int64_t rows = 0;         // pair rows held here (n, or n / ranks when the pair is sharded by rows)
   int64_t block_rows = 0;   // output rows per block
-  int64_t kp = 0;           // row pitch (elements) of the projected operands
+  int64_t kp = 0;           // k pitch (elements) of the projected operands
   int64_t jp = 0;           // row pitch (elements) of the contracted block
-  int64_t ab_hs = 0;        // channel pitch (elements) of the projected operands
+  int64_t ab_rs = 0;        // row pitch (elements) of the projected operands [row][h][k]
   int64_t x_hs = 0;         // channel pitch (elements) of the contracted block (full block)
   bool pad_z = false;       // z is re-laid as f16 [P][128] before the kernels
   size_t off_w16 = 0, off_vec = 0, off_z16 = 0, off_a = 0, off_b = 0, off_x = 0, total = 0;
 };
 
-TriangleLayout triangle_layout(int64_t n, int64_t cz, int64_t ch, int64_t block_rows, int z_dtype);
+// rows < n: the pair rows [rank * rows, (rank + 1) * rows) of a row-sharded pair.
+TriangleLayout triangle_layout(int64_t n, int64_t cz, int64_t ch, int64_t block_rows, int z_dtype, int64_t rows = 0);
+
+// How the projected b operand becomes whole on a row-sharded pair: this rank's
+// rows are written at row b_row0 of the full operand, then exchanged in place.
+struct TriangleExchange {
+  int64_t b_row0 = 0;
+  // all-gathers `bytes_per_rank` bytes per rank in place into `full` on `stream`
+  af2_status (*all_gather)(af2_ctx *ctx, void *full, size_t bytes_per_rank, cudaStream_t stream) = nullptr;
+};
 
 // Launches the whole op on `stream`; the workspace holds TriangleLayout::total bytes.
 af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L, const void *z, int z_dtype,
                            const float *mask, const float *packed, double eps, int residual, void *out,
-                           int out_dtype, void *workspace, cudaStream_t stream);
+                           int out_dtype, void *workspace, cudaStream_t stream,
+                           const TriangleExchange *exchange = nullptr);
 
 // ---- transition (transition.cu) ----
 

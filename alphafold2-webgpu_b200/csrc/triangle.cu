@@ -140,8 +140,7 @@ constexpr uint32_t PJ_SMEM = PJ_OFF_BAR + 256 + 1024;
 struct ProjectArgs {
   const float *mask;
   int64_t mask_rs, mask_ks;  // mask of tile row r, pair k: mask[r * mask_rs + k * mask_ks]
-  __half *a_out, *b_out;     // [128][rows][kp]
-  int64_t out_hs, out_rs;
+  int b_row0;                // row of the full b operand this launch's row 0 lands on
   const __half *w16;
   const float *vec;
   int n, cz, tiles_k, total_tiles;
@@ -423,8 +422,8 @@ __global__ void __launch_bounds__(PJ_THREADS, 1)
         if (!mbar_wait(out_full, it & 1, abort_flag, p.err, kErrWaitEpilogue)) {
           it = -1;
         } else {
-          tma_store_3d(&amap, sbase + PJ_OFF_OUT, k0, r, 0);
-          tma_store_3d(&bmap, sbase + PJ_OFF_OUT + PJ_OUT_BYTES, k0, r, 0);
+          tma_store_3d(&amap, sbase + PJ_OFF_OUT, k0, 0, r);
+          tma_store_3d(&bmap, sbase + PJ_OFF_OUT + PJ_OUT_BYTES, k0, 0, r + p.b_row0);
           bulk_commit();
           store_pending = true;
         }
@@ -516,8 +515,8 @@ __global__ void __launch_bounds__(CT_THREADS, 1)
           }
           const uint32_t dst = sbase + s * CT_STAGE_BYTES;
           mbar_arrive_expect_tx(full(s), CT_STAGE_BYTES);
-          tma_load_3d(dst, &amap, full(s), kb * CT_BK, p.row_begin + mi * CT_BM, h);
-          tma_load_3d(dst + CT_A_BYTES, &bmap, full(s), kb * CT_BK, ni * CT_BN, h);
+          tma_load_3d(dst, &amap, full(s), kb * CT_BK, h, p.row_begin + mi * CT_BM);
+          tma_load_3d(dst + CT_A_BYTES, &bmap, full(s), kb * CT_BK, h, ni * CT_BN);
         }
       }
       {  // every load issued has landed before the CTA exits (immediate unless a consumer gave up)
@@ -988,18 +987,19 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
 // Host side.
 // ---------------------------------------------------------------------------
 
-TriangleLayout triangle_layout(int64_t n, int64_t cz, int64_t ch, int64_t block_rows, int z_dtype) {
+TriangleLayout triangle_layout(int64_t n, int64_t cz, int64_t ch, int64_t block_rows, int z_dtype, int64_t rows) {
   using tri::kChannelPad;
   TriangleLayout L;
   L.n = n;
   L.cz = cz;
   L.ch = ch;
-  L.block_rows = (block_rows <= 0 || block_rows > n) ? n : block_rows;
+  L.rows = (rows <= 0 || rows > n) ? n : rows;
+  L.block_rows = (block_rows <= 0 || block_rows > L.rows) ? L.rows : block_rows;
   L.kp = static_cast<int64_t>(align_up(static_cast<size_t>(n), 8));
   L.jp = L.kp;
-  // Channel pitches are padded by 128 bytes so that the per-channel planes do
-  // not sit an exact power of two apart (rows of 2^k bytes times 2^k rows).
-  L.ab_hs = L.n * L.kp + kChannelPad;
+  // Pitches are padded by 128 bytes so that rows and channel planes do not sit
+  // an exact power of two apart (2^k-byte vectors times 2^k of them).
+  L.ab_rs = tri::C * L.kp + kChannelPad;
   L.x_hs = L.block_rows * L.jp + kChannelPad;
   L.pad_z = (z_dtype == AF2_F32) || cz != tri::C;
   size_t off = 0;
@@ -1008,11 +1008,11 @@ TriangleLayout triangle_layout(int64_t n, int64_t cz, int64_t ch, int64_t block_
   L.off_vec = off;
   off = align_up(off + sizeof(float) * tri::kVecCount * tri::C, 256);
   L.off_z16 = off;
-  if (L.pad_z) off = align_up(off + sizeof(__half) * (size_t)n * n * tri::C, 256);
+  if (L.pad_z) off = align_up(off + sizeof(__half) * (size_t)L.rows * n * tri::C, 256);
   L.off_a = off;
-  off = align_up(off + sizeof(__half) * (size_t)tri::C * L.ab_hs, 256);
+  off = align_up(off + sizeof(__half) * (size_t)L.n * L.ab_rs, 256);
   L.off_b = off;
-  off = align_up(off + sizeof(__half) * (size_t)tri::C * L.ab_hs, 256);
+  off = align_up(off + sizeof(__half) * (size_t)L.n * L.ab_rs, 256);
   L.off_x = off;
   off = align_up(off + sizeof(__half) * (size_t)tri::C * L.x_hs, 256);
   L.total = off;
@@ -1077,7 +1077,7 @@ af2_status launch_output_any(af2_ctx *ctx, int out_dtype, const CUtensorMap &xma
 
 af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L, const void *z, int z_dtype,
                            const float *mask, const float *packed, double eps, int residual, void *out,
-                           int out_dtype, void *workspace, cudaStream_t stream) {
+                           int out_dtype, void *workspace, cudaStream_t stream, const TriangleExchange *exchange) {
   using namespace tri;
   uint8_t *ws = static_cast<uint8_t *>(workspace);
   __half *w16 = reinterpret_cast<__half *>(ws + L.off_w16);
@@ -1086,7 +1086,9 @@ af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L,
   __half *b = reinterpret_cast<__half *>(ws + L.off_b);
   __half *x = reinterpret_cast<__half *>(ws + L.off_x);
   const int n = static_cast<int>(L.n);
-  const int64_t pairs = L.n * L.n;
+  const int64_t rows = L.rows;
+  const int64_t pairs = rows * L.n;
+  const int64_t b_row0 = exchange ? exchange->b_row0 : 0;
 
   {
     LaunchScope scope(ctx, stream, kProfTrianglePrepare);
@@ -1117,53 +1119,55 @@ af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L,
   // Tile rows are pairs (r, k0..k0+63) outgoing and (k0..k0+63, r) incoming.  Both maps
   // describe z in its natural [row][col][c] order; the incoming box is one column wide
   // and 64 rows tall, which lands the same [64 rows][128 B] tile in shared memory.
-  if (!encode_map_3d(&zmap_proj, map_type(zt), zsrc, C, L.n, L.n, row_bytes, row_bytes * L.n, 64,
+  if (!encode_map_3d(&zmap_proj, map_type(zt), zsrc, C, L.n, rows, row_bytes, row_bytes * L.n, 64,
                      out_dir ? PJ_TILE : 1, out_dir ? 1 : PJ_TILE, CU_TENSOR_MAP_SWIZZLE_128B))
     return fail(ctx, AF2_ERR_CUDA, "cuTensorMapEncodeTiled failed for the projection's z map");
   ProjectArgs pa;
   pa.mask = mask;
   pa.mask_rs = out_dir ? L.n : 1;
   pa.mask_ks = out_dir ? 1 : L.n;
-  pa.a_out = a;
-  pa.b_out = b;
-  pa.out_hs = L.ab_hs;
-  pa.out_rs = L.kp;
+  pa.b_row0 = static_cast<int>(b_row0);
   pa.w16 = w16;
   pa.vec = vec;
   pa.n = n;
   pa.cz = (int)L.cz;
   pa.tiles_k = (n + PJ_TILE - 1) / PJ_TILE;
-  pa.total_tiles = n * pa.tiles_k;
+  pa.total_tiles = static_cast<int>(rows) * pa.tiles_k;
   pa.transposed = out_dir ? 0 : 1;
   pa.eps = static_cast<float>(eps);
   pa.err = ctx->err_word;
-  // The gated operands leave through TMA stores: [128 h][N rows][kp], one box = 64 pairs x 128 channels.
+  // The gated operands leave through TMA stores: [row][128 h][kp], one box = 64 pairs x 128 channels.
+  // A row's 128 channel vectors are contiguous, so the rows of a row-sharded
+  // pair are contiguous too and the b operand is exchanged as one block per rank.
   CUtensorMap amap_st, bmap_st;
-  if (!encode_map_3d(&amap_st, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a, L.n, L.n, C, L.kp * 2, L.ab_hs * 2, PJ_TILE, 1, C,
+  if (!encode_map_3d(&amap_st, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a, L.n, C, rows, L.kp * 2, L.ab_rs * 2, PJ_TILE, C, 1,
                      CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !encode_map_3d(&bmap_st, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, b, L.n, L.n, C, L.kp * 2, L.ab_hs * 2, PJ_TILE, 1, C,
+      !encode_map_3d(&bmap_st, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, b, L.n, C, L.n, L.kp * 2, L.ab_rs * 2, PJ_TILE, C, 1,
                      CU_TENSOR_MAP_SWIZZLE_128B))
     return fail(ctx, AF2_ERR_CUDA, "cuTensorMapEncodeTiled failed for the projection's store maps");
   af2_status st = zt == AF2_BF16 ? launch_project<__nv_bfloat16>(ctx, zmap_proj, amap_st, bmap_st, pa, stream)
                                  : launch_project<__half>(ctx, zmap_proj, amap_st, bmap_st, pa, stream);
   if (st != AF2_OK) return st;
+  if (exchange && exchange->all_gather &&
+      (st = exchange->all_gather(ctx, b, (size_t)rows * L.ab_rs * sizeof(__half), stream)) != AF2_OK)
+    return st;
 
   // ---- per block of output rows: contraction, then output ----
   const __half *m_op = out_dir ? a : b;  // rows i of the product
   const __half *n_op = out_dir ? b : a;  // rows j of the product
   CUtensorMap amap, bmap, zmap_out;
-  if (!encode_map_3d(&amap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, m_op, L.n, L.n, C, L.kp * 2, L.ab_hs * 2, CT_BK,
-                     CT_BM, 1, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !encode_map_3d(&bmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, n_op, L.n, L.n, C, L.kp * 2, L.ab_hs * 2, CT_BK,
-                     CT_BN, 1, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !encode_map_3d(&zmap_out, map_type(zt), zsrc, C, L.n, L.n, row_bytes, row_bytes * L.n, 64, 128, 1,
+  if (!encode_map_3d(&amap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, m_op, L.n, C, out_dir ? rows : L.n, L.kp * 2,
+                     L.ab_rs * 2, CT_BK, 1, CT_BM, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_map_3d(&bmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, n_op, L.n, C, L.n, L.kp * 2, L.ab_rs * 2, CT_BK, 1,
+                     CT_BN, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_map_3d(&zmap_out, map_type(zt), zsrc, C, L.n, rows, row_bytes, row_bytes * L.n, 64, 128, 1,
                      CU_TENSOR_MAP_SWIZZLE_128B))
     return fail(ctx, AF2_ERR_CUDA, "cuTensorMapEncodeTiled failed for the contraction maps");
   // 16-bit outputs with 128 channels leave through TMA: [N][N][128], one box = 64 channels x 128 pairs.
   CUtensorMap omap;
   std::memset(&omap, 0, sizeof omap);
   if (out_dtype != AF2_F32 && L.cz == C &&
-      !encode_map_3d(&omap, map_type(out_dtype), out, C, L.n, L.n, row_bytes, row_bytes * L.n, 64, 128, 1,
+      !encode_map_3d(&omap, map_type(out_dtype), out, C, L.n, rows, row_bytes, row_bytes * L.n, 64, 128, 1,
                      CU_TENSOR_MAP_SWIZZLE_128B))
     return fail(ctx, AF2_ERR_CUDA, "cuTensorMapEncodeTiled failed for the output store map");
   static bool contract_configured = false;
@@ -1172,8 +1176,8 @@ af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L,
     if (e != cudaSuccess) return cuda_fail(ctx, e, "configure contraction kernel");
     contract_configured = true;
   }
-  for (int64_t rb = 0; rb < L.n; rb += L.block_rows) {
-    const int rc = static_cast<int>(std::min<int64_t>(L.block_rows, L.n - rb));
+  for (int64_t rb = 0; rb < rows; rb += L.block_rows) {
+    const int rc = static_cast<int>(std::min<int64_t>(L.block_rows, rows - rb));
     ContractArgs ca;
     ca.x_out = x;
     ca.x_hs = (int64_t)rc * L.jp + kChannelPad;

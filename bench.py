@@ -2,23 +2,27 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-One step is one Evoformer pair-stack block's triangle multiplications at
-N=1024, c_z = c_hidden = 128: the outgoing update then the incoming update,
-each added in place into a bf16 pair (the in-model encoder's residual form,
-src/evoformer/block.ts:1720-1725 of the reference).  value = algorithmic
-TFLOP/s over the whole job (FLOP formulas of src/runtime/kernel-cost.ts:158-162,
-481.0 GFLOP per direction), with every input resident in HBM before the timed
-region; the pair (268 MB) is larger than L2, so no flush is needed.
+One step is one Evoformer block's pair GEMM set at N=1024 (the metric's
+workload): the outer-product mean of an S=512, c_m=256 MSA added into the
+pair, the triangle multiplications outgoing then incoming (c_z = c_hidden =
+128), and the pair transition (128 -> 512 -> 128, mixed-q8 weights with f32
+per-output-channel scales), each updating one bf16 pair [1024, 1024, 128] in
+place -- the in-model order and residual form of the reference
+(src/evoformer/block.ts:1673-1751).  value = algorithmic TFLOP/s over the
+whole job (FLOP formulas of src/runtime/kernel-cost.ts: 962.1 triangle +
+1391.6 OPM + 274.9 transition = 2628.6 GFLOP per block), with every input
+resident in HBM before the timed region; the pair and the MSA (268 MB each)
+are larger than L2, so no flush is needed.
 
-e2e times the same step through the reference-facing host form
-(af2_triangle_multiplication_host: f32 host arrays in, f32 host array out,
-like TriangleMultiplication*Gpu.run) from pinned host memory.
+e2e times the same step through the public device-form API with the step's
+inputs copied in from pinned host memory (pair and MSA, bf16) and the pair
+read back, every step.
 
 --impl reference times the CPU restatement of the reference's own CPU path
 (the reference is TypeScript and no JavaScript runtime exists on this box) on
-a bounded sample of the same workload, with every host thread.
+a bounded sample of the same block, with every host thread.
 
-Multi-GPU (torchrun): every rank runs its own independent pair (replicas,
+Multi-GPU (torchrun): every rank runs its own independent block (replicas,
 weak scaling); value sums the work of all ranks over the max-over-ranks time.
 """
 from __future__ import annotations
@@ -38,10 +42,15 @@ sys.path.insert(0, str(ROOT / "alphafold2-webgpu_b200"))
 
 N = 1024
 CZ = CH = 128
+S_MSA, CM, C_OUTER = 512, 256, 32
+HIDDEN = 4 * CZ
 METRIC = "Evoformer pair-GEMM TFLOP/s & ms/block at N=1024; % of B200 bf16 TC peak"
-# dram__bytes_read.sum + dram__bytes_write.sum of one contract_kernel launch, from one ncu
-# capture of this script (profiles/triangle_contract_n1024_dram.md).
-CONTRACT_DRAM_BYTES = {1024: 771_527_680}
+# dram__bytes_read.sum + dram__bytes_write.sum per launch, from ncu captures of
+# this workload (profiles/*.md); kernels without a capture report null.
+KERNEL_DRAM_BYTES = {"triangle.contract": 771_527_680}
+KERNELS = ("weights.prepare", "triangle.prepare", "triangle.relayout", "triangle.project", "triangle.contract",
+           "triangle.output", "opm.normalize", "opm.project", "opm.count", "opm.outer", "opm.output",
+           "transition.prepare", "transition.fused")
 
 
 def triangle_flops(n: int, cz: int = CZ, ch: int = CH) -> float:
@@ -51,6 +60,30 @@ def triangle_flops(n: int, cz: int = CZ, ch: int = CH) -> float:
 
 def contraction_flops(n: int, ch: int = CH) -> float:
     return 2.0 * n * n * n * ch
+
+
+def opm_flops(n: int, s: int = S_MSA, cm: int = CM, c: int = C_OUTER, cz: int = CZ) -> float:
+    """kernel-cost.ts: projection 2 S N c_m 2c, contraction 2 (N c)^2 S, output 2 N^2 c^2 c_z."""
+    return 2.0 * s * n * cm * 2 * c + 2.0 * (n * c) ** 2 * s + 2.0 * n * n * c * c * cz
+
+
+def transition_flops(n: int, c: int = CZ, h: int = HIDDEN) -> float:
+    return 4.0 * n * n * c * h
+
+
+def block_flops(n: int = N, s: int = S_MSA) -> float:
+    return 2 * triangle_flops(n) + opm_flops(n, s) + transition_flops(n)
+
+
+def kernel_flops(name: str, n: int = N, s: int = S_MSA, opm_blocks: int = 1) -> float | None:
+    """Algorithmic FLOPs of one launch of a tensor-core kernel of the block."""
+    return {"triangle.contract": contraction_flops(n),
+            "triangle.project": 2.0 * n * n * CZ * 4 * CH,
+            "triangle.output": 2.0 * n * n * (CH * CZ + CZ * CZ),
+            "opm.outer": 2.0 * (n * C_OUTER) ** 2 * s / opm_blocks,
+            "opm.output": 2.0 * n * n * C_OUTER * C_OUTER * CZ / opm_blocks,
+            "opm.project": 2.0 * s * n * CM * 2 * C_OUTER,
+            "transition.fused": transition_flops(n)}.get(name)
 
 
 def measured_peaks() -> dict:
@@ -130,24 +163,58 @@ class ClockSampler:
                 "reasons": sorted(self.reasons), "samples": len(self.samples)}
 
 
-def cpu_reference_rate(sample_n: int, repeats: int, threads: int) -> tuple[float, float, str]:
-    """Times the oracle (CPU restatement of the reference's CPU path) on a bounded
-    sample: `repeats` x (outgoing + incoming) at N=sample_n.  Returns (TFLOP/s, seconds, description)."""
+def opm_weights(rng, cm=CM, c=C_OUTER, cz=CZ):
+    """The benchmark configs' OPM law: LN gamma 1 / beta 0, W ~ N(0, 1/fan_in) in [in, out], biases 0."""
+    import numpy as np
+    return np.concatenate([np.ones(cm), np.zeros(cm),
+                           rng.standard_normal(cm * c) / np.sqrt(cm), np.zeros(c),
+                           rng.standard_normal(cm * c) / np.sqrt(cm), np.zeros(c),
+                           rng.standard_normal(c * c * cz) / np.sqrt(c * c), np.zeros(cz)]).astype(np.float32)
+
+
+def transition_weights(rng, c=CZ, h=HIDDEN):
+    """Pair transition weights ~N(0, 1/fan_in), [in, out]; the matrices as symmetric int8
+    with one f32 scale per output column (the mixed-q8 format of the benchmark configs)."""
+    import numpy as np
+
+    def q8(w):
+        scale = np.abs(w).max(axis=0) / 127.0
+        scale[scale == 0] = 1.0
+        codes = np.clip(np.floor(w / scale + 0.5), -127, 127).astype(np.int8)
+        return codes, scale.astype(np.float32)
+
+    w1 = (rng.standard_normal((c, h)) / np.sqrt(c)).astype(np.float32)
+    w2 = (rng.standard_normal((h, c)) / np.sqrt(h)).astype(np.float32)
+    return {"ln": (np.ones(c, np.float32), np.zeros(c, np.float32)), "w1": q8(w1), "b1": np.zeros(h, np.float32),
+            "w2": q8(w2), "b2": np.zeros(c, np.float32)}
+
+
+def cpu_block_rate(n: int, s: int, threads: int) -> tuple[float, float, str]:
+    """Times the oracle (CPU restatement of the reference's CPU path) on one block
+    at pair length n and s MSA rows: triangle out + in, OPM, pair transition.
+    Returns (TFLOP/s, seconds, description)."""
     sys.path.insert(0, str(ROOT / "oracle"))
     import numpy as np
 
     import oracle
     rng = np.random.default_rng(0)
-    z = rng.standard_normal((sample_n, sample_n, CZ)).astype(np.float32)
-    mask = np.ones((sample_n, sample_n), np.float32)
-    w = synthetic_weights(rng)
+    z = rng.standard_normal((n, n, CZ)).astype(np.float32)
+    mask = np.ones((n, n), np.float32)
+    msa = rng.standard_normal((s, n, CM)).astype(np.float32)
+    msa_mask = np.ones((s, n), np.float32)
+    wt = [synthetic_weights(rng) for _ in range(2)]
+    wo = opm_weights(rng)
+    tw = transition_weights(rng)
+    dense = np.concatenate([tw["ln"][0], tw["ln"][1], oracle.dequant_q8_columns(*tw["w1"]).ravel(), tw["b1"],
+                            oracle.dequant_q8_columns(*tw["w2"]).ravel(), tw["b2"]])
     t0 = time.perf_counter()
-    for _ in range(repeats):
-        for d in (0, 1):
-            oracle.triangle(d, z, mask, w, 1e-5, threads=threads)
+    z = z + oracle.outer_product_mean(msa, msa_mask, wo, C_OUTER, CZ, threads=threads)
+    for d in (0, 1):
+        z = z + oracle.triangle(d, z, mask, wt[d], 1e-5, threads=threads)
+    z = oracle.transition(z.reshape(-1, CZ), dense, HIDDEN, residual=True, threads=threads)
     dt = time.perf_counter() - t0
-    flops = repeats * 2 * triangle_flops(sample_n)
-    return flops / dt / 1e12, dt, f"{repeats} x (outgoing + incoming) at N={sample_n}, c=128, f64-accumulating CPU port"
+    return block_flops(n, s) / dt / 1e12, dt, (f"one block at N={n}, S={s} (OPM, triangle out + in, pair "
+                                               "transition), f64-accumulating CPU port")
 
 
 def run_reference(args) -> None:
@@ -156,30 +223,32 @@ def run_reference(args) -> None:
         return
     threads = os.cpu_count() or 1
     # Size each step's sample so that warm-up plus timed steps take about a minute.
-    rate, _, _ = cpu_reference_rate(96, 1, threads)
+    rate, _, _ = cpu_block_rate(64, 32, threads)
     budget_flops = rate * 1e12 * 60.0 / max(1, args.steps + args.warmup)
-    sample_n = 32
-    while sample_n < N and 2 * triangle_flops(sample_n + 16) <= budget_flops:
+    sample_n = 48
+    while sample_n < N and block_flops(sample_n + 16, sample_n // 2 + 8) <= budget_flops:
         sample_n += 16
+    sample_s = sample_n // 2
     for _ in range(args.warmup):
-        cpu_reference_rate(sample_n, 1, threads)
+        cpu_block_rate(sample_n, sample_s, threads)
     rates, secs = [], []
     for _ in range(args.steps):
-        r, s, desc = cpu_reference_rate(sample_n, 1, threads)
+        r, sec, desc = cpu_block_rate(sample_n, sample_s, threads)
         rates.append(r)
-        secs.append(s)
+        secs.append(sec)
     value = statistics.median(rates)
-    ms_per_step = triangle_flops(N) * 2 / (value * 1e12) * 1e3
+    ms_per_step = block_flops() / (value * 1e12) * 1e3
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-        "config": {"workload": "triangle multiplication outgoing+incoming, N=1024, c_z=c_hidden=128 "
-                               f"(each step timed on a bounded N={sample_n} sample; ms_per_step extrapolated "
-                               "to N=1024 by FLOPs)",
-                   "N": N, "parallelism": "host threads"},
+        "config": {"workload": "one Evoformer block's pair GEMM set at N=1024, S=512 (OPM, triangle "
+                               f"out + in, pair transition); each step timed on a bounded N={sample_n}, "
+                               f"S={sample_s} sample, ms_per_step extrapolated to N=1024 by FLOPs",
+                   "N": N, "S": S_MSA, "parallelism": "host threads"},
         "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port",
-                         "sample": f"per step: outgoing + incoming at N={sample_n} (median {statistics.median(secs):.2f} s)"},
+                         "sample": f"per step: one block at N={sample_n}, S={sample_s} "
+                                   f"(median {statistics.median(secs):.2f} s)"},
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -213,13 +282,27 @@ def run_ours(args) -> None:
     gen = torch.Generator(device="cuda").manual_seed(1234 + rank)
     pair = torch.randn(N, N, CZ, device="cuda", generator=gen).to(torch.bfloat16)
     mask = torch.ones(N, N, device="cuda")
+    msa = torch.randn(S_MSA, N, CM, device="cuda", generator=gen).to(torch.bfloat16)
+    msa_mask = (torch.rand(S_MSA, N, device="cuda", generator=gen) < 0.9).float()
+    msa_mask[0] = 1
     w_out = torch.from_numpy(synthetic_weights(rng)).cuda()
     w_in = torch.from_numpy(synthetic_weights(rng)).cuda()
+    w_opm = torch.from_numpy(opm_weights(rng)).cuda()
+    tw = transition_weights(rng)
+    tws = {"layerNormScale": torch.from_numpy(tw["ln"][0]).cuda(), "layerNormOffset": torch.from_numpy(tw["ln"][1]).cuda(),
+           "firstWeight": af2cuda.Q8Matrix(torch.from_numpy(tw["w1"][0]).cuda(), torch.from_numpy(tw["w1"][1]).cuda()),
+           "firstBias": torch.from_numpy(tw["b1"]).cuda(),
+           "secondWeight": af2cuda.Q8Matrix(torch.from_numpy(tw["w2"][0]).cuda(), torch.from_numpy(tw["w2"][1]).cuda()),
+           "secondBias": torch.from_numpy(tw["b2"]).cuda()}
+    pair_rows = pair.view(N * N, CZ)
     torch.cuda.synchronize()
 
     def step():
+        af2cuda.encode_outer_product_mean_tensors(dev, msa, msa_mask, w_opm, C_OUTER, CZ, pair=pair, residual=True,
+                                                  stream=sh)
         af2cuda.encode_triangle_multiplication_tensors(dev, 0, pair, mask, w_out, residual=True, stream=sh)
         af2cuda.encode_triangle_multiplication_tensors(dev, 1, pair, mask, w_in, residual=True, stream=sh)
+        af2cuda.encode_transition_tensors(dev, pair_rows, tws, residual=True, stream=sh)
 
     for _ in range(max(args.warmup, 3)):
         step()
@@ -230,9 +313,7 @@ def run_ours(args) -> None:
             dist.barrier()
         torch.cuda.synchronize()
 
-    # ---- timed region: K steps, device events, profiler on for the per-kernel roofline ----
-    L.af2_profile_enable(dev.handle, 1)
-    L.af2_profile_reset(dev.handle)
+    # ---- timed region: K steps on the device, nothing else running ----
     launches0 = dev.launch_count
     barrier()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -246,76 +327,82 @@ def run_ours(args) -> None:
     barrier()
     launches = dev.launch_count - launches0
     ms = start.elapsed_time(stop)
-    kernel = {}
-    for name in ("triangle.prepare", "triangle.relayout", "triangle.project", "triangle.contract", "triangle.output"):
-        c, t = ctypes.c_uint64(), ctypes.c_double()
-        L.af2_profile_read(dev.handle, name.encode(), ctypes.byref(c), ctypes.byref(t))
-        if c.value:
-            kernel[name] = {"launches": int(c.value), "avg_us": t.value / c.value * 1e3,
-                            "share": 0.0, "total_ms": t.value}
-    L.af2_profile_enable(dev.handle, 0)
-    total_kernel_ms = sum(k["total_ms"] for k in kernel.values()) or 1.0
-    for k in kernel.values():
-        k["share"] = k["total_ms"] / total_kernel_ms
     if dist:
         t = torch.tensor([ms], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-    flops_step = 2 * triangle_flops(N)
+    flops_step = block_flops()
     value = world * flops_step * args.steps / (ms * 1e-3) / 1e12
     peaks = measured_peaks()
 
-    # ---- roofline of the dominant kernel (the per-channel contraction) ----
-    con = kernel["triangle.contract"]
-    achieved = contraction_flops(N) / (con["avg_us"] * 1e-6) / 1e12
-    traffic = CONTRACT_DRAM_BYTES.get(N)
-    roofline = {"kernel": "triangle.contract", "bound": "tensor", "achieved": achieved,
-                "peak": peaks["bf16_tflops"], "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
-                "traffic": traffic, "peak_source": f"{peaks['source']} burst bf16",
-                "flops_per_launch": contraction_flops(N), "avg_launch_us": con["avg_us"]}
+    # ---- per-kernel device times (CUDA events around each launch, a separate profiled pass) ----
+    L.af2_profile_enable(dev.handle, 1)
+    L.af2_profile_reset(dev.handle)
+    prof_steps = 3
+    for _ in range(prof_steps):
+        step()
+    dev.sync(sh)
+    kernel = {}
+    for name in KERNELS:
+        c, t = ctypes.c_uint64(), ctypes.c_double()
+        L.af2_profile_read(dev.handle, name.encode(), ctypes.byref(c), ctypes.byref(t))
+        if c.value:
+            kernel[name] = {"launches_per_step": c.value / prof_steps, "avg_us": t.value / c.value * 1e3,
+                            "ms_per_step": t.value / prof_steps, "share": 0.0}
+    L.af2_profile_enable(dev.handle, 0)
+    total_kernel_ms = sum(k["ms_per_step"] for k in kernel.values()) or 1.0
+    for k in kernel.values():
+        k["share"] = k["ms_per_step"] / total_kernel_ms
 
-    # ---- e2e: the reference-facing host form, f32 host arrays in and out ----
-    e2e = None
-    if True:  # every rank: the e2e time is also a max over ranks
-        host_z = torch.empty(N, N, CZ, dtype=torch.float32, pin_memory=True)
-        host_z.copy_(pair.float().cpu())
-        host_out = torch.empty_like(host_z, pin_memory=True)
-        host_mask = torch.ones(N, N, dtype=torch.float32, pin_memory=True)
-        hw = [torch.from_numpy(synthetic_weights(rng)).pin_memory() for _ in range(2)]
-        shape = _lib.TriangleShape(N, CZ, CH)
-        opts = _lib.TriangleOptions(0, 1)
-        stats = _lib.OpStats()
+    # ---- roofline of the dominant kernel ----
+    opm_blocks = int(round(kernel.get("opm.outer", {}).get("launches_per_step", 1)))
+    tensor = {k: v for k, v in kernel.items() if kernel_flops(k, opm_blocks=opm_blocks) is not None}
+    dom = max(tensor, key=lambda k: tensor[k]["ms_per_step"])
+    fl = kernel_flops(dom, opm_blocks=opm_blocks)
+    achieved = fl / (tensor[dom]["avg_us"] * 1e-6) / 1e12
+    roofline = {"kernel": dom, "bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
+                "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"], "traffic": KERNEL_DRAM_BYTES.get(dom),
+                "peak_source": f"{peaks['source']} burst bf16", "flops_per_launch": fl,
+                "avg_launch_us": tensor[dom]["avg_us"]}
 
-        def host_step():
-            src = host_z
-            for d in (0, 1):
-                st = L.af2_triangle_multiplication_host(
-                    dev.handle, d, ctypes.byref(shape), src.data_ptr(), host_mask.data_ptr(), hw[d].data_ptr(),
-                    hw[d].numel(), 1e-5, ctypes.byref(opts), _lib.AF2_F32, host_out.data_ptr(), ctypes.byref(stats))
-                _lib.check(st, dev.handle)
-                src = host_out
+    # ---- e2e: the public device-form API, inputs copied in from pinned host memory every step ----
+    host_pair = torch.empty(N, N, CZ, dtype=torch.bfloat16, pin_memory=True)
+    host_pair.copy_(pair.cpu())
+    host_msa = torch.empty(S_MSA, N, CM, dtype=torch.bfloat16, pin_memory=True)
+    host_msa.copy_(msa.cpu())
+    host_out = torch.empty_like(host_pair, pin_memory=True)
 
+    def host_step():
+        pair.copy_(host_pair, non_blocking=True)
+        msa.copy_(host_msa, non_blocking=True)
+        step()
+        host_out.copy_(pair, non_blocking=True)
+
+    host_step()
+    torch.cuda.synchronize()
+    e2e_steps = max(3, min(args.steps, 10))
+    barrier()
+    e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_start.record(stream)
+    for _ in range(e2e_steps):
         host_step()
-        e2e_steps = max(3, min(args.steps, 10))
-        barrier()
-        t0 = time.perf_counter()
-        for _ in range(e2e_steps):
-            host_step()
-        e2e_s = time.perf_counter() - t0
-        if dist:
-            t = torch.tensor([e2e_s], device="cuda")
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            e2e_s = float(t.item())
-        per_dir_in = N * N * CZ * 4 + N * N * 4 + hw[0].numel() * 4
-        e2e = {"value": world * flops_step * e2e_steps / e2e_s / 1e12, "unit": "TFLOP/s",
-               "h2d_bytes_per_step": 2 * per_dir_in, "d2h_bytes_per_step": 2 * N * N * CZ * 4,
-               "ms_per_step": e2e_s / e2e_steps * 1e3,
-               "path": "af2_triangle_multiplication_host (f32 host arrays, pinned), outgoing then incoming"}
+    e_stop.record(stream)
+    e_stop.synchronize()
+    e2e_ms = e_start.elapsed_time(e_stop)
+    if dist:
+        t = torch.tensor([e2e_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e = {"value": world * flops_step * e2e_steps / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+           "h2d_bytes_per_step": host_pair.numel() * 2 + host_msa.numel() * 2,
+           "d2h_bytes_per_step": host_out.numel() * 2, "ms_per_step": e2e_ms / e2e_steps,
+           "path": "pair and MSA copied in from pinned host memory, the block through the af2cuda device-form "
+                   "API (af2_outer_product_mean, af2_triangle_multiplication x2, af2_transition), pair read back"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
-        rate, secs, desc = cpu_reference_rate(256, 1, threads)
+        rate, secs, desc = cpu_block_rate(128, 64, threads)
         cpu = {"value": rate, "unit": "TFLOP/s", "cores": threads, "kind": "port",
                "sample": f"{desc} ({secs:.1f} s)"}
 
@@ -326,12 +413,17 @@ def run_ours(args) -> None:
             "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-            "config": {"workload": "triangle multiplication outgoing+incoming (one Evoformer block's pair "
-                                   "triangle updates), N=1024, c_z=c_hidden=128, bf16 pair updated in place, "
-                                   "f16 tensor-core operands with f32 accumulation",
-                       "N": N, "c_z": CZ, "c_hidden": CH, "flops_per_step": flops_step,
-                       "l2": "inputs larger than L2 (pair 268 MB bf16; scratch 805 MB), no flush",
+            "config": {"workload": "one Evoformer block's pair GEMM set at N=1024 (OPM of an S=512, c_m=256 MSA "
+                                   "into the pair, triangle multiplication outgoing + incoming with c_z=c_hidden="
+                                   "128, pair transition 128->512->128 with mixed-q8 weights), bf16 pair updated "
+                                   "in place, f16 tensor-core operands with f32 accumulation",
+                       "N": N, "S": S_MSA, "c_m": CM, "c_outer": C_OUTER, "c_z": CZ, "c_hidden": CH,
+                       "flops_per_step": flops_step,
+                       "gflop_per_block": {"triangle": 2 * triangle_flops(N) / 1e9, "opm": opm_flops(N) / 1e9,
+                                           "transition": transition_flops(N) / 1e9},
+                       "l2": "inputs larger than L2 (pair 268 MB, MSA 268 MB, bf16), no flush",
                        "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
+            "ms_per_block": ms / args.steps,
             "pct_of_peak": value / world / peaks["bf16_tflops"],
             "roofline": roofline, "kernels": kernel, "cpu_baseline": cpu, "e2e": e2e,
             "gpu_launches": int(launches), "clocks": clocks.record(),
@@ -345,7 +437,7 @@ def run_ours(args) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
