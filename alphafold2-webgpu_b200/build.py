@@ -57,7 +57,9 @@ def build(verbose: bool = False) -> Path:
         objs = list(pool.map(lambda s: _compile(s, verbose), sources))
     if LIB.exists() and LIB.stat().st_mtime >= max(o.stat().st_mtime for o in objs):
         return LIB
-    cmd = [nvcc(), *ARCH, "-shared", "-o", str(LIB), *map(str, objs), "-cudart", "static"]
+    # NCCL is not linked: the library opens the process's libnccl.so.2 when a
+    # communicator is first created (comm.cu), so it never brings a second copy.
+    cmd = [nvcc(), *ARCH, "-shared", "-o", str(LIB), *map(str, objs), "-cudart", "static", "-ldl"]
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
         raise RuntimeError(f"link failed:\n{res.stderr}")

@@ -42,6 +42,7 @@ enum ProfileKernel {
   kProfOpmCount,
   kProfOpmOuter,
   kProfOpmOutput,
+  kProfShardTranspose,
   kProfCount
 };
 const char *profile_name(int id);
@@ -67,6 +68,11 @@ struct af2_ctx {
   double prof_ms[af2::kProfCount] = {};
   uint64_t allocated = 0, peak = 0;
   std::string last_error;
+  // Row-sharded operators (comm.cu): this rank's NCCL communicator and the
+  // scratch of the distributed pair transpose.
+  void *nccl_comm = nullptr;
+  int nranks = 1, rank = 0;
+  af2::DeviceBuffer shard_scratch;
 };
 
 namespace af2 {
@@ -229,5 +235,11 @@ OpmLayout opm_layout(int64_t s, int64_t n, int64_t cm, int64_t c, int64_t cz, in
 af2_status opm_launch(af2_ctx *ctx, const OpmLayout &L, const void *m, int m_dtype, const float *mask,
                       const float *packed, double ln_eps, double norm_eps, int residual, void *out, int out_dtype,
                       void *workspace, cudaStream_t stream);
+
+// ---- row-sharded operators (comm.cu) ----
+
+af2_status shard_transpose(af2_ctx *ctx, const void *src, void *dst, void *pack, void *recv, int rows, int n,
+                           size_t pair_bytes, cudaStream_t stream);
+void comm_destroy(af2_ctx *ctx);
 
 }  // namespace af2

@@ -56,7 +56,7 @@ const char *profile_name(int id) {
       "triangle.output",     "transition.prepare",   "transition.normalize", "transition.fused",
       "q8.decode",           "weights.prepare",      "activations.convert",  "linear",
       "opm.normalize",       "opm.project",          "opm.count",         "opm.outer",
-      "opm.output"};
+      "opm.output",          "shard.transpose"};
   return (id >= 0 && id < kProfCount) ? names[id] : nullptr;
 }
 
@@ -277,6 +277,7 @@ void af2_destroy(af2_ctx *ctx) {
   if (!ctx) return;
   cudaSetDevice(ctx->device);
   if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+  comm_destroy(ctx);
   if (ctx->workspace.ptr) cudaFree(ctx->workspace.ptr);
   for (auto &s : ctx->staging)
     if (s.ptr) cudaFree(s.ptr);

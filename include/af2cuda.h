@@ -191,6 +191,35 @@ AF2_API af2_status af2_triangle_multiplication_static(af2_ctx *ctx, int directio
                                                       double epsilon, const af2_triangle_options *options,
                                                       void *out, int out_dtype, void *stream);
 
+/* ---- the pair sharded by rows across the GPUs of one box ---------------- */
+
+/*
+ * One process and one context per GPU.  Rank 0 creates a unique id (128
+ * bytes), the host hands it to every rank (for instance with
+ * torch.distributed.broadcast_object_list), and every rank calls
+ * af2_comm_init with it; NCCL carries the exchanges over NVLink.  No
+ * counterpart in the reference, which runs on one device.
+ */
+#define AF2_COMM_UNIQUE_ID_BYTES 128
+AF2_API af2_status af2_comm_unique_id(void *unique_id);
+AF2_API af2_status af2_comm_init(af2_ctx *ctx, const void *unique_id, int nranks, int rank);
+AF2_API af2_status af2_comm_destroy(af2_ctx *ctx);
+
+/*
+ * The device form of triangle multiplication on a pair sharded by rows: this
+ * rank holds rows [rank * L, (rank + 1) * L) of z, mask and out (L = length /
+ * nranks, a multiple of 8), shape->length is the full length.  Outgoing
+ * all-gathers the projected b operand; incoming transposes the pair and the
+ * mask across ranks (all-to-all) and back.  Every rank calls it with the same
+ * arguments, collectively.  Results are bit-identical to the single-GPU
+ * af2_triangle_multiplication.  The incoming update keeps z's dtype.
+ */
+AF2_API af2_status af2_triangle_multiplication_sharded(af2_ctx *ctx, int direction, const af2_triangle_shape *shape,
+                                                       const void *z, int z_dtype, const float *mask,
+                                                       const float *packed_weights, int64_t weight_count,
+                                                       double epsilon, const af2_triangle_options *options,
+                                                       void *out, int out_dtype, void *stream);
+
 /* ---- weights: f32 or mixed-q8 ------------------------------------------ */
 
 typedef enum af2_weight_format {

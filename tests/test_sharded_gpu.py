@@ -1,0 +1,93 @@
+"""Row-sharded triangle multiplication on 2+ GPUs (one process per GPU, the
+library's NCCL communicator): every rank's rows must be bit-identical to the
+single-GPU result.  Skipped on boxes with fewer than two GPUs."""
+import datetime
+import os
+import socket
+import sys
+from pathlib import Path
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, nranks, port, result):
+    sys.path.insert(0, str(ROOT / "alphafold2-webgpu_b200"))
+    sys.path.insert(0, str(ROOT / "tests"))
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import af2cuda
+    from helpers import pack, triangle_case
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=nranks, timeout=datetime.timedelta(seconds=120))
+    dev = af2cuda.Device(rank)
+    ok = True
+    try:
+        uid = [af2cuda.comm_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        af2cuda.comm_init(dev, uid[0], nranks, rank)
+        n = 256
+        r0, r1 = af2cuda.rows_of(n, nranks, rank)
+        z, mask, w = triangle_case(n, seed=7, mask_p=0.9, perturbed=True)
+        mask[:, 17] = 0
+        packed = torch.from_numpy(pack(w)).cuda()
+        mask_d = torch.from_numpy(mask).cuda()
+        torch.cuda.synchronize()
+        for direction in (0, 1):
+            full = torch.from_numpy(z).to("cuda", torch.bfloat16)
+            rows = torch.from_numpy(z[r0:r1]).to("cuda", torch.bfloat16).contiguous()
+            mask_rows = mask_d[r0:r1].contiguous()
+            torch.cuda.synchronize()  # the library runs on its own stream
+            af2cuda.encode_triangle_multiplication_tensors(dev, direction, full, mask_d, packed, residual=True)
+            af2cuda.encode_triangle_multiplication_sharded_tensors(dev, direction, rows, mask_rows, packed, n,
+                                                                   residual=True)
+            dev.sync()
+            ok &= bool(torch.equal(rows, full[r0:r1]))
+        # f32 pair, written out of place (outgoing)
+        zf = torch.from_numpy(z).cuda()
+        ref = torch.empty_like(zf)
+        out_rows = torch.empty(r1 - r0, n, z.shape[2], device="cuda")
+        zf_rows, mask_rows = zf[r0:r1].contiguous(), mask_d[r0:r1].contiguous()
+        torch.cuda.synchronize()
+        af2cuda.encode_triangle_multiplication_tensors(dev, 0, zf, mask_d, packed, out=ref, residual=False)
+        af2cuda.encode_triangle_multiplication_sharded_tensors(dev, 0, zf_rows, mask_rows, packed, n, out=out_rows,
+                                                               residual=False)
+        dev.sync()
+        ok &= bool(torch.equal(out_rows, ref[r0:r1]))
+        af2cuda.comm_destroy(dev)
+    finally:
+        dev.close()
+        dist.destroy_process_group()
+    result[rank] = int(ok)
+
+
+def test_sharded_triangle_is_bit_identical():
+    import torch
+    import torch.multiprocessing as mp
+    count = torch.cuda.device_count()
+    if count < 2:
+        pytest.skip("needs two or more GPUs")
+    nranks = 4 if count >= 4 else 2
+    ctx = mp.get_context("spawn")
+    result = ctx.Array("i", nranks)
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, nranks, port, result)) for r in range(nranks)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(600)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    assert list(result) == [1] * nranks
