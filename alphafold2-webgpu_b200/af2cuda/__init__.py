@@ -13,8 +13,8 @@ from .triangle import (TriangleGpuOptions, TriangleGpuResult, TriangleMultiplica
 from .opm import (OuterProductMeanGpu, OuterProductMeanInput, OuterProductMeanResult, OuterProductMeanWeights,
                   encode_outer_product_mean_tensors, linear_tensors, opm_weight_count, opm_workspace_bytes,
                   pack_outer_product_mean_weights, validate_outer_product_mean_input)
-from .sharded import (comm_destroy, comm_init, comm_unique_id, encode_triangle_multiplication_sharded_tensors,
-                      rows_of)
+from .sharded import (comm_destroy, comm_init, comm_unique_id, encode_outer_product_mean_sharded_tensors,
+                      encode_triangle_multiplication_sharded_tensors, rows_of)
 from .transition import (Q8Matrix, TransitionGpu, TransitionInput, TransitionResult, TransitionWeights,
                          dequant_q8_tensors, encode_transition_tensors, pack_transition_weights,
                          transition_weight_count, transition_workspace_bytes, validate_transition_input)
@@ -33,4 +33,5 @@ __all__ = [
     "OuterProductMeanWeights", "encode_outer_product_mean_tensors", "linear_tensors", "opm_weight_count",
     "opm_workspace_bytes", "pack_outer_product_mean_weights", "validate_outer_product_mean_input",
     "comm_destroy", "comm_init", "comm_unique_id", "encode_triangle_multiplication_sharded_tensors", "rows_of",
+    "encode_outer_product_mean_sharded_tensors",
 ]

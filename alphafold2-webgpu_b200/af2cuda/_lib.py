@@ -119,6 +119,8 @@ SIGNATURES = {
     "af2_comm_destroy": (_i32, [_vp]),
     "af2_triangle_multiplication_sharded": (_i32, [_vp, _i32, ctypes.POINTER(TriangleShape), _vp, _i32, _vp, _vp, _i64,
                                                    _f64, ctypes.POINTER(TriangleOptions), _vp, _i32, _vp]),
+    "af2_outer_product_mean_sharded": (_i32, [_vp, ctypes.POINTER(OpmShape), _vp, _i32, _vp, _vp, _i64,
+                                              ctypes.POINTER(OpmOptions), _vp, _i32, _vp]),
     "af2_linear_workspace_bytes": (_i32, [ctypes.POINTER(LinearShape), _i32, ctypes.POINTER(ctypes.c_uint64)]),
     "af2_linear": (_i32, [_vp, ctypes.POINTER(LinearShape), _vp, _i32, ctypes.POINTER(Matrix), _vp, _i32, _i32, _vp,
                           _i32, _vp, _vp]),

@@ -63,3 +63,26 @@ def encode_triangle_multiplication_sharded_tensors(device: Device, direction, pa
         target.data_ptr(), _DTYPES[_TORCH_DTYPES[str(target.dtype)]], stream or None)
     _lib.check(status, device.handle)
     return target
+
+
+def encode_outer_product_mean_sharded_tensors(device: Device, msa, msa_mask, packed_weights, c_outer: int, c_z: int,
+                                              pair_rows, *, residual: bool = True, row_block: int = 0,
+                                              layer_norm_epsilon: float = 1e-5, normalization_epsilon: float = 1e-3,
+                                              stream: int = 0):
+    """Row-sharded OPM: msa [S, N, c_m] and msa_mask [S, N] whole on every rank,
+    pair_rows [L, N, c_z] this rank's rows of the pair (updated when residual).
+    Collective: every rank calls it together."""
+    from .opm import _TORCH_DTYPES as _T
+    s, n, cm = msa.shape
+    for t in (msa, msa_mask, packed_weights, pair_rows):
+        if not t.is_cuda or not t.is_contiguous():
+            raise _lib.RangeError("tensors must be contiguous CUDA tensors")
+    shape = _lib.OpmShape(s, n, cm, c_outer, c_z)
+    opts = _lib.OpmOptions(float(layer_norm_epsilon), float(normalization_epsilon), int(row_block),
+                           1 if residual else 0)
+    status = _lib.lib().af2_outer_product_mean_sharded(
+        device.handle, ctypes.byref(shape), msa.data_ptr(), _DTYPES[_T[str(msa.dtype)]], msa_mask.data_ptr(),
+        packed_weights.data_ptr(), packed_weights.numel(), ctypes.byref(opts), pair_rows.data_ptr(),
+        _DTYPES[_T[str(pair_rows.dtype)]], stream or None)
+    _lib.check(status, device.handle)
+    return pair_rows

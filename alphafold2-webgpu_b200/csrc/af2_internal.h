@@ -223,18 +223,28 @@ af2_status linear_run(af2_ctx *ctx, const LinearLayout &L, int64_t rows, int64_t
 
 struct OpmLayout {
   int64_t s = 0, n = 0, cm = 0, c = 0, cz = 0;
+  int64_t rows = 0, row0 = 0;  // output residues i held here (all n unless the pair is sharded)
   int64_t cmp = 0;          // c_m padded to 64
   int64_t block_rows = 0;   // residues i per output block (a multiple of 4)
   int out_shift = 0;        // outer is stored times 2^-out_shift (2^out_shift >= S)
   size_t off_wlr = 0, off_wlr_scale = 0, off_wlr_bias = 0, off_wo = 0, off_wo_scale = 0, off_wo_bias = 0;
-  size_t off_ln = 0, off_xn = 0, off_left = 0, off_right = 0, off_rowscale = 0, off_outer = 0, total = 0;
+  size_t off_ln = 0, off_xn = 0, off_mask = 0, off_left = 0, off_right = 0, off_rowscale = 0, off_outer = 0;
+  size_t total = 0;
 };
 
-OpmLayout opm_layout(int64_t s, int64_t n, int64_t cm, int64_t c, int64_t cz, int64_t row_block);
+// rows < n: this rank's residues [row0, row0 + rows) of a row-sharded pair.
+OpmLayout opm_layout(int64_t s, int64_t n, int64_t cm, int64_t c, int64_t cz, int64_t row_block, int64_t rows = 0,
+                     int64_t row0 = 0);
+
+// Row-sharded OPM: this rank's block of the right operand is all-gathered in place.
+struct OpmExchange {
+  int rank = 0;
+  af2_status (*all_gather)(af2_ctx *ctx, void *full, size_t bytes_per_rank, cudaStream_t stream) = nullptr;
+};
 
 af2_status opm_launch(af2_ctx *ctx, const OpmLayout &L, const void *m, int m_dtype, const float *mask,
                       const float *packed, double ln_eps, double norm_eps, int residual, void *out, int out_dtype,
-                      void *workspace, cudaStream_t stream);
+                      void *workspace, cudaStream_t stream, const OpmExchange *exchange = nullptr);
 
 // ---- row-sharded operators (comm.cu) ----
 

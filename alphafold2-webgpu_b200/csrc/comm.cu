@@ -22,6 +22,7 @@
 #include <nccl.h>
 
 #include <algorithm>
+#include <cmath>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -269,6 +270,38 @@ af2_status af2_triangle_multiplication_sharded(af2_ctx *ctx, int direction, cons
                             epsilon, residual, zt, z_dtype, ctx->workspace.ptr, s, &ex)) != AF2_OK)
     return st;
   return shard_transpose(ctx, zt, out, pack, recv, (int)rows, (int)n, shape->c_z * zb, s);
+}
+
+af2_status af2_outer_product_mean_sharded(af2_ctx *ctx, const af2_opm_shape *shape, const void *m, int m_dtype,
+                                          const float *mask, const float *packed_weights, int64_t weight_count,
+                                          const af2_opm_options *options, void *out, int out_dtype, void *stream) {
+  if (!ctx) return AF2_ERR_INVALID_ARGUMENT;
+  char message[256];
+  af2_status st = af2_opm_check(shape, weight_count, message, sizeof message);
+  if (st != AF2_OK) return fail(ctx, st, message);
+  if (!ctx->nccl_comm) return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "af2_comm_init has not been called on this context");
+  if (!m || !mask || !packed_weights || !out) return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "a tensor pointer is NULL");
+  const bool dtypes_ok = (m_dtype == AF2_F32 || m_dtype == AF2_F16 || m_dtype == AF2_BF16) &&
+                         (out_dtype == AF2_F32 || out_dtype == AF2_F16 || out_dtype == AF2_BF16);
+  if (!dtypes_ok) return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "dtype must be AF2_F32, AF2_F16 or AF2_BF16");
+  const int64_t n = shape->length, R = ctx->nranks;
+  if (n % R != 0 || (n / R) % 8 != 0)
+    return fail(ctx, AF2_ERR_UNSUPPORTED, "the sharded OPM needs length divisible by 8 x the rank count");
+  const double ln_eps = (options && options->layer_norm_epsilon != 0) ? options->layer_norm_epsilon : 1e-5;
+  const double norm_eps = (options && options->normalization_epsilon != 0) ? options->normalization_epsilon : 1e-3;
+  if (!(ln_eps > 0) || !std::isfinite(ln_eps) || !(norm_eps > 0) || !std::isfinite(norm_eps))
+    return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "epsilons must be finite and positive");
+  const int64_t rows = n / R;
+  cudaSetDevice(ctx->device);
+  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+  const OpmLayout L = opm_layout(shape->sequences, n, shape->c_m, shape->c_outer, shape->c_z,
+                                 options ? options->row_block_residues : 0, rows, ctx->rank * rows);
+  if ((st = ensure(ctx, ctx->workspace, L.total, "outer product mean scratch")) != AF2_OK) return st;
+  OpmExchange ex;
+  ex.rank = ctx->rank;
+  ex.all_gather = nccl_all_gather_in_place;
+  return opm_launch(ctx, L, m, m_dtype, mask, packed_weights, ln_eps, norm_eps, options ? options->residual : 0, out,
+                    out_dtype, ctx->workspace.ptr, s, &ex);
 }
 
 }  // extern "C"

@@ -41,11 +41,15 @@ constexpr int C = 32;  // outer channels c: the outer tile maps 32 channels to 3
 // 16-byte store of f16.  Otherwise lanes stride the channels one by one.
 template <typename MT, bool VEC>
 __global__ void norm_kernel(const MT *__restrict__ m, int64_t rows, int cm, int cmp, const float *__restrict__ gamma,
-                            const float *__restrict__ beta, float eps, __half *__restrict__ xn) {
+                            const float *__restrict__ beta, float eps, __half *__restrict__ xn, int n_full, int col0,
+                            int cols, const float *__restrict__ mask_in, float *__restrict__ mask_out) {
+  // local row (s, j) of the residue columns [col0, col0 + cols) of an [S][n_full] MSA
   const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
-  const MT *xr = m + row * cm;
+  const int64_t src = (row / cols) * n_full + col0 + row % cols;
+  if (lane == 0) mask_out[row] = mask_in[src];
+  const MT *xr = m + src * cm;
   float v[8];
   if (VEC) {
     if constexpr (sizeof(MT) == 4) {
@@ -101,16 +105,17 @@ __global__ void norm_kernel(const MT *__restrict__ m, int64_t rows, int cm, int 
 // ---- pair counts: rowscale[i*N + j] = 1 / (norm_eps + sum_s mask[s,i] mask[s,j]) ----
 // A 32 x 32 block of pairs per CTA; 64 MSA rows of both residue columns at a
 // time through shared memory; every count sums s in order.
-__global__ void __launch_bounds__(256) count_kernel(const float *__restrict__ mask, int s_count, int n,
-                                                    float norm_eps, float *__restrict__ rowscale) {
+__global__ void __launch_bounds__(256) count_kernel(const float *__restrict__ mask, int s_count, int n, int row0,
+                                                    int rows, float norm_eps, float *__restrict__ rowscale) {
+  // rows i in [row0, row0 + rows), stored from row 0 of rowscale
   __shared__ float mi[64][33], mj[64][33];
-  const int i0 = blockIdx.y * 32, j0 = blockIdx.x * 32;
+  const int i0 = row0 + blockIdx.y * 32, j0 = blockIdx.x * 32;
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
   for (int s0 = 0; s0 < s_count; s0 += 64) {
     for (int r = ty; r < 64; r += 8) {
       const int64_t s = s0 + r;
-      mi[r][tx] = (s < s_count && i0 + tx < n) ? mask[s * n + i0 + tx] : 0.f;
+      mi[r][tx] = (s < s_count && i0 + tx < row0 + rows) ? mask[s * n + i0 + tx] : 0.f;
       mj[r][tx] = (s < s_count && j0 + tx < n) ? mask[s * n + j0 + tx] : 0.f;
     }
     __syncthreads();
@@ -125,7 +130,7 @@ __global__ void __launch_bounds__(256) count_kernel(const float *__restrict__ ma
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
     const int i = i0 + ty + 8 * k, j = j0 + tx;
-    if (i < n && j < n) rowscale[static_cast<int64_t>(i) * n + j] = 1.f / (norm_eps + acc[k]);
+    if (i < row0 + rows && j < n) rowscale[static_cast<int64_t>(i - row0) * n + j] = 1.f / (norm_eps + acc[k]);
   }
 }
 
@@ -138,6 +143,7 @@ constexpr uint32_t OSMEM = OOFF_BAR + 256 + 1024;
 struct OuterArgs {
   __half *outer;  // [(i - i_begin) * n + j][1024]
   int n, i_begin, i_count, tiles_j, k_blocks, total_tiles;
+  int rows_b;     // residues per block of the right operand ([blocks][S][rows_b][c]): n unless sharded
   float scale;
   unsigned int *err;
 };
@@ -199,8 +205,9 @@ __global__ void __launch_bounds__(OTHREADS, 1)
           mbar_arrive_expect_tx(full(s), OSTAGE);
           // [64 s rows][64 (i, a) elements] boxes: 2 for the 128-wide A tile, 4 for the 256-wide B tile
           for (int b = 0; b < 2; ++b) tma_load_3d(dst + b * 8192, &lmap, full(s), i0 * C + b * 64, kb * OBK, 0);
+          const int jb = j0 / p.rows_b, jl = j0 - jb * p.rows_b;  // 8 residues never straddle two blocks
           for (int b = 0; b < 4; ++b)
-            tma_load_3d(dst + OA_BYTES + b * 8192, &rmap, full(s), j0 * C + b * 64, kb * OBK, 0);
+            tma_load_3d(dst + OA_BYTES + b * 8192, &rmap, full(s), jl * C + b * 64, kb * OBK, jb);
         }
       }
       for (int j = std::max(0, it - OSTAGES); j < it; ++j) mbar_wait_drain(full(j % OSTAGES), (j / OSTAGES) & 1, p.err);
@@ -286,17 +293,20 @@ __global__ void __launch_bounds__(OTHREADS, 1)
 
 using namespace opm;
 
-OpmLayout opm_layout(int64_t s, int64_t n, int64_t cm, int64_t c, int64_t cz, int64_t row_block) {
+OpmLayout opm_layout(int64_t s, int64_t n, int64_t cm, int64_t c, int64_t cz, int64_t row_block, int64_t rows,
+                     int64_t row0) {
   OpmLayout L;
   L.s = s;
   L.n = n;
+  L.rows = (rows <= 0 || rows > n) ? n : rows;
+  L.row0 = row0;
   L.cm = cm;
   L.c = c;
   L.cz = cz;
   L.cmp = align_up(cm, 64);
   // Residue block: the outer scratch stays within 256 MiB unless asked otherwise; a multiple of 4.
   int64_t rb = row_block > 0 ? row_block : std::max<int64_t>(4, (int64_t(256) << 20) / (n * c * c * 2));
-  rb = std::min<int64_t>(align_up(std::max<int64_t>(rb, 1), 4), align_up(n, 4));
+  rb = std::min<int64_t>(align_up(std::max<int64_t>(rb, 1), 4), align_up(L.rows, 4));
   L.block_rows = rb;
   int k = 0;
   while ((int64_t(1) << k) < s) ++k;
@@ -315,10 +325,11 @@ OpmLayout opm_layout(int64_t s, int64_t n, int64_t cm, int64_t c, int64_t cz, in
   L.off_wo_scale = take((size_t)o_cols * 4);
   L.off_wo_bias = take((size_t)o_cols * 4);
   L.off_ln = take((size_t)L.cmp * 2 * 4);
-  L.off_xn = take((size_t)s * n * L.cmp * 2);
-  L.off_left = take((size_t)s * n * c * 2);
-  L.off_right = take((size_t)s * n * c * 2);
-  L.off_rowscale = take((size_t)n * n * 4);
+  L.off_xn = take((size_t)s * L.rows * L.cmp * 2);
+  L.off_mask = take((size_t)s * L.rows * 4);
+  L.off_left = take((size_t)s * L.rows * c * 2);
+  L.off_right = take((size_t)s * n * c * 2);  // every rank's block [ranks][S][rows][c]
+  L.off_rowscale = take((size_t)L.rows * n * 4);
   L.off_outer = take((size_t)rb * n * c * c * 2);
   L.total = off;
   return L;
@@ -326,9 +337,10 @@ OpmLayout opm_layout(int64_t s, int64_t n, int64_t cm, int64_t c, int64_t cz, in
 
 af2_status opm_launch(af2_ctx *ctx, const OpmLayout &L, const void *m, int m_dtype, const float *mask,
                       const float *packed, double ln_eps, double norm_eps, int residual, void *out, int out_dtype,
-                      void *workspace, cudaStream_t stream) {
+                      void *workspace, cudaStream_t stream, const OpmExchange *exchange) {
   uint8_t *ws = static_cast<uint8_t *>(workspace);
-  const int64_t s = L.s, n = L.n, cm = L.cm, c = L.c, cz = L.cz;
+  const int64_t s = L.s, n = L.n, cm = L.cm, c = L.c, cz = L.cz, rows = L.rows;
+  const int rank = exchange ? exchange->rank : 0;
   // packOuterProductMeanWeights order (outer-product-mean.ts:68-72).
   const float *ln_w = packed, *ln_b = ln_w + cm, *lw = ln_b + cm, *lb = lw + cm * c, *rw = lb + c, *rb = rw + cm * c;
   const float *ow = rb + c, *ob = ow + c * c * cz;
@@ -354,23 +366,26 @@ af2_status opm_launch(af2_ctx *ctx, const OpmLayout &L, const void *m, int m_dty
                            wo_scale, stream)) != AF2_OK ||
       (st = pad_vectors(ctx, vs, stream)) != AF2_OK)
     return st;
-  // ---- LayerNorm ----
-  const int64_t rows = s * n;
+  // ---- LayerNorm of this rank's residue columns (all of them unless sharded) ----
+  const int64_t xrows = s * rows;
   __half *xn = reinterpret_cast<__half *>(ws + L.off_xn);
+  float *mask_loc = reinterpret_cast<float *>(ws + L.off_mask);
   {
     const int warps = 8;
-    const unsigned blocks = (unsigned)((rows + warps - 1) / warps);
+    const unsigned blocks = (unsigned)((xrows + warps - 1) / warps);
     LaunchScope scope(ctx, stream, kProfOpmNormalize);
     const bool vec = cm == 256 && reinterpret_cast<uintptr_t>(m) % 16 == 0;
     auto run = [&](auto tag) {
       using MT = decltype(tag);
       const MT *mp = static_cast<const MT *>(m);
       if (vec)
-        norm_kernel<MT, true><<<blocks, warps * 32, 0, stream>>>(mp, rows, (int)cm, (int)L.cmp, ln, ln + L.cmp,
-                                                                 (float)ln_eps, xn);
+        norm_kernel<MT, true><<<blocks, warps * 32, 0, stream>>>(mp, xrows, (int)cm, (int)L.cmp, ln, ln + L.cmp,
+                                                                 (float)ln_eps, xn, (int)n, (int)L.row0, (int)rows,
+                                                                 mask, mask_loc);
       else
-        norm_kernel<MT, false><<<blocks, warps * 32, 0, stream>>>(mp, rows, (int)cm, (int)L.cmp, ln, ln + L.cmp,
-                                                                  (float)ln_eps, xn);
+        norm_kernel<MT, false><<<blocks, warps * 32, 0, stream>>>(mp, xrows, (int)cm, (int)L.cmp, ln, ln + L.cmp,
+                                                                  (float)ln_eps, xn, (int)n, (int)L.row0, (int)rows,
+                                                                  mask, mask_loc);
     };
     if (m_dtype == AF2_F32)
       run(float{});
@@ -381,7 +396,8 @@ af2_status opm_launch(af2_ctx *ctx, const OpmLayout &L, const void *m, int m_dty
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(ctx, e, "OPM normalisation");
   }
-  // ---- left / right projection ----
+  // ---- left / right projection: right lands in this rank's block of the full operand ----
+  __half *right_full = reinterpret_cast<__half *>(ws + L.off_right);
   {
     LinearOperands op;
     op.a = xn;
@@ -390,37 +406,41 @@ af2_status opm_launch(af2_ctx *ctx, const OpmLayout &L, const void *m, int m_dty
     op.w = ws + L.off_wlr;
     op.scale = wlr_scale;
     op.bias = wlr_bias;
-    op.row_mask = mask;
-    op.rows = rows;
+    op.row_mask = mask_loc;
+    op.rows = xrows;
     op.cols = 2 * c;
     op.opm_projection = true;
     op.left = ws + L.off_left;
-    op.right = ws + L.off_right;
+    op.right = right_full + (size_t)rank * s * rows * c;
     op.prof = kProfOpmProject;
     if ((st = linear_launch(ctx, op, stream)) != AF2_OK) return st;
   }
-  // ---- pair counts ----
+  if (exchange && exchange->all_gather &&
+      (st = exchange->all_gather(ctx, right_full, (size_t)s * rows * c * sizeof(__half), stream)) != AF2_OK)
+    return st;
+  // ---- pair counts of this rank's rows ----
   float *rowscale = reinterpret_cast<float *>(ws + L.off_rowscale);
   {
     LaunchScope scope(ctx, stream, kProfOpmCount);
-    const dim3 grid((unsigned)((n + 31) / 32), (unsigned)((n + 31) / 32));
-    count_kernel<<<grid, 256, 0, stream>>>(mask, (int)s, (int)n, (float)norm_eps, rowscale);
+    const dim3 grid((unsigned)((n + 31) / 32), (unsigned)((rows + 31) / 32));
+    count_kernel<<<grid, 256, 0, stream>>>(mask, (int)s, (int)n, (int)L.row0, (int)rows, (float)norm_eps, rowscale);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(ctx, e, "OPM pair counts");
   }
-  // ---- outer products and output projection, block by block ----
+  // ---- outer products and output projection, block by block of this rank's rows ----
+  const int64_t blocks_b = n / rows;  // blocks of the right operand
   CUtensorMap lmap, rmap;
-  if (!encode_map_3d(&lmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, ws + L.off_left, n * c, s, 1, n * c * 2,
-                     (uint64_t)s * n * c * 2, 64, 64, 1, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !encode_map_3d(&rmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, ws + L.off_right, n * c, s, 1, n * c * 2,
-                     (uint64_t)s * n * c * 2, 64, 64, 1, CU_TENSOR_MAP_SWIZZLE_128B))
+  if (!encode_map_3d(&lmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, ws + L.off_left, rows * c, s, 1, rows * c * 2,
+                     (uint64_t)s * rows * c * 2, 64, 64, 1, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_map_3d(&rmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, right_full, rows * c, s, blocks_b, rows * c * 2,
+                     (uint64_t)s * rows * c * 2, 64, 64, 1, CU_TENSOR_MAP_SWIZZLE_128B))
     return fail(ctx, AF2_ERR_CUDA, "cuTensorMapEncodeTiled failed for the OPM operands");
   cudaError_t e = cudaFuncSetAttribute(outer_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, OSMEM);
   if (e != cudaSuccess) return cuda_fail(ctx, e, "outer kernel attributes");
   __half *outer = reinterpret_cast<__half *>(ws + L.off_outer);
   const size_t ob_bytes = out_dtype == AF2_F32 ? 4 : 2;
-  for (int64_t i0 = 0; i0 < n; i0 += L.block_rows) {
-    const int64_t ic = std::min<int64_t>(L.block_rows, n - i0);
+  for (int64_t i0 = 0; i0 < rows; i0 += L.block_rows) {
+    const int64_t ic = std::min<int64_t>(L.block_rows, rows - i0);
     OuterArgs a{};
     a.outer = outer;
     a.n = (int)n;
@@ -429,6 +449,7 @@ af2_status opm_launch(af2_ctx *ctx, const OpmLayout &L, const void *m, int m_dty
     a.tiles_j = (int)((n + 7) / 8);
     a.k_blocks = (int)((s + OBK - 1) / OBK);
     a.total_tiles = (int)((ic + 3) / 4) * a.tiles_j;
+    a.rows_b = (int)rows;
     a.scale = std::ldexp(1.f, -L.out_shift);
     a.err = ctx->err_word;
     {

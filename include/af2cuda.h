@@ -220,6 +220,20 @@ AF2_API af2_status af2_triangle_multiplication_sharded(af2_ctx *ctx, int directi
                                                        double epsilon, const af2_triangle_options *options,
                                                        void *out, int out_dtype, void *stream);
 
+/*
+ * The device form of the outer-product mean on a row-sharded pair: m [S, N,
+ * c_m] and mask [S, N] are the whole MSA (every rank passes the same), out
+ * holds this rank's rows [rank * L, (rank + 1) * L) of the [N, N, c_z] update
+ * (L = N / nranks, a multiple of 8).  Each rank normalises and projects only
+ * its own residues; the right operand is all-gathered.  Collective.
+ */
+struct af2_opm_shape;
+struct af2_opm_options;
+AF2_API af2_status af2_outer_product_mean_sharded(af2_ctx *ctx, const struct af2_opm_shape *shape, const void *m,
+                                                  int m_dtype, const float *mask, const float *packed_weights,
+                                                  int64_t weight_count, const struct af2_opm_options *options,
+                                                  void *out, int out_dtype, void *stream);
+
 /* ---- weights: f32 or mixed-q8 ------------------------------------------ */
 
 typedef enum af2_weight_format {

@@ -1,6 +1,7 @@
-"""Row-sharded triangle multiplication on 2+ GPUs (one process per GPU, the
-library's NCCL communicator): every rank's rows must be bit-identical to the
-single-GPU result.  Skipped on boxes with fewer than two GPUs."""
+"""Row-sharded triangle multiplication and outer-product mean on 2+ GPUs (one
+process per GPU, the library's NCCL communicator): every rank's rows must be
+bit-identical to the single-GPU result.  Skipped on boxes with fewer than two
+GPUs."""
 import datetime
 import os
 import socket
@@ -67,6 +68,19 @@ def _worker(rank, nranks, port, result):
                                                                residual=False)
         dev.sync()
         ok &= bool(torch.equal(out_rows, ref[r0:r1]))
+        # outer-product mean of a whole MSA into this rank's pair rows
+        from test_opm_gpu import opm_case, opm_packed
+        m, msa_mask, wo = opm_case(40, n, 64, cz=128, seed=4)
+        msa = torch.from_numpy(m).to("cuda", torch.bfloat16)
+        msa_mask_d = torch.from_numpy(msa_mask).cuda()
+        pw = torch.from_numpy(opm_packed(wo)).cuda()
+        pair_full = torch.from_numpy(z).to("cuda", torch.bfloat16)
+        pair_rows = pair_full[r0:r1].clone()
+        torch.cuda.synchronize()
+        af2cuda.encode_outer_product_mean_tensors(dev, msa, msa_mask_d, pw, 32, 128, pair=pair_full, residual=True)
+        af2cuda.encode_outer_product_mean_sharded_tensors(dev, msa, msa_mask_d, pw, 32, 128, pair_rows, residual=True)
+        dev.sync()
+        ok &= bool(torch.equal(pair_rows, pair_full[r0:r1]))
         af2cuda.comm_destroy(dev)
     finally:
         dev.close()
@@ -74,7 +88,7 @@ def _worker(rank, nranks, port, result):
     result[rank] = int(ok)
 
 
-def test_sharded_triangle_is_bit_identical():
+def test_sharded_pair_ops_are_bit_identical():
     import torch
     import torch.multiprocessing as mp
     count = torch.cuda.device_count()
