@@ -22,8 +22,13 @@ read back, every step.
 (the reference is TypeScript and no JavaScript runtime exists on this box) on
 a bounded sample of the same block, with every host thread.
 
-Multi-GPU (torchrun): every rank runs its own independent block (replicas,
-weak scaling); value sums the work of all ranks over the max-over-ranks time.
+Multi-GPU (torchrun, one process per GPU): the same N=1024 block with the
+pair sharded by rows across the ranks (strong scaling).  The library's NCCL
+communicator all-gathers the projected b operand of the outgoing triangle and
+transposes the pair across ranks (all-to-all) for the incoming one; the OPM
+projects each rank's residues and all-gathers the right operand; the
+transition is row-local.  value = the block's FLOPs over the max-over-ranks
+time.
 """
 from __future__ import annotations
 
@@ -50,7 +55,7 @@ METRIC = "Evoformer pair-GEMM TFLOP/s & ms/block at N=1024; % of B200 bf16 TC pe
 KERNEL_DRAM_BYTES = {"triangle.contract": 771_527_680}
 KERNELS = ("weights.prepare", "triangle.prepare", "triangle.relayout", "triangle.project", "triangle.contract",
            "triangle.output", "opm.normalize", "opm.project", "opm.count", "opm.outer", "opm.output",
-           "transition.prepare", "transition.fused")
+           "transition.prepare", "transition.fused", "shard.transpose")
 
 
 def triangle_flops(n: int, cz: int = CZ, ch: int = CH) -> float:
@@ -75,15 +80,17 @@ def block_flops(n: int = N, s: int = S_MSA) -> float:
     return 2 * triangle_flops(n) + opm_flops(n, s) + transition_flops(n)
 
 
-def kernel_flops(name: str, n: int = N, s: int = S_MSA, opm_blocks: int = 1) -> float | None:
-    """Algorithmic FLOPs of one launch of a tensor-core kernel of the block."""
-    return {"triangle.contract": contraction_flops(n),
-            "triangle.project": 2.0 * n * n * CZ * 4 * CH,
-            "triangle.output": 2.0 * n * n * (CH * CZ + CZ * CZ),
-            "opm.outer": 2.0 * (n * C_OUTER) ** 2 * s / opm_blocks,
-            "opm.output": 2.0 * n * n * C_OUTER * C_OUTER * CZ / opm_blocks,
-            "opm.project": 2.0 * s * n * CM * 2 * C_OUTER,
-            "transition.fused": transition_flops(n)}.get(name)
+def kernel_step_flops(name: str, world: int = 1, n: int = N, s: int = S_MSA) -> float | None:
+    """Algorithmic FLOPs one rank's launches of a tensor-core kernel do per block
+    (each rank does 1/world of every operator on a row-sharded pair)."""
+    per_block = {"triangle.contract": 2 * contraction_flops(n),
+                 "triangle.project": 2 * 2.0 * n * n * CZ * 4 * CH,
+                 "triangle.output": 2 * 2.0 * n * n * (CH * CZ + CZ * CZ),
+                 "opm.outer": 2.0 * (n * C_OUTER) ** 2 * s,
+                 "opm.output": 2.0 * n * n * C_OUTER * C_OUTER * CZ,
+                 "opm.project": 2.0 * s * n * CM * 2 * C_OUTER,
+                 "transition.fused": transition_flops(n)}.get(name)
+    return None if per_block is None else per_block / world
 
 
 def measured_peaks() -> dict:
@@ -278,10 +285,16 @@ def run_ours(args) -> None:
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
     sh = stream.cuda_stream
-    rng = np.random.default_rng(1234 + rank)
+    sharded = world > 1
+    rows = N // world
+    if sharded:
+        uid = [af2cuda.comm_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        af2cuda.comm_init(dev, uid[0], world, rank)
+    rng = np.random.default_rng(1234)
     gen = torch.Generator(device="cuda").manual_seed(1234 + rank)
-    pair = torch.randn(N, N, CZ, device="cuda", generator=gen).to(torch.bfloat16)
-    mask = torch.ones(N, N, device="cuda")
+    pair = torch.randn(rows, N, CZ, device="cuda", generator=gen).to(torch.bfloat16)
+    mask = torch.ones(rows, N, device="cuda")
     msa = torch.randn(S_MSA, N, CM, device="cuda", generator=gen).to(torch.bfloat16)
     msa_mask = (torch.rand(S_MSA, N, device="cuda", generator=gen) < 0.9).float()
     msa_mask[0] = 1
@@ -294,14 +307,21 @@ def run_ours(args) -> None:
            "firstBias": torch.from_numpy(tw["b1"]).cuda(),
            "secondWeight": af2cuda.Q8Matrix(torch.from_numpy(tw["w2"][0]).cuda(), torch.from_numpy(tw["w2"][1]).cuda()),
            "secondBias": torch.from_numpy(tw["b2"]).cuda()}
-    pair_rows = pair.view(N * N, CZ)
+    pair_rows = pair.view(rows * N, CZ)
     torch.cuda.synchronize()
 
     def step():
-        af2cuda.encode_outer_product_mean_tensors(dev, msa, msa_mask, w_opm, C_OUTER, CZ, pair=pair, residual=True,
-                                                  stream=sh)
-        af2cuda.encode_triangle_multiplication_tensors(dev, 0, pair, mask, w_out, residual=True, stream=sh)
-        af2cuda.encode_triangle_multiplication_tensors(dev, 1, pair, mask, w_in, residual=True, stream=sh)
+        if sharded:
+            af2cuda.encode_outer_product_mean_sharded_tensors(dev, msa, msa_mask, w_opm, C_OUTER, CZ, pair,
+                                                              residual=True, stream=sh)
+            for d, w in ((0, w_out), (1, w_in)):
+                af2cuda.encode_triangle_multiplication_sharded_tensors(dev, d, pair, mask, w, N, residual=True,
+                                                                       stream=sh)
+        else:
+            af2cuda.encode_outer_product_mean_tensors(dev, msa, msa_mask, w_opm, C_OUTER, CZ, pair=pair,
+                                                      residual=True, stream=sh)
+            af2cuda.encode_triangle_multiplication_tensors(dev, 0, pair, mask, w_out, residual=True, stream=sh)
+            af2cuda.encode_triangle_multiplication_tensors(dev, 1, pair, mask, w_in, residual=True, stream=sh)
         af2cuda.encode_transition_tensors(dev, pair_rows, tws, residual=True, stream=sh)
 
     for _ in range(max(args.warmup, 3)):
@@ -332,7 +352,7 @@ def run_ours(args) -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     flops_step = block_flops()
-    value = world * flops_step * args.steps / (ms * 1e-3) / 1e12
+    value = flops_step * args.steps / (ms * 1e-3) / 1e12  # the block's work, shared by the ranks
     peaks = measured_peaks()
 
     # ---- per-kernel device times (CUDA events around each launch, a separate profiled pass) ----
@@ -355,18 +375,19 @@ def run_ours(args) -> None:
         k["share"] = k["ms_per_step"] / total_kernel_ms
 
     # ---- roofline of the dominant kernel ----
-    opm_blocks = int(round(kernel.get("opm.outer", {}).get("launches_per_step", 1)))
-    tensor = {k: v for k, v in kernel.items() if kernel_flops(k, opm_blocks=opm_blocks) is not None}
+    tensor = {k: v for k, v in kernel.items() if kernel_step_flops(k, world) is not None}
     dom = max(tensor, key=lambda k: tensor[k]["ms_per_step"])
-    fl = kernel_flops(dom, opm_blocks=opm_blocks)
-    achieved = fl / (tensor[dom]["avg_us"] * 1e-6) / 1e12
+    step_fl = kernel_step_flops(dom, world)
+    achieved = step_fl / (tensor[dom]["ms_per_step"] * 1e-3) / 1e12
+    per_launch = step_fl / tensor[dom]["launches_per_step"]
+    traffic = KERNEL_DRAM_BYTES.get(dom) if world == 1 else None
     roofline = {"kernel": dom, "bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
-                "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"], "traffic": KERNEL_DRAM_BYTES.get(dom),
-                "peak_source": f"{peaks['source']} burst bf16", "flops_per_launch": fl,
+                "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"], "traffic": traffic,
+                "peak_source": f"{peaks['source']} burst bf16", "flops_per_launch": per_launch,
                 "avg_launch_us": tensor[dom]["avg_us"]}
 
     # ---- e2e: the public device-form API, inputs copied in from pinned host memory every step ----
-    host_pair = torch.empty(N, N, CZ, dtype=torch.bfloat16, pin_memory=True)
+    host_pair = torch.empty(rows, N, CZ, dtype=torch.bfloat16, pin_memory=True)
     host_pair.copy_(pair.cpu())
     host_msa = torch.empty(S_MSA, N, CM, dtype=torch.bfloat16, pin_memory=True)
     host_msa.copy_(msa.cpu())
@@ -393,11 +414,12 @@ def run_ours(args) -> None:
         t = torch.tensor([e2e_ms], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
-    e2e = {"value": world * flops_step * e2e_steps / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+    e2e = {"value": flops_step * e2e_steps / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
            "h2d_bytes_per_step": host_pair.numel() * 2 + host_msa.numel() * 2,
            "d2h_bytes_per_step": host_out.numel() * 2, "ms_per_step": e2e_ms / e2e_steps,
-           "path": "pair and MSA copied in from pinned host memory, the block through the af2cuda device-form "
-                   "API (af2_outer_product_mean, af2_triangle_multiplication x2, af2_transition), pair read back"}
+           "path": "pair (this rank's rows) and MSA copied in from pinned host memory, the block through the "
+                   "af2cuda device-form API (outer product mean, triangle multiplication x2, transition; the "
+                   "row-sharded forms on several GPUs), pair rows read back"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -411,7 +433,8 @@ def run_ours(args) -> None:
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "scaling": "strong" if world > 1 else "weak",
             "vs_baseline": None, "dtype": "f16", "data": "synthetic",
             "config": {"workload": "one Evoformer block's pair GEMM set at N=1024 (OPM of an S=512, c_m=256 MSA "
                                    "into the pair, triangle multiplication outgoing + incoming with c_z=c_hidden="
@@ -422,13 +445,18 @@ def run_ours(args) -> None:
                        "gflop_per_block": {"triangle": 2 * triangle_flops(N) / 1e9, "opm": opm_flops(N) / 1e9,
                                            "transition": transition_flops(N) / 1e9},
                        "l2": "inputs larger than L2 (pair 268 MB, MSA 268 MB, bf16), no flush",
-                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
+                       "parallelism": (f"pair rows sharded x{world} (NCCL all-gather of the projected b and "
+                                       "the OPM right operand, all-to-all pair transposes)") if world > 1
+                       else "single GPU"},
             "ms_per_block": ms / args.steps,
             "pct_of_peak": value / world / peaks["bf16_tflops"],
+            "per_gpu_tflops": value / world,
             "roofline": roofline, "kernels": kernel, "cpu_baseline": cpu, "e2e": e2e,
             "gpu_launches": int(launches), "clocks": clocks.record(),
         }
         print(json.dumps(line), flush=True)
+    if sharded:
+        af2cuda.comm_destroy(dev)
     if dist:
         dist.destroy_process_group()
     dev.close()
