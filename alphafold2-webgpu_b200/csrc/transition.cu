@@ -11,12 +11,12 @@
 //
 // Kernel (one CTA per SM, 128-row tiles, persistent):
 //   warp 0      TMA: the x tile (16-bit, straight into the first GEMM's A
-//               operand) and the weight chunks through a 4-deep ring;
-//   warp 1      tcgen05 issue over one continuous stream of 64-wide hidden
-//               chunks j (all tiles of the CTA back to back): D1[j%4] =
-//               xn W1[:, chunk], and three chunks behind it, D2[tile] +=
-//               H[j-3] W2[chunk j-3, :] -- so the tensor pipe always has three
-//               first-GEMM chunks queued while the epilogue turns a finished
+//               operand) and the weight chunks through a 2-deep ring;
+//   warp 1      tcgen05 issue over one continuous stream of 128-wide hidden
+//               chunks j (all tiles of the CTA back to back): D1[j%2] =
+//               xn W1[:, chunk], and one chunk behind it, D2[tile] +=
+//               H[j-1] W2[chunk j-1, :] -- so the tensor pipe has the next
+//               first-GEMM chunk queued while the epilogue turns a finished
 //               one into the second GEMM's operand;
 //   warps 2-5   row warps: LayerNorm of the next x tile in place (one
 //               thread per row), then the second epilogue of this tile:

@@ -10,9 +10,10 @@
 //     (a_p, a_g, b_p, b_g) as one tcgen05 GEMM per 64-pair tile, computed
 //     transposed (D[h][pair] = W[h][:] . zn[pair][:]) so that a TMEM lane is a
 //     hidden channel and the gated result a = mask (p + b_p) sigmoid(g + b_g)
-//     is stored channel-major [h][row][k] with 16-byte vector stores.  The
+//     is stored row-major [row][h][k] with 16-byte vector stores, so the rows
+//     one rank of a row-sharded pair projects form one contiguous block.  The
 //     incoming direction reads z in transposed pair order, so its operands
-//     come out as a'[h][j][k] = a[k][j] and the contraction below is the same
+//     come out as a'[j][h][k] = a[k][j] and the contraction below is the same
 //     NT GEMM for both directions.
 //  2. contract -- per hidden channel h, X[h] = (1/N) A[h] B[h]^T with TMA-fed
 //     128x256x64 tiles, a 4-deep mbarrier pipeline and two TMEM accumulators

@@ -52,7 +52,7 @@ HIDDEN = 4 * CZ
 METRIC = "Evoformer pair-GEMM TFLOP/s & ms/block at N=1024; % of B200 bf16 TC peak"
 # dram__bytes_read.sum + dram__bytes_write.sum per launch, from ncu captures of
 # this workload (profiles/*.md); kernels without a capture report null.
-KERNEL_DRAM_BYTES = {"triangle.contract": 771_527_680}
+KERNEL_DRAM_BYTES = {"triangle.contract": 771_527_680, "opm.outer": 268_619_520}
 KERNELS = ("weights.prepare", "triangle.prepare", "triangle.relayout", "triangle.project", "triangle.contract",
            "triangle.output", "opm.normalize", "opm.project", "opm.count", "opm.outer", "opm.output",
            "transition.prepare", "transition.fused", "shard.transpose")
@@ -224,18 +224,24 @@ def cpu_block_rate(n: int, s: int, threads: int) -> tuple[float, float, str]:
                                                "transition), f64-accumulating CPU port")
 
 
+def cpu_sample_size(threads: int, seconds: float, smallest: int = 64) -> tuple[int, int]:
+    """Pair length and MSA depth (S = N/2) of a CPU block sample that takes about
+    `seconds`, from a calibration run at N=64, S=32 (block FLOPs grow as N^3)."""
+    rate, _, _ = cpu_block_rate(64, 32, threads)
+    budget = rate * 1e12 * seconds
+    n = smallest
+    while n < N and block_flops(n + 16, (n + 16) // 2) <= budget:
+        n += 16
+    return n, n // 2
+
+
 def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     threads = os.cpu_count() or 1
     # Size each step's sample so that warm-up plus timed steps take about a minute.
-    rate, _, _ = cpu_block_rate(64, 32, threads)
-    budget_flops = rate * 1e12 * 60.0 / max(1, args.steps + args.warmup)
-    sample_n = 48
-    while sample_n < N and block_flops(sample_n + 16, sample_n // 2 + 8) <= budget_flops:
-        sample_n += 16
-    sample_s = sample_n // 2
+    sample_n, sample_s = cpu_sample_size(threads, 60.0 / max(1, args.steps + args.warmup), smallest=48)
     for _ in range(args.warmup):
         cpu_block_rate(sample_n, sample_s, threads)
     rates, secs = [], []
@@ -424,7 +430,7 @@ def run_ours(args) -> None:
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
-        rate, secs, desc = cpu_block_rate(128, 64, threads)
+        rate, secs, desc = cpu_block_rate(*cpu_sample_size(threads, 15.0), threads)
         cpu = {"value": rate, "unit": "TFLOP/s", "cores": threads, "kind": "port",
                "sample": f"{desc} ({secs:.1f} s)"}
 
