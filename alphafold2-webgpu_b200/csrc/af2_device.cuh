@@ -210,6 +210,68 @@ __device__ __forceinline__ void mma_f16_acc(uint32_t d_tmem, uint64_t adesc, uin
                : "memory");
 }
 
+// D[tmem] (+)= A[tmem] * B[smem]^T: A is 128 lanes x 16 f16 (8 columns of
+// packed pairs, the lower K element in the low half), K-major.
+__device__ __forceinline__ void mma_f16_ts_first(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc) {
+  asm volatile("tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, 0;" ::"r"(d_tmem), "r"(a_tmem), "l"(bdesc),
+               "r"(idesc)
+               : "memory");
+}
+__device__ __forceinline__ void mma_f16_ts_acc(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc) {
+  asm volatile("tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, 1;" ::"r"(d_tmem), "r"(a_tmem), "l"(bdesc),
+               "r"(idesc)
+               : "memory");
+}
+
+// ---- warp-wide MMA issue ----------------------------------------------------
+// The whole issuing warp runs the MMA loop with warp-uniform control flow and
+// operands, and one lane elected inside each instruction issues it.  With the
+// loop in a single lane (a divergent branch) the descriptors cannot live in
+// uniform registers and every MMA pays for moving them there: measured on B200,
+// M=128 MMAs issue at 100-180 clk each that way, against 48 / 64 / 128 clk (the
+// tensor core's own rate at N = 64 / 128 / 256) from a uniform warp.
+
+// This thread's warp index, provably warp-uniform to the compiler.
+__device__ __forceinline__ int warp_index_uniform() { return __shfl_sync(0xffffffffu, (int)(threadIdx.x >> 5), 0); }
+
+// D[tmem] (+)= A[smem] B[smem]^T from one elected lane of a converged warp.
+__device__ __forceinline__ void umma_first(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\telect.sync _|p, 0xffffffff;\n\t"
+      "@p tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, 0;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc)
+      : "memory");
+}
+__device__ __forceinline__ void umma_acc(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\telect.sync _|p, 0xffffffff;\n\t"
+      "@p tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, 1;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc)
+      : "memory");
+}
+// The same with A in TMEM (128 lanes x 16 f16, packed pairs, K-major).
+__device__ __forceinline__ void umma_ts_first(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\telect.sync _|p, 0xffffffff;\n\t"
+      "@p tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, 0;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc)
+      : "memory");
+}
+__device__ __forceinline__ void umma_ts_acc(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\telect.sync _|p, 0xffffffff;\n\t"
+      "@p tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, 1;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc)
+      : "memory");
+}
+// tcgen05.commit from one elected lane: one arrival on `bar` when every MMA this warp issued has completed.
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\telect.sync _|p, 0xffffffff;\n\t"
+      "@p tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(bar)
+      : "memory");
+}
+
 // A shared-memory descriptor moved by `bytes` (a multiple of 16): the start
 // address field is address >> 4 in the low 14 bits, and every shared address
 // is below 2^18, so the add never carries out of the field.
@@ -246,6 +308,21 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
 }
 
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// 32 lanes x 32 consecutive 32-bit columns stored: thread t writes lane (base lane + t).
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0],"
+      " {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16,"
+      " %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // Shared-memory matrix descriptor for a K-major operand tile in the 128-byte
 // swizzled layout: rows of 64 16-bit elements (128 B), groups of 8 rows 1024 B
@@ -403,6 +480,71 @@ __device__ __forceinline__ float2 unpack2<__half>(uint32_t w) {
 template <>
 __device__ __forceinline__ float2 unpack2<__nv_bfloat16>(uint32_t w) {
   return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+
+// Two f32 values rounded to a packed pair of 16-bit outputs (low half first).
+template <typename OT>
+__device__ __forceinline__ uint32_t pack2_t(float lo, float hi);
+template <>
+__device__ __forceinline__ uint32_t pack2_t<__half>(float lo, float hi) {
+  return pack_half2(lo, hi);
+}
+template <>
+__device__ __forceinline__ uint32_t pack2_t<__nv_bfloat16>(float lo, float hi) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t *>(&h);
+}
+
+// Writes y into columns [c0, c0 + 32) of an output row, or with `residual`
+// adds y to what is there (in f32, rounded once).  Whole 32-column chunks of
+// 16-byte aligned rows (`vector`) use 16-byte accesses; otherwise elements
+// past `cols` are left alone.
+template <typename OT>
+__device__ __forceinline__ void store_out32(OT *orow, int c0, int cols, const float (&y)[32], bool vector,
+                                            bool residual) {
+  if (vector && c0 + 32 <= cols) {
+    if constexpr (sizeof(OT) == 4) {
+      float4 *o4 = reinterpret_cast<float4 *>(orow + c0);
+#pragma unroll
+      for (int w = 0; w < 8; ++w) {
+        float4 val = make_float4(y[4 * w], y[4 * w + 1], y[4 * w + 2], y[4 * w + 3]);
+        if (residual) {
+          const float4 r = o4[w];
+          val.x += r.x;
+          val.y += r.y;
+          val.z += r.z;
+          val.w += r.w;
+        }
+        o4[w] = val;
+      }
+    } else {
+      uint4 *o4 = reinterpret_cast<uint4 *>(orow + c0);
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        float v8[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v8[i] = y[8 * w + i];
+        if (residual) {
+          const uint4 r = o4[w];
+          const uint32_t rw[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 f = unpack2<OT>(rw[i]);
+            v8[2 * i] += f.x;
+            v8[2 * i + 1] += f.y;
+          }
+        }
+        o4[w] = make_uint4(pack2_t<OT>(v8[0], v8[1]), pack2_t<OT>(v8[2], v8[3]), pack2_t<OT>(v8[4], v8[5]),
+                           pack2_t<OT>(v8[6], v8[7]));
+      }
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const int col = c0 + i;
+      if (col < cols) orow[col] = from_f32<OT>(residual ? to_f32<OT>(orow[col]) + y[i] : y[i]);
+    }
+  }
 }
 
 }  // namespace af2

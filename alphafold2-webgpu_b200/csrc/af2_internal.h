@@ -43,6 +43,7 @@ enum ProfileKernel {
   kProfOpmOuter,
   kProfOpmOutput,
   kProfShardTranspose,
+  kProfOpmFused,
   kProfCount
 };
 const char *profile_name(int id);
@@ -176,6 +177,9 @@ struct LinearOperands {
   int relu = 0, residual = 0;
   bool opm_projection = false;    // columns [0, cols/2) -> left, the rest -> right (f16), times row_mask
   void *left = nullptr, *right = nullptr;
+  // seq_pitch > 0: rows are m = i * kmajor_seqs + s, and left / right are written
+  // sequence-contiguous: left [cols / 2][kmajor_rows][seq_pitch], right [rows][cols / 2][seq_pitch]
+  int64_t kmajor_rows = 0, kmajor_seqs = 0, seq_pitch = 0;
   int prof = kProfLinear;
 };
 
@@ -228,6 +232,8 @@ struct OpmLayout {
   int64_t block_rows = 0;   // residues i per output block (a multiple of 4)
   int out_shift = 0;        // outer is stored times 2^-out_shift (2^out_shift >= S)
   size_t off_wlr = 0, off_wlr_scale = 0, off_wlr_bias = 0, off_wo = 0, off_wo_scale = 0, off_wo_bias = 0;
+  bool fused = false;        // outer product and output projection in one kernel (no outer scratch)
+  int64_t seq_pitch = 0;    // fused: left [c][rows][seq_pitch] and right [n][c][seq_pitch], K-major
   size_t off_ln = 0, off_xn = 0, off_mask = 0, off_left = 0, off_right = 0, off_rowscale = 0, off_outer = 0;
   size_t total = 0;
 };

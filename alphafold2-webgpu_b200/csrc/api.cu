@@ -56,7 +56,7 @@ const char *profile_name(int id) {
       "triangle.output",     "transition.prepare",   "transition.normalize", "transition.fused",
       "q8.decode",           "weights.prepare",      "activations.convert",  "linear",
       "opm.normalize",       "opm.project",          "opm.count",         "opm.outer",
-      "opm.output",          "shard.transpose"};
+      "opm.output",          "shard.transpose",      "opm.fused"};
   return (id >= 0 && id < kProfCount) ? names[id] : nullptr;
 }
 

@@ -34,6 +34,7 @@ struct LinearArgs {
   const float *row_mask;      // OPM projection: mask per row
   void *out;                  // LINEAR: [rows][ldo] of OT
   __half *left, *right;       // OPM projection: [rows][half_cols] each
+  int64_t kmajor_rows, kmajor_seqs, seq_pitch;  // seq_pitch > 0: rows m = i * seqs + s, outputs sequence-contiguous
   int64_t rows, ldo;
   int cols, half_cols, k_blocks, tiles_m, tiles_n, total_tiles, bn;
   int relu, residual;
@@ -42,22 +43,6 @@ struct LinearArgs {
 };
 
 enum { kModeLinear = 0, kModeOpmProjection = 1 };
-
-template <typename OT>
-__device__ __forceinline__ uint32_t pack2_t(float lo, float hi);
-template <>
-__device__ __forceinline__ uint32_t pack2_t<__half>(float lo, float hi) {
-  return pack_half2(lo, hi);
-}
-template <>
-__device__ __forceinline__ uint32_t pack2_t<__nv_bfloat16>(float lo, float hi) {
-  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
-  return *reinterpret_cast<uint32_t *>(&h);
-}
-template <>
-__device__ __forceinline__ uint32_t pack2_t<float>(float, float) {
-  return 0;
-}
 
 template <typename OT, int MODE>
 __global__ void __launch_bounds__(THREADS, 1)
@@ -194,6 +179,18 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (MODE == kModeOpmProjection) {
           // columns [0, half) -> left, [half, 2 half) -> right, both scaled by the mask;
           // half is 32, so a chunk is one whole left or right row: 4 x 16-byte stores.
+          if (p.seq_pitch) {
+            // K-major operands of the outer products, sequences contiguous: row m = (i, s) ->
+            // left[a][i][s], right[i][b][s], one channel per store; the lanes of a warp hold
+            // consecutive sequences, so a store covers 64 contiguous bytes
+            const int64_t i = m / p.kmajor_seqs, sq = m - i * p.kmajor_seqs;
+            const bool is_left = c0 < p.half_cols;
+            __half *dst = is_left ? p.left + i * p.seq_pitch + sq : p.right + i * p.half_cols * p.seq_pitch + sq;
+            const int64_t stride = is_left ? p.kmajor_rows * p.seq_pitch : p.seq_pitch;
+#pragma unroll
+            for (int k = 0; k < 32; ++k) dst[k * stride] = __float2half_rn(y[k] * rs);
+            continue;
+          }
           __half *dst = (c0 < p.half_cols ? p.left : p.right) + m * p.half_cols;
           uint32_t pk[16];
 #pragma unroll
@@ -205,50 +202,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           OT *orow = static_cast<OT *>(p.out) + m * p.ldo;
 #pragma unroll
           for (int i = 0; i < 32; ++i) y[i] = (p.relu ? fmaxf(y[i], 0.f) : y[i]) * rs;
-          if (p.vector_out && c0 + 32 <= p.cols) {
-            // 32 contiguous outputs of this row: 16-byte loads (residual) and stores
-            if constexpr (sizeof(OT) == 4) {
-              float4 *o4 = reinterpret_cast<float4 *>(orow + c0);
-#pragma unroll
-              for (int w = 0; w < 8; ++w) {
-                float4 val = make_float4(y[4 * w], y[4 * w + 1], y[4 * w + 2], y[4 * w + 3]);
-                if (p.residual) {
-                  const float4 r = o4[w];
-                  val.x += r.x;
-                  val.y += r.y;
-                  val.z += r.z;
-                  val.w += r.w;
-                }
-                o4[w] = val;
-              }
-            } else {
-              uint4 *o4 = reinterpret_cast<uint4 *>(orow + c0);
-#pragma unroll
-              for (int w = 0; w < 4; ++w) {
-                float v8[8];
-#pragma unroll
-                for (int i = 0; i < 8; ++i) v8[i] = y[8 * w + i];
-                if (p.residual) {
-                  const uint4 r = o4[w];
-                  const uint32_t rw[4] = {r.x, r.y, r.z, r.w};
-#pragma unroll
-                  for (int i = 0; i < 4; ++i) {
-                    const float2 f = unpack2<OT>(rw[i]);
-                    v8[2 * i] += f.x;
-                    v8[2 * i + 1] += f.y;
-                  }
-                }
-                o4[w] = make_uint4(pack2_t<OT>(v8[0], v8[1]), pack2_t<OT>(v8[2], v8[3]), pack2_t<OT>(v8[4], v8[5]),
-                                   pack2_t<OT>(v8[6], v8[7]));
-              }
-            }
-          } else {
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const int col = c0 + i;
-              if (col < p.cols) orow[col] = from_f32<OT>(p.residual ? to_f32<OT>(orow[col]) + y[i] : y[i]);
-            }
-          }
+          store_out32<OT>(orow, c0, p.cols, y, p.vector_out, p.residual);
         }
       }
       tc_fence_before();
@@ -494,6 +448,9 @@ af2_status linear_launch(af2_ctx *ctx, const LinearOperands &op, cudaStream_t st
   a.out = op.out;
   a.left = static_cast<__half *>(op.left);
   a.right = static_cast<__half *>(op.right);
+  a.kmajor_rows = op.kmajor_rows;
+  a.kmajor_seqs = op.kmajor_seqs;
+  a.seq_pitch = op.seq_pitch;
   a.rows = op.rows;
   a.ldo = op.ldo;
   a.cols = (int)op.cols;

@@ -13,6 +13,11 @@
 //   project    the shared tcgen05 GEMM: LN(m) [W_left | W_right], bias, times
 //              the row's mask, split into left and right, f16 [S][N][c]
 //   count      1 / (norm_eps + sum_s mask[s,i] mask[s,j]) per pair
+//   fused      (S <= 1024, c_z <= 128) the outer products and the output
+//              projection in one kernel, the outer products kept on chip; the
+//              normalisation then orders rows residue-major and the
+//              projection writes left [c][N][S] and right [N][c][S], so both
+//              operands are K-major (sequences contiguous); otherwise,
 //   per residue block of output rows i:
 //     outer    tcgen05 GEMM over s with both operands read MN-major straight
 //              from the [S][N*c] layouts: a 128 x 256 tile is 4 residues i x
@@ -42,12 +47,13 @@ constexpr int C = 32;  // outer channels c: the outer tile maps 32 channels to 3
 template <typename MT, bool VEC>
 __global__ void norm_kernel(const MT *__restrict__ m, int64_t rows, int cm, int cmp, const float *__restrict__ gamma,
                             const float *__restrict__ beta, float eps, __half *__restrict__ xn, int n_full, int col0,
-                            int cols, const float *__restrict__ mask_in, float *__restrict__ mask_out) {
-  // local row (s, j) of the residue columns [col0, col0 + cols) of an [S][n_full] MSA
+                            int cols, int seqs, const float *__restrict__ mask_in, float *__restrict__ mask_out) {
+  // local row of the residue columns [col0, col0 + cols) of an [S][n_full] MSA:
+  // row = s * cols + j, or with seqs > 0 (residue-major order) row = j * seqs + s
   const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
-  const int64_t src = (row / cols) * n_full + col0 + row % cols;
+  const int64_t src = seqs > 0 ? (row % seqs) * n_full + col0 + row / seqs : (row / cols) * n_full + col0 + row % cols;
   if (lane == 0) mask_out[row] = mask_in[src];
   const MT *xr = m + src * cm;
   float v[8];
@@ -289,6 +295,334 @@ __global__ void __launch_bounds__(OTHREADS, 1)
   }
 }
 
+// ---- the outer products and the output projection in one kernel ----
+// A tile is 128 residues i (the TMEM lanes) x 2 residues j.  For each outer
+// channel a (a "slice") the tensor core forms
+//   D1[i][(j, b)] = sum_s left[a][i][s] right[j][b][s]      (M 128, N 64, K S)
+// with left streamed through a ring and the tile's right operand resident in
+// shared memory, both K-major (sequences contiguous: MN-major operands run the
+// tensor core several times slower at this N).  Four warps round D1 * 2^-k to f16 in TMEM, and the tensor
+// core multiplies it, read as an A operand straight from TMEM, by the 32 rows
+// of W_o that belong to channel a:
+//   D2_j[i][z] += A2_j[i][b] W_o[a*32 + b][z]                (M 128, N c_z, K 32)
+// The outer products never leave the SM.  After the 32 slices eight warps
+// apply the column scales (which carry 2^k back), b_o, 1/(eps + count) and the
+// residual, and write the pair rows.  D2 sums K = (a, b) in ascending 16-wide
+// steps, as the two-kernel path does, from the same f16 operand values.
+// Tiles are dealt to CTAs in contiguous runs (j-pair major), so a CTA reloads
+// the resident right operand only when its j pair changes.
+constexpr int FTHREADS = 448;  // warp 0 TMA, 1 MMA, 2-5 slice conversion, 6-13 output epilogue
+constexpr int FLST_MAX = 8;    // left ring: [2 x 64 i][64 s] f16 per stage, as many as shared memory holds
+constexpr uint32_t FL_STAGE = 16384, FW_STAGE = 16384;
+constexpr uint32_t kD2Col = 0, kD1Col = 256, kA2Col = 384;  // TMEM columns: D2 x2 (128), D1 x2 (64), A2 x2 (32)
+constexpr uint32_t kFusedSmemLimit = 232448;                  // 227 KB of dynamic shared memory per CTA
+constexpr uint32_t kFusedBarBytes = 512;
+
+// Shared-memory map: right (resident) | left ring | W_o ring (2) | barriers.
+__host__ __device__ constexpr uint32_t fused_off_l(int k_blocks) { return static_cast<uint32_t>(k_blocks) * 8192u; }
+__host__ __device__ constexpr uint32_t fused_off_w(int k_blocks, int lst) {
+  return fused_off_l(k_blocks) + static_cast<uint32_t>(lst) * FL_STAGE;
+}
+__host__ __device__ constexpr uint32_t fused_off_bar(int k_blocks, int lst) {
+  return fused_off_w(k_blocks, lst) + 2 * FW_STAGE;
+}
+__host__ __device__ constexpr uint32_t fused_smem(int k_blocks, int lst) {
+  return fused_off_bar(k_blocks, lst) + kFusedBarBytes + 1024;
+}
+// Left stages that fit beside a resident right operand of k_blocks x 8 KB (4 at S = 1024, 8 at S <= 512).
+__host__ __device__ constexpr int fused_stages(int k_blocks) {
+  int lst = FLST_MAX;
+  while (lst > 2 && fused_smem(k_blocks, lst) > kFusedSmemLimit) --lst;
+  return lst;
+}
+constexpr int kFusedMaxKBlocks = 16;  // S <= 1024: the resident right operand is 128 S bytes
+
+// Tile t = jp * n_ib + r is residue block (r + jp) mod n_ib of j pair jp: CTAs
+// working on different j pairs at the same moment stream different blocks of left.
+__device__ __forceinline__ int fused_tile_ib(int t, int jp, int n_ib) {
+  int ib = t - jp * n_ib + jp % n_ib;
+  return ib >= n_ib ? ib - n_ib : ib;
+}
+
+struct FusedArgs {
+  void *out;                   // this rank's pair rows [rows][n][cz]
+  const float *wscale, *bias;  // per output column (n_out entries)
+  const float *rowscale;       // [rows][n]: 1 / (eps + count)
+  int64_t n, rows;
+  int cz, n_out, n_ib, total_tiles, per_cta, k_blocks;
+  int lst;                     // left ring stages
+  float scale;                 // 2^-k applied to D1 before rounding
+  int residual, vector_out;
+  unsigned int *err;
+};
+
+template <typename OT>
+__global__ void __launch_bounds__(FTHREADS, 1)
+    fused_kernel(const __grid_constant__ CUtensorMap lmap, const __grid_constant__ CUtensorMap rmap,
+                 const __grid_constant__ CUtensorMap wmap, const FusedArgs p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = align1024(smem_raw);
+  const uint32_t sbase = smem_u32(smem);
+  const int lst = p.lst;
+  const uint32_t s_r = sbase, s_l = sbase + fused_off_l(p.k_blocks), s_w = sbase + fused_off_w(p.k_blocks, lst);
+  const uint32_t bar0 = sbase + fused_off_bar(p.k_blocks, lst);
+  auto l_full = [&](int s) { return bar0 + 8u * s; };
+  auto l_empty = [&](int s) { return bar0 + 8u * (FLST_MAX + s); };
+  auto w_full = [&](int s) { return bar0 + 8u * (2 * FLST_MAX + s); };
+  auto w_empty = [&](int s) { return bar0 + 8u * (2 * FLST_MAX + 2 + s); };
+  auto d1_full = [&](int b) { return bar0 + 8u * (2 * FLST_MAX + 4 + b); };
+  auto a2_full = [&](int b) { return bar0 + 8u * (2 * FLST_MAX + 6 + b); };
+  auto a2_empty = [&](int b) { return bar0 + 8u * (2 * FLST_MAX + 8 + b); };
+  const uint32_t r_full = bar0 + 8u * (2 * FLST_MAX + 10), r_empty = r_full + 8u, d2_full = r_full + 16u,
+                 d2_empty = r_full + 24u, drain = r_full + 32u;  // 31 barriers: 248 bytes
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + fused_off_bar(p.k_blocks, lst) + 256);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + fused_off_bar(p.k_blocks, lst) + 264);
+  const int warp = warp_index_uniform(), lane = threadIdx.x & 31;
+  const int t_begin = blockIdx.x * p.per_cta;
+  const int t_end = min(p.total_tiles, t_begin + p.per_cta);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < lst; ++s) {
+      mbar_init(l_full(s), 1);
+      mbar_init(l_empty(s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(w_full(b), 1);
+      mbar_init(w_empty(b), 1);
+      mbar_init(d1_full(b), 1);
+      mbar_init(a2_full(b), 4);
+      mbar_init(a2_empty(b), 1);
+    }
+    mbar_init(r_full, 1);
+    mbar_init(r_empty, 1);
+    mbar_init(d2_full, 1);
+    mbar_init(d2_empty, 8);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_map(&lmap);
+      tma_prefetch_map(&rmap);
+      tma_prefetch_map(&wmap);
+      int ls = 0, lph = 0, lcount = 0, wq = 0, rq = 0, prev_jp = -1;
+      bool ok = true;
+      const uint32_t w_bytes = static_cast<uint32_t>(p.n_out) * 128u;
+      for (int t = t_begin; ok && t < t_end; ++t) {
+        const int jp = t / p.n_ib, ib = fused_tile_ib(t, jp, p.n_ib);
+        if (jp != prev_jp) {
+          // the resident right operand of j = 2 jp, 2 jp + 1: rows 64 jp .. 64 jp + 63 of [n * c][S]
+          if (rq > 0 && !mbar_wait(r_empty, (rq - 1) & 1, abort_flag, p.err, kErrWaitProducer)) break;
+          mbar_arrive_expect_tx(r_full, static_cast<uint32_t>(p.k_blocks) * 8192u);
+          for (int kb = 0; kb < p.k_blocks; ++kb) tma_load_3d(s_r + kb * 8192u, &rmap, r_full, kb * 64, 64 * jp, 0);
+          ++rq;
+          prev_jp = jp;
+        }
+        for (int a = 0; ok && a < C; ++a) {
+          if ((a & 1) == 0) {  // W_o rows of channels a, a + 1: one [n_out][64] K-major tile
+            const int ws = wq & 1;
+            if (!mbar_wait(w_empty(ws), ((wq >> 1) & 1) ^ 1, abort_flag, p.err, kErrWaitProducer)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(w_full(ws), w_bytes);
+            tma_load_3d(s_w + ws * FW_STAGE, &wmap, w_full(ws), 0, 0, a >> 1);
+            ++wq;
+          }
+          for (int kb = 0; kb < p.k_blocks; ++kb) {
+            if (!mbar_wait(l_empty(ls), lph ^ 1, abort_flag, p.err, kErrWaitProducer)) {
+              ok = false;
+              break;
+            }
+            const uint32_t dst = s_l + ls * FL_STAGE;
+            mbar_arrive_expect_tx(l_full(ls), FL_STAGE);
+            tma_load_3d(dst, &lmap, l_full(ls), kb * 64, 128 * ib, a);  // [128 residues][64 sequences]
+            ++lcount;
+            if (++ls == lst) {
+              ls = 0;
+              lph ^= 1;
+            }
+          }
+        }
+      }
+      // loads still in flight (all consumed unless a role gave up)
+      for (int j = max(0, lcount - lst); j < lcount; ++j) mbar_wait_drain(l_full(j % lst), (j / lst) & 1, p.err);
+      for (int j = max(0, wq - 2); j < wq; ++j) mbar_wait_drain(w_full(j & 1), (j >> 1) & 1, p.err);
+      if (rq > 0) mbar_wait_drain(r_full, (rq - 1) & 1, p.err);
+    }
+  } else if (warp == 1) {
+    // MMA issue: the whole warp runs the loop (warp-uniform waits and running
+    // descriptors) and one elected lane issues each instruction.  Every operand
+    // is K-major: a 16-sequence step is 32 bytes (2 descriptor units) along the
+    // 128-byte rows; a left stage is 16 KB (1024 units), a right block 8 KB.
+    const uint32_t idesc1 = idesc_f16_f32(128, 2 * C);
+    const uint32_t idesc2 = idesc_f16_f32(128, p.n_out);  // A in TMEM
+    const uint64_t l_base = sdesc_k_sw128(s_l), r_base = sdesc_k_sw128(s_r), w_base = sdesc_k_sw128(s_w);
+    uint64_t l_desc = l_base;
+    int ls = 0, lph = 0, wq = 0, rq = 0, prev_jp = -1, tile_it = 0;
+    uint32_t g = 0;  // slices issued, over all tiles
+    bool ok = true;
+    // D2 += A2(slice gp) W_o(channel a): issued one slice behind the outer products
+    auto outputs = [&](uint32_t gp, int a) -> bool {
+      const int bp = gp & 1, ws = wq & 1;
+      if (a == 0 && !warp_wait(d2_empty, (tile_it & 1) ^ 1, abort_flag, p.err, kErrWaitMma)) return false;
+      if (!warp_wait(a2_full(bp), (gp >> 1) & 1, abort_flag, p.err, kErrWaitMma)) return false;
+      if ((a & 1) == 0 && !warp_wait(w_full(ws), (wq >> 1) & 1, abort_flag, p.err, kErrWaitMma)) return false;
+      tc_fence_after();
+      const uint64_t bd = w_base + ws * (FW_STAGE >> 4) + (a & 1) * 4;  // channel a's 32 rows: 64 bytes in
+      const uint32_t a2 = tmem + kA2Col + bp * 32;
+      if (a == 0) {
+        umma_ts_first(tmem + kD2Col, a2, bd, idesc2);
+        umma_ts_first(tmem + kD2Col + 128, a2 + 16, bd, idesc2);
+      } else {
+        umma_ts_acc(tmem + kD2Col, a2, bd, idesc2);
+        umma_ts_acc(tmem + kD2Col + 128, a2 + 16, bd, idesc2);
+      }
+      umma_ts_acc(tmem + kD2Col, a2 + 8, bd + 2, idesc2);
+      umma_ts_acc(tmem + kD2Col + 128, a2 + 24, bd + 2, idesc2);
+      umma_commit(a2_empty(bp));
+      if (a & 1) {
+        umma_commit(w_empty(ws));
+        ++wq;
+      }
+      return true;
+    };
+    for (int t = t_begin; ok && t < t_end; ++t, ++tile_it) {
+      const int jp = t / p.n_ib;
+      if (jp != prev_jp) {
+        if (!warp_wait(r_full, rq & 1, abort_flag, p.err, kErrWaitMma)) break;
+        ++rq;
+        prev_jp = jp;
+      }
+      for (int a = 0; a < C; ++a, ++g) {
+        const uint32_t d1 = tmem + kD1Col + (g & 1) * 64;
+        uint64_t r_desc = r_base;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!warp_wait(l_full(ls), lph, abort_flag, p.err, kErrWaitMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          if (kb == 0)
+            umma_first(d1, l_desc, r_desc, idesc1);
+          else
+            umma_acc(d1, l_desc, r_desc, idesc1);
+          umma_acc(d1, l_desc + 2, r_desc + 2, idesc1);
+          umma_acc(d1, l_desc + 4, r_desc + 4, idesc1);
+          umma_acc(d1, l_desc + 6, r_desc + 6, idesc1);
+          umma_commit(l_empty(ls));
+          r_desc += 8192 >> 4;
+          l_desc += FL_STAGE >> 4;
+          if (++ls == lst) {
+            ls = 0;
+            lph ^= 1;
+            l_desc = l_base;
+          }
+        }
+        if (!ok) break;
+        umma_commit(d1_full(g & 1));
+        if (a > 0 && !outputs(g - 1, a - 1)) {
+          ok = false;
+          break;
+        }
+      }
+      if (!ok || !outputs(g - 1, C - 1)) break;
+      umma_commit(d2_full);
+      if (t + 1 < t_end && (t + 1) / p.n_ib != jp) umma_commit(r_empty);
+    }
+    umma_commit(drain);
+    mbar_wait_drain(drain, 0, p.err);
+  } else if (warp < 6) {
+    // ---- slice conversion: D1 (f32) -> A2 (f16 pairs, times 2^-k), lanes 32 q .. 32 q + 31 ----
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    uint32_t g = 0;
+    bool ok = true;
+    for (int t = t_begin; ok && t < t_end; ++t) {
+      for (int a = 0; a < C; ++a, ++g) {
+        const int b = g & 1;
+        if (!warp_wait(d1_full(b), (g >> 1) & 1, abort_flag, p.err, kErrWaitEpilogue) ||
+            !warp_wait(a2_empty(b), ((g >> 1) & 1) ^ 1, abort_flag, p.err, kErrWaitEpilogue)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        uint32_t v[32], pk[32];
+        tmem_ld32(tmem + lane_off + kD1Col + b * 64, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int c = 0; c < 16; ++c)
+          pk[c] = pack_half2(__uint_as_float(v[2 * c]) * p.scale, __uint_as_float(v[2 * c + 1]) * p.scale);
+        tmem_ld32(tmem + lane_off + kD1Col + b * 64 + 32, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int c = 0; c < 16; ++c)
+          pk[16 + c] = pack_half2(__uint_as_float(v[2 * c]) * p.scale, __uint_as_float(v[2 * c + 1]) * p.scale);
+        tmem_st32(tmem + lane_off + kA2Col + b * 32, pk);
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(a2_full(b));
+      }
+    }
+  } else {
+    // ---- output epilogue: warp (q, jh) drains lanes 32 q .. 32 q + 31 of D2_jh ----
+    const int q = warp & 3, jh = (warp - 6) >> 2;
+    const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+    const int chunks = p.n_out / 32;
+    int tile_it = 0;
+    for (int t = t_begin; t < t_end; ++t, ++tile_it) {
+      const int jp = t / p.n_ib, ib = fused_tile_ib(t, jp, p.n_ib);
+      const int64_t i = static_cast<int64_t>(ib) * 128 + q * 32 + lane, j = 2 * jp + jh;
+      if (!warp_wait(d2_full, tile_it & 1, abort_flag, p.err, kErrWaitEpilogue)) break;
+      tc_fence_after();
+      const bool row_ok = i < p.rows && j < p.n;
+      const float rs = row_ok ? p.rowscale[i * p.n + j] : 0.f;
+      OT *orow = static_cast<OT *>(p.out) + (i * p.n + j) * p.cz;
+      for (int ch = 0; ch < chunks; ++ch) {
+        uint32_t v[32];
+        tmem_ld32(tmem + lane_off + kD2Col + jh * 128 + ch * 32, v);
+        tmem_ld_wait();
+        if (ch == chunks - 1) {  // D2 is free for the next tile once every lane has read it
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(d2_empty);
+        }
+        const int c0 = ch * 32;
+        if (!row_ok || c0 >= p.cz) continue;
+        float y[32];
+        const float4 *sc = reinterpret_cast<const float4 *>(p.wscale + c0);
+        const float4 *bi = reinterpret_cast<const float4 *>(p.bias + c0);
+#pragma unroll
+        for (int i4 = 0; i4 < 8; ++i4) {
+          const float4 s4 = __ldg(sc + i4), b4 = __ldg(bi + i4);
+          y[4 * i4 + 0] = fmaf(__uint_as_float(v[4 * i4 + 0]), s4.x, b4.x) * rs;
+          y[4 * i4 + 1] = fmaf(__uint_as_float(v[4 * i4 + 1]), s4.y, b4.y) * rs;
+          y[4 * i4 + 2] = fmaf(__uint_as_float(v[4 * i4 + 2]), s4.z, b4.z) * rs;
+          y[4 * i4 + 3] = fmaf(__uint_as_float(v[4 * i4 + 3]), s4.w, b4.w) * rs;
+        }
+        store_out32<OT>(orow, c0, p.cz, y, p.vector_out, p.residual);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
 }  // namespace opm
 
 using namespace opm;
@@ -311,6 +645,10 @@ OpmLayout opm_layout(int64_t s, int64_t n, int64_t cm, int64_t c, int64_t cz, in
   int k = 0;
   while ((int64_t(1) << k) < s) ++k;
   L.out_shift = k;
+  // One kernel for the outer products and the output projection when the
+  // right operand of a tile fits in shared memory and c_z in one MMA.
+  L.fused = c == C && align_up(s, 64) / 64 <= kFusedMaxKBlocks && cz <= 128;
+  L.seq_pitch = L.fused ? align_up(s, 8) : 0;
   const int64_t lr_cols = linear_cols_pad(2 * c), o_cols = linear_cols_pad(cz), o_inner = align_up(c * c, 64);
   size_t off = 0;
   auto take = [&](size_t bytes) {
@@ -327,13 +665,75 @@ OpmLayout opm_layout(int64_t s, int64_t n, int64_t cm, int64_t c, int64_t cz, in
   L.off_ln = take((size_t)L.cmp * 2 * 4);
   L.off_xn = take((size_t)s * L.rows * L.cmp * 2);
   L.off_mask = take((size_t)s * L.rows * 4);
-  L.off_left = take((size_t)s * L.rows * c * 2);
-  L.off_right = take((size_t)s * n * c * 2);  // every rank's block [ranks][S][rows][c]
+  const int64_t seq_span = L.fused ? L.seq_pitch : s;
+  L.off_left = take((size_t)seq_span * c * L.rows * 2);
+  L.off_right = take((size_t)seq_span * n * c * 2);  // every rank's block: [ranks][S][rows][c], or [n][c][pitch]
   L.off_rowscale = take((size_t)L.rows * n * 4);
-  L.off_outer = take((size_t)rb * n * c * c * 2);
+  L.off_outer = take(L.fused ? 0 : (size_t)rb * n * c * c * 2);
   L.total = off;
   return L;
 }
+
+namespace {
+
+template <typename OT>
+af2_status launch_fused_t(af2_ctx *ctx, const CUtensorMap &lmap, const CUtensorMap &rmap, const CUtensorMap &wmap,
+                          const FusedArgs &a, int grid, cudaStream_t stream) {
+  const uint32_t smem = fused_smem(a.k_blocks, a.lst);
+  cudaError_t e = cudaFuncSetAttribute(fused_kernel<OT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "fused OPM kernel attributes");
+  LaunchScope scope(ctx, stream, kProfOpmFused);
+  fused_kernel<OT><<<grid, FTHREADS, smem, stream>>>(lmap, rmap, wmap, a);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? AF2_OK : cuda_fail(ctx, e, "fused OPM kernel launch");
+}
+
+// The outer products and output projection of this rank's rows, one launch.
+af2_status fused_launch(af2_ctx *ctx, const OpmLayout &L, uint8_t *ws, const __half *right_full, int residual,
+                        void *out, int out_dtype, cudaStream_t stream) {
+  const int64_t s = L.s, n = L.n, c = L.c, cz = L.cz, rows = L.rows;
+  const int64_t o_cols = linear_cols_pad(cz), o_inner = align_up(c * c, 64);
+  CUtensorMap lmap, rmap, wmap;
+  // K-major, sequences contiguous (zero past S):
+  // left [c][rows][pitch]: boxes of 64 sequences x 128 residues of one channel
+  // right [n][c][pitch]: boxes of 64 sequences x 64 rows (2 residues x 32 channels)
+  // W_o [c*c / 64][o_cols][64]: the 64 rows of two channels a per box
+  const uint64_t pitch = L.seq_pitch;
+  if (!encode_map_3d(&lmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, ws + L.off_left, s, rows, c, pitch * 2,
+                     (uint64_t)rows * pitch * 2, 64, 128, 1, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_map_3d(&rmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, right_full, s, n * c, 1, pitch * 2,
+                     (uint64_t)n * c * pitch * 2, 64, 64, 1, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_map_3d(&wmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, ws + L.off_wo, 64, o_cols, o_inner / 64, 128,
+                     (uint64_t)o_cols * 128, 64, (uint32_t)o_cols, 1, CU_TENSOR_MAP_SWIZZLE_128B))
+    return fail(ctx, AF2_ERR_CUDA, "cuTensorMapEncodeTiled failed for the fused OPM operands");
+  FusedArgs a{};
+  a.out = out;
+  a.wscale = reinterpret_cast<const float *>(ws + L.off_wo_scale);
+  a.bias = reinterpret_cast<const float *>(ws + L.off_wo_bias);
+  a.rowscale = reinterpret_cast<const float *>(ws + L.off_rowscale);
+  a.n = n;
+  a.rows = rows;
+  a.cz = (int)cz;
+  a.n_out = (int)o_cols;
+  a.n_ib = (int)((rows + 127) / 128);
+  a.total_tiles = a.n_ib * (int)((n + 1) / 2);
+  a.per_cta = (a.total_tiles + ctx->sm_count - 1) / ctx->sm_count;
+  a.k_blocks = (int)((s + 63) / 64);
+  a.lst = fused_stages(a.k_blocks);
+  a.scale = std::ldexp(1.f, -L.out_shift);
+  a.residual = residual;
+  {
+    const size_t ob = out_dtype == AF2_F32 ? 4 : 2;
+    a.vector_out = reinterpret_cast<uintptr_t>(out) % 16 == 0 && (cz * ob) % 16 == 0;
+  }
+  a.err = ctx->err_word;
+  const int grid = (a.total_tiles + a.per_cta - 1) / a.per_cta;
+  if (out_dtype == AF2_F16) return launch_fused_t<__half>(ctx, lmap, rmap, wmap, a, grid, stream);
+  if (out_dtype == AF2_BF16) return launch_fused_t<__nv_bfloat16>(ctx, lmap, rmap, wmap, a, grid, stream);
+  return launch_fused_t<float>(ctx, lmap, rmap, wmap, a, grid, stream);
+}
+
+}  // namespace
 
 af2_status opm_launch(af2_ctx *ctx, const OpmLayout &L, const void *m, int m_dtype, const float *mask,
                       const float *packed, double ln_eps, double norm_eps, int residual, void *out, int out_dtype,
@@ -381,11 +781,11 @@ af2_status opm_launch(af2_ctx *ctx, const OpmLayout &L, const void *m, int m_dty
       if (vec)
         norm_kernel<MT, true><<<blocks, warps * 32, 0, stream>>>(mp, xrows, (int)cm, (int)L.cmp, ln, ln + L.cmp,
                                                                  (float)ln_eps, xn, (int)n, (int)L.row0, (int)rows,
-                                                                 mask, mask_loc);
+                                                                 L.fused ? (int)s : 0, mask, mask_loc);
       else
         norm_kernel<MT, false><<<blocks, warps * 32, 0, stream>>>(mp, xrows, (int)cm, (int)L.cmp, ln, ln + L.cmp,
                                                                   (float)ln_eps, xn, (int)n, (int)L.row0, (int)rows,
-                                                                  mask, mask_loc);
+                                                                  L.fused ? (int)s : 0, mask, mask_loc);
     };
     if (m_dtype == AF2_F32)
       run(float{});
@@ -411,12 +811,16 @@ af2_status opm_launch(af2_ctx *ctx, const OpmLayout &L, const void *m, int m_dty
     op.cols = 2 * c;
     op.opm_projection = true;
     op.left = ws + L.off_left;
-    op.right = right_full + (size_t)rank * s * rows * c;
+    op.kmajor_rows = rows;
+    op.kmajor_seqs = s;
+    op.seq_pitch = L.seq_pitch;
+    op.right = right_full + (size_t)rank * (L.fused ? L.seq_pitch : s) * rows * c;
     op.prof = kProfOpmProject;
     if ((st = linear_launch(ctx, op, stream)) != AF2_OK) return st;
   }
   if (exchange && exchange->all_gather &&
-      (st = exchange->all_gather(ctx, right_full, (size_t)s * rows * c * sizeof(__half), stream)) != AF2_OK)
+      (st = exchange->all_gather(ctx, right_full, (size_t)(L.fused ? L.seq_pitch : s) * rows * c * sizeof(__half),
+                                 stream)) != AF2_OK)
     return st;
   // ---- pair counts of this rank's rows ----
   float *rowscale = reinterpret_cast<float *>(ws + L.off_rowscale);
@@ -427,8 +831,9 @@ af2_status opm_launch(af2_ctx *ctx, const OpmLayout &L, const void *m, int m_dty
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(ctx, e, "OPM pair counts");
   }
-  // ---- outer products and output projection, block by block of this rank's rows ----
+  if (L.fused) return fused_launch(ctx, L, ws, right_full, residual, out, out_dtype, stream);
   const int64_t blocks_b = n / rows;  // blocks of the right operand
+  // ---- outer products and output projection, block by block of this rank's rows ----
   CUtensorMap lmap, rmap;
   if (!encode_map_3d(&lmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, ws + L.off_left, rows * c, s, 1, rows * c * 2,
                      (uint64_t)s * rows * c * 2, 64, 64, 1, CU_TENSOR_MAP_SWIZZLE_128B) ||

@@ -55,7 +55,7 @@ METRIC = "Evoformer pair-GEMM TFLOP/s & ms/block at N=1024; % of B200 bf16 TC pe
 KERNEL_DRAM_BYTES = {"triangle.contract": 771_527_680, "opm.outer": 268_619_520}
 KERNELS = ("weights.prepare", "triangle.prepare", "triangle.relayout", "triangle.project", "triangle.contract",
            "triangle.output", "opm.normalize", "opm.project", "opm.count", "opm.outer", "opm.output",
-           "transition.prepare", "transition.fused", "shard.transpose")
+           "opm.fused", "transition.prepare", "transition.fused", "shard.transpose")
 
 
 def triangle_flops(n: int, cz: int = CZ, ch: int = CH) -> float:
@@ -88,6 +88,7 @@ def kernel_step_flops(name: str, world: int = 1, n: int = N, s: int = S_MSA) -> 
                  "triangle.output": 2 * 2.0 * n * n * (CH * CZ + CZ * CZ),
                  "opm.outer": 2.0 * (n * C_OUTER) ** 2 * s,
                  "opm.output": 2.0 * n * n * C_OUTER * C_OUTER * CZ,
+                 "opm.fused": 2.0 * (n * C_OUTER) ** 2 * s + 2.0 * n * n * C_OUTER * C_OUTER * CZ,
                  "opm.project": 2.0 * s * n * CM * 2 * C_OUTER,
                  "transition.fused": transition_flops(n)}.get(name)
     return None if per_block is None else per_block / world

@@ -201,8 +201,16 @@ def test_opm_python_validation_and_packing():
 
 
 def test_opm_workspace_blocks_bound_the_outer_scratch():
-    whole = af2cuda.opm_workspace_bytes(512, 768, 256, 32, 128)
-    b4 = af2cuda.opm_workspace_bytes(512, 768, 256, 32, 128, row_block=4)
-    b8 = af2cuda.opm_workspace_bytes(512, 768, 256, 32, 128, row_block=8)
+    # c_z above 128: the two-kernel path, whose outer-product scratch the residue blocks bound
+    whole = af2cuda.opm_workspace_bytes(512, 768, 256, 32, 160)
+    b4 = af2cuda.opm_workspace_bytes(512, 768, 256, 32, 160, row_block=4)
+    b8 = af2cuda.opm_workspace_bytes(512, 768, 256, 32, 160, row_block=8)
     assert b4 < b8 <= whole
     assert b8 - b4 == 4 * 768 * 32 * 32 * 2  # four more residue rows of f16 outer products
+
+
+def test_opm_fused_workspace_has_no_outer_scratch():
+    # S <= 1024 and c_z <= 128: the outer products stay on chip, whatever the residue block
+    fused = af2cuda.opm_workspace_bytes(512, 768, 256, 32, 128)
+    assert fused == af2cuda.opm_workspace_bytes(512, 768, 256, 32, 128, row_block=4)
+    assert fused < 768 * 768 * 32 * 32 * 2 // 4

@@ -63,6 +63,17 @@ def test_opm_matches_oracle(device, s, n, cm, cz):
     assert result.elapsedMilliseconds > 0
 
 
+@pytest.mark.parametrize("s,n,cm,cz", [(1030, 12, 16, 24), (40, 20, 32, 160)])
+def test_opm_two_kernel_path_matches_oracle(device, s, n, cm, cz):
+    """More than 1024 sequences, or c_z above 128: the outer products go through
+    the HBM scratch and the shared output GEMM instead of the fused kernel."""
+    m, mask, w = opm_case(s, n, cm, cz=cz, seed=s + n)
+    expected = oracle.outer_product_mean(m, mask, opm_packed(w), 32, cz)
+    out = af2cuda.OuterProductMeanGpu(device).run(opm_input(m, mask, w)).output.reshape(n, n, cz)
+    assert np.isfinite(out).all()
+    assert relative_max_error(out, expected) <= REL_TOL
+
+
 def test_opm_blocks_are_bit_identical(device):
     m, mask, w = opm_case(33, 46, 64, cz=32, seed=5)
     whole = af2cuda.OuterProductMeanGpu(device).run(opm_input(m, mask, w)).output
