@@ -184,45 +184,6 @@ __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
-// D[tmem] (+)= A[smem] * B[smem]^T, f16/bf16 operands, f32 accumulator.
-__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                        uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-// The same with the accumulate predicate fixed: D = A B (first K step) and
-// D += A B.  A single thread issues every MMA of a CTA, so the issue path is
-// kept free of per-instruction predicate and descriptor arithmetic: callers
-// compute descriptors once and step them by constant offsets (desc_add).
-__device__ __forceinline__ void mma_f16_first(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc) {
-  asm volatile("tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, 0;" ::"r"(d_tmem), "l"(adesc), "l"(bdesc),
-               "r"(idesc)
-               : "memory");
-}
-__device__ __forceinline__ void mma_f16_acc(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc) {
-  asm volatile("tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, 1;" ::"r"(d_tmem), "l"(adesc), "l"(bdesc),
-               "r"(idesc)
-               : "memory");
-}
-
-// D[tmem] (+)= A[tmem] * B[smem]^T: A is 128 lanes x 16 f16 (8 columns of
-// packed pairs, the lower K element in the low half), K-major.
-__device__ __forceinline__ void mma_f16_ts_first(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc) {
-  asm volatile("tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, 0;" ::"r"(d_tmem), "r"(a_tmem), "l"(bdesc),
-               "r"(idesc)
-               : "memory");
-}
-__device__ __forceinline__ void mma_f16_ts_acc(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc) {
-  asm volatile("tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, 1;" ::"r"(d_tmem), "r"(a_tmem), "l"(bdesc),
-               "r"(idesc)
-               : "memory");
-}
-
 // ---- warp-wide MMA issue ----------------------------------------------------
 // The whole issuing warp runs the MMA loop with warp-uniform control flow and
 // operands, and one lane elected inside each instruction issues it.  With the
@@ -277,11 +238,6 @@ __device__ __forceinline__ void umma_commit(uint32_t bar) {
 // is below 2^18, so the add never carries out of the field.
 __host__ __device__ constexpr uint64_t desc_add(uint64_t desc, uint32_t bytes) { return desc + (bytes >> 4); }
 
-// Arrives once on `bar` when every tcgen05 op this thread issued so far has completed.
-__device__ __forceinline__ void mma_commit(uint32_t bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
-               : "memory");
-}
 
 // 32 lanes x 32 consecutive 32-bit columns; thread t of the warp gets lane
 // (base lane + t), columns [col, col + 32).

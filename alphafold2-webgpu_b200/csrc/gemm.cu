@@ -61,7 +61,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   const uint32_t drain = bar0 + 8u * (2 * STAGES + 4);
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + OFF_BAR + 128);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + OFF_BAR + 136);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warp = warp_index_uniform(), lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -110,38 +110,35 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else if (warp == 1) {
     // ---- MMA issuer ----
-    if (lane == 0) {
-      const uint32_t idesc = idesc_f16_f32(BM, p.bn);
-      const uint64_t a_desc = sdesc_k_sw128(sbase);
-      int it = 0, tile_it = 0;
-      bool ok = true;
-      for (int t = blockIdx.x; ok && t < p.total_tiles; t += gridDim.x, ++tile_it) {
-        const int buf = tile_it & 1;
-        if (!mbar_wait(acc_empty(buf), ((tile_it >> 1) & 1) ^ 1, abort_flag, p.err, kErrWaitMma)) break;
-        tc_fence_after();
-        const uint32_t d = tmem + buf * 256;
-        for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
-          const int s = it % STAGES;
-          if (!mbar_wait(full(s), (it / STAGES) & 1, abort_flag, p.err, kErrWaitMma)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint64_t ad = desc_add(a_desc, s * STAGE_BYTES), bd = desc_add(ad, A_BYTES);
-          if (kb == 0)
-            mma_f16_first(d, ad, bd, idesc);
-          else
-            mma_f16_acc(d, ad, bd, idesc);
-#pragma unroll
-          for (int ks = 1; ks < BK / 16; ++ks) mma_f16_acc(d, desc_add(ad, ks * 32), desc_add(bd, ks * 32), idesc);
-          mma_commit(empty(s));
+    const uint32_t idesc = idesc_f16_f32(BM, p.bn);
+    const uint64_t a_desc = sdesc_k_sw128(sbase);
+    int it = 0, tile_it = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; ok && t < p.total_tiles; t += gridDim.x, ++tile_it) {
+      const int buf = tile_it & 1;
+      if (!warp_wait(acc_empty(buf), ((tile_it >> 1) & 1) ^ 1, abort_flag, p.err, kErrWaitMma)) break;
+      tc_fence_after();
+      const uint32_t d = tmem + buf * 256;
+      for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
+        const int s = it % STAGES;
+        if (!warp_wait(full(s), (it / STAGES) & 1, abort_flag, p.err, kErrWaitMma)) {
+          ok = false;
+          break;
         }
-        if (ok) mma_commit(acc_full(buf));
+        tc_fence_after();
+        const uint64_t ad = desc_add(a_desc, s * STAGE_BYTES), bd = desc_add(ad, A_BYTES);
+        if (kb == 0)
+          umma_first(d, ad, bd, idesc);
+        else
+          umma_acc(d, ad, bd, idesc);
+#pragma unroll
+        for (int ks = 1; ks < BK / 16; ++ks) umma_acc(d, desc_add(ad, ks * 32), desc_add(bd, ks * 32), idesc);
+        umma_commit(empty(s));
       }
-      mma_commit(drain);
-      mbar_wait_drain(drain, 0, p.err);
+      if (ok) umma_commit(acc_full(buf));
     }
-    __syncwarp();
+    umma_commit(drain);
+    mbar_wait_drain(drain, 0, p.err);
   } else {
     // ---- epilogue: one output row per thread ----
     const int q = warp & 3;
@@ -254,7 +251,7 @@ template <int FMT>
 __device__ __forceinline__ void prep_block(PrepShared &sh, const MatrixDev &m, int inner, int cols, int inner_pad,
                                            int cols_pad, int row0, int rows_total, float extra_scale,
                                            __half *__restrict__ out, float *__restrict__ scale_out) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warp = warp_index_uniform(), lane = threadIdx.x & 31;
   const int o0 = blockIdx.x * 32, o = o0 + lane;
   constexpr bool codes = FMT == AF2_WEIGHTS_Q8_CHANNEL;
   float vals[kPrepBatch];

@@ -168,7 +168,7 @@ __global__ void __launch_bounds__(OTHREADS, 1)
   const uint32_t drain = bar0 + 8u * (2 * OSTAGES + 4);
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + OOFF_BAR + 128);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + OOFF_BAR + 136);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warp = warp_index_uniform(), lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < OSTAGES; ++s) {
@@ -219,39 +219,36 @@ __global__ void __launch_bounds__(OTHREADS, 1)
       for (int j = std::max(0, it - OSTAGES); j < it; ++j) mbar_wait_drain(full(j % OSTAGES), (j / OSTAGES) & 1, p.err);
     }
   } else if (warp == 1) {
-    if (lane == 0) {
       // both operands MN-major: 64-element MN blocks 8 KB apart, 8-row K groups 1 KB apart
-      constexpr uint32_t kIdesc = idesc_f16_f32(OBM, OBN) | (1u << 15) | (1u << 16);
-      const uint64_t a_desc = sdesc_mn_sw128(sbase, 8192, 1024);
-      int it = 0, tile_it = 0;
-      bool ok = true;
-      for (int t = blockIdx.x; ok && t < p.total_tiles; t += gridDim.x, ++tile_it) {
-        const int buf = tile_it & 1;
-        if (!mbar_wait(acc_empty(buf), ((tile_it >> 1) & 1) ^ 1, abort_flag, p.err, kErrWaitMma)) break;
-        tc_fence_after();
-        const uint32_t d = tmem + buf * OBN;
-        for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
-          const int s = it % OSTAGES;
-          if (!mbar_wait(full(s), (it / OSTAGES) & 1, abort_flag, p.err, kErrWaitMma)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint64_t ad = desc_add(a_desc, s * OSTAGE), bd = desc_add(ad, OA_BYTES);
-          if (kb == 0)
-            mma_f16_first(d, ad, bd, kIdesc);
-          else
-            mma_f16_acc(d, ad, bd, kIdesc);
-#pragma unroll
-          for (int ks = 1; ks < OBK / 16; ++ks) mma_f16_acc(d, desc_add(ad, ks * 2048), desc_add(bd, ks * 2048), kIdesc);
-          mma_commit(empty(s));
+    constexpr uint32_t kIdesc = idesc_f16_f32(OBM, OBN) | (1u << 15) | (1u << 16);
+    const uint64_t a_desc = sdesc_mn_sw128(sbase, 8192, 1024);
+    int it = 0, tile_it = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; ok && t < p.total_tiles; t += gridDim.x, ++tile_it) {
+      const int buf = tile_it & 1;
+      if (!warp_wait(acc_empty(buf), ((tile_it >> 1) & 1) ^ 1, abort_flag, p.err, kErrWaitMma)) break;
+      tc_fence_after();
+      const uint32_t d = tmem + buf * OBN;
+      for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
+        const int s = it % OSTAGES;
+        if (!warp_wait(full(s), (it / OSTAGES) & 1, abort_flag, p.err, kErrWaitMma)) {
+          ok = false;
+          break;
         }
-        if (ok) mma_commit(acc_full(buf));
+        tc_fence_after();
+        const uint64_t ad = desc_add(a_desc, s * OSTAGE), bd = desc_add(ad, OA_BYTES);
+        if (kb == 0)
+          umma_first(d, ad, bd, kIdesc);
+        else
+          umma_acc(d, ad, bd, kIdesc);
+#pragma unroll
+        for (int ks = 1; ks < OBK / 16; ++ks) umma_acc(d, desc_add(ad, ks * 2048), desc_add(bd, ks * 2048), kIdesc);
+        umma_commit(empty(s));
       }
-      mma_commit(drain);
-      mbar_wait_drain(drain, 0, p.err);
+      if (ok) umma_commit(acc_full(buf));
     }
-    __syncwarp();
+    umma_commit(drain);
+    mbar_wait_drain(drain, 0, p.err);
   } else {
     // TMEM lane = (i_local, a) with i_local = this warp's quarter, a = lane;
     // columns = (j_local, b).  Each (pair, a) is 32 contiguous f16 of the row.

@@ -210,7 +210,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   float *vec = reinterpret_cast<float *>(smem + off_vec(kb));
   const float *gamma = vec, *beta = vec + p.cp, *s2v = vec + 2 * p.cp, *b2v = vec + 3 * p.cp;
   const float *s1v = vec + 4 * p.cp, *b1v = vec + 4 * p.cp + p.hp;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warp = warp_index_uniform(), lane = threadIdx.x & 31;
   const int nh = p.nh;
   const int my_tiles = blockIdx.x < p.total_tiles ? (p.total_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
   const int total = my_tiles * nh;  // hidden chunks this CTA works through
@@ -300,70 +300,67 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else if (warp == 1) {
     // ---- MMA issuer ----
-    if (lane == 0) {
-      const uint32_t idesc1 = idesc_f16_f32(TILE, HC);
-      const uint32_t idesc2 = idesc_f16_f32(TILE, p.cp);
-      // Base descriptors; every operand below is one of these plus a constant.
-      const uint64_t a_desc = sdesc_k_sw128(sbase), w_desc = sdesc_k_sw128(sbase + OFF_W),
-                     h_desc = sdesc_k_sw128(sbase + OFF_H);
-      int ws = 0;
-      int it1 = 0, h1 = 0, it2 = 0, h2 = 0;  // tile and step of the next first / second GEMM
-      for (int j = 0; j < total + LAG; ++j) {
-        if (j < total) {  // first GEMM of step j -> D1[j % NBUF]
-          const int buf = it1 & 1, db = j % NBUF, s = ws % STAGES;
-          if ((h1 == 0 && !mbar_wait(a_full(buf), (it1 >> 1) & 1, abort_flag, p.err, kErrWaitMma)) ||
-              !mbar_wait(d1_empty(db), ((j / NBUF) & 1) ^ 1, abort_flag, p.err, kErrWaitMma) ||
-              !mbar_wait(w_full(s), (ws / STAGES) & 1, abort_flag, p.err, kErrWaitMma))
-            break;
-          tc_fence_after();
-          const uint64_t ad = desc_add(a_desc, buf * A_BYTES), wd = desc_add(w_desc, s * W_BYTES);
-          const uint32_t d = tmem + db * HC;
-          mma_f16_first(d, ad, wd, idesc1);
+    const uint32_t idesc1 = idesc_f16_f32(TILE, HC);
+    const uint32_t idesc2 = idesc_f16_f32(TILE, p.cp);
+    // Base descriptors; every operand below is one of these plus a constant.
+    const uint64_t a_desc = sdesc_k_sw128(sbase), w_desc = sdesc_k_sw128(sbase + OFF_W),
+                   h_desc = sdesc_k_sw128(sbase + OFF_H);
+    int ws = 0;
+    int it1 = 0, h1 = 0, it2 = 0, h2 = 0;  // tile and step of the next first / second GEMM
+    for (int j = 0; j < total + LAG; ++j) {
+      if (j < total) {  // first GEMM of step j -> D1[j % NBUF]
+        const int buf = it1 & 1, db = j % NBUF, s = ws % STAGES;
+        if ((h1 == 0 && !warp_wait(a_full(buf), (it1 >> 1) & 1, abort_flag, p.err, kErrWaitMma)) ||
+            !warp_wait(d1_empty(db), ((j / NBUF) & 1) ^ 1, abort_flag, p.err, kErrWaitMma) ||
+            !warp_wait(w_full(s), (ws / STAGES) & 1, abort_flag, p.err, kErrWaitMma))
+          break;
+        tc_fence_after();
+        const uint64_t ad = desc_add(a_desc, buf * A_BYTES), wd = desc_add(w_desc, s * W_BYTES);
+        const uint32_t d = tmem + db * HC;
+        umma_first(d, ad, wd, idesc1);
 #pragma unroll
-          for (int ks = 1; ks < 4 * KB; ++ks)
-            mma_f16_acc(d, desc_add(ad, (ks >> 2) * 16384 + (ks & 3) * 32), desc_add(wd, (ks >> 2) * 16384 + (ks & 3) * 32),
-                        idesc1);
-          mma_commit(w_empty(s));
-          mma_commit(d1_full(db));
-          if (h1 == nh - 1) mma_commit(a_empty(buf));
-          ++ws;
-          if (++h1 == nh) {
-            h1 = 0;
-            ++it1;
-          }
-        }
-        if (j >= LAG) {  // second GEMM of step i = j - LAG: D2[tile] += H[i % NBUF] W2[chunk]
-          const int i = j - LAG, buf = it2 & 1, hb = i % NBUF, s = ws % STAGES;
-          if (!mbar_wait(h_full(hb), (i / NBUF) & 1, abort_flag, p.err, kErrWaitMma) ||
-              !mbar_wait(w_full(s), (ws / STAGES) & 1, abort_flag, p.err, kErrWaitMma) ||
-              (h2 == 0 && !mbar_wait(d2_empty(buf), ((it2 >> 1) & 1) ^ 1, abort_flag, p.err, kErrWaitMma)))
-            break;
-          tc_fence_after();
-          const uint64_t hd = desc_add(h_desc, hb * 32768), wd = desc_add(w_desc, s * W_BYTES);
-          const uint32_t d = tmem + 256 + buf * 128;
-          if (h2 == 0)
-            mma_f16_first(d, hd, wd, idesc2);
-          else
-            mma_f16_acc(d, hd, wd, idesc2);
-#pragma unroll
-          for (int ks = 1; ks < 8; ++ks)
-            mma_f16_acc(d, desc_add(hd, (ks >> 2) * 16384 + (ks & 3) * 32),
-                        desc_add(wd, (ks >> 2) * W2_KSTRIDE + (ks & 3) * 32), idesc2);
-          mma_commit(w_empty(s));
-          mma_commit(h_empty(hb));
-          if (h2 == nh - 1) mma_commit(d2_full(buf));
-          ++ws;
-          if (++h2 == nh) {
-            h2 = 0;
-            ++it2;
-          }
+        for (int ks = 1; ks < 4 * KB; ++ks)
+          umma_acc(d, desc_add(ad, (ks >> 2) * 16384 + (ks & 3) * 32), desc_add(wd, (ks >> 2) * 16384 + (ks & 3) * 32),
+                      idesc1);
+        umma_commit(w_empty(s));
+        umma_commit(d1_full(db));
+        if (h1 == nh - 1) umma_commit(a_empty(buf));
+        ++ws;
+        if (++h1 == nh) {
+          h1 = 0;
+          ++it1;
         }
       }
-      // Every MMA has completed before TMEM is freed, whether or not a consumer gave up.
-      mma_commit(drain);
-      mbar_wait_drain(drain, 0, p.err);
+      if (j >= LAG) {  // second GEMM of step i = j - LAG: D2[tile] += H[i % NBUF] W2[chunk]
+        const int i = j - LAG, buf = it2 & 1, hb = i % NBUF, s = ws % STAGES;
+        if (!warp_wait(h_full(hb), (i / NBUF) & 1, abort_flag, p.err, kErrWaitMma) ||
+            !warp_wait(w_full(s), (ws / STAGES) & 1, abort_flag, p.err, kErrWaitMma) ||
+            (h2 == 0 && !warp_wait(d2_empty(buf), ((it2 >> 1) & 1) ^ 1, abort_flag, p.err, kErrWaitMma)))
+          break;
+        tc_fence_after();
+        const uint64_t hd = desc_add(h_desc, hb * 32768), wd = desc_add(w_desc, s * W_BYTES);
+        const uint32_t d = tmem + 256 + buf * 128;
+        if (h2 == 0)
+          umma_first(d, hd, wd, idesc2);
+        else
+          umma_acc(d, hd, wd, idesc2);
+#pragma unroll
+        for (int ks = 1; ks < 8; ++ks)
+          umma_acc(d, desc_add(hd, (ks >> 2) * 16384 + (ks & 3) * 32),
+                      desc_add(wd, (ks >> 2) * W2_KSTRIDE + (ks & 3) * 32), idesc2);
+        umma_commit(w_empty(s));
+        umma_commit(h_empty(hb));
+        if (h2 == nh - 1) umma_commit(d2_full(buf));
+        ++ws;
+        if (++h2 == nh) {
+          h2 = 0;
+          ++it2;
+        }
+      }
     }
-    __syncwarp();
+    // Every MMA has completed before TMEM is freed, whether or not a consumer gave up.
+    umma_commit(drain);
+    mbar_wait_drain(drain, 0, p.err);
   } else if (warp < 6) {
     // ---- row warps: LayerNorm of tile it+1, then the second epilogue of tile it ----
     const int q = warp & 3;  // TMEM lane quarter this warp may read
@@ -599,7 +596,7 @@ __device__ __forceinline__ void prep_columns(PrepShared &sh, const MatrixDev &m,
                                              float *__restrict__ vec) {
   float(&red)[32][33] = sh.red;
   float(&col_scale)[32] = sh.col_scale;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warp = warp_index_uniform(), lane = threadIdx.x & 31;
   constexpr bool codes = FMT == AF2_WEIGHTS_Q8_CHANNEL;
   // Pass 1: the column's values for this warp (k = warp, warp + 32, ...) in
   // batches, all loads of a batch in flight together.

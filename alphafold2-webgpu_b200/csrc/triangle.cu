@@ -219,7 +219,7 @@ __global__ void __launch_bounds__(PJ_THREADS, 1)
   const uint32_t out_free = bar0 + 8u * 15;  // the staged tile has been read by the TMA stores
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + PJ_OFF_BAR + 192);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + PJ_OFF_BAR + 200);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warp = warp_index_uniform(), lane = threadIdx.x & 31;
 
   for (int m = 0; m < 4; ++m)
     load_weight_matrix(smem + m * 32768, p.w16 + (size_t)m * C * C, threadIdx.x, PJ_THREADS);
@@ -277,45 +277,45 @@ __global__ void __launch_bounds__(PJ_THREADS, 1)
       }
     }
   } else if (warp == 1) {
-    // ---- MMA issuer ----
-    if (lane == 0) {
-      constexpr uint32_t kIdesc = idesc_f16_f32(128, PJ_TILE);
-      int it = 0;
-      bool ok = true;
-      for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x, ++it) {
-        const int s = it % PJ_STAGES;
-        const uint32_t ph = (it / PJ_STAGES) & 1;
-        const int buf = it & 1;
-        const uint32_t bph = (it >> 1) & 1;
-        if (!mbar_wait(acc_empty(buf), bph ^ 1, abort_flag, p.err, kErrWaitMma) ||
-            !mbar_wait(z_ready(s), ph, abort_flag, p.err, kErrWaitMma)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t zs = sbase + PJ_OFF_STAGE + s * PJ_STAGE_BYTES;
+    // ---- MMA issuer: the whole warp runs the loop, one elected lane issues ----
+    constexpr uint32_t kIdesc = idesc_f16_f32(128, PJ_TILE);
+    const uint64_t w_base = sdesc_k_sw128(sbase), z_base = sdesc_k_sw128(sbase + PJ_OFF_STAGE);
+    int s = 0, buf = 0;
+    uint32_t ph = 0, bph = 0;
+    for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x) {
+      if (!warp_wait(acc_empty(buf), bph ^ 1, abort_flag, p.err, kErrWaitMma) ||
+          !warp_wait(z_ready(s), ph, abort_flag, p.err, kErrWaitMma))
+        break;
+      tc_fence_after();
+      const uint64_t zd = z_base + s * (PJ_STAGE_BYTES >> 4);
 #pragma unroll
-        for (int m = 0; m < 4; ++m) {
-          const uint32_t d = tmem + buf * 256 + m * PJ_TILE;
+      for (int m = 0; m < 4; ++m) {
+        const uint32_t d = tmem + buf * 256 + m * PJ_TILE;
 #pragma unroll
-          for (int kc = 0; kc < 2; ++kc) {
+        for (int kc = 0; kc < 2; ++kc) {
 #pragma unroll
-            for (int ks = 0; ks < 4; ++ks) {
-              const uint64_t ad = sdesc_k_sw128(sbase + (m * 2 + kc) * 16384 + ks * 32);
-              const uint64_t bd = sdesc_k_sw128(zs + kc * PJ_CHUNK + ks * 32);
-              mma_f16(d, ad, bd, kIdesc, (kc | ks) != 0);
-            }
+          for (int ks = 0; ks < 4; ++ks) {
+            const uint64_t ad = w_base + (((m * 2 + kc) * 16384 + ks * 32) >> 4);
+            const uint64_t bd = zd + ((kc * PJ_CHUNK + ks * 32) >> 4);
+            if (kc == 0 && ks == 0)
+              umma_first(d, ad, bd, kIdesc);
+            else
+              umma_acc(d, ad, bd, kIdesc);
           }
         }
-        mma_commit(z_empty(s));
-        mma_commit(acc_full(buf));
       }
-      // Every MMA has completed before TMEM is freed, whether or not a consumer gave up.
-      (void)ok;
-      mma_commit(drain);
-      mbar_wait_drain(drain, 0, p.err);
+      umma_commit(z_empty(s));
+      umma_commit(acc_full(buf));
+      if (++s == PJ_STAGES) {
+        s = 0;
+        ph ^= 1;
+      }
+      buf ^= 1;
+      if (buf == 0) bph ^= 1;
     }
-    __syncwarp();
+    // Every MMA has completed before TMEM is freed, whether or not a consumer gave up.
+    umma_commit(drain);
+    mbar_wait_drain(drain, 0, p.err);
   } else if (warp < 6) {
     // ---- LayerNorm of the z tile, in place, 16-bit -> f16 ----
     const int grp = (warp - 2) >> 1;
@@ -473,7 +473,7 @@ __global__ void __launch_bounds__(CT_THREADS, 1)
   const uint32_t drain = bar0 + 8u * (2 * CT_STAGES + 4);
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + CT_OFF_BAR + 128);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + CT_OFF_BAR + 136);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warp = warp_index_uniform(), lane = threadIdx.x & 31;
   const int tiles_per_h = p.tiles_m * p.tiles_n;
 
   if (threadIdx.x == 0) {
@@ -526,45 +526,46 @@ __global__ void __launch_bounds__(CT_THREADS, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      constexpr uint32_t kIdesc = idesc_f16_f32(CT_BM, CT_BN);
-      const uint64_t a_desc = sdesc_k_sw128(sbase);  // stage s: + s * CT_STAGE_BYTES; B follows A
-      int it = 0, tile_it = 0;
-      bool ok = true;
-      for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x, ++tile_it) {
-        const int buf = tile_it & 1;
-        const uint32_t bph = (tile_it >> 1) & 1;
-        if (!mbar_wait(acc_empty(buf), bph ^ 1, abort_flag, p.err, kErrWaitMma)) {
+    // the whole warp runs the issue loop (uniform waits, running descriptors); one elected lane issues
+    constexpr uint32_t kIdesc = idesc_f16_f32(CT_BM, CT_BN);
+    const uint64_t a_base = sdesc_k_sw128(sbase);  // stage s: + s * CT_STAGE_BYTES; B follows A
+    uint64_t ad = a_base;
+    int s = 0, buf = 0;
+    uint32_t ph = 0, bph = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
+      if (!warp_wait(acc_empty(buf), bph ^ 1, abort_flag, p.err, kErrWaitMma)) break;
+      tc_fence_after();
+      const uint32_t d = tmem + buf * CT_BN;
+      for (int kb = 0; kb < p.k_blocks; ++kb) {
+        if (!warp_wait(full(s), ph, abort_flag, p.err, kErrWaitMma)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t d = tmem + buf * CT_BN;
-        for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
-          const int s = it % CT_STAGES;
-          const uint32_t ph = (it / CT_STAGES) & 1;
-          if (!mbar_wait(full(s), ph, abort_flag, p.err, kErrWaitMma)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint64_t ad = desc_add(a_desc, s * CT_STAGE_BYTES), bd = desc_add(ad, CT_A_BYTES);
-          if (kb == 0)
-            mma_f16_first(d, ad, bd, kIdesc);
-          else
-            mma_f16_acc(d, ad, bd, kIdesc);
+        const uint64_t bd = ad + (CT_A_BYTES >> 4);
+        if (kb == 0)
+          umma_first(d, ad, bd, kIdesc);
+        else
+          umma_acc(d, ad, bd, kIdesc);
 #pragma unroll
-          for (int ks = 1; ks < CT_BK / 16; ++ks) mma_f16_acc(d, desc_add(ad, ks * 32), desc_add(bd, ks * 32), kIdesc);
-          mma_commit(empty(s));
+        for (int ks = 1; ks < CT_BK / 16; ++ks) umma_acc(d, ad + ks * 2, bd + ks * 2, kIdesc);
+        umma_commit(empty(s));
+        ad += CT_STAGE_BYTES >> 4;
+        if (++s == CT_STAGES) {
+          s = 0;
+          ph ^= 1;
+          ad = a_base;
         }
-        if (ok) mma_commit(acc_full(buf));
       }
-      // Every MMA has completed before TMEM is freed, whether or not a consumer gave up.
-      (void)ok;
-      mma_commit(drain);
-      mbar_wait_drain(drain, 0, p.err);
+      if (!ok) break;
+      umma_commit(acc_full(buf));
+      buf ^= 1;
+      if (buf == 0) bph ^= 1;
     }
-    __syncwarp();
+    // Every MMA has completed before TMEM is freed, whether or not a consumer gave up.
+    umma_commit(drain);
+    mbar_wait_drain(drain, 0, p.err);
   } else {
     const int q = warp & 3;
     const int row = q * 32 + lane;
@@ -667,7 +668,7 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
   // Per-channel vectors are read straight from global memory: every lane of a
   // warp reads the same element, one broadcast through L1.
   const float *__restrict__ vbz = p.vec + kVBZ * C, *__restrict__ vbg = p.vec + kVBG * C;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warp = warp_index_uniform(), lane = threadIdx.x & 31;
   const bool staged_out = sizeof(OT) == 2 && p.cz == C;
 
   load_weight_matrix(smem, p.w16 + (size_t)kWZ * C * C, threadIdx.x, OP_THREADS);
@@ -726,45 +727,49 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      constexpr uint32_t kIdesc = idesc_f16_f32(128, 128);
-      constexpr uint32_t kIdescMn = idesc_f16_f32_amn(128, 128);
-      int it = 0;
-      bool ok = true;
-      for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x, ++it) {
-        const int s = it % OP_STAGES;
-        const uint32_t ph = (it / OP_STAGES) & 1;
-        const int buf = it & 1;
-        const uint32_t bph = (it >> 1) & 1;
-        if (!mbar_wait(acc_empty(buf), bph ^ 1, abort_flag, p.err, kErrWaitMma) ||
-            !mbar_wait(ready(s), ph, abort_flag, p.err, kErrWaitMma)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t xs = sbase + OP_OFF_STAGE + s * OP_STAGE_BYTES, zs = xs + OP_X_BYTES;
-        const uint32_t d = tmem + buf * 256;
+    // the whole warp runs the issue loop (uniform waits, running descriptors); one elected lane issues
+    constexpr uint32_t kIdesc = idesc_f16_f32(128, 128);
+    constexpr uint32_t kIdescMn = idesc_f16_f32_amn(128, 128);
+    const uint64_t x_base = sdesc_mn_sw128(sbase + OP_OFF_STAGE, 16384, 1024);
+    const uint64_t z_base = sdesc_k_sw128(sbase + OP_OFF_STAGE + OP_X_BYTES);
+    const uint64_t wz = sdesc_k_sw128(sbase), wg = sdesc_k_sw128(sbase + 32768);
+    int s = 0, buf = 0;
+    uint32_t ph = 0, bph = 0;
+    for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x) {
+      if (!warp_wait(acc_empty(buf), bph ^ 1, abort_flag, p.err, kErrWaitMma) ||
+          !warp_wait(ready(s), ph, abort_flag, p.err, kErrWaitMma))
+        break;
+      tc_fence_after();
+      const uint64_t xd = x_base + s * (OP_STAGE_BYTES >> 4), zd = z_base + s * (OP_STAGE_BYTES >> 4);
+      const uint32_t d = tmem + buf * 256;
 #pragma unroll
-        for (int kc = 0; kc < 2; ++kc) {
+      for (int kc = 0; kc < 2; ++kc) {
 #pragma unroll
-          for (int ks = 0; ks < 4; ++ks) {
-            const uint32_t koff = kc * 16384 + ks * 32;
-            // X is MN-major: K step (kc * 4 + ks) * 16 rows = that many 1024-byte atoms / 8 * 2.
-            mma_f16(d, sdesc_mn_sw128(xs + (kc * 4 + ks) * 2048, 16384, 1024), sdesc_k_sw128(sbase + koff),
-                    kIdescMn, (kc | ks) != 0);
-            mma_f16(d + 128, sdesc_k_sw128(zs + koff), sdesc_k_sw128(sbase + 32768 + koff), kIdesc,
-                    (kc | ks) != 0);
+        for (int ks = 0; ks < 4; ++ks) {
+          const uint32_t koff = (kc * 16384 + ks * 32) >> 4;
+          // X is MN-major: K step (kc * 4 + ks) * 16 rows = that many 1024-byte atoms / 8 * 2.
+          const uint64_t xk = xd + (((kc * 4 + ks) * 2048) >> 4);
+          if (kc == 0 && ks == 0) {
+            umma_first(d, xk, wz + koff, kIdescMn);
+            umma_first(d + 128, zd + koff, wg + koff, kIdesc);
+          } else {
+            umma_acc(d, xk, wz + koff, kIdescMn);
+            umma_acc(d + 128, zd + koff, wg + koff, kIdesc);
           }
         }
-        mma_commit(empty(s));
-        mma_commit(acc_full(buf));
       }
-      // Every MMA has completed before TMEM is freed, whether or not a consumer gave up.
-      (void)ok;
-      mma_commit(drain);
-      mbar_wait_drain(drain, 0, p.err);
+      umma_commit(empty(s));
+      umma_commit(acc_full(buf));
+      if (++s == OP_STAGES) {
+        s = 0;
+        ph ^= 1;
+      }
+      buf ^= 1;
+      if (buf == 0) bph ^= 1;
     }
-    __syncwarp();
+    // Every MMA has completed before TMEM is freed, whether or not a consumer gave up.
+    umma_commit(drain);
+    mbar_wait_drain(drain, 0, p.err);
   } else if (warp < 10) {
     // ---- LN_out of X in place (warps 2-5) and LN_in of z (warps 6-9) ----
     // X arrives MN-major: two 64-pair blocks 16 KB apart, each 128 h-rows of
