@@ -44,7 +44,9 @@ def encode_triangle_multiplication_sharded_tensors(device: Device, direction, pa
                                                    length: int, *, out=None, residual: bool = True,
                                                    epsilon: float = 1e-5, stream: int = 0):
     """Row-sharded device form: pair_rows [L, N, c_z] and mask_rows [L, N] are this
-    rank's rows (L = N / nranks).  Collective: every rank calls it together."""
+    rank's rows (L = N / nranks, a multiple of 64; nranks divides 128).  The
+    contraction is sharded by hidden channel between two all-to-alls.
+    Collective: every rank calls it together."""
     rows, n, cz = pair_rows.shape
     if n != length:
         raise _lib.RangeError("pair_rows must be [rows, length, c_z]")

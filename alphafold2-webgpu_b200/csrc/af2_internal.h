@@ -42,7 +42,6 @@ enum ProfileKernel {
   kProfOpmCount,
   kProfOpmOuter,
   kProfOpmOutput,
-  kProfShardTranspose,
   kProfOpmFused,
   kProfCount
 };
@@ -89,6 +88,8 @@ af2_status ensure(af2_ctx *ctx, DeviceBuffer &buf, size_t bytes, const char *wha
 bool encode_map_3d(CUtensorMap *map, CUtensorMapDataType dtype, const void *base, uint64_t d0, uint64_t d1,
                    uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t b0, uint32_t b1,
                    uint32_t b2, CUtensorMapSwizzle swizzle);
+bool encode_map_4d(CUtensorMap *map, CUtensorMapDataType dtype, const void *base, const uint64_t (&dims)[4],
+                   const uint64_t (&strides_bytes)[3], const uint32_t (&box)[4], CUtensorMapSwizzle swizzle);
 
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
@@ -114,30 +115,38 @@ struct TriangleLayout {
   int64_t n = 0, cz = 0, ch = 0;
   int64_t rows = 0;         // pair rows held here (n, or n / ranks when the pair is sharded by rows)
   int64_t block_rows = 0;   // output rows per block
+  int64_t ranks = 1;        // channel shards of the contraction: the ranks of a row-sharded pair
+  int64_t hq = 0;           // hidden channels per shard (128 / ranks)
   int64_t kp = 0;           // k pitch (elements) of the projected operands
   int64_t jp = 0;           // row pitch (elements) of the contracted block
-  int64_t ab_rs = 0;        // row pitch (elements) of the projected operands [row][h][k]
-  int64_t x_hs = 0;         // channel pitch (elements) of the contracted block (full block)
+  int64_t ab_rs = 0;        // row pitch (elements) of the projected operands [group][row][hq][kp]
+  int64_t ab_rows = 0;      // rows of one channel group of the projected operands
+  int64_t x_hs = 0;         // channel pitch (elements) of the contracted block
   bool pad_z = false;       // z is re-laid as f16 [P][128] before the kernels
-  size_t off_w16 = 0, off_vec = 0, off_z16 = 0, off_a = 0, off_b = 0, off_x = 0, total = 0;
+  size_t off_w16 = 0, off_vec = 0, off_z16 = 0, off_a = 0, off_b = 0, off_x = 0;
+  size_t off_a_all = 0, off_b_all = 0, off_x_all = 0;  // channel-sharded: exchanged operands and block
+  size_t total = 0;
 };
 
-// rows < n: the pair rows [rank * rows, (rank + 1) * rows) of a row-sharded pair.
-TriangleLayout triangle_layout(int64_t n, int64_t cz, int64_t ch, int64_t block_rows, int z_dtype, int64_t rows = 0);
+// One GPU: rows = 0.  A row-sharded pair: rows = n / ranks of them here; the
+// layout then depends on the direction (the incoming product's k runs over
+// the local rows).
+TriangleLayout triangle_layout(int64_t n, int64_t cz, int64_t ch, int64_t block_rows, int z_dtype, int64_t rows = 0,
+                               int direction = 0);
 
-// How the projected b operand becomes whole on a row-sharded pair: this rank's
-// rows are written at row b_row0 of the full operand, then exchanged in place.
-struct TriangleExchange {
-  int64_t b_row0 = 0;
-  // all-gathers `bytes_per_rank` bytes per rank in place into `full` on `stream`
-  af2_status (*all_gather)(af2_ctx *ctx, void *full, size_t bytes_per_rank, cudaStream_t stream) = nullptr;
+// Exchange of the channel-sharded contraction: block p of `send` (blocks
+// `stride` bytes apart, `bytes` each) goes to rank p, and rank p's block for
+// this rank lands in block p of `recv`.
+struct TriangleShard {
+  int ranks = 1, rank = 0;
+  af2_status (*all_to_all)(af2_ctx *ctx, const void *send, void *recv, size_t stride, size_t bytes,
+                           cudaStream_t stream) = nullptr;
 };
 
 // Launches the whole op on `stream`; the workspace holds TriangleLayout::total bytes.
 af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L, const void *z, int z_dtype,
                            const float *mask, const float *packed, double eps, int residual, void *out,
-                           int out_dtype, void *workspace, cudaStream_t stream,
-                           const TriangleExchange *exchange = nullptr);
+                           int out_dtype, void *workspace, cudaStream_t stream, const TriangleShard *shard = nullptr);
 
 // ---- transition (transition.cu) ----
 
@@ -254,8 +263,6 @@ af2_status opm_launch(af2_ctx *ctx, const OpmLayout &L, const void *m, int m_dty
 
 // ---- row-sharded operators (comm.cu) ----
 
-af2_status shard_transpose(af2_ctx *ctx, const void *src, void *dst, void *pack, void *recv, int rows, int n,
-                           size_t pair_bytes, cudaStream_t stream);
 void comm_destroy(af2_ctx *ctx);
 
 }  // namespace af2

@@ -56,7 +56,7 @@ const char *profile_name(int id) {
       "triangle.output",     "transition.prepare",   "transition.normalize", "transition.fused",
       "q8.decode",           "weights.prepare",      "activations.convert",  "linear",
       "opm.normalize",       "opm.project",          "opm.count",         "opm.outer",
-      "opm.output",          "shard.transpose",      "opm.fused"};
+      "opm.output",          "opm.fused"};
   return (id >= 0 && id < kProfCount) ? names[id] : nullptr;
 }
 
@@ -115,6 +115,18 @@ bool encode_map_3d(CUtensorMap *map, CUtensorMapDataType dtype, const void *base
   const cuuint32_t estr[3] = {1, 1, 1};
   return g_encode(map, dtype, 3, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                   swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool encode_map_4d(CUtensorMap *map, CUtensorMapDataType dtype, const void *base, const uint64_t (&dims)[4],
+                   const uint64_t (&strides_bytes)[3], const uint32_t (&box)[4], CUtensorMapSwizzle swizzle) {
+  std::call_once(g_encode_once, load_encode);
+  if (!g_encode) return false;
+  const cuuint64_t d[4] = {dims[0], dims[1], dims[2], dims[3]};
+  const cuuint64_t st[3] = {strides_bytes[0], strides_bytes[1], strides_bytes[2]};
+  const cuuint32_t b[4] = {box[0], box[1], box[2], box[3]};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  return g_encode(map, dtype, 4, const_cast<void *>(base), d, st, b, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 namespace {

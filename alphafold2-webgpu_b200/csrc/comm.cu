@@ -3,21 +3,20 @@
 // exchange steps.  The reference has no multi-GPU code; this follows the
 // partitioning its operators allow:
 //
-//   outgoing triangle  x[i,j] = sum_k a[i,k] b[j,k]: every rank projects its
-//                      own pair rows; the projected b operand ([row][h][k],
-//                      one contiguous block per rank) is all-gathered in place,
-//                      and each rank contracts and finishes its own rows;
-//   incoming triangle  incoming(z) = T(outgoing(T(z))) with the transposed
-//                      mask, T the transpose of the pair (x[i,j] = sum_k a[k,j]
-//                      b[k,i] is the outgoing product of the transposed pair):
-//                      the pair and the mask are transposed across ranks by an
-//                      all-to-all (pack, NCCL send/recv, unpack), the outgoing
-//                      path runs on the transposed rows, and the result is
-//                      transposed back.  Every operand value and every
-//                      accumulation order is the one of the single-GPU path, so
-//                      the sharded result is bit-identical to it.
-//   transition / OPM   row-local (every output row depends on its own pair row,
-//                      and on the whole MSA): no exchange.
+//   triangle (both)    every rank projects its own pair rows, split into R
+//                      groups of 128 / R hidden channels; an all-to-all gives
+//                      every rank its channel group of every rank's rows, so
+//                      each rank contracts its channels over the whole N x N
+//                      (the incoming product's k running over the ranks' row
+//                      blocks in order); a second all-to-all returns all 128
+//                      channels of each rank's own rows for the output
+//                      projection.  Per direction a rank moves 3 (R-1)/R^2 of a
+//                      projected operand; every operand value and accumulation
+//                      order is the single-GPU one, so results are bit-identical.
+//   outer product mean every rank normalises and projects its own residue
+//                      columns of the (replicated) MSA; the right operand is
+//                      all-gathered and each rank finishes its own rows.
+//   transition         row-local: no exchange.
 #include <dlfcn.h>
 #include <nccl.h>
 
@@ -33,6 +32,8 @@
 
 namespace af2 {
 namespace {
+
+constexpr int64_t C_CHANNELS = 128;  // hidden channels of the padded triangle kernels
 
 // NCCL entry points, taken from the libnccl.so.2 of the process (the one
 // torch.distributed already loaded, or the system's) when a communicator is
@@ -80,85 +81,27 @@ af2_status nccl_fail(af2_ctx *ctx, ncclResult_t r, const char *what) {
 
 ncclComm_t comm_of(af2_ctx *ctx) { return static_cast<ncclComm_t>(ctx->nccl_comm); }
 
-// pack[s][j][i][:] = src[i][s * rows + j][:] for every destination rank s:
-// the block of this rank's rows that rank s needs, already transposed.
-// unit = bytes moved per thread step (16, 4 or 2).
-template <typename U>
-__global__ void transpose_pack_kernel(const U *__restrict__ src, U *__restrict__ pack, int rows, int n,
-                                      int units_per_pair) {
-  const int64_t total = static_cast<int64_t>(rows) * n * units_per_pair;
-  for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
-       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int u = static_cast<int>(idx % units_per_pair);
-    const int64_t pair = idx / units_per_pair;  // destination order: (s, j, i)
-    const int i = static_cast<int>(pair % rows);
-    const int64_t sj = pair / rows;              // s * rows + j = the source column
-    pack[idx] = src[(static_cast<int64_t>(i) * n + sj) * units_per_pair + u];
-  }
-}
+}  // namespace
 
-// dst[j][r * rows + i][:] = recv[r][j][i][:]: the blocks received from every
-// rank r placed at their columns.
-template <typename U>
-__global__ void transpose_unpack_kernel(const U *__restrict__ recv, U *__restrict__ dst, int rows, int n,
-                                        int units_per_pair) {
-  const int64_t total = static_cast<int64_t>(rows) * n * units_per_pair;
-  for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
-       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int u = static_cast<int>(idx % units_per_pair);
-    const int64_t pair = idx / units_per_pair;  // destination order: (j, column)
-    const int64_t col = pair % n;
-    const int j = static_cast<int>(pair / n);
-    const int r = static_cast<int>(col / rows), i = static_cast<int>(col % rows);
-    dst[idx] = recv[((static_cast<int64_t>(r) * rows + j) * rows + i) * units_per_pair + u];
-  }
-}
-
-template <typename U>
-af2_status launch_transpose_kernels(af2_ctx *ctx, const void *src, void *pack, void *recv, void *dst, int rows, int n,
-                                    size_t pair_bytes, cudaStream_t stream) {
-  const int upp = static_cast<int>(pair_bytes / sizeof(U));
-  const int64_t total = static_cast<int64_t>(rows) * n * upp;
-  const unsigned blocks = static_cast<unsigned>(std::min<int64_t>((total + 255) / 256, 16LL * ctx->sm_count));
-  {
-    LaunchScope scope(ctx, stream, kProfShardTranspose);
-    transpose_pack_kernel<U><<<blocks, 256, 0, stream>>>(static_cast<const U *>(src), static_cast<U *>(pack), rows, n,
-                                                         upp);
-  }
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(ctx, e, "transpose pack");
-  // all-to-all: block s of pack goes to rank s; block r of recv comes from rank r
-  const size_t block = static_cast<size_t>(rows) * rows * pair_bytes;
+// Block p of `send` to rank p, rank p's block into block p of `recv` (blocks
+// `stride` bytes apart, `bytes` each); this rank's own block is a device copy.
+static af2_status nccl_all_to_all(af2_ctx *ctx, const void *send, void *recv, size_t stride, size_t bytes,
+                                  cudaStream_t stream) {
+  const char *src = static_cast<const char *>(send);
+  char *dst = static_cast<char *>(recv);
   ncclComm_t comm = comm_of(ctx);
   ncclResult_t r = g_nccl.GroupStart();
   for (int peer = 0; r == ncclSuccess && peer < ctx->nranks; ++peer) {
-    r = g_nccl.Send(static_cast<const char *>(pack) + peer * block, block, ncclChar, peer, comm, stream);
-    if (r == ncclSuccess) r = g_nccl.Recv(static_cast<char *>(recv) + peer * block, block, ncclChar, peer, comm, stream);
+    if (peer == ctx->rank) continue;
+    r = g_nccl.Send(src + peer * stride, bytes, ncclChar, peer, comm, stream);
+    if (r == ncclSuccess) r = g_nccl.Recv(dst + peer * stride, bytes, ncclChar, peer, comm, stream);
   }
   const ncclResult_t r2 = g_nccl.GroupEnd();
-  if (r != ncclSuccess) return nccl_fail(ctx, r, "pair transpose all-to-all");
-  if (r2 != ncclSuccess) return nccl_fail(ctx, r2, "pair transpose all-to-all");
-  {
-    LaunchScope scope(ctx, stream, kProfShardTranspose);
-    transpose_unpack_kernel<U><<<blocks, 256, 0, stream>>>(static_cast<const U *>(recv), static_cast<U *>(dst), rows,
-                                                           n, upp);
-  }
-  e = cudaGetLastError();
-  return e == cudaSuccess ? AF2_OK : cuda_fail(ctx, e, "transpose unpack");
-}
-
-}  // namespace
-
-// The transpose of a row-sharded [n][n] pair of `pair_bytes` per pair: this
-// rank holds rows [rank * rows, (rank + 1) * rows) of src and receives the
-// same rows of the transpose in dst.  pack and recv hold rows * n pairs each.
-af2_status shard_transpose(af2_ctx *ctx, const void *src, void *dst, void *pack, void *recv, int rows, int n,
-                           size_t pair_bytes, cudaStream_t stream) {
-  if (pair_bytes % 16 == 0)
-    return launch_transpose_kernels<uint4>(ctx, src, pack, recv, dst, rows, n, pair_bytes, stream);
-  if (pair_bytes % 4 == 0)
-    return launch_transpose_kernels<uint32_t>(ctx, src, pack, recv, dst, rows, n, pair_bytes, stream);
-  return launch_transpose_kernels<uint16_t>(ctx, src, pack, recv, dst, rows, n, pair_bytes, stream);
+  if (r != ncclSuccess) return nccl_fail(ctx, r, "channel all-to-all");
+  if (r2 != ncclSuccess) return nccl_fail(ctx, r2, "channel all-to-all");
+  const cudaError_t e = cudaMemcpyAsync(dst + ctx->rank * stride, src + ctx->rank * stride, bytes,
+                                        cudaMemcpyDeviceToDevice, stream);
+  return e == cudaSuccess ? AF2_OK : cuda_fail(ctx, e, "channel all-to-all (own block)");
 }
 
 static af2_status nccl_all_gather_in_place(af2_ctx *ctx, void *full, size_t bytes_per_rank, cudaStream_t stream) {
@@ -238,38 +181,21 @@ af2_status af2_triangle_multiplication_sharded(af2_ctx *ctx, int direction, cons
                          (out_dtype == AF2_F32 || out_dtype == AF2_F16 || out_dtype == AF2_BF16);
   if (!dtypes_ok) return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "dtype must be AF2_F32, AF2_F16 or AF2_BF16");
   const int64_t n = shape->length, R = ctx->nranks;
-  if (n % R != 0 || (n / R) % 8 != 0)
-    return fail(ctx, AF2_ERR_UNSUPPORTED, "the sharded triangle needs length divisible by 8 x the rank count");
-  if (direction == AF2_INCOMING && out_dtype != z_dtype)
-    return fail(ctx, AF2_ERR_UNSUPPORTED, "the sharded incoming update writes the dtype of z");
+  if (C_CHANNELS % R != 0 || n % R != 0 || (n / R) % 64 != 0)
+    return fail(ctx, AF2_ERR_UNSUPPORTED,
+                "the sharded triangle needs a rank count dividing 128 and length divisible by 64 x the rank count");
   const int64_t rows = n / R;
   const int residual = options ? options->residual : 0;
   cudaSetDevice(ctx->device);
   cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
-  const TriangleLayout L = triangle_layout(n, shape->c_z, shape->c_hidden, options ? options->block_rows : 0,
-                                           z_dtype, rows);
-  if ((st = ensure(ctx, ctx->workspace, L.total, "triangle scratch")) != AF2_OK) return st;
-  TriangleExchange ex;
-  ex.b_row0 = ctx->rank * rows;
-  ex.all_gather = nccl_all_gather_in_place;
-  if (direction == AF2_OUTGOING)
-    return triangle_launch(ctx, AF2_OUTGOING, L, z, z_dtype, mask, packed_weights, epsilon, residual, out, out_dtype,
-                           ctx->workspace.ptr, s, &ex);
-  // incoming: transpose the pair and the mask across ranks, take the outgoing
-  // update of the transposed rows in place, transpose back.
-  const size_t zb = z_dtype == AF2_F32 ? 4 : 2;
-  const size_t zbytes = (size_t)rows * n * shape->c_z * zb, mbytes = (size_t)rows * n * sizeof(float);
-  const size_t off_zt = 0, off_mt = align_up(zbytes, 256), off_pack = off_mt + align_up(mbytes, 256),
-               off_recv = off_pack + align_up(zbytes, 256), total = off_recv + align_up(zbytes, 256);
-  if ((st = ensure(ctx, ctx->shard_scratch, total, "pair transpose scratch")) != AF2_OK) return st;
-  uint8_t *sc = static_cast<uint8_t *>(ctx->shard_scratch.ptr);
-  void *zt = sc + off_zt, *mt = sc + off_mt, *pack = sc + off_pack, *recv = sc + off_recv;
-  if ((st = shard_transpose(ctx, z, zt, pack, recv, (int)rows, (int)n, shape->c_z * zb, s)) != AF2_OK ||
-      (st = shard_transpose(ctx, mask, mt, pack, recv, (int)rows, (int)n, sizeof(float), s)) != AF2_OK ||
-      (st = triangle_launch(ctx, AF2_OUTGOING, L, zt, z_dtype, static_cast<const float *>(mt), packed_weights,
-                            epsilon, residual, zt, z_dtype, ctx->workspace.ptr, s, &ex)) != AF2_OK)
-    return st;
-  return shard_transpose(ctx, zt, out, pack, recv, (int)rows, (int)n, shape->c_z * zb, s);
+  const TriangleLayout L = triangle_layout(n, shape->c_z, shape->c_hidden, 0, z_dtype, rows, direction);
+  if ((st = ensure(ctx, ctx->shard_scratch, L.total, "sharded triangle scratch")) != AF2_OK) return st;
+  TriangleShard sh;
+  sh.ranks = static_cast<int>(R);
+  sh.rank = ctx->rank;
+  sh.all_to_all = nccl_all_to_all;
+  return triangle_launch(ctx, direction, L, z, z_dtype, mask, packed_weights, epsilon, residual, out, out_dtype,
+                         ctx->shard_scratch.ptr, s, &sh);
 }
 
 af2_status af2_outer_product_mean_sharded(af2_ctx *ctx, const af2_opm_shape *shape, const void *m, int m_dtype,

@@ -141,10 +141,10 @@ constexpr uint32_t PJ_SMEM = PJ_OFF_BAR + 256 + 1024;
 struct ProjectArgs {
   const float *mask;
   int64_t mask_rs, mask_ks;  // mask of tile row r, pair k: mask[r * mask_rs + k * mask_ks]
-  int b_row0;                // row of the full b operand this launch's row 0 lands on
   const __half *w16;
   const float *vec;
-  int n, cz, tiles_k, total_tiles;
+  int k_extent;              // pairs k per tile row (n, or this rank's rows for a sharded incoming product)
+  int cz, tiles_k, total_tiles;
   int transposed;  // incoming: the z map is [k][j][c] and the box walks k in its outer dimension
   float eps;
   unsigned int *err;
@@ -345,7 +345,7 @@ __global__ void __launch_bounds__(PJ_THREADS, 1)
     uint8_t *stage_row = smem + PJ_OFF_OUT + op * PJ_OUT_BYTES + h * 128;
     float *msk = reinterpret_cast<float *>(smem + PJ_OFF_MASK) + e * 64;
     auto mask_at = [&](int t, int k) -> float {
-      if (t >= p.total_tiles || k >= p.n) return 0.f;
+      if (t >= p.total_tiles || k >= p.k_extent) return 0.f;
       return p.mask[(int64_t)(t / p.tiles_k) * p.mask_rs + (int64_t)k * p.mask_ks];
     };
     int t = blockIdx.x;
@@ -419,12 +419,13 @@ __global__ void __launch_bounds__(PJ_THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(out_full);
       if (storer) {
-        // both operand tiles staged: one TMA store each ([128 h] x 64 pairs of row r)
+        // both operand tiles staged: one TMA store each ([128 h] x 64 pairs of row r; with
+        // channel shards the box's outer dimension scatters the groups of 128 / ranks channels)
         if (!mbar_wait(out_full, it & 1, abort_flag, p.err, kErrWaitEpilogue)) {
           it = -1;
         } else {
-          tma_store_3d(&amap, sbase + PJ_OFF_OUT, k0, 0, r);
-          tma_store_3d(&bmap, sbase + PJ_OFF_OUT + PJ_OUT_BYTES, k0, 0, r + p.b_row0);
+          tma_store_4d(&amap, sbase + PJ_OFF_OUT, k0, 0, r, 0);
+          tma_store_4d(&bmap, sbase + PJ_OFF_OUT + PJ_OUT_BYTES, k0, 0, r, 0);
           bulk_commit();
           store_pending = true;
         }
@@ -451,9 +452,11 @@ constexpr uint32_t CT_OFF_BAR = CT_STAGES * CT_STAGE_BYTES;
 constexpr uint32_t CT_SMEM = CT_OFF_BAR + 256 + 1024;
 
 struct ContractArgs {
-  __half *x_out;  // [128][row_count][jp]
-  int64_t x_hs, x_rs;
+  __half *x_out;  // [row_count / block_rows_out][channels][block_rows_out][jp]
+  int64_t x_hs, x_rs, x_bs;  // channel, row and block pitches of x_out
+  int block_rows_out;        // product rows per block of x_out (one block unless channel-sharded)
   int n, row_begin, row_count;
+  int k_split;               // k extent of one block of the operands' 4th map dimension
   int tiles_m, tiles_n, k_blocks, total_tiles;
   float scale;
   unsigned int *err;
@@ -507,6 +510,7 @@ __global__ void __launch_bounds__(CT_THREADS, 1)
       for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
         const int h = t / tiles_per_h, rem = t % tiles_per_h;
         const int mi = rem / p.tiles_n, ni = rem % p.tiles_n;
+        int kl = 0, kr = 0;  // k = kr * k_split + kl: the operands may hold k in blocks (one per rank)
         for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
           const int s = it % CT_STAGES;
           const uint32_t ph = (it / CT_STAGES) & 1;
@@ -516,8 +520,13 @@ __global__ void __launch_bounds__(CT_THREADS, 1)
           }
           const uint32_t dst = sbase + s * CT_STAGE_BYTES;
           mbar_arrive_expect_tx(full(s), CT_STAGE_BYTES);
-          tma_load_3d(dst, &amap, full(s), kb * CT_BK, h, p.row_begin + mi * CT_BM);
-          tma_load_3d(dst + CT_A_BYTES, &bmap, full(s), kb * CT_BK, h, ni * CT_BN);
+          tma_load_4d(dst, &amap, full(s), kl, h, p.row_begin + mi * CT_BM, kr);
+          tma_load_4d(dst + CT_A_BYTES, &bmap, full(s), kl, h, ni * CT_BN, kr);
+          kl += CT_BK;
+          if (kl >= p.k_split) {
+            kl = 0;
+            ++kr;
+          }
         }
       }
       {  // every load issued has landed before the CTA exits (immediate unless a consumer gave up)
@@ -577,11 +586,12 @@ __global__ void __launch_bounds__(CT_THREADS, 1)
       const uint32_t bph = (tile_it >> 1) & 1;
       if (!warp_wait(acc_full(buf), bph, abort_flag, p.err, kErrWaitEpilogue)) break;
       tc_fence_after();
-      const int gi = mi * CT_BM + row;  // row inside this block
+      const int gi = mi * CT_BM + row;  // row inside this launch
       const bool row_ok = gi < p.row_count;
+      const int blk = gi / p.block_rows_out, gl = gi - blk * p.block_rows_out;
       const int j0 = ni * CT_BN;
       const bool full_cols = j0 + CT_BN <= p.n;
-      __half *xr = p.x_out + h * p.x_hs + (int64_t)gi * p.x_rs + j0;
+      __half *xr = p.x_out + blk * p.x_bs + h * p.x_hs + (int64_t)gl * p.x_rs + j0;
       const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * CT_BN;
 #pragma unroll 1
       for (int chunk = 0; chunk < CT_BN / 32; ++chunk) {
@@ -993,34 +1003,47 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
 // Host side.
 // ---------------------------------------------------------------------------
 
-TriangleLayout triangle_layout(int64_t n, int64_t cz, int64_t ch, int64_t block_rows, int z_dtype, int64_t rows) {
+TriangleLayout triangle_layout(int64_t n, int64_t cz, int64_t ch, int64_t block_rows, int z_dtype, int64_t rows,
+                               int direction) {
   using tri::kChannelPad;
   TriangleLayout L;
   L.n = n;
   L.cz = cz;
   L.ch = ch;
   L.rows = (rows <= 0 || rows > n) ? n : rows;
-  L.block_rows = (block_rows <= 0 || block_rows > L.rows) ? L.rows : block_rows;
-  L.kp = static_cast<int64_t>(align_up(static_cast<size_t>(n), 8));
-  L.jp = L.kp;
+  L.ranks = n / L.rows;
+  L.hq = tri::C / L.ranks;
+  const bool sharded = L.ranks > 1;
+  L.block_rows = (!sharded && block_rows > 0 && block_rows < L.rows) ? block_rows : L.rows;
+  // Projected operands [group][row][hq][k]: one group of hq channels per rank.  Outgoing:
+  // rows i of this rank x all k; incoming: all rows j x this rank's k (its pair rows).
+  const int64_t k_extent = (sharded && direction == AF2_INCOMING) ? L.rows : n;
+  L.ab_rows = (sharded && direction == AF2_INCOMING) ? n : L.rows;
+  L.kp = static_cast<int64_t>(align_up(static_cast<size_t>(k_extent), 8));
+  L.jp = static_cast<int64_t>(align_up(static_cast<size_t>(n), 8));
   // Pitches are padded by 128 bytes so that rows and channel planes do not sit
   // an exact power of two apart (2^k-byte vectors times 2^k of them).
-  L.ab_rs = tri::C * L.kp + kChannelPad;
+  L.ab_rs = L.hq * L.kp + kChannelPad;
   L.x_hs = L.block_rows * L.jp + kChannelPad;
   L.pad_z = (z_dtype == AF2_F32) || cz != tri::C;
+  const size_t ab_bytes = sizeof(__half) * (size_t)L.ranks * L.ab_rows * L.ab_rs;
+  const size_t x_bytes = sizeof(__half) * (size_t)tri::C * L.x_hs;
   size_t off = 0;
-  L.off_w16 = off;
-  off = align_up(off + sizeof(__half) * tri::kMatCount * tri::C * tri::C, 256);
-  L.off_vec = off;
-  off = align_up(off + sizeof(float) * tri::kVecCount * tri::C, 256);
-  L.off_z16 = off;
-  if (L.pad_z) off = align_up(off + sizeof(__half) * (size_t)L.rows * n * tri::C, 256);
-  L.off_a = off;
-  off = align_up(off + sizeof(__half) * (size_t)L.n * L.ab_rs, 256);
-  L.off_b = off;
-  off = align_up(off + sizeof(__half) * (size_t)L.n * L.ab_rs, 256);
-  L.off_x = off;
-  off = align_up(off + sizeof(__half) * (size_t)tri::C * L.x_hs, 256);
+  auto take = [&](size_t bytes) {
+    const size_t at = off;
+    off = align_up(off + bytes, 256);
+    return at;
+  };
+  L.off_w16 = take(sizeof(__half) * tri::kMatCount * tri::C * tri::C);
+  L.off_vec = take(sizeof(float) * tri::kVecCount * tri::C);
+  L.off_z16 = take(L.pad_z ? sizeof(__half) * (size_t)L.rows * n * tri::C : 0);
+  // one GPU: a and b are [n][128][kp] (row-major, the contraction reads them in place)
+  L.off_a = take(sharded ? ab_bytes : sizeof(__half) * (size_t)n * L.ab_rs);
+  L.off_b = take(sharded ? ab_bytes : sizeof(__half) * (size_t)n * L.ab_rs);
+  L.off_x = take(x_bytes);
+  L.off_a_all = sharded ? take(ab_bytes) : L.off_a;
+  L.off_b_all = sharded ? take(ab_bytes) : L.off_b;
+  L.off_x_all = sharded ? take(x_bytes) : L.off_x;
   L.total = off;
   return L;
 }
@@ -1083,7 +1106,7 @@ af2_status launch_output_any(af2_ctx *ctx, int out_dtype, const CUtensorMap &xma
 
 af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L, const void *z, int z_dtype,
                            const float *mask, const float *packed, double eps, int residual, void *out,
-                           int out_dtype, void *workspace, cudaStream_t stream, const TriangleExchange *exchange) {
+                           int out_dtype, void *workspace, cudaStream_t stream, const TriangleShard *shard) {
   using namespace tri;
   uint8_t *ws = static_cast<uint8_t *>(workspace);
   __half *w16 = reinterpret_cast<__half *>(ws + L.off_w16);
@@ -1092,9 +1115,12 @@ af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L,
   __half *b = reinterpret_cast<__half *>(ws + L.off_b);
   __half *x = reinterpret_cast<__half *>(ws + L.off_x);
   const int n = static_cast<int>(L.n);
-  const int64_t rows = L.rows;
+  const int64_t rows = L.rows, R = L.ranks, hq = L.hq;
+  const bool sharded = R > 1;
+  if (sharded && (!shard || !shard->all_to_all || shard->ranks != R))
+    return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "a row-sharded triangle multiplication needs the ranks' exchange");
   const int64_t pairs = rows * L.n;
-  const int64_t b_row0 = exchange ? exchange->b_row0 : 0;
+  const bool out_dir = direction == AF2_OUTGOING;
 
   {
     LaunchScope scope(ctx, stream, kProfTrianglePrepare);
@@ -1119,53 +1145,71 @@ af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L,
   }
 
   // ---- projections ----
+  // Tile rows are pairs (r, k0..k0+63) outgoing and (k0..k0+63, r) incoming.  Both z maps
+  // describe this rank's rows of z in their natural [row][col][c] order; the incoming box
+  // is one column wide and 64 rows tall, which lands the same [64 rows][128 B] tile in
+  // shared memory.  Outgoing: r runs over the local rows, k over all n; incoming: r over
+  // all n columns, k over the local rows.
   const uint64_t row_bytes = C * 2;  // one pair row of the 128-channel z
+  const int64_t r_extent = out_dir ? rows : L.n, k_extent = out_dir ? L.n : rows;
   CUtensorMap zmap_proj;
-  const bool out_dir = direction == AF2_OUTGOING;
-  // Tile rows are pairs (r, k0..k0+63) outgoing and (k0..k0+63, r) incoming.  Both maps
-  // describe z in its natural [row][col][c] order; the incoming box is one column wide
-  // and 64 rows tall, which lands the same [64 rows][128 B] tile in shared memory.
   if (!encode_map_3d(&zmap_proj, map_type(zt), zsrc, C, L.n, rows, row_bytes, row_bytes * L.n, 64,
                      out_dir ? PJ_TILE : 1, out_dir ? 1 : PJ_TILE, CU_TENSOR_MAP_SWIZZLE_128B))
     return fail(ctx, AF2_ERR_CUDA, "cuTensorMapEncodeTiled failed for the projection's z map");
   ProjectArgs pa;
-  pa.mask = mask;
+  pa.mask = mask;  // this rank's rows [rows][n]
   pa.mask_rs = out_dir ? L.n : 1;
   pa.mask_ks = out_dir ? 1 : L.n;
-  pa.b_row0 = static_cast<int>(b_row0);
   pa.w16 = w16;
   pa.vec = vec;
-  pa.n = n;
+  pa.k_extent = static_cast<int>(k_extent);
   pa.cz = (int)L.cz;
-  pa.tiles_k = (n + PJ_TILE - 1) / PJ_TILE;
-  pa.total_tiles = static_cast<int>(rows) * pa.tiles_k;
+  pa.tiles_k = static_cast<int>((k_extent + PJ_TILE - 1) / PJ_TILE);
+  pa.total_tiles = static_cast<int>(r_extent) * pa.tiles_k;
   pa.transposed = out_dir ? 0 : 1;
   pa.eps = static_cast<float>(eps);
   pa.err = ctx->err_word;
-  // The gated operands leave through TMA stores: [row][128 h][kp], one box = 64 pairs x 128 channels.
-  // A row's 128 channel vectors are contiguous, so the rows of a row-sharded
-  // pair are contiguous too and the b operand is exchanged as one block per rank.
+  // The gated operands leave through TMA stores into [group][row][hq][kp]: one box is 64 pairs
+  // x 128 channels of one row, its outer dimension scattering the channel groups (one group
+  // of all 128 channels on one GPU, so a row's channel vectors are contiguous there).
+  const uint64_t ab_dims[4] = {(uint64_t)k_extent, (uint64_t)hq, (uint64_t)L.ab_rows, (uint64_t)R};
+  const uint64_t ab_strides[3] = {(uint64_t)L.kp * 2, (uint64_t)L.ab_rs * 2, (uint64_t)L.ab_rows * L.ab_rs * 2};
+  const uint32_t ab_box[4] = {PJ_TILE, (uint32_t)hq, 1, (uint32_t)R};
   CUtensorMap amap_st, bmap_st;
-  if (!encode_map_3d(&amap_st, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a, L.n, C, rows, L.kp * 2, L.ab_rs * 2, PJ_TILE, C, 1,
+  if (!encode_map_4d(&amap_st, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a, ab_dims, ab_strides, ab_box,
                      CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !encode_map_3d(&bmap_st, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, b, L.n, C, L.n, L.kp * 2, L.ab_rs * 2, PJ_TILE, C, 1,
+      !encode_map_4d(&bmap_st, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, b, ab_dims, ab_strides, ab_box,
                      CU_TENSOR_MAP_SWIZZLE_128B))
     return fail(ctx, AF2_ERR_CUDA, "cuTensorMapEncodeTiled failed for the projection's store maps");
   af2_status st = zt == AF2_BF16 ? launch_project<__nv_bfloat16>(ctx, zmap_proj, amap_st, bmap_st, pa, stream)
                                  : launch_project<__half>(ctx, zmap_proj, amap_st, bmap_st, pa, stream);
   if (st != AF2_OK) return st;
-  if (exchange && exchange->all_gather &&
-      (st = exchange->all_gather(ctx, b, (size_t)rows * L.ab_rs * sizeof(__half), stream)) != AF2_OK)
-    return st;
 
-  // ---- per block of output rows: contraction, then output ----
-  const __half *m_op = out_dir ? a : b;  // rows i of the product
-  const __half *n_op = out_dir ? b : a;  // rows j of the product
+  // ---- channel shards: every rank receives its hq channels of every rank's rows ----
+  __half *a_all = reinterpret_cast<__half *>(ws + L.off_a_all), *b_all = reinterpret_cast<__half *>(ws + L.off_b_all);
+  if (sharded) {
+    const size_t group_bytes = (size_t)L.ab_rows * L.ab_rs * sizeof(__half);
+    if ((st = shard->all_to_all(ctx, a, a_all, group_bytes, group_bytes, stream)) != AF2_OK ||
+        (st = shard->all_to_all(ctx, b, b_all, group_bytes, group_bytes, stream)) != AF2_OK)
+      return st;
+  }
+
+  // ---- contraction maps: [k block][row][hq][k] viewed as {k, h, row, k block} ----
+  // Outgoing: rows i of a x rows j of b, k over all n (one k block).  Incoming: rows i of b'
+  // x rows j of a', k over n in one block per rank (each rank's pair rows), in k order.
+  const __half *m_op = out_dir ? a_all : b_all;  // rows i of the product
+  const __half *n_op = out_dir ? b_all : a_all;  // rows j of the product
+  const int64_t op_rows = sharded ? L.n : (out_dir ? rows : L.n);
+  const int64_t kblk = (sharded && !out_dir) ? rows : L.n, nkblk = (sharded && !out_dir) ? R : 1;
+  const uint64_t m_dims[4] = {(uint64_t)kblk, (uint64_t)hq, (uint64_t)op_rows, (uint64_t)nkblk};
+  const uint64_t n_dims[4] = {(uint64_t)kblk, (uint64_t)hq, (uint64_t)L.n, (uint64_t)nkblk};
+  const uint64_t op_strides[3] = {(uint64_t)L.kp * 2, (uint64_t)L.ab_rs * 2, (uint64_t)L.n * L.ab_rs * 2};
+  const uint32_t m_box[4] = {CT_BK, 1, CT_BM, 1}, n_box[4] = {CT_BK, 1, CT_BN, 1};
   CUtensorMap amap, bmap, zmap_out;
-  if (!encode_map_3d(&amap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, m_op, L.n, C, out_dir ? rows : L.n, L.kp * 2,
-                     L.ab_rs * 2, CT_BK, 1, CT_BM, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !encode_map_3d(&bmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, n_op, L.n, C, L.n, L.kp * 2, L.ab_rs * 2, CT_BK, 1,
-                     CT_BN, CU_TENSOR_MAP_SWIZZLE_128B) ||
+  if (!encode_map_4d(&amap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, m_op, m_dims, op_strides, m_box,
+                     CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_map_4d(&bmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, n_op, n_dims, op_strides, n_box,
+                     CU_TENSOR_MAP_SWIZZLE_128B) ||
       !encode_map_3d(&zmap_out, map_type(zt), zsrc, C, L.n, rows, row_bytes, row_bytes * L.n, 64, 128, 1,
                      CU_TENSOR_MAP_SWIZZLE_128B))
     return fail(ctx, AF2_ERR_CUDA, "cuTensorMapEncodeTiled failed for the contraction maps");
@@ -1182,19 +1226,21 @@ af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L,
     if (e != cudaSuccess) return cuda_fail(ctx, e, "configure contraction kernel");
     contract_configured = true;
   }
-  for (int64_t rb = 0; rb < rows; rb += L.block_rows) {
-    const int rc = static_cast<int>(std::min<int64_t>(L.block_rows, rows - rb));
+  auto contract = [&](int64_t rb, int64_t rc, int64_t rows_per_block) -> af2_status {
     ContractArgs ca;
     ca.x_out = x;
-    ca.x_hs = (int64_t)rc * L.jp + kChannelPad;
+    ca.x_hs = L.x_hs;
     ca.x_rs = L.jp;
+    ca.x_bs = hq * L.x_hs;
+    ca.block_rows_out = static_cast<int>(rows_per_block);
     ca.n = n;
     ca.row_begin = static_cast<int>(rb);
-    ca.row_count = rc;
-    ca.tiles_m = (rc + CT_BM - 1) / CT_BM;
+    ca.row_count = static_cast<int>(rc);
+    ca.k_split = static_cast<int>(kblk);
+    ca.tiles_m = static_cast<int>((rc + CT_BM - 1) / CT_BM);
     ca.tiles_n = (n + CT_BN - 1) / CT_BN;
     ca.k_blocks = (n + CT_BK - 1) / CT_BK;
-    ca.total_tiles = C * ca.tiles_m * ca.tiles_n;
+    ca.total_tiles = static_cast<int>(hq) * ca.tiles_m * ca.tiles_n;
     ca.scale = 1.0f / static_cast<float>(n);
     ca.err = ctx->err_word;
     const int grid = std::max(1, std::min(ca.total_tiles, ctx->sm_count));
@@ -1202,11 +1248,13 @@ af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L,
       LaunchScope scope(ctx, stream, kProfTriangleContract);
       contract_kernel<<<grid, CT_THREADS, CT_SMEM, stream>>>(amap, bmap, ca);
     }
-    if (cudaError_t e = cudaGetLastError(); e != cudaSuccess) return cuda_fail(ctx, e, "launch contraction");
-
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? AF2_OK : cuda_fail(ctx, e, "launch contraction");
+  };
+  auto output = [&](const __half *xb, int64_t rb, int64_t rc) -> af2_status {
     CUtensorMap xmap;
-    if (!encode_map_3d(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x, L.n, rc, C, L.jp * 2, (uint64_t)ca.x_hs * 2,
-                       64, 1, C, CU_TENSOR_MAP_SWIZZLE_128B))
+    if (!encode_map_3d(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, xb, L.n, rc, C, L.jp * 2, (uint64_t)L.x_hs * 2, 64, 1,
+                       C, CU_TENSOR_MAP_SWIZZLE_128B))
       return fail(ctx, AF2_ERR_CUDA, "cuTensorMapEncodeTiled failed for the contracted block");
     OutputArgs oa;
     oa.out = out;
@@ -1217,16 +1265,31 @@ af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L,
     oa.cz = (int)L.cz;
     oa.ch = (int)L.ch;
     oa.row_begin = static_cast<int>(rb);
-    oa.row_count = rc;
+    oa.row_count = static_cast<int>(rc);
     oa.tiles_j = (n + 127) / 128;
-    oa.total_tiles = rc * oa.tiles_j;
+    oa.total_tiles = static_cast<int>(rc) * oa.tiles_j;
     oa.residual = residual;
     oa.eps_in = static_cast<float>(eps);
     oa.eps_out = static_cast<float>(eps / ((double)n * (double)n));
     oa.err = ctx->err_word;
-    st = zt == AF2_BF16 ? launch_output_any<__nv_bfloat16>(ctx, out_dtype, xmap, zmap_out, omap, oa, stream)
-                        : launch_output_any<__half>(ctx, out_dtype, xmap, zmap_out, omap, oa, stream);
-    if (st != AF2_OK) return st;
+    return zt == AF2_BF16 ? launch_output_any<__nv_bfloat16>(ctx, out_dtype, xmap, zmap_out, omap, oa, stream)
+                          : launch_output_any<__half>(ctx, out_dtype, xmap, zmap_out, omap, oa, stream);
+  };
+
+  if (sharded) {
+    // hq channels of every product row, written in one block per destination rank
+    // ([rank][hq][rows][jp]); the exchange gathers all 128 channels of this rank's rows.
+    __half *x_all = reinterpret_cast<__half *>(ws + L.off_x_all);
+    const size_t xblock = (size_t)hq * L.x_hs * sizeof(__half);
+    if ((st = contract(0, L.n, rows)) != AF2_OK ||
+        (st = shard->all_to_all(ctx, x, x_all, xblock, xblock, stream)) != AF2_OK)
+      return st;
+    return output(x_all, 0, rows);
+  }
+  // one GPU: per block of output rows, contraction then output
+  for (int64_t rb = 0; rb < rows; rb += L.block_rows) {
+    const int64_t rc = std::min<int64_t>(L.block_rows, rows - rb);
+    if ((st = contract(rb, rc, rc)) != AF2_OK || (st = output(x, rb, rc)) != AF2_OK) return st;
   }
   return AF2_OK;
 }

@@ -55,7 +55,7 @@ METRIC = "Evoformer pair-GEMM TFLOP/s & ms/block at N=1024; % of B200 bf16 TC pe
 KERNEL_DRAM_BYTES = {"triangle.contract": 771_527_680, "opm.outer": 268_619_520}
 KERNELS = ("weights.prepare", "triangle.prepare", "triangle.relayout", "triangle.project", "triangle.contract",
            "triangle.output", "opm.normalize", "opm.project", "opm.count", "opm.outer", "opm.output",
-           "opm.fused", "transition.prepare", "transition.fused", "shard.transpose")
+           "opm.fused", "transition.prepare", "transition.fused")
 
 
 def triangle_flops(n: int, cz: int = CZ, ch: int = CH) -> float:
@@ -452,8 +452,9 @@ def run_ours(args) -> None:
                        "gflop_per_block": {"triangle": 2 * triangle_flops(N) / 1e9, "opm": opm_flops(N) / 1e9,
                                            "transition": transition_flops(N) / 1e9},
                        "l2": "inputs larger than L2 (pair 268 MB, MSA 268 MB, bf16), no flush",
-                       "parallelism": (f"pair rows sharded x{world} (NCCL all-gather of the projected b and "
-                                       "the OPM right operand, all-to-all pair transposes)") if world > 1
+                       "parallelism": (f"pair rows sharded x{world}: triangle contraction sharded by hidden "
+                                       "channel between two NCCL all-to-alls, OPM right operand all-gathered")
+                       if world > 1
                        else "single GPU"},
             "ms_per_block": ms / args.steps,
             "pct_of_peak": value / world / peaks["bf16_tflops"],

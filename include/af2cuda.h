@@ -208,11 +208,13 @@ AF2_API af2_status af2_comm_destroy(af2_ctx *ctx);
 /*
  * The device form of triangle multiplication on a pair sharded by rows: this
  * rank holds rows [rank * L, (rank + 1) * L) of z, mask and out (L = length /
- * nranks, a multiple of 8), shape->length is the full length.  Outgoing
- * all-gathers the projected b operand; incoming transposes the pair and the
- * mask across ranks (all-to-all) and back.  Every rank calls it with the same
- * arguments, collectively.  Results are bit-identical to the single-GPU
- * af2_triangle_multiplication.  The incoming update keeps z's dtype.
+ * nranks, a multiple of 64; nranks divides 128), shape->length is the full
+ * length.  Each rank projects its rows; an all-to-all gives every rank 128 /
+ * nranks hidden channels of all rows, which it contracts over the whole
+ * length; a second all-to-all returns all channels of the rank's own rows for
+ * the output projection.  Every rank calls it with the same arguments,
+ * collectively.  Results are bit-identical to the single-GPU
+ * af2_triangle_multiplication.
  */
 AF2_API af2_status af2_triangle_multiplication_sharded(af2_ctx *ctx, int direction, const af2_triangle_shape *shape,
                                                        const void *z, int z_dtype, const float *mask,

@@ -1,7 +1,7 @@
-"""Row-sharded triangle multiplication and outer-product mean on 2+ GPUs (one
-process per GPU, the library's NCCL communicator): every rank's rows must be
-bit-identical to the single-GPU result.  Skipped on boxes with fewer than two
-GPUs."""
+"""Row-sharded triangle multiplication (channel-sharded contraction) and
+outer-product mean on 2+ GPUs (one process per GPU, the library's NCCL
+communicator): every rank's rows must be bit-identical to the single-GPU
+result.  Skipped on boxes with fewer than two GPUs."""
 import datetime
 import os
 import socket
@@ -57,17 +57,18 @@ def _worker(rank, nranks, port, result):
                                                                    residual=True)
             dev.sync()
             ok &= bool(torch.equal(rows, full[r0:r1]))
-        # f32 pair, written out of place (outgoing)
+        # f32 pair, written out of place, both directions
         zf = torch.from_numpy(z).cuda()
-        ref = torch.empty_like(zf)
-        out_rows = torch.empty(r1 - r0, n, z.shape[2], device="cuda")
         zf_rows, mask_rows = zf[r0:r1].contiguous(), mask_d[r0:r1].contiguous()
-        torch.cuda.synchronize()
-        af2cuda.encode_triangle_multiplication_tensors(dev, 0, zf, mask_d, packed, out=ref, residual=False)
-        af2cuda.encode_triangle_multiplication_sharded_tensors(dev, 0, zf_rows, mask_rows, packed, n, out=out_rows,
-                                                               residual=False)
-        dev.sync()
-        ok &= bool(torch.equal(out_rows, ref[r0:r1]))
+        for direction in (0, 1):
+            ref = torch.empty_like(zf)
+            out_rows = torch.empty(r1 - r0, n, z.shape[2], device="cuda")
+            torch.cuda.synchronize()
+            af2cuda.encode_triangle_multiplication_tensors(dev, direction, zf, mask_d, packed, out=ref, residual=False)
+            af2cuda.encode_triangle_multiplication_sharded_tensors(dev, direction, zf_rows, mask_rows, packed, n,
+                                                                   out=out_rows, residual=False)
+            dev.sync()
+            ok &= bool(torch.equal(out_rows, ref[r0:r1]))
         # outer-product mean of a whole MSA into this rank's pair rows
         from test_opm_gpu import opm_case, opm_packed
         m, msa_mask, wo = opm_case(40, n, 64, cz=128, seed=4)
