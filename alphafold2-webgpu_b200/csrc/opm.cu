@@ -31,6 +31,7 @@
 #include <algorithm>
 #include <cmath>
 #include <string>
+#include <type_traits>
 
 #include "af2_device.cuh"
 #include "af2_internal.h"
@@ -293,51 +294,70 @@ __global__ void __launch_bounds__(OTHREADS, 1)
 }
 
 // ---- the outer products and the output projection in one kernel ----
-// A tile is 128 residues i (the TMEM lanes) x 2 residues j.  For each outer
-// channel a (a "slice") the tensor core forms
-//   D1[i][(j, b)] = sum_s left[a][i][s] right[j][b][s]      (M 128, N 64, K S)
+// A tile is 128 residues i (the TMEM lanes) x J residues j (J = 3 when the
+// tile's right operand fits beside the left ring, S <= 512; else 2).  For each
+// outer channel a (a "slice") the tensor core forms
+//   D1[i][(j, b)] = sum_s left[a][i][s] right[j][b][s]      (M 128, N 32 J, K S)
 // with left streamed through a ring and the tile's right operand resident in
 // shared memory, both K-major (sequences contiguous: MN-major operands run the
-// tensor core several times slower at this N).  Four warps round D1 * 2^-k to f16 in TMEM, and the tensor
-// core multiplies it, read as an A operand straight from TMEM, by the 32 rows
-// of W_o that belong to channel a:
+// tensor core several times slower at this N).  Four warps round D1 * 2^-k to
+// f16 in TMEM, and the tensor core multiplies it, read as an A operand
+// straight from TMEM, by the 32 rows of W_o that belong to channel a:
 //   D2_j[i][z] += A2_j[i][b] W_o[a*32 + b][z]                (M 128, N c_z, K 32)
 // The outer products never leave the SM.  After the 32 slices eight warps
 // apply the column scales (which carry 2^k back), b_o, 1/(eps + count) and the
 // residual, and write the pair rows.  D2 sums K = (a, b) in ascending 16-wide
 // steps, as the two-kernel path does, from the same f16 operand values.
-// Tiles are dealt to CTAs in contiguous runs (j-pair major), so a CTA reloads
-// the resident right operand only when its j pair changes.
+//
+// TMEM (512 columns): D2_j at 128 j.  J = 2: D1 double-buffered at 256 and
+// 320, A2 at 384 and 416, the output MMAs of slice g issued behind the outer
+// products of slice g + 1.  J = 3: D1 (96 columns) single at 384, A2 written
+// over it; slice g + 1 starts once the output MMAs of slice g have read A2.
+// Each streamed byte of left serves 32 J outputs per sequence, so J = 3 cuts
+// the left traffic per pair (the kernel's bound, through L2) by a third.
+// Tiles are dealt to CTAs in contiguous runs (j-group major), so a CTA reloads
+// the resident right operand only when its j group changes.
 constexpr int FTHREADS = 448;  // warp 0 TMA, 1 MMA, 2-5 slice conversion, 6-13 output epilogue
-constexpr int FLST_MAX = 8;    // left ring: [2 x 64 i][64 s] f16 per stage, as many as shared memory holds
+constexpr int FLST_MAX = 8;    // left ring: [128 i][64 s] f16 per stage, as many as shared memory holds
 constexpr uint32_t FL_STAGE = 16384, FW_STAGE = 16384;
-constexpr uint32_t kD2Col = 0, kD1Col = 256, kA2Col = 384;  // TMEM columns: D2 x2 (128), D1 x2 (64), A2 x2 (32)
-constexpr uint32_t kFusedSmemLimit = 232448;                  // 227 KB of dynamic shared memory per CTA
+constexpr uint32_t kD2Col = 0;
+constexpr uint32_t kFusedSmemLimit = 232448;  // 227 KB of dynamic shared memory per CTA
 constexpr uint32_t kFusedBarBytes = 512;
 
-// Shared-memory map: right (resident) | left ring | W_o ring (2) | barriers.
-__host__ __device__ constexpr uint32_t fused_off_l(int k_blocks) { return static_cast<uint32_t>(k_blocks) * 8192u; }
-__host__ __device__ constexpr uint32_t fused_off_w(int k_blocks, int lst) {
-  return fused_off_l(k_blocks) + static_cast<uint32_t>(lst) * FL_STAGE;
-}
-__host__ __device__ constexpr uint32_t fused_off_bar(int k_blocks, int lst) {
-  return fused_off_w(k_blocks, lst) + 2 * FW_STAGE;
-}
-__host__ __device__ constexpr uint32_t fused_smem(int k_blocks, int lst) {
-  return fused_off_bar(k_blocks, lst) + kFusedBarBytes + 1024;
-}
-// Left stages that fit beside a resident right operand of k_blocks x 8 KB (4 at S = 1024, 8 at S <= 512).
-__host__ __device__ constexpr int fused_stages(int k_blocks) {
-  int lst = FLST_MAX;
-  while (lst > 2 && fused_smem(k_blocks, lst) > kFusedSmemLimit) --lst;
-  return lst;
-}
-constexpr int kFusedMaxKBlocks = 16;  // S <= 1024: the resident right operand is 128 S bytes
+template <int J>
+struct FusedCfg {
+  static constexpr uint32_t kRBlock = J * 32 * 128;            // resident right: bytes per 64-sequence block
+  static constexpr int kNB = J == 2 ? 2 : 1;                    // D1 buffers
+  static constexpr uint32_t kD1Col = J == 2 ? 256 : 384;
+  static constexpr uint32_t kA2Col = J == 2 ? 384 : 384;        // J = 3: over D1
+  static constexpr uint32_t kD1Stride = 64, kA2Stride = 32;     // between buffers (J = 2)
+};
 
-// Tile t = jp * n_ib + r is residue block (r + jp) mod n_ib of j pair jp: CTAs
-// working on different j pairs at the same moment stream different blocks of left.
-__device__ __forceinline__ int fused_tile_ib(int t, int jp, int n_ib) {
-  int ib = t - jp * n_ib + jp % n_ib;
+// Shared-memory map: right (resident) | left ring | W_o ring (2) | barriers.
+__host__ __device__ constexpr uint32_t fused_off_l(int k_blocks, int j) {
+  return static_cast<uint32_t>(k_blocks) * j * 32u * 128u;
+}
+__host__ __device__ constexpr uint32_t fused_off_w(int k_blocks, int j, int lst) {
+  return fused_off_l(k_blocks, j) + static_cast<uint32_t>(lst) * FL_STAGE;
+}
+__host__ __device__ constexpr uint32_t fused_off_bar(int k_blocks, int j, int lst) {
+  return fused_off_w(k_blocks, j, lst) + 2 * FW_STAGE;
+}
+__host__ __device__ constexpr uint32_t fused_smem(int k_blocks, int j, int lst) {
+  return fused_off_bar(k_blocks, j, lst) + kFusedBarBytes + 1024;
+}
+// Left stages that fit beside the resident right operand (0 when fewer than 2 do).
+__host__ __device__ constexpr int fused_stages(int k_blocks, int j) {
+  int lst = FLST_MAX;
+  while (lst > 0 && fused_smem(k_blocks, j, lst) > kFusedSmemLimit) --lst;
+  return lst >= 2 ? lst : 0;
+}
+constexpr int kFusedMaxKBlocks = 16;  // S <= 1024 (J = 2); J = 3 needs S <= 512
+
+// Tile t = jg * n_ib + r is residue block (r + jg) mod n_ib of j group jg: CTAs
+// working on different j groups at the same moment stream different blocks of left.
+__device__ __forceinline__ int fused_tile_ib(int t, int jg, int n_ib) {
+  int ib = t - jg * n_ib + jg % n_ib;
   return ib >= n_ib ? ib - n_ib : ib;
 }
 
@@ -353,16 +373,17 @@ struct FusedArgs {
   unsigned int *err;
 };
 
-template <typename OT>
+template <typename OT, int J>
 __global__ void __launch_bounds__(FTHREADS, 1)
     fused_kernel(const __grid_constant__ CUtensorMap lmap, const __grid_constant__ CUtensorMap rmap,
                  const __grid_constant__ CUtensorMap wmap, const FusedArgs p) {
+  using Cfg = FusedCfg<J>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = align1024(smem_raw);
   const uint32_t sbase = smem_u32(smem);
   const int lst = p.lst;
-  const uint32_t s_r = sbase, s_l = sbase + fused_off_l(p.k_blocks), s_w = sbase + fused_off_w(p.k_blocks, lst);
-  const uint32_t bar0 = sbase + fused_off_bar(p.k_blocks, lst);
+  const uint32_t s_r = sbase, s_l = sbase + fused_off_l(p.k_blocks, J), s_w = sbase + fused_off_w(p.k_blocks, J, lst);
+  const uint32_t bar0 = sbase + fused_off_bar(p.k_blocks, J, lst);
   auto l_full = [&](int s) { return bar0 + 8u * s; };
   auto l_empty = [&](int s) { return bar0 + 8u * (FLST_MAX + s); };
   auto w_full = [&](int s) { return bar0 + 8u * (2 * FLST_MAX + s); };
@@ -372,8 +393,8 @@ __global__ void __launch_bounds__(FTHREADS, 1)
   auto a2_empty = [&](int b) { return bar0 + 8u * (2 * FLST_MAX + 8 + b); };
   const uint32_t r_full = bar0 + 8u * (2 * FLST_MAX + 10), r_empty = r_full + 8u, d2_full = r_full + 16u,
                  d2_empty = r_full + 24u, drain = r_full + 32u;  // 31 barriers: 248 bytes
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + fused_off_bar(p.k_blocks, lst) + 256);
-  volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + fused_off_bar(p.k_blocks, lst) + 264);
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + fused_off_bar(p.k_blocks, J, lst) + 256);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + fused_off_bar(p.k_blocks, J, lst) + 264);
   const int warp = warp_index_uniform(), lane = threadIdx.x & 31;
   const int t_begin = blockIdx.x * p.per_cta;
   const int t_end = min(p.total_tiles, t_begin + p.per_cta);
@@ -412,18 +433,19 @@ __global__ void __launch_bounds__(FTHREADS, 1)
       tma_prefetch_map(&lmap);
       tma_prefetch_map(&rmap);
       tma_prefetch_map(&wmap);
-      int ls = 0, lph = 0, lcount = 0, wq = 0, rq = 0, prev_jp = -1;
+      int ls = 0, lph = 0, lcount = 0, wq = 0, rq = 0, prev_jg = -1;
       bool ok = true;
       const uint32_t w_bytes = static_cast<uint32_t>(p.n_out) * 128u;
       for (int t = t_begin; ok && t < t_end; ++t) {
-        const int jp = t / p.n_ib, ib = fused_tile_ib(t, jp, p.n_ib);
-        if (jp != prev_jp) {
-          // the resident right operand of j = 2 jp, 2 jp + 1: rows 64 jp .. 64 jp + 63 of [n * c][S]
+        const int jg = t / p.n_ib, ib = fused_tile_ib(t, jg, p.n_ib);
+        if (jg != prev_jg) {
+          // the resident right operand of j = J jg .. J jg + J - 1: rows 32 J jg .. of [n * c][S]
           if (rq > 0 && !mbar_wait(r_empty, (rq - 1) & 1, abort_flag, p.err, kErrWaitProducer)) break;
-          mbar_arrive_expect_tx(r_full, static_cast<uint32_t>(p.k_blocks) * 8192u);
-          for (int kb = 0; kb < p.k_blocks; ++kb) tma_load_3d(s_r + kb * 8192u, &rmap, r_full, kb * 64, 64 * jp, 0);
+          mbar_arrive_expect_tx(r_full, static_cast<uint32_t>(p.k_blocks) * Cfg::kRBlock);
+          for (int kb = 0; kb < p.k_blocks; ++kb)
+            tma_load_3d(s_r + kb * Cfg::kRBlock, &rmap, r_full, kb * 64, 32 * J * jg, 0);
           ++rq;
-          prev_jp = jp;
+          prev_jg = jg;
         }
         for (int a = 0; ok && a < C; ++a) {
           if ((a & 1) == 0) {  // W_o rows of channels a, a + 1: one [n_out][64] K-major tile
@@ -461,32 +483,31 @@ __global__ void __launch_bounds__(FTHREADS, 1)
     // MMA issue: the whole warp runs the loop (warp-uniform waits and running
     // descriptors) and one elected lane issues each instruction.  Every operand
     // is K-major: a 16-sequence step is 32 bytes (2 descriptor units) along the
-    // 128-byte rows; a left stage is 16 KB (1024 units), a right block 8 KB.
-    const uint32_t idesc1 = idesc_f16_f32(128, 2 * C);
+    // 128-byte rows; a left stage is 16 KB (1024 units).
+    const uint32_t idesc1 = idesc_f16_f32(128, 32 * J);
     const uint32_t idesc2 = idesc_f16_f32(128, p.n_out);  // A in TMEM
     const uint64_t l_base = sdesc_k_sw128(s_l), r_base = sdesc_k_sw128(s_r), w_base = sdesc_k_sw128(s_w);
     uint64_t l_desc = l_base;
-    int ls = 0, lph = 0, wq = 0, rq = 0, prev_jp = -1, tile_it = 0;
+    int ls = 0, lph = 0, wq = 0, rq = 0, prev_jg = -1, tile_it = 0;
     uint32_t g = 0;  // slices issued, over all tiles
     bool ok = true;
-    // D2 += A2(slice gp) W_o(channel a): issued one slice behind the outer products
+    // D2_j += A2_j(slice gp) W_o(channel a)
     auto outputs = [&](uint32_t gp, int a) -> bool {
-      const int bp = gp & 1, ws = wq & 1;
+      const int bp = gp % Cfg::kNB, ws = wq & 1;
       if (a == 0 && !warp_wait(d2_empty, (tile_it & 1) ^ 1, abort_flag, p.err, kErrWaitMma)) return false;
-      if (!warp_wait(a2_full(bp), (gp >> 1) & 1, abort_flag, p.err, kErrWaitMma)) return false;
+      if (!warp_wait(a2_full(bp), (gp / Cfg::kNB) & 1, abort_flag, p.err, kErrWaitMma)) return false;
       if ((a & 1) == 0 && !warp_wait(w_full(ws), (wq >> 1) & 1, abort_flag, p.err, kErrWaitMma)) return false;
       tc_fence_after();
       const uint64_t bd = w_base + ws * (FW_STAGE >> 4) + (a & 1) * 4;  // channel a's 32 rows: 64 bytes in
-      const uint32_t a2 = tmem + kA2Col + bp * 32;
-      if (a == 0) {
-        umma_ts_first(tmem + kD2Col, a2, bd, idesc2);
-        umma_ts_first(tmem + kD2Col + 128, a2 + 16, bd, idesc2);
-      } else {
-        umma_ts_acc(tmem + kD2Col, a2, bd, idesc2);
-        umma_ts_acc(tmem + kD2Col + 128, a2 + 16, bd, idesc2);
+      const uint32_t a2 = tmem + Cfg::kA2Col + bp * Cfg::kA2Stride;
+#pragma unroll
+      for (int j = 0; j < J; ++j) {
+        if (a == 0)
+          umma_ts_first(tmem + kD2Col + 128 * j, a2 + 16 * j, bd, idesc2);
+        else
+          umma_ts_acc(tmem + kD2Col + 128 * j, a2 + 16 * j, bd, idesc2);
+        umma_ts_acc(tmem + kD2Col + 128 * j, a2 + 16 * j + 8, bd + 2, idesc2);
       }
-      umma_ts_acc(tmem + kD2Col, a2 + 8, bd + 2, idesc2);
-      umma_ts_acc(tmem + kD2Col + 128, a2 + 24, bd + 2, idesc2);
       umma_commit(a2_empty(bp));
       if (a & 1) {
         umma_commit(w_empty(ws));
@@ -495,14 +516,18 @@ __global__ void __launch_bounds__(FTHREADS, 1)
       return true;
     };
     for (int t = t_begin; ok && t < t_end; ++t, ++tile_it) {
-      const int jp = t / p.n_ib;
-      if (jp != prev_jp) {
+      const int jg = t / p.n_ib;
+      if (jg != prev_jg) {
         if (!warp_wait(r_full, rq & 1, abort_flag, p.err, kErrWaitMma)) break;
         ++rq;
-        prev_jp = jp;
+        prev_jg = jg;
       }
       for (int a = 0; a < C; ++a, ++g) {
-        const uint32_t d1 = tmem + kD1Col + (g & 1) * 64;
+        if (J == 3 && g > 0 && !warp_wait(a2_empty(0), ((g - 1) & 1), abort_flag, p.err, kErrWaitMma)) {
+          ok = false;  // D1 holds slice g - 1's A2 until its output MMAs have read it
+          break;
+        }
+        const uint32_t d1 = tmem + Cfg::kD1Col + (g % Cfg::kNB) * Cfg::kD1Stride;
         uint64_t r_desc = r_base;
         for (int kb = 0; kb < p.k_blocks; ++kb) {
           if (!warp_wait(l_full(ls), lph, abort_flag, p.err, kErrWaitMma)) {
@@ -518,7 +543,7 @@ __global__ void __launch_bounds__(FTHREADS, 1)
           umma_acc(d1, l_desc + 4, r_desc + 4, idesc1);
           umma_acc(d1, l_desc + 6, r_desc + 6, idesc1);
           umma_commit(l_empty(ls));
-          r_desc += 8192 >> 4;
+          r_desc += Cfg::kRBlock >> 4;
           l_desc += FL_STAGE >> 4;
           if (++ls == lst) {
             ls = 0;
@@ -527,15 +552,20 @@ __global__ void __launch_bounds__(FTHREADS, 1)
           }
         }
         if (!ok) break;
-        umma_commit(d1_full(g & 1));
-        if (a > 0 && !outputs(g - 1, a - 1)) {
+        umma_commit(d1_full(g % Cfg::kNB));
+        if (J == 3) {  // no lag: this slice's output MMAs follow its conversion
+          if (!outputs(g, a)) {
+            ok = false;
+            break;
+          }
+        } else if (a > 0 && !outputs(g - 1, a - 1)) {
           ok = false;
           break;
         }
       }
-      if (!ok || !outputs(g - 1, C - 1)) break;
+      if (!ok || (J == 2 && !outputs(g - 1, C - 1))) break;
       umma_commit(d2_full);
-      if (t + 1 < t_end && (t + 1) / p.n_ib != jp) umma_commit(r_empty);
+      if (t + 1 < t_end && (t + 1) / p.n_ib != jg) umma_commit(r_empty);
     }
     umma_commit(drain);
     mbar_wait_drain(drain, 0, p.err);
@@ -546,25 +576,26 @@ __global__ void __launch_bounds__(FTHREADS, 1)
     bool ok = true;
     for (int t = t_begin; ok && t < t_end; ++t) {
       for (int a = 0; a < C; ++a, ++g) {
-        const int b = g & 1;
-        if (!warp_wait(d1_full(b), (g >> 1) & 1, abort_flag, p.err, kErrWaitEpilogue) ||
-            !warp_wait(a2_empty(b), ((g >> 1) & 1) ^ 1, abort_flag, p.err, kErrWaitEpilogue)) {
+        const int b = g % Cfg::kNB;
+        if (!warp_wait(d1_full(b), (g / Cfg::kNB) & 1, abort_flag, p.err, kErrWaitEpilogue) ||
+            (J == 2 && !warp_wait(a2_empty(b), ((g >> 1) & 1) ^ 1, abort_flag, p.err, kErrWaitEpilogue))) {
           ok = false;
           break;
         }
         tc_fence_after();
-        uint32_t v[32], pk[32];
-        tmem_ld32(tmem + lane_off + kD1Col + b * 64, v);
-        tmem_ld_wait();
+        // every column is read before any is written (J = 3 writes A2 over D1)
+        uint32_t v[32], pk[16 * J];
 #pragma unroll
-        for (int c = 0; c < 16; ++c)
-          pk[c] = pack_half2(__uint_as_float(v[2 * c]) * p.scale, __uint_as_float(v[2 * c + 1]) * p.scale);
-        tmem_ld32(tmem + lane_off + kD1Col + b * 64 + 32, v);
-        tmem_ld_wait();
+        for (int j = 0; j < J; ++j) {
+          tmem_ld32(tmem + lane_off + Cfg::kD1Col + b * Cfg::kD1Stride + 32 * j, v);
+          tmem_ld_wait();
 #pragma unroll
-        for (int c = 0; c < 16; ++c)
-          pk[16 + c] = pack_half2(__uint_as_float(v[2 * c]) * p.scale, __uint_as_float(v[2 * c + 1]) * p.scale);
-        tmem_st32(tmem + lane_off + kA2Col + b * 32, pk);
+          for (int c = 0; c < 16; ++c)
+            pk[16 * j + c] =
+                pack_half2(__uint_as_float(v[2 * c]) * p.scale, __uint_as_float(v[2 * c + 1]) * p.scale);
+        }
+#pragma unroll
+        for (int j = 0; j < J; ++j) tmem_st16(tmem + lane_off + Cfg::kA2Col + b * Cfg::kA2Stride + 16 * j, pk + 16 * j);
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
@@ -572,42 +603,45 @@ __global__ void __launch_bounds__(FTHREADS, 1)
       }
     }
   } else {
-    // ---- output epilogue: warp (q, jh) drains lanes 32 q .. 32 q + 31 of D2_jh ----
+    // ---- output epilogue: warp (q, jh) drains lanes 32 q .. 32 q + 31 of D2_j, j = jh, jh + 2 ----
     const int q = warp & 3, jh = (warp - 6) >> 2;
     const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
     const int chunks = p.n_out / 32;
     int tile_it = 0;
     for (int t = t_begin; t < t_end; ++t, ++tile_it) {
-      const int jp = t / p.n_ib, ib = fused_tile_ib(t, jp, p.n_ib);
-      const int64_t i = static_cast<int64_t>(ib) * 128 + q * 32 + lane, j = 2 * jp + jh;
+      const int jg = t / p.n_ib, ib = fused_tile_ib(t, jg, p.n_ib);
+      const int64_t i = static_cast<int64_t>(ib) * 128 + q * 32 + lane;
       if (!warp_wait(d2_full, tile_it & 1, abort_flag, p.err, kErrWaitEpilogue)) break;
       tc_fence_after();
-      const bool row_ok = i < p.rows && j < p.n;
-      const float rs = row_ok ? p.rowscale[i * p.n + j] : 0.f;
-      OT *orow = static_cast<OT *>(p.out) + (i * p.n + j) * p.cz;
-      for (int ch = 0; ch < chunks; ++ch) {
-        uint32_t v[32];
-        tmem_ld32(tmem + lane_off + kD2Col + jh * 128 + ch * 32, v);
-        tmem_ld_wait();
-        if (ch == chunks - 1) {  // D2 is free for the next tile once every lane has read it
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(d2_empty);
-        }
-        const int c0 = ch * 32;
-        if (!row_ok || c0 >= p.cz) continue;
-        float y[32];
-        const float4 *sc = reinterpret_cast<const float4 *>(p.wscale + c0);
-        const float4 *bi = reinterpret_cast<const float4 *>(p.bias + c0);
+      for (int jl = jh; jl < J; jl += 2) {
+        const int64_t j = static_cast<int64_t>(J) * jg + jl;
+        const bool row_ok = i < p.rows && j < p.n;
+        const float rs = row_ok ? p.rowscale[i * p.n + j] : 0.f;
+        OT *orow = static_cast<OT *>(p.out) + (i * p.n + j) * p.cz;
+        for (int ch = 0; ch < chunks; ++ch) {
+          uint32_t v[32];
+          tmem_ld32(tmem + lane_off + kD2Col + jl * 128 + ch * 32, v);
+          tmem_ld_wait();
+          if (ch == chunks - 1 && jl + 2 >= J) {  // D2 is free for the next tile once every lane has read it
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(d2_empty);
+          }
+          const int c0 = ch * 32;
+          if (!row_ok || c0 >= p.cz) continue;
+          float y[32];
+          const float4 *sc = reinterpret_cast<const float4 *>(p.wscale + c0);
+          const float4 *bi = reinterpret_cast<const float4 *>(p.bias + c0);
 #pragma unroll
-        for (int i4 = 0; i4 < 8; ++i4) {
-          const float4 s4 = __ldg(sc + i4), b4 = __ldg(bi + i4);
-          y[4 * i4 + 0] = fmaf(__uint_as_float(v[4 * i4 + 0]), s4.x, b4.x) * rs;
-          y[4 * i4 + 1] = fmaf(__uint_as_float(v[4 * i4 + 1]), s4.y, b4.y) * rs;
-          y[4 * i4 + 2] = fmaf(__uint_as_float(v[4 * i4 + 2]), s4.z, b4.z) * rs;
-          y[4 * i4 + 3] = fmaf(__uint_as_float(v[4 * i4 + 3]), s4.w, b4.w) * rs;
+          for (int i4 = 0; i4 < 8; ++i4) {
+            const float4 s4 = __ldg(sc + i4), b4 = __ldg(bi + i4);
+            y[4 * i4 + 0] = fmaf(__uint_as_float(v[4 * i4 + 0]), s4.x, b4.x) * rs;
+            y[4 * i4 + 1] = fmaf(__uint_as_float(v[4 * i4 + 1]), s4.y, b4.y) * rs;
+            y[4 * i4 + 2] = fmaf(__uint_as_float(v[4 * i4 + 2]), s4.z, b4.z) * rs;
+            y[4 * i4 + 3] = fmaf(__uint_as_float(v[4 * i4 + 3]), s4.w, b4.w) * rs;
+          }
+          store_out32<OT>(orow, c0, p.cz, y, p.vector_out, p.residual);
         }
-        store_out32<OT>(orow, c0, p.cz, y, p.vector_out, p.residual);
       }
     }
   }
@@ -673,14 +707,14 @@ OpmLayout opm_layout(int64_t s, int64_t n, int64_t cm, int64_t c, int64_t cz, in
 
 namespace {
 
-template <typename OT>
+template <typename OT, int J>
 af2_status launch_fused_t(af2_ctx *ctx, const CUtensorMap &lmap, const CUtensorMap &rmap, const CUtensorMap &wmap,
                           const FusedArgs &a, int grid, cudaStream_t stream) {
-  const uint32_t smem = fused_smem(a.k_blocks, a.lst);
-  cudaError_t e = cudaFuncSetAttribute(fused_kernel<OT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  const uint32_t smem = fused_smem(a.k_blocks, J, a.lst);
+  cudaError_t e = cudaFuncSetAttribute(fused_kernel<OT, J>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return cuda_fail(ctx, e, "fused OPM kernel attributes");
   LaunchScope scope(ctx, stream, kProfOpmFused);
-  fused_kernel<OT><<<grid, FTHREADS, smem, stream>>>(lmap, rmap, wmap, a);
+  fused_kernel<OT, J><<<grid, FTHREADS, smem, stream>>>(lmap, rmap, wmap, a);
   e = cudaGetLastError();
   return e == cudaSuccess ? AF2_OK : cuda_fail(ctx, e, "fused OPM kernel launch");
 }
@@ -690,16 +724,19 @@ af2_status fused_launch(af2_ctx *ctx, const OpmLayout &L, uint8_t *ws, const __h
                         void *out, int out_dtype, cudaStream_t stream) {
   const int64_t s = L.s, n = L.n, c = L.c, cz = L.cz, rows = L.rows;
   const int64_t o_cols = linear_cols_pad(cz), o_inner = align_up(c * c, 64);
+  const int k_blocks = (int)((s + 63) / 64);
+  // three residues j per tile when their right operand fits beside the left ring, else two
+  const int J = fused_stages(k_blocks, 3) >= 4 ? 3 : 2;
   CUtensorMap lmap, rmap, wmap;
   // K-major, sequences contiguous (zero past S):
   // left [c][rows][pitch]: boxes of 64 sequences x 128 residues of one channel
-  // right [n][c][pitch]: boxes of 64 sequences x 64 rows (2 residues x 32 channels)
+  // right [n][c][pitch]: boxes of 64 sequences x 32 J rows (J residues x 32 channels)
   // W_o [c*c / 64][o_cols][64]: the 64 rows of two channels a per box
   const uint64_t pitch = L.seq_pitch;
   if (!encode_map_3d(&lmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, ws + L.off_left, s, rows, c, pitch * 2,
                      (uint64_t)rows * pitch * 2, 64, 128, 1, CU_TENSOR_MAP_SWIZZLE_128B) ||
       !encode_map_3d(&rmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, right_full, s, n * c, 1, pitch * 2,
-                     (uint64_t)n * c * pitch * 2, 64, 64, 1, CU_TENSOR_MAP_SWIZZLE_128B) ||
+                     (uint64_t)n * c * pitch * 2, 64, (uint32_t)(32 * J), 1, CU_TENSOR_MAP_SWIZZLE_128B) ||
       !encode_map_3d(&wmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, ws + L.off_wo, 64, o_cols, o_inner / 64, 128,
                      (uint64_t)o_cols * 128, 64, (uint32_t)o_cols, 1, CU_TENSOR_MAP_SWIZZLE_128B))
     return fail(ctx, AF2_ERR_CUDA, "cuTensorMapEncodeTiled failed for the fused OPM operands");
@@ -713,10 +750,10 @@ af2_status fused_launch(af2_ctx *ctx, const OpmLayout &L, uint8_t *ws, const __h
   a.cz = (int)cz;
   a.n_out = (int)o_cols;
   a.n_ib = (int)((rows + 127) / 128);
-  a.total_tiles = a.n_ib * (int)((n + 1) / 2);
+  a.total_tiles = a.n_ib * (int)((n + J - 1) / J);
   a.per_cta = (a.total_tiles + ctx->sm_count - 1) / ctx->sm_count;
-  a.k_blocks = (int)((s + 63) / 64);
-  a.lst = fused_stages(a.k_blocks);
+  a.k_blocks = k_blocks;
+  a.lst = fused_stages(k_blocks, J);
   a.scale = std::ldexp(1.f, -L.out_shift);
   a.residual = residual;
   {
@@ -725,9 +762,13 @@ af2_status fused_launch(af2_ctx *ctx, const OpmLayout &L, uint8_t *ws, const __h
   }
   a.err = ctx->err_word;
   const int grid = (a.total_tiles + a.per_cta - 1) / a.per_cta;
-  if (out_dtype == AF2_F16) return launch_fused_t<__half>(ctx, lmap, rmap, wmap, a, grid, stream);
-  if (out_dtype == AF2_BF16) return launch_fused_t<__nv_bfloat16>(ctx, lmap, rmap, wmap, a, grid, stream);
-  return launch_fused_t<float>(ctx, lmap, rmap, wmap, a, grid, stream);
+  auto run = [&](auto jtag) {
+    constexpr int JJ = decltype(jtag)::value;
+    if (out_dtype == AF2_F16) return launch_fused_t<__half, JJ>(ctx, lmap, rmap, wmap, a, grid, stream);
+    if (out_dtype == AF2_BF16) return launch_fused_t<__nv_bfloat16, JJ>(ctx, lmap, rmap, wmap, a, grid, stream);
+    return launch_fused_t<float, JJ>(ctx, lmap, rmap, wmap, a, grid, stream);
+  };
+  return J == 3 ? run(std::integral_constant<int, 3>{}) : run(std::integral_constant<int, 2>{});
 }
 
 }  // namespace

@@ -51,8 +51,9 @@ def opm_input(m, mask, w, c=32, **kw):
                                          af2cuda.OuterProductMeanWeights(**w), **kw)
 
 
+# S <= 640: three residues j per fused tile; 700 sequences: two (the resident right operand is larger)
 @pytest.mark.parametrize("s,n,cm,cz", [(5, 9, 16, 8), (37, 30, 64, 128), (64, 64, 256, 128), (3, 13, 7, 5),
-                                       (130, 21, 256, 64)])
+                                       (130, 21, 256, 64), (700, 20, 16, 32)])
 def test_opm_matches_oracle(device, s, n, cm, cz):
     m, mask, w = opm_case(s, n, cm, cz=cz, seed=s + n + cm)
     expected = oracle.outer_product_mean(m, mask, opm_packed(w), 32, cz)
