@@ -201,6 +201,17 @@ inline int64_t linear_cols_pad(int64_t cols) { return align_up(cols, linear_tile
 af2_status prepare_matrix(af2_ctx *ctx, const af2_matrix &w, int64_t inner, int64_t cols, int64_t inner_pad,
                           int64_t cols_pad, float extra_scale, void *out, float *scale_out, cudaStream_t stream,
                           int64_t row0 = 0, int64_t rows_total = 0);
+// Up to kMaxPrepJobs such preparations in one launch.
+constexpr int kMaxPrepJobs = 4;
+struct PrepJob {
+  af2_matrix w;
+  int64_t inner, cols, inner_pad, cols_pad;
+  float extra_scale;
+  void *out;
+  float *scale_out;
+  int64_t row0 = 0, rows_total = 0;
+};
+af2_status prepare_matrices(af2_ctx *ctx, const PrepJob *jobs, int count, cudaStream_t stream);
 // Up to 8 zero-padded vector copies done by one launch.
 struct VectorSegments {
   const float *src[8];

@@ -224,8 +224,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 // and q8 block weights (decoded exactly to f32 first) the scale is the power
 // of two bringing the column's largest magnitude into [0.5, 1).
 // ---------------------------------------------------------------------------
-constexpr int PREP_THREADS = 1024;
-constexpr int kPrepBatch = 32;  // K values per thread held in registers: inner <= 1024 is read once
+constexpr int PREP_THREADS = 256;
+constexpr int PREP_CHUNK = 128;  // K rows converted per CTA
 
 struct MatrixDev {
   int format, block;
@@ -241,96 +241,86 @@ __device__ __forceinline__ float element(const MatrixDev &m, int64_t i) {
   return code * __half2float(__ushort_as_half(bits));
 }
 
-struct PrepShared {
-  float red[32][33];
-  float col_scale[32];
-  __align__(16) __half stage[32][264];
+struct PrepJobDev {
+  MatrixDev m;
+  int inner, cols, inner_pad, cols_pad, row0, rows_total;
+  float extra_scale;
+  __half *out;
+  float *scale_out;
+};
+struct PrepBatch {
+  PrepJobDev job[kMaxPrepJobs];
 };
 
+// CTA (column group of 32, chunk of 128 K rows, job).  The column's scale
+// needs the maximum over all of its K rows: every CTA of the column group
+// takes it (a read that stays in L2), so no CTA waits for another; the chunk
+// 0 CTA stores the scales.  Then the chunk is rounded to f16 and written as
+// rows [k / 64][rows_total][64] (one 128-byte row segment per column and K block).
 template <int FMT>
-__device__ __forceinline__ void prep_block(PrepShared &sh, const MatrixDev &m, int inner, int cols, int inner_pad,
-                                           int cols_pad, int row0, int rows_total, float extra_scale,
-                                           __half *__restrict__ out, float *__restrict__ scale_out) {
-  const int warp = warp_index_uniform(), lane = threadIdx.x & 31;
+__device__ __forceinline__ void prep_chunk(const PrepJobDev &jb) {
+  __shared__ float red[PREP_THREADS / 32][33];
+  __shared__ float col_scale[32];
+  __shared__ __align__(16) __half stage[32][PREP_CHUNK + 8];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int o0 = blockIdx.x * 32, o = o0 + lane;
+  const int k0 = blockIdx.y * PREP_CHUNK;
+  if (o0 >= jb.cols_pad || k0 >= jb.inner_pad) return;
   constexpr bool codes = FMT == AF2_WEIGHTS_Q8_CHANNEL;
-  float vals[kPrepBatch];
-#pragma unroll
-  for (int b = 0; b < kPrepBatch; ++b) vals[b] = 0.f;  // warps past `inner` keep zeros (the padding)
-  float mx = 0.f;
-  for (int k0 = warp; k0 < inner; k0 += 32 * kPrepBatch) {
-#pragma unroll
-    for (int b = 0; b < kPrepBatch; ++b) {
-      const int k = k0 + 32 * b;
-      vals[b] = (o < cols && k < inner) ? element<FMT>(m, static_cast<int64_t>(k) * cols + o) : 0.f;
-    }
-#pragma unroll
-    for (int b = 0; b < kPrepBatch; ++b) mx = fmaxf(mx, fabsf(vals[b]));
+  if (!codes) {
+    float mx = 0.f;
+    if (o < jb.cols)
+      for (int k = warp; k < jb.inner; k += PREP_THREADS / 32)
+        mx = fmaxf(mx, fabsf(element<FMT>(jb.m, static_cast<int64_t>(k) * jb.cols + o)));
+    red[warp][lane] = mx;
   }
-  sh.red[warp][lane] = mx;
   __syncthreads();
   if (warp == 0) {
-    float v = 0.f;
-    for (int w = 0; w < 32; ++w) v = fmaxf(v, sh.red[w][lane]);
     float scale = 1.f;
-    if (o < cols) {
+    if (o < jb.cols) {
       if (codes) {
-        scale = static_cast<const float *>(m.scales)[o];
-      } else if (v > 0.f && isfinite(v)) {
-        int e;
-        frexpf(v, &e);
-        scale = ldexpf(1.f, e);
+        scale = static_cast<const float *>(jb.m.scales)[o];
+      } else {
+        float v = 0.f;
+        for (int w = 0; w < PREP_THREADS / 32; ++w) v = fmaxf(v, red[w][lane]);
+        if (v > 0.f && isfinite(v)) {
+          int e;
+          frexpf(v, &e);
+          scale = ldexpf(1.f, e);
+        }
       }
     }
-    sh.col_scale[lane] = scale;
-    if (o < cols_pad) scale_out[row0 + o] = scale * extra_scale;
+    col_scale[lane] = scale;
+    if (blockIdx.y == 0 && o < jb.cols_pad) jb.scale_out[jb.row0 + o] = scale * jb.extra_scale;
   }
   __syncthreads();
-  const float inv = codes ? 1.f : 1.f / sh.col_scale[lane];
-  for (int k0 = 0; k0 < inner_pad; k0 += 256) {
-    const int kend = min(k0 + 256, inner_pad);
-    if (inner <= 32 * kPrepBatch) {
-#pragma unroll
-      for (int b = 0; b < kPrepBatch; ++b) {
-        const int k = warp + 32 * b;
-        if (k >= k0 && k < kend) sh.stage[lane][k - k0] = __float2half_rn(vals[b] * inv);
-      }
-      for (int k = k0 + warp; k < kend; k += 32)
-        if (k >= 32 * kPrepBatch) sh.stage[lane][k - k0] = __float2half_rn(0.f);
-    } else {
-      for (int k = k0 + warp; k < kend; k += 32) {
-        float w = 0.f;
-        if (o < cols && k < inner) w = element<FMT>(m, static_cast<int64_t>(k) * cols + o) * inv;
-        sh.stage[lane][k - k0] = __float2half_rn(w);
-      }
+  const float inv = codes ? 1.f : 1.f / col_scale[lane];
+  const int kend = min(k0 + PREP_CHUNK, jb.inner_pad);
+  for (int k = k0 + warp; k < kend; k += PREP_THREADS / 32) {
+    float w = 0.f;
+    if (o < jb.cols && k < jb.inner) w = element<FMT>(jb.m, static_cast<int64_t>(k) * jb.cols + o) * inv;
+    stage[lane][k - k0] = __float2half_rn(w);
+  }
+  __syncthreads();
+  const int kblocks = (kend - k0) >> 6;  // inner_pad is a multiple of 64
+  for (int i = threadIdx.x; i < kblocks * 256; i += PREP_THREADS) {
+    const int blk = i >> 8, r = (i >> 3) & 31, c16 = i & 7;
+    if (o0 + r < jb.cols_pad) {
+      const uint4 v = *reinterpret_cast<const uint4 *>(&stage[r][blk * 64 + c16 * 8]);
+      *reinterpret_cast<uint4 *>(
+          jb.out + ((static_cast<int64_t>((k0 >> 6) + blk) * jb.rows_total + jb.row0 + o0 + r) * 64 + c16 * 8)) = v;
     }
-    __syncthreads();
-    const int blocks = (kend - k0) >> 6;
-    for (int i = threadIdx.x; i < blocks * 256; i += PREP_THREADS) {
-      const int blk = i >> 8, r = (i >> 3) & 31, c16 = i & 7;
-      if (o0 + r < cols_pad) {
-        const uint4 v = *reinterpret_cast<const uint4 *>(&sh.stage[r][blk * 64 + c16 * 8]);
-        *reinterpret_cast<uint4 *>(
-            out + ((static_cast<int64_t>((k0 >> 6) + blk) * rows_total + row0 + o0 + r) * 64 + c16 * 8)) = v;
-      }
-    }
-    __syncthreads();
   }
 }
 
-__global__ void __launch_bounds__(PREP_THREADS)
-    prep_matrix_kernel(MatrixDev m, int inner, int cols, int inner_pad, int cols_pad, int row0, int rows_total,
-                       float extra_scale, __half *__restrict__ out, float *__restrict__ scale_out) {
-  __shared__ PrepShared sh;
-  if (m.format == AF2_WEIGHTS_Q8_CHANNEL)
-    prep_block<AF2_WEIGHTS_Q8_CHANNEL>(sh, m, inner, cols, inner_pad, cols_pad, row0, rows_total, extra_scale, out,
-                                       scale_out);
-  else if (m.format == AF2_WEIGHTS_Q8_BLOCK)
-    prep_block<AF2_WEIGHTS_Q8_BLOCK>(sh, m, inner, cols, inner_pad, cols_pad, row0, rows_total, extra_scale, out,
-                                     scale_out);
+__global__ void __launch_bounds__(PREP_THREADS) prep_matrix_kernel(const PrepBatch batch) {
+  const PrepJobDev &jb = batch.job[blockIdx.z];
+  if (jb.m.format == AF2_WEIGHTS_Q8_CHANNEL)
+    prep_chunk<AF2_WEIGHTS_Q8_CHANNEL>(jb);
+  else if (jb.m.format == AF2_WEIGHTS_Q8_BLOCK)
+    prep_chunk<AF2_WEIGHTS_Q8_BLOCK>(jb);
   else
-    prep_block<AF2_WEIGHTS_F32>(sh, m, inner, cols, inner_pad, cols_pad, row0, rows_total, extra_scale, out,
-                                scale_out);
+    prep_chunk<AF2_WEIGHTS_F32>(jb);
 }
 
 // Segment k: dst[i] = i < n ? src[i] : 0 for i < n_pad (src may be NULL: zeros).
@@ -361,17 +351,30 @@ namespace {
 CUtensorMapDataType f16map() { return CU_TENSOR_MAP_DATA_TYPE_FLOAT16; }
 }  // namespace
 
+af2_status prepare_matrices(af2_ctx *ctx, const PrepJob *jobs, int count, cudaStream_t stream) {
+  if (count < 1 || count > kMaxPrepJobs) return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "weight preparation batch size");
+  PrepBatch b{};
+  unsigned gx = 1, gy = 1;
+  for (int i = 0; i < count; ++i) {
+    const PrepJob &j = jobs[i];
+    b.job[i] = PrepJobDev{MatrixDev{j.w.format, j.w.block, j.w.values, j.w.scales},
+                          (int)j.inner, (int)j.cols, (int)j.inner_pad, (int)j.cols_pad, (int)j.row0,
+                          (int)(j.rows_total ? j.rows_total : j.cols_pad), j.extra_scale,
+                          static_cast<__half *>(j.out), j.scale_out};
+    gx = std::max(gx, (unsigned)((j.cols_pad + 31) / 32));
+    gy = std::max(gy, (unsigned)((j.inner_pad + PREP_CHUNK - 1) / PREP_CHUNK));
+  }
+  LaunchScope scope(ctx, stream, kProfPrepare);
+  prep_matrix_kernel<<<dim3(gx, gy, (unsigned)count), PREP_THREADS, 0, stream>>>(b);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? AF2_OK : cuda_fail(ctx, e, "weight preparation");
+}
+
 af2_status prepare_matrix(af2_ctx *ctx, const af2_matrix &w, int64_t inner, int64_t cols, int64_t inner_pad,
                           int64_t cols_pad, float extra_scale, void *out, float *scale_out, cudaStream_t stream,
                           int64_t row0, int64_t rows_total) {
-  MatrixDev m{w.format, w.block, w.values, w.scales};
-  if (rows_total == 0) rows_total = cols_pad;
-  LaunchScope scope(ctx, stream, kProfPrepare);
-  prep_matrix_kernel<<<(unsigned)((cols_pad + 31) / 32), PREP_THREADS, 0, stream>>>(
-      m, (int)inner, (int)cols, (int)inner_pad, (int)cols_pad, (int)row0, (int)rows_total, extra_scale,
-      static_cast<__half *>(out), scale_out);
-  cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? AF2_OK : cuda_fail(ctx, e, "weight preparation");
+  const PrepJob job{w, inner, cols, inner_pad, cols_pad, extra_scale, out, scale_out, row0, rows_total};
+  return prepare_matrices(ctx, &job, 1, stream);
 }
 
 af2_status pad_vectors(af2_ctx *ctx, const VectorSegments &v, cudaStream_t stream) {

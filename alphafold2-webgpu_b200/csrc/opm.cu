@@ -110,35 +110,47 @@ __global__ void norm_kernel(const MT *__restrict__ m, int64_t rows, int cm, int 
 }
 
 // ---- pair counts: rowscale[i*N + j] = 1 / (norm_eps + sum_s mask[s,i] mask[s,j]) ----
-// A 32 x 32 block of pairs per CTA; 64 MSA rows of both residue columns at a
-// time through shared memory; every count sums s in order.
+// A 64 x 64 block of pairs per CTA (each thread a 4 x 4 register block, pairs
+// 16 apart), 64 MSA rows of both residue columns at a time through shared
+// memory; every count sums s in order.
+constexpr int CNT_TILE = 64;
 __global__ void __launch_bounds__(256) count_kernel(const float *__restrict__ mask, int s_count, int n, int row0,
                                                     int rows, float norm_eps, float *__restrict__ rowscale) {
   // rows i in [row0, row0 + rows), stored from row 0 of rowscale
-  __shared__ float mi[64][33], mj[64][33];
-  const int i0 = row0 + blockIdx.y * 32, j0 = blockIdx.x * 32;
-  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  __shared__ float mi[64][CNT_TILE], mj[64][CNT_TILE];
+  const int i0 = row0 + blockIdx.y * CNT_TILE, j0 = blockIdx.x * CNT_TILE;
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  float acc[4][4] = {};
   for (int s0 = 0; s0 < s_count; s0 += 64) {
-    for (int r = ty; r < 64; r += 8) {
+    for (int e = threadIdx.x; e < 64 * CNT_TILE; e += 256) {
+      const int r = e / CNT_TILE, c = e % CNT_TILE;
       const int64_t s = s0 + r;
-      mi[r][tx] = (s < s_count && i0 + tx < row0 + rows) ? mask[s * n + i0 + tx] : 0.f;
-      mj[r][tx] = (s < s_count && j0 + tx < n) ? mask[s * n + j0 + tx] : 0.f;
+      mi[r][c] = (s < s_count && i0 + c < row0 + rows) ? mask[s * n + i0 + c] : 0.f;
+      mj[r][c] = (s < s_count && j0 + c < n) ? mask[s * n + j0 + c] : 0.f;
     }
     __syncthreads();
-#pragma unroll 8
+#pragma unroll 4
     for (int r = 0; r < 64; ++r) {
-      const float b = mj[r][tx];
+      float a[4], b[4];
 #pragma unroll
-      for (int k = 0; k < 4; ++k) acc[k] = fmaf(mi[r][ty + 8 * k], b, acc[k]);
+      for (int k = 0; k < 4; ++k) {
+        a[k] = mi[r][ty + 16 * k];
+        b[k] = mj[r][tx + 16 * k];
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int v = 0; v < 4; ++v) acc[u][v] = fmaf(a[u], b[v], acc[u][v]);
     }
     __syncthreads();
   }
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const int i = i0 + ty + 8 * k, j = j0 + tx;
-    if (i < row0 + rows && j < n) rowscale[static_cast<int64_t>(i - row0) * n + j] = 1.f / (norm_eps + acc[k]);
-  }
+  for (int u = 0; u < 4; ++u)
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+      const int i = i0 + ty + 16 * u, j = j0 + tx + 16 * v;
+      if (i < row0 + rows && j < n) rowscale[static_cast<int64_t>(i - row0) * n + j] = 1.f / (norm_eps + acc[u][v]);
+    }
 }
 
 // ---- outer products: outer[(i, j)][a*32 + b] = 2^-shift sum_s left[s][i][a] right[s][j][b] ----
@@ -797,12 +809,11 @@ af2_status opm_launch(af2_ctx *ctx, const OpmLayout &L, const void *m, int m_dty
   vs.add(ln_w, cm, L.cmp, ln);
   vs.add(ln_b, cm, L.cmp, ln + L.cmp);
   if (lr_cols > 2 * c) vs.add(nullptr, 0, lr_cols - 2 * c, wlr_scale + 2 * c);
-  if ((st = prepare_matrix(ctx, left_m, cm, c, L.cmp, c, 1.f, ws + L.off_wlr, wlr_scale, stream, 0, lr_cols)) != AF2_OK ||
-      (st = prepare_matrix(ctx, right_m, cm, c, L.cmp, c, 1.f, ws + L.off_wlr, wlr_scale, stream, c, lr_cols)) !=
-          AF2_OK ||
-      (st = prepare_matrix(ctx, out_m, c * c, cz, o_inner, o_cols, std::ldexp(1.f, L.out_shift), ws + L.off_wo,
-                           wo_scale, stream)) != AF2_OK ||
-      (st = pad_vectors(ctx, vs, stream)) != AF2_OK)
+  const PrepJob jobs[3] = {
+      {left_m, cm, c, L.cmp, c, 1.f, ws + L.off_wlr, wlr_scale, 0, lr_cols},
+      {right_m, cm, c, L.cmp, c, 1.f, ws + L.off_wlr, wlr_scale, c, lr_cols},
+      {out_m, c * c, cz, o_inner, o_cols, std::ldexp(1.f, L.out_shift), ws + L.off_wo, wo_scale, 0, 0}};
+  if ((st = prepare_matrices(ctx, jobs, 3, stream)) != AF2_OK || (st = pad_vectors(ctx, vs, stream)) != AF2_OK)
     return st;
   // ---- LayerNorm of this rank's residue columns (all of them unless sharded) ----
   const int64_t xrows = s * rows;
@@ -864,7 +875,7 @@ af2_status opm_launch(af2_ctx *ctx, const OpmLayout &L, const void *m, int m_dty
   float *rowscale = reinterpret_cast<float *>(ws + L.off_rowscale);
   {
     LaunchScope scope(ctx, stream, kProfOpmCount);
-    const dim3 grid((unsigned)((n + 31) / 32), (unsigned)((rows + 31) / 32));
+    const dim3 grid((unsigned)((n + CNT_TILE - 1) / CNT_TILE), (unsigned)((rows + CNT_TILE - 1) / CNT_TILE));
     count_kernel<<<grid, 256, 0, stream>>>(mask, (int)s, (int)n, (int)L.row0, (int)rows, (float)norm_eps, rowscale);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(ctx, e, "OPM pair counts");
