@@ -74,26 +74,28 @@ __global__ void prep_weights_kernel(const float *__restrict__ packed, int cz, in
     }
     w16[idx] = __float2half_rn(v);
   }
-  // Biases: b + W beta (f64 sums), padded with zeros.
-  for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < kVecCount * C; idx += stride) {
-    const int q = idx / C, e = idx % C;
-    double v = 0.0;
-    auto fold = [&](int64_t o_w, int64_t o_b, int64_t o_beta, int rows, int cols) {
-      if (e >= rows) return 0.0;
-      double acc = packed[o_b + e];
-      for (int k = 0; k < cols; ++k) acc += (double)packed[o_w + (int64_t)e * cols + k] * (double)packed[o_beta + k];
-      return acc;
-    };
+  // Biases: b + W beta (f64 sums), padded with zeros; one warp per entry, lanes splitting the sum.
+  const int lane = threadIdx.x & 31;
+  for (int wi = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; wi < kVecCount * C; wi += stride >> 5) {
+    const int q = wi / C, e = wi % C;
+    int64_t o_w = -1, o_b = 0, o_beta = 0;
+    int rows = 0, cols = 0;
     switch (q) {
-      case kVBAP: v = fold(o_apw, o_apb, o_lnib, ch, cz); break;
-      case kVBAG: v = fold(o_agw, o_agb, o_lnib, ch, cz); break;
-      case kVBBP: v = fold(o_bpw, o_bpb, o_lnib, ch, cz); break;
-      case kVBBG: v = fold(o_bgw, o_bgb, o_lnib, ch, cz); break;
-      case kVBZ: v = fold(o_zw, o_zb, o_lnob, cz, ch); break;
-      case kVBG: v = fold(o_gw, o_gb, o_lnib, cz, cz); break;
-      default: v = 0.0; break;  // the LayerNorm slots are not used by the kernels
+      case kVBAP: o_w = o_apw; o_b = o_apb; o_beta = o_lnib; rows = ch; cols = cz; break;
+      case kVBAG: o_w = o_agw; o_b = o_agb; o_beta = o_lnib; rows = ch; cols = cz; break;
+      case kVBBP: o_w = o_bpw; o_b = o_bpb; o_beta = o_lnib; rows = ch; cols = cz; break;
+      case kVBBG: o_w = o_bgw; o_b = o_bgb; o_beta = o_lnib; rows = ch; cols = cz; break;
+      case kVBZ: o_w = o_zw; o_b = o_zb; o_beta = o_lnob; rows = cz; cols = ch; break;
+      case kVBG: o_w = o_gw; o_b = o_gb; o_beta = o_lnib; rows = cz; cols = cz; break;
+      default: break;  // the LayerNorm slots are not used by the kernels
     }
-    vec[idx] = static_cast<float>(v);
+    const bool live = o_w >= 0 && e < rows;
+    double acc = 0.0;
+    if (live)
+      for (int k = lane; k < cols; k += 32) acc += (double)packed[o_w + (int64_t)e * cols + k] * (double)packed[o_beta + k];
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    if (lane == 0) vec[wi] = live ? static_cast<float>(acc + (double)packed[o_b + e]) : 0.f;
   }
 }
 
