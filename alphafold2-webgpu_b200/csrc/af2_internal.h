@@ -136,7 +136,7 @@ TriangleLayout triangle_layout(int64_t n, int64_t cz, int64_t ch, int64_t block_
 
 // Exchange of the channel-sharded contraction: block p of `send` (blocks
 // `stride` bytes apart, `bytes` each) goes to rank p, and rank p's block for
-// this rank lands in block p of `recv`.
+// this rank lands in block p of `recv`; this rank's own block is left alone.
 struct TriangleShard {
   int ranks = 1, rank = 0;
   af2_status (*all_to_all)(af2_ctx *ctx, const void *send, void *recv, size_t stride, size_t bytes,

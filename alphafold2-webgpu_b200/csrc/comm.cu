@@ -84,7 +84,8 @@ ncclComm_t comm_of(af2_ctx *ctx) { return static_cast<ncclComm_t>(ctx->nccl_comm
 }  // namespace
 
 // Block p of `send` to rank p, rank p's block into block p of `recv` (blocks
-// `stride` bytes apart, `bytes` each); this rank's own block is a device copy.
+// `stride` bytes apart, `bytes` each).  This rank's own block is not moved: the
+// triangle kernels read and write it in place.
 static af2_status nccl_all_to_all(af2_ctx *ctx, const void *send, void *recv, size_t stride, size_t bytes,
                                   cudaStream_t stream) {
   const char *src = static_cast<const char *>(send);
@@ -99,9 +100,7 @@ static af2_status nccl_all_to_all(af2_ctx *ctx, const void *send, void *recv, si
   const ncclResult_t r2 = g_nccl.GroupEnd();
   if (r != ncclSuccess) return nccl_fail(ctx, r, "channel all-to-all");
   if (r2 != ncclSuccess) return nccl_fail(ctx, r2, "channel all-to-all");
-  const cudaError_t e = cudaMemcpyAsync(dst + ctx->rank * stride, src + ctx->rank * stride, bytes,
-                                        cudaMemcpyDeviceToDevice, stream);
-  return e == cudaSuccess ? AF2_OK : cuda_fail(ctx, e, "channel all-to-all (own block)");
+  return AF2_OK;
 }
 
 static af2_status nccl_all_gather_in_place(af2_ctx *ctx, void *full, size_t bytes_per_rank, cudaStream_t stream) {

@@ -459,6 +459,11 @@ struct ContractArgs {
   int block_rows_out;        // product rows per block of x_out (one block unless channel-sharded)
   int n, row_begin, row_count;
   int k_split;               // k extent of one block of the operands' 4th map dimension
+  // Channel-sharded: this rank's own share of the operands is read through the *_own maps
+  // (own_mode 1: rows [own_row0, own_row0 + own_rows) of both operands; 2: k block own_kr),
+  // and block own_blk of the product is written to x_own; so neither is copied.
+  int own_mode, own_row0, own_rows, own_kr, own_blk;
+  __half *x_own;
   int tiles_m, tiles_n, k_blocks, total_tiles;
   float scale;
   unsigned int *err;
@@ -466,6 +471,7 @@ struct ContractArgs {
 
 __global__ void __launch_bounds__(CT_THREADS, 1)
     contract_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap bmap,
+                    const __grid_constant__ CUtensorMap amap_own, const __grid_constant__ CUtensorMap bmap_own,
                     const ContractArgs p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = align1024(smem_raw);
@@ -522,8 +528,25 @@ __global__ void __launch_bounds__(CT_THREADS, 1)
           }
           const uint32_t dst = sbase + s * CT_STAGE_BYTES;
           mbar_arrive_expect_tx(full(s), CT_STAGE_BYTES);
-          tma_load_4d(dst, &amap, full(s), kl, h, p.row_begin + mi * CT_BM, kr);
-          tma_load_4d(dst + CT_A_BYTES, &bmap, full(s), kl, h, ni * CT_BN, kr);
+          // A: one 128-row box; B: two, so that no box straddles two ranks' row blocks
+          const bool own_k = p.own_mode == 2 && kr == p.own_kr;
+          auto own_row = [&](int row) {
+            return p.own_mode == 1 && row >= p.own_row0 && row < p.own_row0 + p.own_rows;
+          };
+          const int arow = p.row_begin + mi * CT_BM;
+          if (own_k || own_row(arow))
+            tma_load_4d(dst, &amap_own, full(s), kl, h, own_k ? arow : arow - p.own_row0, 0);
+          else
+            tma_load_4d(dst, &amap, full(s), kl, h, arow, kr);
+#pragma unroll
+          for (int hb = 0; hb < CT_BN / CT_BM; ++hb) {
+            const int brow = ni * CT_BN + hb * CT_BM;
+            const uint32_t bdst = dst + CT_A_BYTES + hb * CT_A_BYTES;
+            if (own_k || own_row(brow))
+              tma_load_4d(bdst, &bmap_own, full(s), kl, h, own_k ? brow : brow - p.own_row0, 0);
+            else
+              tma_load_4d(bdst, &bmap, full(s), kl, h, brow, kr);
+          }
           kl += CT_BK;
           if (kl >= p.k_split) {
             kl = 0;
@@ -593,7 +616,7 @@ __global__ void __launch_bounds__(CT_THREADS, 1)
       const int blk = gi / p.block_rows_out, gl = gi - blk * p.block_rows_out;
       const int j0 = ni * CT_BN;
       const bool full_cols = j0 + CT_BN <= p.n;
-      __half *xr = p.x_out + blk * p.x_bs + h * p.x_hs + (int64_t)gl * p.x_rs + j0;
+      __half *xr = (blk == p.own_blk ? p.x_own : p.x_out + blk * p.x_bs) + h * p.x_hs + (int64_t)gl * p.x_rs + j0;
       const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * CT_BN;
 #pragma unroll 1
       for (int chunk = 0; chunk < CT_BN / 32; ++chunk) {
@@ -1106,6 +1129,8 @@ af2_status launch_output_any(af2_ctx *ctx, int out_dtype, const CUtensorMap &xma
 
 }  // namespace
 
+static int shard_rank(const TriangleShard *shard) { return shard ? shard->rank : 0; }
+
 af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L, const void *z, int z_dtype,
                            const float *mask, const float *packed, double eps, int residual, void *out,
                            int out_dtype, void *workspace, cudaStream_t stream, const TriangleShard *shard) {
@@ -1189,11 +1214,23 @@ af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L,
 
   // ---- channel shards: every rank receives its hq channels of every rank's rows ----
   __half *a_all = reinterpret_cast<__half *>(ws + L.off_a_all), *b_all = reinterpret_cast<__half *>(ws + L.off_b_all);
+  // The contraction reads this rank's own share in place: its k block (incoming), or its
+  // rows when they are whole 128-row tiles (outgoing); otherwise the share is copied over.
+  const int own_mode = !sharded ? 0 : !out_dir ? 2 : rows % CT_BM == 0 ? 1 : 0;
   if (sharded) {
     const size_t group_bytes = (size_t)L.ab_rows * L.ab_rs * sizeof(__half);
     if ((st = shard->all_to_all(ctx, a, a_all, group_bytes, group_bytes, stream)) != AF2_OK ||
         (st = shard->all_to_all(ctx, b, b_all, group_bytes, group_bytes, stream)) != AF2_OK)
       return st;
+    if (own_mode == 0) {
+      const size_t at = (size_t)shard_rank(shard) * group_bytes;
+      cudaError_t e = cudaMemcpyAsync(reinterpret_cast<uint8_t *>(a_all) + at, reinterpret_cast<uint8_t *>(a) + at,
+                                      group_bytes, cudaMemcpyDeviceToDevice, stream);
+      if (e == cudaSuccess)
+        e = cudaMemcpyAsync(reinterpret_cast<uint8_t *>(b_all) + at, reinterpret_cast<uint8_t *>(b) + at, group_bytes,
+                            cudaMemcpyDeviceToDevice, stream);
+      if (e != cudaSuccess) return cuda_fail(ctx, e, "own channel group copy");
+    }
   }
 
   // ---- contraction maps: [k block][row][hq][k] viewed as {k, h, row, k block} ----
@@ -1206,11 +1243,21 @@ af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L,
   const uint64_t m_dims[4] = {(uint64_t)kblk, (uint64_t)hq, (uint64_t)op_rows, (uint64_t)nkblk};
   const uint64_t n_dims[4] = {(uint64_t)kblk, (uint64_t)hq, (uint64_t)L.n, (uint64_t)nkblk};
   const uint64_t op_strides[3] = {(uint64_t)L.kp * 2, (uint64_t)L.ab_rs * 2, (uint64_t)L.n * L.ab_rs * 2};
-  const uint32_t m_box[4] = {CT_BK, 1, CT_BM, 1}, n_box[4] = {CT_BK, 1, CT_BN, 1};
-  CUtensorMap amap, bmap, zmap_out;
-  if (!encode_map_4d(&amap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, m_op, m_dims, op_strides, m_box,
+  const uint32_t box[4] = {CT_BK, 1, CT_BM, 1};  // B tiles are loaded as two of these
+  // this rank's own share, read from the projected operands in place (not exchanged):
+  // outgoing its rows, incoming its k block
+  const size_t group = (size_t)L.ab_rows * L.ab_rs;
+  const __half *m_own = (out_dir ? a : b) + (size_t)shard_rank(shard) * group;
+  const __half *n_own = (out_dir ? b : a) + (size_t)shard_rank(shard) * group;
+  const uint64_t own_dims[4] = {(uint64_t)kblk, (uint64_t)hq, (uint64_t)(out_dir ? rows : L.n), 1};
+  CUtensorMap amap, bmap, amap_own, bmap_own, zmap_out;
+  if (!encode_map_4d(&amap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, m_op, m_dims, op_strides, box,
                      CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !encode_map_4d(&bmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, n_op, n_dims, op_strides, n_box,
+      !encode_map_4d(&bmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, n_op, n_dims, op_strides, box,
+                     CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_map_4d(&amap_own, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, m_own, own_dims, op_strides, box,
+                     CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_map_4d(&bmap_own, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, n_own, own_dims, op_strides, box,
                      CU_TENSOR_MAP_SWIZZLE_128B) ||
       !encode_map_3d(&zmap_out, map_type(zt), zsrc, C, L.n, rows, row_bytes, row_bytes * L.n, 64, 128, 1,
                      CU_TENSOR_MAP_SWIZZLE_128B))
@@ -1239,6 +1286,12 @@ af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L,
     ca.row_begin = static_cast<int>(rb);
     ca.row_count = static_cast<int>(rc);
     ca.k_split = static_cast<int>(kblk);
+    ca.own_mode = own_mode;
+    ca.own_row0 = static_cast<int>(shard_rank(shard) * rows);
+    ca.own_rows = static_cast<int>(rows);
+    ca.own_kr = shard_rank(shard);
+    ca.own_blk = sharded ? shard_rank(shard) : -1;
+    ca.x_own = reinterpret_cast<__half *>(ws + L.off_x_all) + (size_t)shard_rank(shard) * hq * L.x_hs;
     ca.tiles_m = static_cast<int>((rc + CT_BM - 1) / CT_BM);
     ca.tiles_n = (n + CT_BN - 1) / CT_BN;
     ca.k_blocks = (n + CT_BK - 1) / CT_BK;
@@ -1248,7 +1301,7 @@ af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L,
     const int grid = std::max(1, std::min(ca.total_tiles, ctx->sm_count));
     {
       LaunchScope scope(ctx, stream, kProfTriangleContract);
-      contract_kernel<<<grid, CT_THREADS, CT_SMEM, stream>>>(amap, bmap, ca);
+      contract_kernel<<<grid, CT_THREADS, CT_SMEM, stream>>>(amap, bmap, amap_own, bmap_own, ca);
     }
     const cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? AF2_OK : cuda_fail(ctx, e, "launch contraction");

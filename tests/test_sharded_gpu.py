@@ -40,23 +40,25 @@ def _worker(rank, nranks, port, result):
         uid = [af2cuda.comm_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(uid, src=0)
         af2cuda.comm_init(dev, uid[0], nranks, rank)
-        n = 256
-        r0, r1 = af2cuda.rows_of(n, nranks, rank)
-        z, mask, w = triangle_case(n, seed=7, mask_p=0.9, perturbed=True)
-        mask[:, 17] = 0
-        packed = torch.from_numpy(pack(w)).cuda()
-        mask_d = torch.from_numpy(mask).cuda()
-        torch.cuda.synchronize()
-        for direction in (0, 1):
-            full = torch.from_numpy(z).to("cuda", torch.bfloat16)
-            rows = torch.from_numpy(z[r0:r1]).to("cuda", torch.bfloat16).contiguous()
-            mask_rows = mask_d[r0:r1].contiguous()
-            torch.cuda.synchronize()  # the library runs on its own stream
-            af2cuda.encode_triangle_multiplication_tensors(dev, direction, full, mask_d, packed, residual=True)
-            af2cuda.encode_triangle_multiplication_sharded_tensors(dev, direction, rows, mask_rows, packed, n,
-                                                                   residual=True)
-            dev.sync()
-            ok &= bool(torch.equal(rows, full[r0:r1]))
+        # 64 rows per rank: the outgoing product copies the rank's own channel group;
+        # whole 128-row tiles: it reads the group in place
+        for n in sorted({64 * nranks, 256}):
+            r0, r1 = af2cuda.rows_of(n, nranks, rank)
+            z, mask, w = triangle_case(n, seed=7, mask_p=0.9, perturbed=True)
+            mask[:, 17] = 0
+            packed = torch.from_numpy(pack(w)).cuda()
+            mask_d = torch.from_numpy(mask).cuda()
+            torch.cuda.synchronize()
+            for direction in (0, 1):
+                full = torch.from_numpy(z).to("cuda", torch.bfloat16)
+                rows = torch.from_numpy(z[r0:r1]).to("cuda", torch.bfloat16).contiguous()
+                mask_rows = mask_d[r0:r1].contiguous()
+                torch.cuda.synchronize()  # the library runs on its own stream
+                af2cuda.encode_triangle_multiplication_tensors(dev, direction, full, mask_d, packed, residual=True)
+                af2cuda.encode_triangle_multiplication_sharded_tensors(dev, direction, rows, mask_rows, packed, n,
+                                                                       residual=True)
+                dev.sync()
+                ok &= bool(torch.equal(rows, full[r0:r1]))
         # f32 pair, written out of place, both directions
         zf = torch.from_numpy(z).cuda()
         zf_rows, mask_rows = zf[r0:r1].contiguous(), mask_d[r0:r1].contiguous()
