@@ -210,6 +210,7 @@ struct PrepJob {
   void *out;
   float *scale_out;
   int64_t row0 = 0, rows_total = 0;
+  const float *row_scale = nullptr;  // optional factor per inner row k (a LayerNorm gamma folded in)
 };
 af2_status prepare_matrices(af2_ctx *ctx, const PrepJob *jobs, int count, cudaStream_t stream);
 // Up to 8 zero-padded vector copies done by one launch.

@@ -247,6 +247,7 @@ struct PrepJobDev {
   float extra_scale;
   __half *out;
   float *scale_out;
+  const float *row_scale;  // NULL, or a factor per inner row k
 };
 struct PrepBatch {
   PrepJobDev job[kMaxPrepJobs];
@@ -271,7 +272,8 @@ __device__ __forceinline__ void prep_chunk(const PrepJobDev &jb) {
     float mx = 0.f;
     if (o < jb.cols)
       for (int k = warp; k < jb.inner; k += PREP_THREADS / 32)
-        mx = fmaxf(mx, fabsf(element<FMT>(jb.m, static_cast<int64_t>(k) * jb.cols + o)));
+        mx = fmaxf(mx, fabsf(element<FMT>(jb.m, static_cast<int64_t>(k) * jb.cols + o) *
+                             (jb.row_scale ? jb.row_scale[k] : 1.f)));
     red[warp][lane] = mx;
   }
   __syncthreads();
@@ -298,7 +300,8 @@ __device__ __forceinline__ void prep_chunk(const PrepJobDev &jb) {
   const int kend = min(k0 + PREP_CHUNK, jb.inner_pad);
   for (int k = k0 + warp; k < kend; k += PREP_THREADS / 32) {
     float w = 0.f;
-    if (o < jb.cols && k < jb.inner) w = element<FMT>(jb.m, static_cast<int64_t>(k) * jb.cols + o) * inv;
+    if (o < jb.cols && k < jb.inner)
+      w = element<FMT>(jb.m, static_cast<int64_t>(k) * jb.cols + o) * (jb.row_scale ? jb.row_scale[k] : 1.f) * inv;
     stage[lane][k - k0] = __float2half_rn(w);
   }
   __syncthreads();
@@ -360,7 +363,7 @@ af2_status prepare_matrices(af2_ctx *ctx, const PrepJob *jobs, int count, cudaSt
     b.job[i] = PrepJobDev{MatrixDev{j.w.format, j.w.block, j.w.values, j.w.scales},
                           (int)j.inner, (int)j.cols, (int)j.inner_pad, (int)j.cols_pad, (int)j.row0,
                           (int)(j.rows_total ? j.rows_total : j.cols_pad), j.extra_scale,
-                          static_cast<__half *>(j.out), j.scale_out};
+                          static_cast<__half *>(j.out), j.scale_out, j.row_scale};
     gx = std::max(gx, (unsigned)((j.cols_pad + 31) / 32));
     gy = std::max(gy, (unsigned)((j.inner_pad + PREP_CHUNK - 1) / PREP_CHUNK));
   }

@@ -9,6 +9,8 @@
 // test/outer-product-mean-reference.gpu.test.ts:22-79.
 //
 // Launches per call (weights prepared first):
+//   lnproj     (16-bit MSA, fused layouts) LayerNorm and projection in one
+//              kernel, in place of normalize + project below
 //   normalize  LayerNorm of every MSA row -> f16 [S*N][c_m]
 //   project    the shared tcgen05 GEMM: LN(m) [W_left | W_right], bias, times
 //              the row's mask, split into left and right, f16 [S][N][c]
@@ -151,6 +153,265 @@ __global__ void __launch_bounds__(256) count_kernel(const float *__restrict__ ma
       const int i = i0 + ty + 16 * u, j = j0 + tx + 16 * v;
       if (i < row0 + rows && j < n) rowscale[static_cast<int64_t>(i - row0) * n + j] = 1.f / (norm_eps + acc[u][v]);
     }
+}
+
+// bias[o] += sum_k beta[k] W[k][o] over the projection's 2c columns (left then
+// right): the LayerNorm's beta folded into the biases.  One warp per column,
+// lanes splitting k, f64 sums.
+__global__ void fold_beta_kernel(const float *__restrict__ beta, const float *__restrict__ wl,
+                                 const float *__restrict__ wr, int cm, int c, float *__restrict__ bias) {
+  const int o = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (o >= 2 * c) return;
+  const float *w = o < c ? wl : wr;
+  const int col = o < c ? o : o - c;
+  double acc = 0.0;
+  for (int k = lane; k < cm; k += 32) acc += static_cast<double>(beta[k]) * w[static_cast<int64_t>(k) * c + col];
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(kFull, acc, off);
+  if (lane == 0) bias[o] += static_cast<float>(acc);
+}
+
+// ---- LayerNorm and the left/right projection in one kernel ----
+// For a 16-bit MSA and the fused outer-product layouts.  A tile is 128
+// sequences s of one residue i: TMA lands m[s][i][:] as 128 K-major rows of
+// c_m in 64-channel 128B-swizzled chunks (zero past c_m); eight warps
+// normalise it in place to (x - mean) rstd (two threads per row, each over
+// alternate chunks, the statistics combined by one shuffle); one tcgen05 GEMM
+// per tile gives D[s][0..63] = LN(m) [W_left | W_right], with the LayerNorm's
+// gamma folded into the weight rows and beta into the biases; four warps apply
+// the column scale, the bias and the mask and write left[a][i][s] and
+// right[i][b][s] (the lanes
+// of a warp hold consecutive sequences, so each store covers 64 contiguous
+// bytes).  The normalised MSA never reaches HBM.
+constexpr int LP_THREADS = 448;  // warp 0 TMA, 1 MMA, 2-9 LayerNorm, 10-13 epilogue
+constexpr int LP_STAGES = 3;
+constexpr uint32_t LP_CHUNK = 128 * 128;            // 128 rows x 64 channels, 16-bit
+constexpr uint32_t LP_STAGE = 4 * LP_CHUNK;         // c_m <= 256
+constexpr uint32_t LP_W_CHUNK = 64 * 128;           // 64 output columns x 64 channels
+constexpr uint32_t LP_OFF_STAGE = 4 * LP_W_CHUNK;   // 32 KB of weights first
+constexpr uint32_t LP_OFF_BAR = LP_OFF_STAGE + LP_STAGES * LP_STAGE;
+constexpr uint32_t LP_OFF_VEC = LP_OFF_BAR + 256;  // column scales and biases, 64 f32 each
+constexpr uint32_t LP_SMEM = LP_OFF_VEC + 512 + 1024;
+
+struct LnProjArgs {
+  const float *scale, *bias;  // per output column (64: left then right); gamma and beta are folded in
+  const float *mask;          // [S][n_full]
+  const __half *w;            // [chunks][64][64] f16 operand rows
+  __half *left, *right;       // left [c][rows][pitch]; right (this rank's block) [rows][c][pitch]
+  int64_t n_full, rows, pitch;
+  int row0, s_count, cm, chunks, n_sb, total_tiles;
+  float eps;
+  unsigned int *err;
+};
+
+template <typename MT>
+__global__ void __launch_bounds__(LP_THREADS, 1)
+    lnproj_kernel(const __grid_constant__ CUtensorMap mmap, const LnProjArgs p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = align1024(smem_raw);
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bar0 = sbase + LP_OFF_BAR;
+  auto full = [&](int s) { return bar0 + 8u * s; };
+  auto ready = [&](int s) { return bar0 + 8u * (LP_STAGES + s); };
+  auto empty = [&](int s) { return bar0 + 8u * (2 * LP_STAGES + s); };
+  auto acc_full = [&](int b) { return bar0 + 8u * (3 * LP_STAGES + b); };
+  auto acc_empty = [&](int b) { return bar0 + 8u * (3 * LP_STAGES + 2 + b); };
+  const uint32_t drain = bar0 + 8u * (3 * LP_STAGES + 4);
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + LP_OFF_BAR + 192);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + LP_OFF_BAR + 200);
+  const int warp = warp_index_uniform(), lane = threadIdx.x & 31;
+  const uint32_t stage_bytes = static_cast<uint32_t>(p.chunks) * LP_CHUNK;
+
+  // weights: chunk kc, output column r -> 128B-swizzled K-major rows
+  for (int q = threadIdx.x; q < p.chunks * 64 * 8; q += LP_THREADS) {
+    const int kc = q >> 9, r = (q >> 3) & 63, c16 = q & 7;
+    const uint4 v = *reinterpret_cast<const uint4 *>(p.w + (static_cast<size_t>(kc) * 64 + r) * 64 + c16 * 8);
+    *reinterpret_cast<uint4 *>(smem + kc * LP_W_CHUNK + sw128_offset(r, c16)) = v;
+  }
+  float *vsm = reinterpret_cast<float *>(smem + LP_OFF_VEC);  // [0, 64) scales, [64, 128) biases
+  if (threadIdx.x < 128) vsm[threadIdx.x] = threadIdx.x < 64 ? p.scale[threadIdx.x] : p.bias[threadIdx.x - 64];
+  fence_async_smem();
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < LP_STAGES; ++s) {
+      mbar_init(full(s), 1);
+      mbar_init(ready(s), 8);
+      mbar_init(empty(s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(acc_full(b), 1);
+      mbar_init(acc_empty(b), 4);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 128);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_map(&mmap);
+      int it = 0;
+      for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x, ++it) {
+        const int s = it % LP_STAGES;
+        if (!mbar_wait(empty(s), ((it / LP_STAGES) & 1) ^ 1, abort_flag, p.err, kErrWaitProducer)) break;
+        const int i = t / p.n_sb, sb = t - i * p.n_sb;
+        const uint32_t dst = sbase + LP_OFF_STAGE + s * LP_STAGE;
+        mbar_arrive_expect_tx(full(s), stage_bytes);
+        for (int kc = 0; kc < p.chunks; ++kc)
+          tma_load_3d(dst + kc * LP_CHUNK, &mmap, full(s), kc * 64, p.row0 + i, sb * 128);
+      }
+      // every load issued has landed before the CTA exits (immediate unless a consumer gave up)
+      for (int j = it > LP_STAGES ? it - LP_STAGES : 0; j < it; ++j)
+        mbar_wait_drain(full(j % LP_STAGES), (j / LP_STAGES) & 1, p.err);
+    }
+  } else if (warp == 1) {
+    // the whole warp runs the issue loop; one elected lane issues
+    constexpr uint32_t kIdesc = idesc_f16_f32(128, 64);
+    const uint64_t w_base = sdesc_k_sw128(sbase), x_base = sdesc_k_sw128(sbase + LP_OFF_STAGE);
+    int s = 0, buf = 0;
+    uint32_t ph = 0, bph = 0;
+    for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x) {
+      if (!warp_wait(acc_empty(buf), bph ^ 1, abort_flag, p.err, kErrWaitMma) ||
+          !warp_wait(ready(s), ph, abort_flag, p.err, kErrWaitMma))
+        break;
+      tc_fence_after();
+      const uint64_t xd = x_base + s * (LP_STAGE >> 4);
+      const uint32_t d = tmem + buf * 64;
+      for (int kc = 0; kc < p.chunks; ++kc) {
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks) {
+          const uint64_t ad = xd + ((kc * LP_CHUNK + ks * 32) >> 4);
+          const uint64_t bd = w_base + ((kc * LP_W_CHUNK + ks * 32) >> 4);
+          if (kc == 0 && ks == 0)
+            umma_first(d, ad, bd, kIdesc);
+          else
+            umma_acc(d, ad, bd, kIdesc);
+        }
+      }
+      umma_commit(empty(s));
+      umma_commit(acc_full(buf));
+      if (++s == LP_STAGES) {
+        s = 0;
+        ph ^= 1;
+      }
+      buf ^= 1;
+      if (buf == 0) bph ^= 1;
+    }
+    // Every MMA has completed before TMEM is freed, whether or not a consumer gave up.
+    umma_commit(drain);
+    mbar_wait_drain(drain, 0, p.err);
+  } else if (warp < 10) {
+    // ---- LayerNorm in place: a warp takes 16 rows; lanes l and l + 16 share a row, ----
+    // ---- over chunks kc = half, half + 2 (8 lanes of a quarter-warp: 8 rows, no conflicts) ----
+    const int row = (warp - 2) * 16 + (lane & 15), half = lane >> 4;
+    const float inv_cm = 1.f / static_cast<float>(p.cm);
+    const bool ragged = p.cm != p.chunks * 64;
+    int it = 0;
+    for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x, ++it) {
+      const int s = it % LP_STAGES;
+      if (!warp_wait(full(s), (it / LP_STAGES) & 1, abort_flag, p.err, kErrWaitNormalizer)) break;
+      uint8_t *tile = smem + LP_OFF_STAGE + s * LP_STAGE;
+      auto piece = [&](int kc, int c16) { return tile + kc * LP_CHUNK + sw128_offset(row, c16); };
+      // statistics over values shifted by the row's first channel (both threads use it)
+      const float x0 = unpack2<MT>(*reinterpret_cast<const uint32_t *>(piece(0, 0))).x;
+      const float2 neg_x0 = f2(-x0);
+      float2 s1 = f2(0.f), s2 = f2(0.f);
+      for (int kc = half; kc < p.chunks; kc += 2) {
+#pragma unroll
+        for (int c16 = 0; c16 < 8; ++c16) {
+          const uint4 v = *reinterpret_cast<const uint4 *>(piece(kc, c16));
+          const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            float2 d = f2add(unpack2<MT>(w[e]), neg_x0);
+            if (ragged) {  // channels past c_m (zero-filled) stay out of the statistics
+              const int ch = kc * 64 + c16 * 8 + 2 * e;
+              d.x = ch < p.cm ? d.x : 0.f;
+              d.y = ch + 1 < p.cm ? d.y : 0.f;
+            }
+            s1 = f2add(s1, d);
+            s2 = f2fma(d, d, s2);
+          }
+        }
+      }
+      float a1 = s1.x + s1.y, a2 = s2.x + s2.y;
+      a1 += __shfl_xor_sync(kFull, a1, 16);
+      a2 += __shfl_xor_sync(kFull, a2, 16);
+      const float m1 = a1 * inv_cm;
+      const float mean = x0 + m1;
+      const float rstd = rsqrtf(fmaxf(a2 * inv_cm - m1 * m1, 0.f) + p.eps);
+      const float2 r2 = f2(rstd), sh2 = f2(-mean * rstd);
+      for (int kc = half; kc < p.chunks; kc += 2) {
+#pragma unroll
+        for (int c16 = 0; c16 < 8; ++c16) {
+          uint8_t *ptr = piece(kc, c16);
+          const uint4 v = *reinterpret_cast<const uint4 *>(ptr);
+          const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+          uint32_t o[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 y = f2fma(unpack2<MT>(w[e]), r2, sh2);
+            o[e] = pack_half2(y.x, y.y);
+          }
+          *reinterpret_cast<uint4 *>(ptr) = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+      }
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(ready(s));
+    }
+  } else {
+    // ---- epilogue: scale, bias, mask; left[a][i][s], right[i][b][s] ----
+    const int q = warp & 3;
+    int tile_it = 0;
+    for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x, ++tile_it) {
+      const int buf = tile_it & 1;
+      if (!warp_wait(acc_full(buf), (tile_it >> 1) & 1, abort_flag, p.err, kErrWaitEpilogue)) break;
+      tc_fence_after();
+      const int i = t / p.n_sb, sb = t - i * p.n_sb;
+      const int sq = sb * 128 + q * 32 + lane;
+      const bool live = sq < p.s_count;
+      const float mk = live ? p.mask[static_cast<int64_t>(sq) * p.n_full + p.row0 + i] : 0.f;
+      const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * 64;
+#pragma unroll
+      for (int part = 0; part < 2; ++part) {  // 0: left (columns 0-31), 1: right (32-63)
+        uint32_t v[32];
+        __syncwarp();
+        tmem_ld32(taddr + part * 32, v);
+        tmem_ld_wait();
+        if (part == 1) {  // the accumulator is free once every lane has read it
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(acc_empty(buf));
+        }
+        if (live) {
+          __half *dst = part == 0 ? p.left + static_cast<int64_t>(i) * p.pitch + sq
+                                  : p.right + static_cast<int64_t>(i) * C * p.pitch + sq;
+          const int64_t stride = part == 0 ? p.rows * p.pitch : p.pitch;
+#pragma unroll
+          for (int k = 0; k < 32; ++k) {
+            const int col = part * 32 + k;
+            const float y = fmaf(__uint_as_float(v[k]), vsm[col], vsm[64 + col]) * mk;
+            dst[k * stride] = __float2half_rn(y);
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 128);
+  }
 }
 
 // ---- outer products: outer[(i, j)][a*32 + b] = 2^-shift sum_s left[s][i][a] right[s][j][b] ----
@@ -312,24 +573,27 @@ __global__ void __launch_bounds__(OTHREADS, 1)
 //   D1[i][(j, b)] = sum_s left[a][i][s] right[j][b][s]      (M 128, N 32 J, K S)
 // with left streamed through a ring and the tile's right operand resident in
 // shared memory, both K-major (sequences contiguous: MN-major operands run the
-// tensor core several times slower at this N).  Four warps round D1 * 2^-k to
-// f16 in TMEM, and the tensor core multiplies it, read as an A operand
-// straight from TMEM, by the 32 rows of W_o that belong to channel a:
+// tensor core several times slower at this N).  Worker warps round D1 * 2^-k
+// to f16 in TMEM (one warp per lane quarter and residue j, 32 columns each),
+// and the tensor core multiplies it, read as an A operand straight from TMEM,
+// by the 32 rows of W_o that belong to channel a:
 //   D2_j[i][z] += A2_j[i][b] W_o[a*32 + b][z]                (M 128, N c_z, K 32)
-// The outer products never leave the SM.  After the 32 slices eight warps
-// apply the column scales (which carry 2^k back), b_o, 1/(eps + count) and the
-// residual, and write the pair rows.  D2 sums K = (a, b) in ascending 16-wide
-// steps, as the two-kernel path does, from the same f16 operand values.
+// The outer products never leave the SM.  After the 32 slices the same
+// workers apply the column scales (which carry 2^k back), b_o, 1/(eps + count)
+// and the residual, and write the pair rows, while the next tile's first outer
+// products run.  D2 sums K = (a, b) in ascending 16-wide steps, as the
+// two-kernel path does, from the same f16 operand values.
 //
 // TMEM (512 columns): D2_j at 128 j.  J = 2: D1 double-buffered at 256 and
 // 320, A2 at 384 and 416, the output MMAs of slice g issued behind the outer
-// products of slice g + 1.  J = 3: D1 (96 columns) single at 384, A2 written
-// over it; slice g + 1 starts once the output MMAs of slice g have read A2.
+// products of slice g + 1.  J = 3: D1 (96 columns) single at 384, A2_j written
+// over the first half of D1_j; slice g + 1 starts once the output MMAs of
+// slice g have read A2.
 // Each streamed byte of left serves 32 J outputs per sequence, so J = 3 cuts
 // the left traffic per pair (the kernel's bound, through L2) by a third.
 // Tiles are dealt to CTAs in contiguous runs (j-group major), so a CTA reloads
 // the resident right operand only when its j group changes.
-constexpr int FTHREADS = 448;  // warp 0 TMA, 1 MMA, 2-5 slice conversion, 6-13 output epilogue
+constexpr int FTHREADS = 448;  // warp 0 TMA, 1 MMA, 2-13 workers (slice conversion, output epilogue)
 constexpr int FLST_MAX = 8;    // left ring: [128 i][64 s] f16 per stage, as many as shared memory holds
 constexpr uint32_t FL_STAGE = 16384, FW_STAGE = 16384;
 constexpr uint32_t kD2Col = 0;
@@ -343,6 +607,9 @@ struct FusedCfg {
   static constexpr uint32_t kD1Col = J == 2 ? 256 : 384;
   static constexpr uint32_t kA2Col = J == 2 ? 384 : 384;        // J = 3: over D1
   static constexpr uint32_t kD1Stride = 64, kA2Stride = 32;     // between buffers (J = 2)
+  // between the A2 blocks of consecutive residues j: J = 3 writes A2_j over the first 16
+  // columns of D1_j, so each worker overwrites only the columns it has read itself
+  static constexpr uint32_t kA2J = J == 2 ? 16 : 32;
 };
 
 // Shared-memory map: right (resident) | left ring | W_o ring (2) | barriers.
@@ -420,13 +687,13 @@ __global__ void __launch_bounds__(FTHREADS, 1)
       mbar_init(w_full(b), 1);
       mbar_init(w_empty(b), 1);
       mbar_init(d1_full(b), 1);
-      mbar_init(a2_full(b), 4);
+      mbar_init(a2_full(b), 4 * J);
       mbar_init(a2_empty(b), 1);
     }
     mbar_init(r_full, 1);
     mbar_init(r_empty, 1);
     mbar_init(d2_full, 1);
-    mbar_init(d2_empty, 8);
+    mbar_init(d2_empty, 4 * J);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -515,10 +782,10 @@ __global__ void __launch_bounds__(FTHREADS, 1)
 #pragma unroll
       for (int j = 0; j < J; ++j) {
         if (a == 0)
-          umma_ts_first(tmem + kD2Col + 128 * j, a2 + 16 * j, bd, idesc2);
+          umma_ts_first(tmem + kD2Col + 128 * j, a2 + Cfg::kA2J * j, bd, idesc2);
         else
-          umma_ts_acc(tmem + kD2Col + 128 * j, a2 + 16 * j, bd, idesc2);
-        umma_ts_acc(tmem + kD2Col + 128 * j, a2 + 16 * j + 8, bd + 2, idesc2);
+          umma_ts_acc(tmem + kD2Col + 128 * j, a2 + Cfg::kA2J * j, bd, idesc2);
+        umma_ts_acc(tmem + kD2Col + 128 * j, a2 + Cfg::kA2J * j + 8, bd + 2, idesc2);
       }
       umma_commit(a2_empty(bp));
       if (a & 1) {
@@ -581,60 +848,55 @@ __global__ void __launch_bounds__(FTHREADS, 1)
     }
     umma_commit(drain);
     mbar_wait_drain(drain, 0, p.err);
-  } else if (warp < 6) {
-    // ---- slice conversion: D1 (f32) -> A2 (f16 pairs, times 2^-k), lanes 32 q .. 32 q + 31 ----
-    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    uint32_t g = 0;
-    bool ok = true;
-    for (int t = t_begin; ok && t < t_end; ++t) {
-      for (int a = 0; a < C; ++a, ++g) {
-        const int b = g % Cfg::kNB;
-        if (!warp_wait(d1_full(b), (g / Cfg::kNB) & 1, abort_flag, p.err, kErrWaitEpilogue) ||
-            (J == 2 && !warp_wait(a2_empty(b), ((g >> 1) & 1) ^ 1, abort_flag, p.err, kErrWaitEpilogue))) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        // every column is read before any is written (J = 3 writes A2 over D1)
-        uint32_t v[32], pk[16 * J];
-#pragma unroll
-        for (int j = 0; j < J; ++j) {
-          tmem_ld32(tmem + lane_off + Cfg::kD1Col + b * Cfg::kD1Stride + 32 * j, v);
+  } else {
+    // ---- workers: warp (q, jw) owns TMEM lanes 32 q .. 32 q + 31 of residue jw's columns ----
+    // Per slice it converts D1_jw (f32) to A2_jw (f16 pairs, times 2^-k); at the end of a
+    // tile it drains D2_jw: column scales (which carry 2^k back), b_o, 1 / (eps + count) and
+    // the residual, written to the pair rows.  Twelve warps share each slice's conversion,
+    // so the tensor pipe waits for 32 columns per lane, not 32 J.
+    const int q = warp & 3, jw = (warp - 2) >> 2;
+    const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+    const int chunks = p.n_out / 32;
+    if (jw < J) {
+      uint32_t g = 0;
+      int tile_it = 0;
+      bool ok = true;
+      for (int t = t_begin; ok && t < t_end; ++t, ++tile_it) {
+        for (int a = 0; a < C; ++a, ++g) {
+          const int b = g % Cfg::kNB;
+          if (!warp_wait(d1_full(b), (g / Cfg::kNB) & 1, abort_flag, p.err, kErrWaitEpilogue) ||
+              (J == 2 && !warp_wait(a2_empty(b), ((g >> 1) & 1) ^ 1, abort_flag, p.err, kErrWaitEpilogue))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          uint32_t v[32], pk[16];
+          tmem_ld32(tmem + lane_off + Cfg::kD1Col + b * Cfg::kD1Stride + 32 * jw, v);
           tmem_ld_wait();
 #pragma unroll
           for (int c = 0; c < 16; ++c)
-            pk[16 * j + c] =
-                pack_half2(__uint_as_float(v[2 * c]) * p.scale, __uint_as_float(v[2 * c + 1]) * p.scale);
+            pk[c] = pack_half2(__uint_as_float(v[2 * c]) * p.scale, __uint_as_float(v[2 * c + 1]) * p.scale);
+          tmem_st16(tmem + lane_off + Cfg::kA2Col + b * Cfg::kA2Stride + Cfg::kA2J * jw, pk);
+          tmem_st_wait();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(a2_full(b));
         }
-#pragma unroll
-        for (int j = 0; j < J; ++j) tmem_st16(tmem + lane_off + Cfg::kA2Col + b * Cfg::kA2Stride + 16 * j, pk + 16 * j);
-        tmem_st_wait();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(a2_full(b));
-      }
-    }
-  } else {
-    // ---- output epilogue: warp (q, jh) drains lanes 32 q .. 32 q + 31 of D2_j, j = jh, jh + 2 ----
-    const int q = warp & 3, jh = (warp - 6) >> 2;
-    const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
-    const int chunks = p.n_out / 32;
-    int tile_it = 0;
-    for (int t = t_begin; t < t_end; ++t, ++tile_it) {
-      const int jg = t / p.n_ib, ib = fused_tile_ib(t, jg, p.n_ib);
-      const int64_t i = static_cast<int64_t>(ib) * 128 + q * 32 + lane;
-      if (!warp_wait(d2_full, tile_it & 1, abort_flag, p.err, kErrWaitEpilogue)) break;
-      tc_fence_after();
-      for (int jl = jh; jl < J; jl += 2) {
-        const int64_t j = static_cast<int64_t>(J) * jg + jl;
+        if (!ok) break;
+        // ---- output epilogue of this tile: D2_jw, lanes 32 q .. ----
+        const int jg = t / p.n_ib, ib = fused_tile_ib(t, jg, p.n_ib);
+        const int64_t i = static_cast<int64_t>(ib) * 128 + q * 32 + lane;
+        if (!warp_wait(d2_full, tile_it & 1, abort_flag, p.err, kErrWaitEpilogue)) break;
+        tc_fence_after();
+        const int64_t j = static_cast<int64_t>(J) * jg + jw;
         const bool row_ok = i < p.rows && j < p.n;
         const float rs = row_ok ? p.rowscale[i * p.n + j] : 0.f;
         OT *orow = static_cast<OT *>(p.out) + (i * p.n + j) * p.cz;
         for (int ch = 0; ch < chunks; ++ch) {
           uint32_t v[32];
-          tmem_ld32(tmem + lane_off + kD2Col + jl * 128 + ch * 32, v);
+          tmem_ld32(tmem + lane_off + kD2Col + jw * 128 + ch * 32, v);
           tmem_ld_wait();
-          if (ch == chunks - 1 && jl + 2 >= J) {  // D2 is free for the next tile once every lane has read it
+          if (ch == chunks - 1) {  // D2 is free for the next tile once every lane has read it
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(d2_empty);
@@ -799,6 +1061,10 @@ af2_status opm_launch(af2_ctx *ctx, const OpmLayout &L, const void *m, int m_dty
   float *wo_scale = reinterpret_cast<float *>(ws + L.off_wo_scale), *wo_bias = reinterpret_cast<float *>(ws + L.off_wo_bias);
   float *ln = reinterpret_cast<float *>(ws + L.off_ln);
   af2_status st;
+  // 16-bit MSA, fused layouts: LayerNorm and projection in one kernel (gamma and beta folded
+  // into the projection's weights and biases)
+  const bool lnproj = L.fused && m_dtype != AF2_F32 && cm % 8 == 0 && L.cmp <= 256 &&
+                      reinterpret_cast<uintptr_t>(m) % 16 == 0;
   // ---- weights ----
   const af2_matrix left_m{AF2_WEIGHTS_F32, 0, lw, nullptr}, right_m{AF2_WEIGHTS_F32, 0, rw, nullptr};
   const af2_matrix out_m{AF2_WEIGHTS_F32, 0, ow, nullptr};
@@ -809,17 +1075,60 @@ af2_status opm_launch(af2_ctx *ctx, const OpmLayout &L, const void *m, int m_dty
   vs.add(ln_w, cm, L.cmp, ln);
   vs.add(ln_b, cm, L.cmp, ln + L.cmp);
   if (lr_cols > 2 * c) vs.add(nullptr, 0, lr_cols - 2 * c, wlr_scale + 2 * c);
+  const float *fold = lnproj ? ln_w : nullptr;
   const PrepJob jobs[3] = {
-      {left_m, cm, c, L.cmp, c, 1.f, ws + L.off_wlr, wlr_scale, 0, lr_cols},
-      {right_m, cm, c, L.cmp, c, 1.f, ws + L.off_wlr, wlr_scale, c, lr_cols},
+      {left_m, cm, c, L.cmp, c, 1.f, ws + L.off_wlr, wlr_scale, 0, lr_cols, fold},
+      {right_m, cm, c, L.cmp, c, 1.f, ws + L.off_wlr, wlr_scale, c, lr_cols, fold},
       {out_m, c * c, cz, o_inner, o_cols, std::ldexp(1.f, L.out_shift), ws + L.off_wo, wo_scale, 0, 0}};
   if ((st = prepare_matrices(ctx, jobs, 3, stream)) != AF2_OK || (st = pad_vectors(ctx, vs, stream)) != AF2_OK)
     return st;
+  if (lnproj) {
+    LaunchScope scope(ctx, stream, kProfPrepare);
+    fold_beta_kernel<<<(unsigned)((2 * c + 7) / 8), 256, 0, stream>>>(ln_b, lw, rw, (int)cm, (int)c, wlr_bias);
+    if (cudaError_t e = cudaGetLastError(); e != cudaSuccess) return cuda_fail(ctx, e, "OPM LayerNorm fold");
+  }
+  __half *right_full = reinterpret_cast<__half *>(ws + L.off_right);
+  if (lnproj) {
+    CUtensorMap mmap;
+    // m [S][n][c_m] viewed as {c_m, n, S}: a box is 64 channels x 1 residue x 128 sequences
+    if (!encode_map_3d(&mmap, m_dtype == AF2_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                       m, cm, n, s, cm * 2, (uint64_t)n * cm * 2, 64, 1, 128, CU_TENSOR_MAP_SWIZZLE_128B))
+      return fail(ctx, AF2_ERR_CUDA, "cuTensorMapEncodeTiled failed for the OPM's MSA map");
+    LnProjArgs a{};
+    a.scale = wlr_scale;
+    a.bias = wlr_bias;
+    a.mask = mask;
+    a.w = reinterpret_cast<const __half *>(ws + L.off_wlr);
+    a.left = reinterpret_cast<__half *>(ws + L.off_left);
+    a.right = right_full + (size_t)rank * L.seq_pitch * rows * c;
+    a.n_full = n;
+    a.rows = rows;
+    a.pitch = L.seq_pitch;
+    a.row0 = (int)L.row0;
+    a.s_count = (int)s;
+    a.cm = (int)cm;
+    a.chunks = (int)(L.cmp / 64);
+    a.n_sb = (int)((s + 127) / 128);
+    a.total_tiles = (int)(rows * a.n_sb);
+    a.eps = (float)ln_eps;
+    a.err = ctx->err_word;
+    const int grid = std::max(1, std::min(a.total_tiles, ctx->sm_count));
+    auto run = [&](auto tag) -> cudaError_t {
+      using MT = decltype(tag);
+      cudaError_t e = cudaFuncSetAttribute(lnproj_kernel<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, LP_SMEM);
+      if (e != cudaSuccess) return e;
+      LaunchScope scope(ctx, stream, kProfOpmProject);
+      lnproj_kernel<MT><<<grid, LP_THREADS, LP_SMEM, stream>>>(mmap, a);
+      return cudaGetLastError();
+    };
+    const cudaError_t e = m_dtype == AF2_BF16 ? run(__nv_bfloat16{}) : run(__half{});
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "OPM LayerNorm and projection");
+  }
   // ---- LayerNorm of this rank's residue columns (all of them unless sharded) ----
   const int64_t xrows = s * rows;
   __half *xn = reinterpret_cast<__half *>(ws + L.off_xn);
   float *mask_loc = reinterpret_cast<float *>(ws + L.off_mask);
-  {
+  if (!lnproj) {
     const int warps = 8;
     const unsigned blocks = (unsigned)((xrows + warps - 1) / warps);
     LaunchScope scope(ctx, stream, kProfOpmNormalize);
@@ -846,8 +1155,7 @@ af2_status opm_launch(af2_ctx *ctx, const OpmLayout &L, const void *m, int m_dty
     if (e != cudaSuccess) return cuda_fail(ctx, e, "OPM normalisation");
   }
   // ---- left / right projection: right lands in this rank's block of the full operand ----
-  __half *right_full = reinterpret_cast<__half *>(ws + L.off_right);
-  {
+  if (!lnproj) {
     LinearOperands op;
     op.a = xn;
     op.lda = L.cmp;

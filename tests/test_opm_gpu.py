@@ -64,6 +64,28 @@ def test_opm_matches_oracle(device, s, n, cm, cz):
     assert result.elapsedMilliseconds > 0
 
 
+@pytest.mark.parametrize("dtype", ["bfloat16", "float16"])
+@pytest.mark.parametrize("s,n,cm,cz", [(5, 9, 16, 8), (130, 21, 256, 64), (300, 17, 200, 128), (3, 13, 8, 5),
+                                       (256, 33, 128, 128), (700, 20, 48, 32)])
+def test_opm_16bit_msa_matches_oracle(device, dtype, s, n, cm, cz):
+    """A 16-bit MSA is normalised and projected by one kernel (LayerNorm in
+    shared memory, no normalised copy in HBM): ragged c_m (zero-filled past
+    c_m), sequence counts that do not fill the last 128-sequence tile, and the
+    two- and three-residue outer tiles behind it."""
+    import torch
+    m, mask, w = opm_case(s, n, cm, cz=cz, seed=2 * s + n + cm)
+    mt = torch.from_numpy(m).to("cuda", getattr(torch, dtype))
+    expected = oracle.outer_product_mean(mt.float().cpu().numpy(), mask, opm_packed(w), 32, cz)
+    out = torch.zeros((n, n, cz), dtype=torch.float32, device="cuda")
+    af2cuda.encode_outer_product_mean_tensors(device, mt, torch.from_numpy(mask).cuda(),
+                                              torch.from_numpy(opm_packed(w)).cuda(), 32, cz, out=out,
+                                              residual=False)
+    device.sync()
+    got = out.cpu().numpy()
+    assert np.isfinite(got).all()
+    assert relative_max_error(got, expected) <= REL_TOL
+
+
 @pytest.mark.parametrize("s,n,cm,cz", [(1030, 12, 16, 24), (40, 20, 32, 160)])
 def test_opm_two_kernel_path_matches_oracle(device, s, n, cm, cz):
     """More than 1024 sequences, or c_z above 128: the outer products go through
