@@ -112,47 +112,69 @@ __global__ void norm_kernel(const MT *__restrict__ m, int64_t rows, int cm, int 
 }
 
 // ---- pair counts: rowscale[i*N + j] = 1 / (norm_eps + sum_s mask[s,i] mask[s,j]) ----
-// A 64 x 64 block of pairs per CTA (each thread a 4 x 4 register block, pairs
-// 16 apart), 64 MSA rows of both residue columns at a time through shared
-// memory; every count sums s in order.
-constexpr int CNT_TILE = 64;
-__global__ void __launch_bounds__(256) count_kernel(const float *__restrict__ mask, int s_count, int n, int row0,
-                                                    int rows, float norm_eps, float *__restrict__ rowscale) {
+// A 64 x 64 block of pairs per CTA of 128 threads, each thread a 4 (i) x 8 (j)
+// register block of contiguous pairs fed by 16-byte shared-memory loads (three
+// loads per 32 FMAs), 32 MSA rows of both residue ranges at a time; every count
+// sums s in order.
+constexpr int CNT_TILE = 64, CNT_S = 32, CNT_THREADS = 128;
+__global__ void __launch_bounds__(CNT_THREADS) count_kernel(const float *__restrict__ mask, int s_count, int n,
+                                                            int row0, int rows, float norm_eps,
+                                                            float *__restrict__ rowscale) {
   // rows i in [row0, row0 + rows), stored from row 0 of rowscale
-  __shared__ float mi[64][CNT_TILE], mj[64][CNT_TILE];
+  __shared__ __align__(16) float mi[CNT_S][CNT_TILE];
+  __shared__ __align__(16) float mj[CNT_S][CNT_TILE];
   const int i0 = row0 + blockIdx.y * CNT_TILE, j0 = blockIdx.x * CNT_TILE;
-  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
-  float acc[4][4] = {};
-  for (int s0 = 0; s0 < s_count; s0 += 64) {
-    for (int e = threadIdx.x; e < 64 * CNT_TILE; e += 256) {
-      const int r = e / CNT_TILE, c = e % CNT_TILE;
+  const int i_end = row0 + rows;
+  const int tx = threadIdx.x & 7, ty = threadIdx.x >> 3;  // j0 + 8 tx .., i0 + 4 ty ..
+  float acc[4][8] = {};
+  // each thread stages 16 elements of each range per chunk; the next chunk's
+  // loads are in flight while the current one is multiplied
+  constexpr int kPer = CNT_S * CNT_TILE / CNT_THREADS;
+  float ra[kPer], rb[kPer];
+  auto fetch = [&](int s0) {
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+      const int e = threadIdx.x + k * CNT_THREADS, r = e / CNT_TILE, c = e % CNT_TILE;
       const int64_t s = s0 + r;
-      mi[r][c] = (s < s_count && i0 + c < row0 + rows) ? mask[s * n + i0 + c] : 0.f;
-      mj[r][c] = (s < s_count && j0 + c < n) ? mask[s * n + j0 + c] : 0.f;
+      const bool sl = s < s_count;
+      ra[k] = (sl && i0 + c < i_end) ? mask[s * n + i0 + c] : 0.f;
+      rb[k] = (sl && j0 + c < n) ? mask[s * n + j0 + c] : 0.f;
+    }
+  };
+  fetch(0);
+  for (int s0 = 0; s0 < s_count; s0 += CNT_S) {
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+      const int e = threadIdx.x + k * CNT_THREADS, r = e / CNT_TILE, c = e % CNT_TILE;
+      mi[r][c] = ra[k];
+      mj[r][c] = rb[k];
     }
     __syncthreads();
-#pragma unroll 4
-    for (int r = 0; r < 64; ++r) {
-      float a[4], b[4];
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        a[k] = mi[r][ty + 16 * k];
-        b[k] = mj[r][tx + 16 * k];
-      }
+    if (s0 + CNT_S < s_count) fetch(s0 + CNT_S);
+#pragma unroll 8
+    for (int r = 0; r < CNT_S; ++r) {
+      const float4 a = *reinterpret_cast<const float4 *>(&mi[r][ty * 4]);
+      const float4 b0 = *reinterpret_cast<const float4 *>(&mj[r][tx * 8]);
+      const float4 b1 = *reinterpret_cast<const float4 *>(&mj[r][tx * 8 + 4]);
+      const float av[4] = {a.x, a.y, a.z, a.w};
+      const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
 #pragma unroll
       for (int u = 0; u < 4; ++u)
 #pragma unroll
-        for (int v = 0; v < 4; ++v) acc[u][v] = fmaf(a[u], b[v], acc[u][v]);
+        for (int v = 0; v < 8; ++v) acc[u][v] = fmaf(av[u], bv[v], acc[u][v]);
     }
     __syncthreads();
   }
 #pragma unroll
-  for (int u = 0; u < 4; ++u)
+  for (int u = 0; u < 4; ++u) {
+    const int i = i0 + ty * 4 + u;
+    if (i >= i_end) continue;
 #pragma unroll
-    for (int v = 0; v < 4; ++v) {
-      const int i = i0 + ty + 16 * u, j = j0 + tx + 16 * v;
-      if (i < row0 + rows && j < n) rowscale[static_cast<int64_t>(i - row0) * n + j] = 1.f / (norm_eps + acc[u][v]);
+    for (int v = 0; v < 8; ++v) {
+      const int j = j0 + tx * 8 + v;
+      if (j < n) rowscale[static_cast<int64_t>(i - row0) * n + j] = 1.f / (norm_eps + acc[u][v]);
     }
+  }
 }
 
 // bias[o] += sum_k beta[k] W[k][o] over the projection's 2c columns (left then
@@ -1184,7 +1206,8 @@ af2_status opm_launch(af2_ctx *ctx, const OpmLayout &L, const void *m, int m_dty
   {
     LaunchScope scope(ctx, stream, kProfOpmCount);
     const dim3 grid((unsigned)((n + CNT_TILE - 1) / CNT_TILE), (unsigned)((rows + CNT_TILE - 1) / CNT_TILE));
-    count_kernel<<<grid, 256, 0, stream>>>(mask, (int)s, (int)n, (int)L.row0, (int)rows, (float)norm_eps, rowscale);
+    count_kernel<<<grid, CNT_THREADS, 0, stream>>>(mask, (int)s, (int)n, (int)L.row0, (int)rows, (float)norm_eps,
+                                                   rowscale);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(ctx, e, "OPM pair counts");
   }

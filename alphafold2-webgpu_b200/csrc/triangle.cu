@@ -19,11 +19,13 @@
 //     128x256x64 tiles, a 4-deep mbarrier pipeline and two TMEM accumulators
 //     so the epilogue of one tile overlaps the MMAs of the next.  X is stored
 //     f16, pre-scaled by 1/N so any N stays inside the f16 range.
-//  3. output   -- per 128-pair tile: the [h][pair] block of X is transposed
-//     and layer-normalised in shared memory (eps scaled by 1/N^2 to undo the
-//     pre-scale), z is layer-normalised again, and two tcgen05 GEMMs give
-//     LN_out(X) W_z^T and LN(z) W_g^T; the epilogue applies the biases, the
-//     sigmoid gate and the optional residual add and writes the pair rows.
+//  3. output   -- per 128-pair tile: the [h][pair] block of X feeds the first
+//     GEMM as it lands (MN-major), while four warps take its per-pair
+//     LayerNorm statistics (eps scaled by 1/N^2 to undo the pre-scale); z is
+//     layer-normalised again in place; two tcgen05 GEMMs give X W_z'^T and
+//     LN(z) W_g^T, and the epilogue forms LN_out(X) W_z'^T =
+//     rstd (X W_z'^T - mean rowsum(W_z')), applies the biases, the sigmoid
+//     gate and the optional residual add and writes the pair rows.
 //
 // All channel dimensions are padded to 128 (weights zero-padded), with the
 // LayerNorm statistics taken over the real channel counts.
@@ -42,8 +44,10 @@ constexpr int64_t kChannelPad = 64;  // elements added to every channel pitch
 // Prepared weights: six [128][128] f16 matrices, [out][in] row-major.
 enum { kWAP = 0, kWAG = 1, kWBP = 2, kWBG = 3, kWZ = 4, kWG = 5, kMatCount = 6 };
 // Prepared vectors: 128 f32 each.
+// kVZSum: per output channel, the sum over hidden channels of the f16-rounded
+// W_z diag(gamma_out) row (the output kernel normalises X after its GEMM).
 enum {
-  kVLnInW = 0, kVLnInB, kVBAP, kVBAG, kVBBP, kVBBG, kVLnOutW, kVLnOutB, kVBZ, kVBG, kVecCount
+  kVLnInW = 0, kVLnInB, kVBAP, kVBAG, kVBBP, kVBBG, kVLnOutW, kVLnOutB, kVBZ, kVBG, kVZSum, kVecCount
 };
 
 // ---------------------------------------------------------------------------
@@ -89,13 +93,21 @@ __global__ void prep_weights_kernel(const float *__restrict__ packed, int cz, in
       case kVBG: o_w = o_gw; o_b = o_gb; o_beta = o_lnib; rows = cz; cols = cz; break;
       default: break;  // the LayerNorm slots are not used by the kernels
     }
+    if (q == kVZSum) {  // the same rounded values the matrix holds
+      o_w = o_zw;
+      rows = cz;
+      cols = ch;
+    }
     const bool live = o_w >= 0 && e < rows;
     double acc = 0.0;
-    if (live)
+    if (live && q == kVZSum)
+      for (int k = lane; k < cols; k += 32)
+        acc += (double)__half2float(__float2half_rn(packed[o_w + (int64_t)e * cols + k] * packed[o_lnow + k]));
+    else if (live)
       for (int k = lane; k < cols; k += 32) acc += (double)packed[o_w + (int64_t)e * cols + k] * (double)packed[o_beta + k];
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-    if (lane == 0) vec[wi] = live ? static_cast<float>(acc + (double)packed[o_b + e]) : 0.f;
+    if (lane == 0) vec[wi] = live ? static_cast<float>(acc + (q == kVZSum ? 0.0 : (double)packed[o_b + e])) : 0.f;
   }
 }
 
@@ -125,8 +137,8 @@ __device__ __forceinline__ void load_weight_matrix(uint8_t *dst, const __half *s
 // ---------------------------------------------------------------------------
 constexpr int PJ_TILE = 64;      // pairs per tile
 constexpr int PJ_STAGES = 3;
-// warp 0 TMA, 1 MMA, 2-5 LayerNorm (two groups of two warps taking alternate
-// tiles, one thread per pair row), 6-9 epilogue of a, 10-13 epilogue of b.
+// warp 0 TMA, 1 MMA, 2-5 LayerNorm (every tile, two threads per pair row),
+// 6-9 epilogue of a, 10-13 epilogue of b.
 constexpr int PJ_THREADS = 448;
 constexpr uint32_t PJ_CHUNK = PJ_TILE * 128;            // one 64-channel K chunk: 8 KB
 constexpr uint32_t PJ_STAGE_BYTES = 2 * PJ_CHUNK;       // 16 KB
@@ -202,6 +214,56 @@ __device__ __forceinline__ void ln_row_thread(uint8_t *tile, uint32_t chunk_byte
   }
 }
 
+// The same normalisation with two threads per row: thread `half` takes the
+// 64-channel chunk `half`; the pair combines its shifted sums with lane ^ 16
+// (a warp holds 16 rows, so the 8 lanes of a quarter-warp read 8 different
+// rows: no bank conflicts).  Both threads shift by the row's first channel.
+template <typename ZT>
+__device__ __forceinline__ void ln_row_pair(uint8_t *tile, uint32_t chunk_bytes, int row, int half, int cz,
+                                            float inv_cz, float eps) {
+  uint8_t *chunk = tile + half * chunk_bytes;
+  const float x0 = unpack2<ZT>(*reinterpret_cast<const uint32_t *>(tile + sw128_offset(row, 0))).x;
+  const float2 neg_x0 = f2(-x0);
+  float2 s1 = f2(0.f), s2 = f2(0.f);
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    const uint4 v = *reinterpret_cast<const uint4 *>(chunk + sw128_offset(row, c));
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float2 d = f2add(unpack2<ZT>(w[i]), neg_x0);
+      if (cz != 128) {
+        const int ch = half * 64 + c * 8 + 2 * i;
+        d.x = ch < cz ? d.x : 0.f;
+        d.y = ch + 1 < cz ? d.y : 0.f;
+      }
+      s1 = f2add(s1, d);
+      s2 = f2fma(d, d, s2);
+    }
+  }
+  float a1 = s1.x + s1.y, a2 = s2.x + s2.y;
+  a1 += __shfl_xor_sync(kFull, a1, 16);
+  a2 += __shfl_xor_sync(kFull, a2, 16);
+  const float m1 = a1 * inv_cz;
+  const float mean = x0 + m1;
+  const float var = fmaxf(a2 * inv_cz - m1 * m1, 0.f);
+  const float rstd = rsqrtf(var + eps);
+  const float2 r2 = f2(rstd), sh2 = f2(-mean * rstd);
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    uint8_t *ptr = chunk + sw128_offset(row, c);
+    const uint4 v = *reinterpret_cast<const uint4 *>(ptr);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 y = f2fma(unpack2<ZT>(w[i]), r2, sh2);
+      o[i] = pack_half2(y.x, y.y);
+    }
+    *reinterpret_cast<uint4 *>(ptr) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
 template <typename ZT>
 __global__ void __launch_bounds__(PJ_THREADS, 1)
     project_kernel(const __grid_constant__ CUtensorMap zmap, const __grid_constant__ CUtensorMap amap,
@@ -229,7 +291,7 @@ __global__ void __launch_bounds__(PJ_THREADS, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < PJ_STAGES; ++s) {
       mbar_init(z_full(s), 1);
-      mbar_init(z_ready(s), 2);
+      mbar_init(z_ready(s), 4);
       mbar_init(z_empty(s), 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -319,16 +381,15 @@ __global__ void __launch_bounds__(PJ_THREADS, 1)
     umma_commit(drain);
     mbar_wait_drain(drain, 0, p.err);
   } else if (warp < 6) {
-    // ---- LayerNorm of the z tile, in place, 16-bit -> f16 ----
-    const int grp = (warp - 2) >> 1;
-    const int row = ((warp - 2) & 1) * 32 + lane;
+    // ---- LayerNorm of the z tile, in place, 16-bit -> f16 (every tile, in order) ----
+    const int row = (warp - 2) * 16 + (lane & 15), half = lane >> 4;
     const float inv_cz = 1.f / static_cast<float>(p.cz);
-    int it = grp;
-    for (int t = blockIdx.x + grp * gridDim.x; t < p.total_tiles; t += 2 * gridDim.x, it += 2) {
+    int it = 0;
+    for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x, ++it) {
       const int s = it % PJ_STAGES;
       const uint32_t ph = (it / PJ_STAGES) & 1;
       if (!warp_wait(z_full(s), ph, abort_flag, p.err, kErrWaitNormalizer)) break;
-      ln_row_thread<ZT>(smem + PJ_OFF_STAGE + s * PJ_STAGE_BYTES, PJ_CHUNK, row, p.cz, inv_cz, p.eps);
+      ln_row_pair<ZT>(smem + PJ_OFF_STAGE + s * PJ_STAGE_BYTES, PJ_CHUNK, row, half, p.cz, inv_cz, p.eps);
       fence_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(z_ready(s));
@@ -657,9 +718,9 @@ __global__ void __launch_bounds__(CT_THREADS, 1)
 // Kernel 3: LN_out + output projection + gate + residual.
 // ---------------------------------------------------------------------------
 constexpr int OP_STAGES = 2;
-// warp 0 TMA, 1 MMA, 2-5 LN_out of X (two lanes per pair of pairs, each over
-// half the channels), 6-9 LN_in of z (one thread per pair row), 10-13
-// epilogue (one thread per pair row, all 128 output channels).
+// warp 0 TMA, 1 MMA, 2-5 LN_out statistics of X (two lanes per pair of pairs,
+// each over half the channels), 6-9 LN_in of z (one thread per pair row),
+// 10-13 epilogue (one thread per pair row, all 128 output channels).
 constexpr int OP_THREADS = 448;
 constexpr uint32_t OP_W_BYTES = 2 * 2 * 16384;                 // W_z, W_g
 constexpr uint32_t OP_X_BYTES = 128 * 256, OP_Z_BYTES = 128 * 256;
@@ -670,7 +731,8 @@ constexpr uint32_t OP_OFF_STAGE = OP_W_BYTES;
 constexpr uint32_t OP_OFF_OUT = OP_OFF_STAGE + OP_STAGES * OP_STAGE_BYTES;
 constexpr uint32_t OP_OUT_BYTES = 128 * 256;
 constexpr uint32_t OP_OFF_BAR = OP_OFF_OUT + OP_OUT_BYTES;
-constexpr uint32_t OP_SMEM = OP_OFF_BAR + 256 + 1024;
+constexpr uint32_t OP_OFF_XSTAT = OP_OFF_BAR + 256;  // per pair (mean, rstd) of X: 128 float2
+constexpr uint32_t OP_SMEM = OP_OFF_XSTAT + 1024 + 1024;
 
 struct OutputArgs {
   void *out;
@@ -698,11 +760,15 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
   const uint32_t drain = bar0 + 8u * 10;
   const uint32_t out_full = bar0 + 8u * 11;  // all 4 epilogue warps have staged the tile
   const uint32_t out_free = bar0 + 8u * 12;  // the staged tile has been read by TMA
+  const uint32_t stat_full = bar0 + 8u * 13;  // the X warps have written the tile's statistics
+  const uint32_t stat_free = bar0 + 8u * 14;  // the epilogue warps have read them
+  float2 *xstat = reinterpret_cast<float2 *>(smem + OP_OFF_XSTAT);
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + OP_OFF_BAR + 192);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + OP_OFF_BAR + 200);
   // Per-channel vectors are read straight from global memory: every lane of a
   // warp reads the same element, one broadcast through L1.
   const float *__restrict__ vbz = p.vec + kVBZ * C, *__restrict__ vbg = p.vec + kVBG * C;
+  const float *__restrict__ vzs = p.vec + kVZSum * C;
   const int warp = warp_index_uniform(), lane = threadIdx.x & 31;
   const bool staged_out = sizeof(OT) == 2 && p.cz == C;
 
@@ -722,6 +788,8 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
     mbar_init(drain, 1);
     mbar_init(out_full, 4);
     mbar_init(out_free, 1);
+    mbar_init(stat_full, 4);
+    mbar_init(stat_free, 4);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -806,12 +874,12 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
     umma_commit(drain);
     mbar_wait_drain(drain, 0, p.err);
   } else if (warp < 10) {
-    // ---- LN_out of X in place (warps 2-5) and LN_in of z (warps 6-9) ----
+    // ---- LN_out statistics of X (warps 2-5) and LN_in of z in place (warps 6-9) ----
     // X arrives MN-major: two 64-pair blocks 16 KB apart, each 128 h-rows of
     // 128 B, 128B-swizzled.  Lanes 2c and 2c + 1 of an X warp own the adjacent
     // pairs (2c', 2c' + 1) over the lower and upper half of the channels and
-    // combine their shifted sums with one shuffle.  Nobody touches another
-    // lane's columns, so the normalisation is in place.
+    // combine their shifted sums with one shuffle.  X is only read: the GEMM
+    // consumes it as it landed, and the epilogue applies the statistics.
     const float inv_cz = 1.f / static_cast<float>(p.cz), inv_ch = 1.f / static_cast<float>(p.ch);
     const bool x_role = warp < 6;
     const int tx = (warp - 2) * 32 + lane;  // 0..127 among the X warps
@@ -826,11 +894,11 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
       uint8_t *zs = xs + OP_X_BYTES;
       if (x_role) {
         const int pair = 2 * c, mh = pair >> 6, pl = pair & 63;
-        uint8_t *col = xs + mh * 16384 + (pl & 7) * 2;
+        const uint8_t *col = xs + mh * 16384 + (pl & 7) * 2;
         auto word = [&](int h) {
-          return reinterpret_cast<uint32_t *>(col + h * 128 + ((((pl >> 3) ^ (h & 7))) << 4));
+          return *reinterpret_cast<const __half2 *>(col + h * 128 + ((((pl >> 3) ^ (h & 7))) << 4));
         };
-        const float2 x0 = __half22float2(*reinterpret_cast<const __half2 *>(word(0)));
+        const float2 x0 = __half22float2(word(0));
         const float2 neg_x0 = make_float2(-x0.x, -x0.y);
         float2 s1 = f2(0.f), s2 = f2(0.f);
         // The upper half visits its rows in XOR-4 order within each group of
@@ -839,11 +907,15 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
 #pragma unroll 8
         for (int k = 0; k < 64; ++k) {
           const int h = h0 + (k ^ hx);
-          float2 d = f2add(__half22float2(*reinterpret_cast<const __half2 *>(word(h))), neg_x0);
+          float2 d = f2add(__half22float2(word(h)), neg_x0);
           if (p.ch != C && h >= p.ch) d = f2(0.f);
           s1 = f2add(s1, d);
           s2 = f2fma(d, d, s2);
         }
+        // the stage's X has been read: the GEMM may go, the stage may be refilled after it
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(ready(s));
         s1.x += __shfl_xor_sync(kFull, s1.x, 1);
         s1.y += __shfl_xor_sync(kFull, s1.y, 1);
         s2.x += __shfl_xor_sync(kFull, s2.x, 1);
@@ -851,14 +923,15 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
         const float2 m1 = f2mul(s1, f2(inv_ch));
         const float ra = rsqrtf(fmaxf(s2.x * inv_ch - m1.x * m1.x, 0.f) + p.eps_out);
         const float rb = rsqrtf(fmaxf(s2.y * inv_ch - m1.y * m1.y, 0.f) + p.eps_out);
-        const float2 r2 = make_float2(ra, rb);
-        const float2 sh2 = make_float2(-(x0.x + m1.x) * ra, -(x0.y + m1.y) * rb);
-#pragma unroll 8
-        for (int k = 0; k < 64; ++k) {
-          uint32_t *w = word(h0 + (k ^ hx));
-          const float2 y = f2fma(__half22float2(*reinterpret_cast<const __half2 *>(w)), r2, sh2);
-          *w = pack_half2(y.x, y.y);
+        // the previous tile's statistics have been read by the epilogue
+        if (it > 0 && !warp_wait(stat_free, (it - 1) & 1, abort_flag, p.err, kErrWaitNormalizer)) break;
+        if (hh == 0) {
+          xstat[pair] = make_float2(x0.x + m1.x, ra);
+          xstat[pair + 1] = make_float2(x0.y + m1.y, rb);
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(stat_full);
+        continue;
       } else {
         ln_row_thread<ZT>(zs, 16384, zrow, p.cz, inv_cz, p.eps_in);
       }
@@ -868,6 +941,9 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
     }
   } else {
     // ---- epilogue: (LN_out(X) W_z^T + b_z) * sigmoid(LN(z) W_g^T + b_g) (+ residual) ----
+    // LN_out(X) W_z'^T = rstd (D - mean rowsum(W_z')) with D = X W_z'^T from
+    // the tensor core and the pair's (mean, rstd) from the X warps; the gate
+    // is sigmoid(x) = 1/2 + tanh(x / 2) / 2.
     // 16-bit outputs with 128 channels are staged in shared memory and leave
     // through TMA: a plain store, or an add into the pair for the residual
     // form (the old values never pass through the SM).  The first 48
@@ -879,30 +955,27 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
     const int pr = q * 32 + lane;
     const bool storer = warp == 10 && lane == 0;
     bool store_pending = false;
-    const float2 one = f2(1.f), nlog2e = f2(-1.4426950408889634f);
+    const float2 half2f = f2(0.5f);
     uint8_t *stage_row = smem + OP_OFF_OUT + pr * 128;
+    float2 nmean2 = f2(0.f), rstd2 = f2(0.f);  // this pair row's LN_out statistics
     // Output values of 16 channels from their two accumulators.
     auto gate16 = [&](const uint32_t (&vo)[16], const uint32_t (&vg)[16], int c0, float (&v)[16]) {
 #pragma unroll
       for (int c4 = 0; c4 < 4; ++c4) {
         const float4 bz = *reinterpret_cast<const float4 *>(vbz + c0 + c4 * 4);
         const float4 bg = *reinterpret_cast<const float4 *>(vbg + c0 + c4 * 4);
+        const float4 zs = *reinterpret_cast<const float4 *>(vzs + c0 + c4 * 4);
         const float2 bz2[2] = {make_float2(bz.x, bz.y), make_float2(bz.z, bz.w)};
-        const float2 bg2[2] = {f2mul(make_float2(bg.x, bg.y), nlog2e), f2mul(make_float2(bg.z, bg.w), nlog2e)};
+        const float2 bg2[2] = {f2mul(make_float2(bg.x, bg.y), half2f), f2mul(make_float2(bg.z, bg.w), half2f)};
+        const float2 zs2[2] = {make_float2(zs.x, zs.y), make_float2(zs.z, zs.w)};
 #pragma unroll
         for (int i = 0; i < 2; ++i) {
           const int cc = c4 * 4 + 2 * i;
-          // gate = 1 / (1 + 2^(-(g + b_g) log2 e))
-          const float2 arg = f2fma(make_float2(__uint_as_float(vg[cc]), __uint_as_float(vg[cc + 1])), nlog2e, bg2[i]);
-          float2 e;
-          asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e.x) : "f"(arg.x));
-          asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e.y) : "f"(arg.y));
-          const float2 den = f2add(e, one);
-          float2 gate;
-          asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(gate.x) : "f"(den.x));
-          asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(gate.y) : "f"(den.y));
-          const float2 y =
-              f2mul(f2add(make_float2(__uint_as_float(vo[cc]), __uint_as_float(vo[cc + 1])), bz2[i]), gate);
+          const float2 arg = f2fma(make_float2(__uint_as_float(vg[cc]), __uint_as_float(vg[cc + 1])), half2f, bg2[i]);
+          const float2 gate = f2fma(make_float2(tanhf_approx(arg.x), tanhf_approx(arg.y)), half2f, half2f);
+          const float2 xo = f2fma(
+              f2fma(zs2[i], nmean2, make_float2(__uint_as_float(vo[cc]), __uint_as_float(vo[cc + 1]))), rstd2, bz2[i]);
+          const float2 y = f2mul(xo, gate);
           v[cc] = y.x;
           v[cc + 1] = y.y;
         }
@@ -920,8 +993,17 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
       const int il = t / p.tiles_j, j0 = (t % p.tiles_j) * 128, j = j0 + pr;
       const int buf = it & 1;
       const uint32_t bph = (it >> 1) & 1;
-      if (!warp_wait(acc_full(buf), bph, abort_flag, p.err, kErrWaitEpilogue)) break;
+      if (!warp_wait(acc_full(buf), bph, abort_flag, p.err, kErrWaitEpilogue) ||
+          !warp_wait(stat_full, it & 1, abort_flag, p.err, kErrWaitEpilogue))
+        break;
       tc_fence_after();
+      {
+        const float2 st = xstat[pr];
+        nmean2 = f2(-st.x);
+        rstd2 = f2(st.y);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(stat_free);
+      }
       const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * 256;
       if (staged_out) {
         uint32_t vo[2][16], vg[2][16];
