@@ -322,6 +322,18 @@ __device__ __forceinline__ uint64_t sdesc_k_sw128(uint32_t saddr) {
   return d;
 }
 
+// The same for the 64-byte swizzled layout: rows of 32 16-bit elements (64 B),
+// groups of 8 rows 512 B apart; the tile base must be 512-byte aligned.
+__device__ __forceinline__ uint64_t sdesc_k_sw64(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);  // start address
+  d |= static_cast<uint64_t>(1) << 16;                   // leading byte offset (unused when swizzled)
+  d |= static_cast<uint64_t>(512 >> 4) << 32;            // stride byte offset: 8 rows
+  d |= static_cast<uint64_t>(1) << 46;                   // descriptor version (sm_100)
+  d |= static_cast<uint64_t>(4) << 61;                   // SWIZZLE_64B
+  return d;
+}
+
 // Shared-memory matrix descriptor for an MN-major operand tile in the 128-byte
 // swizzled layout: K-rows of 64 16-bit MN-elements (128 B), 8 K-rows per
 // 1024-byte atom.  `lbo` is the byte distance between consecutive 64-element

@@ -617,7 +617,7 @@ __global__ void __launch_bounds__(OTHREADS, 1)
 // the resident right operand only when its j group changes.
 constexpr int FTHREADS = 448;  // warp 0 TMA, 1 MMA, 2-13 workers (slice conversion, output epilogue)
 constexpr int FLST_MAX = 8;    // left ring: [128 i][64 s] f16 per stage, as many as shared memory holds
-constexpr uint32_t FL_STAGE = 16384, FW_STAGE = 16384;
+constexpr uint32_t FL_STAGE = 16384, FW_STAGE = 8192;  // W_o: one channel's 32 rows x c_z, 64B-swizzled
 constexpr uint32_t kD2Col = 0;
 constexpr uint32_t kFusedSmemLimit = 232448;  // 227 KB of dynamic shared memory per CTA
 constexpr uint32_t kFusedBarBytes = 512;
@@ -671,6 +671,7 @@ struct FusedArgs {
   int lst;                     // left ring stages
   float scale;                 // 2^-k applied to D1 before rounding
   int residual, vector_out;
+  int out_bytes;               // bytes per output element
   unsigned int *err;
 };
 
@@ -736,7 +737,7 @@ __global__ void __launch_bounds__(FTHREADS, 1)
       tma_prefetch_map(&wmap);
       int ls = 0, lph = 0, lcount = 0, wq = 0, rq = 0, prev_jg = -1;
       bool ok = true;
-      const uint32_t w_bytes = static_cast<uint32_t>(p.n_out) * 128u;
+      const uint32_t w_bytes = static_cast<uint32_t>(p.n_out) * 64u;
       for (int t = t_begin; ok && t < t_end; ++t) {
         const int jg = t / p.n_ib, ib = fused_tile_ib(t, jg, p.n_ib);
         if (jg != prev_jg) {
@@ -749,14 +750,14 @@ __global__ void __launch_bounds__(FTHREADS, 1)
           prev_jg = jg;
         }
         for (int a = 0; ok && a < C; ++a) {
-          if ((a & 1) == 0) {  // W_o rows of channels a, a + 1: one [n_out][64] K-major tile
+          {  // W_o rows of channel a: one [n_out][32] K-major tile
             const int ws = wq & 1;
             if (!mbar_wait(w_empty(ws), ((wq >> 1) & 1) ^ 1, abort_flag, p.err, kErrWaitProducer)) {
               ok = false;
               break;
             }
             mbar_arrive_expect_tx(w_full(ws), w_bytes);
-            tma_load_3d(s_w + ws * FW_STAGE, &wmap, w_full(ws), 0, 0, a >> 1);
+            tma_load_3d(s_w + ws * FW_STAGE, &wmap, w_full(ws), (a & 1) * 32, 0, a >> 1);
             ++wq;
           }
           for (int kb = 0; kb < p.k_blocks; ++kb) {
@@ -787,7 +788,7 @@ __global__ void __launch_bounds__(FTHREADS, 1)
     // 128-byte rows; a left stage is 16 KB (1024 units).
     const uint32_t idesc1 = idesc_f16_f32(128, 32 * J);
     const uint32_t idesc2 = idesc_f16_f32(128, p.n_out);  // A in TMEM
-    const uint64_t l_base = sdesc_k_sw128(s_l), r_base = sdesc_k_sw128(s_r), w_base = sdesc_k_sw128(s_w);
+    const uint64_t l_base = sdesc_k_sw128(s_l), r_base = sdesc_k_sw128(s_r), w_base = sdesc_k_sw64(s_w);
     uint64_t l_desc = l_base;
     int ls = 0, lph = 0, wq = 0, rq = 0, prev_jg = -1, tile_it = 0;
     uint32_t g = 0;  // slices issued, over all tiles
@@ -797,9 +798,9 @@ __global__ void __launch_bounds__(FTHREADS, 1)
       const int bp = gp % Cfg::kNB, ws = wq & 1;
       if (a == 0 && !warp_wait(d2_empty, (tile_it & 1) ^ 1, abort_flag, p.err, kErrWaitMma)) return false;
       if (!warp_wait(a2_full(bp), (gp / Cfg::kNB) & 1, abort_flag, p.err, kErrWaitMma)) return false;
-      if ((a & 1) == 0 && !warp_wait(w_full(ws), (wq >> 1) & 1, abort_flag, p.err, kErrWaitMma)) return false;
+      if (!warp_wait(w_full(ws), (wq >> 1) & 1, abort_flag, p.err, kErrWaitMma)) return false;
       tc_fence_after();
-      const uint64_t bd = w_base + ws * (FW_STAGE >> 4) + (a & 1) * 4;  // channel a's 32 rows: 64 bytes in
+      const uint64_t bd = w_base + ws * (FW_STAGE >> 4);
       const uint32_t a2 = tmem + Cfg::kA2Col + bp * Cfg::kA2Stride;
 #pragma unroll
       for (int j = 0; j < J; ++j) {
@@ -810,10 +811,8 @@ __global__ void __launch_bounds__(FTHREADS, 1)
         umma_ts_acc(tmem + kD2Col + 128 * j, a2 + Cfg::kA2J * j + 8, bd + 2, idesc2);
       }
       umma_commit(a2_empty(bp));
-      if (a & 1) {
-        umma_commit(w_empty(ws));
-        ++wq;
-      }
+      umma_commit(w_empty(ws));
+      ++wq;
       return true;
     };
     for (int t = t_begin; ok && t < t_end; ++t, ++tile_it) {
@@ -903,6 +902,16 @@ __global__ void __launch_bounds__(FTHREADS, 1)
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(a2_full(b));
+          if (a == C - 4 && p.residual) {
+            // the pair row this thread adds into at the end of the tile: into L2 ahead of time
+            const int jg = t / p.n_ib, ib = fused_tile_ib(t, jg, p.n_ib);
+            const int64_t i = static_cast<int64_t>(ib) * 128 + q * 32 + lane, j = static_cast<int64_t>(J) * jg + jw;
+            if (i < p.rows && j < p.n) {
+              const char *row = reinterpret_cast<const char *>(p.out) + (i * p.n + j) * p.cz * p.out_bytes;
+              for (int off = 0; off < p.cz * p.out_bytes; off += 128)
+                asm volatile("prefetch.global.L2 [%0];" ::"l"(row + off));
+            }
+          }
         }
         if (!ok) break;
         // ---- output epilogue of this tile: D2_jw, lanes 32 q .. ----
@@ -1027,14 +1036,14 @@ af2_status fused_launch(af2_ctx *ctx, const OpmLayout &L, uint8_t *ws, const __h
   // K-major, sequences contiguous (zero past S):
   // left [c][rows][pitch]: boxes of 64 sequences x 128 residues of one channel
   // right [n][c][pitch]: boxes of 64 sequences x 32 J rows (J residues x 32 channels)
-  // W_o [c*c / 64][o_cols][64]: the 64 rows of two channels a per box
+  // W_o [c*c / 64][o_cols][64]: the 32 rows of one channel a per box (64B-swizzled)
   const uint64_t pitch = L.seq_pitch;
   if (!encode_map_3d(&lmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, ws + L.off_left, s, rows, c, pitch * 2,
                      (uint64_t)rows * pitch * 2, 64, 128, 1, CU_TENSOR_MAP_SWIZZLE_128B) ||
       !encode_map_3d(&rmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, right_full, s, n * c, 1, pitch * 2,
                      (uint64_t)n * c * pitch * 2, 64, (uint32_t)(32 * J), 1, CU_TENSOR_MAP_SWIZZLE_128B) ||
       !encode_map_3d(&wmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, ws + L.off_wo, 64, o_cols, o_inner / 64, 128,
-                     (uint64_t)o_cols * 128, 64, (uint32_t)o_cols, 1, CU_TENSOR_MAP_SWIZZLE_128B))
+                     (uint64_t)o_cols * 128, 32, (uint32_t)o_cols, 1, CU_TENSOR_MAP_SWIZZLE_64B))
     return fail(ctx, AF2_ERR_CUDA, "cuTensorMapEncodeTiled failed for the fused OPM operands");
   FusedArgs a{};
   a.out = out;
@@ -1055,6 +1064,7 @@ af2_status fused_launch(af2_ctx *ctx, const OpmLayout &L, uint8_t *ws, const __h
   {
     const size_t ob = out_dtype == AF2_F32 ? 4 : 2;
     a.vector_out = reinterpret_cast<uintptr_t>(out) % 16 == 0 && (cz * ob) % 16 == 0;
+    a.out_bytes = (int)ob;
   }
   a.err = ctx->err_word;
   const int grid = (a.total_tiles + a.per_cta - 1) / a.per_cta;
