@@ -506,10 +506,20 @@ __global__ void __launch_bounds__(PJ_THREADS, 1)
   }
 }
 // ---------------------------------------------------------------------------
-// Kernel 2: per-channel contraction X[h] = s * A[h] B[h]^T.
+// Kernel 2: per-channel contraction X[h] = s * A[h] B[h]^T, on CTA pairs.
 // ---------------------------------------------------------------------------
-constexpr int CT_BM = 128, CT_BN = 256, CT_BK = 64, CT_STAGES = 4, CT_THREADS = 192;
-constexpr uint32_t CT_A_BYTES = CT_BM * 128, CT_B_BYTES = CT_BN * 128;
+// A cluster of two CTAs computes a 256 x 256 tile of one channel with M = 256
+// tcgen05 MMAs (cta_group::2): CTA r holds rows 128 r .. 128 r + 127 of the
+// tile's A and of its B, so an SM reads 8 KB of operands per 128 x 256 x 16
+// step (12 KB with one-CTA 128 x 256 tiles) and a third fewer operand bytes
+// cross from L2.  Each CTA's TMEM receives its 128 rows (two 256-column
+// accumulators, so the epilogue of one tile overlaps the MMAs of the next);
+// the even CTA issues every MMA; the loads of both CTAs complete on its
+// barriers.
+constexpr int CT_BM = 128, CT_BN = 256, CT_BK = 64, CT_STAGES = 6, CT_THREADS = 192;
+constexpr int CT_PAIR_M = 2 * CT_BM;                    // rows of a pair tile
+constexpr uint32_t CT_A_BYTES = CT_BM * 128;             // this CTA's 128 rows of A per K block
+constexpr uint32_t CT_B_BYTES = (CT_BN / 2) * 128;       // and its 128 rows of B
 constexpr uint32_t CT_STAGE_BYTES = CT_A_BYTES + CT_B_BYTES;
 constexpr uint32_t CT_OFF_BAR = CT_STAGES * CT_STAGE_BYTES;
 constexpr uint32_t CT_SMEM = CT_OFF_BAR + 256 + 1024;
@@ -530,7 +540,7 @@ struct ContractArgs {
   unsigned int *err;
 };
 
-__global__ void __launch_bounds__(CT_THREADS, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(CT_THREADS, 1)
     contract_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap bmap,
                     const __grid_constant__ CUtensorMap amap_own, const __grid_constant__ CUtensorMap bmap_own,
                     const ContractArgs p) {
@@ -538,14 +548,19 @@ __global__ void __launch_bounds__(CT_THREADS, 1)
   uint8_t *smem = align1024(smem_raw);
   const uint32_t sbase = smem_u32(smem);
   const uint32_t bar0 = sbase + CT_OFF_BAR;
+  // full: the leader's only (both CTAs' loads complete on it); empty, acc_full: both CTAs
+  // (multicast commits); acc_empty: the leader's, one arrival per epilogue warp of the pair
   auto full = [&](int s) { return bar0 + 8u * s; };
   auto empty = [&](int s) { return bar0 + 8u * (CT_STAGES + s); };
   auto acc_full = [&](int b) { return bar0 + 8u * (2 * CT_STAGES + b); };
   auto acc_empty = [&](int b) { return bar0 + 8u * (2 * CT_STAGES + 2 + b); };
   const uint32_t drain = bar0 + 8u * (2 * CT_STAGES + 4);
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + CT_OFF_BAR + 128);
-  volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + CT_OFF_BAR + 136);
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + CT_OFF_BAR + 192);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + CT_OFF_BAR + 200);
   const int warp = warp_index_uniform(), lane = threadIdx.x & 31;
+  const int rank = static_cast<int>(cluster_rank());
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
   const int tiles_per_h = p.tiles_m * p.tiles_n;
 
   if (threadIdx.x == 0) {
@@ -555,18 +570,18 @@ __global__ void __launch_bounds__(CT_THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(acc_full(b), 1);
-      mbar_init(acc_empty(b), 4);
+      mbar_init(acc_empty(b), 8);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(smem_u32(tmem_slot), 512);
-    tmem_relinquish();
+    tmem_alloc_pair(smem_u32(tmem_slot), 512);
+    tmem_relinquish_pair();
   }
   tc_fence_before();
-  __syncthreads();
+  cluster_sync_all();  // both CTAs' barriers exist before any arrival crosses the pair
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
@@ -576,38 +591,34 @@ __global__ void __launch_bounds__(CT_THREADS, 1)
       tma_prefetch_map(&bmap);
       int it = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
+      for (int t = pair; t < p.total_tiles && ok; t += npairs) {
         const int h = t / tiles_per_h, rem = t % tiles_per_h;
         const int mi = rem / p.tiles_n, ni = rem % p.tiles_n;
         int kl = 0, kr = 0;  // k = kr * k_split + kl: the operands may hold k in blocks (one per rank)
         for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
           const int s = it % CT_STAGES;
           const uint32_t ph = (it / CT_STAGES) & 1;
+          // the stage is free in this CTA once the pair's MMAs have read it (multicast commit)
           if (!mbar_wait(empty(s), ph ^ 1, abort_flag, p.err, kErrWaitProducer)) {
             ok = false;
             break;
           }
           const uint32_t dst = sbase + s * CT_STAGE_BYTES;
-          mbar_arrive_expect_tx(full(s), CT_STAGE_BYTES);
-          // A: one 128-row box; B: two, so that no box straddles two ranks' row blocks
+          if (leader) mbar_arrive_expect_tx(full(s), 2 * CT_STAGE_BYTES);
           const bool own_k = p.own_mode == 2 && kr == p.own_kr;
           auto own_row = [&](int row) {
             return p.own_mode == 1 && row >= p.own_row0 && row < p.own_row0 + p.own_rows;
           };
-          const int arow = p.row_begin + mi * CT_BM;
+          const int arow = p.row_begin + mi * CT_PAIR_M + rank * CT_BM;
           if (own_k || own_row(arow))
-            tma_load_4d(dst, &amap_own, full(s), kl, h, own_k ? arow : arow - p.own_row0, 0);
+            tma_load_4d_pair(dst, &amap_own, full(s), kl, h, own_k ? arow : arow - p.own_row0, 0);
           else
-            tma_load_4d(dst, &amap, full(s), kl, h, arow, kr);
-#pragma unroll
-          for (int hb = 0; hb < CT_BN / CT_BM; ++hb) {
-            const int brow = ni * CT_BN + hb * CT_BM;
-            const uint32_t bdst = dst + CT_A_BYTES + hb * CT_A_BYTES;
-            if (own_k || own_row(brow))
-              tma_load_4d(bdst, &bmap_own, full(s), kl, h, own_k ? brow : brow - p.own_row0, 0);
-            else
-              tma_load_4d(bdst, &bmap, full(s), kl, h, brow, kr);
-          }
+            tma_load_4d_pair(dst, &amap, full(s), kl, h, arow, kr);
+          const int brow = ni * CT_BN + rank * (CT_BN / 2);
+          if (own_k || own_row(brow))
+            tma_load_4d_pair(dst + CT_A_BYTES, &bmap_own, full(s), kl, h, own_k ? brow : brow - p.own_row0, 0);
+          else
+            tma_load_4d_pair(dst + CT_A_BYTES, &bmap, full(s), kl, h, brow, kr);
           kl += CT_BK;
           if (kl >= p.k_split) {
             kl = 0;
@@ -615,64 +626,63 @@ __global__ void __launch_bounds__(CT_THREADS, 1)
           }
         }
       }
-      {  // every load issued has landed before the CTA exits (immediate unless a consumer gave up)
+      // every load issued has landed before the pair exits (the leader's barriers count
+      // both CTAs' bytes; the peer waits for the leader at the final cluster barrier)
+      if (leader)
         for (int j = it > CT_STAGES ? it - CT_STAGES : 0; j < it; ++j)
           mbar_wait_drain(full(j % CT_STAGES), (j / CT_STAGES) & 1, p.err);
-      }
     }
   } else if (warp == 1) {
-    // the whole warp runs the issue loop (uniform waits, running descriptors); one elected lane issues
-    constexpr uint32_t kIdesc = idesc_f16_f32(CT_BM, CT_BN);
-    const uint64_t a_base = sdesc_k_sw128(sbase);  // stage s: + s * CT_STAGE_BYTES; B follows A
-    uint64_t ad = a_base;
-    int s = 0, buf = 0;
-    uint32_t ph = 0, bph = 0;
-    bool ok = true;
-    for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
-      if (!warp_wait(acc_empty(buf), bph ^ 1, abort_flag, p.err, kErrWaitMma)) break;
-      tc_fence_after();
-      const uint32_t d = tmem + buf * CT_BN;
-      for (int kb = 0; kb < p.k_blocks; ++kb) {
-        if (!warp_wait(full(s), ph, abort_flag, p.err, kErrWaitMma)) {
-          ok = false;
-          break;
-        }
+    if (leader) {
+      // the whole warp runs the issue loop (uniform waits, running descriptors); one elected lane issues
+      constexpr uint32_t kIdesc = idesc_f16_f32(CT_PAIR_M, CT_BN);
+      const uint64_t a_base = sdesc_k_sw128(sbase);  // stage s: + s * CT_STAGE_BYTES; B follows A
+      uint64_t ad = a_base;
+      int s = 0, buf = 0;
+      uint32_t ph = 0, bph = 0;
+      bool ok = true;
+      for (int t = pair; t < p.total_tiles && ok; t += npairs) {
+        if (!warp_wait(acc_empty(buf), bph ^ 1, abort_flag, p.err, kErrWaitMma)) break;
         tc_fence_after();
-        const uint64_t bd = ad + (CT_A_BYTES >> 4);
-        if (kb == 0)
-          umma_first(d, ad, bd, kIdesc);
-        else
-          umma_acc(d, ad, bd, kIdesc);
+        const uint32_t d = tmem + buf * CT_BN;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!warp_wait(full(s), ph, abort_flag, p.err, kErrWaitMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t bd = ad + (CT_A_BYTES >> 4);
 #pragma unroll
-        for (int ks = 1; ks < CT_BK / 16; ++ks) umma_acc(d, ad + ks * 2, bd + ks * 2, kIdesc);
-        umma_commit(empty(s));
-        ad += CT_STAGE_BYTES >> 4;
-        if (++s == CT_STAGES) {
-          s = 0;
-          ph ^= 1;
-          ad = a_base;
+          for (int ks = 0; ks < CT_BK / 16; ++ks) umma_pair(d, ad + ks * 2, bd + ks * 2, kIdesc, (kb | ks) != 0);
+          umma_commit_pair_both(empty(s));
+          ad += CT_STAGE_BYTES >> 4;
+          if (++s == CT_STAGES) {
+            s = 0;
+            ph ^= 1;
+            ad = a_base;
+          }
         }
+        if (!ok) break;
+        umma_commit_pair_both(acc_full(buf));
+        buf ^= 1;
+        if (buf == 0) bph ^= 1;
       }
-      if (!ok) break;
-      umma_commit(acc_full(buf));
-      buf ^= 1;
-      if (buf == 0) bph ^= 1;
+      // Every MMA has completed before TMEM is freed, whether or not a consumer gave up.
+      umma_commit_pair(drain);
+      mbar_wait_drain(drain, 0, p.err);
     }
-    // Every MMA has completed before TMEM is freed, whether or not a consumer gave up.
-    umma_commit(drain);
-    mbar_wait_drain(drain, 0, p.err);
   } else {
     const int q = warp & 3;
     const int row = q * 32 + lane;
     int tile_it = 0;
-    for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x, ++tile_it) {
+    for (int t = pair; t < p.total_tiles; t += npairs, ++tile_it) {
       const int h = t / tiles_per_h, rem = t % tiles_per_h;
       const int mi = rem / p.tiles_n, ni = rem % p.tiles_n;
       const int buf = tile_it & 1;
       const uint32_t bph = (tile_it >> 1) & 1;
       if (!warp_wait(acc_full(buf), bph, abort_flag, p.err, kErrWaitEpilogue)) break;
       tc_fence_after();
-      const int gi = mi * CT_BM + row;  // row inside this launch
+      const int gi = mi * CT_PAIR_M + rank * CT_BM + row;  // row inside this launch
       const bool row_ok = gi < p.row_count;
       const int blk = gi / p.block_rows_out, gl = gi - blk * p.block_rows_out;
       const int j0 = ni * CT_BN;
@@ -702,15 +712,15 @@ __global__ void __launch_bounds__(CT_THREADS, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(acc_empty(buf));
+      if (lane == 0) mbar_arrive_leader(acc_empty(buf));
     }
   }
 
   tc_fence_before();
-  __syncthreads();
+  cluster_sync_all();  // the pair's MMAs and loads are done before either CTA releases TMEM or exits
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    tmem_dealloc_pair(tmem, 512);
   }
 }
 
@@ -1325,7 +1335,7 @@ af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L,
   const uint64_t m_dims[4] = {(uint64_t)kblk, (uint64_t)hq, (uint64_t)op_rows, (uint64_t)nkblk};
   const uint64_t n_dims[4] = {(uint64_t)kblk, (uint64_t)hq, (uint64_t)L.n, (uint64_t)nkblk};
   const uint64_t op_strides[3] = {(uint64_t)L.kp * 2, (uint64_t)L.ab_rs * 2, (uint64_t)L.n * L.ab_rs * 2};
-  const uint32_t box[4] = {CT_BK, 1, CT_BM, 1};  // B tiles are loaded as two of these
+  const uint32_t box[4] = {CT_BK, 1, CT_BM, 1};  // each CTA of a pair loads one A and one B box per K block
   // this rank's own share, read from the projected operands in place (not exchanged):
   // outgoing its rows, incoming its k block
   const size_t group = (size_t)L.ab_rows * L.ab_rs;
@@ -1374,13 +1384,14 @@ af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L,
     ca.own_kr = shard_rank(shard);
     ca.own_blk = sharded ? shard_rank(shard) : -1;
     ca.x_own = reinterpret_cast<__half *>(ws + L.off_x_all) + (size_t)shard_rank(shard) * hq * L.x_hs;
-    ca.tiles_m = static_cast<int>((rc + CT_BM - 1) / CT_BM);
+    ca.tiles_m = static_cast<int>((rc + CT_PAIR_M - 1) / CT_PAIR_M);
     ca.tiles_n = (n + CT_BN - 1) / CT_BN;
     ca.k_blocks = (n + CT_BK - 1) / CT_BK;
     ca.total_tiles = static_cast<int>(hq) * ca.tiles_m * ca.tiles_n;
     ca.scale = 1.0f / static_cast<float>(n);
     ca.err = ctx->err_word;
-    const int grid = std::max(1, std::min(ca.total_tiles, ctx->sm_count));
+    // CTA pairs: an even grid, at most one pair per two SMs
+    const int grid = 2 * std::max(1, std::min(ca.total_tiles, ctx->sm_count / 2));
     {
       LaunchScope scope(ctx, stream, kProfTriangleContract);
       contract_kernel<<<grid, CT_THREADS, CT_SMEM, stream>>>(amap, bmap, amap_own, bmap_own, ca);
