@@ -16,7 +16,7 @@
 //     come out as a'[j][h][k] = a[k][j] and the contraction below is the same
 //     NT GEMM for both directions.
 //  2. contract -- per hidden channel h, X[h] = (1/N) A[h] B[h]^T with TMA-fed
-//     128x256x64 tiles, a 4-deep mbarrier pipeline and two TMEM accumulators
+//     256x256x64 tiles on CTA pairs, a 6-deep mbarrier pipeline and two TMEM accumulators
 //     so the epilogue of one tile overlaps the MMAs of the next.  X is stored
 //     f16, pre-scaled by 1/N so any N stays inside the f16 range.
 //  3. output   -- per 128-pair tile: the [h][pair] block of X feeds the first
@@ -1167,6 +1167,23 @@ TriangleLayout triangle_layout(int64_t n, int64_t cz, int64_t ch, int64_t block_
 
 namespace {
 
+// CTA pairs that can be resident at once for a cluster kernel (its __cluster_dims__
+// of two): a persistent grid larger than this would leave pairs waiting for others to
+// finish.  Queried once per kernel; falls back to half the SMs.
+template <typename K>
+int resident_pairs(af2_ctx *ctx, K kernel, int threads, uint32_t smem) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * std::max(1, ctx->sm_count / 2), 1, 1);
+  cfg.blockDim = dim3(threads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  int clusters = 0;
+  if (cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg) != cudaSuccess || clusters < 1) {
+    cudaGetLastError();
+    clusters = std::max(1, ctx->sm_count / 2);
+  }
+  return clusters;
+}
+
 CUtensorMapDataType map_type(int dtype) {
   return dtype == AF2_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
 }
@@ -1362,9 +1379,11 @@ af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L,
                      CU_TENSOR_MAP_SWIZZLE_128B))
     return fail(ctx, AF2_ERR_CUDA, "cuTensorMapEncodeTiled failed for the output store map");
   static bool contract_configured = false;
+  static int contract_pairs = 0;
   if (!contract_configured) {
     cudaError_t e = cudaFuncSetAttribute(contract_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, CT_SMEM);
     if (e != cudaSuccess) return cuda_fail(ctx, e, "configure contraction kernel");
+    contract_pairs = resident_pairs(ctx, contract_kernel, CT_THREADS, CT_SMEM);
     contract_configured = true;
   }
   auto contract = [&](int64_t rb, int64_t rc, int64_t rows_per_block) -> af2_status {
@@ -1390,8 +1409,8 @@ af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L,
     ca.total_tiles = static_cast<int>(hq) * ca.tiles_m * ca.tiles_n;
     ca.scale = 1.0f / static_cast<float>(n);
     ca.err = ctx->err_word;
-    // CTA pairs: an even grid, at most one pair per two SMs
-    const int grid = 2 * std::max(1, std::min(ca.total_tiles, ctx->sm_count / 2));
+    // CTA pairs: an even grid of at most the pairs that can be resident together
+    const int grid = 2 * std::max(1, std::min(ca.total_tiles, contract_pairs));
     {
       LaunchScope scope(ctx, stream, kProfTriangleContract);
       contract_kernel<<<grid, CT_THREADS, CT_SMEM, stream>>>(amap, bmap, amap_own, bmap_own, ca);

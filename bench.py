@@ -52,7 +52,7 @@ HIDDEN = 4 * CZ
 METRIC = "Evoformer pair-GEMM TFLOP/s & ms/block at N=1024; % of B200 bf16 TC peak"
 # dram__bytes_read.sum + dram__bytes_write.sum per launch, from ncu captures of
 # this workload (profiles/*.md); kernels without a capture report null.
-KERNEL_DRAM_BYTES = {"triangle.contract": 771_527_680, "opm.outer": 268_619_520}
+KERNEL_DRAM_BYTES = {"triangle.contract": 776_628_736, "opm.fused": 599_897_344}
 KERNELS = ("weights.prepare", "triangle.prepare", "triangle.relayout", "triangle.project", "triangle.contract",
            "triangle.output", "opm.normalize", "opm.project", "opm.count", "opm.outer", "opm.output",
            "opm.fused", "transition.prepare", "transition.fused")
