@@ -314,10 +314,9 @@ def run_ours(args) -> None:
            "firstBias": torch.from_numpy(tw["b1"]).cuda(),
            "secondWeight": af2cuda.Q8Matrix(torch.from_numpy(tw["w2"][0]).cuda(), torch.from_numpy(tw["w2"][1]).cuda()),
            "secondBias": torch.from_numpy(tw["b2"]).cuda()}
-    pair_rows = pair.view(rows * N, CZ)
     torch.cuda.synchronize()
 
-    def step():
+    def step(pair=pair, msa=msa):
         if sharded:
             af2cuda.encode_outer_product_mean_sharded_tensors(dev, msa, msa_mask, w_opm, C_OUTER, CZ, pair,
                                                               residual=True, stream=sh)
@@ -329,7 +328,7 @@ def run_ours(args) -> None:
                                                       residual=True, stream=sh)
             af2cuda.encode_triangle_multiplication_tensors(dev, 0, pair, mask, w_out, residual=True, stream=sh)
             af2cuda.encode_triangle_multiplication_tensors(dev, 1, pair, mask, w_in, residual=True, stream=sh)
-        af2cuda.encode_transition_tensors(dev, pair_rows, tws, residual=True, stream=sh)
+        af2cuda.encode_transition_tensors(dev, pair.view(rows * N, CZ), tws, residual=True, stream=sh)
 
     for _ in range(max(args.warmup, 3)):
         step()
@@ -394,29 +393,52 @@ def run_ours(args) -> None:
                 "avg_launch_us": tensor[dom]["avg_us"]}
 
     # ---- e2e: the public device-form API, inputs copied in from pinned host memory every step ----
+    # Every step copies its pair rows and MSA in from pinned host memory and reads its pair rows
+    # back.  With two device copies of the inputs, step k+1's host->device copies (one copy
+    # stream) and step k-1's device->host read (another) run while step k's block computes, and
+    # the two directions share PCIe full duplex; the timed region spans all copies of all steps.
     host_pair = torch.empty(rows, N, CZ, dtype=torch.bfloat16, pin_memory=True)
     host_pair.copy_(pair.cpu())
     host_msa = torch.empty(S_MSA, N, CM, dtype=torch.bfloat16, pin_memory=True)
     host_msa.copy_(msa.cpu())
     host_out = torch.empty_like(host_pair, pin_memory=True)
+    pairs2, msas2 = [pair, torch.empty_like(pair)], [msa, torch.empty_like(msa)]
+    h2d_s, d2h_s = torch.cuda.Stream(), torch.cuda.Stream()
 
-    def host_step():
-        pair.copy_(host_pair, non_blocking=True)
-        msa.copy_(host_msa, non_blocking=True)
-        step()
-        host_out.copy_(pair, non_blocking=True)
+    def e2e_run(steps):
+        free = [None, None]  # buffer b has been read back (so its last block is done too)
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(h2d_s)
+        for k in range(steps):
+            b = k % 2
+            with torch.cuda.stream(h2d_s):
+                if free[b] is not None:
+                    h2d_s.wait_event(free[b])
+                pairs2[b].copy_(host_pair, non_blocking=True)
+                msas2[b].copy_(host_msa, non_blocking=True)
+                ready = torch.cuda.Event()
+                ready.record(h2d_s)
+            stream.wait_event(ready)
+            step(pairs2[b], msas2[b])
+            done = torch.cuda.Event()
+            done.record(stream)
+            with torch.cuda.stream(d2h_s):
+                d2h_s.wait_event(done)
+                host_out.copy_(pairs2[b], non_blocking=True)
+                free[b] = torch.cuda.Event()
+                free[b].record(d2h_s)
+        for f in free:
+            if f is not None:
+                stream.wait_event(f)
+        t1.record(stream)
+        t1.synchronize()
+        return t0.elapsed_time(t1)
 
-    host_step()
+    e2e_run(2)
     torch.cuda.synchronize()
     e2e_steps = max(3, min(args.steps, 10))
     barrier()
-    e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e_start.record(stream)
-    for _ in range(e2e_steps):
-        host_step()
-    e_stop.record(stream)
-    e_stop.synchronize()
-    e2e_ms = e_start.elapsed_time(e_stop)
+    e2e_ms = e2e_run(e2e_steps)
     if dist:
         t = torch.tensor([e2e_ms], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -426,7 +448,8 @@ def run_ours(args) -> None:
            "d2h_bytes_per_step": host_out.numel() * 2, "ms_per_step": e2e_ms / e2e_steps,
            "path": "pair (this rank's rows) and MSA copied in from pinned host memory, the block through the "
                    "af2cuda device-form API (outer product mean, triangle multiplication x2, transition; the "
-                   "row-sharded forms on several GPUs), pair rows read back"}
+                   "row-sharded forms on several GPUs), pair rows read back; copies of neighbouring steps "
+                   "overlap the block (two device input buffers, separate copy streams)"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
