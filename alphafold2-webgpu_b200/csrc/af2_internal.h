@@ -73,6 +73,14 @@ struct af2_ctx {
   void *nccl_comm = nullptr;
   int nranks = 1, rank = 0;
   af2::DeviceBuffer shard_scratch;
+  // The peers' shard scratch, mapped into this process (CUDA IPC) while `peer_of` is the
+  // scratch allocation they were opened for; exchanges copy straight into it.
+  void *peer_of = nullptr;
+  std::vector<void *> peer_scratch;
+  std::vector<cudaStream_t> copy_streams;  // one per peer: the exchange's copies run concurrently
+  std::vector<cudaEvent_t> copy_events;
+  int *sync_word = nullptr;                // device word the exchange barriers all-reduce
+  bool ipc_failed = false;                 // mapping refused: exchanges use NCCL send/recv
 };
 
 namespace af2 {
@@ -137,10 +145,17 @@ TriangleLayout triangle_layout(int64_t n, int64_t cz, int64_t ch, int64_t block_
 // Exchange of the channel-sharded contraction: block p of `send` (blocks
 // `stride` bytes apart, `bytes` each) goes to rank p, and rank p's block for
 // this rank lands in block p of `recv`; this rank's own block is left alone.
+// One all-to-all of an exchange: block p of `send` goes to rank p, and rank p's block lands
+// in block p of `recv` (blocks `stride` bytes apart, `bytes` each).  This rank's own block is
+// not moved: the triangle kernels read and write it in place.
+struct ShardTransfer {
+  const void *send;
+  void *recv;
+  size_t stride, bytes;
+};
 struct TriangleShard {
   int ranks = 1, rank = 0;
-  af2_status (*all_to_all)(af2_ctx *ctx, const void *send, void *recv, size_t stride, size_t bytes,
-                           cudaStream_t stream) = nullptr;
+  af2_status (*exchange)(af2_ctx *ctx, const ShardTransfer *transfers, int count, cudaStream_t stream) = nullptr;
 };
 
 // Launches the whole op on `stream`; the workspace holds TriangleLayout::total bytes.

@@ -3,6 +3,15 @@
 // exchange steps.  The reference has no multi-GPU code; this follows the
 // partitioning its operators allow:
 //
+// Exchanges: the triangle's all-to-alls copy straight into the peers' shard
+// scratch, which every rank maps with CUDA IPC (the handles are all-gathered
+// over NCCL once per allocation), with one copy-engine copy per peer on its
+// own stream; a four-byte NCCL all-reduce before the copies (no rank writes
+// into a buffer a peer may still be reading) and one after them (every
+// rank's data has landed before anyone reads it) order the exchange on the
+// device.  Where the mapping is refused the exchange falls back to NCCL
+// send/recv.
+//
 //   triangle (both)    every rank projects its own pair rows, split into R
 //                      groups of 128 / R hidden channels; an all-to-all gives
 //                      every rank its channel group of every rank's rows, so
@@ -43,6 +52,8 @@ struct NcclApi {
   ncclResult_t (*CommInitRank)(ncclComm_t *, int, ncclUniqueId, int) = nullptr;
   ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
   ncclResult_t (*AllGather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*AllReduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                            cudaStream_t) = nullptr;
   ncclResult_t (*Send)(const void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
   ncclResult_t (*Recv)(void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
   ncclResult_t (*GroupStart)() = nullptr;
@@ -61,12 +72,14 @@ void load_nccl() {
   sym(g_nccl.CommInitRank, "ncclCommInitRank");
   sym(g_nccl.CommDestroy, "ncclCommDestroy");
   sym(g_nccl.AllGather, "ncclAllGather");
+  sym(g_nccl.AllReduce, "ncclAllReduce");
   sym(g_nccl.Send, "ncclSend");
   sym(g_nccl.Recv, "ncclRecv");
   sym(g_nccl.GroupStart, "ncclGroupStart");
   sym(g_nccl.GroupEnd, "ncclGroupEnd");
   sym(g_nccl.GetErrorString, "ncclGetErrorString");
-  g_nccl.ok = g_nccl.GetUniqueId && g_nccl.CommInitRank && g_nccl.CommDestroy && g_nccl.AllGather && g_nccl.Send &&
+  g_nccl.ok = g_nccl.GetUniqueId && g_nccl.CommInitRank && g_nccl.CommDestroy && g_nccl.AllGather && g_nccl.AllReduce &&
+              g_nccl.Send &&
               g_nccl.Recv && g_nccl.GroupStart && g_nccl.GroupEnd && g_nccl.GetErrorString;
 }
 
@@ -83,24 +96,135 @@ ncclComm_t comm_of(af2_ctx *ctx) { return static_cast<ncclComm_t>(ctx->nccl_comm
 
 }  // namespace
 
-// Block p of `send` to rank p, rank p's block into block p of `recv` (blocks
-// `stride` bytes apart, `bytes` each).  This rank's own block is not moved: the
-// triangle kernels read and write it in place.
-static af2_status nccl_all_to_all(af2_ctx *ctx, const void *send, void *recv, size_t stride, size_t bytes,
-                                  cudaStream_t stream) {
-  const char *src = static_cast<const char *>(send);
-  char *dst = static_cast<char *>(recv);
+// NCCL send/recv form of the exchange (the fallback when the peers' scratch cannot be mapped).
+static af2_status nccl_exchange(af2_ctx *ctx, const ShardTransfer *tr, int count, cudaStream_t stream) {
   ncclComm_t comm = comm_of(ctx);
   ncclResult_t r = g_nccl.GroupStart();
-  for (int peer = 0; r == ncclSuccess && peer < ctx->nranks; ++peer) {
-    if (peer == ctx->rank) continue;
-    r = g_nccl.Send(src + peer * stride, bytes, ncclChar, peer, comm, stream);
-    if (r == ncclSuccess) r = g_nccl.Recv(dst + peer * stride, bytes, ncclChar, peer, comm, stream);
+  for (int k = 0; r == ncclSuccess && k < count; ++k) {
+    const char *src = static_cast<const char *>(tr[k].send);
+    char *dst = static_cast<char *>(tr[k].recv);
+    for (int peer = 0; r == ncclSuccess && peer < ctx->nranks; ++peer) {
+      if (peer == ctx->rank) continue;
+      r = g_nccl.Send(src + peer * tr[k].stride, tr[k].bytes, ncclChar, peer, comm, stream);
+      if (r == ncclSuccess) r = g_nccl.Recv(dst + peer * tr[k].stride, tr[k].bytes, ncclChar, peer, comm, stream);
+    }
   }
   const ncclResult_t r2 = g_nccl.GroupEnd();
   if (r != ncclSuccess) return nccl_fail(ctx, r, "channel all-to-all");
   if (r2 != ncclSuccess) return nccl_fail(ctx, r2, "channel all-to-all");
   return AF2_OK;
+}
+
+// Every rank's stream reaches this point before any continues (a four-byte all-reduce).
+static af2_status device_barrier(af2_ctx *ctx, cudaStream_t stream) {
+  const ncclResult_t r = g_nccl.AllReduce(ctx->sync_word, ctx->sync_word, 1, ncclInt32, ncclSum, comm_of(ctx), stream);
+  return r == ncclSuccess ? AF2_OK : nccl_fail(ctx, r, "exchange barrier");
+}
+
+static void close_peers(af2_ctx *ctx) {
+  for (void *&p : ctx->peer_scratch)
+    if (p) {
+      cudaIpcCloseMemHandle(p);
+      p = nullptr;
+    }
+  ctx->peer_of = nullptr;
+}
+
+// Maps every peer's shard scratch (a collective: all ranks call it with their own allocation).
+static af2_status map_peers(af2_ctx *ctx, cudaStream_t stream) {
+  close_peers(ctx);
+  const int R = ctx->nranks;
+  cudaIpcMemHandle_t mine;
+  std::memset(&mine, 0, sizeof mine);
+  int ok = cudaIpcGetMemHandle(&mine, ctx->shard_scratch.ptr) == cudaSuccess ? 1 : 0;
+  if (!ok) cudaGetLastError();
+  // [R][handle + flag], gathered through device memory
+  const size_t rec = sizeof(cudaIpcMemHandle_t) + 16;
+  std::vector<char> host(rec * R, 0);
+  std::memcpy(host.data() + rec * ctx->rank, &mine, sizeof mine);
+  std::memcpy(host.data() + rec * ctx->rank + sizeof mine, &ok, sizeof ok);
+  char *dev = nullptr;
+  if (cudaMalloc(&dev, rec * R) != cudaSuccess) return cuda_fail(ctx, cudaGetLastError(), "handle exchange buffer");
+  cudaError_t e = cudaMemcpyAsync(dev + rec * ctx->rank, host.data() + rec * ctx->rank, rec, cudaMemcpyHostToDevice,
+                                  stream);
+  ncclResult_t r = e == cudaSuccess ? g_nccl.AllGather(dev + rec * ctx->rank, dev, rec, ncclChar, comm_of(ctx), stream)
+                                    : ncclSuccess;
+  if (e == cudaSuccess && r == ncclSuccess)
+    e = cudaMemcpyAsync(host.data(), dev, rec * R, cudaMemcpyDeviceToHost, stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+  cudaFree(dev);
+  if (r != ncclSuccess) return nccl_fail(ctx, r, "all-gather of the scratch handles");
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "handle exchange");
+  bool all = true;
+  for (int p = 0; p < R; ++p) {
+    int flag = 0;
+    std::memcpy(&flag, host.data() + rec * p + sizeof mine, sizeof flag);
+    all = all && flag;
+  }
+  ctx->peer_scratch.assign(R, nullptr);
+  for (int p = 0; all && p < R; ++p) {
+    if (p == ctx->rank) continue;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, host.data() + rec * p, sizeof h);
+    if (cudaIpcOpenMemHandle(&ctx->peer_scratch[p], h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+      cudaGetLastError();
+      ctx->peer_scratch[p] = nullptr;
+      all = false;
+    }
+  }
+  // every rank learns whether all mappings succeeded, so all take the same path
+  int fail_count = all ? 0 : 1;
+  int *dflag = nullptr;
+  if (cudaMalloc(&dflag, sizeof(int)) != cudaSuccess) return cuda_fail(ctx, cudaGetLastError(), "mapping vote");
+  e = cudaMemcpyAsync(dflag, &fail_count, sizeof(int), cudaMemcpyHostToDevice, stream);
+  r = e == cudaSuccess ? g_nccl.AllReduce(dflag, dflag, 1, ncclInt32, ncclSum, comm_of(ctx), stream) : ncclSuccess;
+  if (e == cudaSuccess && r == ncclSuccess) e = cudaMemcpyAsync(&fail_count, dflag, sizeof(int), cudaMemcpyDeviceToHost, stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+  cudaFree(dflag);
+  if (r != ncclSuccess) return nccl_fail(ctx, r, "mapping vote");
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "mapping vote");
+  if (fail_count > 0) {
+    close_peers(ctx);
+    ctx->ipc_failed = true;
+    return AF2_OK;
+  }
+  ctx->peer_of = ctx->shard_scratch.ptr;
+  return AF2_OK;
+}
+
+// The triangle's exchange: copies into the peers' mapped scratch between two device barriers.
+static af2_status ipc_exchange(af2_ctx *ctx, const ShardTransfer *tr, int count, cudaStream_t stream) {
+  const char *base = static_cast<const char *>(ctx->shard_scratch.ptr);
+  bool in_scratch = base != nullptr;
+  for (int k = 0; k < count; ++k) {
+    const char *recv = static_cast<const char *>(tr[k].recv);
+    in_scratch = in_scratch && recv >= base &&
+                 recv + tr[k].stride * (ctx->nranks - 1) + tr[k].bytes <= base + ctx->shard_scratch.bytes;
+  }
+  af2_status st;
+  if (!ctx->ipc_failed && in_scratch && ctx->peer_of != ctx->shard_scratch.ptr &&
+      (st = map_peers(ctx, stream)) != AF2_OK)
+    return st;
+  if (ctx->ipc_failed || !in_scratch) return nccl_exchange(ctx, tr, count, stream);
+  if ((st = device_barrier(ctx, stream)) != AF2_OK) return st;
+  // fork: each peer's copies on its own stream, after everything queued on `stream`
+  cudaEvent_t fork = ctx->copy_events[ctx->rank];
+  cudaError_t e = cudaEventRecord(fork, stream);
+  for (int p = 0; e == cudaSuccess && p < ctx->nranks; ++p) {
+    if (p == ctx->rank) continue;
+    cudaStream_t cs = ctx->copy_streams[p];
+    e = cudaStreamWaitEvent(cs, fork, 0);
+    for (int k = 0; e == cudaSuccess && k < count; ++k) {
+      const size_t off = static_cast<const char *>(tr[k].recv) - base + tr[k].stride * ctx->rank;
+      e = cudaMemcpyAsync(static_cast<char *>(ctx->peer_scratch[p]) + off,
+                          static_cast<const char *>(tr[k].send) + tr[k].stride * p, tr[k].bytes,
+                          cudaMemcpyDeviceToDevice, cs);
+    }
+    if (e == cudaSuccess) e = cudaEventRecord(ctx->copy_events[p], cs);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(stream, ctx->copy_events[p], 0);
+  }
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "exchange copies");
+  return device_barrier(ctx, stream);
 }
 
 static af2_status nccl_all_gather_in_place(af2_ctx *ctx, void *full, size_t bytes_per_rank, cudaStream_t stream) {
@@ -111,6 +235,19 @@ static af2_status nccl_all_gather_in_place(af2_ctx *ctx, void *full, size_t byte
 }
 
 void comm_destroy(af2_ctx *ctx) {
+  close_peers(ctx);
+  for (cudaStream_t cs : ctx->copy_streams)
+    if (cs) cudaStreamDestroy(cs);
+  for (cudaEvent_t ev : ctx->copy_events)
+    if (ev) cudaEventDestroy(ev);
+  ctx->copy_streams.clear();
+  ctx->copy_events.clear();
+  ctx->peer_scratch.clear();
+  if (ctx->sync_word) {
+    cudaFree(ctx->sync_word);
+    ctx->sync_word = nullptr;
+  }
+  ctx->ipc_failed = false;
   if (ctx->nccl_comm) {
     g_nccl.CommDestroy(comm_of(ctx));
     ctx->nccl_comm = nullptr;
@@ -154,6 +291,19 @@ af2_status af2_comm_init(af2_ctx *ctx, const void *unique_id, int nranks, int ra
   ctx->nccl_comm = comm;
   ctx->nranks = nranks;
   ctx->rank = rank;
+  // exchange resources: a barrier word, one copy stream and event per rank
+  cudaError_t e = cudaMalloc(&ctx->sync_word, 256);
+  if (e == cudaSuccess) e = cudaMemset(ctx->sync_word, 0, 256);
+  ctx->copy_streams.assign(nranks, nullptr);
+  ctx->copy_events.assign(nranks, nullptr);
+  for (int p = 0; e == cudaSuccess && p < nranks; ++p) {
+    e = cudaStreamCreateWithFlags(&ctx->copy_streams[p], cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->copy_events[p], cudaEventDisableTiming);
+  }
+  if (e != cudaSuccess) {
+    comm_destroy(ctx);
+    return cuda_fail(ctx, e, "exchange streams");
+  }
   return AF2_OK;
 }
 
@@ -161,6 +311,11 @@ af2_status af2_comm_destroy(af2_ctx *ctx) {
   if (!ctx) return AF2_ERR_INVALID_ARGUMENT;
   cudaSetDevice(ctx->device);
   if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+  if (ctx->nccl_comm && ctx->peer_of) {
+    // every rank closes its mappings of the peers' scratch before any rank frees its own
+    close_peers(ctx);
+    if (device_barrier(ctx, ctx->stream) == AF2_OK) cudaStreamSynchronize(ctx->stream);
+  }
   comm_destroy(ctx);
   return AF2_OK;
 }
@@ -188,11 +343,21 @@ af2_status af2_triangle_multiplication_sharded(af2_ctx *ctx, int direction, cons
   cudaSetDevice(ctx->device);
   cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
   const TriangleLayout L = triangle_layout(n, shape->c_z, shape->c_hidden, 0, z_dtype, rows, direction);
-  if ((st = ensure(ctx, ctx->shard_scratch, L.total, "sharded triangle scratch")) != AF2_OK) return st;
+  // sized for both directions at once, so the allocation the peers have mapped does not move
+  // between an outgoing and an incoming call
+  const TriangleLayout L2 = triangle_layout(n, shape->c_z, shape->c_hidden, 0, z_dtype, rows, 1 - direction);
+  const size_t need = std::max(L.total, L2.total);
+  if (ctx->shard_scratch.bytes < need && ctx->peer_of) {
+    // every rank grows at the same call: all close their mappings before any frees its allocation
+    close_peers(ctx);
+    if ((st = device_barrier(ctx, s)) != AF2_OK) return st;
+    if (cudaError_t e = cudaStreamSynchronize(s); e != cudaSuccess) return cuda_fail(ctx, e, "scratch regrowth");
+  }
+  if ((st = ensure(ctx, ctx->shard_scratch, need, "sharded triangle scratch")) != AF2_OK) return st;
   TriangleShard sh;
   sh.ranks = static_cast<int>(R);
   sh.rank = ctx->rank;
-  sh.all_to_all = nccl_all_to_all;
+  sh.exchange = ipc_exchange;
   return triangle_launch(ctx, direction, L, z, z_dtype, mask, packed_weights, epsilon, residual, out, out_dtype,
                          ctx->shard_scratch.ptr, s, &sh);
 }

@@ -33,6 +33,7 @@
 #include "af2_internal.h"
 
 #include <algorithm>
+#include <array>
 #include <cstring>
 
 namespace af2 {
@@ -1253,7 +1254,7 @@ af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L,
   const int n = static_cast<int>(L.n);
   const int64_t rows = L.rows, R = L.ranks, hq = L.hq;
   const bool sharded = R > 1;
-  if (sharded && (!shard || !shard->all_to_all || shard->ranks != R))
+  if (sharded && (!shard || !shard->exchange || shard->ranks != R))
     return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "a row-sharded triangle multiplication needs the ranks' exchange");
   const int64_t pairs = rows * L.n;
   const bool out_dir = direction == AF2_OUTGOING;
@@ -1328,9 +1329,8 @@ af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L,
   const int own_mode = !sharded ? 0 : !out_dir ? 2 : rows % CT_BM == 0 ? 1 : 0;
   if (sharded) {
     const size_t group_bytes = (size_t)L.ab_rows * L.ab_rs * sizeof(__half);
-    if ((st = shard->all_to_all(ctx, a, a_all, group_bytes, group_bytes, stream)) != AF2_OK ||
-        (st = shard->all_to_all(ctx, b, b_all, group_bytes, group_bytes, stream)) != AF2_OK)
-      return st;
+    const ShardTransfer ab[2] = {{a, a_all, group_bytes, group_bytes}, {b, b_all, group_bytes, group_bytes}};
+    if ((st = shard->exchange(ctx, ab, 2, stream)) != AF2_OK) return st;
     if (own_mode == 0) {
       const size_t at = (size_t)shard_rank(shard) * group_bytes;
       cudaError_t e = cudaMemcpyAsync(reinterpret_cast<uint8_t *>(a_all) + at, reinterpret_cast<uint8_t *>(a) + at,
@@ -1449,7 +1449,8 @@ af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L,
     __half *x_all = reinterpret_cast<__half *>(ws + L.off_x_all);
     const size_t xblock = (size_t)hq * L.x_hs * sizeof(__half);
     if ((st = contract(0, L.n, rows)) != AF2_OK ||
-        (st = shard->all_to_all(ctx, x, x_all, xblock, xblock, stream)) != AF2_OK)
+        (st = shard->exchange(ctx, std::array<ShardTransfer, 1>{{{x, x_all, xblock, xblock}}}.data(), 1, stream)) !=
+            AF2_OK)
       return st;
     return output(x_all, 0, rows);
   }
