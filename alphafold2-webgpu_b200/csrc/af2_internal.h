@@ -153,9 +153,20 @@ struct ShardTransfer {
   void *recv;
   size_t stride, bytes;
 };
+// The exchange has two forms.  Direct: `direct` maps the peers' scratch (once per allocation)
+// and reports whether copies can go straight into it; then `open` (every rank has finished
+// reading its receive buffers), any number of `send`s issued between the kernels that produce
+// their data, and `close` (every rank's data has landed).  Otherwise `exchange` moves whole
+// transfers with NCCL send/recv.
 struct TriangleShard {
   int ranks = 1, rank = 0;
   af2_status (*exchange)(af2_ctx *ctx, const ShardTransfer *transfers, int count, cudaStream_t stream) = nullptr;
+  bool (*direct)(af2_ctx *ctx, cudaStream_t stream, af2_status *status) = nullptr;
+  af2_status (*open)(af2_ctx *ctx, cudaStream_t stream) = nullptr;
+  // `bytes` from `src` to the peer's scratch, at the offset `dst_local` has in this rank's
+  af2_status (*send)(af2_ctx *ctx, const void *src, const void *dst_local, size_t bytes, int peer,
+                     cudaStream_t stream) = nullptr;
+  af2_status (*close)(af2_ctx *ctx, cudaStream_t stream) = nullptr;
 };
 
 // Launches the whole op on `stream`; the workspace holds TriangleLayout::total bytes.

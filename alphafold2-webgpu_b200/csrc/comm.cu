@@ -5,12 +5,15 @@
 //
 // Exchanges: the triangle's all-to-alls copy straight into the peers' shard
 // scratch, which every rank maps with CUDA IPC (the handles are all-gathered
-// over NCCL once per allocation), with one copy-engine copy per peer on its
-// own stream; a four-byte NCCL all-reduce before the copies (no rank writes
-// into a buffer a peer may still be reading) and one after them (every
-// rank's data has landed before anyone reads it) order the exchange on the
+// over NCCL once per allocation), with copy-engine copies on one stream per
+// peer issued as soon as the kernel producing each piece has been queued (the
+// projection in two halves of its rows, the contraction one destination row
+// block at a time, the peers' blocks first), so the copies overlap the
+// kernels; a four-byte NCCL all-reduce before the first copy (no rank writes
+// into a buffer a peer may still be reading) and one after each exchange
+// (every rank's data has landed before anyone reads it) order them on the
 // device.  Where the mapping is refused the exchange falls back to NCCL
-// send/recv.
+// send/recv after each whole kernel.
 //
 //   triangle (both)    every rank projects its own pair rows, split into R
 //                      groups of 128 / R hidden channels; an all-to-all gives
@@ -192,38 +195,42 @@ static af2_status map_peers(af2_ctx *ctx, cudaStream_t stream) {
   return AF2_OK;
 }
 
-// The triangle's exchange: copies into the peers' mapped scratch between two device barriers.
-static af2_status ipc_exchange(af2_ctx *ctx, const ShardTransfer *tr, int count, cudaStream_t stream) {
-  const char *base = static_cast<const char *>(ctx->shard_scratch.ptr);
-  bool in_scratch = base != nullptr;
-  for (int k = 0; k < count; ++k) {
-    const char *recv = static_cast<const char *>(tr[k].recv);
-    in_scratch = in_scratch && recv >= base &&
-                 recv + tr[k].stride * (ctx->nranks - 1) + tr[k].bytes <= base + ctx->shard_scratch.bytes;
-  }
-  af2_status st;
-  if (!ctx->ipc_failed && in_scratch && ctx->peer_of != ctx->shard_scratch.ptr &&
-      (st = map_peers(ctx, stream)) != AF2_OK)
-    return st;
-  if (ctx->ipc_failed || !in_scratch) return nccl_exchange(ctx, tr, count, stream);
-  if ((st = device_barrier(ctx, stream)) != AF2_OK) return st;
-  // fork: each peer's copies on its own stream, after everything queued on `stream`
+// Direct exchange: whether copies can go straight into the peers' scratch (mapping it first).
+static bool ipc_direct(af2_ctx *ctx, cudaStream_t stream, af2_status *status) {
+  *status = AF2_OK;
+  if (ctx->ipc_failed || !ctx->shard_scratch.ptr) return false;
+  if (ctx->peer_of != ctx->shard_scratch.ptr && (*status = map_peers(ctx, stream)) != AF2_OK) return false;
+  return !ctx->ipc_failed && ctx->peer_of == ctx->shard_scratch.ptr;
+}
+
+static af2_status ipc_open(af2_ctx *ctx, cudaStream_t stream) { return device_barrier(ctx, stream); }
+
+// One copy on the peer's copy stream, after everything queued on `stream` so far.
+static af2_status ipc_send(af2_ctx *ctx, const void *src, const void *dst_local, size_t bytes, int peer,
+                           cudaStream_t stream) {
+  const char *base = static_cast<const char *>(ctx->shard_scratch.ptr), *dst = static_cast<const char *>(dst_local);
+  if (peer < 0 || peer >= ctx->nranks || peer == ctx->rank || dst < base ||
+      dst + bytes > base + ctx->shard_scratch.bytes || !ctx->peer_scratch[peer])
+    return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "exchange copy outside the shard scratch");
   cudaEvent_t fork = ctx->copy_events[ctx->rank];
+  cudaStream_t cs = ctx->copy_streams[peer];
   cudaError_t e = cudaEventRecord(fork, stream);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(cs, fork, 0);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(static_cast<char *>(ctx->peer_scratch[peer]) + (dst - base), src, bytes,
+                        cudaMemcpyDeviceToDevice, cs);
+  return e == cudaSuccess ? AF2_OK : cuda_fail(ctx, e, "exchange copy");
+}
+
+// Joins the copy streams into `stream`, then the barrier after which every rank's data has landed.
+static af2_status ipc_close(af2_ctx *ctx, cudaStream_t stream) {
+  cudaError_t e = cudaSuccess;
   for (int p = 0; e == cudaSuccess && p < ctx->nranks; ++p) {
     if (p == ctx->rank) continue;
-    cudaStream_t cs = ctx->copy_streams[p];
-    e = cudaStreamWaitEvent(cs, fork, 0);
-    for (int k = 0; e == cudaSuccess && k < count; ++k) {
-      const size_t off = static_cast<const char *>(tr[k].recv) - base + tr[k].stride * ctx->rank;
-      e = cudaMemcpyAsync(static_cast<char *>(ctx->peer_scratch[p]) + off,
-                          static_cast<const char *>(tr[k].send) + tr[k].stride * p, tr[k].bytes,
-                          cudaMemcpyDeviceToDevice, cs);
-    }
-    if (e == cudaSuccess) e = cudaEventRecord(ctx->copy_events[p], cs);
+    e = cudaEventRecord(ctx->copy_events[p], ctx->copy_streams[p]);
     if (e == cudaSuccess) e = cudaStreamWaitEvent(stream, ctx->copy_events[p], 0);
   }
-  if (e != cudaSuccess) return cuda_fail(ctx, e, "exchange copies");
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "exchange join");
   return device_barrier(ctx, stream);
 }
 
@@ -357,7 +364,11 @@ af2_status af2_triangle_multiplication_sharded(af2_ctx *ctx, int direction, cons
   TriangleShard sh;
   sh.ranks = static_cast<int>(R);
   sh.rank = ctx->rank;
-  sh.exchange = ipc_exchange;
+  sh.exchange = nccl_exchange;
+  sh.direct = ipc_direct;
+  sh.open = ipc_open;
+  sh.send = ipc_send;
+  sh.close = ipc_close;
   return triangle_launch(ctx, direction, L, z, z_dtype, mask, packed_weights, epsilon, residual, out, out_dtype,
                          ctx->shard_scratch.ptr, s, &sh);
 }

@@ -159,6 +159,7 @@ struct ProjectArgs {
   const __half *w16;
   const float *vec;
   int k_extent;              // pairs k per tile row (n, or this rank's rows for a sharded incoming product)
+  int r_begin;               // first tile row of this launch (tile t covers row r_begin + t / tiles_k)
   int cz, tiles_k, total_tiles;
   int transposed;  // incoming: the z map is [k][j][c] and the box walks k in its outer dimension
   float eps;
@@ -329,7 +330,7 @@ __global__ void __launch_bounds__(PJ_THREADS, 1)
           ok = false;
           break;
         }
-        const int r = t / p.tiles_k, kb = t % p.tiles_k;
+        const int r = p.r_begin + t / p.tiles_k, kb = t % p.tiles_k;
         const uint32_t dst = sbase + PJ_OFF_STAGE + s * PJ_STAGE_BYTES;
         mbar_arrive_expect_tx(z_full(s), PJ_STAGE_BYTES);
         const int c1 = p.transposed ? r : kb * PJ_TILE, c2 = p.transposed ? kb * PJ_TILE : r;
@@ -410,14 +411,14 @@ __global__ void __launch_bounds__(PJ_THREADS, 1)
     float *msk = reinterpret_cast<float *>(smem + PJ_OFF_MASK) + e * 64;
     auto mask_at = [&](int t, int k) -> float {
       if (t >= p.total_tiles || k >= p.k_extent) return 0.f;
-      return p.mask[(int64_t)(t / p.tiles_k) * p.mask_rs + (int64_t)k * p.mask_ks];
+      return p.mask[(int64_t)(p.r_begin + t / p.tiles_k) * p.mask_rs + (int64_t)k * p.mask_ks];
     };
     int t = blockIdx.x;
     float m0 = mask_at(t, (t % p.tiles_k) * PJ_TILE + lane);
     float m1 = mask_at(t, (t % p.tiles_k) * PJ_TILE + 32 + lane);
     int it = 0;
     for (; t < p.total_tiles; t += gridDim.x, ++it) {
-      const int r = t / p.tiles_k, k0 = (t % p.tiles_k) * PJ_TILE;
+      const int r = p.r_begin + t / p.tiles_k, k0 = (t % p.tiles_k) * PJ_TILE;
       const int buf = it & 1;
       const uint32_t bph = (it >> 1) & 1;
       // this tile's mask goes to shared memory; the next tile's is fetched now
@@ -1302,6 +1303,7 @@ af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L,
   pa.k_extent = static_cast<int>(k_extent);
   pa.cz = (int)L.cz;
   pa.tiles_k = static_cast<int>((k_extent + PJ_TILE - 1) / PJ_TILE);
+  pa.r_begin = 0;
   pa.total_tiles = static_cast<int>(r_extent) * pa.tiles_k;
   pa.transposed = out_dir ? 0 : 1;
   pa.eps = static_cast<float>(eps);
@@ -1318,19 +1320,47 @@ af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L,
       !encode_map_4d(&bmap_st, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, b, ab_dims, ab_strides, ab_box,
                      CU_TENSOR_MAP_SWIZZLE_128B))
     return fail(ctx, AF2_ERR_CUDA, "cuTensorMapEncodeTiled failed for the projection's store maps");
-  af2_status st = zt == AF2_BF16 ? launch_project<__nv_bfloat16>(ctx, zmap_proj, amap_st, bmap_st, pa, stream)
-                                 : launch_project<__half>(ctx, zmap_proj, amap_st, bmap_st, pa, stream);
-  if (st != AF2_OK) return st;
-
   // ---- channel shards: every rank receives its hq channels of every rank's rows ----
   __half *a_all = reinterpret_cast<__half *>(ws + L.off_a_all), *b_all = reinterpret_cast<__half *>(ws + L.off_b_all);
+  const size_t group_bytes = (size_t)L.ab_rows * L.ab_rs * sizeof(__half);
+  const int me = shard_rank(shard);
+  af2_status st = AF2_OK;
+  // Direct exchange: the projection runs in two halves of its tile rows (the rows of every
+  // channel group), and each half's groups are copied to their ranks while the next computes.
+  const bool direct = sharded && shard->direct && shard->direct(ctx, stream, &st);
+  if (st != AF2_OK) return st;
+  if (direct && (st = shard->open(ctx, stream)) != AF2_OK) return st;
+  const int64_t halves = (direct && r_extent >= 2) ? 2 : 1, r_per = (r_extent + halves - 1) / halves;
+  for (int64_t c = 0; c < halves; ++c) {
+    const int64_t r0 = c * r_per, rc = std::min<int64_t>(r_per, r_extent - r0);
+    pa.r_begin = static_cast<int>(r0);
+    pa.total_tiles = static_cast<int>(rc) * pa.tiles_k;
+    st = zt == AF2_BF16 ? launch_project<__nv_bfloat16>(ctx, zmap_proj, amap_st, bmap_st, pa, stream)
+                        : launch_project<__half>(ctx, zmap_proj, amap_st, bmap_st, pa, stream);
+    if (st != AF2_OK) return st;
+    if (!direct) continue;
+    // tile row r is row r of every channel group (outgoing: local pair row; incoming: column)
+    const size_t off = (size_t)r0 * L.ab_rs * sizeof(__half), bytes = (size_t)rc * L.ab_rs * sizeof(__half);
+    for (int64_t q = 1; q < R; ++q) {
+      const int peer = static_cast<int>((me + q) % R);
+      const size_t from = (size_t)peer * group_bytes + off, to = (size_t)me * group_bytes + off;
+      if ((st = shard->send(ctx, reinterpret_cast<uint8_t *>(a) + from, reinterpret_cast<uint8_t *>(a_all) + to, bytes,
+                            peer, stream)) != AF2_OK ||
+          (st = shard->send(ctx, reinterpret_cast<uint8_t *>(b) + from, reinterpret_cast<uint8_t *>(b_all) + to, bytes,
+                            peer, stream)) != AF2_OK)
+        return st;
+    }
+  }
   // The contraction reads this rank's own share in place: its k block (incoming), or its
   // rows when they are whole 128-row tiles (outgoing); otherwise the share is copied over.
   const int own_mode = !sharded ? 0 : !out_dir ? 2 : rows % CT_BM == 0 ? 1 : 0;
   if (sharded) {
-    const size_t group_bytes = (size_t)L.ab_rows * L.ab_rs * sizeof(__half);
-    const ShardTransfer ab[2] = {{a, a_all, group_bytes, group_bytes}, {b, b_all, group_bytes, group_bytes}};
-    if ((st = shard->exchange(ctx, ab, 2, stream)) != AF2_OK) return st;
+    if (direct) {
+      if ((st = shard->close(ctx, stream)) != AF2_OK) return st;
+    } else {
+      const ShardTransfer ab[2] = {{a, a_all, group_bytes, group_bytes}, {b, b_all, group_bytes, group_bytes}};
+      if ((st = shard->exchange(ctx, ab, 2, stream)) != AF2_OK) return st;
+    }
     if (own_mode == 0) {
       const size_t at = (size_t)shard_rank(shard) * group_bytes;
       cudaError_t e = cudaMemcpyAsync(reinterpret_cast<uint8_t *>(a_all) + at, reinterpret_cast<uint8_t *>(a) + at,
@@ -1386,9 +1416,9 @@ af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L,
     contract_pairs = resident_pairs(ctx, contract_kernel, CT_THREADS, CT_SMEM);
     contract_configured = true;
   }
-  auto contract = [&](int64_t rb, int64_t rc, int64_t rows_per_block) -> af2_status {
+  auto contract = [&](int64_t rb, int64_t rc, int64_t rows_per_block, __half *x_base, int own_blk) -> af2_status {
     ContractArgs ca;
-    ca.x_out = x;
+    ca.x_out = x_base;
     ca.x_hs = L.x_hs;
     ca.x_rs = L.jp;
     ca.x_bs = hq * L.x_hs;
@@ -1401,7 +1431,7 @@ af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L,
     ca.own_row0 = static_cast<int>(shard_rank(shard) * rows);
     ca.own_rows = static_cast<int>(rows);
     ca.own_kr = shard_rank(shard);
-    ca.own_blk = sharded ? shard_rank(shard) : -1;
+    ca.own_blk = own_blk;
     ca.x_own = reinterpret_cast<__half *>(ws + L.off_x_all) + (size_t)shard_rank(shard) * hq * L.x_hs;
     ca.tiles_m = static_cast<int>((rc + CT_PAIR_M - 1) / CT_PAIR_M);
     ca.tiles_n = (n + CT_BN - 1) / CT_BN;
@@ -1448,16 +1478,30 @@ af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L,
     // ([rank][hq][rows][jp]); the exchange gathers all 128 channels of this rank's rows.
     __half *x_all = reinterpret_cast<__half *>(ws + L.off_x_all);
     const size_t xblock = (size_t)hq * L.x_hs * sizeof(__half);
-    if ((st = contract(0, L.n, rows)) != AF2_OK ||
-        (st = shard->exchange(ctx, std::array<ShardTransfer, 1>{{{x, x_all, xblock, xblock}}}.data(), 1, stream)) !=
-            AF2_OK)
+    if (direct) {
+      // one destination row block at a time, the peers' first: each block leaves while the
+      // next is contracted, and this rank's own block (written in place) comes last
+      for (int64_t q = 1; q <= R; ++q) {
+        const int d = static_cast<int>((me + q) % R);
+        __half *xb = reinterpret_cast<__half *>(reinterpret_cast<uint8_t *>(x) + (size_t)d * xblock);
+        if ((st = contract((int64_t)d * rows, rows, rows, xb, d == me ? 0 : -1)) != AF2_OK) return st;
+        if (d != me &&
+            (st = shard->send(ctx, xb, reinterpret_cast<uint8_t *>(x_all) + (size_t)me * xblock, xblock, d, stream)) !=
+                AF2_OK)
+          return st;
+      }
+      if ((st = shard->close(ctx, stream)) != AF2_OK) return st;
+    } else if ((st = contract(0, L.n, rows, x, me)) != AF2_OK ||
+               (st = shard->exchange(ctx, std::array<ShardTransfer, 1>{{{x, x_all, xblock, xblock}}}.data(), 1,
+                                     stream)) != AF2_OK) {
       return st;
+    }
     return output(x_all, 0, rows);
   }
   // one GPU: per block of output rows, contraction then output
   for (int64_t rb = 0; rb < rows; rb += L.block_rows) {
     const int64_t rc = std::min<int64_t>(L.block_rows, rows - rb);
-    if ((st = contract(rb, rc, rc)) != AF2_OK || (st = output(x, rb, rc)) != AF2_OK) return st;
+    if ((st = contract(rb, rc, rc, x, -1)) != AF2_OK || (st = output(x, rb, rc)) != AF2_OK) return st;
   }
   return AF2_OK;
 }
