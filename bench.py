@@ -23,10 +23,13 @@ read back, every step.
 a bounded sample of the same block, with every host thread.
 
 Multi-GPU (torchrun, one process per GPU): the same N=1024 block with the
-pair sharded by rows across the ranks (strong scaling).  The library's NCCL
-communicator all-gathers the projected b operand of the outgoing triangle and
-transposes the pair across ranks (all-to-all) for the incoming one; the OPM
-projects each rank's residues and all-gathers the right operand; the
+pair sharded by rows across the ranks (strong scaling).  Each triangle
+direction projects the rank's own rows, exchanges hidden-channel groups so
+that every rank contracts its 128/R channels over the whole N x N, and
+returns the contracted channels of each rank's rows for the output
+projection (two all-to-alls: copy-engine copies into the peers' IPC-mapped
+scratch between NCCL barriers, NCCL send/recv where the mapping is refused);
+the OPM projects each rank's residues and all-gathers the right operand; the
 transition is row-local.  value = the block's FLOPs over the max-over-ranks
 time.
 """
@@ -493,16 +496,203 @@ def run_ours(args) -> None:
     dev.close()
 
 
+WORKLOADS = {
+    "tri128": "config 1: triangle multiplication outgoing, z [128,128,128] f32 ~N(0,1), mask 1, f32 output",
+    "transition": "config 2: pair transition, X [65536,128] f16 ~N(0,1), LayerNorm in, 128->512 ReLU ->128 with "
+                  "symmetric int8 weights and f32 per-output-channel scales, f16 output",
+    "opm": "config 3: outer product mean, MSA [512,256,256] f32 ~N(0,1), mask Bernoulli(0.9) with row 0 ones, "
+           "c=32, output [256,256,128] f32",
+    "block768": "config 4: one block's pair GEMM set at N=768 (OPM with S=512, c_m=256; triangle out + in; pair "
+                "transition with mixed-q8 weights), bf16 pair updated in place",
+    "multimer": "config 5: N=2048 (4 chains x 512, mask 1 inside the four diagonal chain blocks): triangle out + "
+                "in and pair transition on a bf16 pair [2048,2048,128] updated in place, rows sharded over the ranks",
+}
+
+
+def run_workload(args) -> None:
+    """The other BASELINE configs: one step is one call of the named op (or block) on
+    resident device inputs; value = its algorithmic TFLOP/s (kernel-cost.ts formulas)."""
+    import numpy as np
+    import torch
+
+    import af2cuda
+    from af2cuda import _lib
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        if args.workload != "multimer":
+            raise SystemExit(f"--workload {args.workload} runs on one GPU; only 'multimer' is sharded")
+        import datetime
+
+        import torch.distributed as td
+        td.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+        dist = td
+    dev = af2cuda.Device(local)
+    L = _lib.lib()
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    sh = stream.cuda_stream
+    if world > 1:
+        uid = [af2cuda.comm_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        af2cuda.comm_init(dev, uid[0], world, rank)
+    rng = np.random.default_rng(0)
+    gen = torch.Generator(device="cuda").manual_seed(rank)
+    tw = transition_weights(rng)
+
+    def transition_tensors():
+        return {"layerNormScale": torch.from_numpy(tw["ln"][0]).cuda(),
+                "layerNormOffset": torch.from_numpy(tw["ln"][1]).cuda(),
+                "firstWeight": af2cuda.Q8Matrix(torch.from_numpy(tw["w1"][0]).cuda(),
+                                                torch.from_numpy(tw["w1"][1]).cuda()),
+                "firstBias": torch.from_numpy(tw["b1"]).cuda(),
+                "secondWeight": af2cuda.Q8Matrix(torch.from_numpy(tw["w2"][0]).cuda(),
+                                                 torch.from_numpy(tw["w2"][1]).cuda()),
+                "secondBias": torch.from_numpy(tw["b2"]).cuda()}
+
+    wl = args.workload
+    if wl == "tri128":
+        n = 128
+        z = torch.randn(n, n, CZ, device="cuda", generator=gen)
+        mask = torch.ones(n, n, device="cuda")
+        w = torch.from_numpy(synthetic_weights(rng)).cuda()
+        out = torch.empty_like(z)
+        flops = triangle_flops(n)
+
+        def step():
+            af2cuda.encode_triangle_multiplication_tensors(dev, 0, z, mask, w, out=out, residual=False, stream=sh)
+    elif wl == "transition":
+        rows = 65536
+        x = torch.randn(rows, CZ, device="cuda", generator=gen).half()
+        out = torch.empty_like(x)
+        tws = transition_tensors()
+        flops = 4.0 * rows * CZ * HIDDEN
+
+        def step():
+            af2cuda.encode_transition_tensors(dev, x, tws, out=out, residual=False, stream=sh)
+    elif wl == "opm":
+        n, s = 256, 512
+        msa = torch.randn(s, n, CM, device="cuda", generator=gen)
+        msa_mask = (torch.rand(s, n, device="cuda", generator=gen) < 0.9).float()
+        msa_mask[0] = 1
+        w = torch.from_numpy(opm_weights(rng)).cuda()
+        out = torch.empty(n, n, CZ, device="cuda")
+        flops = opm_flops(n, s)
+
+        def step():
+            af2cuda.encode_outer_product_mean_tensors(dev, msa, msa_mask, w, C_OUTER, CZ, out=out, residual=False,
+                                                      stream=sh)
+    else:
+        n = 768 if wl == "block768" else 2048
+        s = S_MSA
+        rows = n // world
+        r0 = rank * rows
+        pair = torch.randn(rows, n, CZ, device="cuda", generator=gen).to(torch.bfloat16)
+        if wl == "multimer":
+            chain = torch.arange(n, device="cuda") // 512
+            mask = (chain[r0:r0 + rows, None] == chain[None, :]).float().contiguous()
+        else:
+            mask = torch.ones(rows, n, device="cuda")
+            msa = torch.randn(s, n, CM, device="cuda", generator=gen).to(torch.bfloat16)
+            msa_mask = (torch.rand(s, n, device="cuda", generator=gen) < 0.9).float()
+            msa_mask[0] = 1
+            w_opm = torch.from_numpy(opm_weights(rng)).cuda()
+        w_tri = [torch.from_numpy(synthetic_weights(rng)).cuda() for _ in range(2)]
+        tws = transition_tensors()
+        flops = 2 * triangle_flops(n) + transition_flops(n) + (opm_flops(n, s) if wl == "block768" else 0.0)
+
+        def step():
+            if wl == "block768":
+                af2cuda.encode_outer_product_mean_tensors(dev, msa, msa_mask, w_opm, C_OUTER, CZ, pair=pair,
+                                                          residual=True, stream=sh)
+            for d in (0, 1):
+                if world > 1:
+                    af2cuda.encode_triangle_multiplication_sharded_tensors(dev, d, pair, mask, w_tri[d], n,
+                                                                           residual=True, stream=sh)
+                else:
+                    af2cuda.encode_triangle_multiplication_tensors(dev, d, pair, mask, w_tri[d], residual=True,
+                                                                   stream=sh)
+            af2cuda.encode_transition_tensors(dev, pair.view(rows * n, CZ), tws, residual=True, stream=sh)
+    torch.cuda.synchronize()
+    for _ in range(max(args.warmup, 3)):
+        step()
+    dev.sync(sh)
+
+    def barrier():
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    launches0 = dev.launch_count
+    barrier()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        start.record(stream)
+        for _ in range(args.steps):
+            step()
+        stop.record(stream)
+        stop.synchronize()
+    dev.sync(sh)
+    barrier()
+    launches = dev.launch_count - launches0
+    ms = start.elapsed_time(stop)
+    if dist:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = flops * args.steps / (ms * 1e-3) / 1e12
+    peaks = measured_peaks()
+    L.af2_profile_enable(dev.handle, 1)
+    L.af2_profile_reset(dev.handle)
+    for _ in range(3):
+        step()
+    dev.sync(sh)
+    kernel = {}
+    for name in KERNELS:
+        c, t = ctypes.c_uint64(), ctypes.c_double()
+        L.af2_profile_read(dev.handle, name.encode(), ctypes.byref(c), ctypes.byref(t))
+        if c.value:
+            kernel[name] = {"launches_per_step": c.value / 3, "avg_us": t.value / c.value * 1e3,
+                            "ms_per_step": t.value / 3}
+    L.af2_profile_enable(dev.handle, 0)
+    total = sum(k["ms_per_step"] for k in kernel.values()) or 1.0
+    for k in kernel.values():
+        k["share"] = k["ms_per_step"] / total
+    if dist:
+        dist.barrier()
+    if rank == 0:
+        print(json.dumps({
+            "metric": f"{wl} TFLOP/s", "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "config": {"workload": WORKLOADS[wl], "flops_per_step": flops},
+            "pct_of_peak": value / world / peaks["bf16_tflops"], "peak_source": f"{peaks['source']} burst bf16",
+            "kernels": kernel, "gpu_launches": int(launches), "clocks": clocks.record()}), flush=True)
+    if world > 1:
+        af2cuda.comm_destroy(dev)
+    if dist:
+        dist.destroy_process_group()
+    dev.close()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["block", *WORKLOADS], default="block",
+                    help="block (default): the metric's N=1024 block; the others: the remaining BASELINE configs")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload != "block":
+        run_workload(args)
     else:
         run_ours(args)
 

@@ -66,3 +66,57 @@ def bf16_round(x: np.ndarray) -> np.ndarray:
     u = a.view(np.uint32)
     u[:] = ((u.astype(np.uint64) + 0x7FFF + ((u >> 16) & 1)) >> 16 << 16).astype(np.uint32)
     return a
+
+
+def spread(count: int, seed: float) -> np.ndarray:
+    """The reference OPM test's inputs, sin((index + 1) * seed) * 0.7 stored as f32
+    (test/outer-product-mean-reference.gpu.test.ts:81-88)."""
+    return (np.sin(np.arange(1, count + 1, dtype=np.float64) * seed) * 0.7).astype(np.float32)
+
+
+def opm_reference_test_case():
+    """The case of test/outer-product-mean-reference.gpu.test.ts:104-124: 9 sequences,
+    8 residues, c_m 12, 32 outer channels, c_z 16, every third mask entry (flat
+    [S, N] index) zero, spread-valued weights, rowBlockResidues 3.
+    Returns (m [S, N, c_m], mask [S, N], weights dict, row_block)."""
+    s, n, cm, c, cz = 9, 8, 12, 32, 16
+    mask = np.ones(s * n, np.float32)
+    mask[::3] = 0
+    w = dict(layerNormScale=spread(cm, 0.31), layerNormOffset=spread(cm, 0.17),
+             leftWeight=spread(cm * c, 0.11), leftBias=spread(c, 0.23),
+             rightWeight=spread(cm * c, 0.13), rightBias=spread(c, 0.29),
+             outputWeight=spread(c * c * cz, 0.07), outputBias=spread(cz, 0.37))
+    return spread(s * n * cm, 0.19).reshape(s, n, cm), mask.reshape(s, n), w, 3
+
+
+def opm_reference_test_expected(m, mask, w, c: int = 32) -> np.ndarray:
+    """The reference test's own `reference()` (test/outer-product-mean-reference.gpu.test.ts:22-79)
+    restated with its storage: sums in f64 (JS numbers), every Float32Array store
+    rounded to f32, the per-pair outer accumulator a Float32Array updated per sequence."""
+    s, n, cm = m.shape
+    cz = w["outputBias"].size
+    x = m.astype(np.float64).reshape(s * n, cm)
+    mean = x.sum(1, keepdims=True) / cm
+    inv = 1 / np.sqrt(((x - mean) ** 2).sum(1, keepdims=True) / cm + 1e-5)
+    xn = ((x - mean) * inv * w["layerNormScale"].astype(np.float64)
+          + w["layerNormOffset"].astype(np.float64)).astype(np.float32).astype(np.float64)
+    flat_mask = mask.reshape(-1).astype(np.float64)
+
+    def project(weight, bias):
+        total = bias.astype(np.float64) + xn @ weight.reshape(cm, c).astype(np.float64)
+        return (flat_mask[:, None] * total).astype(np.float32).reshape(s, n, c)
+
+    left, right = project(w["leftWeight"], w["leftBias"]), project(w["rightWeight"], w["rightBias"])
+    wo = w["outputWeight"].reshape(c * c, cz).astype(np.float64)
+    out = np.zeros((n, n, cz), np.float32)
+    for i in range(n):
+        for j in range(n):
+            pair = np.zeros(c * c, np.float32)
+            count = 0.0
+            for q in range(s):
+                count += float(mask[q, i]) * float(mask[q, j])
+                prod = np.outer(left[q, i].astype(np.float64), right[q, j].astype(np.float64)).ravel()
+                pair = (pair.astype(np.float64) + prod).astype(np.float32)
+            total = w["outputBias"].astype(np.float64) + pair.astype(np.float64) @ wo
+            out[i, j] = (total * (1 / (1e-3 + count))).astype(np.float32)
+    return out

@@ -13,7 +13,7 @@ import pytest
 
 import af2cuda
 import oracle
-from helpers import bf16_round, relative_max_error
+from helpers import bf16_round, opm_reference_test_case, opm_reference_test_expected, relative_max_error
 
 pytestmark = pytest.mark.gpu
 
@@ -103,6 +103,21 @@ def test_opm_blocks_are_bit_identical(device):
     for rb in (4, 12, 45):
         blocked = af2cuda.OuterProductMeanGpu(device).run(opm_input(m, mask, w, rowBlockResidues=rb)).output
         assert np.array_equal(blocked, whole), rb
+
+
+def test_opm_on_the_reference_tests_own_case(device):
+    """test/outer-product-mean-reference.gpu.test.ts:104-130 on this build: its spread
+    inputs, masked entries and rowBlockResidues 3 against that test's CPU reference,
+    at the f16-operand bar; the residue blocks of the reference's blocked-run test
+    (test/evoformer-outer-product-mean.gpu.test.ts:75-81) give the same bits."""
+    m, mask, w, row_block = opm_reference_test_case()
+    expected = opm_reference_test_expected(m, mask, w)
+    out = af2cuda.OuterProductMeanGpu(device).run(opm_input(m, mask, w, rowBlockResidues=row_block)).output
+    assert np.isfinite(out).all()
+    assert relative_max_error(out.reshape(expected.shape), expected) <= REL_TOL
+    for rb in (None, 1, 7, 32):
+        again = af2cuda.OuterProductMeanGpu(device).run(opm_input(m, mask, w, rowBlockResidues=rb)).output
+        assert np.array_equal(again, out), rb
 
 
 def test_opm_fully_masked_residues(device):

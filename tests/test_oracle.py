@@ -6,7 +6,8 @@ import pytest
 
 import oracle
 from conftest import GOLDEN_BUNDLES, bundle_path
-from helpers import pack, triangle_case, triangle_weights
+from helpers import (opm_reference_test_case, opm_reference_test_expected, pack, triangle_case,
+                     triangle_weights)
 
 import af2cuda
 
@@ -102,6 +103,24 @@ def test_f16_packing_known_answers():
     assert np.array_equal(oracle.f16_value(oracle.f16_bits(x)), x.astype(np.float16).astype(np.float64))
 
 
+def test_reference_f16_and_int8_known_answers():
+    """The reference's own KATs: numberToFloat16 (test/float16.test.ts:5-30) and the
+    int8 block decode with stored f16 scales (test/dtype.test.ts:6-23)."""
+    cases = [(0.0, 0x0000), (-0.0, 0x8000), (1.0, 0x3C00), (-2.0, 0xC000), (float("inf"), 0x7C00),
+             (float("-inf"), 0xFC00), (0.5, 0x3800), (-4.0, 0xC400),
+             # round to nearest even
+             (-0.748291015625, 0xB9FC), (16.1171875, 0x4C08), (52.859375, 0x529C), (-78.96875, 0xD4F0),
+             (0.000061005353927612305, 0x0400)]
+    for value, bits in cases:
+        assert int(oracle.f16_bits(np.float32(value))) == bits, value
+    assert int(oracle.f16_bits(np.float32("nan"))) & 0x7C00 == 0x7C00
+    assert oracle.f16_value(0x3C00) == 1 and oracle.f16_value(0xC000) == -2
+    assert oracle.f16_value(0x0001) == 2.0 ** -24 and oracle.f16_value(0x7C00) == float("inf")
+    codes = np.array([1, -2, 3, -4, 5], np.int8)
+    scales = np.array([0x3800, 0x4000], np.uint16)  # 0.5, 2.0
+    assert oracle.dequant_q8_block(codes, scales, 4).tolist() == [0.5, -1, 1.5, -2, 10]
+
+
 def test_q8_block_round_trip():
     rng = np.random.default_rng(1)
     w = (rng.standard_normal(1000) / 8).astype(np.float32)
@@ -146,6 +165,20 @@ def test_outer_product_mean_matches_numpy():
     cnt = np.einsum("si,sj->ij", mask, mask)
     ref = (outer @ f[6] + f[7]) / (1e-3 + cnt)[..., None]
     assert np.abs(out - ref).max() < 1e-5 * np.abs(ref).max()
+
+
+def test_outer_product_mean_on_the_reference_tests_own_case():
+    """The reference's OPM test case (spread inputs, every third mask entry zero):
+    the oracle reproduces that test's CPU `reference()` with its f32 stores exactly
+    (the reference holds its GPU path to mean < 2e-5, max < 2e-4 against it)."""
+    m, mask, w, _ = opm_reference_test_case()
+    packed = np.concatenate([np.asarray(w[k], np.float32).ravel() for k in
+                             ("layerNormScale", "layerNormOffset", "leftWeight", "leftBias", "rightWeight",
+                              "rightBias", "outputWeight", "outputBias")])
+    expected = opm_reference_test_expected(m, mask, w)
+    got = oracle.outer_product_mean(m, mask, packed, 32, 16)
+    assert np.array_equal(got, expected)
+    assert np.abs(expected).max() > 0.1  # not a degenerate case
 
 
 @pytest.mark.parametrize("residual", [False, True])
