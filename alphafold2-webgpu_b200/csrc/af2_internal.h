@@ -43,6 +43,7 @@ enum ProfileKernel {
   kProfOpmOuter,
   kProfOpmOutput,
   kProfOpmFused,
+  kProfTransitionLinear,
   kProfCount
 };
 const char *profile_name(int id);
@@ -183,6 +184,13 @@ struct TransitionLayout {
   bool fast_in = false;    // 16-bit x with 16-byte rows: TMA straight into the kernel, LayerNorm in place
   int64_t chunk_rows = 0;  // rows per kernel launch (bounds the normalised copy otherwise)
   size_t off_w1 = 0, off_w2 = 0, off_vec = 0, off_xn = 0, total = 0;
+  // Wide path (channels above 128 or hidden above 1024, e.g. the MSA transition at c_m = 256):
+  // LayerNorm into an f16 copy, then the shared linear kernel twice, the hidden activations in
+  // an HBM scratch per row chunk.
+  bool wide = false;
+  int64_t k1 = 0, n1 = 0, k2 = 0, n2 = 0;  // padded inner dimension / columns of the two GEMMs
+  int64_t hid_pitch = 0;                   // hidden row pitch (elements)
+  size_t off_s1 = 0, off_b1 = 0, off_s2 = 0, off_b2 = 0, off_hid = 0;
 };
 
 TransitionLayout transition_layout(int64_t rows, int64_t c, int64_t h, int x_dtype);

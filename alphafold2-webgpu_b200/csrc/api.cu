@@ -56,7 +56,7 @@ const char *profile_name(int id) {
       "triangle.output",     "transition.prepare",   "transition.normalize", "transition.fused",
       "q8.decode",           "weights.prepare",      "activations.convert",  "linear",
       "opm.normalize",       "opm.project",          "opm.count",         "opm.outer",
-      "opm.output",          "opm.fused"};
+      "opm.output",          "opm.fused",            "transition.linear"};
   return (id >= 0 && id < kProfCount) ? names[id] : nullptr;
 }
 
@@ -192,10 +192,10 @@ af2_status validate_transition(af2_ctx *ctx, const af2_transition_shape *shape, 
   if (!(epsilon > 0) || !std::isfinite(epsilon))
     return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "epsilon must be finite and positive; received " +
                                                    std::to_string(epsilon));
-  if (shape->channels > 128)
-    return fail(ctx, AF2_ERR_UNSUPPORTED, "transition channels above 128 are not supported by the sm_100a kernel");
-  if (shape->hidden_channels > 1024)
-    return fail(ctx, AF2_ERR_UNSUPPORTED, "transition hidden channels above 1024 are not supported");
+  if (shape->channels > 4096)
+    return fail(ctx, AF2_ERR_UNSUPPORTED, "transition channels above 4096 are not supported");
+  if (shape->hidden_channels > 16384)
+    return fail(ctx, AF2_ERR_UNSUPPORTED, "transition hidden channels above 16384 are not supported");
   if (shape->rows > (int64_t(1) << 30))
     return fail(ctx, AF2_ERR_UNSUPPORTED, "transition rows beyond 2^30 are not supported");
   return AF2_OK;

@@ -551,6 +551,35 @@ __global__ void normalize_kernel(const XT *__restrict__ x, int64_t rows, int c, 
   }
 }
 
+// LayerNorm of rows of any width into f16 rows of pitch `pitch` (zero past c),
+// for the wide path.  One warp per row, three passes over the row (sum, squared
+// deviations, normalised store), the later two served from L1/L2.
+template <typename XT>
+__global__ void layer_norm_rows_kernel(const XT *__restrict__ x, int64_t rows, int c, int pitch,
+                                       const float *__restrict__ gamma, const float *__restrict__ beta, float eps,
+                                       __half *__restrict__ xn) {
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const XT *xr = x + row * c;
+  float s = 0.f;
+  for (int ch = lane; ch < c; ch += 32) s += to_f32<XT>(xr[ch]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(kFull, s, o);
+  const float mean = s / static_cast<float>(c);
+  float q = 0.f;
+  for (int ch = lane; ch < c; ch += 32) {
+    const float d = to_f32<XT>(xr[ch]) - mean;
+    q += d * d;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(kFull, q, o);
+  const float rstd = rsqrtf(q / static_cast<float>(c) + eps);
+  __half *out = xn + row * pitch;
+  for (int ch = lane; ch < pitch; ch += 32)
+    out[ch] = __float2half_rn(ch < c ? (to_f32<XT>(xr[ch]) - mean) * rstd * gamma[ch] + beta[ch] : 0.f);
+}
+
 // ---------------------------------------------------------------------------
 // Weight preparation.
 // ---------------------------------------------------------------------------
@@ -757,6 +786,34 @@ TransitionLayout transition_layout(int64_t rows, int64_t c, int64_t h, int x_dty
   L.rows = rows;
   L.c = c;
   L.h = h;
+  if (c > 128 || h > 1024) {
+    // the fused kernel holds C <= 128 channels and H <= 1024 hidden; wider transitions
+    // (the MSA transition: 256 -> 1024 -> 256) take the two-GEMM path
+    L.wide = true;
+    L.k1 = align_up(c, 64);
+    L.n1 = linear_cols_pad(h);
+    L.k2 = align_up(h, 64);
+    L.n2 = linear_cols_pad(c);
+    L.hid_pitch = align_up(h, 8);
+    const int64_t cap = std::max<int64_t>(128, ((int64_t)256 << 20) / (L.hid_pitch * 2) / 128 * 128);
+    L.chunk_rows = std::min(rows, cap);
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+      const size_t at = off;
+      off = align_up(off + bytes, 256);
+      return at;
+    };
+    L.off_w1 = take((size_t)L.k1 * L.n1 * 2);
+    L.off_s1 = take((size_t)L.n1 * 4);
+    L.off_b1 = take((size_t)L.n1 * 4);
+    L.off_w2 = take((size_t)L.k2 * L.n2 * 2);
+    L.off_s2 = take((size_t)L.n2 * 4);
+    L.off_b2 = take((size_t)L.n2 * 4);
+    L.off_xn = take((size_t)L.chunk_rows * L.k1 * 2);
+    L.off_hid = take((size_t)L.chunk_rows * L.hid_pitch * 2);
+    L.total = off;
+    return L;
+  }
   L.cp = c <= 64 ? 64 : 128;
   L.hp = (h + 127) / 128 * 128;
   L.fast_in = x_dtype != AF2_F32 && c % 8 == 0;
@@ -787,9 +844,86 @@ af2_status transition_prepare(af2_ctx *ctx, const TransitionLayout &L, const af2
   return e == cudaSuccess ? AF2_OK : cuda_fail(ctx, e, "transition weight preparation");
 }
 
+// The wide path, per row chunk: LayerNorm -> f16 copy; hidden = relu(xn W1 + b1) (f16, HBM);
+// out (=, +=) hidden W2 + b2 -- the reference's own kernel sequence (transition.ts:264-361),
+// with both GEMMs on the shared tcgen05 linear kernel.
+static af2_status transition_launch_wide(af2_ctx *ctx, const TransitionLayout &L, const void *x, int x_dtype,
+                                         const af2_transition_weights &w, double eps, int residual, void *out,
+                                         int out_dtype, void *workspace, cudaStream_t stream) {
+  uint8_t *ws = static_cast<uint8_t *>(workspace);
+  float *s1 = reinterpret_cast<float *>(ws + L.off_s1), *b1 = reinterpret_cast<float *>(ws + L.off_b1);
+  float *s2 = reinterpret_cast<float *>(ws + L.off_s2), *b2 = reinterpret_cast<float *>(ws + L.off_b2);
+  PrepJob jobs[2];
+  jobs[0] = PrepJob{w.first_weight, L.c, L.h, L.k1, L.n1, 1.f, ws + L.off_w1, s1};
+  jobs[1] = PrepJob{w.second_weight, L.h, L.c, L.k2, L.n2, 1.f, ws + L.off_w2, s2};
+  VectorSegments v{};
+  v.add(w.first_bias, L.h, L.n1, b1);
+  v.add(w.second_bias, L.c, L.n2, b2);
+  af2_status st;
+  if ((st = prepare_matrices(ctx, jobs, 2, stream)) != AF2_OK || (st = pad_vectors(ctx, v, stream)) != AF2_OK)
+    return st;
+  const size_t xb = x_dtype == AF2_F32 ? 4 : 2, ob = out_dtype == AF2_F32 ? 4 : 2;
+  __half *xn = reinterpret_cast<__half *>(ws + L.off_xn), *hid = reinterpret_cast<__half *>(ws + L.off_hid);
+  for (int64_t r0 = 0; r0 < L.rows; r0 += L.chunk_rows) {
+    const int64_t rows = std::min(L.chunk_rows, L.rows - r0);
+    const void *xsrc = static_cast<const uint8_t *>(x) + r0 * L.c * xb;
+    {
+      const int warps = 8;
+      const unsigned blocks = (unsigned)((rows + warps - 1) / warps);
+      LaunchScope scope(ctx, stream, kProfTransitionNormalize);
+      const int c = (int)L.c, pitch = (int)L.k1;
+      const float e = static_cast<float>(eps);
+      if (x_dtype == AF2_F32)
+        layer_norm_rows_kernel<float><<<blocks, warps * 32, 0, stream>>>(
+            static_cast<const float *>(xsrc), rows, c, pitch, w.layer_norm_scale, w.layer_norm_offset, e, xn);
+      else if (x_dtype == AF2_F16)
+        layer_norm_rows_kernel<__half><<<blocks, warps * 32, 0, stream>>>(
+            static_cast<const __half *>(xsrc), rows, c, pitch, w.layer_norm_scale, w.layer_norm_offset, e, xn);
+      else
+        layer_norm_rows_kernel<__nv_bfloat16><<<blocks, warps * 32, 0, stream>>>(
+            static_cast<const __nv_bfloat16 *>(xsrc), rows, c, pitch, w.layer_norm_scale, w.layer_norm_offset, e,
+            xn);
+      const cudaError_t err = cudaGetLastError();
+      if (err != cudaSuccess) return cuda_fail(ctx, err, "transition normalisation");
+    }
+    LinearOperands g1;
+    g1.a = xn;
+    g1.lda = L.k1;
+    g1.w = ws + L.off_w1;
+    g1.scale = s1;
+    g1.bias = b1;
+    g1.rows = rows;
+    g1.inner = L.c;
+    g1.cols = L.h;
+    g1.out = hid;
+    g1.ldo = L.hid_pitch;
+    g1.out_dtype = AF2_F16;
+    g1.relu = 1;
+    g1.prof = kProfTransitionLinear;
+    if ((st = linear_launch(ctx, g1, stream)) != AF2_OK) return st;
+    LinearOperands g2;
+    g2.a = hid;
+    g2.lda = L.hid_pitch;
+    g2.w = ws + L.off_w2;
+    g2.scale = s2;
+    g2.bias = b2;
+    g2.rows = rows;
+    g2.inner = L.h;
+    g2.cols = L.c;
+    g2.out = static_cast<uint8_t *>(out) + r0 * L.c * ob;
+    g2.ldo = L.c;
+    g2.out_dtype = out_dtype;
+    g2.residual = residual;
+    g2.prof = kProfTransitionLinear;
+    if ((st = linear_launch(ctx, g2, stream)) != AF2_OK) return st;
+  }
+  return AF2_OK;
+}
+
 af2_status transition_launch(af2_ctx *ctx, const TransitionLayout &L, const void *x, int x_dtype,
                              const af2_transition_weights &w, double eps, int residual, void *out, int out_dtype,
                              void *workspace, cudaStream_t stream) {
+  if (L.wide) return transition_launch_wide(ctx, L, x, x_dtype, w, eps, residual, out, out_dtype, workspace, stream);
   af2_status st = transition_prepare(ctx, L, w, workspace, stream);
   if (st != AF2_OK) return st;
   uint8_t *ws = static_cast<uint8_t *>(workspace);

@@ -1479,16 +1479,23 @@ af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L,
     __half *x_all = reinterpret_cast<__half *>(ws + L.off_x_all);
     const size_t xblock = (size_t)hq * L.x_hs * sizeof(__half);
     if (direct) {
-      // one destination row block at a time, the peers' first: each block leaves while the
-      // next is contracted, and this rank's own block (written in place) comes last
-      for (int64_t q = 1; q <= R; ++q) {
-        const int d = static_cast<int>((me + q) % R);
-        __half *xb = reinterpret_cast<__half *>(reinterpret_cast<uint8_t *>(x) + (size_t)d * xblock);
-        if ((st = contract((int64_t)d * rows, rows, rows, xb, d == me ? 0 : -1)) != AF2_OK) return st;
-        if (d != me &&
-            (st = shard->send(ctx, xb, reinterpret_cast<uint8_t *>(x_all) + (size_t)me * xblock, xblock, d, stream)) !=
-                AF2_OK)
-          return st;
+      // one aligned group of destination row blocks at a time (a group spans at least one
+      // 256-row pair tile, so blocks of 64 or 128 rows are not contracted as half-empty
+      // tiles), the groups of peers first: each group's blocks leave while the next group is
+      // contracted, and the group holding this rank's own block (written in place) comes last
+      const int64_t per = std::min<int64_t>(R, (CT_PAIR_M + rows - 1) / rows), groups = R / per;
+      for (int64_t q = 1; q <= groups; ++q) {
+        const int64_t d0 = ((me / per + q) % groups) * per;
+        __half *xb = reinterpret_cast<__half *>(reinterpret_cast<uint8_t *>(x) + (size_t)d0 * xblock);
+        const int own = (me >= d0 && me < d0 + per) ? static_cast<int>(me - d0) : -1;
+        if ((st = contract(d0 * rows, per * rows, rows, xb, own)) != AF2_OK) return st;
+        for (int64_t d = d0; d < d0 + per; ++d) {
+          if (d == me) continue;
+          const uint8_t *src = reinterpret_cast<const uint8_t *>(x) + (size_t)d * xblock;
+          if ((st = shard->send(ctx, src, reinterpret_cast<uint8_t *>(x_all) + (size_t)me * xblock, xblock,
+                                static_cast<int>(d), stream)) != AF2_OK)
+            return st;
+        }
       }
       if ((st = shard->close(ctx, stream)) != AF2_OK) return st;
     } else if ((st = contract(0, L.n, rows, x, me)) != AF2_OK ||

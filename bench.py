@@ -58,7 +58,8 @@ METRIC = "Evoformer pair-GEMM TFLOP/s & ms/block at N=1024; % of B200 bf16 TC pe
 KERNEL_DRAM_BYTES = {"triangle.contract": 776_628_736, "opm.fused": 599_897_344}
 KERNELS = ("weights.prepare", "triangle.prepare", "triangle.relayout", "triangle.project", "triangle.contract",
            "triangle.output", "opm.normalize", "opm.project", "opm.count", "opm.outer", "opm.output",
-           "opm.fused", "transition.prepare", "transition.fused")
+           "opm.fused", "transition.prepare", "transition.normalize", "transition.fused", "transition.linear",
+           "linear", "activations.convert")
 
 
 def triangle_flops(n: int, cz: int = CZ, ch: int = CH) -> float:
@@ -506,6 +507,9 @@ WORKLOADS = {
                 "transition with mixed-q8 weights), bf16 pair updated in place",
     "multimer": "config 5: N=2048 (4 chains x 512, mask 1 inside the four diagonal chain blocks): triangle out + "
                 "in and pair transition on a bf16 pair [2048,2048,128] updated in place, rows sharded over the ranks",
+    "msa_transition": "next-row widening: the MSA transition of the N=1024 block, bf16 MSA rows [512*1024, 256] "
+                      "updated in place, 256->1024 ReLU ->256 with symmetric int8 weights and f32 per-output-"
+                      "channel scales",
 }
 
 
@@ -544,7 +548,7 @@ def run_workload(args) -> None:
     gen = torch.Generator(device="cuda").manual_seed(rank)
     tw = transition_weights(rng)
 
-    def transition_tensors():
+    def transition_tensors(tw=tw):
         return {"layerNormScale": torch.from_numpy(tw["ln"][0]).cuda(),
                 "layerNormOffset": torch.from_numpy(tw["ln"][1]).cuda(),
                 "firstWeight": af2cuda.Q8Matrix(torch.from_numpy(tw["w1"][0]).cuda(),
@@ -574,6 +578,14 @@ def run_workload(args) -> None:
 
         def step():
             af2cuda.encode_transition_tensors(dev, x, tws, out=out, residual=False, stream=sh)
+    elif wl == "msa_transition":
+        rows, c, h = S_MSA * N, CM, 4 * CM
+        x = torch.randn(rows, c, device="cuda", generator=gen).to(torch.bfloat16)
+        tws = transition_tensors(transition_weights(rng, c, h))
+        flops = 4.0 * rows * c * h
+
+        def step():
+            af2cuda.encode_transition_tensors(dev, x, tws, residual=True, stream=sh)
     elif wl == "opm":
         n, s = 256, 512
         msa = torch.randn(s, n, CM, device="cuda", generator=gen)

@@ -140,8 +140,12 @@ def test_transition_weight_count_and_validation():
     assert _tcheck(5, 7, 6, count=3) == (_lib.AF2_ERR_INVALID_ARGUMENT, "packed weights have 3 values; expected 111")
     for eps in (0.0, -1.0, float("inf"), float("nan")):
         assert _tcheck(5, 7, 6, eps=eps)[0] == _lib.AF2_ERR_INVALID_ARGUMENT
-    st, msg = _tcheck(5, 256, 1024)
-    assert st == _lib.AF2_ERR_UNSUPPORTED and "above 128" in msg
+    # the MSA transition (c_m 256 -> 1024) takes the two-GEMM path; the limits lie beyond it
+    assert _tcheck(5, 256, 1024) == (0, "")
+    st, msg = _tcheck(5, 8192, 1024)
+    assert st == _lib.AF2_ERR_UNSUPPORTED and "above 4096" in msg
+    st, msg = _tcheck(5, 64, 32768)
+    assert st == _lib.AF2_ERR_UNSUPPORTED and "above 16384" in msg
 
 
 def test_transition_python_validation_and_packing():
@@ -167,6 +171,15 @@ def test_transition_workspace_is_small():
     small = af2cuda.transition_workspace_bytes(65536, 128, 512)
     big = af2cuda.transition_workspace_bytes(4 * 65536, 128, 512)
     assert small == big and small < 32 << 20
+
+
+def test_wide_transition_workspace_is_bounded_per_chunk():
+    # channels above 128: the hidden activations go through HBM one row chunk at a time,
+    # so the scratch stops growing once the rows exceed one chunk (about 256 MiB of hidden)
+    one = af2cuda.transition_workspace_bytes(4096, 256, 1024)
+    many = af2cuda.transition_workspace_bytes(512 * 1024, 256, 1024)
+    more = af2cuda.transition_workspace_bytes(4 * 512 * 1024, 256, 1024)
+    assert one < many == more < 400 << 20
 
 
 def test_opm_weight_count_and_validation():
