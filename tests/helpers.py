@@ -120,3 +120,26 @@ def opm_reference_test_expected(m, mask, w, c: int = 32) -> np.ndarray:
             total = w["outputBias"].astype(np.float64) + pair.astype(np.float64) @ wo
             out[i, j] = (total * (1 / (1e-3 + count))).astype(np.float32)
     return out
+
+
+def opm_f16_operand_model(m, mask, w, c: int = 32) -> np.ndarray:
+    """The OPM with this build's rounding points for an f32 MSA, in f64 otherwise:
+    LN(m)*gamma + beta, the projection weights, left/right (masked, biased), the outer
+    products and W_o are rounded to f16 (the kernels' power-of-two scalings are exact
+    and left out); sums are exact.  Used to show that a GPU result's distance from the
+    reference is the f16 operand rounding and nothing else."""
+    s, n, cm = m.shape
+    cz = w["outputBias"].size
+
+    def f16(a):
+        return np.asarray(a, np.float64).astype(np.float16).astype(np.float64)
+
+    x = m.astype(np.float64)
+    xn = f16((x - x.mean(-1, keepdims=True)) / np.sqrt(x.var(-1, keepdims=True) + 1e-5) * w["layerNormScale"]
+             + w["layerNormOffset"])
+    msk = mask.astype(np.float64)[..., None]
+    left = f16((xn @ f16(w["leftWeight"].reshape(cm, c)) + w["leftBias"]) * msk)
+    right = f16((xn @ f16(w["rightWeight"].reshape(cm, c)) + w["rightBias"]) * msk)
+    outer = f16(np.einsum("sia,sjb->ijab", left, right).reshape(n, n, c * c))
+    cnt = np.einsum("si,sj->ij", mask.astype(np.float64), mask.astype(np.float64))
+    return (outer @ f16(w["outputWeight"].reshape(c * c, cz)) + w["outputBias"]) / (1e-3 + cnt)[..., None]
