@@ -14,8 +14,9 @@
 //
 // Kernel: one CTA per SM, 128-row tiles of A times BN-column tiles of W (BN
 // <= 256), K in 64-wide blocks through a 4-deep TMA ring; warp 0 issues TMA,
-// warp 1 the tcgen05 MMAs into one of two TMEM accumulators, warps 2-5 drain
-// the other accumulator (one TMEM lane = one output row per thread).
+// warp 1 the tcgen05 MMAs into one of two TMEM accumulators, warps 2-9 drain
+// the other accumulator (one TMEM lane = one output row per thread; two warps
+// per lane quarter, taking alternate 32-column chunks).
 #include <algorithm>
 #include <string>
 
@@ -25,7 +26,9 @@
 namespace af2 {
 namespace gemm {
 
-constexpr int BM = 128, BK = 64, STAGES = 4, THREADS = 192;
+constexpr int BM = 128, BK = 64, STAGES = 4;
+constexpr int EPI_WARPS = 8;  // two per TMEM lane quarter
+constexpr int THREADS = 64 + 32 * EPI_WARPS;
 constexpr uint32_t A_BYTES = BM * 128;
 
 struct LinearArgs {
@@ -70,7 +73,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(acc_full(b), 1);
-      mbar_init(acc_empty(b), 4);
+      mbar_init(acc_empty(b), EPI_WARPS);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -140,8 +143,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     umma_commit(drain);
     mbar_wait_drain(drain, 0, p.err);
   } else {
-    // ---- epilogue: one output row per thread ----
-    const int q = warp & 3;
+    // ---- epilogue: one output row per thread, alternate column chunks per warp of a quarter ----
+    const int q = warp & 3, half = (warp - 2) >> 2;
     const int row = q * 32 + lane;
     int tile_it = 0;
     for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x, ++tile_it) {
@@ -156,7 +159,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       float rs = 1.f;
       if (MODE == kModeLinear && p.row_scale && row_ok) rs = p.row_scale[m];
       if (MODE == kModeOpmProjection && row_ok) rs = p.row_mask[m];
-      for (int chunk = 0; chunk < p.bn / 32; ++chunk) {
+      for (int chunk = half; chunk < p.bn / 32; chunk += 2) {
         uint32_t v[32];
         tmem_ld32(taddr + chunk * 32, v);
         tmem_ld_wait();
