@@ -18,6 +18,8 @@
 // the other accumulator (one TMEM lane = one output row per thread; two warps
 // per lane quarter, taking alternate 32-column chunks).
 #include <algorithm>
+#include <cstring>
+#include <type_traits>
 #include <string>
 
 #include "af2_device.cuh"
@@ -42,15 +44,19 @@ struct LinearArgs {
   int cols, half_cols, k_blocks, tiles_m, tiles_n, total_tiles, bn;
   int relu, residual;
   int vector_out;  // out rows are 16-byte aligned: whole 32-column chunks use vector access
+  int tma_out;     // f16 output, no residual: each warp stages 32 x 32 blocks and stores them by TMA
   unsigned int *err;
 };
+
+// Per epilogue warp: one 32-row x 32-column f16 staging block for the TMA-stored output.
+constexpr uint32_t OUT_STAGE_BYTES = 32 * 64;
 
 enum { kModeLinear = 0, kModeOpmProjection = 1 };
 
 template <typename OT, int MODE>
 __global__ void __launch_bounds__(THREADS, 1)
     linear_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap bmap,
-                  const LinearArgs p) {
+                  const __grid_constant__ CUtensorMap omap, const LinearArgs p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = align1024(smem_raw);
   const uint32_t sbase = smem_u32(smem);
@@ -146,6 +152,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ---- epilogue: one output row per thread, alternate column chunks per warp of a quarter ----
     const int q = warp & 3, half = (warp - 2) >> 2;
     const int row = q * 32 + lane;
+    // the staged path exists for f16 outputs only (the host sets tma_out accordingly)
+    const bool staged = MODE == kModeLinear && std::is_same<OT, __half>::value && p.tma_out;
+    const uint32_t stage_off = OFF_BAR + 256 + (warp - 2) * OUT_STAGE_BYTES;
+    bool store_pending = false;
     int tile_it = 0;
     for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x, ++tile_it) {
       const int mi = t / p.tiles_n, ni = t - mi * p.tiles_n;
@@ -164,6 +174,47 @@ __global__ void __launch_bounds__(THREADS, 1)
         tmem_ld32(taddr + chunk * 32, v);
         tmem_ld_wait();
         const int c0 = n0 + chunk * 32;
+        if (staged) {
+          // rows past p.rows and columns past p.cols are staged too and the TMA store drops them;
+          // a block that starts past the last row or column is not stored at all
+          if (c0 >= p.cols || static_cast<int64_t>(mi) * BM + q * 32 >= p.rows) continue;
+          uint32_t pk[16];
+          const float4 *sc = reinterpret_cast<const float4 *>(p.scale + c0);
+          const float4 *bi = reinterpret_cast<const float4 *>(p.bias + c0);
+#pragma unroll
+          for (int i4 = 0; i4 < 8; ++i4) {
+            const float4 s4 = __ldg(sc + i4), b4 = __ldg(bi + i4);
+            float y0 = fmaf(__uint_as_float(v[4 * i4 + 0]), s4.x, b4.x) * rs;
+            float y1 = fmaf(__uint_as_float(v[4 * i4 + 1]), s4.y, b4.y) * rs;
+            float y2 = fmaf(__uint_as_float(v[4 * i4 + 2]), s4.z, b4.z) * rs;
+            float y3 = fmaf(__uint_as_float(v[4 * i4 + 3]), s4.w, b4.w) * rs;
+            if (p.relu) {
+              y0 = fmaxf(y0, 0.f), y1 = fmaxf(y1, 0.f), y2 = fmaxf(y2, 0.f), y3 = fmaxf(y3, 0.f);
+            }
+            pk[2 * i4] = pack_half2(y0, y1);
+            pk[2 * i4 + 1] = pack_half2(y2, y3);
+          }
+          if (lane == 0 && store_pending) bulk_wait_read_all();  // the last store has read the block
+          __syncwarp();
+          // row `lane` of the block is 64 bytes; its four 16-byte pieces are written in an order
+          // rotated by the lane, so each store instruction covers every bank once per 128 bytes
+          uint8_t *stage_row = smem + stage_off + lane * 64;
+          const uint4 q0 = make_uint4(pk[0], pk[1], pk[2], pk[3]), q1 = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+          const uint4 q2 = make_uint4(pk[8], pk[9], pk[10], pk[11]), q3 = make_uint4(pk[12], pk[13], pk[14], pk[15]);
+#pragma unroll
+          for (int w = 0; w < 4; ++w) {
+            const int pc = (w + lane) & 3;
+            *reinterpret_cast<uint4 *>(stage_row + pc * 16) = pc == 0 ? q0 : pc == 1 ? q1 : pc == 2 ? q2 : q3;
+          }
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_3d(&omap, sbase + stage_off, c0, mi * BM + q * 32, 0);
+            bulk_commit();
+            store_pending = true;
+          }
+          continue;
+        }
         if (!row_ok || c0 >= p.cols) continue;
         float y[32];
         const float4 *sc = reinterpret_cast<const float4 *>(p.scale + c0);
@@ -209,6 +260,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(acc_empty(buf));
     }
+    if (lane == 0 && store_pending) bulk_wait_all();
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -420,15 +473,15 @@ af2_status convert_rows_f16(af2_ctx *ctx, const void *src, int dtype, int64_t ro
 namespace {
 
 template <typename OT, int MODE>
-af2_status launch_linear_t(af2_ctx *ctx, const CUtensorMap &amap, const CUtensorMap &bmap, const LinearArgs &a,
-                           int prof, cudaStream_t stream) {
+af2_status launch_linear_t(af2_ctx *ctx, const CUtensorMap &amap, const CUtensorMap &bmap, const CUtensorMap &omap,
+                           const LinearArgs &a, int prof, cudaStream_t stream) {
   auto kernel = linear_kernel<OT, MODE>;
-  const uint32_t smem = STAGES * (A_BYTES + a.bn * 128u) + 256 + 1024;
+  const uint32_t smem = STAGES * (A_BYTES + a.bn * 128u) + 256 + EPI_WARPS * OUT_STAGE_BYTES + 1024;
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return cuda_fail(ctx, e, "linear kernel attributes");
   const int grid = std::min(a.total_tiles, ctx->sm_count);
   LaunchScope scope(ctx, stream, prof);
-  kernel<<<grid, THREADS, smem, stream>>>(amap, bmap, a);
+  kernel<<<grid, THREADS, smem, stream>>>(amap, bmap, omap, a);
   e = cudaGetLastError();
   return e == cudaSuccess ? AF2_OK : cuda_fail(ctx, e, "linear kernel launch");
 }
@@ -473,10 +526,19 @@ af2_status linear_launch(af2_ctx *ctx, const LinearOperands &op, cudaStream_t st
     a.vector_out = !op.opm_projection && reinterpret_cast<uintptr_t>(op.out) % 16 == 0 && (op.ldo * ob) % 16 == 0;
   }
   a.err = ctx->err_word;
-  if (op.opm_projection) return launch_linear_t<__half, kModeOpmProjection>(ctx, amap, bmap, a, op.prof, stream);
-  if (op.out_dtype == AF2_F16) return launch_linear_t<__half, kModeLinear>(ctx, amap, bmap, a, op.prof, stream);
-  if (op.out_dtype == AF2_BF16) return launch_linear_t<__nv_bfloat16, kModeLinear>(ctx, amap, bmap, a, op.prof, stream);
-  return launch_linear_t<float, kModeLinear>(ctx, amap, bmap, a, op.prof, stream);
+  // f16 outputs without a residual leave through staged TMA stores: [rows][ldo], one box = 32 x 32
+  CUtensorMap omap;
+  std::memset(&omap, 0, sizeof omap);
+  a.tma_out = !op.opm_projection && op.out_dtype == AF2_F16 && !op.residual && a.vector_out;
+  if (a.tma_out && !encode_map_3d(&omap, f16map(), op.out, op.cols, op.rows, 1, op.ldo * 2,
+                                  (uint64_t)op.rows * op.ldo * 2, 32, 32, 1, CU_TENSOR_MAP_SWIZZLE_NONE))
+    return fail(ctx, AF2_ERR_CUDA, "cuTensorMapEncodeTiled failed for a linear layer's output");
+  if (op.opm_projection)
+    return launch_linear_t<__half, kModeOpmProjection>(ctx, amap, bmap, omap, a, op.prof, stream);
+  if (op.out_dtype == AF2_F16) return launch_linear_t<__half, kModeLinear>(ctx, amap, bmap, omap, a, op.prof, stream);
+  if (op.out_dtype == AF2_BF16)
+    return launch_linear_t<__nv_bfloat16, kModeLinear>(ctx, amap, bmap, omap, a, op.prof, stream);
+  return launch_linear_t<float, kModeLinear>(ctx, amap, bmap, omap, a, op.prof, stream);
 }
 
 }  // namespace af2
