@@ -208,3 +208,35 @@ def test_linear_bf16_input(device):
     out = af2cuda.linear_tensors(device, torch.from_numpy(a).to("cuda", torch.bfloat16), torch.from_numpy(w).cuda())
     device.sync()
     assert relative_max_error(out.cpu().numpy(), _linear_reference(a, w, None, False)) <= REL_TOL
+
+
+def _gemm_test_values(count, seed):
+    """values() of test/gemm-half-precision.gpu.test.ts:44-51: a 32-bit linear congruential
+    generator (multiplier 1664525, increment 1013904223), each value state / 2^32 - 0.5, as f32."""
+    out = np.empty(count, np.float64)
+    state = seed & 0xFFFFFFFF
+    for i in range(count):
+        state = (state * 1664525 + 1013904223) & 0xFFFFFFFF
+        out[i] = state / 2.0 ** 32 - 0.5
+    return out.astype(np.float32)
+
+
+@pytest.mark.parametrize("inner", [256, 1024])
+@pytest.mark.parametrize("seeds", [(0x1234567, 0x89ABCDEF, 0x2468ACE), (0x13579BD, 0x2468ACE, 0x1234567)])
+def test_linear_on_the_reference_gemm_test_cases(device, inner, seeds):
+    """The shared projection (createLinearShader) on the cases of
+    test/gemm-half-precision.gpu.test.ts:200-236: GEMM_TILE_ROWS + 17 = 81 rows, 132
+    columns, both contraction depths the model runs, deterministic inputs, against A W + b
+    summed in double precision; the reference's bar for f16 operands with f32 sums is a
+    worst error below 2e-3 of the largest output (tolerance(), :35-41)."""
+    import torch
+    rows, cols = 64 + 17, 132
+    a = _gemm_test_values(rows * inner, seeds[0]).reshape(rows, inner)
+    w = _gemm_test_values(inner * cols, seeds[1]).reshape(inner, cols)
+    b = _gemm_test_values(cols, seeds[2])
+    expected = a.astype(np.float64) @ w.astype(np.float64) + b
+    out = af2cuda.linear_tensors(device, torch.from_numpy(a).cuda(), torch.from_numpy(w).cuda(),
+                                 torch.from_numpy(b).cuda())
+    device.sync()
+    got = out.cpu().numpy()
+    assert np.abs(got - expected).max() / np.abs(expected).max() < 2e-3
