@@ -480,7 +480,8 @@ def run_ours(args) -> None:
                                            "transition": transition_flops(N) / 1e9},
                        "l2": "inputs larger than L2 (pair 268 MB, MSA 268 MB, bf16), no flush",
                        "parallelism": (f"pair rows sharded x{world}: triangle contraction sharded by hidden "
-                                       "channel between two NCCL all-to-alls, OPM right operand all-gathered")
+                                       "channel between two all-to-alls (copy-engine copies into the peers' "
+                                       "IPC-mapped scratch, NCCL barriers), OPM right operand all-gathered")
                        if world > 1
                        else "single GPU"},
             "ms_per_block": ms / args.steps,
