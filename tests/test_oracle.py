@@ -181,6 +181,33 @@ def test_outer_product_mean_on_the_reference_tests_own_case():
     assert np.abs(expected).max() > 0.1  # not a degenerate case
 
 
+def test_projection_first_ordering_matches_the_oracle():
+    """The reference's legacy projection-first OPM (OUTER_PRODUCT_MEAN_INTERMEDIATE_SHADER /
+    OUTPUT_SHADER, src/evoformer/outer-product-mean.ts:260-311): per sequence and residue i,
+    t[s,i,b,z] = sum_a left[s,i,a] W_o[a*c+b, z], then out[i,j,z] = (b_o[z] + sum_{s,b}
+    t[s,i,b,z] right[s,j,b]) / (eps + count).  It is the same sum in another order, so it
+    must agree with the contract-first oracle to rounding."""
+    rng = np.random.default_rng(11)
+    s, n, cm, c, cz = 7, 6, 10, 32, 12
+    m = rng.standard_normal((s, n, cm)).astype(np.float32)
+    mask = (rng.random((s, n)) < 0.8).astype(np.float32)
+    parts = [1 + 0.1 * rng.standard_normal(cm), 0.1 * rng.standard_normal(cm),
+             rng.standard_normal((cm, c)) / np.sqrt(cm), 0.1 * rng.standard_normal(c),
+             rng.standard_normal((cm, c)) / np.sqrt(cm), 0.1 * rng.standard_normal(c),
+             rng.standard_normal((c * c, cz)) / c, 0.1 * rng.standard_normal(cz)]
+    packed = np.concatenate([np.asarray(p, np.float32).ravel() for p in parts])
+    f = [np.asarray(p, np.float32).astype(np.float64) for p in parts]
+    x = m.astype(np.float64)
+    xn = (x - x.mean(-1, keepdims=True)) / np.sqrt(x.var(-1, keepdims=True) + 1e-5) * f[0] + f[1]
+    left = (xn @ f[2] + f[3]) * mask[..., None]
+    right = (xn @ f[4] + f[5]) * mask[..., None]
+    t = np.einsum("sia,abz->sibz", left, f[6].reshape(c, c, cz))
+    cnt = np.einsum("si,sj->ij", mask, mask)
+    projection_first = (f[7] + np.einsum("sibz,sjb->ijz", t, right)) / (1e-3 + cnt)[..., None]
+    got = oracle.outer_product_mean(m, mask, packed, c, cz)
+    assert np.abs(got - projection_first).max() < 1e-5 * np.abs(projection_first).max()
+
+
 @pytest.mark.parametrize("residual", [False, True])
 def test_transition_matches_numpy(residual):
     rng = np.random.default_rng(6)
