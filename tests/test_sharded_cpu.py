@@ -1,4 +1,4 @@
-"""CPU tests (gloo, two and four ranks) of the row-sharded pair's host-side
+"""CPU tests (gloo, two, four and eight ranks) of the row-sharded pair's host-side
 algorithm for the triangle products: every rank projects its own pair rows in
 R channel groups, an all-to-all hands every rank its channel group of all rows,
 each rank contracts its channels over the whole N x N (the incoming product's k
@@ -81,7 +81,7 @@ def _worker(rank, nranks, port, result):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("nranks", [2, 4])
+@pytest.mark.parametrize("nranks", [2, 4, 8])
 def test_channel_sharded_triangle_algorithm_on_gloo(nranks):
     ctx = mp.get_context("spawn")
     result = ctx.Array("i", nranks)
