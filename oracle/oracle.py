@@ -199,3 +199,66 @@ def error_metrics(actual, expected) -> dict:
     out = np.zeros(3, np.float64)
     lib().af2o_error_metrics(_ptr(a, ctypes.c_float), _ptr(e, ctypes.c_float), a.size, _ptr(out, ctypes.c_double))
     return {"meanAbsoluteError": out[0], "maxAbsoluteError": out[1], "rootMeanSquareError": out[2]}
+
+
+def attention(x, mask, weights: dict, batch: int, queries: int, heads: int, transpose: bool = False,
+              pair_bias: dict | None = None, eps: float = 1e-5, residual=None) -> np.ndarray:
+    """Gated multi-head attention as AttentionGpu.run computes it (src/evoformer/attention.ts:1334-1453),
+    restated in f64 numpy; the reference has no CPU implementation of it, so this follows its kernels.
+
+    x: [batch * queries, channels] rows (transpose=False: row b*Q+q; transpose=True: row q*B+b,
+    the column / ending-node view, source_row :300-306); mask: [batch * queries] in the same
+    layout (mask_index :428-433).  weights: queryNormScale/Offset [C], query/key/value/gating
+    Weight [C, H*d] ([in, out], column h*d+i), gatingBias [H*d], outputWeight [H*d, C],
+    outputBias [C].  pair_bias: None; {"source": "normalized-input", "projectionWeight": [C, H]}
+    (bias[h, q, k] from the normalized row (q, k) of this same input, which needs batch ==
+    queries: triangle attention); or {"source": "separate", "activations": [Q*Q, Cp],
+    "layerNormScale", "layerNormOffset", "projectionWeight": [Cp, H]}.
+    Steps: LayerNorm (:266-336); q = xn Wq / sqrt(d), k, v, gate = sigmoid(xn Wg + bg)
+    (:497-566); logits = q.k + 1e9 (mask[k] - 1) + bias, clamped to +-1e8, softmax over keys,
+    times the gate (ATTENTION_FLASH_SHADER :663-731); out = weighted Wo + bo, written back in the
+    input's row layout, plus `residual` when given (:1261-1314)."""
+    x = np.asarray(x, np.float64)
+    rows, c = x.shape
+    B, Q, H = batch, queries, heads
+    d = c // H
+    assert rows == B * Q and d * H == c
+    w = {k: np.asarray(v, np.float64) for k, v in weights.items()}
+    order = np.arange(rows).reshape(B, Q) if not transpose else np.arange(rows).reshape(Q, B).T
+    xs = x[order.ravel()]  # rows in (b, q) order
+    mk = np.asarray(mask, np.float64).ravel()[order.ravel()].reshape(B, Q)
+
+    def layer_norm(t, scale, offset):
+        mean = t.mean(-1, keepdims=True)
+        var = ((t - mean) ** 2).mean(-1, keepdims=True)
+        return (t - mean) / np.sqrt(var + eps) * scale + offset
+
+    xn = layer_norm(xs, w["queryNormScale"], w["queryNormOffset"])
+    q = (xn @ w["queryWeight"].reshape(c, H * d)).reshape(B, Q, H, d) / np.sqrt(d)
+    k = (xn @ w["keyWeight"].reshape(c, H * d)).reshape(B, Q, H, d)
+    v = (xn @ w["valueWeight"].reshape(c, H * d)).reshape(B, Q, H, d)
+    g = 1 / (1 + np.exp(-(xn @ w["gatingWeight"].reshape(c, H * d) + w["gatingBias"]))).reshape(B, Q, H, d)
+    logits = np.einsum("bqhd,bkhd->bhqk", q, k) + (1e9 * (mk - 1))[:, None, None, :]
+    if pair_bias is not None:
+        if pair_bias["source"] == "separate":
+            pa = np.asarray(pair_bias["activations"], np.float64)
+            pn = layer_norm(pa, np.asarray(pair_bias["layerNormScale"], np.float64),
+                            np.asarray(pair_bias["layerNormOffset"], np.float64))
+            bias = (pn @ np.asarray(pair_bias["projectionWeight"], np.float64).reshape(pa.shape[1], H))
+            bias = bias.reshape(Q, Q, H).transpose(2, 0, 1)[None]  # [1, H, q, k]
+        else:
+            assert B == Q, "a bias from the normalized input needs batch == queries"
+            bias = (xn @ np.asarray(pair_bias["projectionWeight"], np.float64).reshape(c, H)).reshape(B, Q, H)
+            bias = bias.transpose(2, 0, 1)[None]  # row index b of the source becomes the query index
+        logits = logits + bias
+    logits = np.clip(logits, -1e8, 1e8)
+    logits -= logits.max(-1, keepdims=True)
+    p = np.exp(logits)
+    p /= p.sum(-1, keepdims=True)
+    weighted = np.einsum("bhqk,bkhd->bqhd", p, v) * g
+    out = weighted.reshape(rows, H * d) @ w["outputWeight"].reshape(H * d, c) + w["outputBias"]
+    result = np.empty_like(out)
+    result[order.ravel()] = out
+    if residual is not None:
+        result = result + np.asarray(residual, np.float64)
+    return result
