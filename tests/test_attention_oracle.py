@@ -20,7 +20,7 @@ def _weights(rng, c, h):
                 outputWeight=rng.standard_normal((c, c)) / math.sqrt(c), outputBias=0.1 * rng.standard_normal(c))
 
 
-def _loops(x, mask, w, B, Q, H, transpose, bias_w):
+def _loops(x, mask, w, B, Q, H, transpose, bias_w, bias_fn=None):
     """Kernel by kernel with scalar loops: LayerNorm per row, the four projections, the
     online-softmax flash loop with the 1e9 mask bias, the +-1e8 clamp and the gate, then
     the output projection written back to the source row."""
@@ -58,6 +58,8 @@ def _loops(x, mask, w, B, Q, H, transpose, bias_w):
                     logit = sum(qv[i] * kv[i] for i in range(d)) + 1e9 * (mask[src(b, k)] - 1)
                     if bias_w is not None:
                         logit += sum(xn[q, k][i] * bias_w[i][h] for i in range(c))
+                    if bias_fn is not None:
+                        logit += bias_fn(h, q, k)
                     logit = min(max(logit, -1e8), 1e8)
                     new_max = max(run_max, logit)
                     scale, e = math.exp(run_max - new_max), math.exp(logit - new_max)
@@ -120,3 +122,29 @@ def test_fully_masked_row_attends_uniformly():
     g = 1 / (1 + np.exp(-(xn @ w["gatingWeight"] + w["gatingBias"])))
     want = (v.mean(0, keepdims=True) * g) @ w["outputWeight"] + w["outputBias"]
     np.testing.assert_allclose(got[:Q], want, rtol=1e-10, atol=1e-10)
+
+
+def test_separate_pair_bias_matches_the_kernel_loops():
+    """MSA row attention's bias: the pair [Q*Q, Cp] normalised with its own LayerNorm and
+    projected to one value per head (createAttentionPairBiasShader, attention.ts:631-661),
+    read at (query, key)."""
+    rng = np.random.default_rng(9)
+    B, Q, c, H, cp = 3, 4, 8, 2, 6
+    w = _weights(rng, c, H)
+    pair = rng.standard_normal((Q * Q, cp))
+    ln_s, ln_o = 1 + 0.1 * rng.standard_normal(cp), 0.1 * rng.standard_normal(cp)
+    pw = rng.standard_normal((cp, H)) / math.sqrt(cp)
+    x = rng.standard_normal((B * Q, c))
+    mask = (rng.random(B * Q) < 0.8).astype(np.float64)
+    got = oracle.attention(x, mask, w, B, Q, H, pair_bias={"source": "separate", "activations": pair,
+                                                              "layerNormScale": ln_s, "layerNormOffset": ln_o,
+                                                              "projectionWeight": pw})
+
+    def bias(h, q, k):
+        r = pair[q * Q + k]
+        mean = r.mean()
+        inv = 1 / math.sqrt(((r - mean) ** 2).mean() + 1e-5)
+        return float((((r - mean) * inv * ln_s + ln_o) * pw[:, h]).sum())
+
+    want = _loops(x, mask, w, B, Q, H, False, None, bias)
+    np.testing.assert_allclose(got, want, rtol=1e-9, atol=1e-9)
