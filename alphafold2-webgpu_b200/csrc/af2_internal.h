@@ -56,6 +56,7 @@ struct ProfilePending {
 struct af2_ctx {
   int device = 0;
   int sm_count = 0;
+  int contract_pairs = 0;  // CTA pairs of the triangle contraction resident together (0: not queried)
   cudaStream_t stream = nullptr;
   unsigned int *err_word = nullptr;  // device word the kernels flag failures in
   af2::DeviceBuffer workspace;       // device-form scratch

@@ -1193,13 +1193,10 @@ CUtensorMapDataType map_type(int dtype) {
 template <typename ZT>
 af2_status launch_project(af2_ctx *ctx, const CUtensorMap &zmap, const CUtensorMap &amap, const CUtensorMap &bmap,
                           const tri::ProjectArgs &a, cudaStream_t stream) {
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(tri::project_kernel<ZT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         tri::PJ_SMEM);
-    if (e != cudaSuccess) return cuda_fail(ctx, e, "configure project kernel");
-    configured = true;
-  }
+  // set on every launch: the attribute belongs to the current device's copy of the kernel
+  cudaError_t ce = cudaFuncSetAttribute(tri::project_kernel<ZT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        tri::PJ_SMEM);
+  if (ce != cudaSuccess) return cuda_fail(ctx, ce, "configure project kernel");
   const int grid = std::max(1, std::min(a.total_tiles, ctx->sm_count));
   {
     LaunchScope scope(ctx, stream, kProfTriangleProject);
@@ -1212,13 +1209,9 @@ af2_status launch_project(af2_ctx *ctx, const CUtensorMap &zmap, const CUtensorM
 template <typename ZT, typename OT>
 af2_status launch_output(af2_ctx *ctx, const CUtensorMap &xmap, const CUtensorMap &zmap, const CUtensorMap &omap,
                          const tri::OutputArgs &a, cudaStream_t stream) {
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(tri::output_kernel<ZT, OT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         tri::OP_SMEM);
-    if (e != cudaSuccess) return cuda_fail(ctx, e, "configure output kernel");
-    configured = true;
-  }
+  cudaError_t ce = cudaFuncSetAttribute(tri::output_kernel<ZT, OT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        tri::OP_SMEM);
+  if (ce != cudaSuccess) return cuda_fail(ctx, ce, "configure output kernel");
   const int grid = std::max(1, std::min(a.total_tiles, ctx->sm_count));
   {
     LaunchScope scope(ctx, stream, kProfTriangleOutput);
@@ -1408,14 +1401,13 @@ af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L,
       !encode_map_3d(&omap, map_type(out_dtype), out, C, L.n, rows, row_bytes, row_bytes * L.n, 64, 128, 1,
                      CU_TENSOR_MAP_SWIZZLE_128B))
     return fail(ctx, AF2_ERR_CUDA, "cuTensorMapEncodeTiled failed for the output store map");
-  static bool contract_configured = false;
-  static int contract_pairs = 0;
-  if (!contract_configured) {
-    cudaError_t e = cudaFuncSetAttribute(contract_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, CT_SMEM);
-    if (e != cudaSuccess) return cuda_fail(ctx, e, "configure contraction kernel");
-    contract_pairs = resident_pairs(ctx, contract_kernel, CT_THREADS, CT_SMEM);
-    contract_configured = true;
-  }
+  // the attribute is per device, so it is set for this context's device on every call; the
+  // resident-pair count it allows is queried once per context
+  if (cudaError_t e = cudaFuncSetAttribute(contract_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, CT_SMEM);
+      e != cudaSuccess)
+    return cuda_fail(ctx, e, "configure contraction kernel");
+  if (ctx->contract_pairs == 0) ctx->contract_pairs = resident_pairs(ctx, contract_kernel, CT_THREADS, CT_SMEM);
+  const int contract_pairs = ctx->contract_pairs;
   auto contract = [&](int64_t rb, int64_t rc, int64_t rows_per_block, __half *x_base, int own_blk) -> af2_status {
     ContractArgs ca;
     ca.x_out = x_base;
