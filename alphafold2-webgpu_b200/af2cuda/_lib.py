@@ -83,6 +83,7 @@ SIGNATURES = {
     "af2_last_error": (ctypes.c_char_p, [_vp]),
     "af2_sync": (_i32, [_vp, _vp]),
     "af2_launch_count": (ctypes.c_uint64, [_vp]),
+    "af2_memory_snapshot": (_i32, [_vp, ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64)]),
     "af2_profile_enable": (_i32, [_vp, _i32]),
     "af2_profile_reset": (_i32, [_vp]),
     "af2_profile_kernel_name": (ctypes.c_char_p, [_i32]),

@@ -27,6 +27,13 @@ class Device:
     def launch_count(self) -> int:
         return int(_lib.lib().af2_launch_count(self.handle))
 
+    def memory_snapshot(self) -> dict:
+        """{"currentBytes", "peakBytes"} of this context's device allocations
+        (the reference allocator's snapshot(), src/runtime/allocator.ts:376-382)."""
+        cur, peak = ctypes.c_uint64(), ctypes.c_uint64()
+        _lib.check(_lib.lib().af2_memory_snapshot(self.handle, ctypes.byref(cur), ctypes.byref(peak)), self.handle)
+        return {"currentBytes": int(cur.value), "peakBytes": int(peak.value)}
+
     def close(self) -> None:
         if self.handle:
             _lib.lib().af2_destroy(self.handle)

@@ -309,6 +309,13 @@ const char *af2_last_error(const af2_ctx *ctx) { return ctx ? ctx->last_error.c_
 
 uint64_t af2_launch_count(const af2_ctx *ctx) { return ctx ? ctx->launches : 0; }
 
+af2_status af2_memory_snapshot(const af2_ctx *ctx, uint64_t *current_bytes, uint64_t *peak_bytes) {
+  if (!ctx) return AF2_ERR_INVALID_ARGUMENT;
+  if (current_bytes) *current_bytes = ctx->allocated;
+  if (peak_bytes) *peak_bytes = ctx->peak;
+  return AF2_OK;
+}
+
 af2_status af2_sync(af2_ctx *ctx, void *stream) {
   if (!ctx) return AF2_ERR_INVALID_ARGUMENT;
   cudaSetDevice(ctx->device);

@@ -33,7 +33,9 @@ std::mutex g_setup_mutex;
 void *g_scratch_address[kMaxDevices] = {};
 
 // The array's name is only a host-side stand-in: the kernels need its device
-// address, looked up once per device with that device current.
+// address, looked up once per device with that device current.  The address is
+// kept for the life of the process, so a cudaDeviceReset while the library is
+// loaded is not supported: the kept address would belong to the destroyed context.
 af2_status scratch_address(af2_ctx *ctx, void **out) {
   if (ctx->device < 0 || ctx->device >= kMaxDevices)
     return fail(ctx, AF2_ERR_UNSUPPORTED, "device ordinal beyond the static scratch table");

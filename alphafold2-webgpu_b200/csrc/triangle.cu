@@ -1171,7 +1171,8 @@ namespace {
 
 // CTA pairs that can be resident at once for a cluster kernel (its __cluster_dims__
 // of two): a persistent grid larger than this would leave pairs waiting for others to
-// finish.  Queried once per kernel; falls back to half the SMs.
+// finish.  Returns 0 when the occupancy query fails, so that the caller uses a fallback
+// for this launch only and asks again next time.
 template <typename K>
 int resident_pairs(af2_ctx *ctx, K kernel, int threads, uint32_t smem) {
   cudaLaunchConfig_t cfg = {};
@@ -1181,7 +1182,7 @@ int resident_pairs(af2_ctx *ctx, K kernel, int threads, uint32_t smem) {
   int clusters = 0;
   if (cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg) != cudaSuccess || clusters < 1) {
     cudaGetLastError();
-    clusters = std::max(1, ctx->sm_count / 2);
+    return 0;
   }
   return clusters;
 }
@@ -1406,8 +1407,10 @@ af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L,
   if (cudaError_t e = cudaFuncSetAttribute(contract_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, CT_SMEM);
       e != cudaSuccess)
     return cuda_fail(ctx, e, "configure contraction kernel");
+  // only a successful query is kept; after a failed one this launch uses half the SMs' worth of
+  // pairs (a grid that may exceed what is resident, which costs time, not results)
   if (ctx->contract_pairs == 0) ctx->contract_pairs = resident_pairs(ctx, contract_kernel, CT_THREADS, CT_SMEM);
-  const int contract_pairs = ctx->contract_pairs;
+  const int contract_pairs = ctx->contract_pairs > 0 ? ctx->contract_pairs : std::max(1, ctx->sm_count / 2);
   auto contract = [&](int64_t rb, int64_t rc, int64_t rows_per_block, __half *x_base, int own_blk) -> af2_status {
     ContractArgs ca;
     ca.x_out = x_base;

@@ -114,6 +114,10 @@ AF2_API int af2_version(void);
 AF2_API af2_status af2_sync(af2_ctx *ctx, void *stream);
 /* Number of kernels this context has launched (monotonic). */
 AF2_API uint64_t af2_launch_count(const af2_ctx *ctx);
+/* Device memory the context holds now and its high-water mark, in bytes: the
+ * currentBytes / peakBytes of the reference allocator's snapshot()
+ * (src/runtime/allocator.ts:8-10,376-382).  Either pointer may be NULL. */
+AF2_API af2_status af2_memory_snapshot(const af2_ctx *ctx, uint64_t *current_bytes, uint64_t *peak_bytes);
 
 /*
  * Per-kernel device timing (the counterpart of the reference's timestamp-query
@@ -182,8 +186,9 @@ AF2_API af2_status af2_triangle_multiplication(af2_ctx *ctx, int direction, cons
  * on each device where the library is loaded until the process exits, and
  * larger shapes return AF2_ERR_UNSUPPORTED.  The first call on each device
  * looks up the array's device address (once); make that first call before any
- * stream capture.  All calls share the array: calls that overlap on the GPU
- * race.  Arguments as af2_triangle_multiplication, without `workspace`.
+ * stream capture, and do not reset the device while the library is loaded.
+ * All calls share the array: calls that overlap on the GPU race.  Arguments
+ * as af2_triangle_multiplication, without `workspace`.
  */
 AF2_API af2_status af2_triangle_multiplication_static(af2_ctx *ctx, int direction, const af2_triangle_shape *shape,
                                                       const void *z, int z_dtype, const float *mask,

@@ -223,25 +223,32 @@ AF2O_EXPORT int64_t af2o_triangle_weight_count(int64_t cz, int64_t ch) {
  * src/triangle/cpu-reference.ts:56-100; direction 1 = incoming, the same
  * with the contraction x[i,j,h] = sum_k a[k,j,h] * b[k,i,h]
  * (src/triangle/shaders.ts:452-455; AlphaFold's 'kjc,kic->ijc').
- * z [n,n,cz], mask [n,n], packed weights in ORDER; out [n,n,cz] (no residual).
+ * z [n,n,cz], mask [n,n], packed weights in ORDER.  Only the output rows i
+ * listed in `rows` (count of them) are produced, into out [count,n,cz] (no
+ * residual): the projections cover every pair, the contraction, output
+ * LayerNorm and output projection only the listed rows.  Every computed
+ * element takes the same operations in the same order as in the whole op.
  */
-AF2O_EXPORT int af2o_triangle(int direction, int64_t n, int64_t cz, int64_t ch, const float *z,
-                              const float *mask, const float *packed, double eps, float *out,
-                              int threads) {
-    if (n <= 0 || cz <= 0 || ch <= 0 || (direction != 0 && direction != 1)) return 1;
+AF2O_EXPORT int af2o_triangle_rows(int direction, int64_t n, int64_t cz, int64_t ch, const float *z,
+                                   const float *mask, const float *packed, double eps, const int64_t *rows,
+                                   int64_t count, float *out, int threads) {
+    if (n <= 0 || cz <= 0 || ch <= 0 || count <= 0 || (direction != 0 && direction != 1)) return 1;
+    for (int64_t r = 0; r < count; ++r)
+        if (rows[r] < 0 || rows[r] >= n) return 1;
     set_threads(threads);
     tri_weights w = unpack_triangle(packed, cz, ch);
-    int64_t pairs = n * n;
+    int64_t pairs = n * n, sel = count * n;
     float *zn = (float *)malloc(sizeof(float) * pairs * cz);
     float *ap = (float *)malloc(sizeof(float) * pairs * ch);
     float *ag = (float *)malloc(sizeof(float) * pairs * ch);
     float *bp = (float *)malloc(sizeof(float) * pairs * ch);
     float *bg = (float *)malloc(sizeof(float) * pairs * ch);
-    float *x = (float *)malloc(sizeof(float) * pairs * ch);
-    float *xn = (float *)malloc(sizeof(float) * pairs * ch);
-    float *gate = (float *)malloc(sizeof(float) * pairs * cz);
-    if (!zn || !ap || !ag || !bp || !bg || !x || !xn || !gate) {
-        free(zn); free(ap); free(ag); free(bp); free(bg); free(x); free(xn); free(gate);
+    float *x = (float *)malloc(sizeof(float) * sel * ch);
+    float *xn = (float *)malloc(sizeof(float) * sel * ch);
+    float *zs = (float *)malloc(sizeof(float) * sel * cz);
+    float *gate = (float *)malloc(sizeof(float) * sel * cz);
+    if (!zn || !ap || !ag || !bp || !bg || !x || !xn || !zs || !gate) {
+        free(zn); free(ap); free(ag); free(bp); free(bg); free(x); free(xn); free(zs); free(gate);
         return 2;
     }
     normalize_rows(z, pairs, cz, w.ln_in_w, w.ln_in_b, eps, zn);
@@ -261,7 +268,8 @@ AF2O_EXPORT int af2o_triangle(int direction, int64_t n, int64_t cz, int64_t ch, 
     }
     /* cpu-reference.ts:77-89 (outgoing) and the transposed einsum (incoming). */
 #pragma omp parallel for schedule(static)
-    for (int64_t i = 0; i < n; ++i) {
+    for (int64_t r = 0; r < count; ++r) {
+        const int64_t i = rows[r];
         for (int64_t j = 0; j < n; ++j) {
             for (int64_t h = 0; h < ch; ++h) {
                 double value = 0;
@@ -272,18 +280,32 @@ AF2O_EXPORT int af2o_triangle(int direction, int64_t n, int64_t cz, int64_t ch, 
                     for (int64_t k = 0; k < n; ++k)
                         value += (double)ap[(k * n + j) * ch + h] * (double)bp[(k * n + i) * ch + h];
                 }
-                x[(i * n + j) * ch + h] = (float)value;
+                x[(r * n + j) * ch + h] = (float)value;
             }
         }
+        memcpy(zs + r * n * cz, zn + i * n * cz, sizeof(float) * n * cz);
     }
     /* cpu-reference.ts:91-99. */
-    normalize_rows(x, pairs, ch, w.ln_out_w, w.ln_out_b, eps, xn);
-    project(xn, pairs, ch, cz, w.z_w, w.z_b, out);
-    project(zn, pairs, cz, cz, w.g_w, w.g_b, gate);
+    normalize_rows(x, sel, ch, w.ln_out_w, w.ln_out_b, eps, xn);
+    project(xn, sel, ch, cz, w.z_w, w.z_b, out);
+    project(zs, sel, cz, cz, w.g_w, w.g_b, gate);
 #pragma omp parallel for schedule(static)
-    for (int64_t idx = 0; idx < pairs * cz; ++idx) out[idx] = (float)((double)out[idx] * sigmoid(gate[idx]));
-    free(zn); free(ap); free(ag); free(bp); free(bg); free(x); free(xn); free(gate);
+    for (int64_t idx = 0; idx < sel * cz; ++idx) out[idx] = (float)((double)out[idx] * sigmoid(gate[idx]));
+    free(zn); free(ap); free(ag); free(bp); free(bg); free(x); free(xn); free(zs); free(gate);
     return 0;
+}
+
+/* The whole op: every output row. */
+AF2O_EXPORT int af2o_triangle(int direction, int64_t n, int64_t cz, int64_t ch, const float *z,
+                              const float *mask, const float *packed, double eps, float *out,
+                              int threads) {
+    if (n <= 0) return 1;
+    int64_t *rows = (int64_t *)malloc(sizeof(int64_t) * n);
+    if (!rows) return 2;
+    for (int64_t i = 0; i < n; ++i) rows[i] = i;
+    int rc = af2o_triangle_rows(direction, n, cz, ch, z, mask, packed, eps, rows, n, out, threads);
+    free(rows);
+    return rc;
 }
 
 /* ------------------------------------------------------------------------ */

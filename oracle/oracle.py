@@ -21,6 +21,7 @@ _i8p = ctypes.POINTER(ctypes.c_int8)
 _u16p = ctypes.POINTER(ctypes.c_uint16)
 _f64p = ctypes.POINTER(ctypes.c_double)
 _i64 = ctypes.c_int64
+_i64p = ctypes.POINTER(ctypes.c_int64)
 
 _lib = None
 
@@ -50,6 +51,9 @@ def lib() -> ctypes.CDLL:
         _lib.af2o_triangle.restype = ctypes.c_int
         _lib.af2o_triangle.argtypes = [ctypes.c_int, _i64, _i64, _i64, _f32p, _f32p, _f32p,
                                        ctypes.c_double, _f32p, ctypes.c_int]
+        _lib.af2o_triangle_rows.restype = ctypes.c_int
+        _lib.af2o_triangle_rows.argtypes = [ctypes.c_int, _i64, _i64, _i64, _f32p, _f32p, _f32p,
+                                            ctypes.c_double, _i64p, _i64, _f32p, ctypes.c_int]
         _lib.af2o_opm_weight_count.restype = _i64
         _lib.af2o_opm_weight_count.argtypes = [_i64, _i64, _i64]
         _lib.af2o_outer_product_mean.restype = ctypes.c_int
@@ -147,6 +151,26 @@ def triangle(direction: int, z, mask, packed, eps: float = 1e-5, threads: int | 
                              threads or default_threads())
     if rc != 0:
         raise RuntimeError(f"oracle triangle failed ({rc})")
+    return out
+
+
+def triangle_rows(direction: int, z, mask, packed, rows, eps: float = 1e-5, threads: int | None = None) -> np.ndarray:
+    """Output rows `rows` of triangle multiplication (no residual): [len(rows), n, cz].  The
+    projections cover every pair; only the listed rows are contracted and projected, each
+    element computed exactly as the whole op computes it."""
+    z = _f32(z)
+    n, n2, cz = z.shape
+    assert n == n2
+    mask = _f32(mask)
+    packed = _f32(packed)
+    ch = _hidden_from_count(cz, packed.size)
+    sel = np.ascontiguousarray(rows, np.int64)
+    out = np.zeros((sel.size, n, cz), np.float32)
+    rc = lib().af2o_triangle_rows(direction, n, cz, ch, _ptr(z, ctypes.c_float), _ptr(mask, ctypes.c_float),
+                                  _ptr(packed, ctypes.c_float), eps, _ptr(sel, ctypes.c_int64), sel.size,
+                                  _ptr(out, ctypes.c_float), threads or default_threads())
+    if rc != 0:
+        raise RuntimeError(f"oracle triangle rows failed ({rc})")
     return out
 
 

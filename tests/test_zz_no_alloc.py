@@ -50,12 +50,19 @@ def test_static_scratch_matches_allocating_entry_point(device, direction):
         got = torch.full_like(zd, float("nan"))
         torch.cuda.synchronize()
         _call("af2_triangle_multiplication", device, direction, zd, md, wd, ref, False, stream.cuda_stream)
+        device.sync(stream.cuda_stream)
+        held = device.memory_snapshot()
         _call("af2_triangle_multiplication_static", device, direction, zd, md, wd, got, False, stream.cuda_stream)
         device.sync(stream.cuda_stream)
+        # the static call allocated nothing through the context
+        assert device.memory_snapshot() == held, f"call {call}"
         want = ref.float().cpu().numpy()
         have = got.float().cpu().numpy()
         assert np.isfinite(have).all(), f"call {call}"
         assert relative_max_error(have, want) <= 2e-3, f"call {call}"
+        # same kernels, same inputs, same stream: the results agree bit for bit, so nothing a
+        # previous call left in the shared array leaks into this one
+        assert torch.equal(got, ref), f"call {call}"
 
 
 def test_static_scratch_rejects_shapes_beyond_its_size(device):
