@@ -5,6 +5,10 @@ The class and option names follow the reference's TypeScript exports
 (src/index.ts) so parity tests read like the reference's own tests.
 """
 from ._lib import Af2Error, RangeError, lib
+from .attention import (AttentionGpu, AttentionInput, AttentionResult, AttentionWeights, NormalizedInputPairBias,
+                        SeparatePairBias, attention_weight_count, attention_workspace_bytes,
+                        encode_attention_tensors, encode_triangle_attention_tensors, pack_attention_weights)
+from .block import encode_evoformer_pair_block_tensors
 from .bundle import TriangleReferenceBundle, load_triangle_reference_bundle_from_files
 from .device import Device
 from .triangle import (TriangleGpuOptions, TriangleGpuResult, TriangleMultiplicationIncomingGpu,
@@ -33,5 +37,8 @@ __all__ = [
     "OuterProductMeanWeights", "encode_outer_product_mean_tensors", "linear_tensors", "opm_weight_count",
     "opm_workspace_bytes", "pack_outer_product_mean_weights", "validate_outer_product_mean_input",
     "comm_destroy", "comm_init", "comm_unique_id", "encode_triangle_multiplication_sharded_tensors", "rows_of",
-    "encode_outer_product_mean_sharded_tensors",
+    "encode_outer_product_mean_sharded_tensors", "AttentionGpu", "AttentionInput", "AttentionResult",
+    "AttentionWeights", "NormalizedInputPairBias", "SeparatePairBias", "attention_weight_count",
+    "attention_workspace_bytes", "encode_attention_tensors", "encode_triangle_attention_tensors",
+    "pack_attention_weights", "encode_evoformer_pair_block_tensors",
 ]

@@ -24,6 +24,7 @@ AF2_ERR_NO_DEVICE = 7
 AF2_F32, AF2_F16, AF2_BF16 = 0, 1, 2
 AF2_OUTGOING, AF2_INCOMING = 0, 1
 AF2_WEIGHTS_F32, AF2_WEIGHTS_Q8_BLOCK, AF2_WEIGHTS_Q8_CHANNEL = 0, 1, 2
+AF2_GEMM_MATRIX, AF2_GEMM_F32 = 0, 1
 
 # Every symbol include/af2cuda.h declares, with (restype, argtypes).
 _vp = ctypes.c_void_p
@@ -71,6 +72,28 @@ class OpmOptions(ctypes.Structure):
                 ("residual", ctypes.c_int32)]
 
 
+class AttentionShape(ctypes.Structure):
+    _fields_ = [("batch", _i64), ("queries", _i64), ("channels", _i64), ("heads", _i64)]
+
+
+class AttentionOptions(ctypes.Structure):
+    _fields_ = [("transpose", ctypes.c_int32), ("pair_bias", ctypes.c_int32), ("residual", ctypes.c_int32)]
+
+
+class PairBlockShape(ctypes.Structure):
+    _fields_ = [("length", _i64), ("sequences", _i64), ("c_m", _i64), ("c_z", _i64), ("c_outer", _i64),
+                ("c_hidden", _i64), ("pair_heads", _i64), ("transition_hidden", _i64)]
+
+
+class PairBlockWeights(ctypes.Structure):
+    _fields_ = [("outer_product_mean", _vp), ("triangle_outgoing", _vp), ("triangle_incoming", _vp),
+                ("attention_starting", _vp), ("attention_ending", _vp), ("pair_transition", TransitionWeights)]
+
+
+class PairBlockOptions(ctypes.Structure):
+    _fields_ = [("include_outer_product_mean", ctypes.c_int32), ("epsilon", _f64)]
+
+
 class LinearShape(ctypes.Structure):
     _fields_ = [("rows", _i64), ("inner", _i64), ("columns", _i64)]
 
@@ -83,6 +106,8 @@ SIGNATURES = {
     "af2_last_error": (ctypes.c_char_p, [_vp]),
     "af2_sync": (_i32, [_vp, _vp]),
     "af2_launch_count": (ctypes.c_uint64, [_vp]),
+    "af2_set_gemm_precision": (_i32, [_vp, _i32]),
+    "af2_get_gemm_precision": (_i32, [_vp]),
     "af2_memory_snapshot": (_i32, [_vp, ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64)]),
     "af2_profile_enable": (_i32, [_vp, _i32]),
     "af2_profile_reset": (_i32, [_vp]),
@@ -122,6 +147,16 @@ SIGNATURES = {
                                                    _f64, ctypes.POINTER(TriangleOptions), _vp, _i32, _vp]),
     "af2_outer_product_mean_sharded": (_i32, [_vp, ctypes.POINTER(OpmShape), _vp, _i32, _vp, _vp, _i64,
                                               ctypes.POINTER(OpmOptions), _vp, _i32, _vp]),
+    "af2_attention_weight_count": (_i64, [ctypes.POINTER(AttentionShape), _i32]),
+    "af2_attention_check": (_i32, [ctypes.POINTER(AttentionShape), _i32, _i64, _f64, ctypes.c_char_p,
+                                   ctypes.c_size_t]),
+    "af2_attention_workspace_bytes": (_i32, [ctypes.POINTER(AttentionShape), _i32, ctypes.POINTER(ctypes.c_uint64)]),
+    "af2_attention_host": (_i32, [_vp, ctypes.POINTER(AttentionShape), _vp, _vp, _vp, _i64, _f64,
+                                  ctypes.POINTER(AttentionOptions), _vp, ctypes.POINTER(OpStats)]),
+    "af2_attention": (_i32, [_vp, ctypes.POINTER(AttentionShape), _vp, _i32, _vp, _vp, _i64, _f64,
+                             ctypes.POINTER(AttentionOptions), _vp, _i32, _vp, _vp]),
+    "af2_evoformer_pair_block": (_i32, [_vp, ctypes.POINTER(PairBlockShape), ctypes.POINTER(PairBlockWeights), _vp, _i32,
+                                        _vp, _vp, _i32, _vp, ctypes.POINTER(PairBlockOptions), _vp]),
     "af2_linear_workspace_bytes": (_i32, [ctypes.POINTER(LinearShape), _i32, ctypes.POINTER(ctypes.c_uint64)]),
     "af2_linear": (_i32, [_vp, ctypes.POINTER(LinearShape), _vp, _i32, ctypes.POINTER(Matrix), _vp, _i32, _i32, _vp,
                           _i32, _vp, _vp]),

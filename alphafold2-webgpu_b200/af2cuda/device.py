@@ -27,6 +27,20 @@ class Device:
     def launch_count(self) -> int:
         return int(_lib.lib().af2_launch_count(self.handle))
 
+    @property
+    def gemm_precision(self) -> str:
+        """The installed GEMM precision: "matrix" (f16 operands, f32 accumulation) or "f32"
+        (split hi/lo f16 operands for the ops that honour it), like the reference's
+        gemmVariant().precision (src/runtime/gemm.ts:175,213-215)."""
+        return {_lib.AF2_GEMM_MATRIX: "matrix", _lib.AF2_GEMM_F32: "f32"}[_lib.lib().af2_get_gemm_precision(self.handle)]
+
+    def set_gemm_precision(self, precision: str) -> None:
+        """Installs "matrix" or "f32" for this device's later calls (forceGemmVariant's role)."""
+        code = {"matrix": _lib.AF2_GEMM_MATRIX, "f32": _lib.AF2_GEMM_F32}.get(precision)
+        if code is None:
+            raise _lib.RangeError(f"precision must be 'matrix' or 'f32'; received {precision}")
+        _lib.check(_lib.lib().af2_set_gemm_precision(self.handle, code), self.handle)
+
     def memory_snapshot(self) -> dict:
         """{"currentBytes", "peakBytes"} of this context's device allocations
         (the reference allocator's snapshot(), src/runtime/allocator.ts:376-382)."""

@@ -121,9 +121,9 @@ class OuterProductMeanGpu:
     def __init__(self, device: Device):
         self.device = device
 
-    def run(self, inp: OuterProductMeanInput, precision: str = "f32") -> OuterProductMeanResult:
+    def run(self, inp: OuterProductMeanInput, host_storage: str = "f32") -> OuterProductMeanResult:
         validate_outer_product_mean_input(inp)
-        io_dtype = _DTYPES[precision]
+        io_dtype = _DTYPES[host_storage]
         if io_dtype == _lib.AF2_BF16:
             raise _lib.RangeError("the host form takes f32 or f16 arrays")
         rb = inp.rowBlockResidues

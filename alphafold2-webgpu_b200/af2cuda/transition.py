@@ -115,9 +115,9 @@ class TransitionGpu:
                                               or not 0 < self.maxChunkRows <= MAX_SAFE_INTEGER):
             raise _lib.RangeError("maxChunkRows must be a positive safe integer")
 
-    def run(self, inp: TransitionInput, precision: str = "f32", residual: bool = False) -> TransitionResult:
+    def run(self, inp: TransitionInput, host_storage: str = "f32", residual: bool = False) -> TransitionResult:
         validate_transition_input(inp)
-        io_dtype = _DTYPES[precision]
+        io_dtype = _DTYPES[host_storage]
         if io_dtype == _lib.AF2_BF16:
             raise _lib.RangeError("the host form takes f32 or f16 arrays")
         x = np.ascontiguousarray(inp.activations, _NP[io_dtype]).ravel()

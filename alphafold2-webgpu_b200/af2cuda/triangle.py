@@ -31,15 +31,21 @@ _NP = {_lib.AF2_F32: np.float32, _lib.AF2_F16: np.float16}
 class TriangleGpuOptions:
     """TriangleGpuOptions, src/triangle/webgpu.ts:9-15.
 
-    precision: "f32" (Float32Array in and out) or "f16" (half-precision
-    arrays in and out).  Either way the products run on the tensor cores with
-    f16 operands and f32 accumulation.  blockRows: output rows per block,
-    which bounds scratch only; results are bit-identical for any value.
-    wholeStorage is accepted for signature parity; operands are always f16.
+    precision: "f32" or "f16", the weight and arithmetic precision; as in the
+    reference (webgpu.ts:93-99) the pair stays f32 in and out either way.  This
+    build runs both on the tensor cores with f16 operands and f32
+    accumulation (the f16 bars of the reference's tests hold for both).
+    blockRows: output rows per block, which bounds scratch only; results are
+    bit-identical for any value.  wholeStorage: "f32" or "f16", the storage
+    of the whole projection; the projected operands are always f16 in HBM
+    here, so both values run the same kernels.
+    hostStorage (not in the reference): "f16" passes the pair to and from the
+    device as half-precision arrays instead of f32 ones.
     """
     precision: str = "f32"
     blockRows: Optional[int] = None
     wholeStorage: str = "f32"
+    hostStorage: str = "f32"
 
 
 @dataclass(frozen=True)
@@ -76,9 +82,13 @@ class _TriangleMultiplicationGpu:
         opts = _options(options)
         if opts.precision not in ("f32", "f16"):
             raise _lib.RangeError(f"precision must be f32 or f16; received {opts.precision}")
+        if opts.wholeStorage not in ("f32", "f16"):
+            raise _lib.RangeError(f"wholeStorage must be f32 or f16; received {opts.wholeStorage}")
+        if opts.hostStorage not in ("f32", "f16"):
+            raise _lib.RangeError(f"hostStorage must be f32 or f16; received {opts.hostStorage}")
         n, cz, ch = inp.shape.length, inp.shape.cZ, inp.shape.cHidden
         block_rows = max(1, min(n, opts.blockRows if opts.blockRows is not None else n))
-        io_dtype = _DTYPES[opts.precision]
+        io_dtype = _DTYPES[opts.hostStorage]
         z = np.ascontiguousarray(inp.z, _NP[io_dtype]).ravel()
         mask = np.ascontiguousarray(inp.mask, np.float32).ravel()
         packed, _ = pack_weights(inp.weights)

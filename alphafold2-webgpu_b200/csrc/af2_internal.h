@@ -44,6 +44,10 @@ enum ProfileKernel {
   kProfOpmOutput,
   kProfOpmFused,
   kProfTransitionLinear,
+  kProfAttentionNormalize,
+  kProfAttentionProject,
+  kProfAttentionFlash,
+  kProfAttentionOutput,
   kProfCount
 };
 const char *profile_name(int id);
@@ -83,6 +87,7 @@ struct af2_ctx {
   std::vector<cudaEvent_t> copy_events;
   int *sync_word = nullptr;                // device word the exchange barriers all-reduce
   bool ipc_failed = false;                 // mapping refused: exchanges use NCCL send/recv
+  int gemm_precision = 0;                  // af2_gemm_precision: what the GEMMs that honour it multiply in
 };
 
 namespace af2 {
@@ -205,6 +210,13 @@ af2_status dequant_launch(af2_ctx *ctx, const af2_matrix &m, int64_t inner, int6
 
 // ---- shared dense projection (gemm.cu) ----
 
+// Destinations of the attention projection epilogue (attention.cu): q and k [b][h][j][32],
+// v transposed [b][h][32][pitch], the gate [rows][channels], the pair bias [h][b][pitch] (or NULL).
+struct AttentionProjection {
+  void *q = nullptr, *k = nullptr, *vt = nullptr, *g = nullptr, *bias = nullptr;  // f16
+  int64_t queries = 0, pitch = 0, channels = 0, heads = 0;
+};
+
 // One tcgen05 GEMM D = A W over prepared weights, with its epilogue.
 struct LinearOperands {
   const void *a = nullptr;        // f16 rows [rows][lda], the first `inner` columns used
@@ -220,11 +232,20 @@ struct LinearOperands {
   int out_dtype = AF2_F32;
   int relu = 0, residual = 0;
   bool opm_projection = false;    // columns [0, cols/2) -> left, the rest -> right (f16), times row_mask
+  // opm_projection in the f32 precision mode: each value v is written as a split operand, left as
+  // blocks (f16(v), f16(v), f16(v - f16(v))) and right as (f16(v), f16(v - f16(v)), f16(v)),
+  // `split_stride_left` / `split_stride_right` elements apart, so that the outer-product GEMM
+  // over the three blocks sums hi hi + hi lo + lo hi
+  int64_t split_stride_left = 0, split_stride_right = 0;
   void *left = nullptr, *right = nullptr;
   // seq_pitch > 0: rows are m = i * kmajor_seqs + s, and left / right are written
   // sequence-contiguous: left [cols / 2][kmajor_rows][seq_pitch], right [rows][cols / 2][seq_pitch]
   int64_t kmajor_rows = 0, kmajor_seqs = 0, seq_pitch = 0;
   int prof = kProfLinear;
+  int bn = 0;                     // column tile (a multiple of 32, at most 256); 0 = chosen from cols
+  // the output row of row m = b * transpose_q + q is q * transpose_b + b (0: row m)
+  int64_t transpose_q = 0, transpose_b = 0;
+  const AttentionProjection *attention = nullptr;  // attention projection epilogue instead of `out`
 };
 
 // Tile width the GEMM uses for `cols` output columns, and the padded column count.
@@ -237,7 +258,7 @@ af2_status prepare_matrix(af2_ctx *ctx, const af2_matrix &w, int64_t inner, int6
                           int64_t cols_pad, float extra_scale, void *out, float *scale_out, cudaStream_t stream,
                           int64_t row0 = 0, int64_t rows_total = 0);
 // Up to kMaxPrepJobs such preparations in one launch.
-constexpr int kMaxPrepJobs = 4;
+constexpr int kMaxPrepJobs = 6;
 struct PrepJob {
   af2_matrix w;
   int64_t inner, cols, inner_pad, cols_pad;
@@ -246,6 +267,9 @@ struct PrepJob {
   float *scale_out;
   int64_t row0 = 0, rows_total = 0;
   const float *row_scale = nullptr;  // optional factor per inner row k (a LayerNorm gamma folded in)
+  // 0: the f16 rounding of each scaled weight; 1: the f16 rounding of what that leaves (w - f16(w)),
+  // the low half of a split operand (f32 precision mode)
+  int part = 0;
 };
 af2_status prepare_matrices(af2_ctx *ctx, const PrepJob *jobs, int count, cudaStream_t stream);
 // Up to 8 zero-padded vector copies done by one launch.
@@ -289,6 +313,7 @@ struct OpmLayout {
   int out_shift = 0;        // outer is stored times 2^-out_shift (2^out_shift >= S)
   size_t off_wlr = 0, off_wlr_scale = 0, off_wlr_bias = 0, off_wo = 0, off_wo_scale = 0, off_wo_bias = 0;
   bool fused = false;        // outer product and output projection in one kernel (no outer scratch)
+  bool split = false;        // f32 precision mode: every GEMM operand as an f16 hi / lo pair, K tripled
   int64_t seq_pitch = 0;    // fused: left [c][rows][seq_pitch] and right [n][c][seq_pitch], K-major
   size_t off_ln = 0, off_xn = 0, off_mask = 0, off_left = 0, off_right = 0, off_rowscale = 0, off_outer = 0;
   size_t total = 0;
@@ -296,7 +321,7 @@ struct OpmLayout {
 
 // rows < n: this rank's residues [row0, row0 + rows) of a row-sharded pair.
 OpmLayout opm_layout(int64_t s, int64_t n, int64_t cm, int64_t c, int64_t cz, int64_t row_block, int64_t rows = 0,
-                     int64_t row0 = 0);
+                     int64_t row0 = 0, bool split = false);
 
 // Row-sharded OPM: this rank's block of the right operand is all-gathered in place.
 struct OpmExchange {
@@ -307,6 +332,25 @@ struct OpmExchange {
 af2_status opm_launch(af2_ctx *ctx, const OpmLayout &L, const void *m, int m_dtype, const float *mask,
                       const float *packed, double ln_eps, double norm_eps, int residual, void *out, int out_dtype,
                       void *workspace, cudaStream_t stream, const OpmExchange *exchange = nullptr);
+
+// ---- gated multi-head attention (attention.cu) ----
+
+struct AttentionLayout {
+  int64_t b = 0, q = 0, c = 0, h = 0;  // batch rows, queries (= keys), channels, heads (head dimension 32)
+  bool bias = false;                   // pair bias from the normalised input (needs b == q)
+  int64_t rows = 0;                    // b * q
+  int64_t pitch = 0;                   // key pitch of the transposed values, the bias and the mask (64-aligned)
+  int64_t k_pad = 0, cols = 0, o_cols = 0;
+  int bn = 0;                          // column tile of the projection GEMM
+  size_t off_w = 0, off_scale = 0, off_bvec = 0, off_wo = 0, off_wo_scale = 0, off_wo_bias = 0, off_ln = 0;
+  size_t off_xn = 0, off_q = 0, off_k = 0, off_vt = 0, off_g = 0, off_pb = 0, off_mb = 0, total = 0;
+};
+
+AttentionLayout attention_layout(int64_t batch, int64_t queries, int64_t channels, int64_t heads, bool bias);
+
+af2_status attention_launch(af2_ctx *ctx, const AttentionLayout &L, int transpose, const void *x, int x_dtype,
+                            const float *mask, const float *packed, double eps, int residual, void *out,
+                            int out_dtype, void *workspace, cudaStream_t stream);
 
 // ---- row-sharded operators (comm.cu) ----
 

@@ -56,7 +56,8 @@ const char *profile_name(int id) {
       "triangle.output",     "transition.prepare",   "transition.normalize", "transition.fused",
       "q8.decode",           "weights.prepare",      "activations.convert",  "linear",
       "opm.normalize",       "opm.project",          "opm.count",         "opm.outer",
-      "opm.output",          "opm.fused",            "transition.linear"};
+      "opm.output",          "opm.fused",            "transition.linear",
+      "attention.normalize", "attention.project",    "attention.flash",   "attention.output"};
   return (id >= 0 && id < kProfCount) ? names[id] : nullptr;
 }
 
@@ -308,6 +309,16 @@ void af2_destroy(af2_ctx *ctx) {
 const char *af2_last_error(const af2_ctx *ctx) { return ctx ? ctx->last_error.c_str() : "no context"; }
 
 uint64_t af2_launch_count(const af2_ctx *ctx) { return ctx ? ctx->launches : 0; }
+
+af2_status af2_set_gemm_precision(af2_ctx *ctx, int precision) {
+  if (!ctx) return AF2_ERR_INVALID_ARGUMENT;
+  if (precision != AF2_GEMM_MATRIX && precision != AF2_GEMM_F32)
+    return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "precision must be AF2_GEMM_MATRIX or AF2_GEMM_F32");
+  ctx->gemm_precision = precision;
+  return AF2_OK;
+}
+
+int af2_get_gemm_precision(const af2_ctx *ctx) { return ctx ? ctx->gemm_precision : AF2_GEMM_MATRIX; }
 
 af2_status af2_memory_snapshot(const af2_ctx *ctx, uint64_t *current_bytes, uint64_t *peak_bytes) {
   if (!ctx) return AF2_ERR_INVALID_ARGUMENT;
@@ -650,6 +661,7 @@ af2_status af2_opm_workspace_bytes(const af2_opm_shape *shape, const af2_opm_opt
   if (!shape || !bytes) return AF2_ERR_INVALID_ARGUMENT;
   af2_ctx scratch;
   if (validate_opm(&scratch, shape, af2_opm_weight_count(shape)) != AF2_OK) return AF2_ERR_INVALID_ARGUMENT;
+  // for the default GEMM precision (the f32 mode takes context-owned scratch only)
   *bytes = opm_layout(shape->sequences, shape->length, shape->c_m, shape->c_outer, shape->c_z,
                       options ? options->row_block_residues : 0)
                .total;
@@ -682,8 +694,12 @@ af2_status af2_outer_product_mean(af2_ctx *ctx, const af2_opm_shape *shape, cons
   int rb, residual;
   if ((st = opm_options(ctx, options, &ln_eps, &norm_eps, &rb, &residual)) != AF2_OK) return st;
   cudaSetDevice(ctx->device);
-  const OpmLayout L = opm_layout(shape->sequences, shape->length, shape->c_m, shape->c_outer, shape->c_z, rb);
+  const OpmLayout L = opm_layout(shape->sequences, shape->length, shape->c_m, shape->c_outer, shape->c_z, rb, 0, 0,
+                                 ctx->gemm_precision == AF2_GEMM_F32);
   void *ws = workspace;
+  if (ws && L.split)
+    return fail(ctx, AF2_ERR_INVALID_ARGUMENT,
+                "in the AF2_GEMM_F32 precision the outer product mean takes context-owned scratch (workspace NULL)");
   if (!ws) {
     if ((st = ensure(ctx, ctx->workspace, L.total, "outer product mean scratch")) != AF2_OK) return st;
     ws = ctx->workspace.ptr;
@@ -717,7 +733,8 @@ af2_status af2_outer_product_mean_host(af2_ctx *ctx, const af2_opm_shape *shape,
       (st = ensure(ctx, ctx->staging[2], w_bytes, "weight upload")) != AF2_OK ||
       (st = ensure(ctx, ctx->staging[3], out_bytes, "output")) != AF2_OK)
     return st;
-  const OpmLayout L = opm_layout(S, N, shape->c_m, shape->c_outer, shape->c_z, rb);
+  const OpmLayout L = opm_layout(S, N, shape->c_m, shape->c_outer, shape->c_z, rb, 0, 0,
+                                 ctx->gemm_precision == AF2_GEMM_F32);
   if ((st = ensure(ctx, ctx->workspace, L.total, "outer product mean scratch")) != AF2_OK) return st;
   cudaStream_t s = ctx->stream;
   cudaError_t e;
@@ -747,6 +764,160 @@ af2_status af2_outer_product_mean_host(af2_ctx *ctx, const af2_opm_shape *shape,
         std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
     // kernel-cost.ts: projection 2 S N c_m 2c, contraction 2 (N c)^2 S, output 2 N^2 c^2 c_z.
     stats->flops = 2 * dS * dN * cm * 2 * c + 2 * dN * c * dN * c * dS + 2 * dN * dN * c * c * cz;
+    stats->workspace_bytes = L.total;
+    stats->peak_bytes = ctx->peak;
+  }
+  return AF2_OK;
+}
+
+int64_t af2_attention_weight_count(const af2_attention_shape *shape, int pair_bias) {
+  if (!shape) return 0;
+  const int64_t c = shape->channels;
+  return 2 * c + 4 * c * c + c + c * c + c + (pair_bias == AF2_PAIR_BIAS_NORMALIZED_INPUT ? c * shape->heads : 0);
+}
+
+}  // extern "C"
+
+namespace af2 {
+namespace {
+// validate (src/evoformer/attention.ts:102-141) for a C caller, then the kernels' limits.
+af2_status validate_attention(af2_ctx *ctx, const af2_attention_shape *shape, int pair_bias, int64_t weight_count,
+                              double epsilon) {
+  if (!shape) return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "shape is NULL");
+  if (!positive_safe(shape->batch) || !positive_safe(shape->queries) || !positive_safe(shape->channels) ||
+      !positive_safe(shape->heads))
+    return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "attention dimensions must be positive safe integers");
+  if (shape->channels % shape->heads != 0 || shape->channels / shape->heads > 32)
+    return fail(ctx, AF2_ERR_INVALID_ARGUMENT,
+                "the fused WebGPU attention path requires an integral head dimension no larger than 32");
+  if (pair_bias != AF2_PAIR_BIAS_NONE && pair_bias != AF2_PAIR_BIAS_NORMALIZED_INPUT)
+    return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "pair_bias must be AF2_PAIR_BIAS_NONE or AF2_PAIR_BIAS_NORMALIZED_INPUT");
+  if ((double)shape->batch * (double)shape->queries * (double)shape->channels > (double)kMaxSafeInteger)
+    return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "tensor dimensions exceed JavaScript's safe integer range");
+  const int64_t expected = af2_attention_weight_count(shape, pair_bias);
+  if (weight_count != expected)
+    return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "packed weights have " + std::to_string(weight_count) +
+                                                   " values; expected " + std::to_string(expected));
+  if (!(epsilon > 0) || !std::isfinite(epsilon))
+    return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "epsilon must be finite and positive; received " +
+                                                   std::to_string(epsilon));
+  if (shape->channels / shape->heads != 32)
+    return fail(ctx, AF2_ERR_UNSUPPORTED, "the sm_100a attention kernel is built for a head dimension of 32");
+  if (shape->channels > 256) return fail(ctx, AF2_ERR_UNSUPPORTED, "attention channels above 256 are not supported");
+  if (pair_bias == AF2_PAIR_BIAS_NORMALIZED_INPUT && shape->batch != shape->queries)
+    return fail(ctx, AF2_ERR_UNSUPPORTED, "a normalized-input pair bias needs batch == queries (triangle attention)");
+  if (shape->queries > (int64_t(1) << 20) || shape->batch > (int64_t(1) << 20) ||
+      shape->batch * shape->queries > (int64_t(1) << 31))
+    return fail(ctx, AF2_ERR_UNSUPPORTED, "attention beyond 2^31 rows is not supported");
+  return AF2_OK;
+}
+}  // namespace
+}  // namespace af2
+
+extern "C" {
+
+af2_status af2_attention_check(const af2_attention_shape *shape, int pair_bias, int64_t weight_count, double epsilon,
+                               char *message, size_t capacity) {
+  af2_ctx scratch;
+  const af2_status st = validate_attention(&scratch, shape, pair_bias, weight_count, epsilon);
+  if (message && capacity > 0) {
+    std::strncpy(message, scratch.last_error.c_str(), capacity - 1);
+    message[capacity - 1] = '\0';
+  }
+  return st;
+}
+
+af2_status af2_attention_workspace_bytes(const af2_attention_shape *shape, int pair_bias, uint64_t *bytes) {
+  if (!shape || !bytes) return AF2_ERR_INVALID_ARGUMENT;
+  af2_ctx scratch;
+  if (validate_attention(&scratch, shape, pair_bias, af2_attention_weight_count(shape, pair_bias), 1e-5) != AF2_OK)
+    return AF2_ERR_INVALID_ARGUMENT;
+  *bytes = attention_layout(shape->batch, shape->queries, shape->channels, shape->heads,
+                            pair_bias == AF2_PAIR_BIAS_NORMALIZED_INPUT)
+               .total;
+  return AF2_OK;
+}
+
+af2_status af2_attention(af2_ctx *ctx, const af2_attention_shape *shape, const void *x, int x_dtype, const float *mask,
+                         const float *packed_weights, int64_t weight_count, double epsilon,
+                         const af2_attention_options *options, void *out, int out_dtype, void *workspace,
+                         void *stream) {
+  if (!ctx) return AF2_ERR_INVALID_ARGUMENT;
+  const int pair_bias = options ? options->pair_bias : AF2_PAIR_BIAS_NONE;
+  af2_status st = validate_attention(ctx, shape, pair_bias, weight_count, epsilon);
+  if (st != AF2_OK) return st;
+  if (!x || !mask || !packed_weights || !out) return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "a tensor pointer is NULL");
+  if (!valid_dtype(x_dtype) || !valid_dtype(out_dtype))
+    return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "dtype must be AF2_F32, AF2_F16 or AF2_BF16");
+  cudaSetDevice(ctx->device);
+  const AttentionLayout L = attention_layout(shape->batch, shape->queries, shape->channels, shape->heads,
+                                             pair_bias == AF2_PAIR_BIAS_NORMALIZED_INPUT);
+  void *ws = workspace;
+  if (!ws) {
+    if ((st = ensure(ctx, ctx->workspace, L.total, "attention scratch")) != AF2_OK) return st;
+    ws = ctx->workspace.ptr;
+  } else if (reinterpret_cast<uintptr_t>(ws) % 256 != 0) {
+    return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "workspace must be 256-byte aligned");
+  }
+  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+  return attention_launch(ctx, L, options ? options->transpose : 0, x, x_dtype, mask, packed_weights, epsilon,
+                          options ? options->residual : 0, out, out_dtype, ws, s);
+}
+
+af2_status af2_attention_host(af2_ctx *ctx, const af2_attention_shape *shape, const float *x, const float *mask,
+                              const float *packed_weights, int64_t weight_count, double epsilon,
+                              const af2_attention_options *options, float *out, af2_op_stats *stats) {
+  if (!ctx) return AF2_ERR_INVALID_ARGUMENT;
+  const int pair_bias = options ? options->pair_bias : AF2_PAIR_BIAS_NONE;
+  af2_status st = validate_attention(ctx, shape, pair_bias, weight_count, epsilon);
+  if (st != AF2_OK) return st;
+  if (!x || !mask || !packed_weights || !out) return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "a tensor pointer is NULL");
+  cudaSetDevice(ctx->device);
+  const auto t0 = std::chrono::steady_clock::now();
+  const size_t rows = (size_t)shape->batch * shape->queries;
+  const size_t x_bytes = rows * shape->channels * sizeof(float), mask_bytes = rows * sizeof(float),
+               w_bytes = (size_t)weight_count * sizeof(float);
+  if ((st = ensure(ctx, ctx->staging[0], x_bytes, "x upload")) != AF2_OK ||
+      (st = ensure(ctx, ctx->staging[1], mask_bytes, "mask upload")) != AF2_OK ||
+      (st = ensure(ctx, ctx->staging[2], w_bytes, "weight upload")) != AF2_OK ||
+      (st = ensure(ctx, ctx->staging[3], x_bytes, "output")) != AF2_OK)
+    return st;
+  const AttentionLayout L = attention_layout(shape->batch, shape->queries, shape->channels, shape->heads,
+                                             pair_bias == AF2_PAIR_BIAS_NORMALIZED_INPUT);
+  if ((st = ensure(ctx, ctx->workspace, L.total, "attention scratch")) != AF2_OK) return st;
+  cudaStream_t s = ctx->stream;
+  const int residual = options ? options->residual : 0;
+  cudaError_t e;
+  if ((e = cudaMemcpyAsync(ctx->staging[0].ptr, x, x_bytes, cudaMemcpyHostToDevice, s)) != cudaSuccess ||
+      (e = cudaMemcpyAsync(ctx->staging[1].ptr, mask, mask_bytes, cudaMemcpyHostToDevice, s)) != cudaSuccess ||
+      (e = cudaMemcpyAsync(ctx->staging[2].ptr, packed_weights, w_bytes, cudaMemcpyHostToDevice, s)) != cudaSuccess)
+    return cuda_fail(ctx, e, "upload inputs");
+  if (residual &&
+      (e = cudaMemcpyAsync(ctx->staging[3].ptr, ctx->staging[0].ptr, x_bytes, cudaMemcpyDeviceToDevice, s)) !=
+          cudaSuccess)
+    return cuda_fail(ctx, e, "seed residual output");
+  cudaEventRecord(ctx->ev_start, s);
+  st = attention_launch(ctx, L, options ? options->transpose : 0, ctx->staging[0].ptr, AF2_F32,
+                        static_cast<const float *>(ctx->staging[1].ptr), static_cast<const float *>(ctx->staging[2].ptr),
+                        epsilon, residual, ctx->staging[3].ptr, AF2_F32, ctx->workspace.ptr, s);
+  if (st != AF2_OK) return st;
+  cudaEventRecord(ctx->ev_stop, s);
+  if ((e = cudaMemcpyAsync(out, ctx->staging[3].ptr, x_bytes, cudaMemcpyDeviceToHost, s)) != cudaSuccess)
+    return cuda_fail(ctx, e, "read back output");
+  if ((e = cudaStreamSynchronize(s)) != cudaSuccess) return cuda_fail(ctx, e, "attention");
+  if ((st = check_device_errors(ctx)) != AF2_OK) return st;
+  if (stats) {
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, ctx->ev_start, ctx->ev_stop);
+    const double r = (double)rows, c = (double)shape->channels, h = (double)shape->heads,
+                 q = (double)shape->queries;
+    stats->device_milliseconds = ms;
+    stats->host_milliseconds =
+        std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+    // kernel-cost.ts:79-92: project gemm(rows, C, 4C), flash 2 gemm(rows H, 32, Q), output gemm(rows, C, C),
+    // pair bias gemm(rows, C, H)
+    stats->flops = 2 * r * c * 4 * c + 4 * r * h * 32 * q + 2 * r * c * c +
+                   (pair_bias == AF2_PAIR_BIAS_NORMALIZED_INPUT ? 2 * r * c * h : 0);
     stats->workspace_bytes = L.total;
     stats->peak_bytes = ctx->peak;
   }

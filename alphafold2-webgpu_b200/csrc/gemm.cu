@@ -39,19 +39,27 @@ struct LinearArgs {
   const float *row_mask;      // OPM projection: mask per row
   void *out;                  // LINEAR: [rows][ldo] of OT
   __half *left, *right;       // OPM projection: [rows][half_cols] each
+  int64_t split_left, split_right;  // OPM projection, f32 mode: element distance of the split blocks (0: off)
   int64_t kmajor_rows, kmajor_seqs, seq_pitch;  // seq_pitch > 0: rows m = i * seqs + s, outputs sequence-contiguous
   int64_t rows, ldo;
   int cols, half_cols, k_blocks, tiles_m, tiles_n, total_tiles, bn;
   int relu, residual;
   int vector_out;  // out rows are 16-byte aligned: whole 32-column chunks use vector access
   int tma_out;     // f16 output, no residual: each warp stages 32 x 32 blocks and stores them by TMA
+  // LINEAR: with transpose_q > 0 row m = b * transpose_q + q is written to row q * transpose_b + b
+  // (the attention output of a transposed view goes back to its source row)
+  int64_t transpose_q, transpose_b;
+  // ATTENTION projection: columns [q | k | v | g | bias] of width C, C, C, C, heads; rows m = b * queries + j
+  __half *att_q, *att_k, *att_vt, *att_g, *att_bias;
+  int64_t att_queries, att_pitch;  // key pitch of the transposed values and of the bias rows
+  int att_c, att_heads;
   unsigned int *err;
 };
 
 // Per epilogue warp: one 32-row x 32-column f16 staging block for the TMA-stored output.
 constexpr uint32_t OUT_STAGE_BYTES = 32 * 64;
 
-enum { kModeLinear = 0, kModeOpmProjection = 1 };
+enum { kModeLinear = 0, kModeOpmProjection = 1, kModeAttentionProjection = 2 };
 
 template <typename OT, int MODE>
 __global__ void __launch_bounds__(THREADS, 1)
@@ -168,6 +176,12 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * 256;
       float rs = 1.f;
       if (MODE == kModeLinear && p.row_scale && row_ok) rs = p.row_scale[m];
+      // LINEAR with a transposed view: the row of the source this output row belongs to
+      int64_t m_out = m;
+      if (MODE == kModeLinear && p.transpose_q > 0) {
+        const int64_t tb = m / p.transpose_q;
+        m_out = (m - tb * p.transpose_q) * p.transpose_b + tb;
+      }
       if (MODE == kModeOpmProjection && row_ok) rs = p.row_mask[m];
       for (int chunk = half; chunk < p.bn / 32; chunk += 2) {
         uint32_t v[32];
@@ -227,6 +241,39 @@ __global__ void __launch_bounds__(THREADS, 1)
           y[4 * i4 + 2] = fmaf(__uint_as_float(v[4 * i4 + 2]), s4.z, b4.z);
           y[4 * i4 + 3] = fmaf(__uint_as_float(v[4 * i4 + 3]), s4.w, b4.w);
         }
+        if (MODE == kModeAttentionProjection) {
+          // gated attention projections of row m = (b, j) (src/evoformer/attention.ts:497-566 and the
+          // pair-bias projection :631-661): q, k -> [b][h][j][32]; v -> transposed [b][h][32][j];
+          // g = sigmoid(.) -> [m][C]; bias -> [h][b][j].  The scales carry log2(e) / sqrt(d) for q
+          // and log2(e) for the bias, so the flash kernel works in base 2.
+          const int C = p.att_c, part = c0 / C, cc = c0 - part * C, h = cc >> 5;
+          const int64_t b = m / p.att_queries, j = m - b * p.att_queries;
+          const int64_t bh = b * p.att_heads + h;
+          if (part <= 1 || part == 3) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              float y0 = y[2 * i], y1 = y[2 * i + 1];
+              if (part == 3) y0 = sigmoidf(y0), y1 = sigmoidf(y1);
+              pk[i] = pack_half2(y0, y1);
+            }
+            __half *dst = part == 0   ? p.att_q + (bh * p.att_queries + j) * 32
+                          : part == 1 ? p.att_k + (bh * p.att_queries + j) * 32
+                                      : p.att_g + m * C + cc;
+            uint4 *d4 = reinterpret_cast<uint4 *>(dst);
+#pragma unroll
+            for (int w = 0; w < 4; ++w) d4[w] = make_uint4(pk[4 * w], pk[4 * w + 1], pk[4 * w + 2], pk[4 * w + 3]);
+          } else if (part == 2) {
+            // the lanes of a warp hold consecutive keys j: each store covers 64 contiguous bytes
+            __half *dst = p.att_vt + bh * 32 * p.att_pitch + j;
+#pragma unroll
+            for (int d = 0; d < 32; ++d) dst[d * p.att_pitch] = __float2half_rn(y[d]);
+          } else if (part == 4 && cc == 0 && p.att_bias) {
+            for (int hh = 0; hh < p.att_heads; ++hh)
+              p.att_bias[(static_cast<int64_t>(hh) * p.att_queries + b) * p.att_pitch + j] = __float2half_rn(y[hh]);
+          }
+          continue;
+        }
         if (MODE == kModeOpmProjection) {
           // columns [0, half) -> left, [half, 2 half) -> right, both scaled by the mask;
           // half is 32, so a chunk is one whole left or right row: 4 x 16-byte stores.
@@ -242,15 +289,39 @@ __global__ void __launch_bounds__(THREADS, 1)
             for (int k = 0; k < 32; ++k) dst[k * stride] = __float2half_rn(y[k] * rs);
             continue;
           }
-          __half *dst = (c0 < p.half_cols ? p.left : p.right) + m * p.half_cols;
+          const bool is_left = c0 < p.half_cols;
+          __half *dst = (is_left ? p.left : p.right) + m * p.half_cols;
           uint32_t pk[16];
+          if (p.split_left) {
+            // f32 precision mode: hi = f16(v), lo = f16(v - hi); left blocks (hi, hi, lo), right (hi, lo, hi)
+            uint32_t lo[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const float v0 = y[2 * i] * rs, v1 = y[2 * i + 1] * rs;
+              const __half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
+              pk[i] = pack_half2(__half2float(h0), __half2float(h1));
+              lo[i] = pack_half2(v0 - __half2float(h0), v1 - __half2float(h1));
+            }
+            const int64_t stride = is_left ? p.split_left : p.split_right;
+            uint4 *b0 = reinterpret_cast<uint4 *>(dst), *b1 = reinterpret_cast<uint4 *>(dst + stride),
+                  *b2 = reinterpret_cast<uint4 *>(dst + 2 * stride);
+#pragma unroll
+            for (int w = 0; w < 4; ++w) {
+              const uint4 hv = make_uint4(pk[4 * w], pk[4 * w + 1], pk[4 * w + 2], pk[4 * w + 3]);
+              const uint4 lv = make_uint4(lo[4 * w], lo[4 * w + 1], lo[4 * w + 2], lo[4 * w + 3]);
+              b0[w] = hv;
+              b1[w] = is_left ? hv : lv;
+              b2[w] = is_left ? lv : hv;
+            }
+            continue;
+          }
 #pragma unroll
           for (int i = 0; i < 16; ++i) pk[i] = pack_half2(y[2 * i] * rs, y[2 * i + 1] * rs);
           uint4 *d4 = reinterpret_cast<uint4 *>(dst);
 #pragma unroll
           for (int w = 0; w < 4; ++w) d4[w] = make_uint4(pk[4 * w], pk[4 * w + 1], pk[4 * w + 2], pk[4 * w + 3]);
         } else {
-          OT *orow = static_cast<OT *>(p.out) + m * p.ldo;
+          OT *orow = static_cast<OT *>(p.out) + m_out * p.ldo;
 #pragma unroll
           for (int i = 0; i < 32; ++i) y[i] = (p.relu ? fmaxf(y[i], 0.f) : y[i]) * rs;
           store_out32<OT>(orow, c0, p.cols, y, p.vector_out, p.residual);
@@ -299,7 +370,7 @@ __device__ __forceinline__ float element(const MatrixDev &m, int64_t i) {
 
 struct PrepJobDev {
   MatrixDev m;
-  int inner, cols, inner_pad, cols_pad, row0, rows_total;
+  int inner, cols, inner_pad, cols_pad, row0, rows_total, part;
   float extra_scale;
   __half *out;
   float *scale_out;
@@ -358,7 +429,8 @@ __device__ __forceinline__ void prep_chunk(const PrepJobDev &jb) {
     float w = 0.f;
     if (o < jb.cols && k < jb.inner)
       w = element<FMT>(jb.m, static_cast<int64_t>(k) * jb.cols + o) * (jb.row_scale ? jb.row_scale[k] : 1.f) * inv;
-    stage[lane][k - k0] = __float2half_rn(w);
+    const __half hw = __float2half_rn(w);
+    stage[lane][k - k0] = jb.part ? __float2half_rn(w - __half2float(hw)) : hw;
   }
   __syncthreads();
   const int kblocks = (kend - k0) >> 6;  // inner_pad is a multiple of 64
@@ -418,7 +490,7 @@ af2_status prepare_matrices(af2_ctx *ctx, const PrepJob *jobs, int count, cudaSt
     const PrepJob &j = jobs[i];
     b.job[i] = PrepJobDev{MatrixDev{j.w.format, j.w.block, j.w.values, j.w.scales},
                           (int)j.inner, (int)j.cols, (int)j.inner_pad, (int)j.cols_pad, (int)j.row0,
-                          (int)(j.rows_total ? j.rows_total : j.cols_pad), j.extra_scale,
+                          (int)(j.rows_total ? j.rows_total : j.cols_pad), j.part, j.extra_scale,
                           static_cast<__half *>(j.out), j.scale_out, j.row_scale};
     gx = std::max(gx, (unsigned)((j.cols_pad + 31) / 32));
     gy = std::max(gy, (unsigned)((j.inner_pad + PREP_CHUNK - 1) / PREP_CHUNK));
@@ -490,7 +562,7 @@ af2_status launch_linear_t(af2_ctx *ctx, const CUtensorMap &amap, const CUtensor
 
 af2_status linear_launch(af2_ctx *ctx, const LinearOperands &op, cudaStream_t stream) {
   const int64_t k_pad = align_up(op.inner, 64);
-  const int bn = op.cols >= 256 ? 256 : (int)align_up(op.cols, 64);
+  const int bn = op.bn > 0 ? op.bn : op.cols >= 256 ? 256 : (int)align_up(op.cols, 64);
   const int64_t cols_pad = align_up(op.cols, bn);
   CUtensorMap amap, bmap;
   // A: f16 rows of pitch lda; K past `inner` reads as zero (TMA fill), matching the zero-padded W rows.
@@ -507,6 +579,8 @@ af2_status linear_launch(af2_ctx *ctx, const LinearOperands &op, cudaStream_t st
   a.out = op.out;
   a.left = static_cast<__half *>(op.left);
   a.right = static_cast<__half *>(op.right);
+  a.split_left = op.split_stride_left;
+  a.split_right = op.split_stride_right;
   a.kmajor_rows = op.kmajor_rows;
   a.kmajor_seqs = op.kmajor_seqs;
   a.seq_pitch = op.seq_pitch;
@@ -521,6 +595,20 @@ af2_status linear_launch(af2_ctx *ctx, const LinearOperands &op, cudaStream_t st
   a.bn = bn;
   a.relu = op.relu;
   a.residual = op.residual;
+  a.transpose_q = op.transpose_q;
+  a.transpose_b = op.transpose_b;
+  const bool attention = op.attention != nullptr;
+  if (attention) {
+    a.att_q = static_cast<__half *>(op.attention->q);
+    a.att_k = static_cast<__half *>(op.attention->k);
+    a.att_vt = static_cast<__half *>(op.attention->vt);
+    a.att_g = static_cast<__half *>(op.attention->g);
+    a.att_bias = static_cast<__half *>(op.attention->bias);
+    a.att_queries = op.attention->queries;
+    a.att_pitch = op.attention->pitch;
+    a.att_c = (int)op.attention->channels;
+    a.att_heads = (int)op.attention->heads;
+  }
   {
     const size_t ob = op.out_dtype == AF2_F32 ? 4 : 2;
     a.vector_out = !op.opm_projection && reinterpret_cast<uintptr_t>(op.out) % 16 == 0 && (op.ldo * ob) % 16 == 0;
@@ -529,12 +617,14 @@ af2_status linear_launch(af2_ctx *ctx, const LinearOperands &op, cudaStream_t st
   // f16 outputs without a residual leave through staged TMA stores: [rows][ldo], one box = 32 x 32
   CUtensorMap omap;
   std::memset(&omap, 0, sizeof omap);
-  a.tma_out = !op.opm_projection && op.out_dtype == AF2_F16 && !op.residual && a.vector_out;
+  a.tma_out = !op.opm_projection && !attention && op.out_dtype == AF2_F16 && !op.residual && a.vector_out &&
+              op.transpose_q == 0;
   if (a.tma_out && !encode_map_3d(&omap, f16map(), op.out, op.cols, op.rows, 1, op.ldo * 2,
                                   (uint64_t)op.rows * op.ldo * 2, 32, 32, 1, CU_TENSOR_MAP_SWIZZLE_NONE))
     return fail(ctx, AF2_ERR_CUDA, "cuTensorMapEncodeTiled failed for a linear layer's output");
   if (op.opm_projection)
     return launch_linear_t<__half, kModeOpmProjection>(ctx, amap, bmap, omap, a, op.prof, stream);
+  if (attention) return launch_linear_t<__half, kModeAttentionProjection>(ctx, amap, bmap, omap, a, op.prof, stream);
   if (op.out_dtype == AF2_F16) return launch_linear_t<__half, kModeLinear>(ctx, amap, bmap, omap, a, op.prof, stream);
   if (op.out_dtype == AF2_BF16)
     return launch_linear_t<__nv_bfloat16, kModeLinear>(ctx, amap, bmap, omap, a, op.prof, stream);

@@ -50,7 +50,10 @@ constexpr int C = 32;  // outer channels c: the outer tile maps 32 channels to 3
 template <typename MT, bool VEC>
 __global__ void norm_kernel(const MT *__restrict__ m, int64_t rows, int cm, int cmp, const float *__restrict__ gamma,
                             const float *__restrict__ beta, float eps, __half *__restrict__ xn, int n_full, int col0,
-                            int cols, int seqs, const float *__restrict__ mask_in, float *__restrict__ mask_out) {
+                            int cols, int seqs, const float *__restrict__ mask_in, float *__restrict__ mask_out,
+                            int split) {
+  // split (f32 precision mode): rows of 3 cmp, [f16(v) | f16(v) | f16(v - f16(v))], the A operand of a
+  // projection whose weights are stacked [W_hi; W_lo; W_hi]
   // local row of the residue columns [col0, col0 + cols) of an [S][n_full] MSA:
   // row = s * cols + j, or with seqs > 0 (residue-major order) row = j * seqs + s
   const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -95,18 +98,36 @@ __global__ void norm_kernel(const MT *__restrict__ m, int64_t rows, int cm, int 
     const float4 b0 = reinterpret_cast<const float4 *>(beta)[2 * lane], b1 = reinterpret_cast<const float4 *>(beta)[2 * lane + 1];
     const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
     const float b[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
-    uint32_t pk[4];
+    uint32_t pk[4], lo[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
-      pk[i] = pack_half2((v[2 * i] - mean) * rstd * g[2 * i] + b[2 * i],
-                         (v[2 * i + 1] - mean) * rstd * g[2 * i + 1] + b[2 * i + 1]);
-    reinterpret_cast<uint4 *>(xn + row * cmp)[lane] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+    for (int i = 0; i < 4; ++i) {
+      const float y0 = (v[2 * i] - mean) * rstd * g[2 * i] + b[2 * i];
+      const float y1 = (v[2 * i + 1] - mean) * rstd * g[2 * i + 1] + b[2 * i + 1];
+      pk[i] = pack_half2(y0, y1);
+      const __half2 h = *reinterpret_cast<const __half2 *>(&pk[i]);
+      lo[i] = pack_half2(y0 - __low2float(h), y1 - __high2float(h));
+    }
+    const int64_t pitch = split ? 3 * cmp : cmp;
+    const uint4 hv = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+    reinterpret_cast<uint4 *>(xn + row * pitch)[lane] = hv;
+    if (split) {
+      reinterpret_cast<uint4 *>(xn + row * pitch + cmp)[lane] = hv;
+      reinterpret_cast<uint4 *>(xn + row * pitch + 2 * cmp)[lane] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    }
   } else {
+    const int64_t pitch = split ? 3 * cmp : cmp;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const int ch = lane + 32 * i;
-      if (ch < cmp)
-        xn[row * cmp + ch] = __float2half_rn(ch < cm ? (v[i] - mean) * rstd * gamma[ch] + beta[ch] : 0.f);
+      if (ch < cmp) {
+        const float y = ch < cm ? (v[i] - mean) * rstd * gamma[ch] + beta[ch] : 0.f;
+        const __half h = __float2half_rn(y);
+        xn[row * pitch + ch] = h;
+        if (split) {
+          xn[row * pitch + cmp + ch] = h;
+          xn[row * pitch + 2 * cmp + ch] = __float2half_rn(y - __half2float(h));
+        }
+      }
     }
   }
 }
@@ -443,10 +464,11 @@ constexpr uint32_t OOFF_BAR = OSTAGES * OSTAGE;
 constexpr uint32_t OSMEM = OOFF_BAR + 256 + 1024;
 
 struct OuterArgs {
-  __half *outer;  // [(i - i_begin) * n + j][1024]
+  __half *outer;  // [(i - i_begin) * n + j][1024], or [..][3 * 1024] when split
   int n, i_begin, i_count, tiles_j, k_blocks, total_tiles;
   int rows_b;     // residues per block of the right operand ([blocks][S][rows_b][c]): n unless sharded
   float scale;
+  int split;  // f32 precision mode: rows [f16(v) | f16(v) | f16(v - f16(v))] for the K-tripled output GEMM
   unsigned int *err;
 };
 
@@ -569,10 +591,26 @@ __global__ void __launch_bounds__(OTHREADS, 1)
 #pragma unroll
         for (int c = 0; c < 32; c += 2)
           pk[c >> 1] = pack_half2(__uint_as_float(v[c]) * p.scale, __uint_as_float(v[c + 1]) * p.scale);
-        uint4 *dst = reinterpret_cast<uint4 *>(p.outer + (static_cast<int64_t>(i - p.i_begin) * p.n + j) * (C * C) +
+        const int64_t pitch = p.split ? 3 * C * C : C * C;
+        uint4 *dst = reinterpret_cast<uint4 *>(p.outer + (static_cast<int64_t>(i - p.i_begin) * p.n + j) * pitch +
                                               lane * C);
 #pragma unroll
         for (int w = 0; w < 4; ++w) dst[w] = make_uint4(pk[4 * w], pk[4 * w + 1], pk[4 * w + 2], pk[4 * w + 3]);
+        if (p.split) {
+          uint32_t lo[16];
+#pragma unroll
+          for (int c = 0; c < 32; c += 2) {
+            const __half2 h = *reinterpret_cast<const __half2 *>(&pk[c >> 1]);
+            lo[c >> 1] = pack_half2(__uint_as_float(v[c]) * p.scale - __low2float(h),
+                                    __uint_as_float(v[c + 1]) * p.scale - __high2float(h));
+          }
+          uint4 *d1 = dst + (C * C) / 8, *d2 = dst + (2 * C * C) / 8;
+#pragma unroll
+          for (int w = 0; w < 4; ++w) {
+            d1[w] = make_uint4(pk[4 * w], pk[4 * w + 1], pk[4 * w + 2], pk[4 * w + 3]);
+            d2[w] = make_uint4(lo[4 * w], lo[4 * w + 1], lo[4 * w + 2], lo[4 * w + 3]);
+          }
+        }
       }
       tc_fence_before();
       __syncwarp();
@@ -964,8 +1002,11 @@ __global__ void __launch_bounds__(FTHREADS, 1)
 using namespace opm;
 
 OpmLayout opm_layout(int64_t s, int64_t n, int64_t cm, int64_t c, int64_t cz, int64_t row_block, int64_t rows,
-                     int64_t row0) {
+                     int64_t row0, bool split) {
   OpmLayout L;
+  // f32 precision mode: every operand an f16 hi / lo pair, each GEMM's K tripled (hi hi + hi lo + lo hi)
+  L.split = split;
+  const int64_t kx = split ? 3 : 1;
   L.s = s;
   L.n = n;
   L.rows = (rows <= 0 || rows > n) ? n : rows;
@@ -975,7 +1016,7 @@ OpmLayout opm_layout(int64_t s, int64_t n, int64_t cm, int64_t c, int64_t cz, in
   L.cz = cz;
   L.cmp = align_up(cm, 64);
   // Residue block: the outer scratch stays within 256 MiB unless asked otherwise; a multiple of 4.
-  int64_t rb = row_block > 0 ? row_block : std::max<int64_t>(4, (int64_t(256) << 20) / (n * c * c * 2));
+  int64_t rb = row_block > 0 ? row_block : std::max<int64_t>(4, (int64_t(256) << 20) / (n * c * c * 2 * kx));
   rb = std::min<int64_t>(align_up(std::max<int64_t>(rb, 1), 4), align_up(L.rows, 4));
   L.block_rows = rb;
   int k = 0;
@@ -983,7 +1024,7 @@ OpmLayout opm_layout(int64_t s, int64_t n, int64_t cm, int64_t c, int64_t cz, in
   L.out_shift = k;
   // One kernel for the outer products and the output projection when the
   // right operand of a tile fits in shared memory and c_z in one MMA.
-  L.fused = c == C && align_up(s, 64) / 64 <= kFusedMaxKBlocks && cz <= 128;
+  L.fused = !split && c == C && align_up(s, 64) / 64 <= kFusedMaxKBlocks && cz <= 128;
   L.seq_pitch = L.fused ? align_up(s, 8) : 0;
   const int64_t lr_cols = linear_cols_pad(2 * c), o_cols = linear_cols_pad(cz), o_inner = align_up(c * c, 64);
   size_t off = 0;
@@ -992,20 +1033,20 @@ OpmLayout opm_layout(int64_t s, int64_t n, int64_t cm, int64_t c, int64_t cz, in
     off = align_up(off + bytes, 256);
     return at;
   };
-  L.off_wlr = take((size_t)L.cmp * lr_cols * 2);
+  L.off_wlr = take((size_t)kx * L.cmp * lr_cols * 2);
   L.off_wlr_scale = take((size_t)lr_cols * 4);
   L.off_wlr_bias = take((size_t)lr_cols * 4);
-  L.off_wo = take((size_t)o_inner * o_cols * 2);
+  L.off_wo = take((size_t)kx * o_inner * o_cols * 2);
   L.off_wo_scale = take((size_t)o_cols * 4);
   L.off_wo_bias = take((size_t)o_cols * 4);
   L.off_ln = take((size_t)L.cmp * 2 * 4);
-  L.off_xn = take((size_t)s * L.rows * L.cmp * 2);
+  L.off_xn = take((size_t)kx * s * L.rows * L.cmp * 2);
   L.off_mask = take((size_t)s * L.rows * 4);
   const int64_t seq_span = L.fused ? L.seq_pitch : s;
-  L.off_left = take((size_t)seq_span * c * L.rows * 2);
-  L.off_right = take((size_t)seq_span * n * c * 2);  // every rank's block: [ranks][S][rows][c], or [n][c][pitch]
+  L.off_left = take((size_t)kx * seq_span * c * L.rows * 2);
+  L.off_right = take((size_t)kx * seq_span * n * c * 2);  // every rank's block: [ranks][S][rows][c], or [n][c][pitch]
   L.off_rowscale = take((size_t)L.rows * n * 4);
-  L.off_outer = take(L.fused ? 0 : (size_t)rb * n * c * c * 2);
+  L.off_outer = take(L.fused ? 0 : (size_t)kx * rb * n * c * c * 2);
   L.total = off;
   return L;
 }
@@ -1097,6 +1138,7 @@ af2_status opm_launch(af2_ctx *ctx, const OpmLayout &L, const void *m, int m_dty
   // into the projection's weights and biases)
   const bool lnproj = L.fused && m_dtype != AF2_F32 && cm % 8 == 0 && L.cmp <= 256 &&
                       reinterpret_cast<uintptr_t>(m) % 16 == 0;
+  const int64_t kx = L.split ? 3 : 1;
   // ---- weights ----
   const af2_matrix left_m{AF2_WEIGHTS_F32, 0, lw, nullptr}, right_m{AF2_WEIGHTS_F32, 0, rw, nullptr};
   const af2_matrix out_m{AF2_WEIGHTS_F32, 0, ow, nullptr};
@@ -1108,12 +1150,27 @@ af2_status opm_launch(af2_ctx *ctx, const OpmLayout &L, const void *m, int m_dty
   vs.add(ln_b, cm, L.cmp, ln + L.cmp);
   if (lr_cols > 2 * c) vs.add(nullptr, 0, lr_cols - 2 * c, wlr_scale + 2 * c);
   const float *fold = lnproj ? ln_w : nullptr;
-  const PrepJob jobs[3] = {
-      {left_m, cm, c, L.cmp, c, 1.f, ws + L.off_wlr, wlr_scale, 0, lr_cols, fold},
-      {right_m, cm, c, L.cmp, c, 1.f, ws + L.off_wlr, wlr_scale, c, lr_cols, fold},
-      {out_m, c * c, cz, o_inner, o_cols, std::ldexp(1.f, L.out_shift), ws + L.off_wo, wo_scale, 0, 0}};
-  if ((st = prepare_matrices(ctx, jobs, 3, stream)) != AF2_OK || (st = pad_vectors(ctx, vs, stream)) != AF2_OK)
-    return st;
+  if (!L.split) {
+    const PrepJob jobs[3] = {
+        {left_m, cm, c, L.cmp, c, 1.f, ws + L.off_wlr, wlr_scale, 0, lr_cols, fold},
+        {right_m, cm, c, L.cmp, c, 1.f, ws + L.off_wlr, wlr_scale, c, lr_cols, fold},
+        {out_m, c * c, cz, o_inner, o_cols, std::ldexp(1.f, L.out_shift), ws + L.off_wo, wo_scale, 0, 0}};
+    if ((st = prepare_matrices(ctx, jobs, 3, stream)) != AF2_OK) return st;
+  } else {
+    // K-tripled weights [W_hi; W_lo; W_hi] against the operands [hi | hi | lo] (norm and outer kernels)
+    const int part[3] = {0, 1, 0};
+    PrepJob lr[6], wo[3];
+    for (int g = 0; g < 3; ++g) {
+      uint8_t *seg = ws + L.off_wlr + (size_t)g * L.cmp * lr_cols * 2;
+      lr[2 * g] = PrepJob{left_m, cm, c, L.cmp, c, 1.f, seg, wlr_scale, 0, lr_cols, nullptr, part[g]};
+      lr[2 * g + 1] = PrepJob{right_m, cm, c, L.cmp, c, 1.f, seg, wlr_scale, c, lr_cols, nullptr, part[g]};
+      wo[g] = PrepJob{out_m, c * c, cz, o_inner, o_cols, std::ldexp(1.f, L.out_shift),
+                      ws + L.off_wo + (size_t)g * o_inner * o_cols * 2, wo_scale, 0, 0, nullptr, part[g]};
+    }
+    if ((st = prepare_matrices(ctx, lr, 6, stream)) != AF2_OK || (st = prepare_matrices(ctx, wo, 3, stream)) != AF2_OK)
+      return st;
+  }
+  if ((st = pad_vectors(ctx, vs, stream)) != AF2_OK) return st;
   if (lnproj) {
     LaunchScope scope(ctx, stream, kProfPrepare);
     fold_beta_kernel<<<(unsigned)((2 * c + 7) / 8), 256, 0, stream>>>(ln_b, lw, rw, (int)cm, (int)c, wlr_bias);
@@ -1171,11 +1228,11 @@ af2_status opm_launch(af2_ctx *ctx, const OpmLayout &L, const void *m, int m_dty
       if (vec)
         norm_kernel<MT, true><<<blocks, warps * 32, 0, stream>>>(mp, xrows, (int)cm, (int)L.cmp, ln, ln + L.cmp,
                                                                  (float)ln_eps, xn, (int)n, (int)L.row0, (int)rows,
-                                                                 L.fused ? (int)s : 0, mask, mask_loc);
+                                                                 L.fused ? (int)s : 0, mask, mask_loc, L.split);
       else
         norm_kernel<MT, false><<<blocks, warps * 32, 0, stream>>>(mp, xrows, (int)cm, (int)L.cmp, ln, ln + L.cmp,
                                                                   (float)ln_eps, xn, (int)n, (int)L.row0, (int)rows,
-                                                                  L.fused ? (int)s : 0, mask, mask_loc);
+                                                                  L.fused ? (int)s : 0, mask, mask_loc, L.split);
     };
     if (m_dtype == AF2_F32)
       run(float{});
@@ -1190,9 +1247,13 @@ af2_status opm_launch(af2_ctx *ctx, const OpmLayout &L, const void *m, int m_dty
   if (!lnproj) {
     LinearOperands op;
     op.a = xn;
-    op.lda = L.cmp;
-    op.inner = L.cmp;
+    op.lda = kx * L.cmp;
+    op.inner = kx * L.cmp;
     op.w = ws + L.off_wlr;
+    if (L.split) {
+      op.split_stride_left = s * rows * c;
+      op.split_stride_right = s * n * c;
+    }
     op.scale = wlr_scale;
     op.bias = wlr_bias;
     op.row_mask = mask_loc;
@@ -1225,10 +1286,12 @@ af2_status opm_launch(af2_ctx *ctx, const OpmLayout &L, const void *m, int m_dty
   const int64_t blocks_b = n / rows;  // blocks of the right operand
   // ---- outer products and output projection, block by block of this rank's rows ----
   CUtensorMap lmap, rmap;
-  if (!encode_map_3d(&lmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, ws + L.off_left, rows * c, s, 1, rows * c * 2,
-                     (uint64_t)s * rows * c * 2, 64, 64, 1, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !encode_map_3d(&rmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, right_full, rows * c, s, blocks_b, rows * c * 2,
-                     (uint64_t)s * rows * c * 2, 64, 64, 1, CU_TENSOR_MAP_SWIZZLE_128B))
+  // the split operands are three stacked [S][rows][c] blocks: one contraction over 3 S sequences
+  const int64_t sk = kx * s;
+  if (!encode_map_3d(&lmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, ws + L.off_left, rows * c, sk, 1, rows * c * 2,
+                     (uint64_t)sk * rows * c * 2, 64, 64, 1, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_map_3d(&rmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, right_full, rows * c, sk, blocks_b, rows * c * 2,
+                     (uint64_t)sk * rows * c * 2, 64, 64, 1, CU_TENSOR_MAP_SWIZZLE_128B))
     return fail(ctx, AF2_ERR_CUDA, "cuTensorMapEncodeTiled failed for the OPM operands");
   cudaError_t e = cudaFuncSetAttribute(outer_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, OSMEM);
   if (e != cudaSuccess) return cuda_fail(ctx, e, "outer kernel attributes");
@@ -1242,7 +1305,8 @@ af2_status opm_launch(af2_ctx *ctx, const OpmLayout &L, const void *m, int m_dty
     a.i_begin = (int)i0;
     a.i_count = (int)ic;
     a.tiles_j = (int)((n + 7) / 8);
-    a.k_blocks = (int)((s + OBK - 1) / OBK);
+    a.k_blocks = (int)((sk + OBK - 1) / OBK);
+    a.split = L.split ? 1 : 0;
     a.total_tiles = (int)((ic + 3) / 4) * a.tiles_j;
     a.rows_b = (int)rows;
     a.scale = std::ldexp(1.f, -L.out_shift);
@@ -1255,8 +1319,8 @@ af2_status opm_launch(af2_ctx *ctx, const OpmLayout &L, const void *m, int m_dty
     }
     LinearOperands op;
     op.a = outer;
-    op.lda = c * c;
-    op.inner = c * c;
+    op.lda = kx * c * c;
+    op.inner = kx * c * c;
     op.w = ws + L.off_wo;
     op.scale = wo_scale;
     op.bias = wo_bias;

@@ -120,6 +120,23 @@ AF2_API uint64_t af2_launch_count(const af2_ctx *ctx);
 AF2_API af2_status af2_memory_snapshot(const af2_ctx *ctx, uint64_t *current_bytes, uint64_t *peak_bytes);
 
 /*
+ * What the GEMMs multiply in: the counterpart of the reference's installed
+ * GEMM variant (src/runtime/gemm.ts:175,208-228, whose precision is "f32" or
+ * "matrix" among others, chosen once per device).  AF2_GEMM_MATRIX (the
+ * default): f16 operands on the tcgen05 tensor cores, f32 accumulation.
+ * AF2_GEMM_F32: every operand of the outer-product mean's three GEMMs is
+ * carried as an f16 pair hi + lo (about 22 significant bits) and each
+ * product summed as hi.hi + hi.lo + lo.hi, still on the tensor cores with f32
+ * accumulation, for results within f32 rounding of the reference's f32 path
+ * (three times the tensor-core work, and the two-kernel OPM path).  The
+ * triangle multiplication, attention and transition kernels multiply f16
+ * operands in either mode.  Per context; takes effect at the next call.
+ */
+typedef enum af2_gemm_precision { AF2_GEMM_MATRIX = 0, AF2_GEMM_F32 = 1 } af2_gemm_precision;
+AF2_API af2_status af2_set_gemm_precision(af2_ctx *ctx, int precision);
+AF2_API int af2_get_gemm_precision(const af2_ctx *ctx);
+
+/*
  * Per-kernel device timing (the counterpart of the reference's timestamp-query
  * profile, src/runtime/execution.ts:482-533).  While enabled every kernel
  * launch is bracketed by CUDA events on its own stream.  af2_profile_read
@@ -374,11 +391,127 @@ AF2_API af2_status af2_outer_product_mean_host(af2_ctx *ctx, const af2_opm_shape
                                                af2_op_stats *stats);
 
 /* Device form: encodeOuterProductMean (src/evoformer/block.ts:1115-1246).  All
- * pointers on the device; workspace NULL = context-owned. */
+ * pointers on the device; workspace NULL = context-owned (required in the
+ * AF2_GEMM_F32 precision; af2_opm_workspace_bytes sizes the default one). */
 AF2_API af2_status af2_outer_product_mean(af2_ctx *ctx, const af2_opm_shape *shape, const void *m, int m_dtype,
                                           const float *mask, const float *packed_weights, int64_t weight_count,
                                           const af2_opm_options *options, void *out, int out_dtype, void *workspace,
                                           void *stream);
+
+/* ---- gated multi-head attention: triangle attention ---------------------- */
+
+/* AttentionInput's dimensions (src/evoformer/attention.ts:47-58): `batch`
+ * independent rows of `queries` positions, `channels` = heads x 32. */
+typedef struct af2_attention_shape {
+    int64_t batch;
+    int64_t queries;  /* queryLength; the keys are the same positions */
+    int64_t channels;
+    int64_t heads;
+} af2_attention_shape;
+
+/* AttentionPairBias (attention.ts:31-45): none, or "normalized-input" -- the
+ * bias of head h at (query q, key k) is LN(x)[q, k] . projectionWeight[:, h],
+ * projected from the attention's own normalised source (triangle attention,
+ * src/evoformer/block.ts:1727-1745; needs batch == queries).  The "separate"
+ * source of MSA row attention is not covered. */
+typedef enum af2_pair_bias { AF2_PAIR_BIAS_NONE = 0, AF2_PAIR_BIAS_NORMALIZED_INPUT = 1 } af2_pair_bias;
+
+typedef struct af2_attention_options {
+    /* AttentionInput.transpose: the column view (row b, position q is source
+     * row q * batch + b) -- the ending-node triangle attention. */
+    int32_t transpose;
+    int32_t pair_bias; /* af2_pair_bias */
+    /* 1: out += attention(x) (encodeAttention with residualTarget). */
+    int32_t residual;
+} af2_attention_options;
+
+/* Length of packAttentionWeights(input).data (attention.ts:179-201): queryNorm
+ * scale and offset [C], query / key / value / gating weights [C, C] ([in,
+ * out]), gating bias [C], output weight [C, C] ([in, out]), output bias [C],
+ * then for a normalized-input bias the projection weight [C, heads]. */
+AF2_API int64_t af2_attention_weight_count(const af2_attention_shape *shape, int pair_bias);
+
+/* validate (attention.ts:102-141) plus the kernels' limits (head dimension 32,
+ * channels <= 256, batch == queries for a normalized-input bias); no device needed. */
+AF2_API af2_status af2_attention_check(const af2_attention_shape *shape, int pair_bias, int64_t weight_count,
+                                       double epsilon, char *message, size_t capacity);
+
+AF2_API af2_status af2_attention_workspace_bytes(const af2_attention_shape *shape, int pair_bias, uint64_t *bytes);
+
+/*
+ * Host form of AttentionGpu.run (attention.ts:1334-1453): x [batch *
+ * queries, channels] and mask [batch * queries] are host f32 arrays in the
+ * source's row order (the transposed view reads them as the reference does);
+ * out [batch * queries, channels] f32 receives the output rows (plus x when
+ * options->residual is 1).
+ */
+AF2_API af2_status af2_attention_host(af2_ctx *ctx, const af2_attention_shape *shape, const float *x,
+                                      const float *mask, const float *packed_weights, int64_t weight_count,
+                                      double epsilon, const af2_attention_options *options, float *out,
+                                      af2_op_stats *stats);
+
+/*
+ * Device form: encodeAttention on device-resident tensors (the triangle
+ * attention calls of src/evoformer/block.ts:1727-1745).  x of x_dtype, mask
+ * f32, packed_weights f32, out of out_dtype; with options->residual = 1 the
+ * result is added into out (out == x updates the pair in place).  workspace:
+ * NULL = context-owned, else af2_attention_workspace_bytes() bytes, 256-byte aligned.
+ */
+AF2_API af2_status af2_attention(af2_ctx *ctx, const af2_attention_shape *shape, const void *x, int x_dtype,
+                                 const float *mask, const float *packed_weights, int64_t weight_count, double epsilon,
+                                 const af2_attention_options *options, void *out, int out_dtype, void *workspace,
+                                 void *stream);
+
+/* ---- the Evoformer pair block ------------------------------------------------ */
+
+/* The dimensions encodeEvoformerPairBlock reads from EvoformerShape and its
+ * weights (src/evoformer/block.ts:174-181,1753-1805). */
+typedef struct af2_pair_block_shape {
+    int64_t length;            /* N residues: pair [N, N, c_z] */
+    int64_t sequences;         /* S: MSA [S, N, c_m] */
+    int64_t c_m;
+    int64_t c_z;
+    int64_t c_outer;           /* outer-product-mean channels */
+    int64_t c_hidden;          /* triangle multiplication hidden channels */
+    int64_t pair_heads;        /* triangle attention heads (head dimension 32) */
+    int64_t transition_hidden; /* pair transition hidden channels */
+} af2_pair_block_shape;
+
+/* EvoformerPairBlockWeights (block.ts:174-181), each op's weights as its own
+ * packed f32 array (device pointers), in the orders the op entry points take:
+ * packOuterProductMeanWeights, triangle ORDER, packAttentionWeights with the
+ * normalized-input pair projection last; the pair transition as
+ * af2_transition_weights (f32 or q8 matrices). */
+typedef struct af2_pair_block_weights {
+    const float *outer_product_mean;
+    const float *triangle_outgoing;
+    const float *triangle_incoming;
+    const float *attention_starting;
+    const float *attention_ending;
+    af2_transition_weights pair_transition;
+} af2_pair_block_weights;
+
+typedef struct af2_pair_block_options {
+    /* encodeEvoformerPairBlock's includeOuterProductMean (0 skips the OPM and
+     * then msa / msa_mask may be NULL). */
+    int32_t include_outer_product_mean;
+    /* LayerNorm epsilon of every op (0 = 1e-5); the OPM's normalisation epsilon stays 1e-3. */
+    double epsilon;
+} af2_pair_block_options;
+
+/*
+ * encodeEvoformerPairBlock (src/evoformer/block.ts:1753-1805) on device
+ * tensors: the outer-product mean of the MSA, triangle multiplication
+ * outgoing and incoming, triangle attention around the starting and the
+ * ending node, and the pair transition, each added into the pair in place, in
+ * that order, on one stream.  msa [S, N, c_m] of msa_dtype, msa_mask [S, N]
+ * f32, pair [N, N, c_z] of pair_dtype, pair_mask [N, N] f32.  Scratch is the
+ * context's, sized once for the largest op.  options may be NULL.
+ */
+AF2_API af2_status af2_evoformer_pair_block(af2_ctx *ctx, const af2_pair_block_shape *shape,
+                                            const af2_pair_block_weights *weights, const void *msa, int msa_dtype,
+                                            const float *msa_mask, void *pair, int pair_dtype, const float *pair_mask,
+                                            const af2_pair_block_options *options, void *stream);
 
 /* ---- the shared dense projection ----------------------------------------- */
 

@@ -227,3 +227,40 @@ def test_opm_fused_workspace_has_no_outer_scratch():
     fused = af2cuda.opm_workspace_bytes(512, 768, 256, 32, 128)
     assert fused == af2cuda.opm_workspace_bytes(512, 768, 256, 32, 128, row_block=4)
     assert fused < 768 * 768 * 32 * 32 * 2 // 4
+
+
+def _attention_check(b, q, c, h, bias=1, count=None, eps=1e-5):
+    shape = _lib.AttentionShape(b, q, c, h)
+    if count is None:
+        count = _lib.lib().af2_attention_weight_count(ctypes.byref(shape), bias)
+    msg = ctypes.create_string_buffer(256)
+    st = _lib.lib().af2_attention_check(ctypes.byref(shape), bias, count, eps, msg, 256)
+    return st, msg.value.decode()
+
+
+def test_attention_weight_count_is_pack_attention_weights_length():
+    c, h = 128, 4
+    rng = np.random.default_rng(0)
+    w = af2cuda.AttentionWeights(*(rng.standard_normal(n).astype(np.float32) for n in
+                                   (c, c, c * c, c * c, c * c, c * c, c, c * c, c)))
+    for bias in (None, af2cuda.NormalizedInputPairBias(np.zeros(c * h, np.float32))):
+        inp = af2cuda.AttentionInput(np.zeros(0), np.zeros(0), 8, 8, c, h, w, pairBias=bias)
+        packed, offsets = af2cuda.pack_attention_weights(inp)
+        assert packed.size == af2cuda.attention_weight_count(8, 8, c, h, 0 if bias is None else 1)
+        assert offsets[:3] == [0, c, 2 * c]
+
+
+def test_attention_validation_mirrors_the_reference():
+    assert _attention_check(64, 64, 128, 4) == (_lib.AF2_OK, "")
+    st, msg = _attention_check(64, 64, 96, 2)
+    assert st == _lib.AF2_ERR_INVALID_ARGUMENT and "head dimension no larger than 32" in msg
+    st, msg = _attention_check(0, 64, 128, 4, count=1)
+    assert st == _lib.AF2_ERR_INVALID_ARGUMENT and "positive safe integers" in msg
+    st, msg = _attention_check(64, 64, 128, 4, count=5)
+    assert st == _lib.AF2_ERR_INVALID_ARGUMENT and "expected" in msg
+    st, msg = _attention_check(64, 64, 128, 4, eps=0)
+    assert st == _lib.AF2_ERR_INVALID_ARGUMENT and "epsilon" in msg
+    # valid for the reference, outside the kernels: head dimension 16, or a bias with batch != queries
+    assert _attention_check(64, 64, 64, 4)[0] == _lib.AF2_ERR_UNSUPPORTED
+    assert _attention_check(3, 64, 128, 4)[0] == _lib.AF2_ERR_UNSUPPORTED
+    assert _attention_check(3, 64, 128, 4, bias=0)[0] == _lib.AF2_OK

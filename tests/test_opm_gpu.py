@@ -133,6 +133,43 @@ def test_opm_on_the_reference_tests_own_case(device):
         assert np.array_equal(again.reshape(expected.shape), out), rb
 
 
+def test_opm_f32_precision_meets_the_reference_tests_f32_bar(device):
+    """The same case with the f32 GEMM precision installed (the reference's own f32 path,
+    which its test holds to mean |d| < 2e-5 and max |d| < 2e-4,
+    test/outer-product-mean-reference.gpu.test.ts:128-129): every operand of the three GEMMs
+    carried as an f16 hi / lo pair on the tensor cores.  It also meets 2e-3 of max|ref|, and
+    its residue blocks give the same bits."""
+    m, mask, w, row_block = opm_reference_test_case()
+    expected = opm_reference_test_expected(m, mask, w)
+    device.set_gemm_precision("f32")
+    try:
+        out = af2cuda.OuterProductMeanGpu(device).run(opm_input(m, mask, w, rowBlockResidues=row_block)).output
+        out = out.reshape(expected.shape)
+        err = oracle.error_metrics(out, expected)
+        assert err["meanAbsoluteError"] < 2e-5 and err["maxAbsoluteError"] < 2e-4, err
+        assert relative_max_error(out, expected) <= REL_TOL
+        for rb in (None, 1, 7):
+            again = af2cuda.OuterProductMeanGpu(device).run(opm_input(m, mask, w, rowBlockResidues=rb)).output
+            assert np.array_equal(again.reshape(expected.shape), out), rb
+    finally:
+        device.set_gemm_precision("matrix")
+    assert device.gemm_precision == "matrix"
+
+
+@pytest.mark.parametrize("s,n,cm,cz", [(37, 30, 64, 128), (130, 21, 256, 64), (700, 20, 16, 32)])
+def test_opm_f32_precision_matches_oracle_tightly(device, s, n, cm, cz):
+    """f32 GEMM precision on the benchmark law's inputs: within 2e-5 of max|ref| (f32 level),
+    where the default f16-operand path is held to 2e-3."""
+    m, mask, w = opm_case(s, n, cm, cz=cz, seed=s + n + cm)
+    expected = oracle.outer_product_mean(m, mask, opm_packed(w), 32, cz)
+    device.set_gemm_precision("f32")
+    try:
+        out = af2cuda.OuterProductMeanGpu(device).run(opm_input(m, mask, w)).output.reshape(n, n, cz)
+    finally:
+        device.set_gemm_precision("matrix")
+    assert relative_max_error(out, expected) <= 2e-5, relative_max_error(out, expected)
+
+
 def test_opm_fully_masked_residues(device):
     m, mask, w = opm_case(20, 17, 32, cz=16, seed=9)
     mask[:, 3] = 0  # residue 3 never observed: count 0, output = b_o / eps

@@ -66,7 +66,7 @@ def test_host_form_f16_and_residual(device):
     x, w = transition_case(513, 128, 512, seed=9)
     x16 = x.astype(np.float16).astype(np.float32)
     expected = oracle.transition(x16, packed(w), 512, residual=True)
-    out = af2cuda.TransitionGpu(device).run(make_input(x16, w), precision="f16", residual=True).output
+    out = af2cuda.TransitionGpu(device).run(make_input(x16, w), host_storage="f16", residual=True).output
     # the f16 output rounding adds at most 2^-11 of each value
     assert relative_max_error(out.reshape(x.shape), expected) <= REL_TOL + 2 ** -11
 

@@ -70,13 +70,32 @@ def test_block_rows_are_bit_identical(device, direction):
         assert np.array_equal(op.run(inp, {"blockRows": rows}).output, whole), rows
 
 
-def test_f16_io(device):
+def test_f16_host_storage(device):
+    """hostStorage "f16" (not a reference option) moves the pair as half-precision arrays."""
     z, mask, w = triangle_case(96, seed=3, perturbed=True)
     z16 = z.astype(np.float16).astype(np.float32)
     expected = oracle.triangle(0, z16, mask, pack(w))
-    out = af2cuda.TriangleMultiplicationOutgoingGpu(device).run(_input(z16, mask, w), {"precision": "f16"}).output
+    out = af2cuda.TriangleMultiplicationOutgoingGpu(device).run(_input(z16, mask, w), {"hostStorage": "f16"}).output
     # f16 output rounding adds at most 2^-11 relative per element.
     assert relative_max_error(out.reshape(z.shape), expected) <= REL_TOL + 2 ** -11
+
+
+@pytest.mark.parametrize("direction", [0, 1])
+def test_precision_option_keeps_the_pair_f32(device, direction):
+    """{precision: "f16"} selects the weight and arithmetic precision; the pair stays f32 in
+    and out, as in the reference (src/triangle/webgpu.ts:56-61,93-99): the output is an f32
+    array within 2e-3 of the oracle on unrounded f32 inputs, identical to the f32 option's,
+    and both whole-projection storages run."""
+    z, mask, w = triangle_case(80, seed=21 + direction, mask_p=0.9, perturbed=True)
+    expected = oracle.triangle(direction, z, mask, pack(w))
+    op = OPS[direction](device)
+    out16 = op.run(_input(z, mask, w), {"precision": "f16"}).output
+    assert out16.dtype == np.float32 and out16.size == z.size
+    assert relative_max_error(out16.reshape(z.shape), expected) <= REL_TOL
+    assert np.array_equal(out16, op.run(_input(z, mask, w), {"precision": "f32"}).output)
+    assert np.array_equal(out16, op.run(_input(z, mask, w), {"precision": "f16", "wholeStorage": "f16"}).output)
+    with pytest.raises(af2cuda.RangeError):
+        op.run(_input(z, mask, w), {"wholeStorage": "bf16"})
 
 
 def test_masked_rows_and_all_masked(device):
