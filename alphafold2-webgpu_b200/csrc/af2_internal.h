@@ -211,7 +211,7 @@ af2_status dequant_launch(af2_ctx *ctx, const af2_matrix &m, int64_t inner, int6
 // ---- shared dense projection (gemm.cu) ----
 
 // Destinations of the attention projection epilogue (attention.cu): q and k [b][h][j][32],
-// v transposed [b][h][32][pitch], the gate [rows][channels], the pair bias [h][b][pitch] (or NULL).
+// v transposed [b][h][32][pitch], the gate [rows][channels], the pair bias transposed [h][k][pitch] (or NULL).
 struct AttentionProjection {
   void *q = nullptr, *k = nullptr, *vt = nullptr, *g = nullptr, *bias = nullptr;  // f16
   int64_t queries = 0, pitch = 0, channels = 0, heads = 0;
@@ -343,7 +343,7 @@ struct AttentionLayout {
   int64_t k_pad = 0, cols = 0, o_cols = 0;
   int bn = 0;                          // column tile of the projection GEMM
   size_t off_w = 0, off_scale = 0, off_bvec = 0, off_wo = 0, off_wo_scale = 0, off_wo_bias = 0, off_ln = 0;
-  size_t off_xn = 0, off_q = 0, off_k = 0, off_vt = 0, off_g = 0, off_pb = 0, off_mb = 0, total = 0;
+  size_t off_xn = 0, off_q = 0, off_k = 0, off_vt = 0, off_g = 0, off_pb = 0, off_mb = 0, off_flags = 0, total = 0;
 };
 
 AttentionLayout attention_layout(int64_t batch, int64_t queries, int64_t channels, int64_t heads, bool bias);

@@ -19,7 +19,7 @@
 //                       normalised rows by [Wq | Wk | Wv | Wg | Wb]: q (times
 //                       log2(e)/sqrt(d)) and k as [b][h][j][32], v transposed
 //                       as [b][h][32][j], sigmoid(gate) as [b*Q + j][C], the
-//                       pair bias (times log2(e)) as [h][q][k];
+//                       pair bias (times log2(e)) transposed, [h][k][q];
 //   attn_flash_kernel   the flash loop, below;
 //   linear_kernel       the output projection, added into the pair rows.
 //
@@ -113,7 +113,7 @@ constexpr int THREADS = 320;  // warp 0 TMA, warp 1 MMA, warps 2-9 softmax (two 
 constexpr int STAGES = 3;
 constexpr uint32_t K_BYTES = 128 * 64;         // [128 keys][32 d] f16, 64B-swizzled
 constexpr uint32_t V_BYTES = 32 * 128 * 2;     // [32 d][128 keys] f16 as two 64-key boxes, 128B-swizzled
-constexpr uint32_t BIAS_BYTES = 128 * 128 * 2; // [128 q][128 keys] f16 as two 64-key boxes
+constexpr uint32_t BIAS_BYTES = 128 * 128 * 2; // [128 keys][128 q] f16 as two 64-query boxes
 constexpr uint32_t MB_BYTES = 128 * 4;
 constexpr uint32_t OFF_K = 0, OFF_V = 2 * K_BYTES, OFF_BIAS = OFF_V + 2 * V_BYTES, OFF_MB = OFF_BIAS + BIAS_BYTES;
 constexpr uint32_t STAGE_BYTES = OFF_MB + 2 * MB_BYTES;  // 66,560: a multiple of 1024
@@ -124,12 +124,20 @@ constexpr uint32_t SMEM_BYTES = OFF_BAR + 256 + 1024;
 static_assert(STAGE_BYTES % 1024 == 0, "stages keep the 1024-byte swizzle alignment");
 static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
 
-// TMEM columns of softmax group g: S at 256 g, P (f16 pairs) at 256 g + 128, O at 256 g + 192.
-constexpr uint32_t TM_GROUP = 256, TM_P = 128, TM_O = 192;
+// TMEM columns of softmax group g: S at 256 g, P (f16 pairs) at 256 g + 128, O at 256 g + 192
+// (to 256 g + 224).  The identity A operand that adds the bias tile to S on the tensor core
+// (shared by both groups) fills the two 32-column gaps: K steps 0-3 (queries 0-63) at 224,
+// K steps 4-7 (queries 64-127) at 480.
+constexpr uint32_t TM_GROUP = 256, TM_P = 128, TM_O = 192, TM_I0 = 224, TM_I1 = 480;
+__host__ __device__ constexpr uint32_t tm_identity(int ks) { return (ks < 4 ? TM_I0 : TM_I1) + 8u * (ks & 3); }
+// The running maximum moves only when a row's maximum grows by more than this (base 2): the
+// probabilities stay below 2^8, exact enough in f16, and O is rescaled far less often.
+constexpr float kLazyRescale = 8.f;
 
 struct FlashArgs {
   __half *weighted;        // [B * Q][C]
   const __half *gate;      // [B * Q][C]
+  const int *flags;        // [B][nkb]: the key block has masked keys or keys past Q
   int64_t batch, queries;
   int channels, heads, nqb, nkb, nbp, units, has_bias;
   unsigned int *err;
@@ -139,6 +147,23 @@ __device__ __forceinline__ float ex2f(float v) {
   float r;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(v));
   return r;
+}
+
+// flags[b][kb] = 1 when block kb of row b has a key with mask != 1 or runs past the last key:
+// only those blocks take the mask add and the clamp (one warp per block).
+__global__ void attn_flag_kernel(const float *__restrict__ mask, int64_t B, int64_t Q, int transpose, int nkb,
+                                 int *__restrict__ flags) {
+  const int64_t w = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (w >= B * nkb) return;
+  const int64_t b = w / nkb, k0 = (w - b * nkb) * 128;
+  bool any = false;
+  for (int i = lane; i < 128; i += 32) {
+    const int64_t k = k0 + i;
+    any |= k >= Q || mask[transpose ? k * B + b : b * Q + k] != 1.f;
+  }
+  any = __any_sync(kFull, any);
+  if (lane == 0) flags[w] = any ? 1 : 0;
 }
 
 __global__ void __launch_bounds__(THREADS, 1)
@@ -164,7 +189,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(full(s), 1);
-      mbar_init(empty(s), 1 + 8);  // the MMAs that read K and V, and the eight softmax warps (bias, mask)
+      mbar_init(empty(s), 1 + 8);  // the MMAs that read the stage, and the eight softmax warps (mask)
     }
     mbar_init(q_full, 1);
     mbar_init(q_empty, 1);
@@ -186,6 +211,26 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  if (warp >= 2 && warp < 6) {
+    // the 128 x 128 identity, f16 pairs along K: lane r holds 1.0 at column r
+    const int r = (warp & 3) * 32 + lane;
+    const uint32_t lanes = static_cast<uint32_t>((warp & 3) * 32) << 16;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const uint32_t taddr = tmem + lanes + (half ? TM_I1 : TM_I0);
+      uint32_t v[32];
+#pragma unroll
+      for (int c = 0; c < 32; ++c) {
+        const int col = 32 * half + c;
+        v[c] = (r == 2 * col) ? 0x00003C00u : (r == 2 * col + 1) ? 0x3C000000u : 0u;
+      }
+      tmem_st32(taddr, v);
+    }
+    tmem_st_wait();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
   const int nkb = p.nkb;
   const uint32_t stage_tx = 2 * K_BYTES + 2 * V_BYTES + (p.has_bias ? BIAS_BYTES : 0) + 2 * MB_BYTES;
 
@@ -220,9 +265,9 @@ __global__ void __launch_bounds__(THREADS, 1)
             tma_load_4d(st + OFF_V + g * V_BYTES + V_BYTES / 2, &vmap, full(s), kb * 128 + 64, 0, h, b);
             tma_load_3d(st + OFF_MB + g * MB_BYTES, &mmap, full(s), kb * 128, b, 0);
           }
-          if (p.has_bias) {
-            tma_load_3d(st + OFF_BIAS, &bmap, full(s), kb * 128, qb * 128, h);
-            tma_load_3d(st + OFF_BIAS + BIAS_BYTES / 2, &bmap, full(s), kb * 128 + 64, qb * 128, h);
+          if (p.has_bias) {  // the transposed bias [h][k][q]: 128 keys x (two boxes of 64 queries)
+            tma_load_3d(st + OFF_BIAS, &bmap, full(s), qb * 128, kb * 128, h);
+            tma_load_3d(st + OFF_BIAS + BIAS_BYTES / 2, &bmap, full(s), qb * 128 + 64, kb * 128, h);
           }
         }
       }
@@ -233,16 +278,29 @@ __global__ void __launch_bounds__(THREADS, 1)
   } else if (warp == 1) {
     // ---- MMA issue (warp-uniform loop, one elected lane per instruction) ----
     const uint32_t idesc_qk = idesc_f16_f32(128, 128), idesc_pv = idesc_f16_f32(128, 32);
+    const uint32_t idesc_bias = idesc_f16_f32(128, 128);  // B = the bias tile, keys x queries, K-major
     int it = 0, uit = 0;
     bool ok = true;
     auto qk = [&](int g, int tile) -> bool {
-      // S_g = Q_g K_g^T over the 32 head channels: two K = 16 steps of 32 bytes in the 64-byte rows
+      // S_g = I . bias (the tile's bias rows, exactly: K runs over the 128 queries, one-hot A from
+      // TMEM) + Q_g K_g^T over the 32 head channels (two K = 16 steps in the 64-byte rows)
       if (!warp_wait(s_free(g), (tile & 1) ^ 1, abort_flag, p.err, kErrWaitMma)) return false;
       tc_fence_after();
       const uint32_t st = sbase + (tile % STAGES) * STAGE_BYTES;
       const uint64_t qd = sdesc_k_sw64(sbase + OFF_Q + g * Q_BYTES), kd = sdesc_k_sw64(st + OFF_K + g * K_BYTES);
       const uint32_t d = tmem + g * TM_GROUP;
-      umma_first(d, qd, kd, idesc_qk);
+      if (p.has_bias) {
+        // the tile holds bias[q][k] as rows k of 128 queries (two 64-query boxes, 128B-swizzled)
+        const uint64_t bd = sdesc_k_sw128(st + OFF_BIAS);
+        umma_ts_first(d, tmem + tm_identity(0), bd, idesc_bias);
+#pragma unroll
+        for (int ks = 1; ks < 8; ++ks)
+          umma_ts_acc(d, tmem + tm_identity(ks), desc_add(bd, (ks >> 2) * (BIAS_BYTES / 2)) + (ks & 3) * 2,
+                      idesc_bias);
+        umma_acc(d, qd, kd, idesc_qk);
+      } else {
+        umma_first(d, qd, kd, idesc_qk);
+      }
       umma_acc(d, qd + 2, kd + 2, idesc_qk);
       umma_commit(s_full(g));
       return true;
@@ -302,9 +360,13 @@ __global__ void __launch_bounds__(THREADS, 1)
     for (int u = blockIdx.x; ok && u < p.units; u += gridDim.x) {
       const int qb = u % p.nqb, rest = u / p.nqb, bp = rest % p.nbp, h = rest / p.nbp;
       const int64_t b = 2 * bp + g, qrow = static_cast<int64_t>(qb) * 128 + r;
+      const int *flags = p.flags + (b < p.batch ? b : 0) * static_cast<int64_t>(nkb);
       float m_run = -INFINITY, l_run = 0.f;
       for (int kb = 0; kb < nkb; ++kb, ++it) {
         const int s = it % STAGES;
+        // masked keys or keys past Q in this block (a row past the batch reads row 0's flags: its
+        // scores are zeros and never stored)
+        const int flagged = __ldg(flags + kb);
         if (!warp_wait(s_full(g), it & 1, abort_flag, p.err, kErrWaitEpilogue)) {
           ok = false;
           break;
@@ -325,53 +387,59 @@ __global__ void __launch_bounds__(THREADS, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(s_free(g));  // S may be overwritten by the next block's scores
-        if (!warp_wait(full(s), (it / STAGES) & 1, abort_flag, p.err, kErrWaitEpilogue)) {
-          ok = false;
-          break;
-        }
-        // logits in base 2: S (q carries log2(e)/sqrt(d)) + bias + mask, clamped; keys past Q drop out
-        const uint8_t *st = smem + s * STAGE_BYTES;
-        const float *mb = reinterpret_cast<const float *>(st + OFF_MB + g * MB_BYTES);
-        const int64_t keys_left = p.queries - static_cast<int64_t>(kb) * 128;
-        const int kvalid = keys_left < 128 ? static_cast<int>(keys_left) : 128;
+        // S = q.k / sqrt(d) + bias, in base 2.  The reference adds 1e9 (mask - 1) and clamps to
+        // +-1e8 (here in base-2 units): exactly that where the block has masked keys (keys past Q
+        // drop out); elsewhere a logit can only reach the clamp if the row maximum is within
+        // 256 of it, and only then is every logit clamped.
         float mx = -INFINITY;
-#pragma unroll
-        for (int c8 = 0; c8 < 16; ++c8) {  // 8 keys at a time
-          float bias8[8];
-          if (p.has_bias) {
-            const int bx = c8 >> 3, ch = c8 & 7;
-            const uint4 bv = *reinterpret_cast<const uint4 *>(st + OFF_BIAS + bx * (BIAS_BYTES / 2) + r * 128 +
-                                                              ((ch ^ (r & 7)) << 4));
-            unpack8<__half>(bv, bias8);
-          } else {
-#pragma unroll
-            for (int e = 0; e < 8; ++e) bias8[e] = 0.f;
+        if (flagged) {
+          if (!warp_wait(full(s), (it / STAGES) & 1, abort_flag, p.err, kErrWaitEpilogue)) {
+            ok = false;
+            break;
           }
-          const float4 m0 = *reinterpret_cast<const float4 *>(mb + c8 * 8);
-          const float4 m1 = *reinterpret_cast<const float4 *>(mb + c8 * 8 + 4);
-          const float mk[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
+          const float *mb = reinterpret_cast<const float *>(smem + s * STAGE_BYTES + OFF_MB + g * MB_BYTES);
+          const int64_t keys_left = p.queries - static_cast<int64_t>(kb) * 128;
+          const int kvalid = keys_left < 128 ? static_cast<int>(keys_left) : 128;
 #pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const int key = c8 * 8 + e;
-            float v = __uint_as_float(t[key]) + bias8[e] + mk[e];
-            v = fminf(fmaxf(v, -kClamp), kClamp);
-            if (key >= kvalid) v = -INFINITY;
-            t[key] = __float_as_uint(v);
-            mx = fmaxf(mx, v);
+          for (int c4 = 0; c4 < 32; ++c4) {
+            const float4 m4 = *reinterpret_cast<const float4 *>(mb + 4 * c4);
+            const float mk[4] = {m4.x, m4.y, m4.z, m4.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int key = 4 * c4 + e;
+              float v = fminf(fmaxf(__uint_as_float(t[key]) + mk[e], -kClamp), kClamp);
+              if (key >= kvalid) v = -INFINITY;
+              t[key] = __float_as_uint(v);
+              mx = fmaxf(mx, v);
+            }
+          }
+        } else {
+#pragma unroll
+          for (int key = 0; key < 128; ++key) mx = fmaxf(mx, __uint_as_float(t[key]));
+          if (__any_sync(kFull, mx > kClamp || mx < 256.f - kClamp)) {
+            mx = -INFINITY;
+#pragma unroll
+            for (int key = 0; key < 128; ++key) {
+              const float v = fminf(fmaxf(__uint_as_float(t[key]), -kClamp), kClamp);
+              t[key] = __float_as_uint(v);
+              mx = fmaxf(mx, v);
+            }
           }
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(empty(s));  // this warp is done with the stage's bias and mask
-        const float m_new = fmaxf(m_run, mx);
-        const float alpha = ex2f(m_run - m_new);  // 0 on the first block (m_run = -inf)
+        if (lane == 0) mbar_arrive(empty(s));  // this warp is done with the stage's mask
+        // lazy maximum: move it (and rescale O and the sum) only when it grows by more than 2^8
+        const bool move = mx > m_run + kLazyRescale;
+        const float m_new = move ? mx : m_run;
+        const float alpha = move ? ex2f(m_run - m_new) : 1.f;  // 0 on the first block (m_run = -inf)
         if (kb > 0) {
-          // P of the previous block has been consumed and O holds its sum: rescale O if the maximum grew
+          // P of the previous block has been consumed and O holds its sum
           if (!warp_wait(o_done(g), (it - 1) & 1, abort_flag, p.err, kErrWaitEpilogue)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          if (__any_sync(kFull, alpha != 1.f)) {
+          if (__any_sync(kFull, move)) {
 #pragma unroll
             for (int hf = 0; hf < 2; ++hf) {
               uint32_t o[16];
@@ -384,21 +452,23 @@ __global__ void __launch_bounds__(THREADS, 1)
             tmem_st_wait();
           }
         }
-        float sum = 0.f;
+        float2 sum2 = make_float2(0.f, 0.f);
+        const float2 neg_m = make_float2(-m_new, -m_new);
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint32_t pk[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            const float p0 = ex2f(__uint_as_float(t[32 * c + 2 * i]) - m_new);
-            const float p1 = ex2f(__uint_as_float(t[32 * c + 2 * i + 1]) - m_new);
-            sum += p0 + p1;
-            pk[i] = pack_half2(p0, p1);
+            const float2 x = f2add(make_float2(__uint_as_float(t[32 * c + 2 * i]), __uint_as_float(t[32 * c + 2 * i + 1])),
+                                   neg_m);
+            const float2 pe = make_float2(ex2f(x.x), ex2f(x.y));
+            sum2 = f2add(sum2, pe);
+            pk[i] = pack_half2(pe.x, pe.y);
           }
           tmem_st16(t_p + 16 * c, pk);
         }
         tmem_st_wait();
-        l_run = l_run * alpha + sum;
+        l_run = l_run * alpha + (sum2.x + sum2.y);
         m_run = m_new;
         tc_fence_before();
         __syncwarp();
@@ -486,6 +556,7 @@ AttentionLayout attention_layout(int64_t batch, int64_t queries, int64_t channel
   L.off_g = take((size_t)L.rows * channels * 2);
   L.off_pb = take(bias ? (size_t)heads * queries * L.pitch * 2 : 0);
   L.off_mb = take((size_t)batch * L.pitch * 4);
+  L.off_flags = take((size_t)batch * ((queries + 127) / 128) * 4);
   L.total = off;
   return L;
 }
@@ -547,6 +618,9 @@ af2_status attention_launch(af2_ctx *ctx, const AttentionLayout &L, int transpos
   {
     LaunchScope scope(ctx, stream, kProfAttentionNormalize);
     attn_mask_kernel<<<(unsigned)((B * Q + 255) / 256), 256, 0, stream>>>(mask, B, Q, transpose, L.pitch, mb);
+    const int nkb = (int)((Q + 127) / 128);
+    attn_flag_kernel<<<(unsigned)((B * nkb + 7) / 8), 256, 0, stream>>>(mask, B, Q, transpose, nkb,
+                                                                       reinterpret_cast<int *>(ws + L.off_flags));
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(ctx, e, "attention mask");
   }
@@ -599,6 +673,7 @@ af2_status attention_launch(af2_ctx *ctx, const AttentionLayout &L, int transpos
     FlashArgs a{};
     a.weighted = xn;  // the normalised rows are dead after the projection
     a.gate = reinterpret_cast<const __half *>(ws + L.off_g);
+    a.flags = reinterpret_cast<const int *>(ws + L.off_flags);
     a.batch = B;
     a.queries = Q;
     a.channels = (int)C;

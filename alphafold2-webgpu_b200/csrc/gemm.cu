@@ -244,7 +244,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (MODE == kModeAttentionProjection) {
           // gated attention projections of row m = (b, j) (src/evoformer/attention.ts:497-566 and the
           // pair-bias projection :631-661): q, k -> [b][h][j][32]; v -> transposed [b][h][32][j];
-          // g = sigmoid(.) -> [m][C]; bias -> [h][b][j].  The scales carry log2(e) / sqrt(d) for q
+          // g = sigmoid(.) -> [m][C]; bias[h][q = b][k = j] -> transposed [h][j][b].  The scales carry log2(e) / sqrt(d) for q
           // and log2(e) for the bias, so the flash kernel works in base 2.
           const int C = p.att_c, part = c0 / C, cc = c0 - part * C, h = cc >> 5;
           const int64_t b = m / p.att_queries, j = m - b * p.att_queries;
@@ -269,8 +269,9 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
             for (int d = 0; d < 32; ++d) dst[d * p.att_pitch] = __float2half_rn(y[d]);
           } else if (part == 4 && cc == 0 && p.att_bias) {
+            // bias[h][q = b][k = j], stored transposed as [h][k][q] (rows of queries)
             for (int hh = 0; hh < p.att_heads; ++hh)
-              p.att_bias[(static_cast<int64_t>(hh) * p.att_queries + b) * p.att_pitch + j] = __float2half_rn(y[hh]);
+              p.att_bias[(static_cast<int64_t>(hh) * p.att_queries + j) * p.att_pitch + b] = __float2half_rn(y[hh]);
           }
           continue;
         }

@@ -59,7 +59,9 @@ KERNEL_DRAM_BYTES = {"triangle.contract": 776_628_736, "opm.fused": 599_897_344}
 KERNELS = ("weights.prepare", "triangle.prepare", "triangle.relayout", "triangle.project", "triangle.contract",
            "triangle.output", "opm.normalize", "opm.project", "opm.count", "opm.outer", "opm.output",
            "opm.fused", "transition.prepare", "transition.normalize", "transition.fused", "transition.linear",
-           "linear", "activations.convert")
+           "linear", "activations.convert", "attention.normalize", "attention.project", "attention.flash",
+           "attention.output")
+PAIR_HEADS = 4
 
 
 def triangle_flops(n: int, cz: int = CZ, ch: int = CH) -> float:
@@ -80,6 +82,12 @@ def transition_flops(n: int, c: int = CZ, h: int = HIDDEN) -> float:
     return 4.0 * n * n * c * h
 
 
+def attention_flops(n: int, c: int = CZ, heads: int = PAIR_HEADS) -> float:
+    """kernel-cost.ts:79-92, one triangle attention direction: project gemm(N^2, C, 4C), flash
+    2 gemm(N H N, 32, N), output gemm(N^2, C, C), pair bias gemm(N^2, C, H)."""
+    return 2.0 * n * n * c * 4 * c + 4.0 * n ** 3 * heads * 32 + 2.0 * n * n * c * c + 2.0 * n * n * c * heads
+
+
 def block_flops(n: int = N, s: int = S_MSA) -> float:
     return 2 * triangle_flops(n) + opm_flops(n, s) + transition_flops(n)
 
@@ -94,7 +102,11 @@ def kernel_step_flops(name: str, world: int = 1, n: int = N, s: int = S_MSA) -> 
                  "opm.output": 2.0 * n * n * C_OUTER * C_OUTER * CZ,
                  "opm.fused": 2.0 * (n * C_OUTER) ** 2 * s + 2.0 * n * n * C_OUTER * C_OUTER * CZ,
                  "opm.project": 2.0 * s * n * CM * 2 * C_OUTER,
-                 "transition.fused": transition_flops(n)}.get(name)
+                 "transition.fused": transition_flops(n),
+                 # triangle attention, both directions (pair-block workloads only)
+                 "attention.flash": 2 * 4.0 * n ** 3 * PAIR_HEADS * 32,
+                 "attention.project": 2 * 2.0 * n * n * CZ * (4 * CZ + PAIR_HEADS),
+                 "attention.output": 2 * 2.0 * n * n * CZ * CZ}.get(name)
     return None if per_block is None else per_block / world
 
 
@@ -182,6 +194,19 @@ def opm_weights(rng, cm=CM, c=C_OUTER, cz=CZ):
                            rng.standard_normal(cm * c) / np.sqrt(cm), np.zeros(c),
                            rng.standard_normal(cm * c) / np.sqrt(cm), np.zeros(c),
                            rng.standard_normal(c * c * cz) / np.sqrt(c * c), np.zeros(cz)]).astype(np.float32)
+
+
+def attention_weights(rng, c=CZ, heads=PAIR_HEADS):
+    """Triangle attention weights in packAttentionWeights order (src/evoformer/attention.ts:179-201):
+    LN gamma 1 / beta 0, q/k/v/gate/output weights ~N(0, 1/fan_in) [in, out], biases 0, the
+    normalized-input pair projection [C, heads] last."""
+    import numpy as np
+
+    def mat(i, o):
+        return (rng.standard_normal((i, o)) / np.sqrt(i)).astype(np.float32).ravel()
+
+    return np.concatenate([np.ones(c), np.zeros(c), mat(c, c), mat(c, c), mat(c, c), mat(c, c), np.zeros(c),
+                           mat(c, c), np.zeros(c), mat(c, heads)]).astype(np.float32)
 
 
 def transition_weights(rng, c=CZ, h=HIDDEN):
@@ -508,6 +533,12 @@ WORKLOADS = {
                 "transition with mixed-q8 weights), bf16 pair updated in place",
     "multimer": "config 5: N=2048 (4 chains x 512, mask 1 inside the four diagonal chain blocks): triangle out + "
                 "in and pair transition on a bf16 pair [2048,2048,128] updated in place, rows sharded over the ranks",
+    "triangle_attention": "next-row widening: triangle attention around the starting and the ending node at "
+                          "N=1024 (c_z=128, 4 heads of 32, pair bias from the normalised pair, mask 1), bf16 pair "
+                          "updated in place",
+    "pair_block": "next-row widening: the whole Evoformer pair block at N=1024 through one af2_evoformer_pair_block "
+                  "call (OPM of an S=512, c_m=256 MSA, triangle multiplication out + in, triangle attention "
+                  "starting + ending, pair transition with mixed-q8 weights), bf16 pair updated in place",
     "msa_transition": "next-row widening: the MSA transition of the N=1024 block, bf16 MSA rows [512*1024, 256] "
                       "updated in place, 256->1024 ReLU ->256 with symmetric int8 weights and f32 per-output-"
                       "channel scales",
@@ -587,6 +618,33 @@ def run_workload(args) -> None:
 
         def step():
             af2cuda.encode_transition_tensors(dev, x, tws, residual=True, stream=sh)
+    elif wl in ("triangle_attention", "pair_block"):
+        n = args.length or N
+        pair = torch.randn(n, n, CZ, device="cuda", generator=gen).to(torch.bfloat16)
+        mask = torch.ones(n, n, device="cuda")
+        w_att = [torch.from_numpy(attention_weights(rng)).cuda() for _ in range(2)]
+        flops = 2 * attention_flops(n)
+        if n != N and wl == "pair_block":
+            raise SystemExit("--length applies to triangle_attention only")
+        if wl == "pair_block":
+            msa = torch.randn(S_MSA, n, CM, device="cuda", generator=gen).to(torch.bfloat16)
+            msa_mask = (torch.rand(S_MSA, n, device="cuda", generator=gen) < 0.9).float()
+            msa_mask[0] = 1
+            block_w = {"outerProductMean": torch.from_numpy(opm_weights(rng)).cuda(),
+                       "triangleMultiplicationOutgoing": torch.from_numpy(synthetic_weights(rng)).cuda(),
+                       "triangleMultiplicationIncoming": torch.from_numpy(synthetic_weights(rng)).cuda(),
+                       "triangleAttentionStarting": w_att[0], "triangleAttentionEnding": w_att[1],
+                       "pairTransition": transition_tensors()}
+            flops += block_flops(n)
+
+        def step():
+            if wl == "pair_block":
+                af2cuda.encode_evoformer_pair_block_tensors(dev, pair, mask, block_w, msa=msa, msa_mask=msa_mask,
+                                                            c_outer=C_OUTER, c_hidden=CH, pair_heads=PAIR_HEADS,
+                                                            stream=sh)
+            else:
+                af2cuda.encode_triangle_attention_tensors(dev, "starting", pair, mask, w_att[0], PAIR_HEADS, stream=sh)
+                af2cuda.encode_triangle_attention_tensors(dev, "ending", pair, mask, w_att[1], PAIR_HEADS, stream=sh)
     elif wl == "opm":
         n, s = 256, 512
         msa = torch.randn(s, n, CM, device="cuda", generator=gen)
@@ -675,6 +733,15 @@ def run_workload(args) -> None:
     total = sum(k["ms_per_step"] for k in kernel.values()) or 1.0
     for k in kernel.values():
         k["share"] = k["ms_per_step"] / total
+    roofline = None
+    if wl in ("triangle_attention", "pair_block") and not args.length:
+        # the dominant tensor kernel of the N=1024 workload, as in the default line
+        tensor = {k: v for k, v in kernel.items() if kernel_step_flops(k) is not None}
+        dom = max(tensor, key=lambda k: tensor[k]["ms_per_step"])
+        achieved = kernel_step_flops(dom) / (tensor[dom]["ms_per_step"] * 1e-3) / 1e12
+        roofline = {"kernel": dom, "bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
+                    "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"], "traffic": None,
+                    "peak_source": f"{peaks['source']} burst bf16", "avg_launch_us": tensor[dom]["avg_us"]}
     if dist:
         dist.barrier()
     if rank == 0:
@@ -684,7 +751,8 @@ def run_workload(args) -> None:
             "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
             "config": {"workload": WORKLOADS[wl], "flops_per_step": flops},
             "pct_of_peak": value / world / peaks["bf16_tflops"], "peak_source": f"{peaks['source']} burst bf16",
-            "kernels": kernel, "gpu_launches": int(launches), "clocks": clocks.record()}), flush=True)
+            "kernels": kernel, "roofline": roofline, "gpu_launches": int(launches),
+            "clocks": clocks.record()}), flush=True)
     if world > 1:
         af2cuda.comm_destroy(dev)
     if dist:
@@ -701,6 +769,8 @@ def main() -> None:
     ap.add_argument("--workload", choices=["block", *WORKLOADS], default="block",
                     help="block (default): the metric's N=1024 block; the others: the remaining BASELINE configs")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--length", type=int, default=0,
+                    help="triangle_attention / pair_block: residues N (default 1024; smaller for profiling)")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)

@@ -38,4 +38,13 @@ def test_sharded_kernel_flops_split_over_ranks():
 
 
 def test_every_workload_is_described():
-    assert set(bench.WORKLOADS) == {"tri128", "transition", "opm", "block768", "multimer", "msa_transition"}
+    assert set(bench.WORKLOADS) == {"tri128", "transition", "opm", "block768", "multimer", "msa_transition",
+                                    "triangle_attention", "pair_block"}
+
+
+def test_attention_flops_follow_kernel_cost():
+    # kernel-cost.ts:79-92 at N=1024, c_z=128, 4 heads of 32: project 137.4 + flash 549.8 + output 34.4
+    # + pair bias 1.07 GFLOP per direction
+    assert bench.attention_flops(1024) / 1e9 == pytest.approx(722.63, abs=0.01)
+    per_kernel = sum(bench.kernel_step_flops(k) for k in ("attention.flash", "attention.project", "attention.output"))
+    assert per_kernel == pytest.approx(2 * bench.attention_flops(1024), rel=1e-12)
