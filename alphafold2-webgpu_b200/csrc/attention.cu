@@ -166,6 +166,8 @@ __global__ void attn_flag_kernel(const float *__restrict__ mask, int64_t B, int6
   if (lane == 0) flags[w] = any ? 1 : 0;
 }
 
+// Ten warps put three on two of the four SM sub-partitions, whose 16,384 registers then cap a
+// thread at 168.
 __global__ void __launch_bounds__(THREADS, 1)
     attn_flash_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
                       const __grid_constant__ CUtensorMap vmap, const __grid_constant__ CUtensorMap bmap,
@@ -362,11 +364,13 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int64_t b = 2 * bp + g, qrow = static_cast<int64_t>(qb) * 128 + r;
       const int *flags = p.flags + (b < p.batch ? b : 0) * static_cast<int64_t>(nkb);
       float m_run = -INFINITY, l_run = 0.f;
+      uint32_t flag_bits = 0;
       for (int kb = 0; kb < nkb; ++kb, ++it) {
         const int s = it % STAGES;
         // masked keys or keys past Q in this block (a row past the batch reads row 0's flags: its
-        // scores are zeros and never stored)
-        const int flagged = __ldg(flags + kb);
+        // scores are zeros and never stored); 32 blocks' flags at a time, one per lane
+        if ((kb & 31) == 0) flag_bits = __ballot_sync(kFull, kb + lane < nkb && __ldg(flags + kb + lane) != 0);
+        const bool flagged = (flag_bits >> (kb & 31)) & 1u;
         if (!warp_wait(s_full(g), it & 1, abort_flag, p.err, kErrWaitEpilogue)) {
           ok = false;
           break;
@@ -414,8 +418,12 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
           }
         } else {
+          float m8[8];  // eight independent chains, not one 128 long
 #pragma unroll
-          for (int key = 0; key < 128; ++key) mx = fmaxf(mx, __uint_as_float(t[key]));
+          for (int i = 0; i < 8; ++i) m8[i] = __uint_as_float(t[i]);
+#pragma unroll
+          for (int key = 8; key < 128; ++key) m8[key & 7] = fmaxf(m8[key & 7], __uint_as_float(t[key]));
+          mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
           if (__any_sync(kFull, mx > kClamp || mx < 256.f - kClamp)) {
             mx = -INFINITY;
 #pragma unroll
@@ -432,6 +440,17 @@ __global__ void __launch_bounds__(THREADS, 1)
         const bool move = mx > m_run + kLazyRescale;
         const float m_new = move ? mx : m_run;
         const float alpha = move ? ex2f(m_run - m_new) : 1.f;  // 0 on the first block (m_run = -inf)
+        // the exponentials, into registers, while the previous block's P . V may still run
+        float2 sum4[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+        const float2 neg_m = make_float2(-m_new, -m_new);
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+          const float2 x = f2add(make_float2(__uint_as_float(t[2 * i]), __uint_as_float(t[2 * i + 1])), neg_m);
+          const float2 pe = make_float2(ex2f(x.x), ex2f(x.y));
+          sum4[i & 3] = f2add(sum4[i & 3], pe);
+          t[i] = pack_half2(pe.x, pe.y);  // P pairs overwrite the consumed logits
+        }
+        const float2 sum2 = f2add(f2add(sum4[0], sum4[1]), f2add(sum4[2], sum4[3]));
         if (kb > 0) {
           // P of the previous block has been consumed and O holds its sum
           if (!warp_wait(o_done(g), (it - 1) & 1, abort_flag, p.err, kErrWaitEpilogue)) {
@@ -452,21 +471,8 @@ __global__ void __launch_bounds__(THREADS, 1)
             tmem_st_wait();
           }
         }
-        float2 sum2 = make_float2(0.f, 0.f);
-        const float2 neg_m = make_float2(-m_new, -m_new);
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t pk[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float2 x = f2add(make_float2(__uint_as_float(t[32 * c + 2 * i]), __uint_as_float(t[32 * c + 2 * i + 1])),
-                                   neg_m);
-            const float2 pe = make_float2(ex2f(x.x), ex2f(x.y));
-            sum2 = f2add(sum2, pe);
-            pk[i] = pack_half2(pe.x, pe.y);
-          }
-          tmem_st16(t_p + 16 * c, pk);
-        }
+        for (int c = 0; c < 4; ++c) tmem_st16(t_p + 16 * c, &t[16 * c]);
         tmem_st_wait();
         l_run = l_run * alpha + (sum2.x + sum2.y);
         m_run = m_new;

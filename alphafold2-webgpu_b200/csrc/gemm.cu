@@ -58,13 +58,25 @@ struct LinearArgs {
 
 // Per epilogue warp: one 32-row x 32-column f16 staging block for the TMA-stored output.
 constexpr uint32_t OUT_STAGE_BYTES = 32 * 64;
+// The column scales and biases, copied to shared memory once per CTA when there are at most this
+// many columns (the epilogue reads 64 of them per 32-column chunk; from global memory each read
+// goes to L2, since the operand ring leaves L1 little room).
+constexpr int kSmemVecCols = 1024;
+constexpr uint32_t VEC_BYTES = 2 * kSmemVecCols * 4;
 
 enum { kModeLinear = 0, kModeOpmProjection = 1, kModeAttentionProjection = 2 };
+
+// Attention projection: TMA store maps of q and k ([b][h][j][32], boxes 32 x 32 rows) and of the
+// transposed values ([b][h][32 d][j], boxes 32 keys x 32 d); the gate goes through `omap`.
+struct AttentionMaps {
+  CUtensorMap q, k, v;
+};
 
 template <typename OT, int MODE>
 __global__ void __launch_bounds__(THREADS, 1)
     linear_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap bmap,
-                  const __grid_constant__ CUtensorMap omap, const LinearArgs p) {
+                  const __grid_constant__ CUtensorMap omap, const __grid_constant__ AttentionMaps amaps,
+                  const LinearArgs p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = align1024(smem_raw);
   const uint32_t sbase = smem_u32(smem);
@@ -163,6 +175,18 @@ __global__ void __launch_bounds__(THREADS, 1)
     // the staged path exists for f16 outputs only (the host sets tma_out accordingly)
     const bool staged = MODE == kModeLinear && std::is_same<OT, __half>::value && p.tma_out;
     const uint32_t stage_off = OFF_BAR + 256 + (warp - 2) * OUT_STAGE_BYTES;
+    const int cols_pad = p.tiles_n * p.bn;
+    const float *vscale = p.scale, *vbias = p.bias;
+    if (cols_pad <= kSmemVecCols) {
+      float *sv = reinterpret_cast<float *>(smem + OFF_BAR + 256 + EPI_WARPS * OUT_STAGE_BYTES);
+      for (int i = threadIdx.x - 64; i < cols_pad; i += 32 * EPI_WARPS) {
+        sv[i] = p.scale[i];
+        sv[kSmemVecCols + i] = p.bias[i];
+      }
+      named_barrier(1, 32 * EPI_WARPS);  // the epilogue warps only
+      vscale = sv;
+      vbias = sv + kSmemVecCols;
+    }
     bool store_pending = false;
     int tile_it = 0;
     for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x, ++tile_it) {
@@ -193,11 +217,11 @@ __global__ void __launch_bounds__(THREADS, 1)
           // a block that starts past the last row or column is not stored at all
           if (c0 >= p.cols || static_cast<int64_t>(mi) * BM + q * 32 >= p.rows) continue;
           uint32_t pk[16];
-          const float4 *sc = reinterpret_cast<const float4 *>(p.scale + c0);
-          const float4 *bi = reinterpret_cast<const float4 *>(p.bias + c0);
+          const float4 *sc = reinterpret_cast<const float4 *>(vscale + c0);
+          const float4 *bi = reinterpret_cast<const float4 *>(vbias + c0);
 #pragma unroll
           for (int i4 = 0; i4 < 8; ++i4) {
-            const float4 s4 = __ldg(sc + i4), b4 = __ldg(bi + i4);
+            const float4 s4 = sc[i4], b4 = bi[i4];
             float y0 = fmaf(__uint_as_float(v[4 * i4 + 0]), s4.x, b4.x) * rs;
             float y1 = fmaf(__uint_as_float(v[4 * i4 + 1]), s4.y, b4.y) * rs;
             float y2 = fmaf(__uint_as_float(v[4 * i4 + 2]), s4.z, b4.z) * rs;
@@ -229,13 +253,74 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
           continue;
         }
+        if (MODE == kModeAttentionProjection) {
+          // a 32-row block inside one batch row b0 (and, for the values, starting on a 16-byte
+          // boundary) leaves through shared memory and one TMA store: q, k, gate as rows of 64
+          // bytes, the values transposed as 32 d rows of 32 keys
+          const int C = p.att_c, part = c0 / C, cc = c0 - part * C, h = cc >> 5;
+          const int64_t m0 = static_cast<int64_t>(mi) * BM + q * 32;
+          const int64_t b0 = m0 / p.att_queries, j0 = m0 - b0 * p.att_queries;
+          if (part <= 3 && m0 < p.rows && j0 + 32 <= p.att_queries && (part != 2 || j0 % 8 == 0)) {
+            float y[32];
+            const float4 *sc = reinterpret_cast<const float4 *>(vscale + c0);
+            const float4 *bi = reinterpret_cast<const float4 *>(vbias + c0);
+#pragma unroll
+            for (int i4 = 0; i4 < 8; ++i4) {
+              const float4 s4 = sc[i4], b4 = bi[i4];
+              y[4 * i4 + 0] = fmaf(__uint_as_float(v[4 * i4 + 0]), s4.x, b4.x);
+              y[4 * i4 + 1] = fmaf(__uint_as_float(v[4 * i4 + 1]), s4.y, b4.y);
+              y[4 * i4 + 2] = fmaf(__uint_as_float(v[4 * i4 + 2]), s4.z, b4.z);
+              y[4 * i4 + 3] = fmaf(__uint_as_float(v[4 * i4 + 3]), s4.w, b4.w);
+            }
+            if (lane == 0 && store_pending) bulk_wait_read_all();  // the last store has read the block
+            __syncwarp();
+            if (part == 2) {
+              __half *st = reinterpret_cast<__half *>(smem + stage_off);
+#pragma unroll
+              for (int d = 0; d < 32; ++d) st[d * 32 + lane] = __float2half_rn(y[d]);
+            } else {
+              uint32_t pk[16];
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                float y0 = y[2 * i], y1 = y[2 * i + 1];
+                if (part == 3) y0 = sigmoidf(y0), y1 = sigmoidf(y1);
+                pk[i] = pack_half2(y0, y1);
+              }
+              uint8_t *stage_row = smem + stage_off + lane * 64;
+              const uint4 q0 = make_uint4(pk[0], pk[1], pk[2], pk[3]), q1 = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+              const uint4 q2 = make_uint4(pk[8], pk[9], pk[10], pk[11]),
+                          q3 = make_uint4(pk[12], pk[13], pk[14], pk[15]);
+#pragma unroll
+              for (int w = 0; w < 4; ++w) {
+                const int pc = (w + lane) & 3;
+                *reinterpret_cast<uint4 *>(stage_row + pc * 16) = pc == 0 ? q0 : pc == 1 ? q1 : pc == 2 ? q2 : q3;
+              }
+            }
+            fence_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              const uint32_t src = sbase + stage_off;
+              if (part == 0)
+                tma_store_4d(&amaps.q, src, 0, (int)j0, h, (int)b0);
+              else if (part == 1)
+                tma_store_4d(&amaps.k, src, 0, (int)j0, h, (int)b0);
+              else if (part == 2)
+                tma_store_4d(&amaps.v, src, (int)j0, 0, h, (int)b0);
+              else
+                tma_store_3d(&omap, src, cc, (int)m0, 0);
+              bulk_commit();
+              store_pending = true;
+            }
+            continue;
+          }
+        }
         if (!row_ok || c0 >= p.cols) continue;
         float y[32];
-        const float4 *sc = reinterpret_cast<const float4 *>(p.scale + c0);
-        const float4 *bi = reinterpret_cast<const float4 *>(p.bias + c0);
+        const float4 *sc = reinterpret_cast<const float4 *>(vscale + c0);
+        const float4 *bi = reinterpret_cast<const float4 *>(vbias + c0);
 #pragma unroll
         for (int i4 = 0; i4 < 8; ++i4) {
-          const float4 s4 = __ldg(sc + i4), b4 = __ldg(bi + i4);
+          const float4 s4 = sc[i4], b4 = bi[i4];
           y[4 * i4 + 0] = fmaf(__uint_as_float(v[4 * i4 + 0]), s4.x, b4.x);
           y[4 * i4 + 1] = fmaf(__uint_as_float(v[4 * i4 + 1]), s4.y, b4.y);
           y[4 * i4 + 2] = fmaf(__uint_as_float(v[4 * i4 + 2]), s4.z, b4.z);
@@ -547,14 +632,14 @@ namespace {
 
 template <typename OT, int MODE>
 af2_status launch_linear_t(af2_ctx *ctx, const CUtensorMap &amap, const CUtensorMap &bmap, const CUtensorMap &omap,
-                           const LinearArgs &a, int prof, cudaStream_t stream) {
+                           const AttentionMaps &amaps, const LinearArgs &a, int prof, cudaStream_t stream) {
   auto kernel = linear_kernel<OT, MODE>;
-  const uint32_t smem = STAGES * (A_BYTES + a.bn * 128u) + 256 + EPI_WARPS * OUT_STAGE_BYTES + 1024;
+  const uint32_t smem = STAGES * (A_BYTES + a.bn * 128u) + 256 + EPI_WARPS * OUT_STAGE_BYTES + VEC_BYTES + 1024;
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return cuda_fail(ctx, e, "linear kernel attributes");
   const int grid = std::min(a.total_tiles, ctx->sm_count);
   LaunchScope scope(ctx, stream, prof);
-  kernel<<<grid, THREADS, smem, stream>>>(amap, bmap, omap, a);
+  kernel<<<grid, THREADS, smem, stream>>>(amap, bmap, omap, amaps, a);
   e = cudaGetLastError();
   return e == cudaSuccess ? AF2_OK : cuda_fail(ctx, e, "linear kernel launch");
 }
@@ -623,13 +708,33 @@ af2_status linear_launch(af2_ctx *ctx, const LinearOperands &op, cudaStream_t st
   if (a.tma_out && !encode_map_3d(&omap, f16map(), op.out, op.cols, op.rows, 1, op.ldo * 2,
                                   (uint64_t)op.rows * op.ldo * 2, 32, 32, 1, CU_TENSOR_MAP_SWIZZLE_NONE))
     return fail(ctx, AF2_ERR_CUDA, "cuTensorMapEncodeTiled failed for a linear layer's output");
+  AttentionMaps amaps;
+  std::memset(&amaps, 0, sizeof amaps);
+  if (attention) {
+    const AttentionProjection &ap = *op.attention;
+    const int64_t B = op.rows / ap.queries, Q = ap.queries, H = ap.heads;
+    const uint64_t qk_dims[4] = {32, (uint64_t)Q, (uint64_t)H, (uint64_t)B};
+    const uint64_t qk_strides[3] = {64, (uint64_t)Q * 64, (uint64_t)H * Q * 64};
+    const uint32_t qk_box[4] = {32, 32, 1, 1};
+    const uint64_t v_dims[4] = {(uint64_t)Q, 32, (uint64_t)H, (uint64_t)B};
+    const uint64_t v_strides[3] = {(uint64_t)ap.pitch * 2, (uint64_t)32 * ap.pitch * 2, (uint64_t)H * 32 * ap.pitch * 2};
+    const uint32_t v_box[4] = {32, 32, 1, 1};
+    if (!encode_map_4d(&amaps.q, f16map(), ap.q, qk_dims, qk_strides, qk_box, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !encode_map_4d(&amaps.k, f16map(), ap.k, qk_dims, qk_strides, qk_box, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !encode_map_4d(&amaps.v, f16map(), ap.vt, v_dims, v_strides, v_box, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !encode_map_3d(&omap, f16map(), ap.g, ap.channels, op.rows, 1, ap.channels * 2,
+                       (uint64_t)op.rows * ap.channels * 2, 32, 32, 1, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return fail(ctx, AF2_ERR_CUDA, "cuTensorMapEncodeTiled failed for the attention projection's outputs");
+  }
   if (op.opm_projection)
-    return launch_linear_t<__half, kModeOpmProjection>(ctx, amap, bmap, omap, a, op.prof, stream);
-  if (attention) return launch_linear_t<__half, kModeAttentionProjection>(ctx, amap, bmap, omap, a, op.prof, stream);
-  if (op.out_dtype == AF2_F16) return launch_linear_t<__half, kModeLinear>(ctx, amap, bmap, omap, a, op.prof, stream);
+    return launch_linear_t<__half, kModeOpmProjection>(ctx, amap, bmap, omap, amaps, a, op.prof, stream);
+  if (attention)
+    return launch_linear_t<__half, kModeAttentionProjection>(ctx, amap, bmap, omap, amaps, a, op.prof, stream);
+  if (op.out_dtype == AF2_F16)
+    return launch_linear_t<__half, kModeLinear>(ctx, amap, bmap, omap, amaps, a, op.prof, stream);
   if (op.out_dtype == AF2_BF16)
-    return launch_linear_t<__nv_bfloat16, kModeLinear>(ctx, amap, bmap, omap, a, op.prof, stream);
-  return launch_linear_t<float, kModeLinear>(ctx, amap, bmap, omap, a, op.prof, stream);
+    return launch_linear_t<__nv_bfloat16, kModeLinear>(ctx, amap, bmap, omap, amaps, a, op.prof, stream);
+  return launch_linear_t<float, kModeLinear>(ctx, amap, bmap, omap, amaps, a, op.prof, stream);
 }
 
 }  // namespace af2
