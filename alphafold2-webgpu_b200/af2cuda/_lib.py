@@ -108,6 +108,8 @@ SIGNATURES = {
     "af2_launch_count": (ctypes.c_uint64, [_vp]),
     "af2_set_gemm_precision": (_i32, [_vp, _i32]),
     "af2_get_gemm_precision": (_i32, [_vp]),
+    "af2_set_weight_cache": (_i32, [_vp, _i32]),
+    "af2_clear_weight_cache": (_i32, [_vp]),
     "af2_memory_snapshot": (_i32, [_vp, ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64)]),
     "af2_profile_enable": (_i32, [_vp, _i32]),
     "af2_profile_reset": (_i32, [_vp]),

@@ -41,6 +41,14 @@ class Device:
             raise _lib.RangeError(f"precision must be 'matrix' or 'f32'; received {precision}")
         _lib.check(_lib.lib().af2_set_gemm_precision(self.handle, code), self.handle)
 
+    def set_weight_cache(self, enable: bool) -> None:
+        """Keeps prepared weights per weights pointer and shape (made once; the weights must not
+        change in place while cached -- see clear_weight_cache)."""
+        _lib.check(_lib.lib().af2_set_weight_cache(self.handle, 1 if enable else 0), self.handle)
+
+    def clear_weight_cache(self) -> None:
+        _lib.check(_lib.lib().af2_clear_weight_cache(self.handle), self.handle)
+
     def memory_snapshot(self) -> dict:
         """{"currentBytes", "peakBytes"} of this context's device allocations
         (the reference allocator's snapshot(), src/runtime/allocator.ts:376-382)."""

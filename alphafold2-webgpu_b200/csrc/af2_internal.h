@@ -22,6 +22,22 @@ struct DeviceBuffer {
 }  // namespace af2
 
 namespace af2 {
+// What a prepared-weights cache entry was made from: the op, its weight pointers and the
+// dimensions and options the preparation depends on.
+struct WeightKey {
+  int kind = 0;
+  const void *ptr[8] = {};
+  int64_t dim[8] = {};
+  bool operator==(const WeightKey &o) const;
+};
+struct CachedWeights {
+  WeightKey key;
+  DeviceBuffer buf;
+};
+enum WeightKind { kWeightsTriangle = 1, kWeightsOpm, kWeightsTransition, kWeightsAttention, kWeightsLinear };
+}  // namespace af2
+
+namespace af2 {
 // Kernels the per-launch profiler distinguishes (labels follow the reference's
 // dispatch labels, src/runtime/kernel-cost.ts:158-162).
 enum ProfileKernel {
@@ -88,6 +104,9 @@ struct af2_ctx {
   int *sync_word = nullptr;                // device word the exchange barriers all-reduce
   bool ipc_failed = false;                 // mapping refused: exchanges use NCCL send/recv
   int gemm_precision = 0;                  // af2_gemm_precision: what the GEMMs that honour it multiply in
+  // af2_set_weight_cache: prepared weights kept per weights pointer and shape, made once
+  bool weight_cache = false;
+  std::vector<af2::CachedWeights> cached_weights;
 };
 
 namespace af2 {
@@ -98,6 +117,17 @@ af2_status fail(af2_ctx *ctx, af2_status status, const std::string &message);
 af2_status cuda_fail(af2_ctx *ctx, cudaError_t e, const char *what);
 // Ensures `buf` holds at least `bytes` (256-byte aligned device memory).
 af2_status ensure(af2_ctx *ctx, DeviceBuffer &buf, size_t bytes, const char *what);
+
+// Where an op's prepared weights -- the prefix [0, bytes) of its scratch layout -- live.  With the
+// context's weight cache on (and `allow` set), the cache entry for `key`: fresh when just made,
+// so the caller prepares into it; else the workspace itself, always fresh.
+struct PreparedRegion {
+  uint8_t *base = nullptr;
+  bool fresh = true;
+};
+af2_status prepared_region(af2_ctx *ctx, const WeightKey &key, size_t bytes, void *workspace, bool allow,
+                           PreparedRegion *out);
+void clear_weight_cache(af2_ctx *ctx);
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point.
 bool encode_map_3d(CUtensorMap *map, CUtensorMapDataType dtype, const void *base, uint64_t d0, uint64_t d1,
@@ -177,9 +207,11 @@ struct TriangleShard {
 };
 
 // Launches the whole op on `stream`; the workspace holds TriangleLayout::total bytes.
+// cache_weights = false keeps the call from allocating a weight-cache entry (the static-scratch form).
 af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L, const void *z, int z_dtype,
                            const float *mask, const float *packed, double eps, int residual, void *out,
-                           int out_dtype, void *workspace, cudaStream_t stream, const TriangleShard *shard = nullptr);
+                           int out_dtype, void *workspace, cudaStream_t stream, const TriangleShard *shard = nullptr,
+                           bool cache_weights = true);
 
 // ---- transition (transition.cu) ----
 

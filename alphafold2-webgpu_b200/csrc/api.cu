@@ -50,6 +50,52 @@ af2_status ensure(af2_ctx *ctx, DeviceBuffer &buf, size_t bytes, const char *wha
   return AF2_OK;
 }
 
+bool WeightKey::operator==(const WeightKey &o) const {
+  if (kind != o.kind) return false;
+  for (int i = 0; i < 8; ++i)
+    if (ptr[i] != o.ptr[i] || dim[i] != o.dim[i]) return false;
+  return true;
+}
+
+af2_status prepared_region(af2_ctx *ctx, const WeightKey &key, size_t bytes, void *workspace, bool allow,
+                           PreparedRegion *out) {
+  if (!ctx->weight_cache || !allow) {
+    out->base = static_cast<uint8_t *>(workspace);
+    out->fresh = true;
+    return AF2_OK;
+  }
+  for (CachedWeights &c : ctx->cached_weights)
+    if (c.key == key && c.buf.bytes >= bytes) {
+      out->base = static_cast<uint8_t *>(c.buf.ptr);
+      out->fresh = false;
+      return AF2_OK;
+    }
+  CachedWeights entry;
+  entry.key = key;
+  const size_t want = align_up(bytes, 256);
+  cudaError_t e = cudaMalloc(&entry.buf.ptr, want);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(ctx, AF2_ERR_OUT_OF_MEMORY, "device allocation for the prepared-weights cache failed");
+  }
+  entry.buf.bytes = want;
+  ctx->allocated += want;
+  if (ctx->allocated > ctx->peak) ctx->peak = ctx->allocated;
+  ctx->cached_weights.push_back(entry);
+  out->base = static_cast<uint8_t *>(entry.buf.ptr);
+  out->fresh = true;
+  return AF2_OK;
+}
+
+void clear_weight_cache(af2_ctx *ctx) {
+  if (!ctx->cached_weights.empty()) cudaDeviceSynchronize();  // no kernel may still read them
+  for (CachedWeights &c : ctx->cached_weights) {
+    cudaFree(c.buf.ptr);
+    ctx->allocated -= c.buf.bytes;
+  }
+  ctx->cached_weights.clear();
+}
+
 const char *profile_name(int id) {
   static const char *names[kProfCount] = {
       "triangle.prepare",    "triangle.relayout",    "triangle.project",  "triangle.contract",
@@ -291,6 +337,7 @@ void af2_destroy(af2_ctx *ctx) {
   cudaSetDevice(ctx->device);
   if (ctx->stream) cudaStreamSynchronize(ctx->stream);
   comm_destroy(ctx);
+  clear_weight_cache(ctx);
   if (ctx->workspace.ptr) cudaFree(ctx->workspace.ptr);
   for (auto &s : ctx->staging)
     if (s.ptr) cudaFree(s.ptr);
@@ -319,6 +366,21 @@ af2_status af2_set_gemm_precision(af2_ctx *ctx, int precision) {
 }
 
 int af2_get_gemm_precision(const af2_ctx *ctx) { return ctx ? ctx->gemm_precision : AF2_GEMM_MATRIX; }
+
+af2_status af2_set_weight_cache(af2_ctx *ctx, int enable) {
+  if (!ctx) return AF2_ERR_INVALID_ARGUMENT;
+  cudaSetDevice(ctx->device);
+  ctx->weight_cache = enable != 0;
+  if (!ctx->weight_cache) clear_weight_cache(ctx);
+  return AF2_OK;
+}
+
+af2_status af2_clear_weight_cache(af2_ctx *ctx) {
+  if (!ctx) return AF2_ERR_INVALID_ARGUMENT;
+  cudaSetDevice(ctx->device);
+  clear_weight_cache(ctx);
+  return AF2_OK;
+}
 
 af2_status af2_memory_snapshot(const af2_ctx *ctx, uint64_t *current_bytes, uint64_t *peak_bytes) {
   if (!ctx) return AF2_ERR_INVALID_ARGUMENT;

@@ -576,21 +576,31 @@ af2_status attention_launch(af2_ctx *ctx, const AttentionLayout &L, int transpos
   // gating weights [C, C] ([in, out]), gating bias, output weight [C, C], output bias, pair projection [C, H].
   const float *ln_s = packed, *ln_o = ln_s + C, *wq = ln_o + C, *wk = wq + C * C, *wv = wk + C * C,
               *wg = wv + C * C, *bg = wg + C * C, *wo = bg + C, *bo = wo + C * C, *wb = bo + C;
-  float *scale = reinterpret_cast<float *>(ws + L.off_scale), *bvec = reinterpret_cast<float *>(ws + L.off_bvec);
-  float *wo_scale = reinterpret_cast<float *>(ws + L.off_wo_scale), *wo_bias = reinterpret_cast<float *>(ws + L.off_wo_bias);
-  float *ln = reinterpret_cast<float *>(ws + L.off_ln);
   af2_status st;
-  {
+  // the prepared weights: the layout's prefix [0, off_xn), in the weight cache or the workspace
+  WeightKey key;
+  key.kind = kWeightsAttention;
+  key.ptr[0] = packed;
+  key.dim[0] = C;
+  key.dim[1] = H;
+  key.dim[2] = L.bias ? 1 : 0;
+  PreparedRegion pw;
+  if ((st = prepared_region(ctx, key, L.off_xn, ws, true, &pw)) != AF2_OK) return st;
+  uint8_t *wp = pw.base;
+  float *scale = reinterpret_cast<float *>(wp + L.off_scale), *bvec = reinterpret_cast<float *>(wp + L.off_bvec);
+  float *wo_scale = reinterpret_cast<float *>(wp + L.off_wo_scale), *wo_bias = reinterpret_cast<float *>(wp + L.off_wo_bias);
+  float *ln = reinterpret_cast<float *>(wp + L.off_ln);
+  if (pw.fresh) {
     const float qscale = kLog2e / std::sqrt(32.f);
     auto f32m = [](const float *p) { return af2_matrix{AF2_WEIGHTS_F32, 0, p, nullptr}; };
     PrepJob jobs[6] = {
-        {f32m(wq), C, C, L.k_pad, C, qscale, ws + L.off_w, scale, 0, L.cols},
-        {f32m(wk), C, C, L.k_pad, C, 1.f, ws + L.off_w, scale, C, L.cols},
-        {f32m(wv), C, C, L.k_pad, C, 1.f, ws + L.off_w, scale, 2 * C, L.cols},
-        {f32m(wg), C, C, L.k_pad, C, 1.f, ws + L.off_w, scale, 3 * C, L.cols},
-        {f32m(wo), C, C, L.k_pad, L.o_cols, 1.f, ws + L.off_wo, wo_scale, 0, 0},
+        {f32m(wq), C, C, L.k_pad, C, qscale, wp + L.off_w, scale, 0, L.cols},
+        {f32m(wk), C, C, L.k_pad, C, 1.f, wp + L.off_w, scale, C, L.cols},
+        {f32m(wv), C, C, L.k_pad, C, 1.f, wp + L.off_w, scale, 2 * C, L.cols},
+        {f32m(wg), C, C, L.k_pad, C, 1.f, wp + L.off_w, scale, 3 * C, L.cols},
+        {f32m(wo), C, C, L.k_pad, L.o_cols, 1.f, wp + L.off_wo, wo_scale, 0, 0},
         // the pair-bias columns (zeros without a bias): the padded tail of the projection
-        {f32m(L.bias ? wb : wq), C, L.bias ? H : 0, L.k_pad, L.cols - 4 * C, kLog2e, ws + L.off_w, scale, 4 * C,
+        {f32m(L.bias ? wb : wq), C, L.bias ? H : 0, L.k_pad, L.cols - 4 * C, kLog2e, wp + L.off_w, scale, 4 * C,
          L.cols},
     };
     if ((st = prepare_matrices(ctx, jobs, 6, stream)) != AF2_OK) return st;
@@ -645,7 +655,7 @@ af2_status attention_launch(af2_ctx *ctx, const AttentionLayout &L, int transpos
     op.a = xn;
     op.lda = C;
     op.inner = C;
-    op.w = ws + L.off_w;
+    op.w = wp + L.off_w;
     op.scale = scale;
     op.bias = bvec;
     op.rows = L.rows;
@@ -703,7 +713,7 @@ af2_status attention_launch(af2_ctx *ctx, const AttentionLayout &L, int transpos
   op.a = xn;
   op.lda = C;
   op.inner = C;
-  op.w = ws + L.off_wo;
+  op.w = wp + L.off_wo;
   op.scale = wo_scale;
   op.bias = wo_bias;
   op.rows = L.rows;

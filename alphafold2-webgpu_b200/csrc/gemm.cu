@@ -766,11 +766,24 @@ af2_status linear_run(af2_ctx *ctx, const LinearLayout &L, int64_t rows, int64_t
                       int a_dtype, const af2_matrix &weight, const float *bias, int activation, int residual,
                       void *out, int out_dtype, void *workspace, cudaStream_t stream) {
   uint8_t *ws = static_cast<uint8_t *>(workspace);
-  float *scale = reinterpret_cast<float *>(ws + L.off_scale), *bvec = reinterpret_cast<float *>(ws + L.off_bias);
-  af2_status st;
-  if ((st = prepare_matrix(ctx, weight, inner, cols, L.k_pad, L.cols_pad, 1.f, ws + L.off_w, scale, stream)) !=
-          AF2_OK ||
-      (st = pad_vector(ctx, bias, bias ? cols : 0, L.cols_pad, bvec, stream)) != AF2_OK)
+  // the prepared weights: the layout's prefix [0, off_a), in the weight cache or the workspace
+  WeightKey key;
+  key.kind = kWeightsLinear;
+  key.ptr[0] = weight.values;
+  key.ptr[1] = weight.scales;
+  key.ptr[2] = bias;
+  key.dim[0] = inner;
+  key.dim[1] = cols;
+  key.dim[2] = weight.format * 65536 + weight.block;
+  PreparedRegion pw;
+  af2_status st = prepared_region(ctx, key, L.off_a, ws, true, &pw);
+  if (st != AF2_OK) return st;
+  uint8_t *wp = pw.base;
+  float *scale = reinterpret_cast<float *>(wp + L.off_scale), *bvec = reinterpret_cast<float *>(wp + L.off_bias);
+  if (pw.fresh &&
+      ((st = prepare_matrix(ctx, weight, inner, cols, L.k_pad, L.cols_pad, 1.f, wp + L.off_w, scale, stream)) !=
+           AF2_OK ||
+       (st = pad_vector(ctx, bias, bias ? cols : 0, L.cols_pad, bvec, stream)) != AF2_OK))
     return st;
   LinearOperands op;
   op.a = a;
@@ -781,7 +794,7 @@ af2_status linear_run(af2_ctx *ctx, const LinearLayout &L, int64_t rows, int64_t
     op.lda = L.k_pad;
   }
   op.inner = inner;
-  op.w = ws + L.off_w;
+  op.w = wp + L.off_w;
   op.scale = scale;
   op.bias = bvec;
   op.rows = rows;

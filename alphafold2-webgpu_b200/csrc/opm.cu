@@ -1066,8 +1066,8 @@ af2_status launch_fused_t(af2_ctx *ctx, const CUtensorMap &lmap, const CUtensorM
 }
 
 // The outer products and output projection of this rank's rows, one launch.
-af2_status fused_launch(af2_ctx *ctx, const OpmLayout &L, uint8_t *ws, const __half *right_full, int residual,
-                        void *out, int out_dtype, cudaStream_t stream) {
+af2_status fused_launch(af2_ctx *ctx, const OpmLayout &L, uint8_t *ws, const uint8_t *wp, const __half *right_full,
+                        int residual, void *out, int out_dtype, cudaStream_t stream) {
   const int64_t s = L.s, n = L.n, c = L.c, cz = L.cz, rows = L.rows;
   const int64_t o_cols = linear_cols_pad(cz), o_inner = align_up(c * c, 64);
   const int k_blocks = (int)((s + 63) / 64);
@@ -1083,13 +1083,13 @@ af2_status fused_launch(af2_ctx *ctx, const OpmLayout &L, uint8_t *ws, const __h
                      (uint64_t)rows * pitch * 2, 64, 128, 1, CU_TENSOR_MAP_SWIZZLE_128B) ||
       !encode_map_3d(&rmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, right_full, s, n * c, 1, pitch * 2,
                      (uint64_t)n * c * pitch * 2, 64, (uint32_t)(32 * J), 1, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !encode_map_3d(&wmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, ws + L.off_wo, 64, o_cols, o_inner / 64, 128,
+      !encode_map_3d(&wmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, wp + L.off_wo, 64, o_cols, o_inner / 64, 128,
                      (uint64_t)o_cols * 128, 32, (uint32_t)o_cols, 1, CU_TENSOR_MAP_SWIZZLE_64B))
     return fail(ctx, AF2_ERR_CUDA, "cuTensorMapEncodeTiled failed for the fused OPM operands");
   FusedArgs a{};
   a.out = out;
-  a.wscale = reinterpret_cast<const float *>(ws + L.off_wo_scale);
-  a.bias = reinterpret_cast<const float *>(ws + L.off_wo_bias);
+  a.wscale = reinterpret_cast<const float *>(wp + L.off_wo_scale);
+  a.bias = reinterpret_cast<const float *>(wp + L.off_wo_bias);
   a.rowscale = reinterpret_cast<const float *>(ws + L.off_rowscale);
   a.n = n;
   a.rows = rows;
@@ -1130,15 +1130,24 @@ af2_status opm_launch(af2_ctx *ctx, const OpmLayout &L, const void *m, int m_dty
   const float *ln_w = packed, *ln_b = ln_w + cm, *lw = ln_b + cm, *lb = lw + cm * c, *rw = lb + c, *rb = rw + cm * c;
   const float *ow = rb + c, *ob = ow + c * c * cz;
   const int64_t lr_cols = linear_cols_pad(2 * c), o_cols = linear_cols_pad(cz), o_inner = align_up(c * c, 64);
-  float *wlr_scale = reinterpret_cast<float *>(ws + L.off_wlr_scale), *wlr_bias = reinterpret_cast<float *>(ws + L.off_wlr_bias);
-  float *wo_scale = reinterpret_cast<float *>(ws + L.off_wo_scale), *wo_bias = reinterpret_cast<float *>(ws + L.off_wo_bias);
-  float *ln = reinterpret_cast<float *>(ws + L.off_ln);
   af2_status st;
   // 16-bit MSA, fused layouts: LayerNorm and projection in one kernel (gamma and beta folded
   // into the projection's weights and biases)
   const bool lnproj = L.fused && m_dtype != AF2_F32 && cm % 8 == 0 && L.cmp <= 256 &&
                       reinterpret_cast<uintptr_t>(m) % 16 == 0;
   const int64_t kx = L.split ? 3 : 1;
+  // the prepared weights: the layout's prefix [0, off_xn), in the weight cache or the workspace
+  WeightKey key;
+  key.kind = kWeightsOpm;
+  key.ptr[0] = packed;
+  const int64_t dims[7] = {cm, c, cz, L.out_shift, lnproj ? 1 : 0, L.split ? 1 : 0, L.cmp};
+  for (int i = 0; i < 7; ++i) key.dim[i] = dims[i];
+  PreparedRegion pw;
+  if ((st = prepared_region(ctx, key, L.off_xn, ws, true, &pw)) != AF2_OK) return st;
+  uint8_t *wp = pw.base;
+  float *wlr_scale = reinterpret_cast<float *>(wp + L.off_wlr_scale), *wlr_bias = reinterpret_cast<float *>(wp + L.off_wlr_bias);
+  float *wo_scale = reinterpret_cast<float *>(wp + L.off_wo_scale), *wo_bias = reinterpret_cast<float *>(wp + L.off_wo_bias);
+  float *ln = reinterpret_cast<float *>(wp + L.off_ln);
   // ---- weights ----
   const af2_matrix left_m{AF2_WEIGHTS_F32, 0, lw, nullptr}, right_m{AF2_WEIGHTS_F32, 0, rw, nullptr};
   const af2_matrix out_m{AF2_WEIGHTS_F32, 0, ow, nullptr};
@@ -1150,28 +1159,30 @@ af2_status opm_launch(af2_ctx *ctx, const OpmLayout &L, const void *m, int m_dty
   vs.add(ln_b, cm, L.cmp, ln + L.cmp);
   if (lr_cols > 2 * c) vs.add(nullptr, 0, lr_cols - 2 * c, wlr_scale + 2 * c);
   const float *fold = lnproj ? ln_w : nullptr;
-  if (!L.split) {
+  if (!pw.fresh) {
+    // prepared by an earlier call with these weights
+  } else if (!L.split) {
     const PrepJob jobs[3] = {
-        {left_m, cm, c, L.cmp, c, 1.f, ws + L.off_wlr, wlr_scale, 0, lr_cols, fold},
-        {right_m, cm, c, L.cmp, c, 1.f, ws + L.off_wlr, wlr_scale, c, lr_cols, fold},
-        {out_m, c * c, cz, o_inner, o_cols, std::ldexp(1.f, L.out_shift), ws + L.off_wo, wo_scale, 0, 0}};
+        {left_m, cm, c, L.cmp, c, 1.f, wp + L.off_wlr, wlr_scale, 0, lr_cols, fold},
+        {right_m, cm, c, L.cmp, c, 1.f, wp + L.off_wlr, wlr_scale, c, lr_cols, fold},
+        {out_m, c * c, cz, o_inner, o_cols, std::ldexp(1.f, L.out_shift), wp + L.off_wo, wo_scale, 0, 0}};
     if ((st = prepare_matrices(ctx, jobs, 3, stream)) != AF2_OK) return st;
   } else {
     // K-tripled weights [W_hi; W_lo; W_hi] against the operands [hi | hi | lo] (norm and outer kernels)
     const int part[3] = {0, 1, 0};
     PrepJob lr[6], wo[3];
     for (int g = 0; g < 3; ++g) {
-      uint8_t *seg = ws + L.off_wlr + (size_t)g * L.cmp * lr_cols * 2;
+      uint8_t *seg = wp + L.off_wlr + (size_t)g * L.cmp * lr_cols * 2;
       lr[2 * g] = PrepJob{left_m, cm, c, L.cmp, c, 1.f, seg, wlr_scale, 0, lr_cols, nullptr, part[g]};
       lr[2 * g + 1] = PrepJob{right_m, cm, c, L.cmp, c, 1.f, seg, wlr_scale, c, lr_cols, nullptr, part[g]};
       wo[g] = PrepJob{out_m, c * c, cz, o_inner, o_cols, std::ldexp(1.f, L.out_shift),
-                      ws + L.off_wo + (size_t)g * o_inner * o_cols * 2, wo_scale, 0, 0, nullptr, part[g]};
+                      wp + L.off_wo + (size_t)g * o_inner * o_cols * 2, wo_scale, 0, 0, nullptr, part[g]};
     }
     if ((st = prepare_matrices(ctx, lr, 6, stream)) != AF2_OK || (st = prepare_matrices(ctx, wo, 3, stream)) != AF2_OK)
       return st;
   }
-  if ((st = pad_vectors(ctx, vs, stream)) != AF2_OK) return st;
-  if (lnproj) {
+  if (pw.fresh && (st = pad_vectors(ctx, vs, stream)) != AF2_OK) return st;
+  if (lnproj && pw.fresh) {
     LaunchScope scope(ctx, stream, kProfPrepare);
     fold_beta_kernel<<<(unsigned)((2 * c + 7) / 8), 256, 0, stream>>>(ln_b, lw, rw, (int)cm, (int)c, wlr_bias);
     if (cudaError_t e = cudaGetLastError(); e != cudaSuccess) return cuda_fail(ctx, e, "OPM LayerNorm fold");
@@ -1187,7 +1198,7 @@ af2_status opm_launch(af2_ctx *ctx, const OpmLayout &L, const void *m, int m_dty
     a.scale = wlr_scale;
     a.bias = wlr_bias;
     a.mask = mask;
-    a.w = reinterpret_cast<const __half *>(ws + L.off_wlr);
+    a.w = reinterpret_cast<const __half *>(wp + L.off_wlr);
     a.left = reinterpret_cast<__half *>(ws + L.off_left);
     a.right = right_full + (size_t)rank * L.seq_pitch * rows * c;
     a.n_full = n;
@@ -1249,7 +1260,7 @@ af2_status opm_launch(af2_ctx *ctx, const OpmLayout &L, const void *m, int m_dty
     op.a = xn;
     op.lda = kx * L.cmp;
     op.inner = kx * L.cmp;
-    op.w = ws + L.off_wlr;
+    op.w = wp + L.off_wlr;
     if (L.split) {
       op.split_stride_left = s * rows * c;
       op.split_stride_right = s * n * c;
@@ -1282,7 +1293,7 @@ af2_status opm_launch(af2_ctx *ctx, const OpmLayout &L, const void *m, int m_dty
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(ctx, e, "OPM pair counts");
   }
-  if (L.fused) return fused_launch(ctx, L, ws, right_full, residual, out, out_dtype, stream);
+  if (L.fused) return fused_launch(ctx, L, ws, wp, right_full, residual, out, out_dtype, stream);
   const int64_t blocks_b = n / rows;  // blocks of the right operand
   // ---- outer products and output projection, block by block of this rank's rows ----
   CUtensorMap lmap, rmap;
@@ -1321,7 +1332,7 @@ af2_status opm_launch(af2_ctx *ctx, const OpmLayout &L, const void *m, int m_dty
     op.a = outer;
     op.lda = kx * c * c;
     op.inner = kx * c * c;
-    op.w = ws + L.off_wo;
+    op.w = wp + L.off_wo;
     op.scale = wo_scale;
     op.bias = wo_bias;
     op.row_scale = rowscale + i0 * n;

@@ -83,5 +83,6 @@ extern "C" af2_status af2_triangle_multiplication_static(af2_ctx *ctx, int direc
   if ((st = scratch_address(ctx, &scratch)) != AF2_OK) return st;
   cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
   return triangle_launch(ctx, direction, L, z, z_dtype, mask, packed_weights, epsilon,
-                         options ? options->residual : 0, out, out_dtype, scratch, s);
+                         options ? options->residual : 0, out, out_dtype, scratch, s, nullptr,
+                         /*cache_weights=*/false);
 }

@@ -831,6 +831,19 @@ TransitionLayout transition_layout(int64_t rows, int64_t c, int64_t h, int x_dty
   return L;
 }
 
+// The key of a transition's prepared weights in the context's weight cache.
+static WeightKey transition_key(const TransitionLayout &L, const af2_transition_weights &w) {
+  WeightKey key;
+  key.kind = kWeightsTransition;
+  const void *ptrs[8] = {w.layer_norm_scale, w.layer_norm_offset, w.first_weight.values, w.first_weight.scales,
+                         w.first_bias,       w.second_weight.values, w.second_weight.scales, w.second_bias};
+  for (int i = 0; i < 8; ++i) key.ptr[i] = ptrs[i];
+  const int64_t dims[6] = {L.c, L.h, w.first_weight.format * 65536 + w.first_weight.block,
+                           w.second_weight.format * 65536 + w.second_weight.block, L.wide ? 1 : 0, L.cp};
+  for (int i = 0; i < 6; ++i) key.dim[i] = dims[i];
+  return key;
+}
+
 af2_status transition_prepare(af2_ctx *ctx, const TransitionLayout &L, const af2_transition_weights &w,
                               void *workspace, cudaStream_t stream) {
   uint8_t *ws = static_cast<uint8_t *>(workspace);
@@ -851,17 +864,23 @@ static af2_status transition_launch_wide(af2_ctx *ctx, const TransitionLayout &L
                                          const af2_transition_weights &w, double eps, int residual, void *out,
                                          int out_dtype, void *workspace, cudaStream_t stream) {
   uint8_t *ws = static_cast<uint8_t *>(workspace);
-  float *s1 = reinterpret_cast<float *>(ws + L.off_s1), *b1 = reinterpret_cast<float *>(ws + L.off_b1);
-  float *s2 = reinterpret_cast<float *>(ws + L.off_s2), *b2 = reinterpret_cast<float *>(ws + L.off_b2);
-  PrepJob jobs[2];
-  jobs[0] = PrepJob{w.first_weight, L.c, L.h, L.k1, L.n1, 1.f, ws + L.off_w1, s1};
-  jobs[1] = PrepJob{w.second_weight, L.h, L.c, L.k2, L.n2, 1.f, ws + L.off_w2, s2};
-  VectorSegments v{};
-  v.add(w.first_bias, L.h, L.n1, b1);
-  v.add(w.second_bias, L.c, L.n2, b2);
-  af2_status st;
-  if ((st = prepare_matrices(ctx, jobs, 2, stream)) != AF2_OK || (st = pad_vectors(ctx, v, stream)) != AF2_OK)
-    return st;
+  // the prepared weights: the layout's prefix [0, off_xn), in the weight cache or the workspace
+  PreparedRegion pw;
+  af2_status st = prepared_region(ctx, transition_key(L, w), L.off_xn, ws, true, &pw);
+  if (st != AF2_OK) return st;
+  uint8_t *wp = pw.base;
+  float *s1 = reinterpret_cast<float *>(wp + L.off_s1), *b1 = reinterpret_cast<float *>(wp + L.off_b1);
+  float *s2 = reinterpret_cast<float *>(wp + L.off_s2), *b2 = reinterpret_cast<float *>(wp + L.off_b2);
+  if (pw.fresh) {
+    PrepJob jobs[2];
+    jobs[0] = PrepJob{w.first_weight, L.c, L.h, L.k1, L.n1, 1.f, wp + L.off_w1, s1};
+    jobs[1] = PrepJob{w.second_weight, L.h, L.c, L.k2, L.n2, 1.f, wp + L.off_w2, s2};
+    VectorSegments v{};
+    v.add(w.first_bias, L.h, L.n1, b1);
+    v.add(w.second_bias, L.c, L.n2, b2);
+    if ((st = prepare_matrices(ctx, jobs, 2, stream)) != AF2_OK || (st = pad_vectors(ctx, v, stream)) != AF2_OK)
+      return st;
+  }
   const size_t xb = x_dtype == AF2_F32 ? 4 : 2, ob = out_dtype == AF2_F32 ? 4 : 2;
   __half *xn = reinterpret_cast<__half *>(ws + L.off_xn), *hid = reinterpret_cast<__half *>(ws + L.off_hid);
   for (int64_t r0 = 0; r0 < L.rows; r0 += L.chunk_rows) {
@@ -889,7 +908,7 @@ static af2_status transition_launch_wide(af2_ctx *ctx, const TransitionLayout &L
     LinearOperands g1;
     g1.a = xn;
     g1.lda = L.k1;
-    g1.w = ws + L.off_w1;
+    g1.w = wp + L.off_w1;
     g1.scale = s1;
     g1.bias = b1;
     g1.rows = rows;
@@ -904,7 +923,7 @@ static af2_status transition_launch_wide(af2_ctx *ctx, const TransitionLayout &L
     LinearOperands g2;
     g2.a = hid;
     g2.lda = L.hid_pitch;
-    g2.w = ws + L.off_w2;
+    g2.w = wp + L.off_w2;
     g2.scale = s2;
     g2.bias = b2;
     g2.rows = rows;
@@ -924,20 +943,24 @@ af2_status transition_launch(af2_ctx *ctx, const TransitionLayout &L, const void
                              const af2_transition_weights &w, double eps, int residual, void *out, int out_dtype,
                              void *workspace, cudaStream_t stream) {
   if (L.wide) return transition_launch_wide(ctx, L, x, x_dtype, w, eps, residual, out, out_dtype, workspace, stream);
-  af2_status st = transition_prepare(ctx, L, w, workspace, stream);
-  if (st != AF2_OK) return st;
   uint8_t *ws = static_cast<uint8_t *>(workspace);
+  // the prepared weights: the layout's prefix [0, off_xn), in the weight cache or the workspace
+  PreparedRegion pw;
+  af2_status st = prepared_region(ctx, transition_key(L, w), L.off_xn, ws, true, &pw);
+  if (st != AF2_OK) return st;
+  uint8_t *wp = pw.base;
+  if (pw.fresh && (st = transition_prepare(ctx, L, w, wp, stream)) != AF2_OK) return st;
   const int kb = static_cast<int>(L.cp / 64);
   CUtensorMap w1map, w2map;
-  if (!encode_map_3d(&w1map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, ws + L.off_w1, 64, L.hp, kb, 128,
+  if (!encode_map_3d(&w1map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, wp + L.off_w1, 64, L.hp, kb, 128,
                      (uint64_t)L.hp * 128, 64, HC, kb, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !encode_map_3d(&w2map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, ws + L.off_w2, 64, L.cp, L.hp / 64, 128,
+      !encode_map_3d(&w2map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, wp + L.off_w2, 64, L.cp, L.hp / 64, 128,
                      (uint64_t)L.cp * 128, 64, L.cp, 2, CU_TENSOR_MAP_SWIZZLE_128B))
     return fail(ctx, AF2_ERR_CUDA, "cuTensorMapEncodeTiled failed for the transition weights");
   const size_t xb = x_dtype == AF2_F32 ? 4 : 2, ob = out_dtype == AF2_F32 ? 4 : 2;
   const bool tma_out = out_dtype != AF2_F32 && L.c % 8 == 0;
   Args a{};
-  a.vec = reinterpret_cast<const float *>(ws + L.off_vec);
+  a.vec = reinterpret_cast<const float *>(wp + L.off_vec);
   a.c = (int)L.c;
   a.cp = (int)L.cp;
   a.kb = kb;
@@ -958,7 +981,7 @@ af2_status transition_launch(af2_ctx *ctx, const TransitionLayout &L, const void
       const unsigned blocks = (unsigned)((rows + warps - 1) / warps);
       {
         LaunchScope scope(ctx, stream, kProfTransitionNormalize);
-        const float *vec = reinterpret_cast<const float *>(ws + L.off_vec);
+        const float *vec = reinterpret_cast<const float *>(wp + L.off_vec);
         if (x_dtype == AF2_F32)
           normalize_kernel<float><<<blocks, warps * 32, 0, stream>>>(static_cast<const float *>(xsrc), rows, a.c,
                                                                      a.cp, vec, a.eps, xn);

@@ -1238,11 +1238,20 @@ static int shard_rank(const TriangleShard *shard) { return shard ? shard->rank :
 
 af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L, const void *z, int z_dtype,
                            const float *mask, const float *packed, double eps, int residual, void *out,
-                           int out_dtype, void *workspace, cudaStream_t stream, const TriangleShard *shard) {
+                           int out_dtype, void *workspace, cudaStream_t stream, const TriangleShard *shard,
+                           bool cache_weights) {
   using namespace tri;
   uint8_t *ws = static_cast<uint8_t *>(workspace);
-  __half *w16 = reinterpret_cast<__half *>(ws + L.off_w16);
-  float *vec = reinterpret_cast<float *>(ws + L.off_vec);
+  // the prepared weights: the layout's prefix [0, off_z16), in the weight cache or the workspace
+  WeightKey key;
+  key.kind = kWeightsTriangle;
+  key.ptr[0] = packed;
+  key.dim[0] = L.cz;
+  key.dim[1] = L.ch;
+  PreparedRegion pw;
+  if (af2_status st = prepared_region(ctx, key, L.off_z16, ws, cache_weights, &pw); st != AF2_OK) return st;
+  __half *w16 = reinterpret_cast<__half *>(pw.base + L.off_w16);
+  float *vec = reinterpret_cast<float *>(pw.base + L.off_vec);
   __half *a = reinterpret_cast<__half *>(ws + L.off_a);
   __half *b = reinterpret_cast<__half *>(ws + L.off_b);
   __half *x = reinterpret_cast<__half *>(ws + L.off_x);
@@ -1254,11 +1263,13 @@ af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L,
   const int64_t pairs = rows * L.n;
   const bool out_dir = direction == AF2_OUTGOING;
 
-  {
-    LaunchScope scope(ctx, stream, kProfTrianglePrepare);
-    prep_weights_kernel<<<96, 256, 0, stream>>>(packed, (int)L.cz, (int)L.ch, w16, vec);
+  if (pw.fresh) {
+    {
+      LaunchScope scope(ctx, stream, kProfTrianglePrepare);
+      prep_weights_kernel<<<96, 256, 0, stream>>>(packed, (int)L.cz, (int)L.ch, w16, vec);
+    }
+    if (cudaError_t e = cudaGetLastError(); e != cudaSuccess) return cuda_fail(ctx, e, "launch weight preparation");
   }
-  if (cudaError_t e = cudaGetLastError(); e != cudaSuccess) return cuda_fail(ctx, e, "launch weight preparation");
 
   const void *zsrc = z;
   int zt = z_dtype;

@@ -137,6 +137,21 @@ AF2_API af2_status af2_set_gemm_precision(af2_ctx *ctx, int precision);
 AF2_API int af2_get_gemm_precision(const af2_ctx *ctx);
 
 /*
+ * Prepared-weights cache (the role of the reference's packing cache per
+ * weights object, src/evoformer/block.ts:1310-1333).  While enabled, each
+ * device-form call looks its weights up by their device pointers and the
+ * dimensions their preparation depends on; the first call prepares them
+ * (f16 operand layouts, folded LayerNorm, scales) into a context-owned
+ * buffer, later calls skip the preparation kernels.  The caller promises
+ * that cached weights are not changed in place: after changing them call
+ * af2_clear_weight_cache (which synchronises the device and frees the
+ * buffers).  Off by default; disabling clears it.  The allocation-free
+ * triangle entry point never uses it.
+ */
+AF2_API af2_status af2_set_weight_cache(af2_ctx *ctx, int enable);
+AF2_API af2_status af2_clear_weight_cache(af2_ctx *ctx);
+
+/*
  * Per-kernel device timing (the counterpart of the reference's timestamp-query
  * profile, src/runtime/execution.ts:482-533).  While enabled every kernel
  * launch is bracketed by CUDA events on its own stream.  af2_profile_read
