@@ -71,11 +71,15 @@ def encode_outer_product_mean_sharded_tensors(device: Device, msa, msa_mask, pac
                                               pair_rows, *, residual: bool = True, row_block: int = 0,
                                               layer_norm_epsilon: float = 1e-5, normalization_epsilon: float = 1e-3,
                                               stream: int = 0):
-    """Row-sharded OPM: msa [S, N, c_m] and msa_mask [S, N] whole on every rank,
-    pair_rows [L, N, c_z] this rank's rows of the pair (updated when residual).
-    Collective: every rank calls it together."""
+    """Row-sharded OPM: msa [S, L, c_m] this rank's residue columns of the MSA,
+    msa_mask [S, N] the whole mask (the same on every rank), pair_rows [L, N, c_z]
+    this rank's rows of the pair (updated when residual).  Collective: every rank
+    calls it together."""
     from .opm import _TORCH_DTYPES as _T
-    s, n, cm = msa.shape
+    s, _, cm = msa.shape
+    n = pair_rows.shape[1]
+    if msa_mask.shape[-1] != n or n % msa.shape[1] != 0:
+        raise _lib.RangeError("msa must hold this rank's residue columns and msa_mask all N of them")
     for t in (msa, msa_mask, packed_weights, pair_rows):
         if not t.is_cuda or not t.is_contiguous():
             raise _lib.RangeError("tensors must be contiguous CUDA tensors")

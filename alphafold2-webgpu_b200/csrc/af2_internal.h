@@ -358,6 +358,7 @@ OpmLayout opm_layout(int64_t s, int64_t n, int64_t cm, int64_t c, int64_t cz, in
 // Row-sharded OPM: this rank's block of the right operand is all-gathered in place.
 struct OpmExchange {
   int rank = 0;
+  bool m_local = false;  // m holds only this rank's residue columns [S][rows][c_m]
   af2_status (*all_gather)(af2_ctx *ctx, void *full, size_t bytes_per_rank, cudaStream_t stream) = nullptr;
 };
 

@@ -25,8 +25,8 @@
 //                      projection.  Per direction a rank moves 3 (R-1)/R^2 of a
 //                      projected operand; every operand value and accumulation
 //                      order is the single-GPU one, so results are bit-identical.
-//   outer product mean every rank normalises and projects its own residue
-//                      columns of the (replicated) MSA; the right operand is
+//   outer product mean every rank holds, normalises and projects its own
+//                      residue columns of the MSA; the right operand is
 //                      all-gathered and each rank finishes its own rows.
 //   transition         row-local: no exchange.
 #include <dlfcn.h>
@@ -400,6 +400,7 @@ af2_status af2_outer_product_mean_sharded(af2_ctx *ctx, const af2_opm_shape *sha
   if ((st = ensure(ctx, ctx->workspace, L.total, "outer product mean scratch")) != AF2_OK) return st;
   OpmExchange ex;
   ex.rank = ctx->rank;
+  ex.m_local = true;
   ex.all_gather = nccl_all_gather_in_place;
   return opm_launch(ctx, L, m, m_dtype, mask, packed_weights, ln_eps, norm_eps, options ? options->residual : 0, out,
                     out_dtype, ctx->workspace.ptr, s, &ex);

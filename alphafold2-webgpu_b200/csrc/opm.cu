@@ -51,7 +51,9 @@ template <typename MT, bool VEC>
 __global__ void norm_kernel(const MT *__restrict__ m, int64_t rows, int cm, int cmp, const float *__restrict__ gamma,
                             const float *__restrict__ beta, float eps, __half *__restrict__ xn, int n_full, int col0,
                             int cols, int seqs, const float *__restrict__ mask_in, float *__restrict__ mask_out,
-                            int split) {
+                            int split, int m_cols, int m_col0) {
+  // m holds m_cols residue columns from m_col0 (n_full and col0 for a whole MSA; the rank's own
+  // columns, m_col0 = 0, for a row-sharded one); the mask is always the whole [S][n_full]
   // split (f32 precision mode): rows of 3 cmp, [f16(v) | f16(v) | f16(v - f16(v))], the A operand of a
   // projection whose weights are stacked [W_hi; W_lo; W_hi]
   // local row of the residue columns [col0, col0 + cols) of an [S][n_full] MSA:
@@ -59,9 +61,10 @@ __global__ void norm_kernel(const MT *__restrict__ m, int64_t rows, int cm, int 
   const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
-  const int64_t src = seqs > 0 ? (row % seqs) * n_full + col0 + row / seqs : (row / cols) * n_full + col0 + row % cols;
+  const int64_t sq = seqs > 0 ? row % seqs : row / cols, jl = seqs > 0 ? row / seqs : row % cols;
+  const int64_t src = sq * n_full + col0 + jl;
   if (lane == 0) mask_out[row] = mask_in[src];
-  const MT *xr = m + src * cm;
+  const MT *xr = m + (sq * m_cols + m_col0 + jl) * cm;
   float v[8];
   if (VEC) {
     if constexpr (sizeof(MT) == 4) {
@@ -239,6 +242,7 @@ constexpr uint32_t LP_SMEM = LP_OFF_VEC + 512 + 1024;
 struct LnProjArgs {
   const float *scale, *bias;  // per output column (64: left then right); gamma and beta are folded in
   const float *mask;          // [S][n_full]
+  int m_row0;                 // the MSA map's column of residue row0 (row0 for a whole MSA, 0 for the rank's own)
   const __half *w;            // [chunks][64][64] f16 operand rows
   __half *left, *right;       // left [c][rows][pitch]; right (this rank's block) [rows][c][pitch]
   int64_t n_full, rows, pitch;
@@ -308,7 +312,7 @@ __global__ void __launch_bounds__(LP_THREADS, 1)
         const uint32_t dst = sbase + LP_OFF_STAGE + s * LP_STAGE;
         mbar_arrive_expect_tx(full(s), stage_bytes);
         for (int kc = 0; kc < p.chunks; ++kc)
-          tma_load_3d(dst + kc * LP_CHUNK, &mmap, full(s), kc * 64, p.row0 + i, sb * 128);
+          tma_load_3d(dst + kc * LP_CHUNK, &mmap, full(s), kc * 64, p.m_row0 + i, sb * 128);
       }
       // every load issued has landed before the CTA exits (immediate unless a consumer gave up)
       for (int j = it > LP_STAGES ? it - LP_STAGES : 0; j < it; ++j)
@@ -1135,6 +1139,9 @@ af2_status opm_launch(af2_ctx *ctx, const OpmLayout &L, const void *m, int m_dty
   // into the projection's weights and biases)
   const bool lnproj = L.fused && m_dtype != AF2_F32 && cm % 8 == 0 && L.cmp <= 256 &&
                       reinterpret_cast<uintptr_t>(m) % 16 == 0;
+  // the MSA's residue columns: all n, or only this rank's rows when the exchange says so
+  const bool m_local = exchange && exchange->m_local;
+  const int64_t m_cols = m_local ? rows : n, m_col0 = m_local ? 0 : L.row0;
   const int64_t kx = L.split ? 3 : 1;
   // the prepared weights: the layout's prefix [0, off_xn), in the weight cache or the workspace
   WeightKey key;
@@ -1190,9 +1197,9 @@ af2_status opm_launch(af2_ctx *ctx, const OpmLayout &L, const void *m, int m_dty
   __half *right_full = reinterpret_cast<__half *>(ws + L.off_right);
   if (lnproj) {
     CUtensorMap mmap;
-    // m [S][n][c_m] viewed as {c_m, n, S}: a box is 64 channels x 1 residue x 128 sequences
+    // m [S][m_cols][c_m] viewed as {c_m, m_cols, S}: a box is 64 channels x 1 residue x 128 sequences
     if (!encode_map_3d(&mmap, m_dtype == AF2_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-                       m, cm, n, s, cm * 2, (uint64_t)n * cm * 2, 64, 1, 128, CU_TENSOR_MAP_SWIZZLE_128B))
+                       m, cm, m_cols, s, cm * 2, (uint64_t)m_cols * cm * 2, 64, 1, 128, CU_TENSOR_MAP_SWIZZLE_128B))
       return fail(ctx, AF2_ERR_CUDA, "cuTensorMapEncodeTiled failed for the OPM's MSA map");
     LnProjArgs a{};
     a.scale = wlr_scale;
@@ -1202,6 +1209,7 @@ af2_status opm_launch(af2_ctx *ctx, const OpmLayout &L, const void *m, int m_dty
     a.left = reinterpret_cast<__half *>(ws + L.off_left);
     a.right = right_full + (size_t)rank * L.seq_pitch * rows * c;
     a.n_full = n;
+    a.m_row0 = (int)m_col0;
     a.rows = rows;
     a.pitch = L.seq_pitch;
     a.row0 = (int)L.row0;
@@ -1239,11 +1247,11 @@ af2_status opm_launch(af2_ctx *ctx, const OpmLayout &L, const void *m, int m_dty
       if (vec)
         norm_kernel<MT, true><<<blocks, warps * 32, 0, stream>>>(mp, xrows, (int)cm, (int)L.cmp, ln, ln + L.cmp,
                                                                  (float)ln_eps, xn, (int)n, (int)L.row0, (int)rows,
-                                                                 L.fused ? (int)s : 0, mask, mask_loc, L.split);
+                                                                 L.fused ? (int)s : 0, mask, mask_loc, L.split, (int)m_cols, (int)m_col0);
       else
         norm_kernel<MT, false><<<blocks, warps * 32, 0, stream>>>(mp, xrows, (int)cm, (int)L.cmp, ln, ln + L.cmp,
                                                                   (float)ln_eps, xn, (int)n, (int)L.row0, (int)rows,
-                                                                  L.fused ? (int)s : 0, mask, mask_loc, L.split);
+                                                                  L.fused ? (int)s : 0, mask, mask_loc, L.split, (int)m_cols, (int)m_col0);
     };
     if (m_dtype == AF2_F32)
       run(float{});

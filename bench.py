@@ -226,6 +226,64 @@ def transition_weights(rng, c=CZ, h=HIDDEN):
             "w2": q8(w2), "b2": np.zeros(c, np.float32)}
 
 
+def multimer_block(dev, torch, af2cuda, rng, world: int, rank: int, sh: int, stream, dist, steps: int = 10) -> dict:
+    """BASELINE config 5 on the job's GPUs: triangle multiplication out + in and the pair transition on a
+    bf16 pair [2048, 2048, 128] (rows sharded over the ranks), mask 1 inside the four 512-residue chain
+    blocks; `steps` timed on CUDA events after 3 warm-up steps, max over ranks."""
+    n = 2048
+    rows = n // world
+    r0 = rank * rows
+    gen = torch.Generator(device="cuda").manual_seed(2048 + rank)
+    pair = torch.randn(rows, n, CZ, device="cuda", generator=gen).to(torch.bfloat16)
+    chain = torch.arange(n, device="cuda") // 512
+    mask = (chain[r0:r0 + rows, None] == chain[None, :]).float().contiguous()
+    w_tri = [torch.from_numpy(synthetic_weights(rng)).cuda() for _ in range(2)]
+    tw = transition_weights(rng)
+    tws = {"layerNormScale": torch.from_numpy(tw["ln"][0]).cuda(), "layerNormOffset": torch.from_numpy(tw["ln"][1]).cuda(),
+           "firstWeight": af2cuda.Q8Matrix(torch.from_numpy(tw["w1"][0]).cuda(), torch.from_numpy(tw["w1"][1]).cuda()),
+           "firstBias": torch.from_numpy(tw["b1"]).cuda(),
+           "secondWeight": af2cuda.Q8Matrix(torch.from_numpy(tw["w2"][0]).cuda(), torch.from_numpy(tw["w2"][1]).cuda()),
+           "secondBias": torch.from_numpy(tw["b2"]).cuda()}
+    torch.cuda.synchronize()
+
+    def step():
+        for d in (0, 1):
+            if world > 1:
+                af2cuda.encode_triangle_multiplication_sharded_tensors(dev, d, pair, mask, w_tri[d], n, residual=True,
+                                                                       stream=sh)
+            else:
+                af2cuda.encode_triangle_multiplication_tensors(dev, d, pair, mask, w_tri[d], residual=True, stream=sh)
+        af2cuda.encode_transition_tensors(dev, pair.view(rows * n, CZ), tws, residual=True, stream=sh)
+
+    for _ in range(3):
+        step()
+    dev.sync(sh)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(steps):
+        step()
+    t1.record(stream)
+    t1.synchronize()
+    dev.sync(sh)
+    ms = t0.elapsed_time(t1) / steps
+    if dist:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    flops = 2 * triangle_flops(n) + transition_flops(n)
+    del pair
+    torch.cuda.empty_cache()
+    return {"workload": "BASELINE config 5: N=2048 (4 chains x 512, mask 1 inside the chain blocks), triangle "
+                        "multiplication out + in and the pair transition on a bf16 pair updated in place, rows "
+                        "sharded over the job's GPUs",
+            "ms_per_block": ms, "tflops": flops / (ms * 1e-3) / 1e12,
+            "per_gpu_tflops": flops / (ms * 1e-3) / 1e12 / world, "flops_per_block": flops, "steps": steps,
+            "warmup": 3, "n_gpus": world}
+
+
 def cpu_block_rate(n: int, s: int, threads: int) -> tuple[float, float, str]:
     """Times the oracle (CPU restatement of the reference's CPU path) on one block
     at pair length n and s MSA rows: triangle out + in, OPM, pair transition.
@@ -333,10 +391,14 @@ def run_ours(args) -> None:
     rng = np.random.default_rng(1234)
     gen = torch.Generator(device="cuda").manual_seed(1234 + rank)
     pair = torch.randn(rows, N, CZ, device="cuda", generator=gen).to(torch.bfloat16)
+    pair_init = pair.clone()  # the step's input before any step ran (the sharded bit-identity check)
     mask = torch.ones(rows, N, device="cuda")
-    msa = torch.randn(S_MSA, N, CM, device="cuda", generator=gen).to(torch.bfloat16)
-    msa_mask = (torch.rand(S_MSA, N, device="cuda", generator=gen) < 0.9).float()
+    # one MSA for the whole job (the same on every rank); a rank holds its own residue columns
+    gen_msa = torch.Generator(device="cuda").manual_seed(4321)
+    msa_full = torch.randn(S_MSA, N, CM, device="cuda", generator=gen_msa).to(torch.bfloat16)
+    msa_mask = (torch.rand(S_MSA, N, device="cuda", generator=gen_msa) < 0.9).float()
     msa_mask[0] = 1
+    msa = msa_full[:, rank * rows:(rank + 1) * rows].contiguous() if sharded else msa_full
     w_out = torch.from_numpy(synthetic_weights(rng)).cuda()
     w_in = torch.from_numpy(synthetic_weights(rng)).cuda()
     w_opm = torch.from_numpy(opm_weights(rng)).cuda()
@@ -431,7 +493,7 @@ def run_ours(args) -> None:
     # the two directions share PCIe full duplex; the timed region spans all copies of all steps.
     host_pair = torch.empty(rows, N, CZ, dtype=torch.bfloat16, pin_memory=True)
     host_pair.copy_(pair.cpu())
-    host_msa = torch.empty(S_MSA, N, CM, dtype=torch.bfloat16, pin_memory=True)
+    host_msa = torch.empty(msa.shape, dtype=torch.bfloat16, pin_memory=True)
     host_msa.copy_(msa.cpu())
     host_out = torch.empty_like(host_pair, pin_memory=True)
     pairs2, msas2 = [pair, torch.empty_like(pair)], [msa, torch.empty_like(msa)]
@@ -478,10 +540,40 @@ def run_ours(args) -> None:
     e2e = {"value": flops_step * e2e_steps / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
            "h2d_bytes_per_step": host_pair.numel() * 2 + host_msa.numel() * 2,
            "d2h_bytes_per_step": host_out.numel() * 2, "ms_per_step": e2e_ms / e2e_steps,
-           "path": "pair (this rank's rows) and MSA copied in from pinned host memory, the block through the "
-                   "af2cuda device-form API (outer product mean, triangle multiplication x2, transition; the "
-                   "row-sharded forms on several GPUs), pair rows read back; copies of neighbouring steps "
-                   "overlap the block (two device input buffers, separate copy streams)"}
+           "path": "pair (this rank's rows) and MSA (this rank's residue columns) copied in from pinned host "
+                   "memory, the block through the af2cuda device-form API (outer product mean, triangle "
+                   "multiplication x2, transition; the row-sharded forms on several GPUs), pair rows read back; "
+                   "copies of neighbouring steps overlap the block (two device input buffers, separate copy "
+                   "streams)"}
+
+    # ---- sharded: one step checked bit for bit against the single-GPU block on rank 0 ----
+    identical = None
+    if sharded:
+        got = pair_init.clone()
+        step(got, msa)
+        dev.sync(sh)
+        torch.cuda.synchronize()
+        inits = [torch.empty_like(pair_init) for _ in range(world)]
+        outs = [torch.empty_like(got) for _ in range(world)]
+        dist.all_gather(inits, pair_init)
+        dist.all_gather(outs, got)
+        flag = torch.zeros(1, device="cuda")
+        if rank == 0:
+            whole = torch.cat(inits).contiguous()
+            mask_whole = torch.ones(N, N, device="cuda")
+            af2cuda.encode_outer_product_mean_tensors(dev, msa_full, msa_mask, w_opm, C_OUTER, CZ, pair=whole,
+                                                      residual=True, stream=sh)
+            af2cuda.encode_triangle_multiplication_tensors(dev, 0, whole, mask_whole, w_out, residual=True, stream=sh)
+            af2cuda.encode_triangle_multiplication_tensors(dev, 1, whole, mask_whole, w_in, residual=True, stream=sh)
+            af2cuda.encode_transition_tensors(dev, whole.view(N * N, CZ), tws, residual=True, stream=sh)
+            dev.sync(sh)
+            flag[0] = 1.0 if torch.equal(whole, torch.cat(outs)) else 0.0
+        dist.broadcast(flag, src=0)
+        identical = bool(flag.item() == 1.0)
+
+    # ---- the multimer config: N=2048, chain-block mask, triangle out + in and the
+    # pair transition, rows sharded over the same ranks ----
+    multimer = multimer_block(dev, torch, af2cuda, rng, world, rank, sh, stream, dist)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -517,7 +609,10 @@ def run_ours(args) -> None:
             "per_gpu_tflops": value / world,
             "roofline": roofline, "kernels": kernel, "cpu_baseline": cpu, "e2e": e2e,
             "gpu_launches": int(launches), "clocks": clocks.record(),
+            "multimer_n2048": multimer,
         }
+        if identical is not None:
+            line["sharded_bit_identical"] = identical
         print(json.dumps(line), flush=True)
     if sharded:
         af2cuda.comm_destroy(dev)

@@ -260,11 +260,12 @@ AF2_API af2_status af2_triangle_multiplication_sharded(af2_ctx *ctx, int directi
                                                        void *out, int out_dtype, void *stream);
 
 /*
- * The device form of the outer-product mean on a row-sharded pair: m [S, N,
- * c_m] and mask [S, N] are the whole MSA (every rank passes the same), out
- * holds this rank's rows [rank * L, (rank + 1) * L) of the [N, N, c_z] update
- * (L = N / nranks, a multiple of 8).  Each rank normalises and projects only
- * its own residues; the right operand is all-gathered.  Collective.
+ * The device form of the outer-product mean on a row-sharded pair: m [S, L,
+ * c_m] holds this rank's residue columns [rank * L, (rank + 1) * L) of the
+ * MSA, mask [S, N] the whole MSA mask (every rank passes the same), out this
+ * rank's rows of the [N, N, c_z] update (L = N / nranks, a multiple of 8).
+ * Each rank normalises and projects its own residues; the right operand is
+ * all-gathered.  Collective.
  */
 struct af2_opm_shape;
 struct af2_opm_options;

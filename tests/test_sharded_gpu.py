@@ -81,7 +81,9 @@ def _worker(rank, nranks, port, result):
         pair_rows = pair_full[r0:r1].clone()
         torch.cuda.synchronize()
         af2cuda.encode_outer_product_mean_tensors(dev, msa, msa_mask_d, pw, 32, 128, pair=pair_full, residual=True)
-        af2cuda.encode_outer_product_mean_sharded_tensors(dev, msa, msa_mask_d, pw, 32, 128, pair_rows, residual=True)
+        msa_cols = msa[:, r0:r1].contiguous()  # this rank's residue columns
+        af2cuda.encode_outer_product_mean_sharded_tensors(dev, msa_cols, msa_mask_d, pw, 32, 128, pair_rows,
+                                                          residual=True)
         dev.sync()
         ok &= bool(torch.equal(pair_rows, pair_full[r0:r1]))
         af2cuda.comm_destroy(dev)
