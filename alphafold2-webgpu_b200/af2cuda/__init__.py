@@ -22,6 +22,10 @@ from .sharded import (comm_destroy, comm_init, comm_unique_id, encode_outer_prod
 from .transition import (Q8Matrix, TransitionGpu, TransitionInput, TransitionResult, TransitionWeights,
                          dequant_q8_tensors, encode_transition_tensors, pack_transition_weights,
                          transition_weight_count, transition_workspace_bytes, validate_transition_input)
+from .tensor_store import (FileTensorStore, block_range, quantize_q8_block, read_tensor_range, tensor_byte_length,
+                           tensor_elements, write_tensor_manifest)
+from .weights import (encode_outer_product_mean_weight_tensors, encode_triangle_multiplication_weight_tensors,
+                      opm_tensor_sizes, stored_weights, triangle_tensor_sizes)
 from .types import (ORDER, TriangleMultiplicationInput, TriangleMultiplicationWeights, TriangleShape,
                     error_metrics, expected_weight_element_count, pack_weights, validate_triangle_input)
 
@@ -40,5 +44,8 @@ __all__ = [
     "encode_outer_product_mean_sharded_tensors", "AttentionGpu", "AttentionInput", "AttentionResult",
     "AttentionWeights", "NormalizedInputPairBias", "SeparatePairBias", "attention_weight_count",
     "attention_workspace_bytes", "encode_attention_tensors", "encode_triangle_attention_tensors",
-    "pack_attention_weights", "encode_evoformer_pair_block_tensors",
+    "pack_attention_weights", "encode_evoformer_pair_block_tensors", "FileTensorStore", "block_range",
+    "quantize_q8_block", "read_tensor_range", "tensor_byte_length", "tensor_elements", "write_tensor_manifest",
+    "encode_outer_product_mean_weight_tensors", "encode_triangle_multiplication_weight_tensors", "opm_tensor_sizes",
+    "stored_weights", "triangle_tensor_sizes",
 ]

@@ -127,6 +127,11 @@ SIGNATURES = {
     "af2_triangle_multiplication_static": (_i32, [_vp, _i32, ctypes.POINTER(TriangleShape), _vp, _i32, _vp, _vp, _i64,
                                                   _f64, ctypes.POINTER(TriangleOptions), _vp, _i32, _vp]),
     "af2_dequant_q8": (_i32, [_vp, ctypes.POINTER(Matrix), _i64, _i64, _vp, _vp]),
+    "af2_triangle_multiplication_weights": (_i32, [_vp, _i32, ctypes.POINTER(TriangleShape), _vp, _i32, _vp,
+                                                   ctypes.POINTER(Matrix), _f64, ctypes.POINTER(TriangleOptions), _vp,
+                                                   _i32, _vp, _vp]),
+    "af2_outer_product_mean_weights": (_i32, [_vp, ctypes.POINTER(OpmShape), _vp, _i32, _vp, ctypes.POINTER(Matrix),
+                                              ctypes.POINTER(OpmOptions), _vp, _i32, _vp, _vp]),
     "af2_transition_weight_count": (_i64, [_i64, _i64]),
     "af2_transition_check": (_i32, [ctypes.POINTER(TransitionShape), _i64, _f64, ctypes.c_char_p, ctypes.c_size_t]),
     "af2_transition_workspace_bytes": (_i32, [ctypes.POINTER(TransitionShape), ctypes.POINTER(ctypes.c_uint64)]),

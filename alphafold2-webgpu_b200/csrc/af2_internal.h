@@ -26,7 +26,7 @@ namespace af2 {
 // dimensions and options the preparation depends on.
 struct WeightKey {
   int kind = 0;
-  const void *ptr[8] = {};
+  const void *ptr[32] = {};
   int64_t dim[8] = {};
   bool operator==(const WeightKey &o) const;
 };
@@ -34,7 +34,10 @@ struct CachedWeights {
   WeightKey key;
   DeviceBuffer buf;
 };
-enum WeightKind { kWeightsTriangle = 1, kWeightsOpm, kWeightsTransition, kWeightsAttention, kWeightsLinear };
+enum WeightKind {
+  kWeightsTriangle = 1, kWeightsOpm, kWeightsTransition, kWeightsAttention, kWeightsLinear, kWeightsTriangleTensors,
+  kWeightsOpmTensors
+};
 }  // namespace af2
 
 namespace af2 {
@@ -208,10 +211,11 @@ struct TriangleShard {
 
 // Launches the whole op on `stream`; the workspace holds TriangleLayout::total bytes.
 // cache_weights = false keeps the call from allocating a weight-cache entry (the static-scratch form).
+// tensors (16 matrices in ORDER, f32 or q8 block; NULL: `packed` holds them) replaces `packed`.
 af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L, const void *z, int z_dtype,
                            const float *mask, const float *packed, double eps, int residual, void *out,
                            int out_dtype, void *workspace, cudaStream_t stream, const TriangleShard *shard = nullptr,
-                           bool cache_weights = true);
+                           bool cache_weights = true, const af2_matrix *tensors = nullptr);
 
 // ---- transition (transition.cu) ----
 
@@ -348,6 +352,9 @@ struct OpmLayout {
   bool split = false;        // f32 precision mode: every GEMM operand as an f16 hi / lo pair, K tripled
   int64_t seq_pitch = 0;    // fused: left [c][rows][seq_pitch] and right [n][c][seq_pitch], K-major
   size_t off_ln = 0, off_xn = 0, off_mask = 0, off_left = 0, off_right = 0, off_rowscale = 0, off_outer = 0;
+  // per-tensor weights: the decoded small tensors (LayerNorm, W_left, W_right, biases) in f32,
+  // read only by the preparation, which runs before the kernels that reuse this region
+  size_t off_stage = 0;
   size_t total = 0;
 };
 
@@ -364,7 +371,10 @@ struct OpmExchange {
 
 af2_status opm_launch(af2_ctx *ctx, const OpmLayout &L, const void *m, int m_dtype, const float *mask,
                       const float *packed, double ln_eps, double norm_eps, int residual, void *out, int out_dtype,
-                      void *workspace, cudaStream_t stream, const OpmExchange *exchange = nullptr);
+                      void *workspace, cudaStream_t stream, const OpmExchange *exchange = nullptr,
+                      const af2_matrix *tensors = nullptr);
+// tensors (8 matrices in packOuterProductMeanWeights order, f32 or q8 block; NULL: `packed` holds
+// them) replaces `packed`.
 
 // ---- gated multi-head attention (attention.cu) ----
 

@@ -52,8 +52,10 @@ af2_status ensure(af2_ctx *ctx, DeviceBuffer &buf, size_t bytes, const char *wha
 
 bool WeightKey::operator==(const WeightKey &o) const {
   if (kind != o.kind) return false;
+  for (int i = 0; i < 32; ++i)
+    if (ptr[i] != o.ptr[i]) return false;
   for (int i = 0; i < 8; ++i)
-    if (ptr[i] != o.ptr[i] || dim[i] != o.dim[i]) return false;
+    if (dim[i] != o.dim[i]) return false;
   return true;
 }
 
@@ -501,6 +503,54 @@ af2_status af2_triangle_multiplication(af2_ctx *ctx, int direction, const af2_tr
                          options ? options->residual : 0, out, out_dtype, ws, s);
 }
 
+// One tensor each (the reference's TensorStore records): f32, or int8 codes with f16 block scales.
+static af2_status validate_tensors(af2_ctx *ctx, const af2_matrix *tensors, int count, const char *op) {
+  if (!tensors) return fail(ctx, AF2_ERR_INVALID_ARGUMENT, std::string(op) + " weight tensors are NULL");
+  for (int t = 0; t < count; ++t) {
+    const af2_matrix &m = tensors[t];
+    const std::string name = std::string(op) + " weight tensor " + std::to_string(t);
+    if (m.format == AF2_WEIGHTS_Q8_CHANNEL)
+      return fail(ctx, AF2_ERR_UNSUPPORTED, name + ": per-channel q8 is for the transition's matrices only");
+    if (af2_status st = validate_matrix(ctx, m, name.c_str()); st != AF2_OK) return st;
+    if (m.format == AF2_WEIGHTS_F32 && reinterpret_cast<uintptr_t>(m.values) % 4 != 0)
+      return fail(ctx, AF2_ERR_INVALID_ARGUMENT, name + ": f32 values must be 4-byte aligned");
+    if (m.format == AF2_WEIGHTS_Q8_BLOCK && reinterpret_cast<uintptr_t>(m.scales) % 2 != 0)
+      return fail(ctx, AF2_ERR_INVALID_ARGUMENT, name + ": scales must be 2-byte aligned");
+  }
+  return AF2_OK;
+}
+
+af2_status af2_triangle_multiplication_weights(af2_ctx *ctx, int direction, const af2_triangle_shape *shape,
+                                               const void *z, int z_dtype, const float *mask,
+                                               const af2_matrix *tensors, double epsilon,
+                                               const af2_triangle_options *options, void *out, int out_dtype,
+                                               void *workspace, void *stream) {
+  if (!ctx) return AF2_ERR_INVALID_ARGUMENT;
+  af2_status st = shape ? validate_triangle(ctx, direction, shape, af2_triangle_weight_count(shape->c_z, shape->c_hidden),
+                                            epsilon)
+                        : fail(ctx, AF2_ERR_INVALID_ARGUMENT, "shape is NULL");
+  if (st != AF2_OK) return st;
+  if ((st = validate_tensors(ctx, tensors, AF2_TRIANGLE_TENSORS, "triangle")) != AF2_OK) return st;
+  if (!z || !mask || !out) return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "a tensor pointer is NULL");
+  if (!valid_dtype(z_dtype) || !valid_dtype(out_dtype))
+    return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "dtype must be AF2_F32, AF2_F16 or AF2_BF16");
+  if (options && options->block_rows < 0)
+    return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "blockRows must be a positive safe integer");
+  cudaSetDevice(ctx->device);
+  const TriangleLayout L = triangle_layout(shape->length, shape->c_z, shape->c_hidden,
+                                           options ? options->block_rows : 0, z_dtype);
+  void *ws = workspace;
+  if (!ws) {
+    if ((st = ensure(ctx, ctx->workspace, L.total, "triangle scratch")) != AF2_OK) return st;
+    ws = ctx->workspace.ptr;
+  } else if (reinterpret_cast<uintptr_t>(ws) % 256 != 0) {
+    return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "workspace must be 256-byte aligned");
+  }
+  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+  return triangle_launch(ctx, direction, L, z, z_dtype, mask, nullptr, epsilon, options ? options->residual : 0, out,
+                         out_dtype, ws, s, nullptr, true, tensors);
+}
+
 af2_status af2_triangle_multiplication_host(af2_ctx *ctx, int direction, const af2_triangle_shape *shape,
                                             const void *z, const float *mask, const float *packed_weights,
                                             int64_t weight_count, double epsilon,
@@ -770,6 +820,39 @@ af2_status af2_outer_product_mean(af2_ctx *ctx, const af2_opm_shape *shape, cons
   }
   cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
   return opm_launch(ctx, L, m, m_dtype, mask, packed_weights, ln_eps, norm_eps, residual, out, out_dtype, ws, s);
+}
+
+af2_status af2_outer_product_mean_weights(af2_ctx *ctx, const af2_opm_shape *shape, const void *m, int m_dtype,
+                                          const float *mask, const af2_matrix *tensors,
+                                          const af2_opm_options *options, void *out, int out_dtype, void *workspace,
+                                          void *stream) {
+  if (!ctx) return AF2_ERR_INVALID_ARGUMENT;
+  if (!shape) return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "shape is NULL");
+  af2_status st = validate_opm(ctx, shape, af2_opm_weight_count(shape));
+  if (st != AF2_OK) return st;
+  if ((st = validate_tensors(ctx, tensors, AF2_OPM_TENSORS, "outer product mean")) != AF2_OK) return st;
+  if (!m || !mask || !out) return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "a tensor pointer is NULL");
+  if (!valid_dtype(m_dtype) || !valid_dtype(out_dtype))
+    return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "dtype must be AF2_F32, AF2_F16 or AF2_BF16");
+  double ln_eps, norm_eps;
+  int rb, residual;
+  if ((st = opm_options(ctx, options, &ln_eps, &norm_eps, &rb, &residual)) != AF2_OK) return st;
+  cudaSetDevice(ctx->device);
+  const OpmLayout L = opm_layout(shape->sequences, shape->length, shape->c_m, shape->c_outer, shape->c_z, rb, 0, 0,
+                                 ctx->gemm_precision == AF2_GEMM_F32);
+  void *ws = workspace;
+  if (ws && L.split)
+    return fail(ctx, AF2_ERR_INVALID_ARGUMENT,
+                "in the AF2_GEMM_F32 precision the outer product mean takes context-owned scratch (workspace NULL)");
+  if (!ws) {
+    if ((st = ensure(ctx, ctx->workspace, L.total, "outer product mean scratch")) != AF2_OK) return st;
+    ws = ctx->workspace.ptr;
+  } else if (reinterpret_cast<uintptr_t>(ws) % 256 != 0) {
+    return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "workspace must be 256-byte aligned");
+  }
+  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+  return opm_launch(ctx, L, m, m_dtype, mask, nullptr, ln_eps, norm_eps, residual, out, out_dtype, ws, s, nullptr,
+                    tensors);
 }
 
 af2_status af2_outer_product_mean_host(af2_ctx *ctx, const af2_opm_shape *shape, const void *m, const float *mask,

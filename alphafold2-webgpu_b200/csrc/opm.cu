@@ -1051,7 +1051,8 @@ OpmLayout opm_layout(int64_t s, int64_t n, int64_t cm, int64_t c, int64_t cz, in
   L.off_right = take((size_t)kx * seq_span * n * c * 2);  // every rank's block: [ranks][S][rows][c], or [n][c][pitch]
   L.off_rowscale = take((size_t)L.rows * n * 4);
   L.off_outer = take(L.fused ? 0 : (size_t)kx * rb * n * c * c * 2);
-  L.total = off;
+  L.off_stage = L.off_xn;
+  L.total = std::max(off, align_up(L.off_stage + (size_t)(2 * cm + 2 * (cm * c + c) + cz) * 4, 256));
   return L;
 }
 
@@ -1126,13 +1127,17 @@ af2_status fused_launch(af2_ctx *ctx, const OpmLayout &L, uint8_t *ws, const uin
 
 af2_status opm_launch(af2_ctx *ctx, const OpmLayout &L, const void *m, int m_dtype, const float *mask,
                       const float *packed, double ln_eps, double norm_eps, int residual, void *out, int out_dtype,
-                      void *workspace, cudaStream_t stream, const OpmExchange *exchange) {
+                      void *workspace, cudaStream_t stream, const OpmExchange *exchange, const af2_matrix *tensors) {
   uint8_t *ws = static_cast<uint8_t *>(workspace);
   const int64_t s = L.s, n = L.n, cm = L.cm, c = L.c, cz = L.cz, rows = L.rows;
   const int rank = exchange ? exchange->rank : 0;
   // packOuterProductMeanWeights order (outer-product-mean.ts:68-72).
-  const float *ln_w = packed, *ln_b = ln_w + cm, *lw = ln_b + cm, *lb = lw + cm * c, *rw = lb + c, *rb = rw + cm * c;
-  const float *ow = rb + c, *ob = ow + c * c * cz;
+  const float *ln_w = nullptr, *ln_b = nullptr, *lw = nullptr, *lb = nullptr, *rw = nullptr, *rb = nullptr;
+  const float *ow = nullptr, *ob = nullptr;
+  if (!tensors) {
+    ln_w = packed, ln_b = ln_w + cm, lw = ln_b + cm, lb = lw + cm * c, rw = lb + c, rb = rw + cm * c;
+    ow = rb + c, ob = ow + c * c * cz;
+  }
   const int64_t lr_cols = linear_cols_pad(2 * c), o_cols = linear_cols_pad(cz), o_inner = align_up(c * c, 64);
   af2_status st;
   // 16-bit MSA, fused layouts: LayerNorm and projection in one kernel (gamma and beta folded
@@ -1145,8 +1150,10 @@ af2_status opm_launch(af2_ctx *ctx, const OpmLayout &L, const void *m, int m_dty
   const int64_t kx = L.split ? 3 : 1;
   // the prepared weights: the layout's prefix [0, off_xn), in the weight cache or the workspace
   WeightKey key;
-  key.kind = kWeightsOpm;
+  key.kind = tensors ? kWeightsOpmTensors : kWeightsOpm;
   key.ptr[0] = packed;
+  if (tensors)
+    for (int t = 0; t < 8; ++t) key.ptr[t] = tensors[t].values, key.ptr[8 + t] = tensors[t].scales;
   const int64_t dims[7] = {cm, c, cz, L.out_shift, lnproj ? 1 : 0, L.split ? 1 : 0, L.cmp};
   for (int i = 0; i < 7; ++i) key.dim[i] = dims[i];
   PreparedRegion pw;
@@ -1156,8 +1163,26 @@ af2_status opm_launch(af2_ctx *ctx, const OpmLayout &L, const void *m, int m_dty
   float *wo_scale = reinterpret_cast<float *>(wp + L.off_wo_scale), *wo_bias = reinterpret_cast<float *>(wp + L.off_wo_bias);
   float *ln = reinterpret_cast<float *>(wp + L.off_ln);
   // ---- weights ----
+  if (tensors && pw.fresh) {
+    // the small tensors in f32: f32 ones as given, q8 ones decoded into the staging region
+    // (the products code x f16 scale are exact in f32, so the decode is the reference's own)
+    float *stage = reinterpret_cast<float *>(ws + L.off_stage);
+    const float **dst[7] = {&ln_w, &ln_b, &lw, &lb, &rw, &rb, &ob};
+    const int src[7] = {0, 1, 2, 3, 4, 5, 7};
+    const int64_t count[7] = {cm, cm, cm * c, c, cm * c, c, cz};
+    for (int i = 0; i < 7; ++i) {
+      const af2_matrix &t = tensors[src[i]];
+      if (t.format == AF2_WEIGHTS_F32) {
+        *dst[i] = static_cast<const float *>(t.values);
+      } else {
+        if ((st = dequant_launch(ctx, t, 1, count[i], stage, stream)) != AF2_OK) return st;
+        *dst[i] = stage;
+      }
+      stage += count[i];
+    }
+  }
   const af2_matrix left_m{AF2_WEIGHTS_F32, 0, lw, nullptr}, right_m{AF2_WEIGHTS_F32, 0, rw, nullptr};
-  const af2_matrix out_m{AF2_WEIGHTS_F32, 0, ow, nullptr};
+  const af2_matrix out_m = tensors ? tensors[6] : af2_matrix{AF2_WEIGHTS_F32, 0, ow, nullptr};
   VectorSegments vs{};
   vs.add(lb, c, c, wlr_bias);
   vs.add(rb, c, lr_cols - c, wlr_bias + c);

@@ -52,30 +52,53 @@ enum {
 };
 
 // ---------------------------------------------------------------------------
-// Weight preparation: the packed f32 array in the reference's ORDER
+// Weight preparation: the 16 tensors of the reference's ORDER
 // (src/triangle/weights.ts:4-10) -> zero-padded f16 matrices + f32 vectors.
+// They arrive either as the packed f32 array or as one tensor each, f32 or
+// mixed-q8 (int8 codes with an f16 scale per 64-element block of the
+// flattened tensor, src/reference/dtype.ts:86-97); q8 codes are decoded here,
+// on the way into the f16 operands.
 // ---------------------------------------------------------------------------
-__global__ void prep_weights_kernel(const float *__restrict__ packed, int cz, int ch, __half *__restrict__ w16,
-                                    float *__restrict__ vec) {
+enum {
+  kTLnInW = 0, kTLnInB, kTApW, kTApB, kTAgW, kTAgB, kTBpW, kTBpB, kTBgW, kTBgB, kTLnOutW, kTLnOutB, kTZW, kTZB,
+  kTGW, kTGB, kTensorCount
+};
+
+// The packed f32 array: tensor t starts at offset[t].
+struct PackedAccess {
+  const float *packed;
+  int64_t offset[kTensorCount];
+  __device__ __forceinline__ float operator()(int t, int64_t i) const { return packed[offset[t] + i]; }
+};
+
+// One tensor each: f32 values or block-scaled int8 codes.
+struct TensorAccess {
+  const void *values[kTensorCount];
+  const uint16_t *scales[kTensorCount];  // NULL: f32
+  int block[kTensorCount];
+  __device__ __forceinline__ float operator()(int t, int64_t i) const {
+    if (!scales[t]) return static_cast<const float *>(values[t])[i];
+    const float code = static_cast<float>(static_cast<const int8_t *>(values[t])[i]);
+    return code * __half2float(__ushort_as_half(scales[t][i / block[t]]));
+  }
+};
+
+template <typename Acc>
+__global__ void prep_weights_kernel(const Acc w, int cz, int ch, __half *__restrict__ w16, float *__restrict__ vec) {
   // The LayerNorm affine maps are folded into the projections that follow
   // them: LN(x) W^T + b = ((x - mean) rstd) (W diag(gamma))^T + (b + W beta),
   // so the kernels normalise without gamma/beta and the weights carry them.
-  const int64_t o_lniw = 0, o_lnib = cz, o_apw = 2 * cz;
-  const int64_t o_apb = o_apw + (int64_t)ch * cz, o_agw = o_apb + ch, o_agb = o_agw + (int64_t)ch * cz;
-  const int64_t o_bpw = o_agb + ch, o_bpb = o_bpw + (int64_t)ch * cz, o_bgw = o_bpb + ch;
-  const int64_t o_bgb = o_bgw + (int64_t)ch * cz, o_lnow = o_bgb + ch, o_lnob = o_lnow + ch;
-  const int64_t o_zw = o_lnob + ch, o_zb = o_zw + (int64_t)cz * ch, o_gw = o_zb + cz, o_gb = o_gw + (int64_t)cz * cz;
   const int stride = gridDim.x * blockDim.x;
   for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < kMatCount * C * C; idx += stride) {
     const int m = idx / (C * C), r = (idx / C) % C, c = idx % C;
     float v = 0.f;
     switch (m) {
-      case kWAP: if (r < ch && c < cz) v = packed[o_apw + (int64_t)r * cz + c] * packed[o_lniw + c]; break;
-      case kWAG: if (r < ch && c < cz) v = packed[o_agw + (int64_t)r * cz + c] * packed[o_lniw + c]; break;
-      case kWBP: if (r < ch && c < cz) v = packed[o_bpw + (int64_t)r * cz + c] * packed[o_lniw + c]; break;
-      case kWBG: if (r < ch && c < cz) v = packed[o_bgw + (int64_t)r * cz + c] * packed[o_lniw + c]; break;
-      case kWZ: if (r < cz && c < ch) v = packed[o_zw + (int64_t)r * ch + c] * packed[o_lnow + c]; break;
-      default: if (r < cz && c < cz) v = packed[o_gw + (int64_t)r * cz + c] * packed[o_lniw + c]; break;
+      case kWAP: if (r < ch && c < cz) v = w(kTApW, (int64_t)r * cz + c) * w(kTLnInW, c); break;
+      case kWAG: if (r < ch && c < cz) v = w(kTAgW, (int64_t)r * cz + c) * w(kTLnInW, c); break;
+      case kWBP: if (r < ch && c < cz) v = w(kTBpW, (int64_t)r * cz + c) * w(kTLnInW, c); break;
+      case kWBG: if (r < ch && c < cz) v = w(kTBgW, (int64_t)r * cz + c) * w(kTLnInW, c); break;
+      case kWZ: if (r < cz && c < ch) v = w(kTZW, (int64_t)r * ch + c) * w(kTLnOutW, c); break;
+      default: if (r < cz && c < cz) v = w(kTGW, (int64_t)r * cz + c) * w(kTLnInW, c); break;
     }
     w16[idx] = __float2half_rn(v);
   }
@@ -83,33 +106,47 @@ __global__ void prep_weights_kernel(const float *__restrict__ packed, int cz, in
   const int lane = threadIdx.x & 31;
   for (int wi = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; wi < kVecCount * C; wi += stride >> 5) {
     const int q = wi / C, e = wi % C;
-    int64_t o_w = -1, o_b = 0, o_beta = 0;
+    int tw = -1, tb = 0, tbeta = 0;
     int rows = 0, cols = 0;
     switch (q) {
-      case kVBAP: o_w = o_apw; o_b = o_apb; o_beta = o_lnib; rows = ch; cols = cz; break;
-      case kVBAG: o_w = o_agw; o_b = o_agb; o_beta = o_lnib; rows = ch; cols = cz; break;
-      case kVBBP: o_w = o_bpw; o_b = o_bpb; o_beta = o_lnib; rows = ch; cols = cz; break;
-      case kVBBG: o_w = o_bgw; o_b = o_bgb; o_beta = o_lnib; rows = ch; cols = cz; break;
-      case kVBZ: o_w = o_zw; o_b = o_zb; o_beta = o_lnob; rows = cz; cols = ch; break;
-      case kVBG: o_w = o_gw; o_b = o_gb; o_beta = o_lnib; rows = cz; cols = cz; break;
+      case kVBAP: tw = kTApW; tb = kTApB; tbeta = kTLnInB; rows = ch; cols = cz; break;
+      case kVBAG: tw = kTAgW; tb = kTAgB; tbeta = kTLnInB; rows = ch; cols = cz; break;
+      case kVBBP: tw = kTBpW; tb = kTBpB; tbeta = kTLnInB; rows = ch; cols = cz; break;
+      case kVBBG: tw = kTBgW; tb = kTBgB; tbeta = kTLnInB; rows = ch; cols = cz; break;
+      case kVBZ: tw = kTZW; tb = kTZB; tbeta = kTLnOutB; rows = cz; cols = ch; break;
+      case kVBG: tw = kTGW; tb = kTGB; tbeta = kTLnInB; rows = cz; cols = cz; break;
       default: break;  // the LayerNorm slots are not used by the kernels
     }
     if (q == kVZSum) {  // the same rounded values the matrix holds
-      o_w = o_zw;
+      tw = kTZW;
       rows = cz;
       cols = ch;
     }
-    const bool live = o_w >= 0 && e < rows;
+    const bool live = tw >= 0 && e < rows;
     double acc = 0.0;
     if (live && q == kVZSum)
       for (int k = lane; k < cols; k += 32)
-        acc += (double)__half2float(__float2half_rn(packed[o_w + (int64_t)e * cols + k] * packed[o_lnow + k]));
+        acc += (double)__half2float(__float2half_rn(w(tw, (int64_t)e * cols + k) * w(kTLnOutW, k)));
     else if (live)
-      for (int k = lane; k < cols; k += 32) acc += (double)packed[o_w + (int64_t)e * cols + k] * (double)packed[o_beta + k];
+      for (int k = lane; k < cols; k += 32) acc += (double)w(tw, (int64_t)e * cols + k) * (double)w(tbeta, k);
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-    if (lane == 0) vec[wi] = live ? static_cast<float>(acc + (q == kVZSum ? 0.0 : (double)packed[o_b + e])) : 0.f;
+    if (lane == 0) vec[wi] = live ? static_cast<float>(acc + (q == kVZSum ? 0.0 : (double)w(tb, e))) : 0.f;
   }
+}
+
+// Offsets of the 16 tensors in the packed array (src/triangle/weights.ts:4-10).
+static PackedAccess packed_access(const float *packed, int64_t cz, int64_t ch) {
+  const int64_t sizes[kTensorCount] = {cz, cz, ch * cz, ch, ch * cz, ch, ch * cz, ch, ch * cz, ch, ch, ch,
+                                       cz * ch, cz, cz * cz, cz};
+  PackedAccess a{};
+  a.packed = packed;
+  int64_t off = 0;
+  for (int t = 0; t < kTensorCount; ++t) {
+    a.offset[t] = off;
+    off += sizes[t];
+  }
+  return a;
 }
 
 // z [pairs][cz] (any dtype) -> f16 [pairs][128], zero-padded channels.
@@ -1239,7 +1276,7 @@ static int shard_rank(const TriangleShard *shard) { return shard ? shard->rank :
 af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L, const void *z, int z_dtype,
                            const float *mask, const float *packed, double eps, int residual, void *out,
                            int out_dtype, void *workspace, cudaStream_t stream, const TriangleShard *shard,
-                           bool cache_weights) {
+                           bool cache_weights, const af2_matrix *tensors) {
   using namespace tri;
   uint8_t *ws = static_cast<uint8_t *>(workspace);
   // the prepared weights: the layout's prefix [0, off_z16), in the weight cache or the workspace
@@ -1248,6 +1285,10 @@ af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L,
   key.ptr[0] = packed;
   key.dim[0] = L.cz;
   key.dim[1] = L.ch;
+  if (tensors) {  // one tensor each: the key is their value arrays (the scales live beside them)
+    key.kind = kWeightsTriangleTensors;
+    for (int t = 0; t < kTensorCount; ++t) key.ptr[t] = tensors[t].values, key.ptr[16 + t] = tensors[t].scales;
+  }
   PreparedRegion pw;
   if (af2_status st = prepared_region(ctx, key, L.off_z16, ws, cache_weights, &pw); st != AF2_OK) return st;
   __half *w16 = reinterpret_cast<__half *>(pw.base + L.off_w16);
@@ -1266,7 +1307,19 @@ af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L,
   if (pw.fresh) {
     {
       LaunchScope scope(ctx, stream, kProfTrianglePrepare);
-      prep_weights_kernel<<<96, 256, 0, stream>>>(packed, (int)L.cz, (int)L.ch, w16, vec);
+      if (tensors) {
+        TensorAccess acc{};
+        for (int t = 0; t < kTensorCount; ++t) {
+          acc.values[t] = tensors[t].values;
+          const bool q8 = tensors[t].format == AF2_WEIGHTS_Q8_BLOCK;
+          acc.scales[t] = q8 ? static_cast<const uint16_t *>(tensors[t].scales) : nullptr;
+          acc.block[t] = q8 ? tensors[t].block : 1;
+        }
+        prep_weights_kernel<<<96, 256, 0, stream>>>(acc, (int)L.cz, (int)L.ch, w16, vec);
+      } else {
+        prep_weights_kernel<<<96, 256, 0, stream>>>(packed_access(packed, L.cz, L.ch), (int)L.cz, (int)L.ch, w16,
+                                                    vec);
+      }
     }
     if (cudaError_t e = cudaGetLastError(); e != cudaSuccess) return cuda_fail(ctx, e, "launch weight preparation");
   }

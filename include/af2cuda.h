@@ -305,6 +305,29 @@ typedef struct af2_matrix {
 AF2_API af2_status af2_dequant_q8(af2_ctx *ctx, const af2_matrix *matrix, int64_t inner, int64_t cols, float *out,
                                   void *stream);
 
+/*
+ * Per-tensor weights.  The reference's model files hold each weight tensor on
+ * its own (a TensorStore record: f32, or int8 codes with one f16 scale per 64
+ * elements, src/reference/tensor-store.ts:4-13, dtype.ts:66-99), and its host
+ * decodes them to f32 before packing.  These forms take the tensors as they
+ * are stored, one af2_matrix each (AF2_WEIGHTS_F32 or AF2_WEIGHTS_Q8_BLOCK;
+ * AF2_WEIGHTS_Q8_CHANNEL returns AF2_ERR_UNSUPPORTED), and turn the codes into
+ * the kernels' f16 operands on the device.  The decode is the reference's own,
+ * bit for bit (a 7-bit code times an 11-bit scale is exact in f32), so the
+ * results equal the packed forms given the decoded f32 weights.
+ */
+
+/* TriangleMultiplicationWeights (src/triangle/types.ts:9-26) in ORDER
+ * (src/triangle/weights.ts:4-10); projection weights are [out, in]. */
+#define AF2_TRIANGLE_TENSORS 16
+/* Device form of the triangle multiplication from 16 tensors; other arguments
+ * and the workspace as af2_triangle_multiplication. */
+AF2_API af2_status af2_triangle_multiplication_weights(af2_ctx *ctx, int direction, const af2_triangle_shape *shape,
+                                                       const void *z, int z_dtype, const float *mask,
+                                                       const af2_matrix *tensors, double epsilon,
+                                                       const af2_triangle_options *options, void *out, int out_dtype,
+                                                       void *workspace, void *stream);
+
 /* ---- transition ---------------------------------------------------------- */
 
 /* TransitionInput's dimensions, src/evoformer/transition.ts:18-25. */
@@ -413,6 +436,18 @@ AF2_API af2_status af2_outer_product_mean(af2_ctx *ctx, const af2_opm_shape *sha
                                           const float *mask, const float *packed_weights, int64_t weight_count,
                                           const af2_opm_options *options, void *out, int out_dtype, void *workspace,
                                           void *stream);
+
+/* OuterProductMeanWeights in the order of packOuterProductMeanWeights
+ * (outer-product-mean.ts:68-72): LayerNorm scale and offset, leftWeight
+ * [c_m, c], leftBias, rightWeight [c_m, c], rightBias, outputWeight
+ * [c*c, c_z], outputBias. */
+#define AF2_OPM_TENSORS 8
+/* Device form of the outer product mean from 8 tensors (per-tensor weights
+ * above); other arguments and the workspace as af2_outer_product_mean. */
+AF2_API af2_status af2_outer_product_mean_weights(af2_ctx *ctx, const af2_opm_shape *shape, const void *m, int m_dtype,
+                                                  const float *mask, const af2_matrix *tensors,
+                                                  const af2_opm_options *options, void *out, int out_dtype,
+                                                  void *workspace, void *stream);
 
 /* ---- gated multi-head attention: triangle attention ---------------------- */
 
