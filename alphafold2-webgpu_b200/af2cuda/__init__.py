@@ -17,8 +17,9 @@ from .triangle import (TriangleGpuOptions, TriangleGpuResult, TriangleMultiplica
 from .opm import (OuterProductMeanGpu, OuterProductMeanInput, OuterProductMeanResult, OuterProductMeanWeights,
                   encode_outer_product_mean_tensors, linear_tensors, opm_weight_count, opm_workspace_bytes,
                   pack_outer_product_mean_weights, validate_outer_product_mean_input)
-from .sharded import (comm_destroy, comm_init, comm_unique_id, encode_outer_product_mean_sharded_tensors,
-                      encode_triangle_multiplication_sharded_tensors, rows_of)
+from .sharded import (PeerLost, PeerMonitor, comm_abort, comm_destroy, comm_init, comm_set_timeout, comm_unique_id,
+                      encode_outer_product_mean_sharded_tensors, encode_triangle_multiplication_sharded_tensors,
+                      rows_of)
 from .transition import (Q8Matrix, TransitionGpu, TransitionInput, TransitionResult, TransitionWeights,
                          dequant_q8_tensors, encode_transition_tensors, pack_transition_weights,
                          transition_weight_count, transition_workspace_bytes, validate_transition_input)
@@ -47,5 +48,5 @@ __all__ = [
     "pack_attention_weights", "encode_evoformer_pair_block_tensors", "FileTensorStore", "block_range",
     "quantize_q8_block", "read_tensor_range", "tensor_byte_length", "tensor_elements", "write_tensor_manifest",
     "encode_outer_product_mean_weight_tensors", "encode_triangle_multiplication_weight_tensors", "opm_tensor_sizes",
-    "stored_weights", "triangle_tensor_sizes",
+    "stored_weights", "triangle_tensor_sizes", "PeerLost", "PeerMonitor", "comm_set_timeout", "comm_abort",
 ]

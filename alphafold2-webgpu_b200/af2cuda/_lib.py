@@ -150,6 +150,8 @@ SIGNATURES = {
     "af2_comm_unique_id": (_i32, [_vp]),
     "af2_comm_init": (_i32, [_vp, _vp, _i32, _i32]),
     "af2_comm_destroy": (_i32, [_vp]),
+    "af2_comm_set_timeout": (_i32, [_vp, _f64]),
+    "af2_comm_abort": (_i32, [_vp]),
     "af2_triangle_multiplication_sharded": (_i32, [_vp, _i32, ctypes.POINTER(TriangleShape), _vp, _i32, _vp, _vp, _i64,
                                                    _f64, ctypes.POINTER(TriangleOptions), _vp, _i32, _vp]),
     "af2_outer_product_mean_sharded": (_i32, [_vp, ctypes.POINTER(OpmShape), _vp, _i32, _vp, _vp, _i64,

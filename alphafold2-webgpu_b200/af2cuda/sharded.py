@@ -34,6 +34,76 @@ def comm_destroy(device: Device) -> None:
     _lib.check(_lib.lib().af2_comm_destroy(device.handle), device.handle)
 
 
+def comm_set_timeout(device: Device, seconds: float) -> None:
+    """Deadline of the library's host waits on work with collectives (af2_comm_set_timeout):
+    after it, or at the communicator's first asynchronous error, the communicator is
+    aborted and the wait raises Af2Error with AF2_ERR_NCCL."""
+    _lib.check(_lib.lib().af2_comm_set_timeout(device.handle, float(seconds)), device.handle)
+
+
+def comm_abort(device: Device) -> None:
+    """Ends this rank's communicator without a collective (af2_comm_abort): after a peer is
+    lost, or when this rank leaves.  The Device stays usable."""
+    _lib.check(_lib.lib().af2_comm_abort(device.handle), device.handle)
+
+
+class PeerLost(RuntimeError):
+    """A rank left or stopped answering between steps."""
+
+    def __init__(self, missing, step):
+        super().__init__(f"rank(s) {sorted(missing)} did not reach step {step}")
+        self.missing = sorted(missing)
+        self.step = step
+
+
+class PeerMonitor:
+    """Host-side liveness of the ranks that share a communicator, through a
+    torch.distributed store (the TCPStore of the process group, for instance).
+
+    Before each step's launches every rank calls ``step()``: it marks the rank as
+    having reached the step and waits (at most ``timeout`` seconds) until every
+    rank has, so a rank that left or died between steps is found on the host
+    before any collective that would wait for it is queued.  A rank that leaves
+    on purpose calls ``leave()``, and the others see it at once instead of at the
+    deadline."""
+
+    def __init__(self, store, rank: int, nranks: int, timeout: float = 60.0, prefix: str = "af2/peers"):
+        self.store, self.rank, self.nranks = store, rank, nranks
+        self.timeout, self.prefix = float(timeout), prefix
+        self.count = 0
+
+    def _key(self, what, rank, step=None):
+        return f"{self.prefix}/{what}/{rank}" + ("" if step is None else f"/{step}")
+
+    def _left(self):
+        return {r for r in range(self.nranks) if r != self.rank and self.store.check([self._key("left", r)])}
+
+    def step(self) -> int:
+        """Marks this rank at the next step and waits for the others; raises PeerLost."""
+        import time
+        step = self.count
+        self.store.set(self._key("step", self.rank, step), "1")
+        waiting = set(range(self.nranks)) - {self.rank}
+        deadline = time.monotonic() + self.timeout
+        while waiting:
+            gone = self._left() & waiting
+            if gone:
+                raise PeerLost(gone, step)
+            for r in list(waiting):
+                if self.store.check([self._key("step", r, step)]):
+                    waiting.discard(r)
+            if waiting and time.monotonic() > deadline:
+                raise PeerLost(waiting, step)
+            if waiting:
+                time.sleep(0.005)
+        self.count += 1
+        return step
+
+    def leave(self) -> None:
+        """Tells the other ranks that this one has left (between steps)."""
+        self.store.set(self._key("left", self.rank), "1")
+
+
 def rows_of(length: int, nranks: int, rank: int) -> tuple[int, int]:
     """[begin, end) of the pair rows rank `rank` holds."""
     per = length // nranks

@@ -106,6 +106,10 @@ struct af2_ctx {
   std::vector<cudaEvent_t> copy_events;
   int *sync_word = nullptr;                // device word the exchange barriers all-reduce
   bool ipc_failed = false;                 // mapping refused: exchanges use NCCL send/recv
+  // failure detection: host waits on a stream that may hold collectives give up after this many
+  // seconds (or at the communicator's first asynchronous error) and abort the communicator
+  double comm_timeout_s = 600.0;
+  bool comm_aborted = false;
   int gemm_precision = 0;                  // af2_gemm_precision: what the GEMMs that honour it multiply in
   // af2_set_weight_cache: prepared weights kept per weights pointer and shape, made once
   bool weight_cache = false;
@@ -118,6 +122,10 @@ namespace af2 {
 af2_status fail(af2_ctx *ctx, af2_status status, const std::string &message);
 // Maps a CUDA error to AF2_ERR_CUDA (or AF2_ERR_OUT_OF_MEMORY) with context.
 af2_status cuda_fail(af2_ctx *ctx, cudaError_t e, const char *what);
+// Waits for `stream` on the host.  With a communicator: polls the stream and the communicator's
+// asynchronous error with the context's deadline, and on an error or timeout aborts the
+// communicator and returns AF2_ERR_NCCL (comm.cu).
+af2_status comm_wait(af2_ctx *ctx, cudaStream_t stream, const char *what);
 // Ensures `buf` holds at least `bytes` (256-byte aligned device memory).
 af2_status ensure(af2_ctx *ctx, DeviceBuffer &buf, size_t bytes, const char *what);
 

@@ -28,8 +28,7 @@ af2_status cuda_fail(af2_ctx *ctx, cudaError_t e, const char *what) {
 af2_status ensure(af2_ctx *ctx, DeviceBuffer &buf, size_t bytes, const char *what) {
   if (buf.bytes >= bytes) return AF2_OK;
   if (buf.ptr) {
-    cudaError_t e = cudaStreamSynchronize(ctx->stream);
-    if (e != cudaSuccess) return cuda_fail(ctx, e, "synchronize before regrowing scratch");
+    if (af2_status st = comm_wait(ctx, ctx->stream, "synchronize before regrowing scratch"); st != AF2_OK) return st;
     cudaFree(buf.ptr);
     ctx->allocated -= buf.bytes;
     buf.ptr = nullptr;
@@ -395,9 +394,16 @@ af2_status af2_sync(af2_ctx *ctx, void *stream) {
   if (!ctx) return AF2_ERR_INVALID_ARGUMENT;
   cudaSetDevice(ctx->device);
   cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
-  cudaError_t e = cudaStreamSynchronize(s);
-  if (e != cudaSuccess) return cuda_fail(ctx, e, "stream synchronize");
+  if (af2_status st = comm_wait(ctx, s, "stream synchronize"); st != AF2_OK) return st;
   return check_device_errors(ctx);
+}
+
+af2_status af2_comm_set_timeout(af2_ctx *ctx, double seconds) {
+  if (!ctx) return AF2_ERR_INVALID_ARGUMENT;
+  if (!(seconds >= 0) || !std::isfinite(seconds))
+    return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "the timeout must be finite and non-negative");
+  ctx->comm_timeout_s = seconds;
+  return AF2_OK;
 }
 
 af2_status af2_profile_enable(af2_ctx *ctx, int enable) {

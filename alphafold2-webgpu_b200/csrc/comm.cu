@@ -41,6 +41,7 @@
 
 #include "af2_device.cuh"
 #include "af2_internal.h"
+#include "watchdog.h"
 
 namespace af2 {
 namespace {
@@ -62,6 +63,8 @@ struct NcclApi {
   ncclResult_t (*GroupStart)() = nullptr;
   ncclResult_t (*GroupEnd)() = nullptr;
   const char *(*GetErrorString)(ncclResult_t) = nullptr;
+  ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t *) = nullptr;
+  ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
   bool ok = false;
 };
 NcclApi g_nccl;
@@ -81,9 +84,11 @@ void load_nccl() {
   sym(g_nccl.GroupStart, "ncclGroupStart");
   sym(g_nccl.GroupEnd, "ncclGroupEnd");
   sym(g_nccl.GetErrorString, "ncclGetErrorString");
+  sym(g_nccl.CommGetAsyncError, "ncclCommGetAsyncError");
+  sym(g_nccl.CommAbort, "ncclCommAbort");
   g_nccl.ok = g_nccl.GetUniqueId && g_nccl.CommInitRank && g_nccl.CommDestroy && g_nccl.AllGather && g_nccl.AllReduce &&
-              g_nccl.Send &&
-              g_nccl.Recv && g_nccl.GroupStart && g_nccl.GroupEnd && g_nccl.GetErrorString;
+              g_nccl.Send && g_nccl.Recv && g_nccl.GroupStart && g_nccl.GroupEnd && g_nccl.GetErrorString &&
+              g_nccl.CommGetAsyncError && g_nccl.CommAbort;
 }
 
 bool nccl_available() {
@@ -154,10 +159,11 @@ static af2_status map_peers(af2_ctx *ctx, cudaStream_t stream) {
                                     : ncclSuccess;
   if (e == cudaSuccess && r == ncclSuccess)
     e = cudaMemcpyAsync(host.data(), dev, rec * R, cudaMemcpyDeviceToHost, stream);
-  if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+  af2_status waited = e == cudaSuccess && r == ncclSuccess ? comm_wait(ctx, stream, "handle exchange") : AF2_OK;
   cudaFree(dev);
   if (r != ncclSuccess) return nccl_fail(ctx, r, "all-gather of the scratch handles");
   if (e != cudaSuccess) return cuda_fail(ctx, e, "handle exchange");
+  if (waited != AF2_OK) return waited;
   bool all = true;
   for (int p = 0; p < R; ++p) {
     int flag = 0;
@@ -182,10 +188,11 @@ static af2_status map_peers(af2_ctx *ctx, cudaStream_t stream) {
   e = cudaMemcpyAsync(dflag, &fail_count, sizeof(int), cudaMemcpyHostToDevice, stream);
   r = e == cudaSuccess ? g_nccl.AllReduce(dflag, dflag, 1, ncclInt32, ncclSum, comm_of(ctx), stream) : ncclSuccess;
   if (e == cudaSuccess && r == ncclSuccess) e = cudaMemcpyAsync(&fail_count, dflag, sizeof(int), cudaMemcpyDeviceToHost, stream);
-  if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+  waited = e == cudaSuccess && r == ncclSuccess ? comm_wait(ctx, stream, "mapping vote") : AF2_OK;
   cudaFree(dflag);
   if (r != ncclSuccess) return nccl_fail(ctx, r, "mapping vote");
   if (e != cudaSuccess) return cuda_fail(ctx, e, "mapping vote");
+  if (waited != AF2_OK) return waited;
   if (fail_count > 0) {
     close_peers(ctx);
     ctx->ipc_failed = true;
@@ -255,6 +262,7 @@ void comm_destroy(af2_ctx *ctx) {
     ctx->sync_word = nullptr;
   }
   ctx->ipc_failed = false;
+  ctx->comm_aborted = false;
   if (ctx->nccl_comm) {
     g_nccl.CommDestroy(comm_of(ctx));
     ctx->nccl_comm = nullptr;
@@ -266,6 +274,63 @@ void comm_destroy(af2_ctx *ctx) {
   }
   ctx->nranks = 1;
   ctx->rank = 0;
+}
+
+// Ends the communicator after a failure: its kernels stop waiting, so the streams drain.
+static void comm_abort(af2_ctx *ctx) {
+  if (!ctx->nccl_comm) return;
+  g_nccl.CommAbort(comm_of(ctx));
+  ctx->nccl_comm = nullptr;
+  ctx->comm_aborted = true;
+}
+
+static af2_status comm_ready(af2_ctx *ctx) {
+  if (ctx->comm_aborted)
+    return fail(ctx, AF2_ERR_NCCL,
+                "the communicator was aborted after a failure: af2_comm_destroy, then af2_comm_init");
+  if (!ctx->nccl_comm) return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "af2_comm_init has not been called on this context");
+  return AF2_OK;
+}
+
+af2_status comm_wait(af2_ctx *ctx, cudaStream_t stream, const char *what) {
+  if (!ctx->nccl_comm) {
+    const cudaError_t e = cudaStreamSynchronize(stream);
+    return e == cudaSuccess ? AF2_OK : cuda_fail(ctx, e, what);
+  }
+  cudaError_t stream_error = cudaSuccess;
+  ncclResult_t peer_error = ncclSuccess;
+  ncclComm_t comm = comm_of(ctx);
+  const WaitOutcome w = wait_with_watchdog(
+      [&] {
+        const cudaError_t e = cudaStreamQuery(stream);
+        if (e == cudaSuccess) return StreamState::kDone;
+        if (e == cudaErrorNotReady) return StreamState::kPending;
+        stream_error = e;
+        return StreamState::kError;
+      },
+      [&] {
+        ncclResult_t r = ncclSuccess;
+        if (g_nccl.CommGetAsyncError(comm, &r) != ncclSuccess) r = ncclInternalError;
+        if (r == ncclSuccess || r == ncclInProgress) return PeerState::kOk;
+        peer_error = r;
+        return PeerState::kError;
+      },
+      ctx->comm_timeout_s);
+  if (w == WaitOutcome::kDone) return AF2_OK;
+  if (w == WaitOutcome::kStreamError) return cuda_fail(ctx, stream_error, what);
+  std::string message = std::string(what) + ": " + wait_outcome_text(w);
+  if (w == WaitOutcome::kPeerError) message += std::string(" (") + g_nccl.GetErrorString(peer_error) + ")";
+  else message += " (" + std::to_string(ctx->comm_timeout_s) + " s)";
+  comm_abort(ctx);
+  // the aborted communicator's kernels return; give the stream a bounded time to drain
+  const WaitOutcome drained = wait_with_watchdog(
+      [&] {
+        const cudaError_t e = cudaStreamQuery(stream);
+        return e == cudaSuccess ? StreamState::kDone : e == cudaErrorNotReady ? StreamState::kPending : StreamState::kError;
+      },
+      [] { return PeerState::kOk; }, 30.0);
+  if (drained != WaitOutcome::kDone) message += "; the stream had not drained 30 s after the abort";
+  return fail(ctx, AF2_ERR_NCCL, message + "; the communicator was aborted: af2_comm_destroy, then af2_comm_init");
 }
 
 }  // namespace af2
@@ -287,7 +352,8 @@ af2_status af2_comm_init(af2_ctx *ctx, const void *unique_id, int nranks, int ra
   if (!ctx) return AF2_ERR_INVALID_ARGUMENT;
   if (!unique_id || nranks < 1 || rank < 0 || rank >= nranks)
     return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "a unique id, nranks >= 1 and 0 <= rank < nranks are required");
-  if (ctx->nccl_comm) return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "this context already has a communicator");
+  if (ctx->nccl_comm || ctx->comm_aborted)
+    return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "this context already has a communicator (af2_comm_destroy first)");
   if (!nccl_available()) return fail(ctx, AF2_ERR_NCCL, "libnccl.so.2 could not be opened");
   cudaSetDevice(ctx->device);
   ncclUniqueId id;
@@ -317,14 +383,36 @@ af2_status af2_comm_init(af2_ctx *ctx, const void *unique_id, int nranks, int ra
 af2_status af2_comm_destroy(af2_ctx *ctx) {
   if (!ctx) return AF2_ERR_INVALID_ARGUMENT;
   cudaSetDevice(ctx->device);
-  if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+  // a failed wait aborts the communicator; the rest of the teardown is local
+  af2_status st = ctx->stream ? comm_wait(ctx, ctx->stream, "af2_comm_destroy") : AF2_OK;
   if (ctx->nccl_comm && ctx->peer_of) {
     // every rank closes its mappings of the peers' scratch before any rank frees its own
     close_peers(ctx);
-    if (device_barrier(ctx, ctx->stream) == AF2_OK) cudaStreamSynchronize(ctx->stream);
+    if (st == AF2_OK && (st = device_barrier(ctx, ctx->stream)) == AF2_OK)
+      st = comm_wait(ctx, ctx->stream, "af2_comm_destroy");
   }
   comm_destroy(ctx);
-  return AF2_OK;
+  return st;
+}
+
+af2_status af2_comm_abort(af2_ctx *ctx) {
+  if (!ctx) return AF2_ERR_INVALID_ARGUMENT;
+  cudaSetDevice(ctx->device);
+  comm_abort(ctx);
+  // the streams hold no collective that can still wait: drain them (bounded) before freeing
+  af2_status st = AF2_OK;
+  if (ctx->stream) {
+    const WaitOutcome w = wait_with_watchdog(
+        [&] {
+          const cudaError_t e = cudaStreamQuery(ctx->stream);
+          return e == cudaSuccess ? StreamState::kDone : e == cudaErrorNotReady ? StreamState::kPending
+                                                                                : StreamState::kError;
+        },
+        [] { return PeerState::kOk; }, 30.0);
+    if (w != WaitOutcome::kDone) st = fail(ctx, AF2_ERR_NCCL, "af2_comm_abort: the stream did not drain");
+  }
+  comm_destroy(ctx);
+  return st;
 }
 
 af2_status af2_triangle_multiplication_sharded(af2_ctx *ctx, int direction, const af2_triangle_shape *shape,
@@ -336,7 +424,7 @@ af2_status af2_triangle_multiplication_sharded(af2_ctx *ctx, int direction, cons
   char message[256];
   af2_status st = af2_triangle_check(direction, shape, weight_count, epsilon, message, sizeof message);
   if (st != AF2_OK) return fail(ctx, st, message);
-  if (!ctx->nccl_comm) return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "af2_comm_init has not been called on this context");
+  if ((st = comm_ready(ctx)) != AF2_OK) return st;
   if (!z || !mask || !packed_weights || !out) return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "a tensor pointer is NULL");
   const bool dtypes_ok = (z_dtype == AF2_F32 || z_dtype == AF2_F16 || z_dtype == AF2_BF16) &&
                          (out_dtype == AF2_F32 || out_dtype == AF2_F16 || out_dtype == AF2_BF16);
@@ -358,7 +446,7 @@ af2_status af2_triangle_multiplication_sharded(af2_ctx *ctx, int direction, cons
     // every rank grows at the same call: all close their mappings before any frees its allocation
     close_peers(ctx);
     if ((st = device_barrier(ctx, s)) != AF2_OK) return st;
-    if (cudaError_t e = cudaStreamSynchronize(s); e != cudaSuccess) return cuda_fail(ctx, e, "scratch regrowth");
+    if ((st = comm_wait(ctx, s, "scratch regrowth")) != AF2_OK) return st;
   }
   if ((st = ensure(ctx, ctx->shard_scratch, need, "sharded triangle scratch")) != AF2_OK) return st;
   TriangleShard sh;
@@ -380,7 +468,7 @@ af2_status af2_outer_product_mean_sharded(af2_ctx *ctx, const af2_opm_shape *sha
   char message[256];
   af2_status st = af2_opm_check(shape, weight_count, message, sizeof message);
   if (st != AF2_OK) return fail(ctx, st, message);
-  if (!ctx->nccl_comm) return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "af2_comm_init has not been called on this context");
+  if ((st = comm_ready(ctx)) != AF2_OK) return st;
   if (!m || !mask || !packed_weights || !out) return fail(ctx, AF2_ERR_INVALID_ARGUMENT, "a tensor pointer is NULL");
   const bool dtypes_ok = (m_dtype == AF2_F32 || m_dtype == AF2_F16 || m_dtype == AF2_BF16) &&
                          (out_dtype == AF2_F32 || out_dtype == AF2_F16 || out_dtype == AF2_BF16);

@@ -243,6 +243,27 @@ AF2_API af2_status af2_comm_init(af2_ctx *ctx, const void *unique_id, int nranks
 AF2_API af2_status af2_comm_destroy(af2_ctx *ctx);
 
 /*
+ * Failure detection.  All ranks must make the same sequence of sharded calls
+ * with the same shapes (as NCCL's collectives require); a rank that fails or
+ * leaves otherwise leaves its peers' collectives waiting.  Every host wait of
+ * a context with a communicator (af2_sync, af2_comm_destroy, the library's
+ * own waits) polls the stream and ncclCommGetAsyncError; at the
+ * communicator's first asynchronous error, or when the work has not finished
+ * `seconds` after the wait began (default 600; 0 = no deadline), it aborts
+ * the communicator (ncclCommAbort ends its kernels, so the stream drains and
+ * the context stays usable) and returns AF2_ERR_NCCL.  Later sharded calls
+ * return AF2_ERR_NCCL until af2_comm_destroy and a new af2_comm_init.  The
+ * detection is on the host only; ranks should leave between steps (nothing
+ * of theirs in flight) and tell the others through the host (a store or a
+ * heartbeat) before the others' next launch.
+ */
+AF2_API af2_status af2_comm_set_timeout(af2_ctx *ctx, double seconds);
+/* Ends this rank's communicator without any collective -- for a rank whose
+ * peer is lost, or that leaves -- and frees the exchange resources; the
+ * context stays usable for single-GPU calls and a new af2_comm_init. */
+AF2_API af2_status af2_comm_abort(af2_ctx *ctx);
+
+/*
  * The device form of triangle multiplication on a pair sharded by rows: this
  * rank holds rows [rank * L, (rank + 1) * L) of z, mask and out (L = length /
  * nranks, a multiple of 64; nranks divides 128), shape->length is the full

@@ -110,3 +110,90 @@ def test_sharded_pair_ops_are_bit_identical():
         p.join(600)
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     assert list(result) == [1] * nranks
+
+
+def _leave_worker(rank, nranks, port, result):
+    """Two sharded steps with a short watchdog deadline; then the last rank leaves between
+    steps (nothing of its own in flight), and the others find it on the host before the
+    next step's launches, abort their communicators locally and keep using their GPUs."""
+    sys.path.insert(0, str(ROOT / "alphafold2-webgpu_b200"))
+    sys.path.insert(0, str(ROOT / "tests"))
+    import torch
+    import torch.distributed as dist
+
+    import af2cuda
+    from helpers import pack, triangle_case
+
+    torch.cuda.set_device(rank)
+    store = dist.TCPStore("127.0.0.1", port, nranks, rank == 0, timeout=datetime.timedelta(seconds=60))
+    dist.init_process_group("gloo", store=store, rank=rank, world_size=nranks, timeout=datetime.timedelta(seconds=60))
+    dev = af2cuda.Device(rank)
+    ok = True
+    try:
+        uid = [af2cuda.comm_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        af2cuda.comm_init(dev, uid[0], nranks, rank)
+        af2cuda.comm_set_timeout(dev, 20.0)
+        mon = af2cuda.PeerMonitor(store, rank, nranks, timeout=10.0)
+        n = 64 * nranks
+        r0, r1 = af2cuda.rows_of(n, nranks, rank)
+        z, mask, w = triangle_case(n, seed=3)
+        packed = torch.from_numpy(pack(w)).cuda()
+        rows = torch.from_numpy(z[r0:r1]).to("cuda", torch.bfloat16).contiguous()
+        mask_rows = torch.from_numpy(mask[r0:r1]).cuda().contiguous()
+        torch.cuda.synchronize()
+        for step in range(3):
+            if step == 2 and rank == nranks - 1:
+                mon.leave()
+                af2cuda.comm_abort(dev)
+                break
+            try:
+                mon.step()
+            except af2cuda.PeerLost as e:
+                ok &= step == 2 and e.missing == [nranks - 1]
+                af2cuda.comm_abort(dev)
+                # the context still runs single-GPU work
+                full = torch.from_numpy(z).to("cuda", torch.bfloat16)
+                mask_d = torch.from_numpy(mask).cuda()
+                torch.cuda.synchronize()
+                af2cuda.encode_triangle_multiplication_tensors(dev, 0, full, mask_d, packed)
+                dev.sync()
+                ok &= bool(torch.isfinite(full.float()).all())
+                try:  # the sharded form now reports that there is no communicator
+                    af2cuda.encode_triangle_multiplication_sharded_tensors(dev, 0, rows, mask_rows, packed, n)
+                    ok = False
+                except af2cuda.Af2Error:
+                    pass
+                break
+            af2cuda.encode_triangle_multiplication_sharded_tensors(dev, step % 2, rows, mask_rows, packed, n)
+            dev.sync()  # the watchdog's wait
+        else:
+            ok = False
+    finally:
+        dev.close()
+    result[rank] = int(ok)
+
+
+def test_rank_leaving_between_steps_is_found_on_the_host():
+    import torch
+    import torch.multiprocessing as mp
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two or more GPUs")
+    nranks = 2
+    ctx = mp.get_context("spawn")
+    result = ctx.Array("i", nranks)
+    port = _free_port()
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    old = os.environ.copy()
+    os.environ.update(env)
+    try:
+        procs = [ctx.Process(target=_leave_worker, args=(r, nranks, port, result)) for r in range(nranks)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(300)
+    finally:
+        os.environ.clear()
+        os.environ.update(old)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    assert list(result) == [1] * nranks
