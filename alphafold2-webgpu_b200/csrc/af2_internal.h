@@ -118,6 +118,10 @@ struct af2_ctx {
 
 namespace af2 {
 
+// Kernel-selection override from the environment (measurement of the alternatives a shape
+// rule chooses between): the integer value of `name`, or `fallback` when unset or not a number.
+int tuning_override(const char *name, int fallback);
+
 // Sets ctx->last_error and returns `status`.
 af2_status fail(af2_ctx *ctx, af2_status status, const std::string &message);
 // Maps a CUDA error to AF2_ERR_CUDA (or AF2_ERR_OUT_OF_MEMORY) with context.

@@ -7,6 +7,7 @@
 #include <chrono>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -18,6 +19,14 @@ namespace af2 {
 af2_status fail(af2_ctx *ctx, af2_status status, const std::string &message) {
   if (ctx) ctx->last_error = message;
   return status;
+}
+
+int tuning_override(const char *name, int fallback) {
+  const char *v = std::getenv(name);
+  if (!v || !*v) return fallback;
+  char *end = nullptr;
+  const long x = std::strtol(v, &end, 10);
+  return (end && *end == '\0') ? static_cast<int>(x) : fallback;
 }
 
 af2_status cuda_fail(af2_ctx *ctx, cudaError_t e, const char *what) {

@@ -1076,8 +1076,10 @@ af2_status fused_launch(af2_ctx *ctx, const OpmLayout &L, uint8_t *ws, const uin
   const int64_t s = L.s, n = L.n, c = L.c, cz = L.cz, rows = L.rows;
   const int64_t o_cols = linear_cols_pad(cz), o_inner = align_up(c * c, 64);
   const int k_blocks = (int)((s + 63) / 64);
-  // three residues j per tile when their right operand fits beside the left ring, else two
-  const int J = fused_stages(k_blocks, 3) >= 4 ? 3 : 2;
+  // three residues j per tile when their right operand fits beside the left ring, else two;
+  // AF2_OPM_TILE_RESIDUES=2 selects two where three fit (S = 512, N = 1024: 2.15 ms
+  // against 1.49 ms with three, one B200)
+  const int J = fused_stages(k_blocks, 3) >= 4 && tuning_override("AF2_OPM_TILE_RESIDUES", 3) != 2 ? 3 : 2;
   CUtensorMap lmap, rmap, wmap;
   // K-major, sequences contiguous (zero past S):
   // left [c][rows][pitch]: boxes of 64 sequences x 128 residues of one channel

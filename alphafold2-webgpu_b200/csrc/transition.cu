@@ -786,9 +786,10 @@ TransitionLayout transition_layout(int64_t rows, int64_t c, int64_t h, int x_dty
   L.rows = rows;
   L.c = c;
   L.h = h;
-  if (c > 128 || h > 1024) {
+  if (c > 128 || h > 1024 || tuning_override("AF2_TRANSITION_WIDE", 0) == 1) {
     // the fused kernel holds C <= 128 channels and H <= 1024 hidden; wider transitions
-    // (the MSA transition: 256 -> 1024 -> 256) take the two-GEMM path
+    // (the MSA transition: 256 -> 1024 -> 256) take the two-GEMM path, which
+    // AF2_TRANSITION_WIDE=1 also selects for shapes the fused kernel holds
     L.wide = true;
     L.k1 = align_up(c, 64);
     L.n1 = linear_cols_pad(h);

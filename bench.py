@@ -53,9 +53,12 @@ CZ = CH = 128
 S_MSA, CM, C_OUTER = 512, 256, 32
 HIDDEN = 4 * CZ
 METRIC = "Evoformer pair-GEMM TFLOP/s & ms/block at N=1024; % of B200 bf16 TC peak"
-# dram__bytes_read.sum + dram__bytes_write.sum per launch, from ncu captures of
-# this workload (profiles/*.md); kernels without a capture report null.
-KERNEL_DRAM_BYTES = {"triangle.contract": 776_628_736, "opm.fused": 599_897_344}
+# dram__bytes_read.sum + dram__bytes_write.sum per launch of the default block at N=1024, from
+# one single-pass ncu capture of this workload (profiles/block_n1024_launches.md, the mean over
+# 14 block steps); kernels without a capture report null.
+KERNEL_DRAM_BYTES = {"opm.fused": 604_527_488, "triangle.contract": 772_069_933, "triangle.project": 747_826_084,
+                     "triangle.output": 750_942_893, "transition.fused": 473_526_034, "opm.project": 314_003_584,
+                     "opm.count": 2_133_156}
 KERNELS = ("weights.prepare", "triangle.prepare", "triangle.relayout", "triangle.project", "triangle.contract",
            "triangle.output", "opm.normalize", "opm.project", "opm.count", "opm.outer", "opm.output",
            "opm.fused", "transition.prepare", "transition.normalize", "transition.fused", "transition.linear",

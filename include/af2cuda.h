@@ -163,6 +163,20 @@ AF2_API af2_status af2_profile_reset(af2_ctx *ctx);
 AF2_API const char *af2_profile_kernel_name(int index);
 AF2_API af2_status af2_profile_read(af2_ctx *ctx, const char *kernel, uint64_t *launches, double *milliseconds);
 
+/*
+ * Kernel selection.  Each op picks its kernels from the shape: the fused
+ * outer-product mean (c = 32, S <= 1024, c_z <= 128) with three residues j
+ * per tile where their operands fit in shared memory (two otherwise), else
+ * the two-kernel path through an HBM scratch; the fused transition (C <= 128,
+ * H <= 1024), else LayerNorm plus two linear GEMMs; the 16-bit MSA's
+ * LayerNorm fused into the OPM projection.  Two environment variables select
+ * the alternative where both are valid, to measure the choice:
+ * AF2_OPM_TILE_RESIDUES=2 (two residues per fused OPM tile; results are
+ * bit-identical) and AF2_TRANSITION_WIDE=1 (the two-GEMM transition for
+ * shapes the fused kernel holds; results agree to f16 rounding).  They are
+ * read at each call.
+ */
+
 /* ---- triangle multiplication ------------------------------------------ */
 
 /* expectedWeightElementCount, src/triangle/weights.ts:36-40. */
