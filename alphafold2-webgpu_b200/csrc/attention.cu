@@ -42,6 +42,7 @@
 #include <cmath>
 #include <cstring>
 #include <string>
+#include <type_traits>
 
 #include "af2_device.cuh"
 #include "af2_internal.h"
@@ -95,6 +96,56 @@ __global__ void attn_norm_kernel(const T *__restrict__ x, int64_t rows, int C, i
       const int c = lane + 32 * i;
       out[c] = __float2half_rn((v[i] - mean) * inv * gamma[c] + beta[c]);
     }
+}
+
+// The same LayerNorm for C = 128, four rows per warp: lane l holds channels 4l .. 4l + 3 of each
+// row (one 8-byte load of a 16-bit row, 16 bytes of an f32 one), the four rows' loads issued
+// together; two-pass statistics over the row held in registers, as above.
+template <typename T>
+__global__ void attn_norm128_kernel(const T *__restrict__ x, int64_t rows, int64_t B, int64_t Q, int transpose,
+                                    const float *__restrict__ gamma, const float *__restrict__ beta, float eps,
+                                    __half *__restrict__ xn) {
+  constexpr int R = 4;
+  const int lane = threadIdx.x & 31;
+  const int64_t m0 = (static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5)) * R;
+  if (m0 >= rows) return;
+  float v[R][4];
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int64_t m = m0 + r;
+    if (m < rows) {
+      const int64_t b = m / Q, q = m - b * Q;
+      const T *row = x + (transpose ? q * B + b : m) * 128 + 4 * lane;
+      if constexpr (std::is_same<T, float>::value) {
+        const float4 f = *reinterpret_cast<const float4 *>(row);
+        v[r][0] = f.x, v[r][1] = f.y, v[r][2] = f.z, v[r][3] = f.w;
+      } else {
+        const uint2 u = *reinterpret_cast<const uint2 *>(row);
+        const float2 a = unpack2<T>(u.x), c = unpack2<T>(u.y);
+        v[r][0] = a.x, v[r][1] = a.y, v[r][2] = c.x, v[r][3] = c.y;
+      }
+    } else {
+      v[r][0] = v[r][1] = v[r][2] = v[r][3] = 0.f;
+    }
+  }
+  const float4 g = reinterpret_cast<const float4 *>(gamma)[lane], bt = reinterpret_cast<const float4 *>(beta)[lane];
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    float sum = (v[r][0] + v[r][1]) + (v[r][2] + v[r][3]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(kFull, sum, o);
+    const float mean = sum * (1.f / 128.f);
+    const float c0 = v[r][0] - mean, c1 = v[r][1] - mean, c2 = v[r][2] - mean, c3 = v[r][3] - mean;
+    float var = (c0 * c0 + c1 * c1) + (c2 * c2 + c3 * c3);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) var += __shfl_xor_sync(kFull, var, o);
+    const float inv = rsqrtf(var * (1.f / 128.f) + eps);
+    if (m0 + r < rows) {
+      const uint2 o = make_uint2(pack_half2(c0 * inv * g.x + bt.x, c1 * inv * g.y + bt.y),
+                                 pack_half2(c2 * inv * g.z + bt.z, c3 * inv * g.w + bt.w));
+      *reinterpret_cast<uint2 *>(xn + (m0 + r) * 128 + 4 * lane) = o;
+    }
+  }
 }
 
 // mb[b][k] = 1e9 (mask - 1) log2(e) for the view's row b and key k (mask_index, attention.ts:428-433).
@@ -614,7 +665,22 @@ af2_status attention_launch(af2_ctx *ctx, const AttentionLayout &L, int transpos
     if ((st = pad_vectors(ctx, vs, stream)) != AF2_OK) return st;
   }
   __half *xn = reinterpret_cast<__half *>(ws + L.off_xn);
-  {
+  if (C == 128 && reinterpret_cast<uintptr_t>(x) % 16 == 0) {
+    const int warps = 8;
+    const unsigned blocks = (unsigned)((L.rows + 4 * warps - 1) / (4 * warps));
+    LaunchScope scope(ctx, stream, kProfAttentionNormalize);
+    if (x_dtype == AF2_F32)
+      attn_norm128_kernel<float><<<blocks, warps * 32, 0, stream>>>(static_cast<const float *>(x), L.rows, B, Q,
+                                                                    transpose, ln, ln + C, (float)eps, xn);
+    else if (x_dtype == AF2_BF16)
+      attn_norm128_kernel<__nv_bfloat16><<<blocks, warps * 32, 0, stream>>>(
+          static_cast<const __nv_bfloat16 *>(x), L.rows, B, Q, transpose, ln, ln + C, (float)eps, xn);
+    else
+      attn_norm128_kernel<__half><<<blocks, warps * 32, 0, stream>>>(static_cast<const __half *>(x), L.rows, B, Q,
+                                                                     transpose, ln, ln + C, (float)eps, xn);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "attention LayerNorm");
+  } else {
     const int warps = 8;
     const unsigned blocks = (unsigned)((L.rows + warps - 1) / warps);
     LaunchScope scope(ctx, stream, kProfAttentionNormalize);

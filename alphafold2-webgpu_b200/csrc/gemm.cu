@@ -46,6 +46,8 @@ struct LinearArgs {
   int relu, residual;
   int vector_out;  // out rows are 16-byte aligned: whole 32-column chunks use vector access
   int tma_out;     // f16 output, no residual: each warp stages 32 x 32 blocks and stores them by TMA
+  int stage_bufs;  // staging blocks per epilogue warp (2 when shared memory allows: a store in flight
+                   // while the next block is staged)
   // LINEAR: with transpose_q > 0 row m = b * transpose_q + q is written to row q * transpose_b + b
   // (the attention output of a transposed view goes back to its source row)
   int64_t transpose_q, transpose_b;
@@ -174,11 +176,12 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int row = q * 32 + lane;
     // the staged path exists for f16 outputs only (the host sets tma_out accordingly)
     const bool staged = MODE == kModeLinear && std::is_same<OT, __half>::value && p.tma_out;
-    const uint32_t stage_off = OFF_BAR + 256 + (warp - 2) * OUT_STAGE_BYTES;
+    const uint32_t stage_base = OFF_BAR + 256 + (warp - 2) * p.stage_bufs * OUT_STAGE_BYTES;
+    int sb = 0;  // the staging block this warp fills next
     const int cols_pad = p.tiles_n * p.bn;
     const float *vscale = p.scale, *vbias = p.bias;
     if (cols_pad <= kSmemVecCols) {
-      float *sv = reinterpret_cast<float *>(smem + OFF_BAR + 256 + EPI_WARPS * OUT_STAGE_BYTES);
+      float *sv = reinterpret_cast<float *>(smem + OFF_BAR + 256 + EPI_WARPS * p.stage_bufs * OUT_STAGE_BYTES);
       for (int i = threadIdx.x - 64; i < cols_pad; i += 32 * EPI_WARPS) {
         sv[i] = p.scale[i];
         sv[kSmemVecCols + i] = p.bias[i];
@@ -232,8 +235,16 @@ __global__ void __launch_bounds__(THREADS, 1)
             pk[2 * i4] = pack_half2(y0, y1);
             pk[2 * i4 + 1] = pack_half2(y2, y3);
           }
-          if (lane == 0 && store_pending) bulk_wait_read_all();  // the last store has read the block
+          // the store that last used this block has read it
+          if (lane == 0 && store_pending) {
+            if (p.stage_bufs > 1)
+              bulk_wait_read_but_one();
+            else
+              bulk_wait_read_all();
+          }
           __syncwarp();
+          const uint32_t stage_off = stage_base + sb * OUT_STAGE_BYTES;
+          sb = sb + 1 == p.stage_bufs ? 0 : sb + 1;
           // row `lane` of the block is 64 bytes; its four 16-byte pieces are written in an order
           // rotated by the lane, so each store instruction covers every bank once per 128 bytes
           uint8_t *stage_row = smem + stage_off + lane * 64;
@@ -272,8 +283,16 @@ __global__ void __launch_bounds__(THREADS, 1)
               y[4 * i4 + 2] = fmaf(__uint_as_float(v[4 * i4 + 2]), s4.z, b4.z);
               y[4 * i4 + 3] = fmaf(__uint_as_float(v[4 * i4 + 3]), s4.w, b4.w);
             }
-            if (lane == 0 && store_pending) bulk_wait_read_all();  // the last store has read the block
+            // the store that last used this block has read it
+            if (lane == 0 && store_pending) {
+              if (p.stage_bufs > 1)
+                bulk_wait_read_but_one();
+              else
+                bulk_wait_read_all();
+            }
             __syncwarp();
+            const uint32_t stage_off = stage_base + sb * OUT_STAGE_BYTES;
+            sb = sb + 1 == p.stage_bufs ? 0 : sb + 1;
             if (part == 2) {
               __half *st = reinterpret_cast<__half *>(smem + stage_off);
 #pragma unroll
@@ -634,7 +653,8 @@ template <typename OT, int MODE>
 af2_status launch_linear_t(af2_ctx *ctx, const CUtensorMap &amap, const CUtensorMap &bmap, const CUtensorMap &omap,
                            const AttentionMaps &amaps, const LinearArgs &a, int prof, cudaStream_t stream) {
   auto kernel = linear_kernel<OT, MODE>;
-  const uint32_t smem = STAGES * (A_BYTES + a.bn * 128u) + 256 + EPI_WARPS * OUT_STAGE_BYTES + VEC_BYTES + 1024;
+  const uint32_t smem =
+      STAGES * (A_BYTES + a.bn * 128u) + 256 + EPI_WARPS * a.stage_bufs * OUT_STAGE_BYTES + VEC_BYTES + 1024;
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return cuda_fail(ctx, e, "linear kernel attributes");
   const int grid = std::min(a.total_tiles, ctx->sm_count);
@@ -708,6 +728,10 @@ af2_status linear_launch(af2_ctx *ctx, const LinearOperands &op, cudaStream_t st
   if (a.tma_out && !encode_map_3d(&omap, f16map(), op.out, op.cols, op.rows, 1, op.ldo * 2,
                                   (uint64_t)op.rows * op.ldo * 2, 32, 32, 1, CU_TENSOR_MAP_SWIZZLE_NONE))
     return fail(ctx, AF2_ERR_CUDA, "cuTensorMapEncodeTiled failed for a linear layer's output");
+  // two staging blocks per epilogue warp where shared memory holds them (tiles up to 192 columns)
+  a.stage_bufs = STAGES * (A_BYTES + a.bn * 128u) + 256 + EPI_WARPS * 2 * OUT_STAGE_BYTES + VEC_BYTES + 1024 <= 232448u
+                     ? 2
+                     : 1;
   AttentionMaps amaps;
   std::memset(&amaps, 0, sizeof amaps);
   if (attention) {
