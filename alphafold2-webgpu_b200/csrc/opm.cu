@@ -140,7 +140,11 @@ __global__ void norm_kernel(const MT *__restrict__ m, int64_t rows, int cm, int 
 // register block of contiguous pairs fed by 16-byte shared-memory loads (three
 // loads per 32 FMAs), 32 MSA rows of both residue ranges at a time; every count
 // sums s in order.
-constexpr int CNT_TILE = 64, CNT_S = 32, CNT_THREADS = 128;
+constexpr int CNT_TILE = 64, CNT_S = 32, CNT_THREADS = 256;
+// 1 / (eps + sum_s mask[s][i] mask[s][j]) for a 64 x 64 block of pairs: 256 threads, each a 4 x 4
+// register block summed with packed f32x2 FMAs (two j per instruction), over chunks of 32
+// sequences staged in shared memory while the next chunk's loads are in flight.  Every product
+// is summed in ascending s, so the result does not depend on the blocking.
 __global__ void __launch_bounds__(CNT_THREADS) count_kernel(const float *__restrict__ mask, int s_count, int n,
                                                             int row0, int rows, float norm_eps,
                                                             float *__restrict__ rowscale) {
@@ -149,10 +153,10 @@ __global__ void __launch_bounds__(CNT_THREADS) count_kernel(const float *__restr
   __shared__ __align__(16) float mj[CNT_S][CNT_TILE];
   const int i0 = row0 + blockIdx.y * CNT_TILE, j0 = blockIdx.x * CNT_TILE;
   const int i_end = row0 + rows;
-  const int tx = threadIdx.x & 7, ty = threadIdx.x >> 3;  // j0 + 8 tx .., i0 + 4 ty ..
-  float acc[4][8] = {};
-  // each thread stages 16 elements of each range per chunk; the next chunk's
-  // loads are in flight while the current one is multiplied
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;  // j0 + 4 tx .., i0 + 4 ty ..
+  float2 acc[4][2];
+#pragma unroll
+  for (int u = 0; u < 4; ++u) acc[u][0] = acc[u][1] = make_float2(0.f, 0.f);
   constexpr int kPer = CNT_S * CNT_TILE / CNT_THREADS;
   float ra[kPer], rb[kPer];
   auto fetch = [&](int s0) {
@@ -178,14 +182,14 @@ __global__ void __launch_bounds__(CNT_THREADS) count_kernel(const float *__restr
 #pragma unroll 8
     for (int r = 0; r < CNT_S; ++r) {
       const float4 a = *reinterpret_cast<const float4 *>(&mi[r][ty * 4]);
-      const float4 b0 = *reinterpret_cast<const float4 *>(&mj[r][tx * 8]);
-      const float4 b1 = *reinterpret_cast<const float4 *>(&mj[r][tx * 8 + 4]);
+      const float4 b = *reinterpret_cast<const float4 *>(&mj[r][tx * 4]);
       const float av[4] = {a.x, a.y, a.z, a.w};
-      const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+      const float2 b01 = make_float2(b.x, b.y), b23 = make_float2(b.z, b.w);
 #pragma unroll
-      for (int u = 0; u < 4; ++u)
-#pragma unroll
-        for (int v = 0; v < 8; ++v) acc[u][v] = fmaf(av[u], bv[v], acc[u][v]);
+      for (int u = 0; u < 4; ++u) {
+        acc[u][0] = f2fma(f2(av[u]), b01, acc[u][0]);
+        acc[u][1] = f2fma(f2(av[u]), b23, acc[u][1]);
+      }
     }
     __syncthreads();
   }
@@ -193,10 +197,11 @@ __global__ void __launch_bounds__(CNT_THREADS) count_kernel(const float *__restr
   for (int u = 0; u < 4; ++u) {
     const int i = i0 + ty * 4 + u;
     if (i >= i_end) continue;
+    const float vals[4] = {acc[u][0].x, acc[u][0].y, acc[u][1].x, acc[u][1].y};
 #pragma unroll
-    for (int v = 0; v < 8; ++v) {
-      const int j = j0 + tx * 8 + v;
-      if (j < n) rowscale[static_cast<int64_t>(i - row0) * n + j] = 1.f / (norm_eps + acc[u][v]);
+    for (int v = 0; v < 4; ++v) {
+      const int j = j0 + tx * 4 + v;
+      if (j < n) rowscale[static_cast<int64_t>(i - row0) * n + j] = 1.f / (norm_eps + vals[v]);
     }
   }
 }
