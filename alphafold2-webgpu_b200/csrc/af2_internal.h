@@ -219,6 +219,9 @@ struct TriangleShard {
   af2_status (*send)(af2_ctx *ctx, const void *src, const void *dst_local, size_t bytes, int peer,
                      cudaStream_t stream) = nullptr;
   af2_status (*close)(af2_ctx *ctx, cudaStream_t stream) = nullptr;
+  // the peer's shard scratch mapped into this process (valid after `direct` returned true), at
+  // the same layout offsets as this rank's: kernels store their peer's pieces straight into it
+  void *(*peer_base)(af2_ctx *ctx, int peer) = nullptr;
 };
 
 // Launches the whole op on `stream`; the workspace holds TriangleLayout::total bytes.

@@ -212,6 +212,10 @@ static bool ipc_direct(af2_ctx *ctx, cudaStream_t stream, af2_status *status) {
 
 static af2_status ipc_open(af2_ctx *ctx, cudaStream_t stream) { return device_barrier(ctx, stream); }
 
+static void *ipc_peer_base(af2_ctx *ctx, int peer) {
+  return (peer >= 0 && peer < static_cast<int>(ctx->peer_scratch.size())) ? ctx->peer_scratch[peer] : nullptr;
+}
+
 // One copy on the peer's copy stream, after everything queued on `stream` so far.
 static af2_status ipc_send(af2_ctx *ctx, const void *src, const void *dst_local, size_t bytes, int peer,
                            cudaStream_t stream) {
@@ -457,6 +461,7 @@ af2_status af2_triangle_multiplication_sharded(af2_ctx *ctx, int direction, cons
   sh.open = ipc_open;
   sh.send = ipc_send;
   sh.close = ipc_close;
+  sh.peer_base = ipc_peer_base;
   return triangle_launch(ctx, direction, L, z, z_dtype, mask, packed_weights, epsilon, residual, out, out_dtype,
                          ctx->shard_scratch.ptr, s, &sh);
 }

@@ -200,7 +200,17 @@ struct ProjectArgs {
   int cz, tiles_k, total_tiles;
   int transposed;  // incoming: the z map is [k][j][c] and the box walks k in its outer dimension
   float eps;
+  int store_maps;  // 1: one store per operand (box of all groups); R: one per channel group
+  int hq;          // channels per group
   unsigned int *err;
+};
+
+// Where the gated operands go: map 0 covers all channel groups of this rank's operand buffer,
+// or map g covers group g alone (in the buffer of the rank that contracts it: a peer's scratch
+// mapped into this process, or this rank's own buffer for its own group).
+constexpr int kMaxStoreMaps = 8;
+struct ProjectStoreMaps {
+  CUtensorMap a[kMaxStoreMaps], b[kMaxStoreMaps];
 };
 
 // Normalisation of pair row `row` of a 128B-swizzled K-major tile (two
@@ -305,8 +315,8 @@ __device__ __forceinline__ void ln_row_pair(uint8_t *tile, uint32_t chunk_bytes,
 
 template <typename ZT>
 __global__ void __launch_bounds__(PJ_THREADS, 1)
-    project_kernel(const __grid_constant__ CUtensorMap zmap, const __grid_constant__ CUtensorMap amap,
-                   const __grid_constant__ CUtensorMap bmap, const ProjectArgs p) {
+    project_kernel(const __grid_constant__ CUtensorMap zmap, const __grid_constant__ ProjectStoreMaps smaps,
+                   const ProjectArgs p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = align1024(smem_raw);
   const uint32_t sbase = smem_u32(smem);
@@ -356,8 +366,6 @@ __global__ void __launch_bounds__(PJ_THREADS, 1)
     // ---- TMA producer ----
     if (lane == 0) {
       tma_prefetch_map(&zmap);
-      tma_prefetch_map(&amap);
-      tma_prefetch_map(&bmap);
       int it = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x, ++it) {
@@ -526,8 +534,18 @@ __global__ void __launch_bounds__(PJ_THREADS, 1)
         if (!mbar_wait(out_full, it & 1, abort_flag, p.err, kErrWaitEpilogue)) {
           it = -1;
         } else {
-          tma_store_4d(&amap, sbase + PJ_OFF_OUT, k0, 0, r, 0);
-          tma_store_4d(&bmap, sbase + PJ_OFF_OUT + PJ_OUT_BYTES, k0, 0, r, 0);
+          if (p.store_maps == 1) {
+            tma_store_4d(&smaps.a[0], sbase + PJ_OFF_OUT, k0, 0, r, 0);
+            tma_store_4d(&smaps.b[0], sbase + PJ_OFF_OUT + PJ_OUT_BYTES, k0, 0, r, 0);
+          } else {
+            // group g's hq staged rows start g hq x 128 bytes in (a multiple of 1024: the
+            // swizzle pattern is the whole block's)
+            for (int g = 0; g < p.store_maps; ++g) {
+              const uint32_t off = static_cast<uint32_t>(g * p.hq) * 128u;
+              tma_store_4d(&smaps.a[g], sbase + PJ_OFF_OUT + off, k0, 0, r, 0);
+              tma_store_4d(&smaps.b[g], sbase + PJ_OFF_OUT + PJ_OUT_BYTES + off, k0, 0, r, 0);
+            }
+          }
           bulk_commit();
           store_pending = true;
         }
@@ -1229,7 +1247,7 @@ CUtensorMapDataType map_type(int dtype) {
 }
 
 template <typename ZT>
-af2_status launch_project(af2_ctx *ctx, const CUtensorMap &zmap, const CUtensorMap &amap, const CUtensorMap &bmap,
+af2_status launch_project(af2_ctx *ctx, const CUtensorMap &zmap, const tri::ProjectStoreMaps &smaps,
                           const tri::ProjectArgs &a, cudaStream_t stream) {
   // set on every launch: the attribute belongs to the current device's copy of the kernel
   cudaError_t ce = cudaFuncSetAttribute(tri::project_kernel<ZT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1238,7 +1256,7 @@ af2_status launch_project(af2_ctx *ctx, const CUtensorMap &zmap, const CUtensorM
   const int grid = std::max(1, std::min(a.total_tiles, ctx->sm_count));
   {
     LaunchScope scope(ctx, stream, kProfTriangleProject);
-    tri::project_kernel<ZT><<<grid, tri::PJ_THREADS, tri::PJ_SMEM, stream>>>(zmap, amap, bmap, a);
+    tri::project_kernel<ZT><<<grid, tri::PJ_THREADS, tri::PJ_SMEM, stream>>>(zmap, smaps, a);
   }
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? AF2_OK : cuda_fail(ctx, e, "launch project kernel");
@@ -1372,31 +1390,56 @@ af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L,
   const uint64_t ab_dims[4] = {(uint64_t)k_extent, (uint64_t)hq, (uint64_t)L.ab_rows, (uint64_t)R};
   const uint64_t ab_strides[3] = {(uint64_t)L.kp * 2, (uint64_t)L.ab_rs * 2, (uint64_t)L.ab_rows * L.ab_rs * 2};
   const uint32_t ab_box[4] = {PJ_TILE, (uint32_t)hq, 1, (uint32_t)R};
-  CUtensorMap amap_st, bmap_st;
-  if (!encode_map_4d(&amap_st, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a, ab_dims, ab_strides, ab_box,
+  ProjectStoreMaps smaps;
+  std::memset(&smaps, 0, sizeof smaps);
+  if (!encode_map_4d(&smaps.a[0], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a, ab_dims, ab_strides, ab_box,
                      CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !encode_map_4d(&bmap_st, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, b, ab_dims, ab_strides, ab_box,
+      !encode_map_4d(&smaps.b[0], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, b, ab_dims, ab_strides, ab_box,
                      CU_TENSOR_MAP_SWIZZLE_128B))
     return fail(ctx, AF2_ERR_CUDA, "cuTensorMapEncodeTiled failed for the projection's store maps");
+  pa.store_maps = 1;
+  pa.hq = static_cast<int>(hq);
   // ---- channel shards: every rank receives its hq channels of every rank's rows ----
   __half *a_all = reinterpret_cast<__half *>(ws + L.off_a_all), *b_all = reinterpret_cast<__half *>(ws + L.off_b_all);
   const size_t group_bytes = (size_t)L.ab_rows * L.ab_rs * sizeof(__half);
   const int me = shard_rank(shard);
   af2_status st = AF2_OK;
-  // Direct exchange: the projection runs in two halves of its tile rows (the rows of every
-  // channel group), and each half's groups are copied to their ranks while the next computes.
+  // Direct exchange by copies (peer stores unavailable): the projection runs in two halves of
+  // its tile rows (the rows of every channel group), and each half's groups are copied to their
+  // ranks while the next computes.
   const bool direct = sharded && shard->direct && shard->direct(ctx, stream, &st);
   if (st != AF2_OK) return st;
   if (direct && (st = shard->open(ctx, stream)) != AF2_OK) return st;
-  const int64_t halves = (direct && r_extent >= 2) ? 2 : 1, r_per = (r_extent + halves - 1) / halves;
+  // With the peers' scratch mapped, channel group g leaves the projection by TMA store straight
+  // into rank g's receive buffer (its slot for this rank), and this rank's own group into its
+  // own buffer: no copies after the kernel.
+  const bool peer_stores = direct && shard->peer_base && R <= kMaxStoreMaps && R > 1;
+  if (peer_stores) {
+    const uint64_t g_dims[4] = {(uint64_t)k_extent, (uint64_t)hq, (uint64_t)L.ab_rows, 1};
+    const uint32_t g_box[4] = {PJ_TILE, (uint32_t)hq, 1, 1};
+    const size_t slot = (size_t)me * group_bytes;
+    for (int g = 0; g < R; ++g) {
+      uint8_t *peer = g == me ? nullptr : static_cast<uint8_t *>(shard->peer_base(ctx, g));
+      if (g != me && !peer) return fail(ctx, AF2_ERR_CUDA, "a peer's scratch is not mapped");
+      const void *dst_a = g == me ? reinterpret_cast<uint8_t *>(a) + slot : peer + L.off_a_all + slot;
+      const void *dst_b = g == me ? reinterpret_cast<uint8_t *>(b) + slot : peer + L.off_b_all + slot;
+      if (!encode_map_4d(&smaps.a[g], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, dst_a, g_dims, ab_strides, g_box,
+                         CU_TENSOR_MAP_SWIZZLE_128B) ||
+          !encode_map_4d(&smaps.b[g], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, dst_b, g_dims, ab_strides, g_box,
+                         CU_TENSOR_MAP_SWIZZLE_128B))
+        return fail(ctx, AF2_ERR_CUDA, "cuTensorMapEncodeTiled failed for the projection's peer store maps");
+    }
+    pa.store_maps = static_cast<int>(R);
+  }
+  const int64_t halves = (direct && !peer_stores && r_extent >= 2) ? 2 : 1, r_per = (r_extent + halves - 1) / halves;
   for (int64_t c = 0; c < halves; ++c) {
     const int64_t r0 = c * r_per, rc = std::min<int64_t>(r_per, r_extent - r0);
     pa.r_begin = static_cast<int>(r0);
     pa.total_tiles = static_cast<int>(rc) * pa.tiles_k;
-    st = zt == AF2_BF16 ? launch_project<__nv_bfloat16>(ctx, zmap_proj, amap_st, bmap_st, pa, stream)
-                        : launch_project<__half>(ctx, zmap_proj, amap_st, bmap_st, pa, stream);
+    st = zt == AF2_BF16 ? launch_project<__nv_bfloat16>(ctx, zmap_proj, smaps, pa, stream)
+                        : launch_project<__half>(ctx, zmap_proj, smaps, pa, stream);
     if (st != AF2_OK) return st;
-    if (!direct) continue;
+    if (!direct || peer_stores) continue;
     // tile row r is row r of every channel group (outgoing: local pair row; incoming: column)
     const size_t off = (size_t)r0 * L.ab_rs * sizeof(__half), bytes = (size_t)rc * L.ab_rs * sizeof(__half);
     for (int64_t q = 1; q < R; ++q) {
