@@ -1409,11 +1409,16 @@ af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L,
   // ranks while the next computes.
   const bool direct = sharded && shard->direct && shard->direct(ctx, stream, &st);
   if (st != AF2_OK) return st;
-  if (direct && (st = shard->open(ctx, stream)) != AF2_OK) return st;
   // With the peers' scratch mapped, channel group g leaves the projection by TMA store straight
   // into rank g's receive buffer (its slot for this rank), and this rank's own group into its
   // own buffer: no copies after the kernel.
   const bool peer_stores = direct && shard->peer_base && R <= kMaxStoreMaps && R > 1;
+  // Before writing into the peers' receive buffers every peer must be done reading them.  The
+  // shard scratch serves only this op, and the previous call ended with a barrier that every
+  // rank passes only after its contraction (the reader of a and b) and whose output kernel (the
+  // reader of X) precedes this call's projection barrier, so with peer stores no barrier is
+  // needed here; the copy path keeps one.
+  if (direct && !peer_stores && (st = shard->open(ctx, stream)) != AF2_OK) return st;
   if (peer_stores) {
     const uint64_t g_dims[4] = {(uint64_t)k_extent, (uint64_t)hq, (uint64_t)L.ab_rows, 1};
     const uint32_t g_box[4] = {PJ_TILE, (uint32_t)hq, 1, 1};
