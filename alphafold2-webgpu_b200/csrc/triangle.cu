@@ -214,59 +214,15 @@ struct ProjectStoreMaps {
 };
 
 // Normalisation of pair row `row` of a 128B-swizzled K-major tile (two
-// 64-channel chunks `chunk_bytes` apart), in place, 16-bit input -> f16, one
-// thread per row: (x - mean) * rstd.  The LayerNorm's gamma and beta are
-// folded into the weights that consume the tile.  Channels >= cz are padding
-// (zero input) and stay out of the statistics; the weights ignore them.  The
-// statistics are one pass over values shifted by the row's first element,
-// which keeps the f32 sums well conditioned.
-template <typename ZT>
-__device__ __forceinline__ void ln_row_thread(uint8_t *tile, uint32_t chunk_bytes, int row, int cz, float inv_cz,
-                                              float eps) {
-  auto chunk_ptr = [&](int c) { return tile + (c >> 3) * chunk_bytes + sw128_offset(row, c & 7); };
-  const float2 x0 = f2(unpack2<ZT>(reinterpret_cast<const uint32_t *>(chunk_ptr(0))[0]).x);
-  const float2 neg_x0 = f2(-x0.x);
-  float2 s1 = f2(0.f), s2 = f2(0.f);  // even and odd channels, summed separately
-#pragma unroll 4
-  for (int c = 0; c < 16; ++c) {
-    const uint4 v = *reinterpret_cast<const uint4 *>(chunk_ptr(c));
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      float2 d = f2add(unpack2<ZT>(w[i]), neg_x0);
-      if (cz != 128) {
-        const int ch = c * 8 + 2 * i;
-        d.x = ch < cz ? d.x : 0.f;
-        d.y = ch + 1 < cz ? d.y : 0.f;
-      }
-      s1 = f2add(s1, d);
-      s2 = f2fma(d, d, s2);
-    }
-  }
-  const float m1 = (s1.x + s1.y) * inv_cz;
-  const float mean = x0.x + m1;
-  const float var = fmaxf((s2.x + s2.y) * inv_cz - m1 * m1, 0.f);
-  const float rstd = rsqrtf(var + eps);
-  const float2 r2 = f2(rstd), sh2 = f2(-mean * rstd);
-#pragma unroll 4
-  for (int c = 0; c < 16; ++c) {
-    uint8_t *ptr = chunk_ptr(c);
-    const uint4 v = *reinterpret_cast<const uint4 *>(ptr);
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-    uint32_t o[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float2 y = f2fma(unpack2<ZT>(w[i]), r2, sh2);
-      o[i] = pack_half2(y.x, y.y);
-    }
-    *reinterpret_cast<uint4 *>(ptr) = make_uint4(o[0], o[1], o[2], o[3]);
-  }
-}
-
-// The same normalisation with two threads per row: thread `half` takes the
+// 64-channel chunks `chunk_bytes` apart), in place, 16-bit input -> f16:
+// (x - mean) * rstd, with two threads per row: thread `half` takes the
 // 64-channel chunk `half`; the pair combines its shifted sums with lane ^ 16
 // (a warp holds 16 rows, so the 8 lanes of a quarter-warp read 8 different
-// rows: no bank conflicts).  Both threads shift by the row's first channel.
+// rows: no bank conflicts).  The LayerNorm's gamma and beta are folded into
+// the weights that consume the tile.  Channels >= cz are padding (zero input)
+// and stay out of the statistics.  The statistics are one pass over values
+// shifted by the row's first channel (both threads use it), which keeps the
+// f32 sums well conditioned.
 template <typename ZT>
 __device__ __forceinline__ void ln_row_pair(uint8_t *tile, uint32_t chunk_bytes, int row, int half, int cz,
                                             float inv_cz, float eps) {
@@ -786,9 +742,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(CT_THREADS, 1)
 // ---------------------------------------------------------------------------
 constexpr int OP_STAGES = 2;
 // warp 0 TMA, 1 MMA, 2-5 LN_out statistics of X (two lanes per pair of pairs,
-// each over half the channels), 6-9 LN_in of z (one thread per pair row),
-// 10-13 epilogue (one thread per pair row, all 128 output channels).
-constexpr int OP_THREADS = 448;
+// each over half the channels), 6-13 LN_in of z (two threads per pair row),
+// 14-21 epilogue (two warps per TMEM lane quarter: one thread per pair row and
+// half of the 128 output channels).  Two warps per SM sub-partition in each
+// of the z LayerNorm and the epilogue keep their dependent chains overlapped.
+constexpr int OP_THREADS = 704;
 constexpr uint32_t OP_W_BYTES = 2 * 2 * 16384;                 // W_z, W_g
 constexpr uint32_t OP_X_BYTES = 128 * 256, OP_Z_BYTES = 128 * 256;
 constexpr uint32_t OP_STAGE_BYTES = OP_X_BYTES + OP_Z_BYTES;
@@ -845,18 +803,18 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < OP_STAGES; ++s) {
       mbar_init(full(s), 1);
-      mbar_init(ready(s), 8);
+      mbar_init(ready(s), 12);
       mbar_init(empty(s), 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(acc_full(b), 1);
-      mbar_init(acc_empty(b), 4);
+      mbar_init(acc_empty(b), 8);
     }
     mbar_init(drain, 1);
-    mbar_init(out_full, 4);
+    mbar_init(out_full, 8);
     mbar_init(out_free, 1);
     mbar_init(stat_full, 4);
-    mbar_init(stat_free, 4);
+    mbar_init(stat_free, 8);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -940,8 +898,8 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
     // Every MMA has completed before TMEM is freed, whether or not a consumer gave up.
     umma_commit(drain);
     mbar_wait_drain(drain, 0, p.err);
-  } else if (warp < 10) {
-    // ---- LN_out statistics of X (warps 2-5) and LN_in of z in place (warps 6-9) ----
+  } else if (warp < 14) {
+    // ---- LN_out statistics of X (warps 2-5) and LN_in of z in place (warps 6-13) ----
     // X arrives MN-major: two 64-pair blocks 16 KB apart, each 128 h-rows of
     // 128 B, 128B-swizzled.  Lanes 2c and 2c + 1 of an X warp own the adjacent
     // pairs (2c', 2c' + 1) over the lower and upper half of the channels and
@@ -951,7 +909,8 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
     const bool x_role = warp < 6;
     const int tx = (warp - 2) * 32 + lane;  // 0..127 among the X warps
     const int c = tx >> 1, hh = tx & 1;
-    const int zrow = (warp - 6) * 32 + lane;
+    // z: a warp holds 16 rows, lanes l and l + 16 the two 64-channel halves of one
+    const int zrow = (warp - 6) * 16 + (lane & 15), zhalf = lane >> 4;
     int it = 0;
     for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x, ++it) {
       const int s = it % OP_STAGES;
@@ -1000,7 +959,7 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
         if (lane == 0) mbar_arrive(stat_full);
         continue;
       } else {
-        ln_row_thread<ZT>(zs, 16384, zrow, p.cz, inv_cz, p.eps_in);
+        ln_row_pair<ZT>(zs, 16384, zrow, zhalf, p.cz, inv_cz, p.eps_in);
       }
       fence_async_smem();
       __syncwarp();
@@ -1013,47 +972,59 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
     // is sigmoid(x) = 1/2 + tanh(x / 2) / 2.
     // 16-bit outputs with 128 channels are staged in shared memory and leave
     // through TMA: a plain store, or an add into the pair for the residual
-    // form (the old values never pass through the SM).  The first 48
-    // channels of a row are computed into registers before the staging buffer
-    // is claimed, so the previous tile's TMA keeps reading it meanwhile.
+    // form (the old values never pass through the SM).  A thread owns one pair
+    // row and 64 of its channels (warps 14-17 the first half, 18-21 the
+    // second); the first 32 are computed into registers before the staging
+    // buffer is claimed, so the previous tile's TMA keeps reading it meanwhile.
     // Other outputs are written (and, for the residual, read) by the thread
     // that owns the row.
     const int q = warp & 3;
     const int pr = q * 32 + lane;
-    const bool storer = warp == 10 && lane == 0;
+    const int cbase = ((warp - 14) >> 2) * 64;  // this thread's channels: cbase .. cbase + 63
+    const bool storer = warp == 14 && lane == 0;
     bool store_pending = false;
     const float2 half2f = f2(0.5f);
     uint8_t *stage_row = smem + OP_OFF_OUT + pr * 128;
     float2 nmean2 = f2(0.f), rstd2 = f2(0.f);  // this pair row's LN_out statistics
-    // Output values of 16 channels from their two accumulators.
-    auto gate16 = [&](const uint32_t (&vo)[16], const uint32_t (&vg)[16], int c0, float (&v)[16]) {
+    // The per-channel vectors of 8 channels c0 .. c0 + 7 (b_z, b_g / 2 and the
+    // row sums of W_z'), loaded before the TMEM load they accompany: the TMEM
+    // wait is a compiler barrier for memory accesses, so loads written after it
+    // would only start once the accumulator has arrived.
+    struct Vec8 {
+      float4 bz[2], bg[2], zs[2];
+    };
+    auto load_vec8 = [&](int c0, Vec8 &v) {
 #pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) {
-        const float4 bz = *reinterpret_cast<const float4 *>(vbz + c0 + c4 * 4);
-        const float4 bg = *reinterpret_cast<const float4 *>(vbg + c0 + c4 * 4);
-        const float4 zs = *reinterpret_cast<const float4 *>(vzs + c0 + c4 * 4);
-        const float2 bz2[2] = {make_float2(bz.x, bz.y), make_float2(bz.z, bz.w)};
-        const float2 bg2[2] = {f2mul(make_float2(bg.x, bg.y), half2f), f2mul(make_float2(bg.z, bg.w), half2f)};
-        const float2 zs2[2] = {make_float2(zs.x, zs.y), make_float2(zs.z, zs.w)};
+      for (int h = 0; h < 2; ++h) {
+        v.bz[h] = *reinterpret_cast<const float4 *>(vbz + c0 + h * 4);
+        v.bg[h] = *reinterpret_cast<const float4 *>(vbg + c0 + h * 4);
+        v.zs[h] = *reinterpret_cast<const float4 *>(vzs + c0 + h * 4);
+      }
+    };
+    // Output values of those 8 channels from their two accumulators, handed to
+    // sink(cc, value pair of channels c0 + cc, c0 + cc + 1).
+    auto gate8 = [&](const uint32_t (&vo)[8], const uint32_t (&vg)[8], const Vec8 &v, auto &&sink) {
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const float2 bz2[2] = {make_float2(v.bz[h].x, v.bz[h].y), make_float2(v.bz[h].z, v.bz[h].w)};
+        const float2 bg2[2] = {f2mul(make_float2(v.bg[h].x, v.bg[h].y), half2f),
+                               f2mul(make_float2(v.bg[h].z, v.bg[h].w), half2f)};
+        const float2 zs2[2] = {make_float2(v.zs[h].x, v.zs[h].y), make_float2(v.zs[h].z, v.zs[h].w)};
 #pragma unroll
         for (int i = 0; i < 2; ++i) {
-          const int cc = c4 * 4 + 2 * i;
+          const int cc = h * 4 + 2 * i;
           const float2 arg = f2fma(make_float2(__uint_as_float(vg[cc]), __uint_as_float(vg[cc + 1])), half2f, bg2[i]);
           const float2 gate = f2fma(make_float2(tanhf_approx(arg.x), tanhf_approx(arg.y)), half2f, half2f);
           const float2 xo = f2fma(
               f2fma(zs2[i], nmean2, make_float2(__uint_as_float(vo[cc]), __uint_as_float(vo[cc + 1]))), rstd2, bz2[i]);
-          const float2 y = f2mul(xo, gate);
-          v[cc] = y.x;
-          v[cc + 1] = y.y;
+          sink(cc, f2mul(xo, gate));
         }
       }
     };
-    // 16 channels c0.. as OT into the staged row: chunks (c0 % 64) / 8 and +1 of half c0 / 64.
-    auto stage16 = [&](const uint4 (&o)[2], int c0) {
+    // 8 channels c0.. as OT into the staged row: chunk (c0 % 64) / 8 of half c0 / 64.
+    auto stage8 = [&](const uint4 &o, int c0) {
       uint8_t *half_row = stage_row + (c0 >> 6) * 16384;
-      const int ch8 = (c0 & 63) >> 3;
-      *reinterpret_cast<uint4 *>(half_row + (((ch8) ^ (pr & 7)) << 4)) = o[0];
-      *reinterpret_cast<uint4 *>(half_row + (((ch8 + 1) ^ (pr & 7)) << 4)) = o[1];
+      *reinterpret_cast<uint4 *>(half_row + ((((c0 & 63) >> 3) ^ (pr & 7)) << 4)) = o;
     };
     int it = 0;
     for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x, ++it) {
@@ -1073,30 +1044,27 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
       }
       const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * 256;
       if (staged_out) {
-        uint32_t vo[2][16], vg[2][16];
-        uint4 held[3][2];  // channels 0..47 as OT, waiting for the staging buffer
-        tmem_ld16(taddr, vo[0]);
-        tmem_ld16(taddr + 128, vg[0]);
-        tmem_ld_wait();
+        uint4 held[4];  // channels cbase .. cbase + 31 as OT, waiting for the staging buffer
         bool ok = true;
 #pragma unroll
         for (int part = 0; part < 8; ++part) {
-          const int cur = part & 1;
-          if (part + 1 < 8) {
-            tmem_ld16(taddr + (part + 1) * 16, vo[cur ^ 1]);
-            tmem_ld16(taddr + 128 + (part + 1) * 16, vg[cur ^ 1]);
-          }
-          float v[16];
-          gate16(vo[cur], vg[cur], part * 16, v);
-          uint4 o[2];
-          OT *e16 = reinterpret_cast<OT *>(o);
-#pragma unroll
-          for (int cc = 0; cc < 16; ++cc) e16[cc] = from_f32<OT>(v[cc]);
-          if (part < 3) {
-            held[part][0] = o[0];
-            held[part][1] = o[1];
+          const int c0 = cbase + part * 8;
+          Vec8 vec;
+          load_vec8(c0, vec);
+          uint32_t vo[8], vg[8];
+          tmem_ld8(taddr + c0, vo);
+          tmem_ld8(taddr + 128 + c0, vg);
+          tmem_ld_wait();
+          uint4 o;
+          OT *e16 = reinterpret_cast<OT *>(&o);
+          gate8(vo, vg, vec, [&](int cc, float2 y) {
+            e16[cc] = from_f32<OT>(y.x);
+            e16[cc + 1] = from_f32<OT>(y.y);
+          });
+          if (part < 4) {
+            held[part] = o;
           } else {
-            if (part == 3) {  // claim the staging buffer, then release the held channels into it
+            if (part == 4) {  // claim the staging buffer, then release the held channels into it
               if (storer && store_pending) {
                 bulk_wait_read_all();
                 mbar_arrive(out_free);
@@ -1105,11 +1073,10 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
               ok = warp_wait(out_free, (it & 1) ^ 1, abort_flag, p.err, kErrWaitEpilogue);
               if (!ok) break;
 #pragma unroll
-              for (int hp = 0; hp < 3; ++hp) stage16(held[hp], hp * 16);
+              for (int hp = 0; hp < 4; ++hp) stage8(held[hp], cbase + hp * 8);
             }
-            stage16(o, part * 16);
+            stage8(o, c0);
           }
-          if (part + 1 < 8) tmem_ld_wait();
         }
         if (!ok) break;
         fence_async_smem();
@@ -1118,16 +1085,21 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
         const bool live = j < p.n;
 #pragma unroll 1
         for (int part = 0; part < 8; ++part) {
-          const int c0 = part * 16;
-          uint32_t vo[16], vg[16];
-          tmem_ld16(taddr + c0, vo);
-          tmem_ld16(taddr + 128 + c0, vg);
+          const int c0 = cbase + part * 8;
+          Vec8 vec;
+          load_vec8(c0, vec);
+          uint32_t vo[8], vg[8];
+          tmem_ld8(taddr + c0, vo);
+          tmem_ld8(taddr + 128 + c0, vg);
           tmem_ld_wait();
-          float v[16];
-          gate16(vo, vg, c0, v);
+          float v[8];
+          gate8(vo, vg, vec, [&](int cc, float2 y) {
+            v[cc] = y.x;
+            v[cc + 1] = y.y;
+          });
           if (live) {
 #pragma unroll
-            for (int cc = 0; cc < 16; ++cc) {
+            for (int cc = 0; cc < 8; ++cc) {
               if (c0 + cc < p.cz) {
                 float x = v[cc];
                 if (p.residual) x += to_f32<OT>(orow[c0 + cc]);
