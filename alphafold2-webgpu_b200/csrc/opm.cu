@@ -653,11 +653,12 @@ __global__ void __launch_bounds__(OTHREADS, 1)
 // products run.  D2 sums K = (a, b) in ascending 16-wide steps, as the
 // two-kernel path does, from the same f16 operand values.
 //
-// TMEM (512 columns): D2_j at 128 j.  J = 2: D1 double-buffered at 256 and
-// 320, A2 at 384 and 416, the output MMAs of slice g issued behind the outer
-// products of slice g + 1.  J = 3: D1 (96 columns) single at 384, A2_j written
-// over the first half of D1_j; slice g + 1 starts once the output MMAs of
-// slice g have read A2.
+// TMEM (512 columns): D2_j at 128 j.  The output MMAs of slice g are issued
+// behind the outer products of slice g + 1.  J = 2: D1 double-buffered at 256
+// and 320, A2 at 384 and 416.  J = 3: D1 (96 columns) single at 384, released
+// to the outer products of slice g + 1 as soon as the workers have loaded it;
+// A2_0 and A2_1 at 480 and 496 and A2_2, for which TMEM has no room left, in
+// an 8 KB shared-memory tile (64B-swizzled, K-major) read by an SS MMA.
 // Each streamed byte of left serves 32 J outputs per sequence, so J = 3 cuts
 // the left traffic per pair (the kernel's bound, through L2) by a third.
 // Tiles are dealt to CTAs in contiguous runs (j-group major), so a CTA reloads
@@ -674,22 +675,26 @@ struct FusedCfg {
   static constexpr uint32_t kRBlock = J * 32 * 128;            // resident right: bytes per 64-sequence block
   static constexpr int kNB = J == 2 ? 2 : 1;                    // D1 buffers
   static constexpr uint32_t kD1Col = J == 2 ? 256 : 384;
-  static constexpr uint32_t kA2Col = J == 2 ? 384 : 384;        // J = 3: over D1
+  static constexpr uint32_t kA2Col = J == 2 ? 384 : 480;
   static constexpr uint32_t kD1Stride = 64, kA2Stride = 32;     // between buffers (J = 2)
-  // between the A2 blocks of consecutive residues j: J = 3 writes A2_j over the first 16
-  // columns of D1_j, so each worker overwrites only the columns it has read itself
-  static constexpr uint32_t kA2J = J == 2 ? 16 : 32;
+  static constexpr uint32_t kA2J = 16;                          // between the A2 blocks of residues j
+  static constexpr int kA2Tmem = 2;  // residues whose A2 is in TMEM (J = 3: the third's is in shared memory)
 };
 
-// Shared-memory map: right (resident) | left ring | W_o ring (2) | barriers.
+// Shared-memory map: right (resident) | left ring | W_o ring (2) | A2 tile of the
+// third residue (J = 3: [128 i][32 b] f16, 64B-swizzled) | barriers.
 __host__ __device__ constexpr uint32_t fused_off_l(int k_blocks, int j) {
   return static_cast<uint32_t>(k_blocks) * j * 32u * 128u;
 }
 __host__ __device__ constexpr uint32_t fused_off_w(int k_blocks, int j, int lst) {
   return fused_off_l(k_blocks, j) + static_cast<uint32_t>(lst) * FL_STAGE;
 }
-__host__ __device__ constexpr uint32_t fused_off_bar(int k_blocks, int j, int lst) {
+constexpr uint32_t kFusedA2Bytes = 128 * 64;
+__host__ __device__ constexpr uint32_t fused_off_a2(int k_blocks, int j, int lst) {
   return fused_off_w(k_blocks, j, lst) + 2 * FW_STAGE;
+}
+__host__ __device__ constexpr uint32_t fused_off_bar(int k_blocks, int j, int lst) {
+  return fused_off_a2(k_blocks, j, lst) + (j == 3 ? kFusedA2Bytes : 0u);
 }
 __host__ __device__ constexpr uint32_t fused_smem(int k_blocks, int j, int lst) {
   return fused_off_bar(k_blocks, j, lst) + kFusedBarBytes + 1024;
@@ -741,7 +746,9 @@ __global__ void __launch_bounds__(FTHREADS, 1)
   auto a2_full = [&](int b) { return bar0 + 8u * (2 * FLST_MAX + 6 + b); };
   auto a2_empty = [&](int b) { return bar0 + 8u * (2 * FLST_MAX + 8 + b); };
   const uint32_t r_full = bar0 + 8u * (2 * FLST_MAX + 10), r_empty = r_full + 8u, d2_full = r_full + 16u,
-                 d2_empty = r_full + 24u, drain = r_full + 32u;  // 31 barriers: 248 bytes
+                 d2_empty = r_full + 24u, drain = r_full + 32u;
+  const uint32_t d1_free = r_full + 40u;  // J = 3: the workers have loaded D1 (32 barriers: 256 bytes)
+  const uint32_t s_a2 = sbase + fused_off_a2(p.k_blocks, J, lst);
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + fused_off_bar(p.k_blocks, J, lst) + 256);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + fused_off_bar(p.k_blocks, J, lst) + 264);
   const int warp = warp_index_uniform(), lane = threadIdx.x & 31;
@@ -764,6 +771,7 @@ __global__ void __launch_bounds__(FTHREADS, 1)
     mbar_init(r_empty, 1);
     mbar_init(d2_full, 1);
     mbar_init(d2_empty, 4 * J);
+    mbar_init(d1_free, 4 * J);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -797,16 +805,6 @@ __global__ void __launch_bounds__(FTHREADS, 1)
           prev_jg = jg;
         }
         for (int a = 0; ok && a < C; ++a) {
-          {  // W_o rows of channel a: one [n_out][32] K-major tile
-            const int ws = wq & 1;
-            if (!mbar_wait(w_empty(ws), ((wq >> 1) & 1) ^ 1, abort_flag, p.err, kErrWaitProducer)) {
-              ok = false;
-              break;
-            }
-            mbar_arrive_expect_tx(w_full(ws), w_bytes);
-            tma_load_3d(s_w + ws * FW_STAGE, &wmap, w_full(ws), (a & 1) * 32, 0, a >> 1);
-            ++wq;
-          }
           for (int kb = 0; kb < p.k_blocks; ++kb) {
             if (!mbar_wait(l_empty(ls), lph ^ 1, abort_flag, p.err, kErrWaitProducer)) {
               ok = false;
@@ -820,6 +818,18 @@ __global__ void __launch_bounds__(FTHREADS, 1)
               ls = 0;
               lph ^= 1;
             }
+          }
+          if (!ok) break;
+          {  // W_o rows of channel a: one [n_out][32] K-major tile, used by the output MMAs that
+             // follow the next slice's outer products, so it is loaded after this slice's left
+            const int ws = wq & 1;
+            if (!mbar_wait(w_empty(ws), ((wq >> 1) & 1) ^ 1, abort_flag, p.err, kErrWaitProducer)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(w_full(ws), w_bytes);
+            tma_load_3d(s_w + ws * FW_STAGE, &wmap, w_full(ws), (a & 1) * 32, 0, a >> 1);
+            ++wq;
           }
         }
       }
@@ -851,11 +861,20 @@ __global__ void __launch_bounds__(FTHREADS, 1)
       const uint32_t a2 = tmem + Cfg::kA2Col + bp * Cfg::kA2Stride;
 #pragma unroll
       for (int j = 0; j < J; ++j) {
-        if (a == 0)
-          umma_ts_first(tmem + kD2Col + 128 * j, a2 + Cfg::kA2J * j, bd, idesc2);
-        else
-          umma_ts_acc(tmem + kD2Col + 128 * j, a2 + Cfg::kA2J * j, bd, idesc2);
-        umma_ts_acc(tmem + kD2Col + 128 * j, a2 + Cfg::kA2J * j + 8, bd + 2, idesc2);
+        if (j < Cfg::kA2Tmem) {
+          if (a == 0)
+            umma_ts_first(tmem + kD2Col + 128 * j, a2 + Cfg::kA2J * j, bd, idesc2);
+          else
+            umma_ts_acc(tmem + kD2Col + 128 * j, a2 + Cfg::kA2J * j, bd, idesc2);
+          umma_ts_acc(tmem + kD2Col + 128 * j, a2 + Cfg::kA2J * j + 8, bd + 2, idesc2);
+        } else {  // J = 3, third residue: A2 from the shared-memory tile
+          const uint64_t ad = sdesc_k_sw64(s_a2);
+          if (a == 0)
+            umma_first(tmem + kD2Col + 128 * j, ad, bd, idesc2);
+          else
+            umma_acc(tmem + kD2Col + 128 * j, ad, bd, idesc2);
+          umma_acc(tmem + kD2Col + 128 * j, ad + 2, bd + 2, idesc2);
+        }
       }
       umma_commit(a2_empty(bp));
       umma_commit(w_empty(ws));
@@ -870,8 +889,8 @@ __global__ void __launch_bounds__(FTHREADS, 1)
         prev_jg = jg;
       }
       for (int a = 0; a < C; ++a, ++g) {
-        if (J == 3 && g > 0 && !warp_wait(a2_empty(0), ((g - 1) & 1), abort_flag, p.err, kErrWaitMma)) {
-          ok = false;  // D1 holds slice g - 1's A2 until its output MMAs have read it
+        if (J == 3 && g > 0 && !warp_wait(d1_free, ((g - 1) & 1), abort_flag, p.err, kErrWaitMma)) {
+          ok = false;  // the single D1 is free once the workers have loaded slice g - 1's
           break;
         }
         const uint32_t d1 = tmem + Cfg::kD1Col + (g % Cfg::kNB) * Cfg::kD1Stride;
@@ -900,17 +919,12 @@ __global__ void __launch_bounds__(FTHREADS, 1)
         }
         if (!ok) break;
         umma_commit(d1_full(g % Cfg::kNB));
-        if (J == 3) {  // no lag: this slice's output MMAs follow its conversion
-          if (!outputs(g, a)) {
-            ok = false;
-            break;
-          }
-        } else if (a > 0 && !outputs(g - 1, a - 1)) {
+        if (a > 0 && !outputs(g - 1, a - 1)) {
           ok = false;
           break;
         }
       }
-      if (!ok || (J == 2 && !outputs(g - 1, C - 1))) break;
+      if (!ok || !outputs(g - 1, C - 1)) break;
       umma_commit(d2_full);
       if (t + 1 < t_end && (t + 1) / p.n_ib != jg) umma_commit(r_empty);
     }
@@ -941,11 +955,36 @@ __global__ void __launch_bounds__(FTHREADS, 1)
           uint32_t v[32], pk[16];
           tmem_ld32(tmem + lane_off + Cfg::kD1Col + b * Cfg::kD1Stride + 32 * jw, v);
           tmem_ld_wait();
+          if (J == 3) {  // D1 is loaded: the next slice's outer products may overwrite it
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(d1_free);
+          }
 #pragma unroll
           for (int c = 0; c < 16; ++c)
             pk[c] = pack_half2(__uint_as_float(v[2 * c]) * p.scale, __uint_as_float(v[2 * c + 1]) * p.scale);
-          tmem_st16(tmem + lane_off + Cfg::kA2Col + b * Cfg::kA2Stride + Cfg::kA2J * jw, pk);
-          tmem_st_wait();
+          // J = 3: the previous slice's output MMAs have read A2
+          if (J == 3 && g > 0) {
+            if (!warp_wait(a2_empty(0), (g - 1) & 1, abort_flag, p.err, kErrWaitEpilogue)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+          }
+          if (jw < Cfg::kA2Tmem) {
+            tmem_st16(tmem + lane_off + Cfg::kA2Col + b * Cfg::kA2Stride + Cfg::kA2J * jw, pk);
+            tmem_st_wait();
+          } else {
+            // row i = 32 q + lane of the [128][32] f16 tile, 64 bytes in four 16-byte chunks,
+            // chunk c stored at c ^ ((i >> 1) & 3) (the 64-byte swizzle)
+            const int i = q * 32 + lane;
+            uint8_t *row = smem + fused_off_a2(p.k_blocks, J, lst) + i * 64;
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+              *reinterpret_cast<uint4 *>(row + ((c ^ ((i >> 1) & 3)) << 4)) =
+                  make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+            fence_async_smem();
+          }
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(a2_full(b));
