@@ -45,20 +45,21 @@ namespace trn {
 
 constexpr int TILE = 128;     // rows per tile (one TMEM lane each)
 constexpr int HC = 128;       // hidden channels per chunk (the first GEMM's N)
-constexpr int STAGES = 2;     // weight-chunk ring
+constexpr int STAGES = 4;     // weight-chunk ring
 constexpr int LAG = 1;        // second-GEMM chunks trail the first by this many
-constexpr int NBUF = 2;       // D1 accumulators and H operand buffers (> LAG)
+constexpr int NBUF = 2;       // D1 accumulators, each holding its H operand once converted (> LAG)
 constexpr int THREADS = 448;  // 14 warps: 0 TMA, 1 MMA, 2-5 LayerNorm + second epilogue, 6-13 first epilogue
 
 // Shared-memory map (bytes from the 1024-aligned base); kb = channel blocks of 64.
 //   A  2 x [kb][128 rows][128 B]      x tiles (normalised in place)
 //   W  STAGES x kb x 16 KB            weight chunks: W1 [kb][128 h][128 B], W2 [2][cp][128 B]
-//   H  NBUF x [2][128 rows][128 B]    relu(hidden) chunks, f16
 //   O  [128 rows][128 B]              output staging (64 channels at a time)
+// The relu(hidden) chunks (the second GEMM's A operand, f16) never reach shared
+// memory: the first epilogue writes each into the first 64 TMEM columns of the
+// D1 accumulator it came from, and the second GEMM reads A from TMEM.
 //   barriers, then gamma beta scale2 bias2 [cp] and scale1 bias1 [hp]
 __host__ __device__ constexpr uint32_t off_w(int kb) { return 2u * kb * 16384u; }
-__host__ __device__ constexpr uint32_t off_h(int kb) { return off_w(kb) + STAGES * kb * 16384u; }
-__host__ __device__ constexpr uint32_t off_o(int kb) { return off_h(kb) + NBUF * 32768u; }
+__host__ __device__ constexpr uint32_t off_o(int kb) { return off_w(kb) + STAGES * kb * 16384u; }
 __host__ __device__ constexpr uint32_t off_bar(int kb) { return off_o(kb) + 16384u; }
 __host__ __device__ constexpr uint32_t off_vec(int kb) { return off_bar(kb) + 512u; }
 
@@ -189,7 +190,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint8_t *smem = align1024(smem_raw);
   const uint32_t sbase = smem_u32(smem);
   constexpr int kb = KB;
-  const uint32_t OFF_W = off_w(kb), OFF_H = off_h(kb), OFF_O = off_o(kb), OFF_BAR = off_bar(kb);
+  const uint32_t OFF_W = off_w(kb), OFF_O = off_o(kb), OFF_BAR = off_bar(kb);
   const uint32_t A_BYTES = kb * 16384u, W_BYTES = kb * 16384u;
   const uint32_t W2_KSTRIDE = p.cp * 128u;  // bytes between the two 64-wide K blocks of a W2 chunk
   const uint32_t bar0 = sbase + OFF_BAR;
@@ -303,8 +304,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint32_t idesc1 = idesc_f16_f32(TILE, HC);
     const uint32_t idesc2 = idesc_f16_f32(TILE, p.cp);
     // Base descriptors; every operand below is one of these plus a constant.
-    const uint64_t a_desc = sdesc_k_sw128(sbase), w_desc = sdesc_k_sw128(sbase + OFF_W),
-                   h_desc = sdesc_k_sw128(sbase + OFF_H);
+    const uint64_t a_desc = sdesc_k_sw128(sbase), w_desc = sdesc_k_sw128(sbase + OFF_W);
     int ws = 0;
     int it1 = 0, h1 = 0, it2 = 0, h2 = 0;  // tile and step of the next first / second GEMM
     for (int j = 0; j < total + LAG; ++j) {
@@ -331,23 +331,25 @@ __global__ void __launch_bounds__(THREADS, 1)
           ++it1;
         }
       }
-      if (j >= LAG) {  // second GEMM of step i = j - LAG: D2[tile] += H[i % NBUF] W2[chunk]
+      if (j >= LAG) {  // second GEMM of step i = j - LAG: D2[tile] += H[i % NBUF] W2[chunk], H in TMEM
         const int i = j - LAG, buf = it2 & 1, hb = i % NBUF, s = ws % STAGES;
         if (!warp_wait(h_full(hb), (i / NBUF) & 1, abort_flag, p.err, kErrWaitMma) ||
             !warp_wait(w_full(s), (ws / STAGES) & 1, abort_flag, p.err, kErrWaitMma) ||
             (h2 == 0 && !warp_wait(d2_empty(buf), ((it2 >> 1) & 1) ^ 1, abort_flag, p.err, kErrWaitMma)))
           break;
         tc_fence_after();
-        const uint64_t hd = desc_add(h_desc, hb * 32768), wd = desc_add(w_desc, s * W_BYTES);
+        // H of step i: 128 rows x 128 hidden f16 = 64 TMEM columns at D1[hb]; a K step of
+        // 16 hidden channels is 8 columns
+        const uint32_t hd = tmem + hb * HC;
+        const uint64_t wd = desc_add(w_desc, s * W_BYTES);
         const uint32_t d = tmem + 256 + buf * 128;
         if (h2 == 0)
-          umma_first(d, hd, wd, idesc2);
+          umma_ts_first(d, hd, wd, idesc2);
         else
-          umma_acc(d, hd, wd, idesc2);
+          umma_ts_acc(d, hd, wd, idesc2);
 #pragma unroll
         for (int ks = 1; ks < 8; ++ks)
-          umma_acc(d, desc_add(hd, (ks >> 2) * 16384 + (ks & 3) * 32),
-                      desc_add(wd, (ks >> 2) * W2_KSTRIDE + (ks & 3) * 32), idesc2);
+          umma_ts_acc(d, hd + ks * 8, desc_add(wd, (ks >> 2) * W2_KSTRIDE + (ks & 3) * 32), idesc2);
         umma_commit(w_empty(s));
         umma_commit(h_empty(hb));
         if (h2 == nh - 1) umma_commit(d2_full(buf));
@@ -451,10 +453,11 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (lane == 0 && store_pending) bulk_wait_all();
   } else {
     // ---- first epilogue, two groups of four warps taking alternate chunks:
-    //      D1 chunk -> relu(scale1 * acc + b1) -> f16 H operand rows ----
+    //      D1 chunk -> relu(scale1 * acc + b1) -> f16 H, written back over the
+    //      first 64 columns of the same accumulator (each half after this
+    //      thread has loaded the columns it overwrites) ----
     const int q = warp & 3;  // TMEM lane quarter this warp may read
     const int group = (warp - 6) >> 2;
-    const int row = q * 32 + lane;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
     ChunkCursor cur;
     cur.start(nh);
@@ -465,24 +468,17 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (!warp_wait(d1_full(db), ph, abort_flag, p.err, kErrWaitEpilogue)) break;
       tc_fence_after();
       if (!warp_wait(h_empty(db), ph ^ 1, abort_flag, p.err, kErrWaitEpilogue)) break;
-      uint8_t *hbuf = smem + OFF_H + db * 32768;
 #pragma unroll 1
-      for (int half = 0; half < 2; ++half) {  // 64 hidden channels = one 128-byte K block of the H row
+      for (int half = 0; half < 2; ++half) {  // 64 hidden channels: 64 f32 columns in, 32 packed f16 columns out
         uint32_t v[2][32];
         tmem_ld32(lane_base + db * HC + half * 64, v[0]);
         tmem_ld32(lane_base + db * HC + half * 64 + 32, v[1]);
         tmem_ld_wait();
-        if (half == 1) {  // the whole accumulator has been read: release it
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(d1_empty(db));
-        }
         const float4 *sc = reinterpret_cast<const float4 *>(s1v + h * HC + half * 64);
         const float4 *bi = reinterpret_cast<const float4 *>(b1v + h * HC + half * 64);
-        uint8_t *hrow = hbuf + half * 16384;
+        uint32_t pk[32];
 #pragma unroll
-        for (int c16 = 0; c16 < 8; ++c16) {  // 8 hidden channels = one 16-byte chunk of the row
-          uint32_t pk[4];
+        for (int c16 = 0; c16 < 8; ++c16) {  // 8 hidden channels
 #pragma unroll
           for (int i2 = 0; i2 < 2; ++i2) {
             const float4 sv = sc[c16 * 2 + i2], bv = bi[c16 * 2 + i2];
@@ -493,15 +489,19 @@ __global__ void __launch_bounds__(THREADS, 1)
             const float2 y1 =
                 f2fma(make_float2(__uint_as_float(v[c >> 5][(c + 2) & 31]), __uint_as_float(v[c >> 5][(c + 3) & 31])),
                       make_float2(sv.z, sv.w), make_float2(bv.z, bv.w));
-            pk[i2 * 2] = pack_half2_relu(y0.x, y0.y);
-            pk[i2 * 2 + 1] = pack_half2_relu(y1.x, y1.y);
+            pk[c16 * 4 + i2 * 2] = pack_half2_relu(y0.x, y0.y);
+            pk[c16 * 4 + i2 * 2 + 1] = pack_half2_relu(y1.x, y1.y);
           }
-          *reinterpret_cast<uint4 *>(hrow + sw128_offset(row, c16)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
         }
+        tmem_st32(lane_base + db * HC + half * 32, pk);
       }
-      fence_async_smem();
+      tmem_st_wait();
+      tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(h_full(db));
+      if (lane == 0) {
+        mbar_arrive(h_full(db));
+        mbar_arrive(d1_empty(db));
+      }
     }
   }
 
