@@ -48,7 +48,8 @@ constexpr int HC = 128;       // hidden channels per chunk (the first GEMM's N)
 constexpr int STAGES = 4;     // weight-chunk ring
 constexpr int LAG = 1;        // second-GEMM chunks trail the first by this many
 constexpr int NBUF = 2;       // D1 accumulators, each holding its H operand once converted (> LAG)
-constexpr int THREADS = 448;  // 14 warps: 0 TMA, 1 MMA, 2-5 LayerNorm + second epilogue, 6-13 first epilogue
+// 14 warps: 0 TMA, 1 MMA, 2-5 second epilogue, 6-9 LayerNorm of the x tiles, 10-13 first epilogue
+constexpr int THREADS = 448;
 
 // Shared-memory map (bytes from the 1024-aligned base); kb = channel blocks of 64.
 //   A  2 x [kb][128 rows][128 B]      x tiles (normalised in place)
@@ -363,8 +364,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     // Every MMA has completed before TMEM is freed, whether or not a consumer gave up.
     umma_commit(drain);
     mbar_wait_drain(drain, 0, p.err);
-  } else if (warp < 6) {
-    // ---- row warps: LayerNorm of tile it+1, then the second epilogue of tile it ----
+  } else if (warp < 10) {
+    // ---- row warps: 2-5 the second epilogue of every tile, 6-9 the LayerNorm of every
+    //      x tile (running ahead of the first GEMMs by the two x buffers) ----
     const int q = warp & 3;  // TMEM lane quarter this warp may read
     const int row = q * 32 + lane;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
@@ -443,26 +445,24 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       return true;
     };
-    // The next tile's LayerNorm comes first: the first GEMM of tile it+1 must
-    // not wait for the output of tile it.
-    bool ok = my_tiles == 0 || layer_norm(0);
-    for (int it = 0; ok && it < my_tiles; ++it) {
-      if (it + 1 < my_tiles) ok = layer_norm(it + 1);
-      ok = ok && second_epilogue(it);
+    if (warp >= 6) {
+      for (int it = 0; it < my_tiles; ++it)
+        if (!layer_norm(it)) break;
+    } else {
+      for (int it = 0; it < my_tiles; ++it)
+        if (!second_epilogue(it)) break;
     }
     if (lane == 0 && store_pending) bulk_wait_all();
   } else {
-    // ---- first epilogue, two groups of four warps taking alternate chunks:
+    // ---- first epilogue, four warps taking every chunk:
     //      D1 chunk -> relu(scale1 * acc + b1) -> f16 H, written back over the
     //      first 64 columns of the same accumulator (each half after this
     //      thread has loaded the columns it overwrites) ----
     const int q = warp & 3;  // TMEM lane quarter this warp may read
-    const int group = (warp - 6) >> 2;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
     ChunkCursor cur;
     cur.start(nh);
-    if (group == 1) cur.advance();
-    for (int j = group; j < total; j += 2, cur.advance(), cur.advance()) {
+    for (int j = 0; j < total; ++j, cur.advance()) {
       const int db = j % NBUF, h = cur.chunk;
       const uint32_t ph = (j / NBUF) & 1;
       if (!warp_wait(d1_full(db), ph, abort_flag, p.err, kErrWaitEpilogue)) break;
