@@ -111,6 +111,18 @@ __device__ __forceinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity, u
   return false;
 }
 
+// 4-byte asynchronous copy global -> shared (zero-filled when `valid` is false;
+// the source is then not read), and the arrive-on of `bar` that fires once all
+// of this thread's earlier such copies have landed (counted against the
+// barrier's expected arrivals).
+__device__ __forceinline__ void cp_async_4(uint32_t dst, const void *src, bool valid) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(valid ? 4 : 0) : "memory");
+}
+__device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 // ---- proxy fences / named barriers -----------------------------------------
 
 // Makes this thread's generic-proxy shared-memory writes visible to the async

@@ -182,10 +182,14 @@ constexpr uint32_t PJ_CHUNK = PJ_TILE * 128;            // one 64-channel K chun
 constexpr uint32_t PJ_STAGE_BYTES = 2 * PJ_CHUNK;       // 16 KB
 constexpr uint32_t PJ_W_BYTES = 4 * 2 * 16384;          // 128 KB
 constexpr uint32_t PJ_OFF_STAGE = PJ_W_BYTES;
-constexpr uint32_t PJ_OFF_MASK = PJ_OFF_STAGE + PJ_STAGES * PJ_STAGE_BYTES;  // 8 warps x 64 f32
+// Mask ring: each tile's 64 mask values, copied in by the producer warp and
+// read by the epilogue (a ring of its own: the z stage is refilled before the
+// epilogue of its tile runs).
+constexpr int PJ_MASK_SLOTS = 4;
+constexpr uint32_t PJ_OFF_MASK = PJ_OFF_STAGE + PJ_STAGES * PJ_STAGE_BYTES;
 // Output staging: the tile's gated a and b, each [128 h][64 pairs] f16 in
 // 128B-swizzled rows, written to HBM by two TMA stores.
-constexpr uint32_t PJ_OFF_OUT = PJ_OFF_MASK + 8 * 256;
+constexpr uint32_t PJ_OFF_OUT = PJ_OFF_MASK + 2048;  // PJ_MASK_SLOTS x 64 f32 (1 KB), rounded up
 constexpr uint32_t PJ_OUT_BYTES = 128 * 128;
 constexpr uint32_t PJ_OFF_BAR = PJ_OFF_OUT + 2 * PJ_OUT_BYTES;
 constexpr uint32_t PJ_SMEM = PJ_OFF_BAR + 256 + 1024;
@@ -286,6 +290,8 @@ __global__ void __launch_bounds__(PJ_THREADS, 1)
   const uint32_t drain = bar0 + 8u * 13;
   const uint32_t out_full = bar0 + 8u * 14;  // all 8 epilogue warps have staged the tile
   const uint32_t out_free = bar0 + 8u * 15;  // the staged tile has been read by the TMA stores
+  auto mask_full = [&](int m) { return bar0 + 8u * (16 + m); };   // a tile's mask has landed
+  auto mask_empty = [&](int m) { return bar0 + 8u * (20 + m); };  // the epilogue has read it
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + PJ_OFF_BAR + 192);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + PJ_OFF_BAR + 200);
   const int warp = warp_index_uniform(), lane = threadIdx.x & 31;
@@ -306,6 +312,10 @@ __global__ void __launch_bounds__(PJ_THREADS, 1)
     mbar_init(drain, 1);
     mbar_init(out_full, 8);
     mbar_init(out_free, 1);
+    for (int m = 0; m < PJ_MASK_SLOTS; ++m) {
+      mbar_init(mask_full(m), 32);
+      mbar_init(mask_empty(m), 8);
+    }
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -319,30 +329,47 @@ __global__ void __launch_bounds__(PJ_THREADS, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    // ---- TMA producer ----
-    if (lane == 0) {
-      tma_prefetch_map(&zmap);
-      int it = 0;
-      bool ok = true;
-      for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x, ++it) {
-        const int s = it % PJ_STAGES;
-        const uint32_t ph = (it / PJ_STAGES) & 1;
-        if (!mbar_wait(z_empty(s), ph ^ 1, abort_flag, p.err, kErrWaitProducer)) {
-          ok = false;
-          break;
-        }
-        const int r = p.r_begin + t / p.tiles_k, kb = t % p.tiles_k;
+    // ---- producer: lane 0 issues the z tiles by TMA, every lane copies two of the
+    //      tile's 64 mask values (cp.async, zero past the extent) ----
+    if (lane == 0) tma_prefetch_map(&zmap);
+    int it = 0;
+    int tr = blockIdx.x / p.tiles_k, tk = blockIdx.x % p.tiles_k;  // tile t = tr tiles_k + tk
+    const int dr = gridDim.x / p.tiles_k, dk = gridDim.x % p.tiles_k;
+    for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x, ++it) {
+      const int s = it % PJ_STAGES, m = it % PJ_MASK_SLOTS;
+      const uint32_t ph = (it / PJ_STAGES) & 1;
+      if (!warp_wait(z_empty(s), ph ^ 1, abort_flag, p.err, kErrWaitProducer) ||
+          !warp_wait(mask_empty(m), ((it / PJ_MASK_SLOTS) & 1) ^ 1, abort_flag, p.err, kErrWaitProducer))
+        break;
+      const int r = p.r_begin + tr, kb = tk;
+      if (lane == 0) {
         const uint32_t dst = sbase + PJ_OFF_STAGE + s * PJ_STAGE_BYTES;
         mbar_arrive_expect_tx(z_full(s), PJ_STAGE_BYTES);
         const int c1 = p.transposed ? r : kb * PJ_TILE, c2 = p.transposed ? kb * PJ_TILE : r;
         tma_load_3d(dst, &zmap, z_full(s), 0, c1, c2);
         tma_load_3d(dst + PJ_CHUNK, &zmap, z_full(s), 64, c1, c2);
       }
-      {  // every load issued has landed before the CTA exits (immediate unless a consumer gave up)
-        for (int j = it > PJ_STAGES ? it - PJ_STAGES : 0; j < it; ++j)
-          mbar_wait_drain(z_full(j % PJ_STAGES), (j / PJ_STAGES) & 1, p.err);
+      const uint32_t mdst = sbase + PJ_OFF_MASK + m * 256;
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int k = kb * PJ_TILE + hh * 32 + lane;
+        const bool valid = k < p.k_extent;
+        const float *src = valid ? p.mask + (int64_t)r * p.mask_rs + (int64_t)k * p.mask_ks : p.mask;
+        cp_async_4(mdst + (hh * 32 + lane) * 4, src, valid);
+      }
+      cp_async_arrive_noinc(mask_full(m));
+      tk += dk;
+      tr += dr;
+      if (tk >= p.tiles_k) {
+        tk -= p.tiles_k;
+        ++tr;
       }
     }
+    // every load issued has landed before the CTA exits (immediate unless a consumer gave up)
+    cp_async_wait_all();
+    if (lane == 0)
+      for (int j = it > PJ_STAGES ? it - PJ_STAGES : 0; j < it; ++j)
+        mbar_wait_drain(z_full(j % PJ_STAGES), (j / PJ_STAGES) & 1, p.err);
   } else if (warp == 1) {
     // ---- MMA issuer: the whole warp runs the loop, one elected lane issues ----
     constexpr uint32_t kIdesc = idesc_f16_f32(128, PJ_TILE);
@@ -409,27 +436,23 @@ __global__ void __launch_bounds__(PJ_THREADS, 1)
     const float bias_g = p.vec[(op ? kVBBG : kVBAG) * C + h];
     const float2 half2f = f2(0.5f), gate_shift = f2(0.5f * bias_g), bias_p2 = f2(bias_p);
     uint8_t *stage_row = smem + PJ_OFF_OUT + op * PJ_OUT_BYTES + h * 128;
-    float *msk = reinterpret_cast<float *>(smem + PJ_OFF_MASK) + e * 64;
-    auto mask_at = [&](int t, int k) -> float {
-      if (t >= p.total_tiles || k >= p.k_extent) return 0.f;
-      return p.mask[(int64_t)(p.r_begin + t / p.tiles_k) * p.mask_rs + (int64_t)k * p.mask_ks];
-    };
-    int t = blockIdx.x;
-    float m0 = mask_at(t, (t % p.tiles_k) * PJ_TILE + lane);
-    float m1 = mask_at(t, (t % p.tiles_k) * PJ_TILE + 32 + lane);
+    int tr = blockIdx.x / p.tiles_k, tk = blockIdx.x % p.tiles_k;  // tile t = tr tiles_k + tk
+    const int dr = gridDim.x / p.tiles_k, dk = gridDim.x % p.tiles_k;
     int it = 0;
-    for (; t < p.total_tiles; t += gridDim.x, ++it) {
-      const int r = p.r_begin + t / p.tiles_k, k0 = (t % p.tiles_k) * PJ_TILE;
-      const int buf = it & 1;
+    for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x, ++it) {
+      const int r = p.r_begin + tr, k0 = tk * PJ_TILE;
+      tk += dk;
+      tr += dr;
+      if (tk >= p.tiles_k) {
+        tk -= p.tiles_k;
+        ++tr;
+      }
+      const int buf = it & 1, m = it % PJ_MASK_SLOTS;
       const uint32_t bph = (it >> 1) & 1;
-      // this tile's mask goes to shared memory; the next tile's is fetched now
-      msk[lane] = m0;
-      msk[32 + lane] = m1;
-      const int tn = t + gridDim.x;
-      m0 = mask_at(tn, (tn % p.tiles_k) * PJ_TILE + lane);
-      m1 = mask_at(tn, (tn % p.tiles_k) * PJ_TILE + 32 + lane);
-      __syncwarp();
-      if (!warp_wait(acc_full(buf), bph, abort_flag, p.err, kErrWaitEpilogue)) break;
+      const float *msk = reinterpret_cast<const float *>(smem + PJ_OFF_MASK + m * 256);
+      if (!warp_wait(acc_full(buf), bph, abort_flag, p.err, kErrWaitEpilogue) ||
+          !warp_wait(mask_full(m), (it / PJ_MASK_SLOTS) & 1, abort_flag, p.err, kErrWaitEpilogue))
+        break;
       tc_fence_after();
       const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * 256 + op * 2 * PJ_TILE;
       // The whole tile leaves TMEM first (loads pipelined one part ahead of the
@@ -469,7 +492,10 @@ __global__ void __launch_bounds__(PJ_THREADS, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(acc_empty(buf));
+      if (lane == 0) {
+        mbar_arrive(acc_empty(buf));
+        mbar_arrive(mask_empty(m));
+      }
       if (storer && store_pending) {  // the previous tile's stores have read the staging buffer
         bulk_wait_read_all();
         mbar_arrive(out_free);
