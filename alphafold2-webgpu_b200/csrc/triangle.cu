@@ -560,7 +560,11 @@ constexpr int CT_PAIR_M = 2 * CT_BM;                    // rows of a pair tile
 constexpr uint32_t CT_A_BYTES = CT_BM * 128;             // this CTA's 128 rows of A per K block
 constexpr uint32_t CT_B_BYTES = (CT_BN / 2) * 128;       // and its 128 rows of B
 constexpr uint32_t CT_STAGE_BYTES = CT_A_BYTES + CT_B_BYTES;
-constexpr uint32_t CT_OFF_BAR = CT_STAGES * CT_STAGE_BYTES;
+// Epilogue staging: per epilogue warp two [32 rows][32 columns] f16 blocks (64B-swizzled rows),
+// each written to the product by one TMA store.
+constexpr uint32_t CT_OFF_XSTAGE = CT_STAGES * CT_STAGE_BYTES;
+constexpr uint32_t CT_XSTAGE_BYTES = 2048;
+constexpr uint32_t CT_OFF_BAR = CT_OFF_XSTAGE + 4 * 2 * CT_XSTAGE_BYTES;
 constexpr uint32_t CT_SMEM = CT_OFF_BAR + 256 + 1024;
 
 struct ContractArgs {
@@ -582,6 +586,7 @@ struct ContractArgs {
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(CT_THREADS, 1)
     contract_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap bmap,
                     const __grid_constant__ CUtensorMap amap_own, const __grid_constant__ CUtensorMap bmap_own,
+                    const __grid_constant__ CUtensorMap xmap_out, const __grid_constant__ CUtensorMap xmap_own,
                     const ContractArgs p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = align1024(smem_raw);
@@ -711,9 +716,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(CT_THREADS, 1)
       mbar_wait_drain(drain, 0, p.err);
     }
   } else {
+    // Epilogue: each warp takes its TMEM lane quarter (32 product rows) in chunks of 32 columns:
+    // TMEM -> scaled f16 -> a 64B-swizzled block in shared memory -> one TMA store into the
+    // product (x_out, or x_own for this rank's own block), two blocks in flight per warp.
     const int q = warp & 3;
-    const int row = q * 32 + lane;
-    int tile_it = 0;
+    const uint32_t stage0 = sbase + CT_OFF_XSTAGE + (warp - 2) * 2 * CT_XSTAGE_BYTES;
+    uint8_t *stage0_ptr = smem + CT_OFF_XSTAGE + (warp - 2) * 2 * CT_XSTAGE_BYTES;
+    int tile_it = 0, stores = 0;
     for (int t = pair; t < p.total_tiles; t += npairs, ++tile_it) {
       const int h = t / tiles_per_h, rem = t % tiles_per_h;
       const int mi = rem / p.tiles_n, ni = rem % p.tiles_n;
@@ -721,12 +730,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(CT_THREADS, 1)
       const uint32_t bph = (tile_it >> 1) & 1;
       if (!warp_wait(acc_full(buf), bph, abort_flag, p.err, kErrWaitEpilogue)) break;
       tc_fence_after();
-      const int gi = mi * CT_PAIR_M + rank * CT_BM + row;  // row inside this launch
-      const bool row_ok = gi < p.row_count;
-      const int blk = gi / p.block_rows_out, gl = gi - blk * p.block_rows_out;
+      const int g0 = mi * CT_PAIR_M + rank * CT_BM + q * 32;  // the warp's first row inside this launch
+      const bool rows_ok = g0 < p.row_count;
+      const int blk = g0 / p.block_rows_out, gl0 = g0 - blk * p.block_rows_out;
+      const bool own = blk == p.own_blk;
       const int j0 = ni * CT_BN;
-      const bool full_cols = j0 + CT_BN <= p.n;
-      __half *xr = (blk == p.own_blk ? p.x_own : p.x_out + blk * p.x_bs) + h * p.x_hs + (int64_t)gl * p.x_rs + j0;
       const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * CT_BN;
 #pragma unroll 1
       for (int chunk = 0; chunk < CT_BN / 32; ++chunk) {
@@ -737,22 +745,32 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(CT_THREADS, 1)
 #pragma unroll
         for (int c = 0; c < 32; c += 2)
           pk[c >> 1] = pack_half2(__uint_as_float(v[c]) * p.scale, __uint_as_float(v[c + 1]) * p.scale);
-        if (row_ok) {
-          if (full_cols) {
-            uint4 *d = reinterpret_cast<uint4 *>(xr + chunk * 32);
+        const int sb = stores & 1;
+        if (lane == 0 && stores >= 2) bulk_wait_read_but_one();  // this block's previous store has read it
+        __syncwarp();
+        uint8_t *srow = stage0_ptr + sb * CT_XSTAGE_BYTES + lane * 64;
 #pragma unroll
-            for (int w = 0; w < 4; ++w) d[w] = make_uint4(pk[4 * w], pk[4 * w + 1], pk[4 * w + 2], pk[4 * w + 3]);
-          } else {
-            const __half *hv = reinterpret_cast<const __half *>(pk);
-            for (int c = 0; c < 32; ++c)
-              if (j0 + chunk * 32 + c < p.n) xr[chunk * 32 + c] = hv[c];
-          }
+        for (int c = 0; c < 4; ++c)
+          *reinterpret_cast<uint4 *>(srow + ((c ^ ((lane >> 1) & 3)) << 4)) =
+              make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+        fence_async_smem();
+        __syncwarp();
+        const int jc = j0 + chunk * 32;
+        if (lane == 0 && rows_ok && jc < p.n) {  // rows and columns past the product are clipped
+          const uint32_t src = stage0 + sb * CT_XSTAGE_BYTES;
+          if (own)
+            tma_store_3d(&xmap_own, src, jc, gl0, h);
+          else
+            tma_store_4d(&xmap_out, src, jc, gl0, h, blk);
         }
+        if (lane == 0) bulk_commit();
+        ++stores;
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_leader(acc_empty(buf));
     }
+    if (lane == 0) bulk_wait_all();
   }
 
   tc_fence_before();
@@ -1544,11 +1562,26 @@ af2_status triangle_launch(af2_ctx *ctx, int direction, const TriangleLayout &L,
     ca.total_tiles = static_cast<int>(hq) * ca.tiles_m * ca.tiles_n;
     ca.scale = 1.0f / static_cast<float>(n);
     ca.err = ctx->err_word;
+    // product stores: [block][hq][rows_per_block][jp] (x_base) and this rank's own block, boxes of
+    // 32 columns x 32 rows
+    CUtensorMap xmap_out, xmap_own;
+    std::memset(&xmap_own, 0, sizeof xmap_own);
+    const uint64_t nblk = static_cast<uint64_t>((rc + rows_per_block - 1) / rows_per_block);
+    const uint64_t xdims[4] = {static_cast<uint64_t>(n), static_cast<uint64_t>(rows_per_block),
+                               static_cast<uint64_t>(hq), nblk};
+    const uint64_t xstr[3] = {static_cast<uint64_t>(L.jp) * 2, static_cast<uint64_t>(L.x_hs) * 2,
+                              static_cast<uint64_t>(hq * L.x_hs) * 2};
+    const uint32_t xbox[4] = {32, 32, 1, 1};
+    if (!encode_map_4d(&xmap_out, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x_base, xdims, xstr, xbox,
+                       CU_TENSOR_MAP_SWIZZLE_64B) ||
+        (own_blk >= 0 && !encode_map_3d(&xmap_own, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, ca.x_own, n, rows_per_block, hq,
+                                        L.jp * 2, (uint64_t)L.x_hs * 2, 32, 32, 1, CU_TENSOR_MAP_SWIZZLE_64B)))
+      return fail(ctx, AF2_ERR_CUDA, "cuTensorMapEncodeTiled failed for the contraction's product maps");
     // CTA pairs: an even grid of at most the pairs that can be resident together
     const int grid = 2 * std::max(1, std::min(ca.total_tiles, contract_pairs));
     {
       LaunchScope scope(ctx, stream, kProfTriangleContract);
-      contract_kernel<<<grid, CT_THREADS, CT_SMEM, stream>>>(amap, bmap, amap_own, bmap_own, ca);
+      contract_kernel<<<grid, CT_THREADS, CT_SMEM, stream>>>(amap, bmap, amap_own, bmap_own, xmap_out, xmap_own, ca);
     }
     const cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? AF2_OK : cuda_fail(ctx, e, "launch contraction");
