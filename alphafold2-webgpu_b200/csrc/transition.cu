@@ -468,32 +468,36 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (!warp_wait(d1_full(db), ph, abort_flag, p.err, kErrWaitEpilogue)) break;
       tc_fence_after();
       if (!warp_wait(h_empty(db), ph ^ 1, abort_flag, p.err, kErrWaitEpilogue)) break;
+      // Each thread converts rows rq, rq + 8 of each 16-lane group of the quarter and the column
+      // pairs 8k + 2 cp (the 16x256b TMEM shape), so it needs the scale and bias of 16 of a
+      // half's 64 channels, loaded once for its four rows (four different addresses per warp).
+      const int rq_cp = lane & 3;
 #pragma unroll 1
       for (int half = 0; half < 2; ++half) {  // 64 hidden channels: 64 f32 columns in, 32 packed f16 columns out
-        uint32_t v[2][32];
-        tmem_ld32(lane_base + db * HC + half * 64, v[0]);
-        tmem_ld32(lane_base + db * HC + half * 64 + 32, v[1]);
-        tmem_ld_wait();
-        const float4 *sc = reinterpret_cast<const float4 *>(s1v + h * HC + half * 64);
-        const float4 *bi = reinterpret_cast<const float4 *>(b1v + h * HC + half * 64);
-        uint32_t pk[32];
+        float2 sv[8], bv[8];
 #pragma unroll
-        for (int c16 = 0; c16 < 8; ++c16) {  // 8 hidden channels
-#pragma unroll
-          for (int i2 = 0; i2 < 2; ++i2) {
-            const float4 sv = sc[c16 * 2 + i2], bv = bi[c16 * 2 + i2];
-            const int c = c16 * 8 + i2 * 4;
-            const float2 y0 =
-                f2fma(make_float2(__uint_as_float(v[c >> 5][c & 31]), __uint_as_float(v[c >> 5][(c + 1) & 31])),
-                      make_float2(sv.x, sv.y), make_float2(bv.x, bv.y));
-            const float2 y1 =
-                f2fma(make_float2(__uint_as_float(v[c >> 5][(c + 2) & 31]), __uint_as_float(v[c >> 5][(c + 3) & 31])),
-                      make_float2(sv.z, sv.w), make_float2(bv.z, bv.w));
-            pk[c16 * 4 + i2 * 2] = pack_half2_relu(y0.x, y0.y);
-            pk[c16 * 4 + i2 * 2 + 1] = pack_half2_relu(y1.x, y1.y);
-          }
+        for (int k = 0; k < 8; ++k) {
+          const int c = h * HC + half * 64 + 8 * k + 2 * rq_cp;
+          sv[k] = *reinterpret_cast<const float2 *>(s1v + c);
+          bv[k] = *reinterpret_cast<const float2 *>(b1v + c);
         }
-        tmem_st32(lane_base + db * HC + half * 32, pk);
+#pragma unroll
+        for (int g = 0; g < 2; ++g) {  // lanes 32 q + 16 g .. 32 q + 16 g + 15
+          const uint32_t gbase = lane_base + (static_cast<uint32_t>(16 * g) << 16) + db * HC;
+          uint32_t v[32];
+          tmem_ld_16x256b_x8(gbase + half * 64, v);
+          tmem_ld_wait();
+          uint32_t pk[16];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const float2 y0 = f2fma(make_float2(__uint_as_float(v[4 * k]), __uint_as_float(v[4 * k + 1])), sv[k], bv[k]);
+            const float2 y1 =
+                f2fma(make_float2(__uint_as_float(v[4 * k + 2]), __uint_as_float(v[4 * k + 3])), sv[k], bv[k]);
+            pk[2 * k] = pack_half2_relu(y0.x, y0.y);
+            pk[2 * k + 1] = pack_half2_relu(y1.x, y1.y);
+          }
+          tmem_st_16x128b_x8(gbase + half * 32, pk);
+        }
       }
       tmem_st_wait();
       tc_fence_before();
