@@ -385,6 +385,14 @@ __device__ __forceinline__ void tmem_ld_16x256b_x8(uint32_t taddr, uint32_t (&r)
       : "r"(taddr));
 }
 
+// The 16x256b shape once (8 columns): r[0], r[1] = lane (base + t / 4), columns 2 (t % 4) and
+// + 1; r[2], r[3] = the same columns of lane (base + 8 + t / 4).
+__device__ __forceinline__ void tmem_ld_16x256b_x1(uint32_t taddr, uint32_t (&r)[4]) {
+  asm volatile("tcgen05.ld.sync.aligned.16x256b.x1.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(taddr));
+}
+
 // 16 lanes x 32 consecutive 32-bit columns stored in the 16x128b shape, repeated 8 times:
 // thread t writes, for k = 0..7, r[2k] to lane (base + t / 4), column 4k + t % 4, and r[2k + 1]
 // to lane (base + 8 + t / 4), the same column.

@@ -1079,7 +1079,7 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
           !warp_wait(stat_full, it & 1, abort_flag, p.err, kErrWaitEpilogue))
         break;
       tc_fence_after();
-      {
+      if (!staged_out) {
         const float2 st = xstat[pr];
         nmean2 = f2(-st.x);
         rstd2 = f2(st.y);
@@ -1088,27 +1088,59 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
       }
       const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * 256;
       if (staged_out) {
-        uint4 held[4];  // channels cbase .. cbase + 31 as OT, waiting for the staging buffer
+        // TMEM in the 16x256b shape: this thread takes rows 16 g + 8 hh + rq of the quarter
+        // (g, hh = 0, 1) and the channel pairs c = cbase + 8k + 2 cp, so it loads the three
+        // per-channel vectors of two channels per k once for four rows; each 4-byte pair is
+        // staged at its place in the 128B-swizzled row.
+        const int rq = lane >> 2, cp = lane & 3;
+        float nmean[4], rstdv[4];
+#pragma unroll
+        for (int ri = 0; ri < 4; ++ri) {
+          const float2 st = xstat[q * 32 + 8 * ri + rq];
+          nmean[ri] = -st.x;
+          rstdv[ri] = st.y;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(stat_free);
+        uint8_t *stage_half = smem + OP_OFF_OUT + (cbase >> 6) * 16384;
+        auto stage_pair = [&](int ri, int k, uint32_t v) {
+          const int r = q * 32 + 8 * ri + rq;
+          *reinterpret_cast<uint32_t *>(stage_half + r * 128 + ((k ^ (r & 7)) << 4) + 4 * cp) = v;
+        };
+        uint32_t held[4][4];  // k = 0..3, rows ri: held until the staging buffer is claimed
         bool ok = true;
 #pragma unroll
-        for (int part = 0; part < 8; ++part) {
-          const int c0 = cbase + part * 8;
-          Vec8 vec;
-          load_vec8(c0, vec);
-          uint32_t vo[8], vg[8];
-          tmem_ld8(taddr + c0, vo);
-          tmem_ld8(taddr + 128 + c0, vg);
+        for (int k = 0; k < 8; ++k) {
+          const int c = cbase + 8 * k + 2 * cp;
+          const float2 bz2 = *reinterpret_cast<const float2 *>(vbz + c);
+          const float2 bg2 = f2mul(*reinterpret_cast<const float2 *>(vbg + c), half2f);
+          const float2 zs2 = *reinterpret_cast<const float2 *>(vzs + c);
+          uint32_t vo[2][4], vg[2][4];
+#pragma unroll
+          for (int g = 0; g < 2; ++g) {
+            const uint32_t ga = taddr + (static_cast<uint32_t>(16 * g) << 16) + cbase + 8 * k;
+            tmem_ld_16x256b_x1(ga, vo[g]);
+            tmem_ld_16x256b_x1(ga + 128, vg[g]);
+          }
           tmem_ld_wait();
-          uint4 o;
-          OT *e16 = reinterpret_cast<OT *>(&o);
-          gate8(vo, vg, vec, [&](int cc, float2 y) {
-            e16[cc] = from_f32<OT>(y.x);
-            e16[cc + 1] = from_f32<OT>(y.y);
-          });
-          if (part < 4) {
-            held[part] = o;
+          uint32_t out[4];
+#pragma unroll
+          for (int ri = 0; ri < 4; ++ri) {
+            const int g = ri >> 1, hh = ri & 1;
+            const float2 arg =
+                f2fma(make_float2(__uint_as_float(vg[g][2 * hh]), __uint_as_float(vg[g][2 * hh + 1])), half2f, bg2);
+            const float2 gate = f2fma(make_float2(tanhf_approx(arg.x), tanhf_approx(arg.y)), half2f, half2f);
+            const float2 xo =
+                f2fma(f2fma(zs2, f2(nmean[ri]), make_float2(__uint_as_float(vo[g][2 * hh]), __uint_as_float(vo[g][2 * hh + 1]))),
+                      f2(rstdv[ri]), bz2);
+            const float2 y = f2mul(xo, gate);
+            out[ri] = pack2_t<OT>(y.x, y.y);
+          }
+          if (k < 4) {
+#pragma unroll
+            for (int ri = 0; ri < 4; ++ri) held[k][ri] = out[ri];
           } else {
-            if (part == 4) {  // claim the staging buffer, then release the held channels into it
+            if (k == 4) {  // claim the staging buffer, then release the held channels into it
               if (storer && store_pending) {
                 bulk_wait_read_all();
                 mbar_arrive(out_free);
@@ -1117,9 +1149,12 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
               ok = warp_wait(out_free, (it & 1) ^ 1, abort_flag, p.err, kErrWaitEpilogue);
               if (!ok) break;
 #pragma unroll
-              for (int hp = 0; hp < 4; ++hp) stage8(held[hp], cbase + hp * 8);
+              for (int kh = 0; kh < 4; ++kh)
+#pragma unroll
+                for (int ri = 0; ri < 4; ++ri) stage_pair(ri, kh, held[kh][ri]);
             }
-            stage8(o, c0);
+#pragma unroll
+            for (int ri = 0; ri < 4; ++ri) stage_pair(ri, k, out[ri]);
           }
         }
         if (!ok) break;
