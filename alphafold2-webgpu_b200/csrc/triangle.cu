@@ -429,13 +429,21 @@ __global__ void __launch_bounds__(PJ_THREADS, 1)
     const int e = warp - 6;        // 0..7
     const int op = e >> 2;         // 0: a (a_p, a_g), 1: b (b_p, b_g)
     const int q = warp & 3;        // TMEM lane quarter this warp may read
-    const int h = q * 32 + lane;
+    // TMEM in the 16x256b shape: this thread takes channels h = 32 q + 8 ri + rq (ri = 0..3)
+    // and the pair columns 8k + 2 cp, + 1 (k = 0..7), so it reads each pair's mask once for
+    // four channels; each 4-byte pair is staged at its place in the channel's swizzled row.
+    const int rq = lane >> 2, cp = lane & 3;
     const bool storer = e == 0 && lane == 0;
     bool store_pending = false;  // storer: a committed store may still be reading the staging buffer
-    const float bias_p = p.vec[(op ? kVBBP : kVBAP) * C + h];
-    const float bias_g = p.vec[(op ? kVBBG : kVBAG) * C + h];
-    const float2 half2f = f2(0.5f), gate_shift = f2(0.5f * bias_g), bias_p2 = f2(bias_p);
-    uint8_t *stage_row = smem + PJ_OFF_OUT + op * PJ_OUT_BYTES + h * 128;
+    float2 gate_shift[4], bias_p2[4];
+#pragma unroll
+    for (int ri = 0; ri < 4; ++ri) {
+      const int h = q * 32 + 8 * ri + rq;
+      gate_shift[ri] = f2(0.5f * p.vec[(op ? kVBBG : kVBAG) * C + h]);
+      bias_p2[ri] = f2(p.vec[(op ? kVBBP : kVBAP) * C + h]);
+    }
+    const float2 half2f = f2(0.5f);
+    uint8_t *stage_op = smem + PJ_OFF_OUT + op * PJ_OUT_BYTES;
     int tr = blockIdx.x / p.tiles_k, tk = blockIdx.x % p.tiles_k;  // tile t = tr tiles_k + tk
     const int dr = gridDim.x / p.tiles_k, dk = gridDim.x % p.tiles_k;
     int it = 0;
@@ -455,40 +463,33 @@ __global__ void __launch_bounds__(PJ_THREADS, 1)
         break;
       tc_fence_after();
       const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * 256 + op * 2 * PJ_TILE;
-      // The whole tile leaves TMEM first (loads pipelined one part ahead of the
-      // math) and stays in registers as packed f16, so the accumulator is
-      // released early and the previous tile's TMA store keeps reading the
+      // The whole tile leaves TMEM first and stays in registers as packed f16, so the
+      // accumulator is released early and the previous tile's TMA store keeps reading the
       // staging buffer meanwhile.
-      uint32_t pk[PJ_TILE / 2];
-      uint32_t vp[2][16], vg[2][16];
-      tmem_ld16(taddr, vp[0]);
-      tmem_ld16(taddr + PJ_TILE, vg[0]);
-      tmem_ld_wait();
+      uint32_t pk[8][4];  // [k][ri]: pairs 8k + 2cp, + 1 of channel 32 q + 8 ri + rq
 #pragma unroll
-      for (int part = 0; part < PJ_TILE / 16; ++part) {
-        const int cur = part & 1;
-        if (part + 1 < PJ_TILE / 16) {
-          tmem_ld16(taddr + (part + 1) * 16, vp[cur ^ 1]);
-          tmem_ld16(taddr + PJ_TILE + (part + 1) * 16, vg[cur ^ 1]);
+      for (int k = 0; k < PJ_TILE / 8; ++k) {
+        const float2 mm = *reinterpret_cast<const float2 *>(msk + 8 * k + 2 * cp);
+        uint32_t vp[2][4], vg[2][4];
+#pragma unroll
+        for (int g = 0; g < 2; ++g) {
+          const uint32_t ga = taddr + (static_cast<uint32_t>(16 * g) << 16) + 8 * k;
+          tmem_ld_16x256b_x1(ga, vp[g]);
+          tmem_ld_16x256b_x1(ga + PJ_TILE, vg[g]);
         }
+        tmem_ld_wait();
 #pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4) {
-          const float4 mk = *reinterpret_cast<const float4 *>(msk + part * 16 + c4 * 4);
-          const float2 mm[2] = {make_float2(mk.x, mk.y), make_float2(mk.z, mk.w)};
-#pragma unroll
-          for (int i = 0; i < 2; ++i) {
-            const int c = c4 * 4 + 2 * i;
-            // a = mask (p + b_p) sigmoid(g + b_g), sigmoid(x) = 0.5 + 0.5 tanh(x / 2)
-            const float2 arg = f2fma(make_float2(__uint_as_float(vg[cur][c]), __uint_as_float(vg[cur][c + 1])),
-                                     half2f, gate_shift);
-            const float2 sg = f2fma(make_float2(tanhf_approx(arg.x), tanhf_approx(arg.y)), half2f, half2f);
-            const float2 pb =
-                f2add(make_float2(__uint_as_float(vp[cur][c]), __uint_as_float(vp[cur][c + 1])), bias_p2);
-            const float2 y = f2mul(f2mul(pb, sg), mm[i]);
-            pk[part * 8 + c4 * 2 + i] = pack_half2(y.x, y.y);
-          }
+        for (int ri = 0; ri < 4; ++ri) {
+          const int g = ri >> 1, hh = ri & 1;
+          // a = mask (p + b_p) sigmoid(g + b_g), sigmoid(x) = 0.5 + 0.5 tanh(x / 2)
+          const float2 arg =
+              f2fma(make_float2(__uint_as_float(vg[g][2 * hh]), __uint_as_float(vg[g][2 * hh + 1])), half2f, gate_shift[ri]);
+          const float2 sg = f2fma(make_float2(tanhf_approx(arg.x), tanhf_approx(arg.y)), half2f, half2f);
+          const float2 pb =
+              f2add(make_float2(__uint_as_float(vp[g][2 * hh]), __uint_as_float(vp[g][2 * hh + 1])), bias_p2[ri]);
+          const float2 y = f2mul(f2mul(pb, sg), mm);
+          pk[k][ri] = pack_half2(y.x, y.y);
         }
-        if (part + 1 < PJ_TILE / 16) tmem_ld_wait();
       }
       tc_fence_before();
       __syncwarp();
@@ -502,11 +503,14 @@ __global__ void __launch_bounds__(PJ_THREADS, 1)
         store_pending = false;
       }
       if (!warp_wait(out_free, (it & 1) ^ 1, abort_flag, p.err, kErrWaitEpilogue)) break;
-      // 64 pairs = the eight 16-byte chunks of this channel's staged row
+      // 64 pairs = the eight 16-byte chunks of each channel's staged row; this thread's 4 bytes
 #pragma unroll
-      for (int ch = 0; ch < 8; ++ch)
-        *reinterpret_cast<uint4 *>(stage_row + (((ch ^ (h & 7))) << 4)) =
-            make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]);
+      for (int ri = 0; ri < 4; ++ri) {
+        const int h = q * 32 + 8 * ri + rq;
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          *reinterpret_cast<uint32_t *>(stage_op + h * 128 + ((k ^ (h & 7)) << 4) + 4 * cp) = pk[k][ri];
+      }
       fence_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(out_full);
