@@ -56,9 +56,9 @@ METRIC = "Evoformer pair-GEMM TFLOP/s & ms/block at N=1024; % of B200 bf16 TC pe
 # dram__bytes_read.sum + dram__bytes_write.sum per launch of the default block at N=1024, from
 # one single-pass ncu capture of this workload (profiles/block_n1024_launches.md, the mean over
 # 14 block steps); kernels without a capture report null.
-KERNEL_DRAM_BYTES = {"opm.fused": 607_803_355, "triangle.contract": 771_655_781, "triangle.project": 750_263_707,
-                     "triangle.output": 750_905_792, "transition.fused": 473_941_285, "opm.project": 313_924_937,
-                     "opm.count": 2_118_766}
+KERNEL_DRAM_BYTES = {"opm.fused": 606_830_208, "triangle.contract": 777_577_673, "triangle.project": 747_430_601,
+                     "triangle.output": 750_551_470, "transition.fused": 473_526_985, "opm.project": 314_026_478,
+                     "opm.count": 2_116_352}
 KERNELS = ("weights.prepare", "triangle.prepare", "triangle.relayout", "triangle.project", "triangle.contract",
            "triangle.output", "opm.normalize", "opm.project", "opm.count", "opm.outer", "opm.output",
            "opm.fused", "transition.prepare", "transition.normalize", "transition.fused", "transition.linear",
