@@ -1020,12 +1020,13 @@ __global__ void __launch_bounds__(OP_THREADS, 1)
     // is sigmoid(x) = 1/2 + tanh(x / 2) / 2.
     // 16-bit outputs with 128 channels are staged in shared memory and leave
     // through TMA: a plain store, or an add into the pair for the residual
-    // form (the old values never pass through the SM).  A thread owns one pair
-    // row and 64 of its channels (warps 14-17 the first half, 18-21 the
-    // second); the first 32 are computed into registers before the staging
-    // buffer is claimed, so the previous tile's TMA keeps reading it meanwhile.
-    // Other outputs are written (and, for the residual, read) by the thread
-    // that owns the row.
+    // form (the old values never pass through the SM).  Warps 14-17 take the
+    // first 64 channels, 18-21 the second; in the staged form a thread owns
+    // four pair rows and two of every eight of its half's channels (the 16x256b
+    // TMEM shape), and the first half of them are computed into registers
+    // before the staging buffer is claimed, so the previous tile's TMA keeps
+    // reading it meanwhile.  Other outputs are written (and, for the residual,
+    // read) by the thread that owns the row, one row and 64 channels each.
     const int q = warp & 3;
     const int pr = q * 32 + lane;
     const int cbase = ((warp - 14) >> 2) * 64;  // this thread's channels: cbase .. cbase + 63
