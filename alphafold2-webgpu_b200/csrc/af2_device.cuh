@@ -614,6 +614,12 @@ __device__ __forceinline__ uint32_t pack2_t<__nv_bfloat16>(float lo, float hi) {
   __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t *>(&h);
 }
+// f32 outputs never take a packed 16-bit path; this only lets shared kernel
+// code that branches on the output type compile for f32.
+template <>
+__device__ __forceinline__ uint32_t pack2_t<float>(float, float) {
+  return 0;
+}
 
 // Writes y into columns [c0, c0 + 32) of an output row, or with `residual`
 // adds y to what is there (in f32, rounded once).  Whole 32-column chunks of
