@@ -159,6 +159,59 @@ __device__ __forceinline__ void ln_row(uint8_t *tile, int kb, int row, int c, fl
   }
 }
 
+// The same LayerNorm for tiles of two 64-channel blocks with four threads per
+// row: thread `quarter` takes channels 32 quarter .. 32 quarter + 31 (block
+// quarter / 2, 16-byte chunks 4 (quarter % 2) ..) and holds their gamma and
+// beta in registers (g, b), so a tile costs no loads of them; the four combine
+// their shifted sums with lanes ^ 8 and ^ 16.
+template <typename XT>
+__device__ __forceinline__ void ln_row_quad(uint8_t *tile, int row, int quarter, int c, float inv_c, float eps,
+                                            const float2 (&g)[16], const float2 (&b)[16]) {
+  uint8_t *blk = tile + (quarter >> 1) * 16384;
+  const int c0 = (quarter & 1) * 4;
+  const float x0 = unpack2<XT>(*reinterpret_cast<const uint32_t *>(tile + sw128_offset(row, 0))).x;
+  const float2 neg_x0 = f2(-x0);
+  float2 s1 = f2(0.f), s2 = f2(0.f);
+  uint4 v[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) v[k] = *reinterpret_cast<const uint4 *>(blk + sw128_offset(row, c0 + k));
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const uint32_t w[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float2 d = f2add(unpack2<XT>(w[i]), neg_x0);
+      const int ch = quarter * 32 + k * 8 + 2 * i;
+      d.x = ch < c ? d.x : 0.f;
+      d.y = ch + 1 < c ? d.y : 0.f;
+      s1 = f2add(s1, d);
+      s2 = f2fma(d, d, s2);
+    }
+  }
+  float a1 = s1.x + s1.y, a2 = s2.x + s2.y;
+  a1 += __shfl_xor_sync(kFull, a1, 8);
+  a2 += __shfl_xor_sync(kFull, a2, 8);
+  a1 += __shfl_xor_sync(kFull, a1, 16);
+  a2 += __shfl_xor_sync(kFull, a2, 16);
+  const float m1 = a1 * inv_c;
+  const float mean = x0 + m1;
+  const float var = fmaxf(a2 * inv_c - m1 * m1, 0.f);
+  const float rstd = rsqrtf(var + eps);
+  const float2 r2 = f2(rstd), nm2 = f2(-mean);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const uint32_t w[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
+    uint32_t o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 a = f2mul(g[4 * k + i], r2);  // rstd * gamma
+      const float2 y = f2fma(f2add(unpack2<XT>(w[i]), nm2), a, b[4 * k + i]);
+      o[i] = pack_half2(y.x, y.y);
+    }
+    *reinterpret_cast<uint4 *>(blk + sw128_offset(row, c0 + k)) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
 // Two f32 -> packed f16 with ReLU (cvt.rn.relu: max(0, round(v)) = round(max(0, v))).
 __device__ __forceinline__ uint32_t pack_half2_relu(float lo, float hi) {
   uint32_t r;
@@ -445,7 +498,29 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       return true;
     };
-    if (warp >= 6) {
+    if (warp >= 6 && KB == 2) {
+      // two 64-channel blocks: four threads per row, 32 rows per pass, gamma and beta of the
+      // thread's 32 channels held in registers for the whole launch
+      const int quarter = lane >> 3, rl = (warp - 6) * 8 + (lane & 7);
+      float2 gq[16], bq[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        gq[i] = *reinterpret_cast<const float2 *>(gamma + quarter * 32 + 2 * i);
+        bq[i] = *reinterpret_cast<const float2 *>(beta + quarter * 32 + 2 * i);
+      }
+      for (int it = 0; it < my_tiles; ++it) {
+        const int buf = it & 1;
+        if (!warp_wait(a_raw(buf), (it >> 1) & 1, abort_flag, p.err, kErrWaitNormalizer)) break;
+        if (p.normalize) {
+#pragma unroll 1
+          for (int pass = 0; pass < TILE / 32; ++pass)
+            ln_row_quad<XT>(smem + buf * A_BYTES, pass * 32 + rl, quarter, p.c, inv_c, p.eps, gq, bq);
+          fence_async_smem();
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(a_full(buf));
+      }
+    } else if (warp >= 6) {
       for (int it = 0; it < my_tiles; ++it)
         if (!layer_norm(it)) break;
     } else {
