@@ -643,9 +643,10 @@ __global__ void __launch_bounds__(OTHREADS, 1)
 // with left streamed through a ring and the tile's right operand resident in
 // shared memory, both K-major (sequences contiguous: MN-major operands run the
 // tensor core several times slower at this N).  Worker warps round D1 * 2^-k
-// to f16 in TMEM (one warp per lane quarter and residue j, 32 columns each),
-// and the tensor core multiplies it, read as an A operand straight from TMEM,
-// by the 32 rows of W_o that belong to channel a:
+// to f16 (one warp per lane quarter and residue j, 32 columns each) into A2,
+// and the tensor core multiplies it, read as an A operand from TMEM (or, for
+// the third residue of a three-residue tile, from shared memory), by the 32
+// rows of W_o that belong to channel a:
 //   D2_j[i][z] += A2_j[i][b] W_o[a*32 + b][z]                (M 128, N c_z, K 32)
 // The outer products never leave the SM.  After the 32 slices the same
 // workers apply the column scales (which carry 2^k back), b_o, 1/(eps + count)
